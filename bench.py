@@ -1,0 +1,401 @@
+#!/usr/bin/env python3
+"""Benchmark of the PFSS hot path on B200 (one process per GPU).
+
+Workload: a FaithfulARS truncation bundle --
+N = 4,194,304 masked Q32 inputs (|x| < 2^40, f = 16, seed 2), 4 raw DCF
+queries per element (2 x 64-bit, 2 x 16-bit, broadcast myl7 keys, AES-128-MMO
+PRG), the additive boolean plan and the ARS postproc, all in one fused
+launch per party.  Metric: DCF pred-evals per second (one pred-eval = one
+(element, query, party) evaluation), whole job.
+
+At N = 1 the GPU evaluates both parties on the 4,194,304 elements (the
+reference's setting: both parties on one GPU).  At N >= 2, ranks
+[0, N/2) are party 0 and [N/2, N) party 1; each rank evaluates its party on
+its own shard of 2 x 4,194,304 elements, so per-GPU work is the same at every
+N (weak scaling) and no data-path collective is involved.
+
+Legs: `value` (inputs resident in HBM, CUDA events on the launch stream,
+L2 flushed between steps), `e2e` (host-buffer C-ABI call from pinned memory,
+copies inside the timed region), the roofline of the fused kernel, a bounded
+CPU baseline (the reference's own myl7 dcf_eval, OpenMP over elements) and
+the clocks sampled during the timed region.  `--impl reference` times only
+the reference CPU implementation on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_ELEM = 1 << 22
+FRAC = 16
+SEED = 2
+KIND_ARS = 1
+METRIC = "DCF pred-evals/sec (FaithfulARS trunc bundle, 4 queries/element)"
+UNIT = "pred-evals/s"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# workload material (product dealer + keygen; deterministic from the seed)
+# ---------------------------------------------------------------------------
+
+def prg_state() -> np.ndarray:
+    from suf_b200.engine import host_mt19937_64
+
+    return host_mt19937_64(0x5EED_0002, 16).view(np.uint8).copy()
+
+
+def dealer(ctx):
+    """Both parties' bundle descriptors and myl7 keys (product keygen)."""
+    from suf_b200 import GROUP_ADD
+    from suf_b200.engine import Context, host_mt19937_64
+
+    r_in, d0, d1, thetas = Context.trunc_gen(KIND_ARS, FRAC, SEED)
+    words = host_mt19937_64(SEED ^ 0x6D796C37, 4 * max(d0.nq, 1)).view(np.uint8).reshape(-1, 2, 16)
+    keys0, keys1 = [], []
+    for q in range(d0.nq):
+        k0, k1 = ctx.myl7_gen(GROUP_ADD, d0.q_bits[q], int(thetas[q]), (1).to_bytes(8, "little"), words[q, 0],
+                              words[q, 1])
+        keys0.append(k0)
+        keys1.append(k1)
+    return r_in, (d0, d1), (keys0, keys1)
+
+
+def inputs(r_in: int, n: int, shard: int) -> np.ndarray:
+    rng = np.random.default_rng([SEED, shard])
+    x = rng.integers(-(2**40) + 1, 2**40, n, dtype=np.int64).view(np.uint64)
+    return x + np.uint64(r_in)
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append([s.strip() for s in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            try:
+                sm.append(float(s[1]))
+                mx = float(s[2])
+                for nm, v in zip(names, s[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200.engine import Context
+    from suf_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    ctx = Context(local)
+    ctx.prg_init(prg_state())
+    r_in, descs, keys = dealer(ctx)
+    nq = int(descs[0].nq)
+    if ws == 1:
+        parties = [0, 1]
+        n = N_ELEM
+        shard = 0
+    else:
+        half = max(ws // 2, 1)
+        parties = [0 if rank < half else 1]
+        n = 2 * N_ELEM
+        shard = rank % half
+    xhat_h = inputs(r_in, n, shard)
+    stream = torch.cuda.Stream(device=dev)
+    d_x = torch.from_numpy(xhat_h.view(np.int64)).to(dev)
+    d_y = {p: torch.empty(n, dtype=torch.int64, device=dev) for p in parties}
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+    torch.cuda.synchronize()
+
+    def step():
+        for p in parties:
+            ctx.trunc_bundle_eval(descs[p], keys[p], d_x, d_y=d_y[p], stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    ctx.sync(stream)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        time.sleep(0.3)
+        with torch.cuda.stream(stream):
+            for k in range(args.steps):
+                flush.fill_(k)  # write 256 MB (> 126 MB L2) between timed steps
+                evs[k][0].record(stream)
+                step()
+                evs[k][1].record(stream)
+        torch.cuda.synchronize()
+        ctx.sync(stream)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms_steps = [a.elapsed_time(b) for a, b in evs]
+    ms = sum(ms_steps) / len(ms_steps)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    units_per_rank = n * nq * len(parties)
+    total_units = units_per_rank * ws
+    value = total_units / (ms_max / 1e3)
+
+    # ---- e2e: host-buffer C-ABI entry point, pinned host memory, copies timed ----
+    x_pin = torch.from_numpy(xhat_h.view(np.int64)).pin_memory()
+    y_pin = {p: torch.empty(n, dtype=torch.int64).pin_memory() for p in parties}
+    x_np = x_pin.numpy().view(np.uint64)
+    y_np = {p: y_pin[p].numpy().view(np.uint64) for p in parties}
+    for _ in range(max(1, args.warmup // 2)):
+        for p in parties:
+            ctx.trunc_bundle_eval_host(descs[p], keys[p], x_np, y=y_np[p])
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e2e_ms = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for p in parties:
+            ctx.trunc_bundle_eval_host(descs[p], keys[p], x_np, y=y_np[p])
+        e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    e2e_t = torch.tensor([sum(e2e_ms) / len(e2e_ms)], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_ms_max = float(e2e_t.item())
+    e2e_value = total_units / (e2e_ms_max / 1e3)
+
+    # correctness guard on the measured outputs (reconstruction when both parties are local)
+    ok = None
+    if len(parties) == 2:
+        y0 = d_y[0].cpu().numpy().view(np.uint64)
+        y1 = d_y[1].cpu().numpy().view(np.uint64)
+        x = (xhat_h - np.uint64(r_in)).view(np.int64)
+        ok = bool(((y0 + y1) == (x >> FRAC).view(np.uint64)).all())
+
+    peaks = measured_peaks()
+    # algorithmic bytes of the fused kernel per launch: x^ read + y written (8 + 8 B per element)
+    kernel_ms = ms_max / len(parties)
+    alg_bytes = 16.0 * n
+    achieved_gbs = alg_bytes / (kernel_ms / 1e3) / 1e9
+    levels = sum(int(descs[0].q_bits[q]) for q in range(nq))
+    aes_blocks = 2.0 * levels * n  # two AES-128 blocks per tree level (selected child only)
+    roofline = {
+        "bound": "hbm", "achieved": round(achieved_gbs, 2), "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
+        "frac": round(achieved_gbs / peaks.get("hbm_gbs", 6650.0), 5),
+        "traffic": None, "kernel": "trunc_bundle_kernel",
+        "note": ("the fused bundle reads 8 B and writes 8 B per element; it is bound by the AES-128 engine on "
+                 "the integer/shared-memory pipes, see aes_blocks_per_s"),
+        "aes_blocks_per_s": round(aes_blocks / (kernel_ms / 1e3), 1),
+        "kernel_ms": round(kernel_ms, 4),
+    }
+    out = None
+    if rank == 0:
+        cpu = cpu_baseline(args, descs, keys, r_in, ws) if (ws == 1 and not args.no_cpu) else None
+        out = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128", "data": "synthetic (seeded, configs[1] shapes)",
+            "config": {"workload": "configs[1]: FaithfulARS trunc bundle, f=16, |x|<2^40, seed 2",
+                       "n_elements_per_party_per_gpu": n if ws > 1 else N_ELEM, "queries_per_element": nq,
+                       "query_bits": [int(descs[0].q_bits[q]) for q in range(nq)],
+                       "parties_per_gpu": len(parties), "keys": "broadcast myl7 (AES-128-MMO PRG)",
+                       "l2": "256 MB buffer written between timed steps", "parallelism": f"party x element shards on {ws} GPU(s)"},
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": 8 * n * len(parties),
+                    "d2h_bytes_per_step": 8 * n * len(parties), "ms_per_step": round(e2e_ms_max, 3),
+                    "path": "sufb200_trunc_bundle_eval_host (pinned host x^ in, y out)"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "gpu_launches": args.steps * len(parties),
+            "reconstruction_ok": ok,
+            "ms_per_step_all": [round(v, 4) for v in ms_steps],
+        }
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the reference's own myl7 dcf_eval; test infrastructure under oracle/)
+# ---------------------------------------------------------------------------
+
+def cpu_eval_bundle(descs, keys, xhat, parties):
+    """The reference CPU path of the bundle: per query, the reference's own
+    myl7 dcf_eval over all elements (OpenMP in the harness), then the
+    composite boolean plan + ARS postproc (oracle restatement)."""
+    from oracle.oracle import GROUP_ADD, Oracle, RefMyl7, desc_from_fields
+
+    ref = RefMyl7(GROUP_ADD)
+    ref.prg_init(prg_state())
+    orc = Oracle()
+    ys = []
+    for p in parties:
+        d = descs[p]
+        pred = np.zeros((d.nq, xhat.size), dtype=np.uint64)
+        for q in range(d.nq):
+            k = keys[p][q]
+            pred[q] = ref.eval_omp(int(d.q_bits[q]), k, k.size, True, xhat, 8).view(np.uint64).ravel()
+        ys.append(orc.trunc_combine(desc_from_fields(d), xhat, pred.ravel()))
+    return ys
+
+
+def cpu_baseline(args, descs, keys, r_in, ws):
+    from oracle.oracle import RefMyl7
+
+    if not RefMyl7.available():
+        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
+                "sample": "oracle/_ref not built (needs the reference checkout at build time)"}
+    n = args.cpu_sample
+    xhat = inputs(r_in, n, 0)
+    t0 = time.perf_counter()
+    cpu_eval_bundle(descs, keys, xhat, [0, 1])
+    dt = time.perf_counter() - t0
+    nq = int(descs[0].nq)
+    return {"value": round(n * nq * 2 / dt, 1), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+            "sample": f"{n} elements x {nq} queries x 2 parties, reference myl7 dcf_eval (OpenMP over elements, "
+                      f"{os.cpu_count()} threads) + composite plan/postproc; {dt:.2f} s"}
+
+
+def run_reference(args, ws, rank):
+    from oracle.oracle import RefMyl7
+
+    if rank != 0:
+        return None
+    if not RefMyl7.available():
+        return {"impl": "reference", "unavailable": "oracle/_ref (reference myl7 sources) was not built"}
+    from suf_b200.engine import Context
+
+    ctx = Context.__new__(Context)  # dealer only: host context, no GPU work
+    import ctypes as C
+    from suf_b200 import _lib
+
+    h = C.c_void_p()
+    _lib.check(_lib.lib().sufb200_ctx_create(-1, C.byref(h)))
+    ctx._L, ctx.h, ctx.device = _lib.lib(), h, -1
+    ctx.prg_init(prg_state())
+    r_in, descs, keys = dealer(ctx)
+    n = args.cpu_sample
+    xhat = inputs(r_in, n, 0)
+    nq = int(descs[0].nq)
+    for _ in range(args.warmup):
+        cpu_eval_bundle(descs, keys, xhat[: max(1, n // 8)], [0, 1])
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_eval_bundle(descs, keys, xhat, [0, 1])
+        times.append(time.perf_counter() - t0)
+    ctx.close()
+    dt = sum(times) / len(times)
+    v = n * nq * 2 / dt
+    return {"metric": METRIC, "value": round(v, 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128", "data": "synthetic (seeded, configs[1] shapes)",
+            "impl": "reference",
+            "config": {"workload": "configs[1]: FaithfulARS trunc bundle, f=16, |x|<2^40, seed 2",
+                       "sample_elements_per_step": n, "queries_per_element": nq, "parties": 2},
+            "cpu_baseline": {"value": round(v, 1), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+                             "sample": f"{n} elements x {nq} queries x 2 parties per step"},
+            "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-sample", type=int, default=1 << 17)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        out = run_reference(args, ws, rank)
+    else:
+        out = run_ours(args, ws, rank, local)
+    if rank == 0 and out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

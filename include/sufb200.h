@@ -1,0 +1,270 @@
+/*
+ * sufb200.h -- C ABI of the B200-native PFSS evaluation engine (libsufb200.so).
+ *
+ * Plain pointers and sizes only.  "d_" arguments are device pointers on the
+ * context's device; everything else is host memory.  `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  Every entry
+ * point returns SUFB200_OK (0) or a negative SUFB200_ERR_* code and records a
+ * message retrievable with sufb200_last_error() (thread-local).  There is no
+ * CPU fallback: a missing device, a failed launch or a rejected argument is
+ * an error.
+ *
+ * Device-side key checks (header fields of device-resident keys) are
+ * reported through a per-context status word: sufb200_ctx_sync() waits for
+ * the stream and returns SUFB200_ERR_KEY if any kernel flagged a bad key
+ * since the last sync (the outputs of such elements are zero).
+ *
+ * Each comment names the reference interface (ponyyuhan/SUF, path:line)
+ * that the entry point replaces.
+ */
+#ifndef SUFB200_H_
+#define SUFB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SUFB200_OK 0
+#define SUFB200_ERR_INVALID (-1)      /* bad argument (null pointer, size, range) */
+#define SUFB200_ERR_CUDA (-2)         /* CUDA runtime error (launch, copy, device) */
+#define SUFB200_ERR_KEY (-3)          /* key blob header / size mismatch */
+#define SUFB200_ERR_UNSUPPORTED (-4)  /* valid but outside this engine's scope */
+#define SUFB200_ERR_NOT_READY (-5)    /* sufb200_prg_init not called yet */
+
+#define SUFB200_GROUP_ADD 0 /* myl7 u128_le group: additive shares mod 2^64 (low 8 bytes) */
+#define SUFB200_GROUP_XOR 1 /* myl7 bytes group: XOR shares */
+
+typedef struct sufb200_ctx_s* sufb200_ctx;
+
+/* ---- library / context -------------------------------------------------- */
+
+/* ABI version (major*10000 + minor*100 + patch). */
+int sufb200_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* sufb200_last_error(void);
+
+#define SUFB200_HOST_ONLY (-1) /* device argument of a dealer-only context */
+
+/* Bind a context to `device` (cudaSetDevice on the calling thread), build
+ * the AES tables and measure the shared-memory layout.  device =
+ * SUFB200_HOST_ONLY makes a dealer-only context (no GPU needed) that accepts
+ * sufb200_prg_init and the keygen calls; its evaluation calls return
+ * SUFB200_ERR_UNSUPPORTED.  One context per
+ * party per device, like one GpuPfssBackend per party
+ * (src/demo/bench_suf_transformer.cpp:902-903); calls on one context must be
+ * serialised by the caller (the reference guards its backend with a mutex,
+ * cuda/pfss_backend_gpu.cu:529). */
+int sufb200_ctx_create(int device, sufb200_ctx* out);
+int sufb200_ctx_destroy(sufb200_ctx ctx);
+
+/* Wait for `stream`, then report and clear the device status word. */
+int sufb200_ctx_sync(sufb200_ctx ctx, void* stream);
+
+/* Number of SMs of the context's device (grid sizing reference). */
+int sufb200_ctx_sm_count(sufb200_ctx ctx);
+
+/* ---- myl7 PRG-tree DCF --------------------------------------------------- */
+
+/* Install the fixed AES-128-MMO PRG keys: state[16j .. 16j+16) is key j,
+ * j = 0..3 (len >= 64; the reference build passes kBlocks*16 = 128 bytes).
+ * Replaces prg_init, third_party/myl7_fss/src/prg/aes128_mmo.c:16-31. */
+int sufb200_prg_init(sufb200_ctx ctx, const uint8_t* state, size_t len);
+
+/* Bytes of one party's key for `in_bits` and `payload_len`
+ * (include/proto/myl7_fss_backend.hpp:156-159). */
+size_t sufb200_myl7_key_bytes(int in_bits, int payload_len);
+
+/* Dealer: one key pair for f(x) = payload if x < alpha else 0, with the
+ * party seeds supplied by the caller (16 bytes per 16-byte payload chunk).
+ * Byte-identical to Myl7FssBackend::gen_dcf (myl7_fss_backend.hpp:131-213,
+ * which draws the seeds from std::random_device) around dcf_gen
+ * (third_party/myl7_fss/src/dcf.c:42-142).  Host computation. */
+int sufb200_myl7_gen(sufb200_ctx ctx, int group, int in_bits, uint64_t alpha, const uint8_t* payload,
+                     int payload_len, const uint8_t* seeds0, const uint8_t* seeds1, uint8_t* key0,
+                     uint8_t* key1);
+
+/* Dealer, batched: n key pairs (alphas[i], same payload), seeds0/1 hold
+ * 16*chunks bytes per element; keys0/1 are [n][key_bytes].  OpenMP. */
+int sufb200_myl7_gen_batch(sufb200_ctx ctx, int group, int in_bits, const uint64_t* alphas, size_t n,
+                           const uint8_t* payload, int payload_len, const uint8_t* seeds0, const uint8_t* seeds1,
+                           uint8_t* keys0, uint8_t* keys1);
+
+/* Evaluate myl7 keys (one 16-byte chunk, out_bytes <= 8) at d_xs[i], on the
+ * device.  broadcast = 0: d_keys is [n][key_bytes]; broadcast = 1: one key
+ * for all n.  d_out is [n][out_bytes] (little-endian low bytes of the group
+ * element).  Replaces Myl7FssBackend::eval_dcf per element
+ * (myl7_fss_backend.hpp:215-256) and, for this key format,
+ * PfssGpuStagedEval::eval_dcf_many_u64_device[_broadcast]
+ * (include/proto/backend_gpu.hpp:17-38). */
+int sufb200_myl7_dcf_eval(sufb200_ctx ctx, int group, int in_bits, const uint8_t* d_keys, size_t key_bytes,
+                          int broadcast, const uint64_t* d_xs, size_t n, int out_bytes, void* d_out,
+                          void* stream);
+
+/* Host-buffer form of the same evaluation: keys, xs and outs in host memory
+ * (copied in and out inside the call; returns after the result is in outs).
+ * Replaces PfssBackendBatch::eval_dcf_many_u64
+ * (include/proto/pfss_backend_batch.hpp:11-28) for myl7 keys. */
+int sufb200_myl7_dcf_eval_host(sufb200_ctx ctx, int group, int in_bits, const uint8_t* keys, size_t key_bytes,
+                               int broadcast, const uint64_t* xs, size_t n, int out_bytes, uint8_t* outs);
+
+/* ---- fused truncation / ARS bundle ------------------------------------- */
+
+#define SUFB200_TRUNC_FAITHFUL_TR 0
+#define SUFB200_TRUNC_FAITHFUL_ARS 1
+#define SUFB200_TRUNC_GAPARS 2
+
+/* One party's public bundle description.  Query q is a DCF on the low
+ * q_bits[q] bits of x^ with AddU64 payload 1 (compile_suf_to_pfss_two_programs,
+ * src/compiler/suf_to_pfss.cpp:300-556; composite_gen_trunc_gate,
+ * include/gates/composite_fss.hpp:645-833).  Boolean outputs follow the
+ * AddU64 plan of composite_eval_batch_backend (composite_fss.hpp:1385-1638):
+ *   carry = [party0] - (b - a + carry_w) with a = q[carry_a], b = q[carry_b]
+ *   sign  = b - a + sign_w with a = q[sign_a], b = q[sign_b]
+ *   wrap  = q[wrap_q]
+ * (-1 = constant 0), then the postproc hook of `kind`
+ * (include/gates/postproc_hooks.hpp:173-376). */
+typedef struct sufb200_trunc_desc {
+  int32_t kind, frac_bits, party, nq;
+  int32_t q_bits[4];
+  int32_t carry_a, carry_b, sign_a, sign_b, wrap_q, reserved;
+  uint64_t carry_w, sign_w; /* this party's shares of the rotation wrap bits */
+  uint64_t haty;            /* base coefficient share + r_out share */
+  uint64_t r_hi;            /* share of r_in >> f */
+  uint64_t m;               /* GapARS: share of 2^(64-f) * MSB(r_in) */
+} sufb200_trunc_desc;
+
+/* Dealer for one bundle: draws r_in and the share splits from
+ * mt19937_64(rng_seed) in the order of composite_gen_trunc_gate, fills both
+ * parties' descriptors and writes the nq query thresholds to thetas[4];
+ * returns r_in through *r_in_out.  The caller then makes one myl7 key pair
+ * per query (in_bits = q_bits[q], alpha = thetas[q], payload = u64 1 LE). */
+int sufb200_trunc_gen(int kind, int frac_bits, uint64_t rng_seed, sufb200_trunc_desc* d0, sufb200_trunc_desc* d1,
+                      uint64_t* thetas, uint64_t* r_in_out);
+
+/* Fused bundle evaluation: all nq broadcast DCFs, the boolean plan and the
+ * postproc in one launch.  keys[q] (host) is this party's myl7 key of query q
+ * (ADD group, 8-byte payload).  d_y is [n]; d_bools ([n][3] = carry, sign,
+ * wrap shares) may be NULL.  Replaces the AddU64 truncation branch of
+ * composite_eval_batch_backend followed by
+ * FaithfulTruncPostProc / FaithfulArsPostProc / GapArsPostProc::run_batch. */
+int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                              const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y,
+                              uint64_t* d_bools, void* stream);
+
+/* Host-buffer form: xhat, y (and bools, may be NULL) in host memory; copies
+ * in and out inside the call and returns when y is on the host.  Replaces
+ * composite_eval_batch_backend with a host CompositeBatchInput::hatx
+ * (composite_fss.hpp:155-229) followed by the kind's postproc hook. */
+int sufb200_trunc_bundle_eval_host(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                                   const size_t* key_bytes, const uint64_t* xhat, size_t n, uint64_t* y,
+                                   uint64_t* bools);
+
+/* ---- reference GPU-backend key formats (cuda/pfss_backend_gpu.cu) -------- */
+
+/* Threshold "DCF" blob [in_bits u16][payload_len u16][alpha u64][payload]
+ * (DcfKeyHeader, pfss_backend_gpu.cu:69-73,197-221); party 1 carries zeros.
+ * Returns the blob size; writes it when out != NULL. */
+size_t sufb200_thr_dcf_build(int in_bits, uint64_t alpha, const uint8_t* payload, int payload_len, uint8_t* out);
+
+/* out = payload if (x & m) < (alpha & m) else 0 (eval_dcf_many_kernel
+ * [_broadcast], pfss_backend_gpu.cu:386-433). */
+int sufb200_thr_dcf_eval(sufb200_ctx ctx, int in_bits, const uint8_t* d_keys, size_t key_bytes, int broadcast,
+                         const uint64_t* d_xs, size_t n, int out_bytes, void* d_out, void* stream);
+
+/* Packed-compare blob (PackedCmpKeyHeader, 208 bytes + thresholds;
+ * build_packed_cmp_key, pfss_backend_gpu.cu:257-288).  seed is 16 bytes. */
+size_t sufb200_packed_lt_build(int party, uint64_t nonce, int in_bits, const uint64_t* thresholds, int num_thr,
+                               const uint8_t* seed, uint8_t* out);
+
+/* XOR-shared bitmasks 1[x < thr_j], AES-CTR masked with the kernel counter
+ * layout ctr = nonce ^ (idx << 32) ^ (w/2), idx = idx_base + i
+ * (packed_cmp_kernel_keyed[_broadcast], cuda/pfss_kernels.cu:240-423).
+ * d_out is [n][out_words] u64. */
+int sufb200_packed_lt_eval(sufb200_ctx ctx, const uint8_t* d_keys, size_t key_bytes, int broadcast,
+                           const uint64_t* d_xs, size_t n, int in_bits, int out_words, uint64_t idx_base,
+                           uint64_t* d_out, void* stream);
+
+/* Interval-LUT blob (IntervalKeyHeader, 216 bytes + cuts + payload;
+ * build_interval_key, pfss_backend_gpu.cu:223-255).  cuts has intervals+1
+ * entries, payload intervals*out_words. */
+size_t sufb200_interval_lut_build(int party, uint64_t nonce, int in_bits, int out_words, const uint64_t* cuts,
+                                  int intervals, const uint64_t* payload, const uint8_t* seed, uint8_t* out);
+
+/* Additive shares of the interval's payload row, AES-CTR masked with
+ * ctr = nonce ^ (idx << 32) ^ (iv*out_words + w) (vector_lut_kernel_keyed
+ * [_broadcast], cuda/pfss_kernels.cu:545-642).  d_out is [n][out_words]. */
+int sufb200_interval_lut_eval(sufb200_ctx ctx, const uint8_t* d_keys, size_t key_bytes, int broadcast,
+                              const uint64_t* d_xs, size_t n, int out_words, uint64_t idx_base, uint64_t* d_out,
+                              void* stream);
+
+/* seed_from_id (pfss_backend_gpu.cu:189-194): 16 bytes from
+ * mt19937_64(id ^ tweak * 0x9e3779b97f4a7c15). */
+int sufb200_seed_from_id(uint64_t id, uint64_t tweak, uint8_t* seed16);
+
+/* ---- elementwise / row primitives (include/runtime/cuda_primitives.hpp) -- */
+
+/* z = c + d*b + e*a (+ d*e on party 0) mod 2^64 (launch_beaver_mul_kernel). */
+int sufb200_beaver_mul(int party, const uint64_t* d_a, const uint64_t* d_b, const uint64_t* d_c,
+                       const uint64_t* d_d_open, const uint64_t* d_e_open, uint64_t* d_out, size_t n, void* stream);
+
+/* Same with {a,b,c} triples interleaved (launch_beaver_mul_aos_kernel). */
+int sufb200_beaver_mul_aos(int party, const uint64_t* d_triples, const uint64_t* d_d_open,
+                           const uint64_t* d_e_open, uint64_t* d_out, size_t n, void* stream);
+
+/* ((c3*x + c2)*x + c1)*x + c0 mod 2^64 (launch_horner_cubic_kernel). */
+int sufb200_horner_cubic(const uint64_t* d_x, const uint64_t* d_c0, const uint64_t* d_c1, const uint64_t* d_c2,
+                         const uint64_t* d_c3, uint64_t* d_out, size_t n, void* stream);
+
+/* Truncation postproc (launch_trunc_postproc_kernel): kind_gapars 0 =
+ * faithful (sign_idx < 0 for TR, >= 0 for ARS), 1 = GapARS. */
+int sufb200_trunc_postproc(int party, int kind_gapars, int frac_bits, uint64_t r_hi_share, uint64_t m_share,
+                           const uint64_t* d_hatx, const uint64_t* d_arith, size_t arith_stride, int arith_idx,
+                           const uint64_t* d_bools, size_t bool_stride, int carry_idx, int sign_idx, int wrap_idx,
+                           uint64_t* d_out, size_t n, void* stream);
+
+/* out[i*out_words + j] += r_out[j], r_out in host memory, out_words <= 8
+ * (launch_add_rout_aos_kernel). */
+int sufb200_add_rout_aos(uint64_t* d_out, size_t elems, int out_words, const uint64_t* r_out, size_t r_out_words,
+                         void* stream);
+
+/* Per-row sums mod 2^64, optional valid lengths (launch_row_sum_kernel). */
+int sufb200_row_sum(const uint64_t* d_mat, int rows, int cols, const int* d_valid_lens, uint64_t* d_out_rows,
+                    void* stream);
+
+/* Ragged rows back to back, offsets[rows+1] (launch_row_sum_ragged_kernel). */
+int sufb200_row_sum_ragged(const uint64_t* d_vals, const int* d_row_offsets, int rows, uint64_t* d_out_rows,
+                           void* stream);
+
+/* sum (x - mean)^2 per row (launch_row_variance_kernel). */
+int sufb200_row_variance(const uint64_t* d_mat, const uint64_t* d_mean, int rows, int cols, const int* d_valid_lens,
+                         uint64_t* d_out_rows, void* stream);
+
+/* Row-broadcast Beaver mul (launch_row_broadcast_mul_kernel). */
+int sufb200_row_broadcast_mul(int party, const uint64_t* d_A, const uint64_t* d_B_rows, const uint64_t* d_C,
+                              const uint64_t* d_d_open, const uint64_t* d_e_open_rows, int rows, int cols,
+                              const int* d_valid_lens, uint64_t* d_out, void* stream);
+
+/* Dense bitstream of eff_bits-wide values (launch_pack_eff_bits_kernel /
+ * launch_unpack_eff_bits_kernel); packed has ceil(n*eff_bits/64) words. */
+int sufb200_pack_eff_bits(const uint64_t* d_in, int eff_bits, uint64_t* d_packed, size_t n, void* stream);
+int sufb200_unpack_eff_bits(const uint64_t* d_packed, int eff_bits, uint64_t* d_out, size_t n, void* stream);
+
+/* Open: unpack remote packed share, add local, mask to ring_bits
+ * (launch_unpack_add_mod_kernel). */
+int sufb200_unpack_add_mod(const uint64_t* d_local, const uint64_t* d_packed_remote, int eff_bits, uint64_t* d_out,
+                           size_t n, int ring_bits, void* stream);
+
+/* ---- host utilities ----------------------------------------------------- */
+
+/* n successive draws of mt19937_64(seed) (the reference's mask / key RNG). */
+int sufb200_host_mt19937_64(uint64_t seed, uint64_t* out, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SUFB200_H_ */

@@ -45,6 +45,18 @@ class TruncDesc(C.Structure):
     ]
 
 
+def desc_from_fields(src) -> TruncDesc:
+    """Copy a bundle descriptor with the same field names (e.g. the product's
+    sufb200_trunc_desc mirror) into the oracle's layout."""
+    d = TruncDesc()
+    for name in ("kind", "frac_bits", "party", "nq", "carry_a", "carry_b", "sign_a", "sign_b", "wrap_q",
+                 "carry_w", "sign_w", "haty", "r_hi", "m"):
+        setattr(d, name, getattr(src, name))
+    for i in range(4):
+        d.q_bits[i] = src.q_bits[i]
+    return d
+
+
 def build_oracle(quiet: bool = True) -> None:
     """Compile liboracle.so (and oracle/_ref when the reference is present)."""
     import subprocess

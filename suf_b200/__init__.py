@@ -1,0 +1,18 @@
+"""suf_b200 -- B200-native PFSS evaluation engine (host side).
+
+The compute path is libsufb200.so (CUDA, sm_100a) behind the C ABI in
+include/sufb200.h; this package binds it (`_lib`), wraps it (`engine`) and
+mirrors the reference backend interface (`backend`).
+"""
+from ._lib import (  # noqa: F401
+    GROUP_ADD,
+    GROUP_XOR,
+    TRUNC_FAITHFUL_ARS,
+    TRUNC_FAITHFUL_TR,
+    TRUNC_GAPARS,
+    SufB200Error,
+    TruncDesc,
+)
+
+__all__ = ["GROUP_ADD", "GROUP_XOR", "TRUNC_FAITHFUL_TR", "TRUNC_FAITHFUL_ARS", "TRUNC_GAPARS", "SufB200Error",
+           "TruncDesc"]

@@ -1,0 +1,603 @@
+// capi.cu -- the extern "C" boundary of libsufb200.so (include/sufb200.h).
+//
+// Argument validation, context lifetime, error reporting and the host-buffer
+// entry points.  No path here falls back to host evaluation: every
+// evaluation runs on the device or returns an error.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "host_aes.hpp"
+#include "kernels.hpp"
+#include "keygen.hpp"
+#include "primitives.hpp"
+#include "sufb200_internal.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SUFB200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define SUFB200_CHECK_CUDA(expr, what)          \
+  do {                                          \
+    cudaError_t e_ = (expr);                    \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+__global__ void probe_kernel(uint32_t* out) {
+  extern __shared__ __align__(16) uint8_t sufb200_dyn_smem[];
+  if (threadIdx.x == 0) out[0] = static_cast<uint32_t>(__cvta_generic_to_shared(sufb200_dyn_smem));
+}
+
+bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+// Host-side per-context device buffers for the host-buffer entry points.
+struct HostIo {
+  std::mutex mu;
+  cudaStream_t stream = nullptr;
+  uint8_t* d_keys = nullptr;
+  size_t keys_cap = 0;
+  uint64_t* d_xs = nullptr;
+  size_t xs_cap = 0;
+  uint8_t* d_out = nullptr;
+  size_t out_cap = 0;
+};
+
+int grow(void** p, size_t* cap, size_t want) {
+  if (want <= *cap) return 0;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  cudaError_t e = cudaMalloc(p, want);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (host-io buffer)");
+  *cap = want;
+  return 0;
+}
+
+std::mutex g_io_mu;
+std::vector<std::pair<sufb200_ctx, HostIo*>> g_io;
+
+HostIo* io_of(sufb200_ctx ctx, bool create) {
+  std::lock_guard<std::mutex> lk(g_io_mu);
+  for (auto& kv : g_io)
+    if (kv.first == ctx) return kv.second;
+  if (!create) return nullptr;
+  HostIo* io = new HostIo();
+  g_io.emplace_back(ctx, io);
+  return io;
+}
+
+void io_release(sufb200_ctx ctx) {
+  std::lock_guard<std::mutex> lk(g_io_mu);
+  for (size_t i = 0; i < g_io.size(); i++) {
+    if (g_io[i].first == ctx) {
+      HostIo* io = g_io[i].second;
+      if (io->d_keys) cudaFree(io->d_keys);
+      if (io->d_xs) cudaFree(io->d_xs);
+      if (io->d_out) cudaFree(io->d_out);
+      if (io->stream) cudaStreamDestroy(io->stream);
+      delete io;
+      g_io.erase(g_io.begin() + static_cast<long>(i));
+      return;
+    }
+  }
+}
+
+int check_ctx(sufb200_ctx ctx, bool need_prg) {
+  if (!ctx) return fail(SUFB200_ERR_INVALID, "null context");
+  if (ctx->device < 0) return fail(SUFB200_ERR_UNSUPPORTED, "host-only context: no device to evaluate on");
+  if (need_prg && !ctx->prg_ready) return fail(SUFB200_ERR_NOT_READY, "sufb200_prg_init has not been called");
+  cudaError_t e = cudaSetDevice(ctx->device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  return 0;
+}
+
+int myl7_args(sufb200_ctx ctx, int group, int in_bits, const void* keys, size_t key_bytes, const void* xs,
+              int out_bytes, const void* out) {
+  if (group != SUFB200_GROUP_ADD && group != SUFB200_GROUP_XOR) return fail(SUFB200_ERR_INVALID, "bad group");
+  if (in_bits < 1 || in_bits > 64) return fail(SUFB200_ERR_INVALID, "in_bits out of range [1,64]");
+  if (out_bytes < 1 || out_bytes > 8)
+    return fail(SUFB200_ERR_UNSUPPORTED, "out_bytes must be 1..8 (one 16-byte payload chunk, low 8 bytes)");
+  if (key_bytes != sufb200::host::myl7_key_bytes(in_bits, out_bytes))
+    return fail(SUFB200_ERR_KEY, "key_bytes does not match in_bits/out_bytes (myl7 layout, one chunk)");
+  if (!keys || !xs || !out) return fail(SUFB200_ERR_INVALID, "null pointer");
+  if (!aligned8(xs)) return fail(SUFB200_ERR_INVALID, "xs must be 8-byte aligned");
+  if (out_bytes == 8 && !aligned8(out)) return fail(SUFB200_ERR_INVALID, "out must be 8-byte aligned");
+  (void)ctx;
+  return 0;
+}
+
+}  // namespace
+
+namespace sufb200 {
+cudaError_t probe_dyn_smem_base(uint32_t* d_out, cudaStream_t st) {
+  probe_kernel<<<1, 32, 1024, st>>>(d_out);
+  return cudaGetLastError();
+}
+}  // namespace sufb200
+
+extern "C" {
+
+int sufb200_version(void) { return 10000; }
+
+const char* sufb200_last_error(void) { return g_err.c_str(); }
+
+int sufb200_ctx_create(int device, sufb200_ctx* out) {
+  if (!out) return fail(SUFB200_ERR_INVALID, "null out");
+  *out = nullptr;
+  if (device == SUFB200_HOST_ONLY) {
+    auto* ctx = new sufb200_ctx_s();
+    ctx->device = SUFB200_HOST_ONLY;
+    *out = ctx;
+    return SUFB200_OK;
+  }
+  int ndev = 0;
+  cudaError_t e = cudaGetDeviceCount(&ndev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev) return fail(SUFB200_ERR_INVALID, "device index out of range");
+  SUFB200_CHECK_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  cudaDeviceProp prop;
+  SUFB200_CHECK_CUDA(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    return fail(SUFB200_ERR_UNSUPPORTED, "libsufb200 is built for sm_100a (B200); device is sm_" +
+                                             std::to_string(prop.major) + std::to_string(prop.minor));
+  auto* ctx = new sufb200_ctx_s();
+  ctx->device = device;
+  ctx->sm_count = prop.multiProcessorCount;
+  const auto& tabs = sufb200::host::aes_tables();
+  e = cudaMalloc(&ctx->d_t0, 256 * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemcpy(ctx->d_t0, tabs.t0, 256 * sizeof(uint32_t), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->d_status, 2 * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, 2 * sizeof(uint32_t));
+  uint32_t base = 0;
+  if (e == cudaSuccess) e = sufb200::probe_dyn_smem_base(ctx->d_status + 1, nullptr);
+  if (e == cudaSuccess) e = cudaMemcpy(&base, ctx->d_status + 1, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    int rc = cuda_fail(e, "context setup");
+    sufb200_ctx_destroy(ctx);
+    return rc;
+  }
+  if (base > sufb200::kTabBase || sufb200::kTabEnd - base > prop.sharedMemPerBlockOptin) {
+    sufb200_ctx_destroy(ctx);
+    return fail(SUFB200_ERR_UNSUPPORTED, "shared-memory window does not fit the AES table layout (base " +
+                                             std::to_string(base) + ")");
+  }
+  ctx->dyn_base = base;
+  ctx->aes_dyn_bytes = sufb200::kTabEnd - base;
+  *out = ctx;
+  return SUFB200_OK;
+}
+
+int sufb200_ctx_destroy(sufb200_ctx ctx) {
+  if (!ctx) return SUFB200_OK;
+  if (ctx->device < 0) {
+    delete ctx;
+    return SUFB200_OK;
+  }
+  cudaSetDevice(ctx->device);
+  io_release(ctx);
+  if (ctx->d_t0) cudaFree(ctx->d_t0);
+  if (ctx->d_status) cudaFree(ctx->d_status);
+  if (ctx->d_scratch) cudaFree(ctx->d_scratch);
+  delete ctx;
+  return SUFB200_OK;
+}
+
+int sufb200_ctx_sm_count(sufb200_ctx ctx) { return ctx ? ctx->sm_count : 0; }
+
+int sufb200_ctx_sync(sufb200_ctx ctx, void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  SUFB200_CHECK_CUDA(cudaStreamSynchronize(as_stream(stream)), "cudaStreamSynchronize");
+  uint32_t st = 0;
+  SUFB200_CHECK_CUDA(cudaMemcpy(&st, ctx->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost), "read status");
+  if (st) {
+    SUFB200_CHECK_CUDA(cudaMemset(ctx->d_status, 0, sizeof(uint32_t)), "clear status");
+    if (st & sufb200::kStatusSmemLayout) return fail(SUFB200_ERR_CUDA, "kernel found an unexpected shared-memory layout");
+    if (st & sufb200::kStatusBadKeyHeader)
+      return fail(SUFB200_ERR_KEY, "a key header did not match the call (in_bits / chunks / party / payload_len)");
+    return fail(SUFB200_ERR_INVALID, "device reported a bad argument");
+  }
+  return SUFB200_OK;
+}
+
+int sufb200_prg_init(sufb200_ctx ctx, const uint8_t* state, size_t len) {
+  if (!ctx || !state) return fail(SUFB200_ERR_INVALID, "null argument");
+  if (len < 64) return fail(SUFB200_ERR_INVALID, "PRG state needs >= 64 bytes (4 AES-128 keys)");
+  uint32_t w[4][44];
+  for (int j = 0; j < 4; j++) sufb200::host::aes128_expand_words(state + 16 * j, w[j]);
+  for (int h = 0; h < 2; h++)
+    for (int r = 0; r < 11; r++)
+      for (int c = 0; c < 4; c++) {
+        ctx->prg.base[h][r][c] = w[h][4 * r + c];
+        ctx->prg.diff[h][r][c] = w[h][4 * r + c] ^ w[h + 2][4 * r + c];
+      }
+  for (int j = 0; j < 4; j++)
+    for (int r = 0; r < 11; r++)
+      for (int c = 0; c < 4; c++) ctx->prg4.rk[j][r][c] = w[j][4 * r + c];
+  ctx->prg_ready = true;
+  return SUFB200_OK;
+}
+
+size_t sufb200_myl7_key_bytes(int in_bits, int payload_len) {
+  if (in_bits < 1 || in_bits > 64 || payload_len < 1) return 0;
+  return sufb200::host::myl7_key_bytes(in_bits, payload_len);
+}
+
+static sufb200::host::PrgHostKeys host_keys(const sufb200_ctx_s* ctx) {
+  sufb200::host::PrgHostKeys k;
+  for (int j = 0; j < 4; j++)
+    for (int r = 0; r < 11; r++)
+      for (int c = 0; c < 4; c++) k.rk[j][4 * r + c] = ctx->prg4.rk[j][r][c];
+  return k;
+}
+
+int sufb200_myl7_gen(sufb200_ctx ctx, int group, int in_bits, uint64_t alpha, const uint8_t* payload,
+                     int payload_len, const uint8_t* seeds0, const uint8_t* seeds1, uint8_t* key0, uint8_t* key1) {
+  if (!ctx) return fail(SUFB200_ERR_INVALID, "null context");
+  if (!ctx->prg_ready) return fail(SUFB200_ERR_NOT_READY, "sufb200_prg_init has not been called");
+  if (!payload || !seeds0 || !seeds1 || !key0 || !key1) return fail(SUFB200_ERR_INVALID, "null pointer");
+  if (group != SUFB200_GROUP_ADD && group != SUFB200_GROUP_XOR) return fail(SUFB200_ERR_INVALID, "bad group");
+  if (in_bits < 1 || in_bits > 64 || payload_len < 1 || (payload_len + 15) / 16 > 255)
+    return fail(SUFB200_ERR_INVALID, "in_bits / payload_len out of range");
+  const auto k = host_keys(ctx);
+  if (sufb200::host::myl7_gen_pair(k, group == SUFB200_GROUP_ADD, in_bits, alpha, payload, payload_len, seeds0,
+                                   seeds1, key0, key1))
+    return fail(SUFB200_ERR_INVALID, "myl7 keygen rejected its arguments");
+  return SUFB200_OK;
+}
+
+int sufb200_myl7_gen_batch(sufb200_ctx ctx, int group, int in_bits, const uint64_t* alphas, size_t n,
+                           const uint8_t* payload, int payload_len, const uint8_t* seeds0, const uint8_t* seeds1,
+                           uint8_t* keys0, uint8_t* keys1) {
+  if (!ctx) return fail(SUFB200_ERR_INVALID, "null context");
+  if (!ctx->prg_ready) return fail(SUFB200_ERR_NOT_READY, "sufb200_prg_init has not been called");
+  if (n == 0) return SUFB200_OK;
+  if (!alphas || !payload || !seeds0 || !seeds1 || !keys0 || !keys1) return fail(SUFB200_ERR_INVALID, "null pointer");
+  if (group != SUFB200_GROUP_ADD && group != SUFB200_GROUP_XOR) return fail(SUFB200_ERR_INVALID, "bad group");
+  if (in_bits < 1 || in_bits > 64 || payload_len < 1 || (payload_len + 15) / 16 > 255)
+    return fail(SUFB200_ERR_INVALID, "in_bits / payload_len out of range");
+  const auto k = host_keys(ctx);
+  if (sufb200::host::myl7_gen_batch(k, group == SUFB200_GROUP_ADD, in_bits, alphas, n, payload, payload_len, seeds0,
+                                    seeds1, keys0, keys1))
+    return fail(SUFB200_ERR_INVALID, "myl7 batch keygen failed");
+  return SUFB200_OK;
+}
+
+int sufb200_myl7_dcf_eval(sufb200_ctx ctx, int group, int in_bits, const uint8_t* d_keys, size_t key_bytes,
+                          int broadcast, const uint64_t* d_xs, size_t n, int out_bytes, void* d_out, void* stream) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (n == 0) return SUFB200_OK;
+  if (int rc = myl7_args(ctx, group, in_bits, d_keys, key_bytes, d_xs, out_bytes, d_out)) return rc;
+  sufb200::DcfLaunch a{d_keys, key_bytes, d_xs, n, d_out, ctx->d_t0, ctx->d_status, in_bits, out_bytes};
+  SUFB200_CHECK_CUDA(sufb200::launch_myl7_eval(ctx, group, a, broadcast ? 1 : 0, as_stream(stream)),
+                     "myl7 DCF eval launch");
+  return SUFB200_OK;
+}
+
+int sufb200_myl7_dcf_eval_host(sufb200_ctx ctx, int group, int in_bits, const uint8_t* keys, size_t key_bytes,
+                               int broadcast, const uint64_t* xs, size_t n, int out_bytes, uint8_t* outs) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (n == 0) return SUFB200_OK;
+  if (int rc = myl7_args(ctx, group, in_bits, keys, key_bytes, xs, out_bytes, outs)) return rc;
+  // Host-side header check of every key, as the reference adapter does per element.
+  const size_t nk = broadcast ? 1 : n;
+  for (size_t i = 0; i < nk; i++) {
+    const uint8_t* k = keys + i * key_bytes;
+    uint32_t pl;
+    std::memcpy(&pl, k + 4, 4);
+    if (k[0] != in_bits || k[1] != 1 || k[2] > 1 || pl != static_cast<uint32_t>(out_bytes))
+      return fail(SUFB200_ERR_KEY, "key " + std::to_string(i) + ": header does not match in_bits/out_bytes");
+  }
+  HostIo* io = io_of(ctx, true);
+  std::lock_guard<std::mutex> lk(io->mu);
+  if (!io->stream) SUFB200_CHECK_CUDA(cudaStreamCreateWithFlags(&io->stream, cudaStreamNonBlocking), "stream");
+  if (int rc = grow(reinterpret_cast<void**>(&io->d_keys), &io->keys_cap, nk * key_bytes)) return rc;
+  if (int rc = grow(reinterpret_cast<void**>(&io->d_xs), &io->xs_cap, n * 8)) return rc;
+  if (int rc = grow(reinterpret_cast<void**>(&io->d_out), &io->out_cap, n * static_cast<size_t>(out_bytes)))
+    return rc;
+  SUFB200_CHECK_CUDA(cudaMemcpyAsync(io->d_keys, keys, nk * key_bytes, cudaMemcpyHostToDevice, io->stream), "H2D keys");
+  SUFB200_CHECK_CUDA(cudaMemcpyAsync(io->d_xs, xs, n * 8, cudaMemcpyHostToDevice, io->stream), "H2D xs");
+  sufb200::DcfLaunch a{io->d_keys, key_bytes, io->d_xs, n, io->d_out, ctx->d_t0, ctx->d_status, in_bits, out_bytes};
+  SUFB200_CHECK_CUDA(sufb200::launch_myl7_eval(ctx, group, a, broadcast ? 1 : 0, io->stream), "myl7 DCF eval launch");
+  SUFB200_CHECK_CUDA(cudaMemcpyAsync(outs, io->d_out, n * static_cast<size_t>(out_bytes), cudaMemcpyDeviceToHost,
+                                     io->stream),
+                     "D2H outs");
+  return sufb200_ctx_sync(ctx, io->stream);
+}
+
+int sufb200_trunc_gen(int kind, int frac_bits, uint64_t rng_seed, sufb200_trunc_desc* d0, sufb200_trunc_desc* d1,
+                      uint64_t* thetas, uint64_t* r_in_out) {
+  if (!d0 || !d1 || !thetas) return fail(SUFB200_ERR_INVALID, "null pointer");
+  if (sufb200::host::trunc_gen(kind, frac_bits, rng_seed, d0, d1, thetas, r_in_out))
+    return fail(SUFB200_ERR_INVALID, "bad truncation kind / frac_bits");
+  return SUFB200_OK;
+}
+
+int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                              const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y,
+                              uint64_t* d_bools, void* stream) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (!desc || !keys || !key_bytes) return fail(SUFB200_ERR_INVALID, "null pointer");
+  if (desc->nq < 0 || desc->nq > 4) return fail(SUFB200_ERR_UNSUPPORTED, "bundle has more than 4 queries");
+  if (desc->kind < 0 || desc->kind > 2 || desc->party < 0 || desc->party > 1)
+    return fail(SUFB200_ERR_INVALID, "bad kind / party");
+  if (desc->frac_bits < 0 || desc->frac_bits > 64) return fail(SUFB200_ERR_INVALID, "frac_bits out of range");
+  const int idx[5] = {desc->carry_a, desc->carry_b, desc->sign_a, desc->sign_b, desc->wrap_q};
+  for (int v : idx)
+    if (v >= desc->nq) return fail(SUFB200_ERR_INVALID, "query index out of range");
+  if ((desc->carry_a >= 0) != (desc->carry_b >= 0) || (desc->sign_a >= 0) != (desc->sign_b >= 0))
+    return fail(SUFB200_ERR_INVALID, "rotation operands must come in pairs");
+  if (n == 0) return SUFB200_OK;
+  if (!d_xhat || !d_y || !aligned8(d_xhat) || !aligned8(d_y) || (d_bools && !aligned8(d_bools)))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  std::vector<uint8_t> blob;
+  sufb200::TruncLaunch a{};
+  a.desc = *desc;
+  for (int q = 0; q < desc->nq; q++) {
+    const int nb = desc->q_bits[q];
+    if (nb < 1 || nb > 64) return fail(SUFB200_ERR_INVALID, "query in_bits out of range");
+    if (!keys[q] || key_bytes[q] != sufb200::host::myl7_key_bytes(nb, 8))
+      return fail(SUFB200_ERR_KEY, "query " + std::to_string(q) + ": key size does not match an 8-byte myl7 key");
+    const uint8_t* k = keys[q];
+    uint32_t pl;
+    std::memcpy(&pl, k + 4, 4);
+    if (k[0] != nb || k[1] != 1 || k[2] != desc->party || pl != 8)
+      return fail(SUFB200_ERR_KEY, "query " + std::to_string(q) + ": key header does not match the bundle");
+    a.key_off[q] = static_cast<uint32_t>(blob.size());
+    blob.insert(blob.end(), k, k + key_bytes[q]);
+    while (blob.size() % 16) blob.push_back(0);
+  }
+  cudaStream_t st = as_stream(stream);
+  uint8_t* d_keys = nullptr;
+  if (!blob.empty()) {
+    SUFB200_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d_keys), blob.size(), st), "cudaMallocAsync keys");
+    cudaError_t e = cudaMemcpyAsync(d_keys, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+      cudaFreeAsync(d_keys, st);
+      return cuda_fail(e, "H2D bundle keys");
+    }
+  }
+  a.keys = d_keys;
+  a.xhat = d_xhat;
+  a.n = n;
+  a.y = d_y;
+  a.bools = d_bools;
+  a.t0 = ctx->d_t0;
+  a.status = ctx->d_status;
+  cudaError_t e = sufb200::launch_trunc_bundle(ctx, a, st);
+  if (d_keys) cudaFreeAsync(d_keys, st);
+  if (e != cudaSuccess) return cuda_fail(e, "trunc bundle launch");
+  return SUFB200_OK;
+}
+
+int sufb200_trunc_bundle_eval_host(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                                   const size_t* key_bytes, const uint64_t* xhat, size_t n, uint64_t* y,
+                                   uint64_t* bools) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (n == 0) return SUFB200_OK;
+  if (!xhat || !y) return fail(SUFB200_ERR_INVALID, "null host buffer");
+  HostIo* io = io_of(ctx, true);
+  std::lock_guard<std::mutex> lk(io->mu);
+  if (!io->stream) SUFB200_CHECK_CUDA(cudaStreamCreateWithFlags(&io->stream, cudaStreamNonBlocking), "stream");
+  const size_t out_bytes = n * 8 * (bools ? 4 : 1);
+  if (int rc = grow(reinterpret_cast<void**>(&io->d_xs), &io->xs_cap, n * 8)) return rc;
+  if (int rc = grow(reinterpret_cast<void**>(&io->d_out), &io->out_cap, out_bytes)) return rc;
+  uint64_t* d_y = reinterpret_cast<uint64_t*>(io->d_out);
+  uint64_t* d_b = bools ? d_y + n : nullptr;
+  SUFB200_CHECK_CUDA(cudaMemcpyAsync(io->d_xs, xhat, n * 8, cudaMemcpyHostToDevice, io->stream), "H2D xhat");
+  if (int rc = sufb200_trunc_bundle_eval(ctx, desc, keys, key_bytes, io->d_xs, n, d_y, d_b, io->stream)) return rc;
+  SUFB200_CHECK_CUDA(cudaMemcpyAsync(y, d_y, n * 8, cudaMemcpyDeviceToHost, io->stream), "D2H y");
+  if (bools)
+    SUFB200_CHECK_CUDA(cudaMemcpyAsync(bools, d_b, n * 24, cudaMemcpyDeviceToHost, io->stream), "D2H bools");
+  return sufb200_ctx_sync(ctx, io->stream);
+}
+
+// ---- reference GPU-backend formats -----------------------------------------
+
+size_t sufb200_thr_dcf_build(int in_bits, uint64_t alpha, const uint8_t* payload, int payload_len, uint8_t* out) {
+  if (in_bits < 1 || in_bits > 64 || payload_len < 0 || payload_len > 0xFFFF) return 0;
+  return sufb200::host::thr_dcf_build(in_bits, alpha, payload, payload_len, out);
+}
+
+int sufb200_thr_dcf_eval(sufb200_ctx ctx, int in_bits, const uint8_t* d_keys, size_t key_bytes, int broadcast,
+                         const uint64_t* d_xs, size_t n, int out_bytes, void* d_out, void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  if (n == 0) return SUFB200_OK;
+  if (in_bits < 1 || in_bits > 64) return fail(SUFB200_ERR_INVALID, "in_bits out of range");
+  if (out_bytes < 0 || key_bytes != 12 + static_cast<size_t>(out_bytes))
+    return fail(SUFB200_ERR_KEY, "key_bytes must be 12 + out_bytes");
+  if (!d_keys || !d_xs || (!d_out && out_bytes > 0)) return fail(SUFB200_ERR_INVALID, "null pointer");
+  if (!aligned8(d_xs) || (out_bytes == 8 && !aligned8(d_out))) return fail(SUFB200_ERR_INVALID, "misaligned pointer");
+  sufb200::RefFmtLaunch a{d_keys, key_bytes, broadcast ? 1 : 0, d_xs, n, 0, d_out, in_bits, 0, out_bytes,
+                          ctx->d_t0, ctx->d_status};
+  SUFB200_CHECK_CUDA(sufb200::launch_thr_dcf(ctx, a, as_stream(stream)), "threshold DCF launch");
+  return SUFB200_OK;
+}
+
+size_t sufb200_packed_lt_build(int party, uint64_t nonce, int in_bits, const uint64_t* thresholds, int num_thr,
+                               const uint8_t* seed, uint8_t* out) {
+  if (in_bits < 1 || in_bits > 64 || num_thr < 1 || num_thr > 0xFFFF || party < 0 || party > 1) return 0;
+  if (out && (!thresholds || !seed)) return 0;
+  return sufb200::host::packed_lt_build(party, nonce, in_bits, thresholds, num_thr, seed, out);
+}
+
+int sufb200_packed_lt_eval(sufb200_ctx ctx, const uint8_t* d_keys, size_t key_bytes, int broadcast,
+                           const uint64_t* d_xs, size_t n, int in_bits, int out_words, uint64_t idx_base,
+                           uint64_t* d_out, void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  if (n == 0) return SUFB200_OK;
+  if (in_bits < 1 || in_bits > 64 || out_words < 1) return fail(SUFB200_ERR_INVALID, "in_bits / out_words");
+  if (key_bytes < 208 + 8 || key_bytes % 8) return fail(SUFB200_ERR_KEY, "packed key_bytes too small or not 8k");
+  if (!d_keys || !d_xs || !d_out || !aligned8(d_keys) || !aligned8(d_xs) || !aligned8(d_out))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned pointer");
+  sufb200::RefFmtLaunch a{d_keys, key_bytes, broadcast ? 1 : 0, d_xs, n, idx_base, d_out, in_bits, out_words, 0,
+                          ctx->d_t0, ctx->d_status};
+  SUFB200_CHECK_CUDA(sufb200::launch_packed_lt(ctx, a, as_stream(stream)), "packed compare launch");
+  return SUFB200_OK;
+}
+
+size_t sufb200_interval_lut_build(int party, uint64_t nonce, int in_bits, int out_words, const uint64_t* cuts,
+                                  int intervals, const uint64_t* payload, const uint8_t* seed, uint8_t* out) {
+  if (in_bits < 1 || in_bits > 64 || out_words < 1 || out_words > 0xFFFF || intervals < 1 || party < 0 || party > 1)
+    return 0;
+  if (out && (!cuts || !payload || !seed)) return 0;
+  return sufb200::host::interval_lut_build(party, nonce, in_bits, out_words, cuts, intervals, payload, seed, out);
+}
+
+int sufb200_interval_lut_eval(sufb200_ctx ctx, const uint8_t* d_keys, size_t key_bytes, int broadcast,
+                              const uint64_t* d_xs, size_t n, int out_words, uint64_t idx_base, uint64_t* d_out,
+                              void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  if (n == 0) return SUFB200_OK;
+  if (out_words < 1) return fail(SUFB200_ERR_INVALID, "out_words must be >= 1");
+  if (key_bytes < 216 + 24 || key_bytes % 8) return fail(SUFB200_ERR_KEY, "interval key_bytes too small or not 8k");
+  if (!d_keys || !d_xs || !d_out || !aligned8(d_keys) || !aligned8(d_xs) || !aligned8(d_out))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned pointer");
+  sufb200::RefFmtLaunch a{d_keys, key_bytes, broadcast ? 1 : 0, d_xs, n, idx_base, d_out, 0, out_words, 0,
+                          ctx->d_t0, ctx->d_status};
+  SUFB200_CHECK_CUDA(sufb200::launch_interval_lut(ctx, a, as_stream(stream)), "interval LUT launch");
+  return SUFB200_OK;
+}
+
+int sufb200_seed_from_id(uint64_t id, uint64_t tweak, uint8_t* seed16) {
+  if (!seed16) return fail(SUFB200_ERR_INVALID, "null seed");
+  sufb200::host::seed_from_id(id, tweak, seed16);
+  return SUFB200_OK;
+}
+
+// ---- primitives -------------------------------------------------------------
+
+static int prim_rc(cudaError_t e, const char* what) { return e == cudaSuccess ? SUFB200_OK : cuda_fail(e, what); }
+
+static int cur_sm() {
+  int dev = 0, sm = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev);
+  return sm;
+}
+
+int sufb200_beaver_mul(int party, const uint64_t* d_a, const uint64_t* d_b, const uint64_t* d_c,
+                       const uint64_t* d_d_open, const uint64_t* d_e_open, uint64_t* d_out, size_t n, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_a || !d_b || !d_c || !d_d_open || !d_e_open || !d_out) return fail(SUFB200_ERR_INVALID, "null pointer");
+  return prim_rc(sufb200::prim_beaver_mul(cur_sm(), party, d_a, d_b, d_c, d_d_open, d_e_open, d_out, n,
+                                          as_stream(stream)),
+                 "beaver_mul");
+}
+
+int sufb200_beaver_mul_aos(int party, const uint64_t* d_triples, const uint64_t* d_d_open, const uint64_t* d_e_open,
+                           uint64_t* d_out, size_t n, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_triples || !d_d_open || !d_e_open || !d_out) return fail(SUFB200_ERR_INVALID, "null pointer");
+  return prim_rc(sufb200::prim_beaver_mul_aos(cur_sm(), party, d_triples, d_d_open, d_e_open, d_out, n,
+                                              as_stream(stream)),
+                 "beaver_mul_aos");
+}
+
+int sufb200_horner_cubic(const uint64_t* d_x, const uint64_t* d_c0, const uint64_t* d_c1, const uint64_t* d_c2,
+                         const uint64_t* d_c3, uint64_t* d_out, size_t n, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_x || !d_c0 || !d_c1 || !d_c2 || !d_c3 || !d_out) return fail(SUFB200_ERR_INVALID, "null pointer");
+  return prim_rc(sufb200::prim_horner_cubic(cur_sm(), d_x, d_c0, d_c1, d_c2, d_c3, d_out, n, as_stream(stream)),
+                 "horner_cubic");
+}
+
+int sufb200_trunc_postproc(int party, int kind_gapars, int frac_bits, uint64_t r_hi_share, uint64_t m_share,
+                           const uint64_t* d_hatx, const uint64_t* d_arith, size_t arith_stride, int arith_idx,
+                           const uint64_t* d_bools, size_t bool_stride, int carry_idx, int sign_idx, int wrap_idx,
+                           uint64_t* d_out, size_t n, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_arith || !d_out || arith_idx < 0 || static_cast<size_t>(arith_idx) >= arith_stride)
+    return fail(SUFB200_ERR_INVALID, "bad arith operand");
+  return prim_rc(sufb200::prim_trunc_postproc(cur_sm(), party, kind_gapars, frac_bits, r_hi_share, m_share, d_hatx,
+                                              d_arith, arith_stride, arith_idx, d_bools, bool_stride, carry_idx,
+                                              sign_idx, wrap_idx, d_out, n, as_stream(stream)),
+                 "trunc_postproc");
+}
+
+int sufb200_add_rout_aos(uint64_t* d_out, size_t elems, int out_words, const uint64_t* r_out, size_t r_out_words,
+                         void* stream) {
+  if (elems == 0) return SUFB200_OK;
+  if (!d_out || !r_out || out_words < 1) return fail(SUFB200_ERR_INVALID, "bad argument");
+  if (out_words > 8 || r_out_words > 8) return fail(SUFB200_ERR_UNSUPPORTED, "add_rout_aos supports <= 8 words");
+  return prim_rc(sufb200::prim_add_rout_aos(cur_sm(), d_out, elems, out_words, r_out, r_out_words, as_stream(stream)),
+                 "add_rout_aos");
+}
+
+int sufb200_row_sum(const uint64_t* d_mat, int rows, int cols, const int* d_valid_lens, uint64_t* d_out_rows,
+                    void* stream) {
+  if (rows <= 0) return SUFB200_OK;
+  if (!d_mat || !d_out_rows || cols < 0) return fail(SUFB200_ERR_INVALID, "bad argument");
+  return prim_rc(sufb200::prim_row_sum(cur_sm(), d_mat, rows, cols, d_valid_lens, d_out_rows, as_stream(stream)),
+                 "row_sum");
+}
+
+int sufb200_row_sum_ragged(const uint64_t* d_vals, const int* d_row_offsets, int rows, uint64_t* d_out_rows,
+                           void* stream) {
+  if (rows <= 0) return SUFB200_OK;
+  if (!d_vals || !d_row_offsets || !d_out_rows) return fail(SUFB200_ERR_INVALID, "bad argument");
+  return prim_rc(sufb200::prim_row_sum_ragged(cur_sm(), d_vals, d_row_offsets, rows, d_out_rows, as_stream(stream)),
+                 "row_sum_ragged");
+}
+
+int sufb200_row_variance(const uint64_t* d_mat, const uint64_t* d_mean, int rows, int cols, const int* d_valid_lens,
+                         uint64_t* d_out_rows, void* stream) {
+  if (rows <= 0) return SUFB200_OK;
+  if (!d_mat || !d_mean || !d_out_rows || cols < 0) return fail(SUFB200_ERR_INVALID, "bad argument");
+  return prim_rc(sufb200::prim_row_variance(cur_sm(), d_mat, d_mean, rows, cols, d_valid_lens, d_out_rows,
+                                            as_stream(stream)),
+                 "row_variance");
+}
+
+int sufb200_row_broadcast_mul(int party, const uint64_t* d_A, const uint64_t* d_B_rows, const uint64_t* d_C,
+                              const uint64_t* d_d_open, const uint64_t* d_e_open_rows, int rows, int cols,
+                              const int* d_valid_lens, uint64_t* d_out, void* stream) {
+  if (rows <= 0 || cols <= 0) return SUFB200_OK;
+  if (!d_A || !d_B_rows || !d_C || !d_d_open || !d_e_open_rows || !d_out) return fail(SUFB200_ERR_INVALID, "null");
+  return prim_rc(sufb200::prim_row_broadcast_mul(cur_sm(), party, d_A, d_B_rows, d_C, d_d_open, d_e_open_rows, rows,
+                                                 cols, d_valid_lens, d_out, as_stream(stream)),
+                 "row_broadcast_mul");
+}
+
+int sufb200_pack_eff_bits(const uint64_t* d_in, int eff_bits, uint64_t* d_packed, size_t n, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_in || !d_packed || eff_bits < 1 || eff_bits > 64) return fail(SUFB200_ERR_INVALID, "bad argument");
+  return prim_rc(sufb200::prim_pack_eff_bits(cur_sm(), d_in, eff_bits, d_packed, n, as_stream(stream)), "pack");
+}
+
+int sufb200_unpack_eff_bits(const uint64_t* d_packed, int eff_bits, uint64_t* d_out, size_t n, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_packed || !d_out || eff_bits < 1 || eff_bits > 64) return fail(SUFB200_ERR_INVALID, "bad argument");
+  return prim_rc(sufb200::prim_unpack_eff_bits(cur_sm(), d_packed, eff_bits, d_out, n, as_stream(stream)), "unpack");
+}
+
+int sufb200_unpack_add_mod(const uint64_t* d_local, const uint64_t* d_packed_remote, int eff_bits, uint64_t* d_out,
+                           size_t n, int ring_bits, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_local || !d_packed_remote || !d_out || eff_bits < 1 || eff_bits > 64 || ring_bits < 1 || ring_bits > 64)
+    return fail(SUFB200_ERR_INVALID, "bad argument");
+  return prim_rc(sufb200::prim_unpack_add_mod(cur_sm(), d_local, d_packed_remote, eff_bits, d_out, n, ring_bits,
+                                              as_stream(stream)),
+                 "unpack_add_mod");
+}
+
+int sufb200_host_mt19937_64(uint64_t seed, uint64_t* out, size_t n) {
+  if (!out && n) return fail(SUFB200_ERR_INVALID, "null out");
+  std::mt19937_64 rng(seed);
+  for (size_t i = 0; i < n; i++) out[i] = rng();
+  return SUFB200_OK;
+}
+
+}  // extern "C"

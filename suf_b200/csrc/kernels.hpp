@@ -1,0 +1,65 @@
+// kernels.hpp -- launch helpers shared between the kernel translation units
+// and the C ABI (capi.cu).  Internal to the library.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "sufb200_internal.cuh"
+
+namespace sufb200 {
+
+struct DcfLaunch {
+  const uint8_t* keys;  // device: [n][key_bytes] or one key (broadcast)
+  size_t key_bytes;
+  const uint64_t* xs;  // device [n]
+  size_t n;
+  void* out;  // device [n][out_bytes]
+  const uint32_t* t0;
+  uint32_t* status;
+  int in_bits;
+  int out_bytes;
+};
+
+cudaError_t launch_myl7_eval(const sufb200_ctx_s* ctx, int group, const DcfLaunch& a, int broadcast,
+                             cudaStream_t st);
+
+// Fused truncation bundle (trunc_bundle.cu).
+struct TruncLaunch {
+  sufb200_trunc_desc desc;
+  const uint8_t* keys;       // device: concatenated per-query broadcast keys
+  uint32_t key_off[4];       // byte offset of query q's key inside `keys`
+  const uint64_t* xhat;      // device [n]
+  size_t n;
+  uint64_t* y;               // device [n]
+  uint64_t* bools;           // device [n][3] (carry, sign, wrap) or nullptr
+  const uint32_t* t0;
+  uint32_t* status;
+};
+cudaError_t launch_trunc_bundle(const sufb200_ctx_s* ctx, const TruncLaunch& a, cudaStream_t st);
+
+// Reference GPU-backend key formats (ref_formats.cu).
+struct RefFmtLaunch {
+  const uint8_t* keys;
+  size_t key_bytes;
+  int broadcast;
+  const uint64_t* xs;
+  size_t n;
+  uint64_t idx_base;
+  void* out;
+  int in_bits;
+  int out_words;  // packed / LUT
+  int out_bytes;  // threshold DCF
+  const uint32_t* t0;
+  uint32_t* status;
+};
+cudaError_t launch_thr_dcf(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
+cudaError_t launch_packed_lt(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
+cudaError_t launch_interval_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
+
+// Probe of the dynamic shared-memory base (capi.cu uses it at context setup).
+cudaError_t probe_dyn_smem_base(uint32_t* d_out, cudaStream_t st);
+
+}  // namespace sufb200

@@ -1,0 +1,241 @@
+// ref_formats.cu -- the reference GPU backend's own key formats on sm_100a.
+//
+// Threshold "DCF" (DcfKeyHeader), packed multi-threshold compare
+// (PackedCmpKeyHeader) and interval LUT (IntervalKeyHeader) blobs of
+// cuda/pfss_backend_gpu.cu:69-94, evaluated with the counter layout of the
+// reference kernels (cuda/pfss_kernels.cu:240-719): one AES-128 block masks
+// two output words, ctr = nonce ^ (idx << 32) ^ (...), block = [ctr LE][0^8].
+// The AES runs on the shared-memory T-table engine; broadcast keys keep
+// their round keys, thresholds / cutpoints and payload rows in shared memory.
+#include "aes_smem.cuh"
+#include "kernels.hpp"
+
+namespace sufb200 {
+
+namespace {
+
+constexpr uint32_t kStageBytes = 48u * 1024u;  // broadcast-key staging budget
+
+__device__ __forceinline__ uint64_t mask_bits(int bits) {
+  return bits <= 0 ? 0ull : (bits >= 64 ? ~0ull : ((1ull << bits) - 1ull));
+}
+
+__device__ __forceinline__ Blk ctr_block(uint64_t ctr) {
+  Blk b;
+  b.w[0] = static_cast<uint32_t>(ctr);
+  b.w[1] = static_cast<uint32_t>(ctr >> 32);
+  b.w[2] = 0;
+  b.w[3] = 0;
+  return b;
+}
+
+// ---- threshold DCF (no AES; HBM-bound) ------------------------------------
+__device__ __forceinline__ uint32_t ldb32(const uint8_t* p) {
+  return static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8) | (static_cast<uint32_t>(p[2]) << 16) |
+         (static_cast<uint32_t>(p[3]) << 24);
+}
+
+__global__ void thr_dcf_kernel(const RefFmtLaunch a) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const uint64_t m = mask_bits(a.in_bits);
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    const uint8_t* k = a.keys + (a.broadcast ? 0 : i * a.key_bytes);
+    const uint32_t h = ldb32(k);
+    const uint64_t alpha = static_cast<uint64_t>(ldb32(k + 4)) | (static_cast<uint64_t>(ldb32(k + 8)) << 32);
+    if ((h & 0xFFFFu) != static_cast<uint32_t>(a.in_bits) || (h >> 16) != static_cast<uint32_t>(a.out_bytes)) {
+      atomicOr(a.status, kStatusBadKeyHeader);
+    }
+    const bool lt = (a.xs[i] & m) < (alpha & m);
+    uint8_t* o = reinterpret_cast<uint8_t*>(a.out) + i * static_cast<size_t>(a.out_bytes);
+    if (a.out_bytes == 8) {
+      uint64_t p = 0;
+      if (lt)
+        p = static_cast<uint64_t>(ldb32(k + 12)) | (static_cast<uint64_t>(ldb32(k + 16)) << 32);
+      reinterpret_cast<uint64_t*>(a.out)[i] = p;
+    } else {
+      for (int b = 0; b < a.out_bytes; b++) o[b] = lt ? k[12 + b] : 0;
+    }
+  }
+}
+
+// ---- packed compare ----------------------------------------------------------
+__device__ __forceinline__ uint64_t packed_word(int wi, uint64_t x, int num_thr, bool sorted, int pos,
+                                                const uint64_t* thr, uint64_t m) {
+  const int base = wi * 64;
+  const int lim = base + 64 < num_thr ? base + 64 : num_thr;
+  uint64_t word = 0;
+  if (sorted) {
+    const int len = lim - base;
+    if (len > 0) {
+      const uint64_t bits = len >= 64 ? ~0ull : ((1ull << len) - 1ull);
+      if (pos <= base) word = bits;
+      else if (pos >= lim) word = 0;
+      else word = bits ^ ((1ull << (pos - base)) - 1ull);
+    }
+  } else {
+    for (int b = base; b < lim; b++)
+      if (x < (thr[b] & m)) word |= 1ull << (b - base);
+  }
+  return word;
+}
+
+__global__ void __launch_bounds__(kAesThreads, 1) packed_lt_kernel(const RefFmtLaunch a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    return;
+  }
+  uint32_t* s_rk = reinterpret_cast<uint32_t*>(smem);                 // 176 B
+  uint64_t* s_thr = reinterpret_cast<uint64_t*>(smem + 256);          // staged thresholds
+  bool thr_in_smem = false;
+  if (a.broadcast) {
+    const int num_thr = static_cast<int>(reinterpret_cast<const uint16_t*>(a.keys)[1]);
+    thr_in_smem = 8u * static_cast<uint32_t>(num_thr) <= kStageBytes;
+    for (int i = threadIdx.x; i < 44; i += blockDim.x) s_rk[i] = reinterpret_cast<const uint32_t*>(a.keys + 32)[i];
+    if (thr_in_smem)
+      for (int i = threadIdx.x; i < num_thr; i += blockDim.x)
+        s_thr[i] = reinterpret_cast<const uint64_t*>(a.keys + 208)[i];
+  }
+  aes_fill_tables(a.t0);
+  __syncthreads();
+  const uint32_t lb = lane_base();
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    const uint8_t* k = a.keys + (a.broadcast ? 0 : i * a.key_bytes);
+    const uint64_t h = *reinterpret_cast<const uint64_t*>(k);
+    const int in_bits = static_cast<int>(h & 0xFFFF);
+    const int num_thr = static_cast<int>((h >> 16) & 0xFFFF);
+    const uint32_t party = static_cast<uint32_t>((h >> 32) & 0xFF);
+    const bool sorted = ((h >> 40) & 1ull) != 0;
+    const int words = (num_thr + 63) / 64;
+    uint64_t* out = reinterpret_cast<uint64_t*>(a.out) + i * static_cast<size_t>(a.out_words);
+    if (words != a.out_words || in_bits != a.in_bits || 208u + 8u * static_cast<size_t>(num_thr) > a.key_bytes) {
+      atomicOr(a.status, kStatusBadKeyHeader);
+      for (int w = 0; w < a.out_words; w++) out[w] = 0;
+      continue;
+    }
+    const uint64_t nonce = *reinterpret_cast<const uint64_t*>(k + 8);
+    const uint32_t* rk = a.broadcast ? s_rk : reinterpret_cast<const uint32_t*>(k + 32);
+    const uint64_t* thr = (a.broadcast && thr_in_smem) ? s_thr : reinterpret_cast<const uint64_t*>(k + 208);
+    const uint64_t m = mask_bits(in_bits);
+    const uint64_t x = a.xs[i] & m;
+    int pos = 0;
+    if (sorted) {
+      int lo = 0, hi = num_thr;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (x < (thr[mid] & m)) hi = mid; else lo = mid + 1;
+      }
+      pos = lo;
+    }
+    const uint64_t idx = a.idx_base + i;
+    for (int w = 0; w < words; w += 2) {
+      const uint64_t w0 = packed_word(w, x, num_thr, sorted, pos, thr, m);
+      const uint64_t w1 = (w + 1 < words) ? packed_word(w + 1, x, num_thr, sorted, pos, thr, m) : 0ull;
+      const Blk ks = aes_encrypt_smem_rk(ctr_block(nonce ^ (idx << 32) ^ static_cast<uint64_t>(w / 2)), lb, rk);
+      const uint64_t ks0 = (static_cast<uint64_t>(ks.w[1]) << 32) | ks.w[0];
+      const uint64_t ks1 = (static_cast<uint64_t>(ks.w[3]) << 32) | ks.w[2];
+      out[w] = party == 0 ? ks0 : (w0 ^ ks0);
+      if (w + 1 < words) out[w + 1] = party == 0 ? ks1 : (w1 ^ ks1);
+    }
+  }
+}
+
+// ---- interval LUT --------------------------------------------------------
+__global__ void __launch_bounds__(kAesThreads, 1) interval_lut_kernel(const RefFmtLaunch a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    return;
+  }
+  uint32_t* s_rk = reinterpret_cast<uint32_t*>(smem);
+  uint64_t* s_tab = reinterpret_cast<uint64_t*>(smem + 256);  // cuts then payload
+  bool tab_in_smem = false;
+  if (a.broadcast) {
+    const uint64_t h = *reinterpret_cast<const uint64_t*>(a.keys);
+    const uint32_t ivs = static_cast<uint32_t>(h >> 32), ow = static_cast<uint32_t>((h >> 16) & 0xFFFF);
+    const size_t words = static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow;
+    tab_in_smem = 216u + 8u * words <= a.key_bytes && 8u * words <= kStageBytes;
+    for (int i = threadIdx.x; i < 44; i += blockDim.x) s_rk[i] = reinterpret_cast<const uint32_t*>(a.keys + 40)[i];
+    if (tab_in_smem)
+      for (size_t i = threadIdx.x; i < words; i += blockDim.x)
+        s_tab[i] = reinterpret_cast<const uint64_t*>(a.keys + 216)[i];
+  }
+  aes_fill_tables(a.t0);
+  __syncthreads();
+  const uint32_t lb = lane_base();
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    const uint8_t* k = a.keys + (a.broadcast ? 0 : i * a.key_bytes);
+    const uint64_t h = *reinterpret_cast<const uint64_t*>(k);
+    const int in_bits = static_cast<int>(h & 0xFFFF);
+    const int ow = static_cast<int>((h >> 16) & 0xFFFF);
+    const uint32_t ivs = static_cast<uint32_t>(h >> 32);
+    const uint32_t party = k[8];
+    uint64_t* out = reinterpret_cast<uint64_t*>(a.out) + i * static_cast<size_t>(a.out_words);
+    const size_t need = 216u + 8u * (static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow);
+    if (ow != a.out_words || ivs == 0 || need > a.key_bytes) {
+      atomicOr(a.status, kStatusBadKeyHeader);
+      for (int w = 0; w < a.out_words; w++) out[w] = 0;
+      continue;
+    }
+    const uint64_t nonce = *reinterpret_cast<const uint64_t*>(k + 16);
+    const uint32_t* rk = a.broadcast ? s_rk : reinterpret_cast<const uint32_t*>(k + 40);
+    const uint64_t* cuts = (a.broadcast && tab_in_smem) ? s_tab : reinterpret_cast<const uint64_t*>(k + 216);
+    const uint64_t* pay = cuts + ivs + 1;
+    const uint64_t m = mask_bits(in_bits);
+    const uint64_t x = a.xs[i] & m;
+    int iv = static_cast<int>(ivs) - 1;
+    if (ivs > 1) {
+      int lo = 0, hi = static_cast<int>(ivs);
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if ((cuts[mid] & m) <= x) lo = mid + 1; else hi = mid;
+      }
+      iv = lo - 1;
+      if (iv < 0) iv = 0;
+      if (iv >= static_cast<int>(ivs)) iv = static_cast<int>(ivs) - 1;
+    }
+    const uint64_t idx = a.idx_base + i;
+    const uint64_t* row = pay + static_cast<size_t>(iv) * ow;
+    for (int w = 0; w < ow; w += 2) {
+      const uint64_t ctr = nonce ^ (idx << 32) ^ (static_cast<uint64_t>(iv) * static_cast<uint64_t>(ow) + w);
+      const Blk ks = aes_encrypt_smem_rk(ctr_block(ctr), lb, rk);
+      const uint64_t ks0 = (static_cast<uint64_t>(ks.w[1]) << 32) | ks.w[0];
+      const uint64_t ks1 = (static_cast<uint64_t>(ks.w[3]) << 32) | ks.w[2];
+      out[w] = party == 0 ? ks0 : (row[w] - ks0);
+      if (w + 1 < ow) out[w + 1] = party == 0 ? ks1 : (row[w + 1] - ks1);
+    }
+  }
+}
+
+int grid_for(const sufb200_ctx_s* ctx, size_t n, int threads, int per_sm) {
+  const size_t want = (n + threads - 1) / threads;
+  const size_t cap = static_cast<size_t>(ctx->sm_count) * per_sm;
+  return static_cast<int>(want < cap ? (want ? want : 1) : cap);
+}
+
+}  // namespace
+
+cudaError_t launch_thr_dcf(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st) {
+  thr_dcf_kernel<<<grid_for(ctx, a.n, 256, 8), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_packed_lt(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(packed_lt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  packed_lt_kernel<<<grid_for(ctx, a.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_interval_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(interval_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  interval_lut_kernel<<<grid_for(ctx, a.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace sufb200

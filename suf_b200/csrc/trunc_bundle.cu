@@ -1,0 +1,165 @@
+// trunc_bundle.cu -- fused truncation / ARS bundle for sm_100a.
+//
+// One launch evaluates every raw predicate query of a FaithfulTR /
+// FaithfulARS / GapARS gate (broadcast myl7 keys, AddU64 payload 1), folds
+// the additive boolean plan of composite_eval_batch_backend
+// (include/gates/composite_fss.hpp:1385-1638) and applies the postproc hook
+// (include/gates/postproc_hooks.hpp:173-376), writing one y share per
+// element.  The reference runs the same steps as nq separate GPU calls, each
+// followed by a device-to-host copy, then two OpenMP host loops.
+#include "dcf_walk.cuh"
+#include "kernels.hpp"
+
+namespace sufb200 {
+
+namespace {
+
+struct QueryKeySmem {
+  uint4 cw_s[64];
+  uint64_t cw_v[64];
+  uint32_t cw_t[64];
+  uint4 seed;
+  uint64_t np1_lo;
+  uint32_t ok;
+  uint32_t pad;
+};
+static_assert(4 * sizeof(QueryKeySmem) < kTabBase - 4096, "staging must fit below the tables");
+
+__device__ __forceinline__ uint32_t ldb32(const uint8_t* p) {
+  return static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8) | (static_cast<uint32_t>(p[2]) << 16) |
+         (static_cast<uint32_t>(p[3]) << 24);
+}
+__device__ __forceinline__ uint64_t ldb64(const uint8_t* p) {
+  return static_cast<uint64_t>(ldb32(p)) | (static_cast<uint64_t>(ldb32(p + 4)) << 32);
+}
+
+__device__ __forceinline__ uint64_t pick4(int q, uint64_t p0, uint64_t p1, uint64_t p2, uint64_t p3) {
+  return q == 0 ? p0 : (q == 1 ? p1 : (q == 2 ? p2 : p3));
+}
+
+__global__ void __launch_bounds__(kAesThreads, 1) trunc_bundle_kernel(const PrgParams prg, const TruncLaunch a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    return;
+  }
+  const sufb200_trunc_desc& d = a.desc;
+  QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);
+  for (int q = 0; q < d.nq; q++) {
+    const uint8_t* k = a.keys + a.key_off[q];
+    const int nb = d.q_bits[q];
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+      const uint8_t* c = k + 24 + 33 * i;
+      ks[q].cw_s[i] = make_uint4(ldb32(c), ldb32(c + 4), ldb32(c + 8), ldb32(c + 12));
+      ks[q].cw_v[i] = ldb64(c + 16);
+      ks[q].cw_t[i] = c[32];
+    }
+    if (threadIdx.x == 0) {
+      const uint64_t hdr = ldb64(k);
+      const bool ok = (hdr & 0xFF) == static_cast<uint64_t>(nb) && ((hdr >> 8) & 0xFF) == 1 &&
+                      ((hdr >> 16) & 0xFF) == static_cast<uint64_t>(d.party) && (hdr >> 32) == 8;
+      ks[q].seed = make_uint4(ldb32(k + 8), ldb32(k + 12), ldb32(k + 16), ldb32(k + 20) & 0x7FFFFFFFu);
+      ks[q].np1_lo = ldb64(k + 24 + 33 * nb);
+      ks[q].ok = ok ? 1u : 0u;
+    }
+  }
+  aes_fill_tables(a.t0);
+  __syncthreads();
+  for (int q = 0; q < d.nq; q++) {
+    if (!ks[q].ok) {
+      if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.status, kStatusBadKeyHeader);
+      return;
+    }
+  }
+  const uint32_t lb = lane_base();
+  const uint32_t party = static_cast<uint32_t>(d.party);
+  const int f = d.frac_bits;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    const uint64_t xh = a.xhat[i];
+    uint64_t pr[4] = {0, 0, 0, 0};
+#pragma unroll 1
+    for (int q = 0; q < d.nq; q++) {
+      const int nb = d.q_bits[q];
+      const uint64_t x = nb >= 64 ? xh : (xh & ((1ull << nb) - 1ull));
+      const QueryKeySmem& K = ks[q];
+      Blk s;
+      s.w[0] = K.seed.x;
+      s.w[1] = K.seed.y;
+      s.w[2] = K.seed.z;
+      s.w[3] = K.seed.w;
+      uint32_t t = party;
+      uint64_t v = 0;
+      for (int lv = 0; lv < nb; lv++) {
+        CwLevel cw;
+        const uint4 cs = K.cw_s[lv];
+        cw.s.w[0] = cs.x;
+        cw.s.w[1] = cs.y;
+        cw.s.w[2] = cs.z;
+        cw.s.w[3] = cs.w;
+        cw.v = K.cw_v[lv];
+        cw.t = K.cw_t[lv];
+        walk_level<SUFB200_GROUP_ADD>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (nb - 1 - lv)) & 1ull), party,
+                                      cw);
+      }
+      v = walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, K.np1_lo);
+      if (q == 0) pr[0] = v;
+      else if (q == 1) pr[1] = v;
+      else if (q == 2) pr[2] = v;
+      else pr[3] = v;
+    }
+    const uint64_t one = party == 0 ? 1ull : 0ull;
+    uint64_t carry = 0, sign = 0, wrap = 0;
+    if (d.carry_a >= 0) {
+      const uint64_t qa = pick4(d.carry_a, pr[0], pr[1], pr[2], pr[3]);
+      const uint64_t qb = pick4(d.carry_b, pr[0], pr[1], pr[2], pr[3]);
+      carry = one - ((qb - qa) + d.carry_w);
+    }
+    if (d.sign_a >= 0) {
+      const uint64_t qa = pick4(d.sign_a, pr[0], pr[1], pr[2], pr[3]);
+      const uint64_t qb = pick4(d.sign_b, pr[0], pr[1], pr[2], pr[3]);
+      sign = (qb - qa) + d.sign_w;
+    }
+    if (d.wrap_q >= 0) wrap = pick4(d.wrap_q, pr[0], pr[1], pr[2], pr[3]);
+    uint64_t y;
+    if (d.kind == SUFB200_TRUNC_GAPARS) {
+      // GapArsPostProc::run_batch, postproc_hooks.hpp:324-375
+      const uint64_t hb = xh + (1ull << 62);
+      uint64_t top = 0;
+      if (party == 0 && f >= 0 && f < 64) top = f == 0 ? hb : (hb >> f);
+      y = d.haty + top - d.r_hi - carry;
+      if (f > 0 && f < 64 && ((hb >> 63) & 1ull) == 0) y += d.m;
+      if (party == 0) y -= (f >= 0 && f <= 62) ? (1ull << (62 - f)) : 0ull;
+    } else {
+      // FaithfulTruncPostProc / FaithfulArsPostProc::run_batch, postproc_hooks.hpp:198-290
+      const uint64_t top = (party == 0 && f < 64) ? (xh >> f) : 0ull;
+      const uint64_t modulus = (f <= 0 || f >= 64) ? 0ull : (1ull << (64 - f));
+      y = d.haty + top - d.r_hi - carry;
+      if (modulus) y += wrap * modulus;
+      if (d.kind == SUFB200_TRUNC_FAITHFUL_ARS) {
+        const uint64_t sign_mask = (f <= 0 || f >= 64) ? 0ull : (~0ull << (64 - f));
+        y += sign * sign_mask;
+      }
+    }
+    a.y[i] = y;
+    if (a.bools) {
+      a.bools[3 * i + 0] = carry;
+      a.bools[3 * i + 1] = sign;
+      a.bools[3 * i + 2] = wrap;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_trunc_bundle(const sufb200_ctx_s* ctx, const TruncLaunch& a, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(trunc_bundle_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  const size_t want = (a.n + kAesThreads - 1) / kAesThreads;
+  const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
+  trunc_bundle_kernel<<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a);
+  return cudaGetLastError();
+}
+
+}  // namespace sufb200

@@ -1,0 +1,254 @@
+"""Python host side of the engine: a thin object layer over the C ABI.
+
+Device buffers are torch tensors on the context's device (PyTorch supplies
+device memory and streams; the arithmetic runs in libsufb200's kernels).
+Host buffers are numpy arrays.  Every call checks the C status code and
+raises `SufB200Error` on failure -- there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import GROUP_ADD, GROUP_XOR, SufB200Error, TruncDesc, check  # noqa: F401
+
+
+def _np_ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def _t_ptr(t) -> int:
+    return int(t.data_ptr())
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        import torch
+
+        return int(torch.cuda.current_stream().cuda_stream) or None
+    if isinstance(stream, int):
+        return stream or None
+    return int(stream.cuda_stream) or None
+
+
+def host_mt19937_64(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.uint64)
+    check(_lib.lib().sufb200_host_mt19937_64(C.c_uint64(seed), _np_ptr(out) if n else None, n))
+    return out
+
+
+def myl7_key_bytes(in_bits: int, payload_len: int) -> int:
+    return int(_lib.lib().sufb200_myl7_key_bytes(in_bits, payload_len))
+
+
+class Context:
+    """One engine context: a device, the AES tables and the PRG keys."""
+
+    def __init__(self, device: int = 0):
+        self._L = _lib.lib()
+        h = C.c_void_p()
+        check(self._L.sufb200_ctx_create(device, C.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self) -> None:
+        if self.h:
+            self._L.sufb200_ctx_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def sm_count(self) -> int:
+        return int(self._L.sufb200_ctx_sm_count(self.h))
+
+    def sync(self, stream=None) -> None:
+        check(self._L.sufb200_ctx_sync(self.h, _stream_ptr(stream)))
+
+    # -- myl7 PRG-tree DCF --------------------------------------------------
+    def prg_init(self, state) -> None:
+        s = np.ascontiguousarray(np.frombuffer(bytes(state), dtype=np.uint8) if isinstance(state, (bytes, bytearray))
+                                 else state, dtype=np.uint8)
+        check(self._L.sufb200_prg_init(self.h, _np_ptr(s), s.size))
+
+    def myl7_gen(self, group: int, in_bits: int, alpha: int, payload: bytes, seeds0, seeds1):
+        kb = myl7_key_bytes(in_bits, len(payload))
+        k0 = np.zeros(kb, dtype=np.uint8)
+        k1 = np.zeros(kb, dtype=np.uint8)
+        pl = np.frombuffer(bytes(payload), dtype=np.uint8).copy()
+        s0 = np.ascontiguousarray(seeds0, dtype=np.uint8)
+        s1 = np.ascontiguousarray(seeds1, dtype=np.uint8)
+        check(self._L.sufb200_myl7_gen(self.h, group, in_bits, C.c_uint64(alpha & (2**64 - 1)), _np_ptr(pl),
+                                       len(payload), _np_ptr(s0), _np_ptr(s1), _np_ptr(k0), _np_ptr(k1)))
+        return k0, k1
+
+    def myl7_gen_batch(self, group: int, in_bits: int, alphas: np.ndarray, payload: bytes, seeds0: np.ndarray,
+                       seeds1: np.ndarray):
+        alphas = np.ascontiguousarray(alphas, dtype=np.uint64)
+        n = alphas.size
+        kb = myl7_key_bytes(in_bits, len(payload))
+        keys0 = np.empty((n, kb), dtype=np.uint8)
+        keys1 = np.empty((n, kb), dtype=np.uint8)
+        pl = np.frombuffer(bytes(payload), dtype=np.uint8).copy()
+        s0 = np.ascontiguousarray(seeds0, dtype=np.uint8)
+        s1 = np.ascontiguousarray(seeds1, dtype=np.uint8)
+        check(self._L.sufb200_myl7_gen_batch(self.h, group, in_bits, _np_ptr(alphas), n, _np_ptr(pl), len(payload),
+                                             _np_ptr(s0), _np_ptr(s1), _np_ptr(keys0), _np_ptr(keys1)))
+        return keys0, keys1
+
+    def myl7_eval(self, group: int, in_bits: int, d_keys, key_bytes: int, broadcast: bool, d_xs, out_bytes: int,
+                  d_out=None, stream=None):
+        import torch
+
+        n = d_xs.numel()
+        if d_out is None:
+            d_out = torch.empty(n * out_bytes, dtype=torch.uint8, device=d_xs.device)
+        check(self._L.sufb200_myl7_dcf_eval(self.h, group, in_bits, _t_ptr(d_keys), key_bytes, int(broadcast),
+                                            _t_ptr(d_xs), n, out_bytes, _t_ptr(d_out), _stream_ptr(stream)))
+        return d_out
+
+    def myl7_eval_host(self, group: int, in_bits: int, keys: np.ndarray, key_bytes: int, broadcast: bool,
+                       xs: np.ndarray, out_bytes: int, outs: np.ndarray | None = None) -> np.ndarray:
+        keys = np.ascontiguousarray(keys, dtype=np.uint8)
+        xs = np.ascontiguousarray(xs, dtype=np.uint64)
+        if outs is None:
+            outs = np.zeros((xs.size, out_bytes), dtype=np.uint8)
+        check(self._L.sufb200_myl7_dcf_eval_host(self.h, group, in_bits, _np_ptr(keys), key_bytes, int(broadcast),
+                                                 _np_ptr(xs), xs.size, out_bytes, _np_ptr(outs)))
+        return outs
+
+    # -- truncation bundles ---------------------------------------------------
+    @staticmethod
+    def trunc_gen(kind: int, frac_bits: int, seed: int):
+        d0, d1 = TruncDesc(), TruncDesc()
+        thetas = np.zeros(4, dtype=np.uint64)
+        r_in = C.c_uint64()
+        check(_lib.lib().sufb200_trunc_gen(kind, frac_bits, C.c_uint64(seed), C.byref(d0), C.byref(d1),
+                                           _np_ptr(thetas), C.byref(r_in)))
+        return int(r_in.value), d0, d1, thetas
+
+    def trunc_bundle_eval(self, desc: TruncDesc, keys: Sequence[np.ndarray], d_xhat, d_y=None, d_bools=None,
+                          stream=None):
+        import torch
+
+        n = d_xhat.numel()
+        if d_y is None:
+            d_y = torch.empty(n, dtype=torch.int64, device=d_xhat.device)
+        nq = int(desc.nq)
+        karr = [np.ascontiguousarray(k, dtype=np.uint8) for k in keys[:nq]]
+        ptrs = (C.c_void_p * 4)(*[_np_ptr(k) for k in karr], *([None] * (4 - nq)))
+        sizes = (C.c_size_t * 4)(*[k.size for k in karr], *([0] * (4 - nq)))
+        check(self._L.sufb200_trunc_bundle_eval(self.h, C.byref(desc), C.cast(ptrs, C.c_void_p),
+                                                C.cast(sizes, C.c_void_p), _t_ptr(d_xhat), n, _t_ptr(d_y),
+                                                _t_ptr(d_bools) if d_bools is not None else None,
+                                                _stream_ptr(stream)))
+        return d_y
+
+    def trunc_bundle_eval_host(self, desc: TruncDesc, keys: Sequence[np.ndarray], xhat: np.ndarray,
+                               y: np.ndarray | None = None, bools: np.ndarray | None = None) -> np.ndarray:
+        """Host buffers in and out (pinned memory makes the copies true DMA)."""
+        xhat = np.ascontiguousarray(xhat, dtype=np.uint64)
+        if y is None:
+            y = np.empty(xhat.size, dtype=np.uint64)
+        nq = int(desc.nq)
+        karr = [np.ascontiguousarray(k, dtype=np.uint8) for k in keys[:nq]]
+        ptrs = (C.c_void_p * 4)(*[_np_ptr(k) for k in karr], *([None] * (4 - nq)))
+        sizes = (C.c_size_t * 4)(*[k.size for k in karr], *([0] * (4 - nq)))
+        check(self._L.sufb200_trunc_bundle_eval_host(self.h, C.byref(desc), C.cast(ptrs, C.c_void_p),
+                                                     C.cast(sizes, C.c_void_p), _np_ptr(xhat), xhat.size,
+                                                     _np_ptr(y), _np_ptr(bools) if bools is not None else None))
+        return y
+
+    # -- reference GPU-backend formats ------------------------------------------
+    def thr_dcf_eval(self, in_bits, d_keys, key_bytes, broadcast, d_xs, out_bytes, d_out=None, stream=None):
+        import torch
+
+        n = d_xs.numel()
+        if d_out is None:
+            d_out = torch.empty(max(n * out_bytes, 1), dtype=torch.uint8, device=d_xs.device)
+        check(self._L.sufb200_thr_dcf_eval(self.h, in_bits, _t_ptr(d_keys), key_bytes, int(broadcast),
+                                           _t_ptr(d_xs), n, out_bytes, _t_ptr(d_out), _stream_ptr(stream)))
+        return d_out
+
+    def packed_lt_eval(self, d_keys, key_bytes, broadcast, d_xs, in_bits, out_words, idx_base=0, d_out=None,
+                       stream=None):
+        import torch
+
+        n = d_xs.numel()
+        if d_out is None:
+            d_out = torch.empty(n * out_words, dtype=torch.int64, device=d_xs.device)
+        check(self._L.sufb200_packed_lt_eval(self.h, _t_ptr(d_keys), key_bytes, int(broadcast), _t_ptr(d_xs), n,
+                                             in_bits, out_words, C.c_uint64(idx_base), _t_ptr(d_out),
+                                             _stream_ptr(stream)))
+        return d_out
+
+    def interval_lut_eval(self, d_keys, key_bytes, broadcast, d_xs, out_words, idx_base=0, d_out=None, stream=None):
+        import torch
+
+        n = d_xs.numel()
+        if d_out is None:
+            d_out = torch.empty(n * out_words, dtype=torch.int64, device=d_xs.device)
+        check(self._L.sufb200_interval_lut_eval(self.h, _t_ptr(d_keys), key_bytes, int(broadcast), _t_ptr(d_xs), n,
+                                                out_words, C.c_uint64(idx_base), _t_ptr(d_out),
+                                                _stream_ptr(stream)))
+        return d_out
+
+
+# -- key builders for the reference formats (host) ---------------------------------
+
+def thr_dcf_key(in_bits: int, alpha: int, payload: bytes) -> np.ndarray:
+    L = _lib.lib()
+    n = int(L.sufb200_thr_dcf_build(in_bits, C.c_uint64(alpha & (2**64 - 1)), None, len(payload), None))
+    if n == 0:
+        raise SufB200Error(_lib.ERR_INVALID, "bad threshold DCF arguments")
+    out = np.zeros(n, dtype=np.uint8)
+    pl = np.frombuffer(bytes(payload), dtype=np.uint8).copy() if payload else None
+    L.sufb200_thr_dcf_build(in_bits, C.c_uint64(alpha & (2**64 - 1)), _np_ptr(pl) if pl is not None else None,
+                            len(payload), _np_ptr(out))
+    return out
+
+
+def seed_from_id(nid: int, tweak: int) -> np.ndarray:
+    s = np.zeros(16, dtype=np.uint8)
+    check(_lib.lib().sufb200_seed_from_id(C.c_uint64(nid), C.c_uint64(tweak), _np_ptr(s)))
+    return s
+
+
+def packed_lt_key(party: int, nonce: int, in_bits: int, thresholds, seed) -> np.ndarray:
+    L = _lib.lib()
+    thr = np.ascontiguousarray(thresholds, dtype=np.uint64)
+    sd = np.ascontiguousarray(seed, dtype=np.uint8)
+    n = int(L.sufb200_packed_lt_build(party, C.c_uint64(nonce), in_bits, None, thr.size, None, None))
+    if n == 0:
+        raise SufB200Error(_lib.ERR_INVALID, "bad packed-compare arguments")
+    out = np.zeros(n, dtype=np.uint8)
+    L.sufb200_packed_lt_build(party, C.c_uint64(nonce), in_bits, _np_ptr(thr), thr.size, _np_ptr(sd), _np_ptr(out))
+    return out
+
+
+def interval_lut_key(party: int, nonce: int, in_bits: int, out_words: int, cuts, payload, seed) -> np.ndarray:
+    L = _lib.lib()
+    cuts = np.ascontiguousarray(cuts, dtype=np.uint64)
+    pay = np.ascontiguousarray(payload, dtype=np.uint64)
+    sd = np.ascontiguousarray(seed, dtype=np.uint8)
+    iv = cuts.size - 1
+    n = int(L.sufb200_interval_lut_build(party, C.c_uint64(nonce), in_bits, out_words, None, iv, None, None, None))
+    if n == 0:
+        raise SufB200Error(_lib.ERR_INVALID, "bad interval-LUT arguments")
+    out = np.zeros(n, dtype=np.uint8)
+    L.sufb200_interval_lut_build(party, C.c_uint64(nonce), in_bits, out_words, _np_ptr(cuts), iv, _np_ptr(pay),
+                                 _np_ptr(sd), _np_ptr(out))
+    return out

@@ -1,0 +1,86 @@
+"""GPU parity: fused truncation / ARS bundles (FaithfulTR, FaithfulARS,
+GapARS) against the oracle's composite eval + postproc, per share and per
+boolean port, plus exact reconstruction at the configs[1] size."""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle.oracle import KIND_ARS, KIND_GAPARS, KIND_TR
+from tests.conftest import from_dev, to_dev
+from tests.helpers import oracle_trunc_eval, signed_fixed, to_product_desc, trunc_material
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("kind", [KIND_TR, KIND_ARS, KIND_GAPARS])
+@pytest.mark.parametrize("f", [4, 12, 16])
+def test_bundle_bit_exact_per_share(ctx, torch_cuda, oracle, prg_state, kind, f):
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(31 * kind + f)
+    n = 3000
+    x = signed_fixed(rng, n, 40)
+    for seed in (2, 12345):
+        r_in, descs, keys = trunc_material(oracle, kind, f, seed)
+        xhat = x + np.uint64(r_in)
+        dx = to_dev(torch_cuda, xhat)
+        ys = []
+        for p in (0, 1):
+            db = torch_cuda.zeros(3 * n, dtype=torch_cuda.int64, device="cuda")
+            dy = ctx.trunc_bundle_eval(to_product_desc(descs[p]), keys[p], dx, d_bools=db)
+            ctx.sync()
+            exp_y, exp_b = oracle_trunc_eval(oracle, descs[p], keys[p], xhat, want_bools=True)
+            got = from_dev(dy)
+            assert (got == exp_y).all()
+            assert (from_dev(db).reshape(n, 3) == exp_b).all()
+            ys.append(got)
+        exp = (x >> np.uint64(f)) if kind == KIND_TR else (x.view(np.int64) >> f).view(np.uint64)
+        assert ((ys[0] + ys[1]) == exp).all()
+
+
+def test_reference_trunc_vectors(ctx, torch_cuda, oracle, prg_state):
+    """src/demo/test_cuda_trunc_gapars.cpp / test_pfss_gpu.cpp inputs {16,-8,3,-1}, f=4."""
+    oracle.prg_init(prg_state)
+    v = json.loads((Path(__file__).parent / "golden" / "ref_vectors.json").read_text())["trunc"]
+    plain = np.array(v["plain"], dtype=np.int64)
+    for kind in (KIND_TR, KIND_ARS, KIND_GAPARS):
+        for seed in v["seeds"]:
+            r_in, descs, keys = trunc_material(oracle, kind, v["frac_bits"], seed)
+            dx = to_dev(torch_cuda, plain.view(np.uint64) + np.uint64(r_in))
+            y = sum(from_dev(ctx.trunc_bundle_eval(to_product_desc(descs[p]), keys[p], dx)) for p in (0, 1))
+            ctx.sync()
+            if kind == KIND_TR:
+                exp = plain.view(np.uint64) >> np.uint64(v["frac_bits"])
+            else:
+                exp = np.array(v["expect_ars"], dtype=np.int64).view(np.uint64)
+            assert (y == exp).all()
+
+
+def test_bundle_rejects_mismatched_keys(ctx, torch_cuda, oracle, prg_state):
+    from suf_b200 import SufB200Error
+
+    oracle.prg_init(prg_state)
+    r_in, descs, keys = trunc_material(oracle, KIND_ARS, 16, 2)
+    dx = to_dev(torch_cuda, np.arange(16, dtype=np.uint64))
+    with pytest.raises(SufB200Error):  # party-1 keys with the party-0 descriptor
+        ctx.trunc_bundle_eval(to_product_desc(descs[0]), keys[1], dx)
+
+
+def test_config2_size_reconstruction(ctx, torch_cuda, oracle, prg_state):
+    """N = 4,194,304, |x| < 2^40 with 32 fractional bits, f = 16, seed 2."""
+    oracle.prg_init(prg_state)
+    n = 1 << 22
+    rng = np.random.default_rng(2)
+    x = signed_fixed(rng, n, 40)
+    r_in, descs, keys = trunc_material(oracle, KIND_ARS, 16, 2)
+    xhat = x + np.uint64(r_in)
+    dx = to_dev(torch_cuda, xhat)
+    y0 = from_dev(ctx.trunc_bundle_eval(to_product_desc(descs[0]), keys[0], dx))
+    y1 = from_dev(ctx.trunc_bundle_eval(to_product_desc(descs[1]), keys[1], dx))
+    ctx.sync()
+    assert ((y0 + y1) == (x.view(np.int64) >> 16).view(np.uint64)).all()
+    idx = rng.integers(0, n, 256)
+    assert (y0[idx] == oracle_trunc_eval(oracle, descs[0], keys[0], xhat[idx])).all()

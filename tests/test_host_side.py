@@ -1,0 +1,190 @@
+"""CPU tests of the product library's host side: exports, dealer keygen,
+key builders and the CPU build of the device AES engine / walk."""
+from __future__ import annotations
+
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle.oracle import GROUP_ADD, GROUP_XOR, KIND_ARS, KIND_GAPARS, KIND_TR
+from tests.helpers import seeds_for
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def built():
+    from suf_b200.build import build
+
+    return build()
+
+
+def header_functions() -> list[str]:
+    txt = (ROOT / "include" / "sufb200.h").read_text()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(sufb200_\w+)\s*\(", txt)))
+
+
+def test_library_exports_every_header_symbol(built):
+    lib = C.CDLL(str(built))
+    names = header_functions()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    from suf_b200 import _lib
+
+    assert sorted(_lib.exported_symbols()) == names
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    from suf_b200 import _lib
+
+    with pytest.raises(FileNotFoundError):
+        _lib.load(tmp_path / "libsufb200.so")
+
+
+@pytest.fixture(scope="module")
+def host_ctx(built, prg_state):
+    from suf_b200.engine import Context
+
+    import suf_b200._lib as L
+
+    h = C.c_void_p()
+    L.check(L.lib().sufb200_ctx_create(-1, C.byref(h)))
+    ctx = Context.__new__(Context)
+    ctx._L = L.lib()
+    ctx.h = h
+    ctx.device = -1
+    ctx.prg_init(prg_state)
+    yield ctx
+    ctx.close()
+
+
+def test_host_only_context_rejects_evaluation(host_ctx):
+    from suf_b200 import SufB200Error
+
+    import suf_b200._lib as L
+
+    rc = L.lib().sufb200_myl7_dcf_eval(host_ctx.h, 0, 64, None, 2152, 1, None, 1, 8, None, None)
+    assert rc == L.ERR_UNSUPPORTED
+    with pytest.raises(SufB200Error):
+        L.check(rc)
+
+
+@pytest.mark.parametrize("group", [GROUP_ADD, GROUP_XOR])
+def test_product_keygen_matches_oracle(oracle, prg_state, host_ctx, group):
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(5)
+    for in_bits, plen in ((1, 8), (9, 1), (16, 8), (64, 8), (64, 20)):
+        alpha = int(rng.integers(0, 2**63)) & ((1 << in_bits) - 1)
+        payload = rng.integers(0, 256, plen, dtype=np.uint8).tobytes()
+        nch = (plen + 15) // 16
+        s0, s1 = rng.integers(0, 256, (2, 16 * nch), dtype=np.uint8)
+        a0, a1 = host_ctx.myl7_gen(group, in_bits, alpha, payload, s0, s1)
+        b0, b1 = oracle.myl7_gen(group, in_bits, alpha, payload, s0, s1)
+        assert (a0 == b0).all() and (a1 == b1).all()
+
+
+def test_product_batch_keygen(oracle, prg_state, host_ctx):
+    oracle.prg_init(prg_state)
+    n = 37
+    alphas = oracle.mt64(1, n)
+    s0, s1 = seeds_for(1, n, oracle)
+    k0, k1 = host_ctx.myl7_gen_batch(GROUP_ADD, 64, alphas, (1).to_bytes(8, "little"), s0, s1)
+    for i in (0, 17, n - 1):
+        b0, b1 = oracle.myl7_gen(GROUP_ADD, 64, int(alphas[i]), (1).to_bytes(8, "little"), s0[i], s1[i])
+        assert (k0[i] == b0).all() and (k1[i] == b1).all()
+
+
+@pytest.mark.parametrize("kind", [KIND_TR, KIND_ARS, KIND_GAPARS])
+@pytest.mark.parametrize("f", [4, 12, 16])
+def test_product_trunc_dealer_matches_oracle(oracle, kind, f):
+    from suf_b200.engine import Context
+
+    for seed in (1, 2, 12345):
+        r_a, p0, p1, thetas = Context.trunc_gen(kind, f, seed)
+        r_b, o0, o1 = oracle.trunc_gen(kind, f, seed)
+        assert r_a == r_b
+        for p, o in ((p0, o0), (p1, o1)):
+            for name in ("kind", "frac_bits", "party", "nq", "carry_a", "carry_b", "sign_a", "sign_b", "wrap_q",
+                         "carry_w", "sign_w", "haty", "r_hi", "m"):
+                assert getattr(p, name) == getattr(o, name), name
+            assert list(p.q_bits) == list(o.q_bits)
+        assert [int(t) for t in thetas[: o0.nq]] == [int(t) for t in o0.q_theta[: o0.nq]]
+
+
+def test_product_key_builders_match_oracle(oracle):
+    from suf_b200 import engine as E
+
+    assert (E.thr_dcf_key(6, 5, b"\xaa") == oracle.thr_dcf_key(6, 5, b"\xaa")).all()
+    for nid, tweak in ((1, 0), (2, 7), (12345, 3)):
+        assert (E.seed_from_id(nid, tweak) == oracle.seed_from_id(nid, tweak)).all()
+    seed = oracle.seed_from_id(4, 0)
+    thr = [60, 5, 12, 33, 48]
+    assert (E.packed_lt_key(1, 4, 6, thr, seed) == oracle.packed_key(1, 4, 6, thr, seed)).all()
+    cuts, pay = [0, 20, 40, 64], [100, 200, 300, 400, 500, 600]
+    assert (E.interval_lut_key(0, 5, 6, 2, cuts, pay, seed) == oracle.interval_key(0, 5, 6, 2, cuts, pay,
+                                                                                     seed)).all()
+
+
+def test_host_mt19937_64_matches_oracle(oracle):
+    from suf_b200.engine import host_mt19937_64
+
+    assert (host_mt19937_64(1, 1000) == oracle.mt64(1, 1000)).all()
+
+
+# ---- CPU build of the device AES engine and walk (table layout, selectors) ----
+
+@pytest.fixture(scope="module")
+def emu(tmp_path_factory):
+    out = tmp_path_factory.mktemp("emu") / "libemu.so"
+    subprocess.run(["g++", "-std=c++17", "-O1", "-fPIC", "-shared", "-I/usr/local/cuda/include", "-o", str(out),
+                    str(ROOT / "tests" / "hostemu" / "emu_shim.cpp")], check=True)
+    E = C.CDLL(str(out))
+    E.emu_dcf_eval.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_uint64, C.c_int, C.POINTER(C.c_uint64)]
+    return E
+
+
+def test_emulated_engine_aes_and_prg(emu, oracle, prg_state):
+    p = lambda a: a.ctypes.data  # noqa: E731
+    emu.emu_prg_init(C.c_void_p(p(prg_state)))
+    rng = np.random.default_rng(9)
+    for lane in range(32):
+        key = rng.integers(0, 256, 16, dtype=np.uint8)
+        blk = rng.integers(0, 256, 16, dtype=np.uint8)
+        out = np.zeros(16, np.uint8)
+        emu.emu_aes(C.c_void_p(p(key)), C.c_void_p(p(blk)), lane, C.c_void_p(p(out)))
+        assert (out == oracle.aes_ecb(key.tobytes(), blk)[0]).all()
+        seed = rng.integers(0, 256, 16, dtype=np.uint8)
+        seed[15] &= 0x7F
+        for xb in (0, 1):
+            A = np.zeros(16, np.uint8)
+            B = np.zeros(8, np.uint8)
+            emu.emu_prg_level(C.c_void_p(p(seed)), xb, lane, C.c_void_p(p(A)), C.c_void_p(p(B)))
+            ka = prg_state[32 * xb: 32 * xb + 16].tobytes()
+            kb = prg_state[32 * xb + 16: 32 * xb + 32].tobytes()
+            assert (A == (oracle.aes_ecb(ka, seed)[0] ^ seed)).all()
+            assert (B == (oracle.aes_ecb(kb, seed)[0] ^ seed)[:8]).all()
+
+
+@pytest.mark.parametrize("group", [GROUP_ADD, GROUP_XOR])
+def test_emulated_walk_matches_oracle(emu, oracle, prg_state, group):
+    emu.emu_prg_init(C.c_void_p(prg_state.ctypes.data))
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(13 + group)
+    for nb in (1, 5, 16, 64):
+        alpha = int(rng.integers(0, 2**63)) & ((1 << nb) - 1)
+        s0, s1 = rng.integers(0, 256, (2, 16), dtype=np.uint8)
+        k0, k1 = oracle.myl7_gen(group, nb, alpha, rng.integers(0, 256, 8, dtype=np.uint8).tobytes(), s0, s1)
+        xs = rng.integers(0, 2**63, 40, dtype=np.uint64)
+        xs[0] = alpha
+        for k in (k0, k1):
+            ref = oracle.myl7_eval(group, k, k.size, True, xs, 8).view(np.uint64).ravel()
+            for i, x in enumerate(xs):
+                v = C.c_uint64()
+                emu.emu_dcf_eval(group, k.ctypes.data, nb, C.c_uint64(int(x)), i % 32, C.byref(v))
+                assert v.value == int(ref[i])
