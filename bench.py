@@ -168,14 +168,15 @@ def run_ours(args, ws, rank, local):
     ctx.prg_init(prg_state())
     r_in, descs, keys = dealer(ctx)
     nq = int(descs[0].nq)
+    n_elem = args.n_elem
     if ws == 1:
         parties = [0, 1]
-        n = N_ELEM
+        n = n_elem
         shard = 0
     else:
         half = max(ws // 2, 1)
         parties = [0 if rank < half else 1]
-        n = 2 * N_ELEM
+        n = 2 * n_elem
         shard = rank % half
     xhat_h = inputs(r_in, n, shard)
     stream = torch.cuda.Stream(device=dev)
@@ -275,7 +276,7 @@ def run_ours(args, ws, rank, local):
             "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128", "data": "synthetic (seeded, configs[1] shapes)",
             "config": {"workload": "configs[1]: FaithfulARS trunc bundle, f=16, |x|<2^40, seed 2",
-                       "n_elements_per_party_per_gpu": n if ws > 1 else N_ELEM, "queries_per_element": nq,
+                       "n_elements_per_party_per_gpu": n, "queries_per_element": nq,
                        "query_bits": [int(descs[0].q_bits[q]) for q in range(nq)],
                        "parties_per_gpu": len(parties), "keys": "broadcast myl7 (AES-128-MMO PRG)",
                        "l2": "256 MB buffer written between timed steps", "parallelism": f"party x element shards on {ws} GPU(s)"},
@@ -387,6 +388,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=1 << 17)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--n-elem", type=int, default=N_ELEM,
+                    help="elements per party at N=1 (default: the configs[1] size; smaller only for profiling)")
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.impl == "reference":

@@ -16,6 +16,21 @@ def _p(t):
     return int(t.data_ptr()) if t is not None else None
 
 
+class Keep:
+    """Holds device tensors until the kernels that read them have run (a
+    tensor freed before its kernel executes returns its memory to the caching
+    allocator, which may hand it to the next upload)."""
+
+    def __init__(self, torch):
+        self.torch = torch
+        self.held = []
+
+    def dev(self, a):
+        t = to_dev(self.torch, a)
+        self.held.append(t)
+        return _p(t)
+
+
 @pytest.fixture(scope="module")
 def L():
     from suf_b200 import _lib
@@ -76,11 +91,12 @@ def test_trunc_postproc(ctx, torch_cuda, L, gap):
     bools = rng.integers(0, 2, (n, 3), dtype=np.uint64)
     arith = np.stack([rand_u64(rng, n), base], axis=1)
     f, rhi, m = 12, int(rand_u64(rng, 1)[0]), int(rand_u64(rng, 1)[0])
+    k = Keep(torch_cuda)
     for party in (0, 1):
         out = torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda")
-        L.check(L.lib().sufb200_trunc_postproc(party, gap, f, C.c_uint64(rhi), C.c_uint64(m), _p(to_dev(torch_cuda,
-                hatx)), _p(to_dev(torch_cuda, arith.ravel())), 2, 1, _p(to_dev(torch_cuda, bools.ravel())), 3, 0, 1, 2,
-                _p(out), n, None))
+        L.check(L.lib().sufb200_trunc_postproc(party, gap, f, C.c_uint64(rhi), C.c_uint64(m), k.dev(hatx),
+                                               k.dev(arith.ravel()), 2, 1, k.dev(bools.ravel()), 3, 0, 1, 2, _p(out), n,
+                                               None))
         exp = _postproc_ref(party, gap, f, rhi, m, hatx, base, bools[:, 0], bools[:, 1], bools[:, 2])
         assert (from_dev(out) == exp).all()
 
@@ -98,16 +114,16 @@ def test_row_reductions(ctx, torch_cuda, oracle, L):
     L.check(L.lib().sufb200_row_sum(_p(dmat), rows, cols, None, _p(out), None))
     assert (from_dev(out) == oracle.row_sum(mat)).all()
     mean = rand_u64(rng, rows)
-    L.check(L.lib().sufb200_row_variance(_p(dmat), _p(to_dev(torch_cuda, mean)), rows, cols, _p(dval), _p(out), None))
+    k = Keep(torch_cuda)
+    L.check(L.lib().sufb200_row_variance(_p(dmat), k.dev(mean), rows, cols, _p(dval), _p(out), None))
     assert (from_dev(out) == oracle.row_variance(mat, mean, valid)).all()
     offs = np.concatenate([[0], np.cumsum(valid)]).astype(np.int32)
     vals = np.concatenate([mat[r, : valid[r]] for r in range(rows)])
-    L.check(L.lib().sufb200_row_sum_ragged(_p(to_dev(torch_cuda, vals)), _p(torch_cuda.from_numpy(offs).cuda()), rows,
-                                           _p(out), None))
+    L.check(L.lib().sufb200_row_sum_ragged(k.dev(vals), k.dev(offs), rows, _p(out), None))
     assert (from_dev(out) == oracle.row_sum(mat, valid)).all()
     ln = rand_u64(rng, 128 * 768).reshape(128, 768)  # LayerNorm rows
     out2 = torch_cuda.empty(128, dtype=torch_cuda.int64, device="cuda")
-    L.check(L.lib().sufb200_row_sum(_p(to_dev(torch_cuda, ln.ravel())), 128, 768, None, _p(out2), None))
+    L.check(L.lib().sufb200_row_sum(k.dev(ln.ravel()), 128, 768, None, _p(out2), None))
     assert (from_dev(out2) == oracle.row_sum(ln)).all()
 
 
@@ -118,9 +134,11 @@ def test_row_broadcast_mul(ctx, torch_cuda, L):
     B, e = rand_u64(rng, rows), rand_u64(rng, rows)
     valid = np.array([(r % 128) + 1 for r in range(rows)], dtype=np.int32)
     out = torch_cuda.empty(rows * cols, dtype=torch_cuda.int64, device="cuda")
+    k = Keep(torch_cuda)
+    ptrs = [k.dev(v) for v in (A, B, C_, d, e)]
+    dval = k.dev(valid)
     for party in (0, 1):
-        L.check(L.lib().sufb200_row_broadcast_mul(party, *[_p(to_dev(torch_cuda, v)) for v in (A, B, C_, d, e)], rows,
-                                                  cols, _p(torch_cuda.from_numpy(valid).cuda()), _p(out), None))
+        L.check(L.lib().sufb200_row_broadcast_mul(party, *ptrs, rows, cols, dval, _p(out), None))
         r = np.repeat(np.arange(rows), cols)
         with np.errstate(over="ignore"):
             exp = C_ + d * B[r] + e[r] * A + (d * e[r] if party == 0 else 0)
@@ -135,12 +153,13 @@ def test_eff_bits_pack_unpack_and_open(ctx, torch_cuda, oracle, L, eff_bits):
     xs = rand_u64(rng, n)
     words = (n * eff_bits + 63) // 64
     dp = torch_cuda.zeros(words, dtype=torch_cuda.int64, device="cuda")
-    L.check(L.lib().sufb200_pack_eff_bits(_p(to_dev(torch_cuda, xs)), eff_bits, _p(dp), n, None))
+    k = Keep(torch_cuda)
+    L.check(L.lib().sufb200_pack_eff_bits(k.dev(xs), eff_bits, _p(dp), n, None))
     assert (from_dev(dp) == oracle.pack_eff_bits(xs, eff_bits)).all()
     du = torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda")
     L.check(L.lib().sufb200_unpack_eff_bits(_p(dp), eff_bits, _p(du), n, None))
     mask = np.uint64((1 << eff_bits) - 1 if eff_bits < 64 else 2**64 - 1)
     assert (from_dev(du) == (xs & mask)).all()
     local = rand_u64(rng, n)
-    L.check(L.lib().sufb200_unpack_add_mod(_p(to_dev(torch_cuda, local)), _p(dp), eff_bits, _p(du), n, eff_bits, None))
+    L.check(L.lib().sufb200_unpack_add_mod(k.dev(local), _p(dp), eff_bits, _p(du), n, eff_bits, None))
     assert (from_dev(du) == ((local + (xs & mask)) & mask)).all()
