@@ -163,6 +163,28 @@ int sufb200_trunc_bundle_eval_host(sufb200_ctx ctx, const sufb200_trunc_desc* de
                                    const size_t* key_bytes, const uint64_t* xhat, size_t n, uint64_t* y,
                                    uint64_t* bools);
 
+/* Size of the fixed key staging array of sufb200_trunc_bundle_eval_noalloc. */
+#define SUFB200_NOALLOC_KEY_BYTES 16384
+
+/* Allocation-free form of sufb200_trunc_bundle_eval (no counterpart in the
+ * reference; it exists for callers that cannot allocate device memory when
+ * they evaluate -- a runtime that owns all device memory through its own
+ * arena, or code that must not re-enter or grow the CUDA allocator).  The
+ * bundle's keys are staged in one fixed array of SUFB200_NOALLOC_KEY_BYTES
+ * (16 KiB, room for four 64-bit-input keys) that every device loading the
+ * library holds until exit; the call makes no cudaMalloc / cudaFree or other
+ * allocating call, and rejects (SUFB200_ERR_INVALID) a bundle whose keys,
+ * each padded to 16 bytes, exceed that size.  The first call on each device
+ * looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current, so make it before any stream capture.  All calls on a
+ * device share the array and it keeps the last call's contents: calls whose
+ * copies and kernels overlap on the GPU (different streams, no ordering)
+ * race with each other.  Arguments, checks and outputs are otherwise those
+ * of sufb200_trunc_bundle_eval. */
+int sufb200_trunc_bundle_eval_noalloc(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                                      const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y,
+                                      uint64_t* d_bools, void* stream);
+
 /* ---- reference GPU-backend key formats (cuda/pfss_backend_gpu.cu) -------- */
 
 /* Threshold "DCF" blob [in_bits u16][payload_len u16][alpha u64][payload]

@@ -27,6 +27,8 @@ TRUNC_FAITHFUL_TR = 0
 TRUNC_FAITHFUL_ARS = 1
 TRUNC_GAPARS = 2
 
+NOALLOC_KEY_BYTES = 16384  # SUFB200_NOALLOC_KEY_BYTES
+
 
 class SufB200Error(RuntimeError):
     def __init__(self, code: int, msg: str):
@@ -69,6 +71,7 @@ _SIGS = {
     "sufb200_trunc_gen": (_i, [_i, _i, _u64, C.POINTER(TruncDesc), C.POINTER(TruncDesc), _vp, _vp]),
     "sufb200_trunc_bundle_eval": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "sufb200_trunc_bundle_eval_host": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp]),
+    "sufb200_trunc_bundle_eval_noalloc": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "sufb200_thr_dcf_build": (_sz, [_i, _u64, _vp, _i, _vp]),
     "sufb200_thr_dcf_eval": (_i, [_vp, _i, _vp, _sz, _i, _vp, _sz, _i, _vp, _vp]),
     "sufb200_packed_lt_build": (_sz, [_i, _u64, _i, _vp, _i, _vp, _vp]),

@@ -123,6 +123,8 @@ int myl7_args(sufb200_ctx ctx, int group, int in_bits, const void* keys, size_t 
 }  // namespace
 
 namespace sufb200 {
+int record_error(int code, const std::string& msg) { return fail(code, msg); }
+
 cudaError_t probe_dyn_smem_base(uint32_t* d_out, cudaStream_t st) {
   probe_kernel<<<1, 32, 1024, st>>>(d_out);
   return cudaGetLastError();

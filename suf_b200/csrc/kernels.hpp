@@ -4,6 +4,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <string>
 
 #include <cuda_runtime.h>
 
@@ -58,6 +59,9 @@ struct RefFmtLaunch {
 cudaError_t launch_thr_dcf(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
 cudaError_t launch_packed_lt(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
 cudaError_t launch_interval_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
+
+// Records `msg` as the calling thread's sufb200_last_error() and returns code.
+int record_error(int code, const std::string& msg);
 
 // Probe of the dynamic shared-memory base (capi.cu uses it at context setup).
 cudaError_t probe_dyn_smem_base(uint32_t* d_out, cudaStream_t st);
