@@ -4,6 +4,7 @@
 // entry points.  No path here falls back to host evaluation: every
 // evaluation runs on the device or returns an error.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <random>
@@ -13,6 +14,7 @@
 #include "host_aes.hpp"
 #include "kernels.hpp"
 #include "keygen.hpp"
+#include "prefix.cuh"
 #include "primitives.hpp"
 #include "sufb200_internal.cuh"
 
@@ -43,6 +45,19 @@ __global__ void probe_kernel(uint32_t* out) {
 }
 
 bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+// Broadcast-key batches at least this large take the shared-prefix path
+// (prefix.cuh); SUFB200_PREFIX=0 in the environment selects the direct walk.
+size_t prefix_min_n() {
+  static const size_t v = [] {
+    const char* e = std::getenv("SUFB200_PREFIX");
+    if (e && std::string(e) == "0") return ~static_cast<size_t>(0);
+    return static_cast<size_t>(16384);
+  }();
+  return v;
+}
+
+constexpr size_t kAccBytes = 256;  // RangeAcc slot, keeps the frontier 256-byte aligned
 
 // Host-side per-context device buffers for the host-buffer entry points.
 struct HostIo {
@@ -284,8 +299,23 @@ int sufb200_myl7_dcf_eval(sufb200_ctx ctx, int group, int in_bits, const uint8_t
   if (n == 0) return SUFB200_OK;
   if (int rc = myl7_args(ctx, group, in_bits, d_keys, key_bytes, d_xs, out_bytes, d_out)) return rc;
   sufb200::DcfLaunch a{d_keys, key_bytes, d_xs, n, d_out, ctx->d_t0, ctx->d_status, in_bits, out_bytes};
-  SUFB200_CHECK_CUDA(sufb200::launch_myl7_eval(ctx, group, a, broadcast ? 1 : 0, as_stream(stream)),
-                     "myl7 DCF eval launch");
+  cudaStream_t st = as_stream(stream);
+  if (broadcast && n >= prefix_min_n()) {
+    const uint32_t kmax = sufb200::prefix_budget(n);
+    uint8_t* scratch = nullptr;
+    SUFB200_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&scratch), kAccBytes + 32ull * kmax, st),
+                       "cudaMallocAsync prefix scratch");
+    auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch);
+    auto* F = reinterpret_cast<sufb200::FrontierEntry*>(scratch + kAccBytes);
+    sufb200::FrontierLaunch fl{d_keys, in_bits, out_bytes, acc, kmax, F, ctx->d_t0, ctx->d_status};
+    cudaError_t e = sufb200::launch_range(ctx, d_xs, n, acc, st);
+    if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, group, fl, st);
+    if (e == cudaSuccess) e = sufb200::launch_myl7_bcast_prefix(ctx, group, a, acc, kmax, F, st);
+    cudaFreeAsync(scratch, st);
+    if (e != cudaSuccess) return cuda_fail(e, "myl7 DCF prefix launch");
+    return SUFB200_OK;
+  }
+  SUFB200_CHECK_CUDA(sufb200::launch_myl7_eval(ctx, group, a, broadcast ? 1 : 0, st), "myl7 DCF eval launch");
   return SUFB200_OK;
 }
 
@@ -363,24 +393,38 @@ int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, c
     while (blob.size() % 16) blob.push_back(0);
   }
   cudaStream_t st = as_stream(stream);
-  uint8_t* d_keys = nullptr;
-  if (!blob.empty()) {
-    SUFB200_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d_keys), blob.size(), st), "cudaMallocAsync keys");
-    cudaError_t e = cudaMemcpyAsync(d_keys, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
-    if (e != cudaSuccess) {
-      cudaFreeAsync(d_keys, st);
-      return cuda_fail(e, "H2D bundle keys");
-    }
-  }
-  a.keys = d_keys;
+  const bool prefix = n >= prefix_min_n() && desc->nq > 0;
+  const uint32_t kmax = sufb200::prefix_budget(n);
+  const size_t blob_bytes = (blob.size() + 255) & ~static_cast<size_t>(255);
+  const size_t scratch_bytes =
+      blob_bytes + (prefix ? kAccBytes + 32ull * kmax * static_cast<size_t>(desc->nq) : 0) + 256;
+  uint8_t* scratch = nullptr;
+  SUFB200_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&scratch), scratch_bytes, st),
+                     "cudaMallocAsync bundle scratch");
+  cudaError_t e = cudaSuccess;
+  if (!blob.empty()) e = cudaMemcpyAsync(scratch, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
+  a.keys = scratch;
   a.xhat = d_xhat;
   a.n = n;
   a.y = d_y;
   a.bools = d_bools;
   a.t0 = ctx->d_t0;
   a.status = ctx->d_status;
-  cudaError_t e = sufb200::launch_trunc_bundle(ctx, a, st);
-  if (d_keys) cudaFreeAsync(d_keys, st);
+  if (e == cudaSuccess && prefix) {
+    auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch + blob_bytes);
+    sufb200::FrontierEntry* F[4] = {nullptr, nullptr, nullptr, nullptr};
+    e = sufb200::launch_range(ctx, d_xhat, n, acc, st);
+    for (int q = 0; q < desc->nq && e == cudaSuccess; q++) {
+      F[q] = reinterpret_cast<sufb200::FrontierEntry*>(scratch + blob_bytes + kAccBytes + 32ull * kmax * q);
+      sufb200::FrontierLaunch fl{scratch + a.key_off[q], desc->q_bits[q], 8, acc, kmax, F[q], ctx->d_t0,
+                                 ctx->d_status};
+      e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fl, st);
+    }
+    if (e == cudaSuccess) e = sufb200::launch_trunc_bundle_prefix(ctx, a, acc, kmax, F, st);
+  } else if (e == cudaSuccess) {
+    e = sufb200::launch_trunc_bundle(ctx, a, st);
+  }
+  cudaFreeAsync(scratch, st);
   if (e != cudaSuccess) return cuda_fail(e, "trunc bundle launch");
   return SUFB200_OK;
 }

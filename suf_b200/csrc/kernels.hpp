@@ -60,6 +60,27 @@ cudaError_t launch_thr_dcf(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cuda
 cudaError_t launch_packed_lt(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
 cudaError_t launch_interval_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
 
+// Shared-prefix evaluation of broadcast keys (prefix.cu, prefix.cuh).
+struct RangeAcc;
+struct FrontierEntry;
+struct FrontierLaunch {
+  const uint8_t* key;  // device: one myl7 key
+  int in_bits;
+  int out_bytes;
+  const RangeAcc* acc;
+  uint32_t kmax;
+  FrontierEntry* out;  // device [kmax]
+  const uint32_t* t0;
+  uint32_t* status;
+};
+uint32_t prefix_budget(size_t n);
+cudaError_t launch_range(const sufb200_ctx_s* ctx, const uint64_t* xs, size_t n, RangeAcc* acc, cudaStream_t st);
+cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierLaunch& f, cudaStream_t st);
+cudaError_t launch_myl7_bcast_prefix(const sufb200_ctx_s* ctx, int group, const DcfLaunch& a, const RangeAcc* acc,
+                                     uint32_t kmax, const FrontierEntry* F, cudaStream_t st);
+cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaunch& a, const RangeAcc* acc,
+                                       uint32_t kmax, FrontierEntry* const F[4], cudaStream_t st);
+
 // Records `msg` as the calling thread's sufb200_last_error() and returns code.
 int record_error(int code, const std::string& msg);
 

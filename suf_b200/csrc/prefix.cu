@@ -1,0 +1,232 @@
+// prefix.cu -- range, frontier and resume kernels of the shared-prefix
+// evaluation of broadcast myl7 DCF keys (see prefix.cuh for the method).
+#include "bcast_key.cuh"
+#include "kernels.hpp"
+#include "prefix.cuh"
+
+namespace sufb200 {
+
+namespace {
+
+__device__ __forceinline__ uint64_t warp_min_u64(uint64_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t w = __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    v = w < v ? w : v;
+  }
+  return v;
+}
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t w = __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    v = w > v ? w : v;
+  }
+  return v;
+}
+
+// Signed offsets from the pivot xs[0], biased by flipping the sign bit so
+// unsigned order is signed order; one atomic pair per warp.
+__global__ void range_kernel(const uint64_t* __restrict__ xs, size_t n, RangeAcc* acc) {
+  const uint64_t pivot = xs[0];
+  uint64_t mn = ~0ull, mx = 0ull;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const uint64_t b = (xs[i] - pivot) ^ (1ull << 63);
+    mn = b < mn ? b : mn;
+    mx = b > mx ? b : mx;
+  }
+  mn = warp_min_u64(mn);
+  mx = warp_max_u64(mx);
+  if ((threadIdx.x & 31) == 0) {
+    atomicMin(&acc->min_b, static_cast<unsigned long long>(mn));
+    atomicMax(&acc->max_b, static_cast<unsigned long long>(mx));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) acc->pivot = pivot;
+}
+
+template <int GROUP>
+__global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParams prg, const FrontierLaunch f) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(f.status, kStatusSmemLayout);
+    return;
+  }
+  BcastKeySmem* ks = reinterpret_cast<BcastKeySmem*>(smem);
+  stage_bcast_key(ks, f.key, f.in_bits, f.out_bytes);
+  aes_fill_tables(f.t0);
+  __syncthreads();
+  if (!ks->ok) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(f.status, kStatusBadKeyHeader);
+    return;
+  }
+  const uint32_t lb = lane_base();
+  const int n = f.in_bits;
+  const Plan plan = make_plan(*f.acc, n, f.kmax);
+  const int D = static_cast<int>(plan.depth);
+  const uint32_t party = ks->party;
+  for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < plan.count; j += gridDim.x * blockDim.x) {
+    const uint64_t pre = (plan.first + j) & nbit_mask(D);
+    const uint64_t x = D ? (pre << (n - D)) : 0ull;
+    Blk s;
+    s.w[0] = ks->seed.x;
+    s.w[1] = ks->seed.y;
+    s.w[2] = ks->seed.z;
+    s.w[3] = ks->seed.w;
+    uint32_t t = party;
+    uint64_t v = 0;
+    for (int lv = 0; lv < D; lv++) {
+      CwLevel cw;
+      const uint4 cs = ks->cw_s[lv];
+      cw.s.w[0] = cs.x;
+      cw.s.w[1] = cs.y;
+      cw.s.w[2] = cs.z;
+      cw.s.w[3] = cs.w;
+      cw.v = ks->cw_v[lv];
+      cw.t = ks->cw_t[lv];
+      walk_level<GROUP>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (n - 1 - lv)) & 1ull), party, cw);
+    }
+    FrontierEntry e;
+    if (D == n) {
+      e.s[0] = e.s[1] = e.s[2] = e.s[3] = 0;
+      e.v = walk_finish<GROUP>(s, t, v, party, ks->np1_lo);
+      e.t = 0;
+    } else {
+      e.s[0] = s.w[0];
+      e.s[1] = s.w[1];
+      e.s[2] = s.w[2];
+      e.s[3] = s.w[3];
+      e.v = v;
+      e.t = t;
+    }
+    e.pad = 0;
+    f.out[j] = e;
+  }
+}
+
+template <int GROUP>
+__global__ void __launch_bounds__(kAesThreads, 1)
+    myl7_eval_bcast_prefix_kernel(const PrgParams prg, const DcfLaunch a, const RangeAcc* acc, uint32_t kmax,
+                                  const FrontierEntry* __restrict__ F) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    return;
+  }
+  BcastKeySmem* ks = reinterpret_cast<BcastKeySmem*>(smem);
+  stage_bcast_key(ks, a.keys, a.in_bits, a.out_bytes);
+  aes_fill_tables(a.t0);
+  __syncthreads();
+  if (!ks->ok) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.status, kStatusBadKeyHeader);
+    return;
+  }
+  const uint32_t lb = lane_base();
+  const int n = a.in_bits;
+  const Plan plan = make_plan(*acc, n, kmax);
+  const uint64_t xmask = nbit_mask(n);
+  const uint32_t party = ks->party;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    const uint64_t x = a.xs[i] & xmask;
+    const uint32_t idx = plan_index(plan, x, n);
+    Blk s;
+    uint32_t t;
+    uint64_t v;
+    int start;
+    if (idx < plan.count) {
+      const FrontierEntry e = F[idx];
+      if (plan.depth == static_cast<uint32_t>(n)) {
+        store_out(a.out, i, a.out_bytes, e.v);
+        continue;
+      }
+      s.w[0] = e.s[0];
+      s.w[1] = e.s[1];
+      s.w[2] = e.s[2];
+      s.w[3] = e.s[3];
+      t = e.t;
+      v = e.v;
+      start = static_cast<int>(plan.depth);
+    } else {  // outside the measured window: walk from the root
+      s.w[0] = ks->seed.x;
+      s.w[1] = ks->seed.y;
+      s.w[2] = ks->seed.z;
+      s.w[3] = ks->seed.w;
+      t = party;
+      v = 0;
+      start = 0;
+    }
+    for (int lv = start; lv < n; lv++) {
+      CwLevel cw;
+      const uint4 cs = ks->cw_s[lv];
+      cw.s.w[0] = cs.x;
+      cw.s.w[1] = cs.y;
+      cw.s.w[2] = cs.z;
+      cw.s.w[3] = cs.w;
+      cw.v = ks->cw_v[lv];
+      cw.t = ks->cw_t[lv];
+      walk_level<GROUP>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (n - 1 - lv)) & 1ull), party, cw);
+    }
+    store_out(a.out, i, a.out_bytes, walk_finish<GROUP>(s, t, v, party, ks->np1_lo));
+  }
+}
+
+int aes_grid(const sufb200_ctx_s* ctx, size_t work) {
+  const size_t want = (work + kAesThreads - 1) / kAesThreads;
+  return static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
+}
+
+template <typename K>
+cudaError_t set_smem(K kernel, const sufb200_ctx_s* ctx) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(ctx->aes_dyn_bytes));
+}
+
+}  // namespace
+
+uint32_t prefix_budget(size_t n) {
+  size_t k = n / 16;
+  if (k < 256) k = 256;
+  if (k > 65536) k = 65536;
+  return static_cast<uint32_t>(k);
+}
+
+cudaError_t launch_range(const sufb200_ctx_s* ctx, const uint64_t* xs, size_t n, RangeAcc* acc, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(&acc->min_b, 0xFF, sizeof(uint64_t), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(&acc->max_b, 0, 2 * sizeof(uint64_t), st);
+  if (e != cudaSuccess) return e;
+  const size_t want = (n + 255) / 256;
+  const size_t cap = static_cast<size_t>(ctx->sm_count) * 4;
+  range_kernel<<<static_cast<int>(want < cap ? (want ? want : 1) : cap), 256, 0, st>>>(xs, n, acc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierLaunch& f, cudaStream_t st) {
+  const size_t work = f.kmax;
+  cudaError_t e;
+  if (group == SUFB200_GROUP_ADD) {
+    if ((e = set_smem(frontier_kernel<SUFB200_GROUP_ADD>, ctx)) != cudaSuccess) return e;
+    frontier_kernel<SUFB200_GROUP_ADD><<<aes_grid(ctx, work), kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, f);
+  } else {
+    if ((e = set_smem(frontier_kernel<SUFB200_GROUP_XOR>, ctx)) != cudaSuccess) return e;
+    frontier_kernel<SUFB200_GROUP_XOR><<<aes_grid(ctx, work), kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, f);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_myl7_bcast_prefix(const sufb200_ctx_s* ctx, int group, const DcfLaunch& a, const RangeAcc* acc,
+                                     uint32_t kmax, const FrontierEntry* F, cudaStream_t st) {
+  cudaError_t e;
+  if (group == SUFB200_GROUP_ADD) {
+    if ((e = set_smem(myl7_eval_bcast_prefix_kernel<SUFB200_GROUP_ADD>, ctx)) != cudaSuccess) return e;
+    myl7_eval_bcast_prefix_kernel<SUFB200_GROUP_ADD>
+        <<<aes_grid(ctx, a.n), kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a, acc, kmax, F);
+  } else {
+    if ((e = set_smem(myl7_eval_bcast_prefix_kernel<SUFB200_GROUP_XOR>, ctx)) != cudaSuccess) return e;
+    myl7_eval_bcast_prefix_kernel<SUFB200_GROUP_XOR>
+        <<<aes_grid(ctx, a.n), kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a, acc, kmax, F);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace sufb200

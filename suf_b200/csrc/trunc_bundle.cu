@@ -9,6 +9,7 @@
 // followed by a device-to-host copy, then two OpenMP host loops.
 #include "dcf_walk.cuh"
 #include "kernels.hpp"
+#include "prefix.cuh"
 
 namespace sufb200 {
 
@@ -37,14 +38,57 @@ __device__ __forceinline__ uint64_t pick4(int q, uint64_t p0, uint64_t p1, uint6
   return q == 0 ? p0 : (q == 1 ? p1 : (q == 2 ? p2 : p3));
 }
 
-__global__ void __launch_bounds__(kAesThreads, 1) trunc_bundle_kernel(const PrgParams prg, const TruncLaunch a) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  if (!aes_layout_ok()) {
-    if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
-    return;
+// The AddU64 boolean plan (composite_fss.hpp:1539-1605) and the kind's
+// postproc hook (postproc_hooks.hpp:173-376) for one element.
+__device__ __forceinline__ void combine_store(const sufb200_trunc_desc& d, uint64_t xh, const uint64_t pr[4],
+                                              uint64_t* y_out, uint64_t* bools, size_t i) {
+  const uint32_t party = static_cast<uint32_t>(d.party);
+  const int f = d.frac_bits;
+  const uint64_t one = party == 0 ? 1ull : 0ull;
+  uint64_t carry = 0, sign = 0, wrap = 0;
+  if (d.carry_a >= 0) {
+    const uint64_t qa = pick4(d.carry_a, pr[0], pr[1], pr[2], pr[3]);
+    const uint64_t qb = pick4(d.carry_b, pr[0], pr[1], pr[2], pr[3]);
+    carry = one - ((qb - qa) + d.carry_w);
   }
+  if (d.sign_a >= 0) {
+    const uint64_t qa = pick4(d.sign_a, pr[0], pr[1], pr[2], pr[3]);
+    const uint64_t qb = pick4(d.sign_b, pr[0], pr[1], pr[2], pr[3]);
+    sign = (qb - qa) + d.sign_w;
+  }
+  if (d.wrap_q >= 0) wrap = pick4(d.wrap_q, pr[0], pr[1], pr[2], pr[3]);
+  uint64_t y;
+  if (d.kind == SUFB200_TRUNC_GAPARS) {
+    // GapArsPostProc::run_batch, postproc_hooks.hpp:324-375
+    const uint64_t hb = xh + (1ull << 62);
+    uint64_t top = 0;
+    if (party == 0 && f >= 0 && f < 64) top = f == 0 ? hb : (hb >> f);
+    y = d.haty + top - d.r_hi - carry;
+    if (f > 0 && f < 64 && ((hb >> 63) & 1ull) == 0) y += d.m;
+    if (party == 0) y -= (f >= 0 && f <= 62) ? (1ull << (62 - f)) : 0ull;
+  } else {
+    // FaithfulTruncPostProc / FaithfulArsPostProc::run_batch, postproc_hooks.hpp:198-290
+    const uint64_t top = (party == 0 && f < 64) ? (xh >> f) : 0ull;
+    const uint64_t modulus = (f <= 0 || f >= 64) ? 0ull : (1ull << (64 - f));
+    y = d.haty + top - d.r_hi - carry;
+    if (modulus) y += wrap * modulus;
+    if (d.kind == SUFB200_TRUNC_FAITHFUL_ARS) {
+      const uint64_t sign_mask = (f <= 0 || f >= 64) ? 0ull : (~0ull << (64 - f));
+      y += sign * sign_mask;
+    }
+  }
+  y_out[i] = y;
+  if (bools) {
+    bools[3 * i + 0] = carry;
+    bools[3 * i + 1] = sign;
+    bools[3 * i + 2] = wrap;
+  }
+}
+
+// Stage every query key of the bundle into shared memory, fill the AES
+// tables; false (status flagged) when a key header does not match.
+__device__ __forceinline__ bool stage_bundle(QueryKeySmem* ks, const TruncLaunch& a) {
   const sufb200_trunc_desc& d = a.desc;
-  QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);
   for (int q = 0; q < d.nq; q++) {
     const uint8_t* k = a.keys + a.key_off[q];
     const int nb = d.q_bits[q];
@@ -68,12 +112,49 @@ __global__ void __launch_bounds__(kAesThreads, 1) trunc_bundle_kernel(const PrgP
   for (int q = 0; q < d.nq; q++) {
     if (!ks[q].ok) {
       if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.status, kStatusBadKeyHeader);
-      return;
+      return false;
     }
   }
+  return true;
+}
+
+// Walk levels [from, n) of one query from state (s, t, v); returns the share.
+__device__ __forceinline__ uint64_t walk_query(const PrgParams& prg, uint32_t lb, const QueryKeySmem& K, int n,
+                                               uint64_t x, uint32_t party, Blk s, uint32_t t, uint64_t v, int from) {
+  for (int lv = from; lv < n; lv++) {
+    CwLevel cw;
+    const uint4 cs = K.cw_s[lv];
+    cw.s.w[0] = cs.x;
+    cw.s.w[1] = cs.y;
+    cw.s.w[2] = cs.z;
+    cw.s.w[3] = cs.w;
+    cw.v = K.cw_v[lv];
+    cw.t = K.cw_t[lv];
+    walk_level<SUFB200_GROUP_ADD>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (n - 1 - lv)) & 1ull), party, cw);
+  }
+  return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, K.np1_lo);
+}
+
+__device__ __forceinline__ Blk seed_blk(const QueryKeySmem& K) {
+  Blk s;
+  s.w[0] = K.seed.x;
+  s.w[1] = K.seed.y;
+  s.w[2] = K.seed.z;
+  s.w[3] = K.seed.w;
+  return s;
+}
+
+__global__ void __launch_bounds__(kAesThreads, 1) trunc_bundle_kernel(const PrgParams prg, const TruncLaunch a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    return;
+  }
+  const sufb200_trunc_desc& d = a.desc;
+  QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);
+  if (!stage_bundle(ks, a)) return;
   const uint32_t lb = lane_base();
   const uint32_t party = static_cast<uint32_t>(d.party);
-  const int f = d.frac_bits;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
     const uint64_t xh = a.xhat[i];
@@ -82,71 +163,69 @@ __global__ void __launch_bounds__(kAesThreads, 1) trunc_bundle_kernel(const PrgP
     for (int q = 0; q < d.nq; q++) {
       const int nb = d.q_bits[q];
       const uint64_t x = nb >= 64 ? xh : (xh & ((1ull << nb) - 1ull));
-      const QueryKeySmem& K = ks[q];
-      Blk s;
-      s.w[0] = K.seed.x;
-      s.w[1] = K.seed.y;
-      s.w[2] = K.seed.z;
-      s.w[3] = K.seed.w;
-      uint32_t t = party;
-      uint64_t v = 0;
-      for (int lv = 0; lv < nb; lv++) {
-        CwLevel cw;
-        const uint4 cs = K.cw_s[lv];
-        cw.s.w[0] = cs.x;
-        cw.s.w[1] = cs.y;
-        cw.s.w[2] = cs.z;
-        cw.s.w[3] = cs.w;
-        cw.v = K.cw_v[lv];
-        cw.t = K.cw_t[lv];
-        walk_level<SUFB200_GROUP_ADD>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (nb - 1 - lv)) & 1ull), party,
-                                      cw);
-      }
-      v = walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, K.np1_lo);
+      const uint64_t v = walk_query(prg, lb, ks[q], nb, x, party, seed_blk(ks[q]), party, 0, 0);
       if (q == 0) pr[0] = v;
       else if (q == 1) pr[1] = v;
       else if (q == 2) pr[2] = v;
       else pr[3] = v;
     }
-    const uint64_t one = party == 0 ? 1ull : 0ull;
-    uint64_t carry = 0, sign = 0, wrap = 0;
-    if (d.carry_a >= 0) {
-      const uint64_t qa = pick4(d.carry_a, pr[0], pr[1], pr[2], pr[3]);
-      const uint64_t qb = pick4(d.carry_b, pr[0], pr[1], pr[2], pr[3]);
-      carry = one - ((qb - qa) + d.carry_w);
-    }
-    if (d.sign_a >= 0) {
-      const uint64_t qa = pick4(d.sign_a, pr[0], pr[1], pr[2], pr[3]);
-      const uint64_t qb = pick4(d.sign_b, pr[0], pr[1], pr[2], pr[3]);
-      sign = (qb - qa) + d.sign_w;
-    }
-    if (d.wrap_q >= 0) wrap = pick4(d.wrap_q, pr[0], pr[1], pr[2], pr[3]);
-    uint64_t y;
-    if (d.kind == SUFB200_TRUNC_GAPARS) {
-      // GapArsPostProc::run_batch, postproc_hooks.hpp:324-375
-      const uint64_t hb = xh + (1ull << 62);
-      uint64_t top = 0;
-      if (party == 0 && f >= 0 && f < 64) top = f == 0 ? hb : (hb >> f);
-      y = d.haty + top - d.r_hi - carry;
-      if (f > 0 && f < 64 && ((hb >> 63) & 1ull) == 0) y += d.m;
-      if (party == 0) y -= (f >= 0 && f <= 62) ? (1ull << (62 - f)) : 0ull;
-    } else {
-      // FaithfulTruncPostProc / FaithfulArsPostProc::run_batch, postproc_hooks.hpp:198-290
-      const uint64_t top = (party == 0 && f < 64) ? (xh >> f) : 0ull;
-      const uint64_t modulus = (f <= 0 || f >= 64) ? 0ull : (1ull << (64 - f));
-      y = d.haty + top - d.r_hi - carry;
-      if (modulus) y += wrap * modulus;
-      if (d.kind == SUFB200_TRUNC_FAITHFUL_ARS) {
-        const uint64_t sign_mask = (f <= 0 || f >= 64) ? 0ull : (~0ull << (64 - f));
-        y += sign * sign_mask;
+    combine_store(d, xh, pr, a.y, a.bools, i);
+  }
+}
+
+
+// Large batches: every query resumes from its frontier entry (prefix.cuh).
+struct FrontierSet {
+  const FrontierEntry* F[4];
+};
+
+__global__ void __launch_bounds__(kAesThreads, 1)
+    trunc_bundle_prefix_kernel(const PrgParams prg, const TruncLaunch a, const RangeAcc* acc, uint32_t kmax,
+                               const FrontierSet fs) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    return;
+  }
+  const sufb200_trunc_desc& d = a.desc;
+  QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);
+  if (!stage_bundle(ks, a)) return;
+  const uint32_t lb = lane_base();
+  const uint32_t party = static_cast<uint32_t>(d.party);
+  Plan plan[4];
+  for (int q = 0; q < 4; q++) plan[q] = q < d.nq ? make_plan(*acc, d.q_bits[q], kmax) : Plan{0, 1, 0};
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    const uint64_t xh = a.xhat[i];
+    uint64_t pr[4] = {0, 0, 0, 0};
+#pragma unroll 1
+    for (int q = 0; q < d.nq; q++) {
+      const int nb = d.q_bits[q];
+      const uint64_t x = xh & nbit_mask(nb);
+      const Plan& P = plan[q];
+      const uint32_t idx = plan_index(P, x, nb);
+      uint64_t v;
+      if (idx < P.count) {
+        const FrontierEntry e = fs.F[q][idx];
+        if (P.depth == static_cast<uint32_t>(nb)) {
+          v = e.v;
+        } else {
+          Blk s;
+          s.w[0] = e.s[0];
+          s.w[1] = e.s[1];
+          s.w[2] = e.s[2];
+          s.w[3] = e.s[3];
+          v = walk_query(prg, lb, ks[q], nb, x, party, s, e.t, e.v, static_cast<int>(P.depth));
+        }
+      } else {
+        v = walk_query(prg, lb, ks[q], nb, x, party, seed_blk(ks[q]), party, 0, 0);
       }
+      if (q == 0) pr[0] = v;
+      else if (q == 1) pr[1] = v;
+      else if (q == 2) pr[2] = v;
+      else pr[3] = v;
     }
-    a.y[i] = y;
-    if (a.bools) {
-      a.bools[3 * i + 0] = carry;
-      a.bools[3 * i + 1] = sign;
-      a.bools[3 * i + 2] = wrap;
-    }
+    combine_store(d, xh, pr, a.y, a.bools, i);
   }
 }
 
@@ -159,6 +238,18 @@ cudaError_t launch_trunc_bundle(const sufb200_ctx_s* ctx, const TruncLaunch& a, 
   const size_t want = (a.n + kAesThreads - 1) / kAesThreads;
   const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
   trunc_bundle_kernel<<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaunch& a, const RangeAcc* acc,
+                                       uint32_t kmax, FrontierEntry* const F[4], cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(trunc_bundle_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  FrontierSet fs{{F[0], F[1], F[2], F[3]}};
+  const size_t want = (a.n + kAesThreads - 1) / kAesThreads;
+  const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
+  trunc_bundle_prefix_kernel<<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a, acc, kmax, fs);
   return cudaGetLastError();
 }
 

@@ -99,3 +99,21 @@ extern "C" int emu_dcf_eval(int group, const uint8_t* k, int in_bits, uint64_t x
   *out = group == 0 ? walk_finish<0>(s, t, v, party, np1) : walk_finish<1>(s, t, v, party, np1);
   return 0;
 }
+
+// ---- shared-prefix plan (prefix.cuh) on the CPU --------------------------------
+#include "../../suf_b200/csrc/prefix.cuh"
+
+extern "C" int emu_make_plan(uint64_t pivot, uint64_t min_b, uint64_t max_b, int n, uint32_t kmax, uint32_t* depth,
+                             uint32_t* count, uint64_t* first) {
+  RangeAcc r{min_b, max_b, pivot, 0};
+  Plan p = make_plan(r, n, kmax);
+  *depth = p.depth;
+  *count = p.count;
+  *first = p.first;
+  return 0;
+}
+
+extern "C" uint32_t emu_plan_index(uint32_t depth, uint32_t count, uint64_t first, uint64_t x, int n) {
+  Plan p{depth, count, first};
+  return plan_index(p, x, n);
+}

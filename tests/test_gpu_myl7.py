@@ -3,6 +3,7 @@ oracle, the reference-generated golden keys and, at full size, the
 reconstruction property.  Bit-exact: all arithmetic is in Z_2^64."""
 from __future__ import annotations
 
+import zlib
 from pathlib import Path
 
 import numpy as np
@@ -158,3 +159,37 @@ def test_full_size_reconstruction_property(ctx, torch_cuda, oracle, prg_state):
     # spot-check shares against the oracle
     idx = rng.integers(0, n, 512)
     assert (o0[idx] == oracle.myl7_eval(GROUP_ADD, k0, k0.size, True, xs[idx], 8).view(np.uint64).ravel()).all()
+
+
+def _window_inputs(rng, n, mode, in_bits):
+    """Inputs shaped to stress the shared-prefix plan (prefix.cuh)."""
+    mask = np.uint64((1 << in_bits) - 1 if in_bits < 64 else 2**64 - 1)
+    if mode == "uniform":
+        xs = rand_u64(rng, n)
+    elif mode == "clustered":  # x^ = x + r with |x| < 2^40, the bench's shape
+        r = np.uint64(int(rng.integers(0, 2**63)) * 2 + 1)
+        xs = rng.integers(-(2**40) + 1, 2**40, n, dtype=np.int64).view(np.uint64) + r
+    elif mode == "wrap":  # straddles 2^64 (and 2^in_bits after masking)
+        xs = rng.integers(-(2**20), 2**20, n, dtype=np.int64).view(np.uint64)
+    else:  # constant
+        xs = np.full(n, np.uint64(int(rng.integers(0, 2**63))))
+    return xs & mask if in_bits < 64 else xs
+
+
+@pytest.mark.parametrize("group", [GROUP_ADD, GROUP_XOR])
+@pytest.mark.parametrize("in_bits", [64, 37, 16])
+@pytest.mark.parametrize("mode", ["uniform", "clustered", "wrap", "constant"])
+def test_broadcast_shared_prefix_path_bit_exact(ctx, torch_cuda, oracle, prg_state, group, in_bits, mode):
+    """N above the shared-prefix threshold: every share equals the oracle's."""
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(zlib.crc32(f"{group}-{in_bits}-{mode}".encode()))
+    n = 40_000
+    xs = _window_inputs(rng, n, mode, in_bits)
+    alpha = int(xs[n // 2]) & ((1 << in_bits) - 1)  # threshold inside the window
+    s0, s1 = seeds_for(900 + in_bits, 1, oracle)
+    k0, k1 = oracle.myl7_gen(group, in_bits, alpha, (0x0102030405060708).to_bytes(8, "little"), s0[0], s1[0])
+    dx = to_dev(torch_cuda, xs)
+    for k in (k0, k1):
+        out = ctx.myl7_eval(group, in_bits, to_dev(torch_cuda, k), k.size, True, dx, 8)
+        ctx.sync()
+        assert (from_dev(out, np.uint8).reshape(n, 8) == oracle.myl7_eval(group, k, k.size, True, xs, 8)).all()

@@ -84,3 +84,28 @@ def test_config2_size_reconstruction(ctx, torch_cuda, oracle, prg_state):
     assert ((y0 + y1) == (x.view(np.int64) >> 16).view(np.uint64)).all()
     idx = rng.integers(0, n, 256)
     assert (y0[idx] == oracle_trunc_eval(oracle, descs[0], keys[0], xhat[idx])).all()
+
+
+@pytest.mark.parametrize("kind", [KIND_TR, KIND_ARS, KIND_GAPARS])
+def test_bundle_shared_prefix_path_bit_exact(ctx, torch_cuda, oracle, prg_state, kind):
+    """N above the shared-prefix threshold (frontier tables for the 64-bit
+    queries, full-domain tables for the 16-bit ones), per share and bool."""
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(77 + kind)
+    n = 40_000
+    x = signed_fixed(rng, n, 40)
+    x[:4] = np.array([0, 1, -1, 2**40 - 1], dtype=np.int64).view(np.uint64)
+    r_in, descs, keys = trunc_material(oracle, kind, 16, 5)
+    xhat = x + np.uint64(r_in)
+    dx = to_dev(torch_cuda, xhat)
+    ys = []
+    for p in (0, 1):
+        db = torch_cuda.zeros(3 * n, dtype=torch_cuda.int64, device="cuda")
+        y = from_dev(ctx.trunc_bundle_eval(to_product_desc(descs[p]), keys[p], dx, d_bools=db))
+        ctx.sync()
+        exp_y, exp_b = oracle_trunc_eval(oracle, descs[p], keys[p], xhat, want_bools=True)
+        assert (y == exp_y).all()
+        assert (from_dev(db).reshape(n, 3) == exp_b).all()
+        ys.append(y)
+    exp = (x >> np.uint64(16)) if kind == KIND_TR else (x.view(np.int64) >> 16).view(np.uint64)
+    assert ((ys[0] + ys[1]) == exp).all()
