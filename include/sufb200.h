@@ -67,6 +67,12 @@ int sufb200_ctx_sync(sufb200_ctx ctx, void* stream);
 /* Number of SMs of the context's device (grid sizing reference). */
 int sufb200_ctx_sm_count(sufb200_ctx ctx);
 
+/* Measured ceiling of the shared-memory AES-128 engine on this device: AES
+ * blocks per second of the DCF walk's two-block MMO step with no other work
+ * (every SM, ~1 ms; synchronises the device).  The roofline denominator of
+ * the DCF kernels.  No counterpart in the reference. */
+int sufb200_probe_aes_engine(sufb200_ctx ctx, double* blocks_per_s);
+
 /* ---- myl7 PRG-tree DCF --------------------------------------------------- */
 
 /* Install the fixed AES-128-MMO PRG keys: state[16j .. 16j+16) is key j,
@@ -279,6 +285,32 @@ int sufb200_unpack_eff_bits(const uint64_t* d_packed, int eff_bits, uint64_t* d_
  * (launch_unpack_add_mod_kernel). */
 int sufb200_unpack_add_mod(const uint64_t* d_local, const uint64_t* d_packed_remote, int eff_bits, uint64_t* d_out,
                            size_t n, int ring_bits, void* stream);
+
+/* Unpack, add local and sign-extend to ring_bits
+ * (launch_unpack_add_to_signed_kernel). */
+int sufb200_unpack_add_to_signed(const uint64_t* d_local, const uint64_t* d_packed_remote, int eff_bits,
+                                 uint64_t* d_out, size_t n, int ring_bits, void* stream);
+
+/* local + remote, sign-extended to ring_bits (launch_open_add_to_signed_kernel). */
+int sufb200_open_add_to_signed(const uint64_t* d_local, const uint64_t* d_remote, uint64_t* d_out, size_t n,
+                               int ring_bits, void* stream);
+
+/* Row mean = row sum / len, unsigned (launch_row_mean_kernel). */
+int sufb200_row_mean(const uint64_t* d_mat, int rows, int cols, const int* d_valid_lens, uint64_t* d_out_rows,
+                     void* stream);
+
+/* x >> frac_bits (launch_trunc_shift_kernel). */
+int sufb200_trunc_shift(const uint64_t* d_in, uint64_t* d_out, int frac_bits, size_t n, void* stream);
+
+/* Beaver matmul out = C + D*B + A*E (+ D*E on party 0) mod 2^64 for
+ * `batches` instances sharing the triple (A [MxK], B [KxN] or [NxK] when
+ * w_transposed, C [MxN]); D, E, out per instance.  With has_scale, each
+ * output is the low word of (int128)(int64)acc * mul_const >> mul_shift
+ * (launch_beaver_matmul2d[_batched]_kernel, cuda/cuda_primitives.cu:391-628). */
+int sufb200_beaver_matmul2d(int party, const uint64_t* d_D_open, const uint64_t* d_E_open, const uint64_t* d_A,
+                            const uint64_t* d_B, const uint64_t* d_C, int batches, int M, int K, int N,
+                            int w_transposed, int has_scale, int64_t mul_const, int mul_shift, uint64_t* d_out,
+                            void* stream);
 
 /* ---- host utilities ----------------------------------------------------- */
 

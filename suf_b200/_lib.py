@@ -62,6 +62,7 @@ _SIGS = {
     "sufb200_ctx_destroy": (_i, [_vp]),
     "sufb200_ctx_sync": (_i, [_vp, _vp]),
     "sufb200_ctx_sm_count": (_i, [_vp]),
+    "sufb200_probe_aes_engine": (_i, [_vp, C.POINTER(C.c_double)]),
     "sufb200_prg_init": (_i, [_vp, _vp, _sz]),
     "sufb200_myl7_key_bytes": (_sz, [_i, _i]),
     "sufb200_myl7_gen": (_i, [_vp, _i, _i, _u64, _vp, _i, _vp, _vp, _vp, _vp]),
@@ -91,6 +92,11 @@ _SIGS = {
     "sufb200_pack_eff_bits": (_i, [_vp, _i, _vp, _sz, _vp]),
     "sufb200_unpack_eff_bits": (_i, [_vp, _i, _vp, _sz, _vp]),
     "sufb200_unpack_add_mod": (_i, [_vp, _vp, _i, _vp, _sz, _i, _vp]),
+    "sufb200_unpack_add_to_signed": (_i, [_vp, _vp, _i, _vp, _sz, _i, _vp]),
+    "sufb200_open_add_to_signed": (_i, [_vp, _vp, _vp, _sz, _i, _vp]),
+    "sufb200_row_mean": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
+    "sufb200_trunc_shift": (_i, [_vp, _vp, _i, _sz, _vp]),
+    "sufb200_beaver_matmul2d": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, C.c_int64, _i, _vp, _vp]),
     "sufb200_host_mt19937_64": (_i, [_u64, _vp, _sz]),
 }
 

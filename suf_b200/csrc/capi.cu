@@ -194,6 +194,22 @@ int sufb200_ctx_create(int device, sufb200_ctx* out) {
   }
   ctx->dyn_base = base;
   ctx->aes_dyn_bytes = sufb200::kTabEnd - base;
+  // A private stream-ordered pool for per-call scratch that keeps its memory
+  // mapped between calls (the default pool returns it at every sync).
+  cudaMemPoolProps pp{};
+  pp.allocType = cudaMemAllocationTypePinned;
+  pp.location.type = cudaMemLocationTypeDevice;
+  pp.location.id = device;
+  e = cudaMemPoolCreate(&ctx->pool, &pp);
+  if (e == cudaSuccess) {
+    uint64_t keep = ~0ull;
+    e = cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+  if (e != cudaSuccess) {
+    int rc = cuda_fail(e, "memory pool setup");
+    sufb200_ctx_destroy(ctx);
+    return rc;
+  }
   *out = ctx;
   return SUFB200_OK;
 }
@@ -209,11 +225,22 @@ int sufb200_ctx_destroy(sufb200_ctx ctx) {
   if (ctx->d_t0) cudaFree(ctx->d_t0);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->d_scratch) cudaFree(ctx->d_scratch);
+  if (ctx->pool) {
+    cudaDeviceSynchronize();
+    cudaMemPoolDestroy(ctx->pool);
+  }
   delete ctx;
   return SUFB200_OK;
 }
 
 int sufb200_ctx_sm_count(sufb200_ctx ctx) { return ctx ? ctx->sm_count : 0; }
+
+int sufb200_probe_aes_engine(sufb200_ctx ctx, double* blocks_per_s) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (!blocks_per_s) return fail(SUFB200_ERR_INVALID, "null out");
+  SUFB200_CHECK_CUDA(sufb200::probe_aes_engine(ctx, blocks_per_s), "AES engine probe");
+  return sufb200_ctx_sync(ctx, nullptr);
+}
 
 int sufb200_ctx_sync(sufb200_ctx ctx, void* stream) {
   if (int rc = check_ctx(ctx, false)) return rc;
@@ -303,8 +330,9 @@ int sufb200_myl7_dcf_eval(sufb200_ctx ctx, int group, int in_bits, const uint8_t
   if (broadcast && n >= prefix_min_n()) {
     const uint32_t kmax = sufb200::prefix_budget(n);
     uint8_t* scratch = nullptr;
-    SUFB200_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&scratch), kAccBytes + 32ull * kmax, st),
-                       "cudaMallocAsync prefix scratch");
+    SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), kAccBytes + 32ull * kmax,
+                                               ctx->pool, st),
+                       "prefix scratch allocation");
     auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch);
     auto* F = reinterpret_cast<sufb200::FrontierEntry*>(scratch + kAccBytes);
     sufb200::FrontierLaunch fl{d_keys, in_bits, out_bytes, acc, kmax, F, ctx->d_t0, ctx->d_status};
@@ -399,8 +427,8 @@ int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, c
   const size_t scratch_bytes =
       blob_bytes + (prefix ? kAccBytes + 32ull * kmax * static_cast<size_t>(desc->nq) : 0) + 256;
   uint8_t* scratch = nullptr;
-  SUFB200_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&scratch), scratch_bytes, st),
-                     "cudaMallocAsync bundle scratch");
+  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), scratch_bytes, ctx->pool, st),
+                     "bundle scratch allocation");
   cudaError_t e = cudaSuccess;
   if (!blob.empty()) e = cudaMemcpyAsync(scratch, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
   a.keys = scratch;
@@ -637,6 +665,51 @@ int sufb200_unpack_add_mod(const uint64_t* d_local, const uint64_t* d_packed_rem
   return prim_rc(sufb200::prim_unpack_add_mod(cur_sm(), d_local, d_packed_remote, eff_bits, d_out, n, ring_bits,
                                               as_stream(stream)),
                  "unpack_add_mod");
+}
+
+int sufb200_unpack_add_to_signed(const uint64_t* d_local, const uint64_t* d_packed_remote, int eff_bits,
+                                 uint64_t* d_out, size_t n, int ring_bits, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_local || !d_packed_remote || !d_out || eff_bits < 1 || eff_bits > 64 || ring_bits < 1 || ring_bits > 64)
+    return fail(SUFB200_ERR_INVALID, "bad argument");
+  return prim_rc(sufb200::prim_unpack_add_to_signed(cur_sm(), d_local, d_packed_remote, eff_bits, d_out, n, ring_bits,
+                                                    as_stream(stream)),
+                 "unpack_add_to_signed");
+}
+
+int sufb200_open_add_to_signed(const uint64_t* d_local, const uint64_t* d_remote, uint64_t* d_out, size_t n,
+                               int ring_bits, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_local || !d_remote || !d_out || ring_bits < 1 || ring_bits > 64) return fail(SUFB200_ERR_INVALID, "bad argument");
+  return prim_rc(sufb200::prim_open_add_to_signed(cur_sm(), d_local, d_remote, d_out, n, ring_bits, as_stream(stream)),
+                 "open_add_to_signed");
+}
+
+int sufb200_row_mean(const uint64_t* d_mat, int rows, int cols, const int* d_valid_lens, uint64_t* d_out_rows,
+                     void* stream) {
+  if (rows <= 0) return SUFB200_OK;
+  if (!d_mat || !d_out_rows || cols < 0) return fail(SUFB200_ERR_INVALID, "bad argument");
+  return prim_rc(sufb200::prim_row_mean(cur_sm(), d_mat, rows, cols, d_valid_lens, d_out_rows, as_stream(stream)),
+                 "row_mean");
+}
+
+int sufb200_trunc_shift(const uint64_t* d_in, uint64_t* d_out, int frac_bits, size_t n, void* stream) {
+  if (n == 0) return SUFB200_OK;
+  if (!d_in || !d_out) return fail(SUFB200_ERR_INVALID, "null pointer");
+  return prim_rc(sufb200::prim_trunc_shift(cur_sm(), d_in, d_out, frac_bits, n, as_stream(stream)), "trunc_shift");
+}
+
+int sufb200_beaver_matmul2d(int party, const uint64_t* d_D_open, const uint64_t* d_E_open, const uint64_t* d_A,
+                            const uint64_t* d_B, const uint64_t* d_C, int batches, int M, int K, int N,
+                            int w_transposed, int has_scale, int64_t mul_const, int mul_shift, uint64_t* d_out,
+                            void* stream) {
+  if (batches <= 0 || M <= 0 || K <= 0 || N <= 0) return SUFB200_OK;
+  if (batches > 65535) return fail(SUFB200_ERR_UNSUPPORTED, "more than 65535 batches");
+  if (!d_D_open || !d_E_open || !d_A || !d_B || !d_C || !d_out) return fail(SUFB200_ERR_INVALID, "null pointer");
+  return prim_rc(sufb200::prim_beaver_matmul(party, d_D_open, d_E_open, d_A, d_B, d_C, batches, M, K, N,
+                                             w_transposed ? 1 : 0, has_scale, mul_const, mul_shift, d_out,
+                                             as_stream(stream)),
+                 "beaver_matmul2d");
 }
 
 int sufb200_host_mt19937_64(uint64_t seed, uint64_t* out, size_t n) {

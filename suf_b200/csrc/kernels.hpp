@@ -81,6 +81,9 @@ cudaError_t launch_myl7_bcast_prefix(const sufb200_ctx_s* ctx, int group, const 
 cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaunch& a, const RangeAcc* acc,
                                        uint32_t kmax, FrontierEntry* const F[4], cudaStream_t st);
 
+// Measured AES-128 block rate of the shared-memory engine (probe.cu).
+cudaError_t probe_aes_engine(const sufb200_ctx_s* ctx, double* blocks_per_s);
+
 // Records `msg` as the calling thread's sufb200_last_error() and returns code.
 int record_error(int code, const std::string& msg);
 

@@ -6,7 +6,7 @@
 // from inside an allocator callback or a memory-pool teardown), or a caller
 // that must not let the CUDA caching allocator grow during a latency-critical
 // phase.  sufb200_trunc_bundle_eval stages the bundle's keys in a buffer it
-// obtains with cudaMallocAsync; the entry point here stages them instead in
+// takes from a stream-ordered memory pool; the entry point here stages them in
 // one fixed array that the library image carries on every device, so the
 // call itself allocates nothing on the device or the host.
 //

@@ -330,3 +330,167 @@ cudaError_t prim_unpack_add_mod(int sm, const uint64_t* local, const uint64_t* p
 }
 
 }  // namespace sufb200
+
+// ---- Beaver matmul, row mean, signed opens, shift (cuda_primitives.hpp:130-240) ----
+
+namespace sufb200 {
+
+namespace {
+
+// Low word of the arithmetic right shift by `sh` of the signed 128-bit
+// product acc * c (beaver_scaled_acc semantics, cuda/cuda_primitives.cu:391-417).
+__device__ __forceinline__ uint64_t scaled_acc(uint64_t acc, int has_scale, int64_t c, int sh) {
+  if (!has_scale) return acc;
+  const int64_t a = static_cast<int64_t>(acc);
+  const uint64_t lo = static_cast<uint64_t>(a) * static_cast<uint64_t>(c);
+  if (sh <= 0) return lo;
+  const int64_t hi = __mul64hi(a, c);
+  if (sh >= 64) return static_cast<uint64_t>(hi >> (sh - 64 > 63 ? 63 : sh - 64));
+  return (lo >> sh) | (static_cast<uint64_t>(hi) << (64 - sh));
+}
+
+constexpr int kMT = 32, kKT = 16;
+
+// out = C + D*B + A*E (+ D*E on party 0), mod 2^64, per batch b (D, E and out
+// per batch; the triple A, B, C shared), 32 x 32 output tile per CTA, K in
+// steps of 16 staged in shared memory.  Sums mod 2^64 are order-free, so the
+// tiling is bit-exact with the reference's per-element loop.
+template <bool TRANS>
+__global__ void __launch_bounds__(256) beaver_matmul_kernel(int party, const uint64_t* __restrict__ D,
+                                                            const uint64_t* __restrict__ E,
+                                                            const uint64_t* __restrict__ A,
+                                                            const uint64_t* __restrict__ B,
+                                                            const uint64_t* __restrict__ C, int M, int K, int N,
+                                                            int has_scale, int64_t mul_const, int mul_shift,
+                                                            uint64_t* __restrict__ out) {
+  __shared__ uint64_t sD[kMT][kKT + 1], sA[kMT][kKT + 1], sE[kKT][kMT + 1], sB[kKT][kMT + 1];
+  const int b = blockIdx.z;
+  const size_t mk = static_cast<size_t>(M) * K, kn = static_cast<size_t>(K) * N, mn = static_cast<size_t>(M) * N;
+  const uint64_t* Db = D + b * mk;
+  const uint64_t* Eb = E + b * kn;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  const int m0 = blockIdx.y * kMT, n0 = blockIdx.x * kMT;
+  uint64_t acc[4] = {0, 0, 0, 0};
+  for (int k0 = 0; k0 < K; k0 += kKT) {
+    for (int e = ty * 32 + tx; e < kMT * kKT; e += 256) {
+      const int r = e / kKT, c = e % kKT;
+      const int m = m0 + r, k = k0 + c;
+      const bool ok = m < M && k < K;
+      sD[r][c] = ok ? Db[static_cast<size_t>(m) * K + k] : 0ull;
+      sA[r][c] = ok ? A[static_cast<size_t>(m) * K + k] : 0ull;
+    }
+    for (int e = ty * 32 + tx; e < kKT * kMT; e += 256) {
+      const int r = e / kMT, c = e % kMT;
+      const int k = k0 + r, n = n0 + c;
+      const bool ok = k < K && n < N;
+      const size_t bi = TRANS ? static_cast<size_t>(n) * K + k : static_cast<size_t>(k) * N + n;
+      sE[r][c] = ok ? Eb[bi] : 0ull;
+      sB[r][c] = ok ? B[bi] : 0ull;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int kk = 0; kk < kKT; kk++) {
+      const uint64_t e = sE[kk][tx], bb = sB[kk][tx];
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint64_t d = sD[ty + 8 * r][kk];
+        acc[r] += d * bb + sA[ty + 8 * r][kk] * e + (party == 0 ? d * e : 0ull);
+      }
+    }
+    __syncthreads();
+  }
+  const int n = n0 + tx;
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const int m = m0 + ty + 8 * r;
+    if (m < M && n < N) {
+      const size_t o = static_cast<size_t>(m) * N + n;
+      out[b * mn + o] = scaled_acc(C[o] + acc[r], has_scale, mul_const, mul_shift);
+    }
+  }
+}
+
+__global__ void row_mean_kernel(const uint64_t* __restrict__ mat, int rows, int cols, const int* __restrict__ valid,
+                                uint64_t* __restrict__ out) {
+  __shared__ uint64_t part[kThreads / 32];
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    int len = valid ? valid[r] : cols;
+    if (len > cols) len = cols;
+    const uint64_t* row = mat + static_cast<size_t>(r) * static_cast<size_t>(cols);
+    uint64_t acc = 0;
+    for (int c = threadIdx.x; c < len; c += blockDim.x) acc += row[c];
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      uint64_t v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0ull;
+      v = warp_sum(v);
+      if (threadIdx.x == 0) out[r] = len > 0 ? v / static_cast<uint64_t>(len) : 0ull;
+    }
+    __syncthreads();
+  }
+}
+
+__device__ __forceinline__ uint64_t to_signed_ring(uint64_t v, int ring_bits) {
+  if (ring_bits >= 64) return v;
+  const uint64_t m = (1ull << ring_bits) - 1ull;
+  v &= m;
+  if (v & (1ull << (ring_bits - 1))) v |= ~m;
+  return v;
+}
+
+__global__ void open_add_to_signed_kernel(const uint64_t* __restrict__ local, const uint64_t* __restrict__ remote,
+                                          uint64_t* __restrict__ out, size_t n, int ring_bits) {
+  SUFB200_GRID_LOOP(i, n) out[i] = to_signed_ring(local[i] + remote[i], ring_bits);
+}
+
+__global__ void unpack_add_to_signed_kernel(const uint64_t* __restrict__ local, const uint64_t* __restrict__ packed,
+                                            int b, uint64_t* __restrict__ out, size_t n, size_t words, int ring_bits) {
+  SUFB200_GRID_LOOP(i, n) out[i] = to_signed_ring(local[i] + unpack_one(packed, words, b, i), ring_bits);
+}
+
+__global__ void trunc_shift_kernel(const uint64_t* __restrict__ in, uint64_t* __restrict__ out, int f, size_t n) {
+  SUFB200_GRID_LOOP(i, n) out[i] = f <= 0 ? in[i] : (f >= 64 ? 0ull : (in[i] >> f));
+}
+
+}  // namespace
+
+cudaError_t prim_beaver_matmul(int party, const uint64_t* D, const uint64_t* E, const uint64_t* A, const uint64_t* B,
+                               const uint64_t* C, int batches, int M, int K, int N, int w_transposed, int has_scale,
+                               int64_t mul_const, int mul_shift, uint64_t* out, cudaStream_t st) {
+  const dim3 grid((N + kMT - 1) / kMT, (M + kMT - 1) / kMT, batches), block(32, 8);
+  if (w_transposed)
+    beaver_matmul_kernel<true><<<grid, block, 0, st>>>(party, D, E, A, B, C, M, K, N, has_scale, mul_const, mul_shift,
+                                                       out);
+  else
+    beaver_matmul_kernel<false><<<grid, block, 0, st>>>(party, D, E, A, B, C, M, K, N, has_scale, mul_const,
+                                                        mul_shift, out);
+  return cudaGetLastError();
+}
+
+cudaError_t prim_row_mean(int sm, const uint64_t* mat, int rows, int cols, const int* valid, uint64_t* out,
+                          cudaStream_t st) {
+  const int grid = rows < sm * 8 ? rows : sm * 8;
+  row_mean_kernel<<<grid, kThreads, 0, st>>>(mat, rows, cols, valid, out);
+  return cudaGetLastError();
+}
+
+cudaError_t prim_open_add_to_signed(int sm, const uint64_t* local, const uint64_t* remote, uint64_t* out, size_t n,
+                                    int ring_bits, cudaStream_t st) {
+  open_add_to_signed_kernel<<<grid_for(sm, n), kThreads, 0, st>>>(local, remote, out, n, ring_bits);
+  return cudaGetLastError();
+}
+
+cudaError_t prim_unpack_add_to_signed(int sm, const uint64_t* local, const uint64_t* packed, int b, uint64_t* out,
+                                      size_t n, int ring_bits, cudaStream_t st) {
+  unpack_add_to_signed_kernel<<<grid_for(sm, n), kThreads, 0, st>>>(local, packed, b, out, n,
+                                                                      packed_word_count(n, b), ring_bits);
+  return cudaGetLastError();
+}
+
+cudaError_t prim_trunc_shift(int sm, const uint64_t* in, uint64_t* out, int f, size_t n, cudaStream_t st) {
+  trunc_shift_kernel<<<grid_for(sm, n), kThreads, 0, st>>>(in, out, f, n);
+  return cudaGetLastError();
+}
+
+}  // namespace sufb200

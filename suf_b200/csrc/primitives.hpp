@@ -35,4 +35,15 @@ cudaError_t prim_unpack_eff_bits(int sm, const uint64_t* packed, int b, uint64_t
 cudaError_t prim_unpack_add_mod(int sm, const uint64_t* local, const uint64_t* packed, int b, uint64_t* out, size_t n,
                                 int ring_bits, cudaStream_t st);
 
+cudaError_t prim_beaver_matmul(int party, const uint64_t* D, const uint64_t* E, const uint64_t* A, const uint64_t* B,
+                               const uint64_t* C, int batches, int M, int K, int N, int w_transposed, int has_scale,
+                               int64_t mul_const, int mul_shift, uint64_t* out, cudaStream_t st);
+cudaError_t prim_row_mean(int sm, const uint64_t* mat, int rows, int cols, const int* valid, uint64_t* out,
+                          cudaStream_t st);
+cudaError_t prim_open_add_to_signed(int sm, const uint64_t* local, const uint64_t* remote, uint64_t* out, size_t n,
+                                    int ring_bits, cudaStream_t st);
+cudaError_t prim_unpack_add_to_signed(int sm, const uint64_t* local, const uint64_t* packed, int b, uint64_t* out,
+                                      size_t n, int ring_bits, cudaStream_t st);
+cudaError_t prim_trunc_shift(int sm, const uint64_t* in, uint64_t* out, int f, size_t n, cudaStream_t st);
+
 }  // namespace sufb200

@@ -92,6 +92,7 @@ struct sufb200_ctx_s {
   uint32_t* d_status = nullptr;  // device status word
   uint8_t* d_scratch = nullptr;  // staging for small broadcast keys / descriptors
   size_t scratch_bytes = 0;
+  cudaMemPool_t pool = nullptr;  // stream-ordered scratch; keeps its memory between calls
   bool prg_ready = false;
   sufb200::PrgParams prg{};
   sufb200::PrgKeys4 prg4{};

@@ -75,6 +75,12 @@ class Context:
     def sm_count(self) -> int:
         return int(self._L.sufb200_ctx_sm_count(self.h))
 
+    def probe_aes_engine(self) -> float:
+        """Measured AES-128 blocks/s of the shared-memory engine (roofline peak)."""
+        v = C.c_double()
+        check(self._L.sufb200_probe_aes_engine(self.h, C.byref(v)))
+        return float(v.value)
+
     def sync(self, stream=None) -> None:
         check(self._L.sufb200_ctx_sync(self.h, _stream_ptr(stream)))
 

@@ -163,3 +163,75 @@ def test_eff_bits_pack_unpack_and_open(ctx, torch_cuda, oracle, L, eff_bits):
     local = rand_u64(rng, n)
     L.check(L.lib().sufb200_unpack_add_mod(k.dev(local), _p(dp), eff_bits, _p(du), n, eff_bits, None))
     assert (from_dev(du) == ((local + (xs & mask)) & mask)).all()
+
+
+def _scaled(acc, has_scale, c, sh):
+    """beaver_scaled_acc (cuda/cuda_primitives.cu:391-417) on Python ints."""
+    if not has_scale:
+        return acc
+    a = acc - (1 << 64) if acc >= 1 << 63 else acc
+    prod = a * c
+    return ((prod >> sh) if sh > 0 else prod) & (2**64 - 1)
+
+
+@pytest.mark.parametrize("trans", [0, 1])
+@pytest.mark.parametrize("scale", [(0, 0, 0), (1, 4096, 12), (1, -77, 0), (1, 3, 70)])
+def test_beaver_matmul2d(ctx, torch_cuda, L, trans, scale):
+    """Attention shapes: QK^T 12 x (128x64 . 64x128), ragged edges 37x29x45."""
+    rng = np.random.default_rng(31 + trans)
+    has_scale, mul_const, mul_shift = scale
+    for batches, M, K, N in ((12, 128, 64, 128), (3, 37, 29, 45)):
+        D = rand_u64(rng, batches * M * K).reshape(batches, M, K)
+        E = rand_u64(rng, batches * K * N).reshape(batches, K, N)
+        A = rand_u64(rng, M * K).reshape(M, K)
+        B = rand_u64(rng, K * N).reshape(K, N)
+        Cm = rand_u64(rng, M * N).reshape(M, N)
+        Et = np.ascontiguousarray(E.transpose(0, 2, 1)) if trans else E
+        Bt = np.ascontiguousarray(B.T) if trans else B
+        k = Keep(torch_cuda)
+        out = torch_cuda.empty(batches * M * N, dtype=torch_cuda.int64, device="cuda")
+        for party in (0, 1):
+            L.check(L.lib().sufb200_beaver_matmul2d(party, k.dev(D.ravel()), k.dev(Et.ravel()), k.dev(A.ravel()),
+                                                    k.dev(Bt.ravel()), k.dev(Cm.ravel()), batches, M, K, N, trans,
+                                                    has_scale, mul_const, mul_shift, _p(out), None))
+            got = from_dev(out).reshape(batches, M, N)
+            with np.errstate(over="ignore"):
+                acc = Cm[None] + D @ B[None] + A[None] @ E + ((D @ E) if party == 0 else 0)
+            if has_scale:
+                exp = np.vectorize(lambda v: _scaled(int(v), 1, mul_const, mul_shift), otypes=[np.uint64])(acc)
+            else:
+                exp = acc
+            assert (got == exp).all()
+
+
+def test_row_mean_signed_opens_shift(ctx, torch_cuda, oracle, L):
+    rng = np.random.default_rng(8)
+    rows, cols = 128, 768
+    mat = rand_u64(rng, rows * cols).reshape(rows, cols)
+    valid = rng.integers(0, cols + 1, rows).astype(np.int32)
+    k = Keep(torch_cuda)
+    out = torch_cuda.empty(rows, dtype=torch_cuda.int64, device="cuda")
+    L.check(L.lib().sufb200_row_mean(k.dev(mat.ravel()), rows, cols, k.dev(valid), _p(out), None))
+    sums = oracle.row_sum(mat, valid)
+    exp = np.array([int(s) // int(v) if v > 0 else 0 for s, v in zip(sums, valid)], dtype=np.uint64)
+    assert (from_dev(out) == exp).all()
+    n = 10_001
+    a, b = rand_u64(rng, n), rand_u64(rng, n)
+    for ring in (37, 50, 64):
+        o = torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda")
+        L.check(L.lib().sufb200_open_add_to_signed(k.dev(a), k.dev(b), _p(o), n, ring, None))
+        m = (1 << ring) - 1
+        exp = np.array([((int(x) + int(y)) & m) - ((1 << ring) if ((int(x) + int(y)) & m) >> (ring - 1) else 0)
+                        for x, y in zip(a, b)], dtype=np.int64).view(np.uint64)
+        assert (from_dev(o) == exp).all()
+        packed = oracle.pack_eff_bits(b, ring)
+        L.check(L.lib().sufb200_unpack_add_to_signed(k.dev(a), k.dev(packed), ring, _p(o), n, ring, None))
+        bm = b & np.uint64(m)
+        exp2 = np.array([((int(x) + int(y)) & m) - ((1 << ring) if ((int(x) + int(y)) & m) >> (ring - 1) else 0)
+                         for x, y in zip(a, bm)], dtype=np.int64).view(np.uint64)
+        assert (from_dev(o) == exp2).all()
+    for f in (0, 12, 63, 64):
+        o = torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda")
+        L.check(L.lib().sufb200_trunc_shift(k.dev(a), _p(o), f, n, None))
+        exp = a if f == 0 else (np.zeros_like(a) if f >= 64 else a >> np.uint64(f))
+        assert (from_dev(o) == exp).all()
