@@ -98,7 +98,7 @@ M64 = (1 << 64) - 1
 # DRAM bytes per element of one fused call, from the ncu capture summarised in
 # profiles/trunc_bundle_prefix_kernel_ars_f16.md (dram read + write per launch
 # divided by the elements of that launch).
-TRAFFIC_BYTES_PER_ELEMENT = None
+TRAFFIC_BYTES_PER_ELEMENT = 14.07
 
 
 def plan_for(xh: np.ndarray, nbits: int, kmax: int):
@@ -302,7 +302,7 @@ def run_ours(args, ws, rank, local):
         "bound": "lsu", "unit": "G AES-128 blocks/s",
         "achieved": round(achieved / 1e9, 2), "peak": round(engine_peak / 1e9, 2),
         "frac": round(achieved / engine_peak, 4),
-        "traffic": TRAFFIC_BYTES_PER_ELEMENT * n,
+        "traffic": (TRAFFIC_BYTES_PER_ELEMENT * n) if TRAFFIC_BYTES_PER_ELEMENT is not None else None,
         "kernel": "trunc_bundle_prefix_kernel (+ frontier_kernel, range_kernel)",
         "peak_source": "sufb200_probe_aes_engine: the DCF walk's two-block AES-128-MMO step on every SM, "
                        "measured in this run (the table-load (LSU) and integer (ALU) pipes it saturates are the "
