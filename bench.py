@@ -83,6 +83,20 @@ def dealer(ctx):
     return r_in, (d0, d1), (keys0, keys1)
 
 
+def assignment(ws: int, rank: int, n_elem: int = N_ELEM):
+    """(parties, elements, shard) of one rank.  N = 1: both parties on the
+    configs[1] batch.  N >= 2: ranks [0, N/2) hold party 0 and [N/2, N)
+    party 1, each on its own shard of 2 * n_elem elements (the same per-GPU
+    work as N = 1: weak scaling); paired ranks j and j + N/2 hold the same
+    shard, so the two parties' shares of an element live on paired GPUs."""
+    if ws <= 1:
+        return [0, 1], n_elem, 0
+    if ws % 2:
+        raise ValueError("the party split needs an even number of GPUs")
+    half = ws // 2
+    return [0 if rank < half else 1], 2 * n_elem, rank % half
+
+
 def inputs(r_in: int, n: int, shard: int) -> np.ndarray:
     rng = np.random.default_rng([SEED, shard])
     x = rng.integers(-(2**40) + 1, 2**40, n, dtype=np.int64).view(np.uint64)
@@ -193,6 +207,15 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
 
 
+def launches_per_call(desc, n: int) -> int:
+    """Kernels one sufb200_trunc_bundle_eval call launches: the shared-prefix
+    path (n >= 16384) runs range_kernel, nq frontier_kernel launches and
+    trunc_bundle_prefix_kernel; below that one trunc_bundle_kernel."""
+    if n >= 16384 and os.environ.get("SUFB200_PREFIX", "1") != "0":
+        return 2 + int(desc.nq)
+    return 1
+
+
 def run_ours(args, ws, rank, local):
     import torch
     import torch.distributed as dist
@@ -208,16 +231,7 @@ def run_ours(args, ws, rank, local):
     ctx.prg_init(prg_state())
     r_in, descs, keys = dealer(ctx)
     nq = int(descs[0].nq)
-    n_elem = args.n_elem
-    if ws == 1:
-        parties = [0, 1]
-        n = n_elem
-        shard = 0
-    else:
-        half = max(ws // 2, 1)
-        parties = [0 if rank < half else 1]
-        n = 2 * n_elem
-        shard = rank % half
+    parties, n, shard = assignment(ws, rank, args.n_elem)
     xhat_h = inputs(r_in, n, shard)
     stream = torch.cuda.Stream(device=dev)
     d_x = torch.from_numpy(xhat_h.view(np.int64)).to(dev)
@@ -284,13 +298,28 @@ def run_ours(args, ws, rank, local):
     e2e_ms_max = float(e2e_t.item())
     e2e_value = total_units / (e2e_ms_max / 1e3)
 
-    # correctness guard on the measured outputs (reconstruction when both parties are local)
-    ok = None
+    # correctness guard on the measured outputs: y0 + y1 == x >> f.  With both
+    # parties local it is checked in place; across GPUs the paired ranks
+    # (j, j + N/2) swap their shares over NCCL (outside the timed region).
+    x = (xhat_h - np.uint64(r_in)).view(np.int64)
     if len(parties) == 2:
         y0 = d_y[0].cpu().numpy().view(np.uint64)
         y1 = d_y[1].cpu().numpy().view(np.uint64)
-        x = (xhat_h - np.uint64(r_in)).view(np.int64)
         ok = bool(((y0 + y1) == (x >> FRAC).view(np.uint64)).all())
+    else:
+        half = ws // 2
+        peer = (rank + half) % ws
+        other = torch.empty_like(d_y[parties[0]])
+        reqs = dist.batch_isend_irecv([dist.P2POp(dist.isend, d_y[parties[0]], peer),
+                                       dist.P2POp(dist.irecv, other, peer)])
+        for r in reqs:
+            r.wait()
+        ysum = d_y[parties[0]].cpu().numpy().view(np.uint64) + other.cpu().numpy().view(np.uint64)
+        ok = bool((ysum == (x >> FRAC).view(np.uint64)).all())
+    if ws > 1:
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = bool(flag.item())
 
     peaks = measured_peaks()
     engine_peak = ctx.probe_aes_engine()  # AES-128 blocks/s of the T-table engine, measured now
@@ -330,7 +359,8 @@ def run_ours(args, ws, rank, local):
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
-            "gpu_launches": args.steps * len(parties),
+            # per fused call: range_kernel + one frontier_kernel per query + the main kernel
+            "gpu_launches": args.steps * len(parties) * (launches_per_call(descs[0], n)),
             "reconstruction_ok": ok,
             "ms_per_step_all": [round(v, 4) for v in ms_steps],
         }
@@ -345,6 +375,14 @@ def run_ours(args, ws, rank, local):
 # CPU legs (the reference's own myl7 dcf_eval; test infrastructure under oracle/)
 # ---------------------------------------------------------------------------
 
+def host_threads() -> int:
+    """Host cores this process may run on (all of them for the CPU legs)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_eval_bundle(descs, keys, xhat, parties):
     """The reference CPU path of the bundle: per query, the reference's own
     myl7 dcf_eval over all elements (OpenMP in the harness), then the
@@ -352,6 +390,7 @@ def cpu_eval_bundle(descs, keys, xhat, parties):
     from oracle.oracle import GROUP_ADD, Oracle, RefMyl7, desc_from_fields
 
     ref = RefMyl7(GROUP_ADD)
+    ref.set_threads(host_threads())
     ref.prg_init(prg_state())
     orc = Oracle()
     ys = []
@@ -377,9 +416,10 @@ def cpu_baseline(args, descs, keys, r_in, ws):
     cpu_eval_bundle(descs, keys, xhat, [0, 1])
     dt = time.perf_counter() - t0
     nq = int(descs[0].nq)
-    return {"value": round(n * nq * 2 / dt, 1), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
-            "sample": f"{n} elements x {nq} queries x 2 parties, reference myl7 dcf_eval (OpenMP over elements, "
-                      f"{os.cpu_count()} threads) + composite plan/postproc; {dt:.2f} s"}
+    return {"value": round(n * nq * 2 / dt, 1), "unit": UNIT, "cores": host_threads(), "kind": "reference",
+            "sample": f"{n} elements x {nq} queries x 2 parties (the whole configs[1] batch when n = 4194304), "
+                      f"reference myl7 dcf_eval (OpenMP over elements, {host_threads()} threads) + composite "
+                      f"plan/postproc; {dt:.2f} s"}
 
 
 def run_reference(args, ws, rank):
@@ -400,7 +440,7 @@ def run_reference(args, ws, rank):
     ctx._L, ctx.h, ctx.device = _lib.lib(), h, -1
     ctx.prg_init(prg_state())
     r_in, descs, keys = dealer(ctx)
-    n = args.cpu_sample
+    n = args.ref_sample
     xhat = inputs(r_in, n, 0)
     nq = int(descs[0].nq)
     for _ in range(args.warmup):
@@ -419,7 +459,7 @@ def run_reference(args, ws, rank):
             "impl": "reference",
             "config": {"workload": "configs[1]: FaithfulARS trunc bundle, f=16, |x|<2^40, seed 2",
                        "sample_elements_per_step": n, "queries_per_element": nq, "parties": 2},
-            "cpu_baseline": {"value": round(v, 1), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+            "cpu_baseline": {"value": round(v, 1), "unit": UNIT, "cores": host_threads(), "kind": "reference",
                              "sample": f"{n} elements x {nq} queries x 2 parties per step"},
             "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -430,7 +470,10 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-sample", type=int, default=1 << 17)
+    ap.add_argument("--cpu-sample", type=int, default=N_ELEM,
+                    help="elements of the one-pass cpu_baseline leg (default: the whole configs[1] batch)")
+    ap.add_argument("--ref-sample", type=int, default=1 << 20,
+                    help="elements per step of the --impl reference arm")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--n-elem", type=int, default=N_ELEM,
                     help="elements per party at N=1 (default: the configs[1] size; smaller only for profiling)")

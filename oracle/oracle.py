@@ -290,6 +290,8 @@ class RefMyl7:
         L.ref_adapter_gen.argtypes = [C.c_int, C.c_uint64, _u8p, C.c_int, _u8p, _u8p, C.c_size_t]
         L.ref_adapter_eval_many.argtypes = [C.c_int, _u8p, C.c_size_t, C.c_int, _u64p, C.c_size_t, _u8p, C.c_int]
         L.ref_eval_many_omp.argtypes = [C.c_int, _u8p, C.c_size_t, C.c_int, _u64p, C.c_size_t, _u8p, C.c_int]
+        L.ref_set_threads.argtypes = [C.c_int]
+        L.ref_set_threads.restype = C.c_int
 
     @staticmethod
     def available(group: int = GROUP_ADD) -> bool:
@@ -333,6 +335,10 @@ class RefMyl7:
         if rc:
             raise RuntimeError(f"ref_adapter_eval_many rc={rc}")
         return out
+
+    def set_threads(self, n: int) -> int:
+        """OpenMP threads of eval_omp (n <= 0 leaves it); returns the count in effect."""
+        return int(self.L.ref_set_threads(int(n)))
 
     def eval_omp(self, in_bits, keys, key_bytes, broadcast, xs, out_len):
         xs = np.ascontiguousarray(xs, dtype=np.uint64)

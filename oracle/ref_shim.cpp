@@ -8,6 +8,8 @@
 // The result, oracle/_ref/libmyl7ref_{add,xor}.so, runs the reference's
 // actual DCF code so tests can pin oracle/suf_oracle.c and the CUDA kernels
 // per share.  Only tests/ and bench.py's reference leg load it.
+#include <omp.h>
+
 #include <cstdint>
 #include <cstring>
 #include <stdexcept>
@@ -126,6 +128,14 @@ int ref_adapter_eval_many(int in_bits, const uint8_t* keys, size_t key_bytes, in
   } catch (...) {
     return -1;
   }
+}
+
+// Thread count of the OpenMP loops below (the launcher's OMP_NUM_THREADS, e.g.
+// torchrun's default of 1, would otherwise decide it).  Returns the count now
+// in effect.
+int ref_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
 }
 
 // Same walk, run in parallel over elements (the harness-level OpenMP loop the
