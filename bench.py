@@ -116,6 +116,7 @@ TRAFFIC_BYTES_PER_ELEMENT = 14.07
 
 
 def plan_for(xh: np.ndarray, nbits: int, kmax: int):
+    """(D, count, first) of the shared-prefix plan (make_plan in prefix.cuh)."""
     piv = int(xh[0])
     off = (xh - np.uint64(piv)).view(np.int64)
     mn, mx = int(off.min()), int(off.max())
@@ -126,20 +127,38 @@ def plan_for(xh: np.ndarray, nbits: int, kmax: int):
         sh = nbits - d
         bm = (1 << sh) - 1
         cnt = (width >> sh) + (((lo_n & bm) + (width & bm)) >> sh) + 1
-        if cnt >= (1 << d):
+        covers_all = cnt >= (1 << d)
+        if covers_all:
             cnt = 1 << d
         if cnt <= kmax:
-            return d, cnt
-    return 0, 1
+            return d, cnt, 0 if covers_all else lo_n >> sh
+    return 0, 1, 0
+
+
+def prefix_budget(n: int) -> int:
+    return min(max(n // 8 * 5, 256), 1 << 23)
+
+
+def frontier_blocks(d: int, cnt: int, first: int) -> int:
+    """AES blocks of the frontier pass for one key: subtree roots at level
+    d - h walked from the root (2 blocks a level), then every child of each
+    h-level subtree (2 blocks each) -- expand_height / root_count in prefix.cuh."""
+    h = 0
+    while h < 5 and h < d and (cnt >> (h + 1)) >= 16384:
+        h += 1
+    roots = (((first & ((1 << h) - 1)) + cnt - 1) >> h) + 1
+    if d - h < 64:
+        roots = min(roots, 1 << (d - h))
+    return roots * (2 * (d - h) + 2 * ((1 << (h + 1)) - 2))
 
 
 def executed_aes_blocks(desc, xh: np.ndarray, n: int) -> float:
-    kmax = min(max(n // 16, 256), 65536)
+    kmax = prefix_budget(n)
     total = 0
     for q in range(desc.nq):
         nb = int(desc.q_bits[q])
-        d, cnt = plan_for(xh, nb, kmax) if n >= 16384 else (0, 1)
-        total += n * 2 * (nb - d) + cnt * 2 * d
+        d, cnt, first = plan_for(xh, nb, kmax) if n >= 16384 else (0, 1, 0)
+        total += n * 2 * (nb - d) + (frontier_blocks(d, cnt, first) if n >= 16384 else 0)
     return float(total)
 
 
@@ -209,10 +228,10 @@ def measured_peaks() -> dict:
 
 def launches_per_call(desc, n: int) -> int:
     """Kernels one sufb200_trunc_bundle_eval call launches: the shared-prefix
-    path (n >= 16384) runs range_kernel, nq frontier_kernel launches and
-    trunc_bundle_prefix_kernel; below that one trunc_bundle_kernel."""
+    path (n >= 16384) runs range_kernel, one frontier_kernel for all queries
+    and trunc_bundle_prefix_kernel; below that one trunc_bundle_kernel."""
     if n >= 16384 and os.environ.get("SUFB200_PREFIX", "1") != "0":
-        return 2 + int(desc.nq)
+        return 3
     return 1
 
 
@@ -336,7 +355,8 @@ def run_ours(args, ws, rank, local):
         "peak_source": "sufb200_probe_aes_engine: the DCF walk's two-block AES-128-MMO step on every SM, "
                        "measured in this run (the table-load (LSU) and integer (ALU) pipes it saturates are the "
                        "bound; see profiles/)",
-        "work_model": "executed AES blocks = N * sum_q 2*(n_q - D_q) + frontier sum_q count_q * 2 * D_q",
+        "work_model": "executed AES blocks = N * sum_q 2*(n_q - D_q) + frontier sum_q roots_q * (2*(D_q - h_q) "
+                      "+ 2*(2^(h_q+1) - 2))",
         "hbm": {"achieved": round(hbm_gbs, 2), "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
                 "frac": round(hbm_gbs / peaks.get("hbm_gbs", 6650.0), 5)},
         "kernel_ms": round(kernel_ms, 4),
@@ -359,7 +379,7 @@ def run_ours(args, ws, rank, local):
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
-            # per fused call: range_kernel + one frontier_kernel per query + the main kernel
+            # per fused call: range_kernel + frontier_kernel + the main kernel
             "gpu_launches": args.steps * len(parties) * (launches_per_call(descs[0], n)),
             "reconstruction_ok": ok,
             "ms_per_step_all": [round(v, 4) for v in ms_steps],

@@ -335,9 +335,11 @@ int sufb200_myl7_dcf_eval(sufb200_ctx ctx, int group, int in_bits, const uint8_t
                        "prefix scratch allocation");
     auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch);
     auto* F = reinterpret_cast<sufb200::FrontierEntry*>(scratch + kAccBytes);
-    sufb200::FrontierLaunch fl{d_keys, in_bits, out_bytes, acc, kmax, F, ctx->d_t0, ctx->d_status};
+    sufb200::FrontierBatch fb{};
+    fb.q[0] = sufb200::FrontierLaunch{d_keys, in_bits, out_bytes, acc, kmax, F, ctx->d_t0, ctx->d_status};
+    fb.nq = 1;
     cudaError_t e = sufb200::launch_range(ctx, d_xs, n, acc, st);
-    if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, group, fl, st);
+    if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, group, fb, st);
     if (e == cudaSuccess) e = sufb200::launch_myl7_bcast_prefix(ctx, group, a, acc, kmax, F, st);
     cudaFreeAsync(scratch, st);
     if (e != cudaSuccess) return cuda_fail(e, "myl7 DCF prefix launch");
@@ -441,13 +443,15 @@ int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, c
   if (e == cudaSuccess && prefix) {
     auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch + blob_bytes);
     sufb200::FrontierEntry* F[4] = {nullptr, nullptr, nullptr, nullptr};
-    e = sufb200::launch_range(ctx, d_xhat, n, acc, st);
-    for (int q = 0; q < desc->nq && e == cudaSuccess; q++) {
+    sufb200::FrontierBatch fb{};
+    fb.nq = desc->nq;
+    for (int q = 0; q < desc->nq; q++) {
       F[q] = reinterpret_cast<sufb200::FrontierEntry*>(scratch + blob_bytes + kAccBytes + 32ull * kmax * q);
-      sufb200::FrontierLaunch fl{scratch + a.key_off[q], desc->q_bits[q], 8, acc, kmax, F[q], ctx->d_t0,
-                                 ctx->d_status};
-      e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fl, st);
+      fb.q[q] = sufb200::FrontierLaunch{scratch + a.key_off[q], desc->q_bits[q], 8, acc, kmax, F[q], ctx->d_t0,
+                                        ctx->d_status};
     }
+    e = sufb200::launch_range(ctx, d_xhat, n, acc, st);
+    if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
     if (e == cudaSuccess) e = sufb200::launch_trunc_bundle_prefix(ctx, a, acc, kmax, F, st);
   } else if (e == cudaSuccess) {
     e = sufb200::launch_trunc_bundle(ctx, a, st);

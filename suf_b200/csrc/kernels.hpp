@@ -73,9 +73,15 @@ struct FrontierLaunch {
   const uint32_t* t0;
   uint32_t* status;
 };
+// The frontier tables of up to four keys over one batch, built in one launch
+// (blockIdx.y selects the key).
+struct FrontierBatch {
+  FrontierLaunch q[4];
+  int nq;
+};
 uint32_t prefix_budget(size_t n);
 cudaError_t launch_range(const sufb200_ctx_s* ctx, const uint64_t* xs, size_t n, RangeAcc* acc, cudaStream_t st);
-cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierLaunch& f, cudaStream_t st);
+cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st);
 cudaError_t launch_myl7_bcast_prefix(const sufb200_ctx_s* ctx, int group, const DcfLaunch& a, const RangeAcc* acc,
                                      uint32_t kmax, const FrontierEntry* F, cudaStream_t st);
 cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaunch& a, const RangeAcc* acc,

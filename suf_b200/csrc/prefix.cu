@@ -45,9 +45,45 @@ __global__ void range_kernel(const uint64_t* __restrict__ xs, size_t n, RangeAcc
   if (blockIdx.x == 0 && threadIdx.x == 0) acc->pivot = pivot;
 }
 
+SUFB200_DEV CwLevel load_cw(const BcastKeySmem* ks, int lv) {
+  CwLevel cw;
+  const uint4 cs = ks->cw_s[lv];
+  cw.s.w[0] = cs.x;
+  cw.s.w[1] = cs.y;
+  cw.s.w[2] = cs.z;
+  cw.s.w[3] = cs.w;
+  cw.v = ks->cw_v[lv];
+  cw.t = ks->cw_t[lv];
+  return cw;
+}
+
 template <int GROUP>
-__global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParams prg, const FrontierLaunch f) {
+SUFB200_DEV void emit_entry(FrontierEntry* out, uint64_t slot, bool final_level, const Blk& s, uint32_t t,
+                            uint64_t v, uint32_t party, uint64_t np1_lo) {
+  FrontierEntry e;
+  if (final_level) {
+    e.s[0] = e.s[1] = e.s[2] = e.s[3] = 0;
+    e.v = walk_finish<GROUP>(s, t, v, party, np1_lo);
+    e.t = 0;
+  } else {
+    e.s[0] = s.w[0];
+    e.s[1] = s.w[1];
+    e.s[2] = s.w[2];
+    e.s[3] = s.w[3];
+    e.v = v;
+    e.t = t;
+  }
+  e.pad = 0;
+  out[slot] = e;
+}
+
+// Frontier pass (blockIdx.y = key): one thread per subtree root
+// (frontier_root in prefix.cuh), roots dealt out round-robin over the blocks
+// so a small pass still spreads over all SMs.
+template <int GROUP>
+__global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParams prg, const FrontierBatch b) {
   extern __shared__ __align__(16) uint8_t smem[];
+  const FrontierLaunch f = b.q[blockIdx.y];
   if (!aes_layout_ok()) {
     if (threadIdx.x == 0) atomicOr(f.status, kStatusSmemLayout);
     return;
@@ -61,47 +97,25 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
     return;
   }
   const uint32_t lb = lane_base();
-  const int n = f.in_bits;
-  const Plan plan = make_plan(*f.acc, n, f.kmax);
-  const int D = static_cast<int>(plan.depth);
+  const Plan plan = make_plan(*f.acc, f.in_bits, f.kmax);
+  const int h = expand_height(plan);
+  const uint64_t roots = root_count(plan, h);
   const uint32_t party = ks->party;
-  for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < plan.count; j += gridDim.x * blockDim.x) {
-    const uint64_t pre = (plan.first + j) & nbit_mask(D);
-    const uint64_t x = D ? (pre << (n - D)) : 0ull;
-    Blk s;
-    s.w[0] = ks->seed.x;
-    s.w[1] = ks->seed.y;
-    s.w[2] = ks->seed.z;
-    s.w[3] = ks->seed.w;
-    uint32_t t = party;
-    uint64_t v = 0;
-    for (int lv = 0; lv < D; lv++) {
-      CwLevel cw;
-      const uint4 cs = ks->cw_s[lv];
-      cw.s.w[0] = cs.x;
-      cw.s.w[1] = cs.y;
-      cw.s.w[2] = cs.z;
-      cw.s.w[3] = cs.w;
-      cw.v = ks->cw_v[lv];
-      cw.t = ks->cw_t[lv];
-      walk_level<GROUP>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (n - 1 - lv)) & 1ull), party, cw);
-    }
-    FrontierEntry e;
-    if (D == n) {
-      e.s[0] = e.s[1] = e.s[2] = e.s[3] = 0;
-      e.v = walk_finish<GROUP>(s, t, v, party, ks->np1_lo);
-      e.t = 0;
-    } else {
-      e.s[0] = s.w[0];
-      e.s[1] = s.w[1];
-      e.s[2] = s.w[2];
-      e.s[3] = s.w[3];
-      e.v = v;
-      e.t = t;
-    }
-    e.pad = 0;
-    f.out[j] = e;
-  }
+  const bool final_level = static_cast<int>(plan.depth) == f.in_bits;
+  const uint64_t np1_lo = ks->np1_lo;
+  FrontierEntry* out = f.out;
+  Blk seed;
+  seed.w[0] = ks->seed.x;
+  seed.w[1] = ks->seed.y;
+  seed.w[2] = ks->seed.z;
+  seed.w[3] = ks->seed.w;
+  const auto cw_at = [ks](int lv) { return load_cw(ks, lv); };
+  const auto emit = [=](uint64_t slot, const Blk& s, uint32_t t, uint64_t v) {
+    emit_entry<GROUP>(out, slot, final_level, s, t, v, party, np1_lo);
+  };
+  const uint64_t step = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t j = static_cast<uint64_t>(threadIdx.x) * gridDim.x + blockIdx.x; j < roots; j += step)
+    frontier_root<GROUP>(prg, lb, seed, party, plan, h, j, cw_at, emit);
 }
 
 template <int GROUP>
@@ -184,10 +198,14 @@ cudaError_t set_smem(K kernel, const sufb200_ctx_s* ctx) {
 
 }  // namespace
 
+// Frontier entries allowed per key.  One level deeper saves 2 AES blocks per
+// element and costs about 6.4 blocks per added entry (subtree expansion), so
+// the best depth has about 0.3 N - 0.6 N entries; 5N/8 keeps a window that
+// straddles a bucket boundary at that depth.  Capped at 2^23 entries (256 MB).
 uint32_t prefix_budget(size_t n) {
-  size_t k = n / 16;
+  size_t k = n / 8 * 5;
   if (k < 256) k = 256;
-  if (k > 65536) k = 65536;
+  if (k > (1u << 23)) k = 1u << 23;
   return static_cast<uint32_t>(k);
 }
 
@@ -201,15 +219,18 @@ cudaError_t launch_range(const sufb200_ctx_s* ctx, const uint64_t* xs, size_t n,
   return cudaGetLastError();
 }
 
-cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierLaunch& f, cudaStream_t st) {
-  const size_t work = f.kmax;
+cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st) {
+  if (b.nq < 1 || b.nq > 4) return cudaErrorInvalidValue;
+  uint32_t work = 0;
+  for (int q = 0; q < b.nq; q++) work = b.q[q].kmax > work ? b.q[q].kmax : work;
+  const dim3 grid(static_cast<unsigned>(aes_grid(ctx, work)), static_cast<unsigned>(b.nq));
   cudaError_t e;
   if (group == SUFB200_GROUP_ADD) {
     if ((e = set_smem(frontier_kernel<SUFB200_GROUP_ADD>, ctx)) != cudaSuccess) return e;
-    frontier_kernel<SUFB200_GROUP_ADD><<<aes_grid(ctx, work), kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, f);
+    frontier_kernel<SUFB200_GROUP_ADD><<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, b);
   } else {
     if ((e = set_smem(frontier_kernel<SUFB200_GROUP_XOR>, ctx)) != cudaSuccess) return e;
-    frontier_kernel<SUFB200_GROUP_XOR><<<aes_grid(ctx, work), kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, f);
+    frontier_kernel<SUFB200_GROUP_XOR><<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, b);
   }
   return cudaGetLastError();
 }

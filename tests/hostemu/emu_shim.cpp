@@ -117,3 +117,90 @@ extern "C" uint32_t emu_plan_index(uint32_t depth, uint32_t count, uint64_t firs
   Plan p{depth, count, first};
   return plan_index(p, x, n);
 }
+
+namespace {
+CwLevel key_cw(const uint8_t* k, int lv) {
+  const uint8_t* c = k + 24 + 33 * lv;
+  CwLevel cw;
+  std::memcpy(cw.s.w, c, 16);
+  std::memcpy(&cw.v, c + 16, 8);
+  cw.t = c[32];
+  return cw;
+}
+
+template <int GROUP>
+void frontier_all(const uint8_t* k, int n, const Plan& plan, uint32_t min_roots, uint64_t* out) {
+  const uint32_t lb = lane_base();
+  const uint32_t party = k[2];
+  Blk seed;
+  std::memcpy(seed.w, k + 8, 16);
+  seed.w[3] &= 0x7FFFFFFFu;
+  uint64_t np1;
+  std::memcpy(&np1, k + 24 + 33 * n, 8);
+  const int h = expand_height(plan, min_roots);
+  const uint64_t roots = root_count(plan, h);
+  const bool final_level = static_cast<int>(plan.depth) == n;
+  const auto cw_at = [k](int lv) { return key_cw(k, lv); };
+  const auto emit = [&](uint64_t slot, const Blk& s, uint32_t t, uint64_t v) {
+    uint64_t* e = out + 4 * slot;
+    const uint64_t writes = (e[3] >> 32) + 1ull;
+    if (final_level) {
+      e[0] = e[1] = 0;
+      e[2] = walk_finish<GROUP>(s, t, v, party, np1);
+      e[3] = 0;
+    } else {
+      e[0] = (static_cast<uint64_t>(s.w[1]) << 32) | s.w[0];
+      e[1] = (static_cast<uint64_t>(s.w[3]) << 32) | s.w[2];
+      e[2] = v;
+      e[3] = t;
+    }
+    e[3] |= writes << 32;  // times written: the caller checks every slot was written once
+  };
+  for (uint64_t j = 0; j < roots; j++) frontier_root<GROUP>(g_prg, lb, seed, party, plan, h, j, cw_at, emit);
+}
+}  // namespace
+
+// The frontier pass of prefix.cu on the CPU: out[4 * slot ..] = {s lo, s hi,
+// v, t | writes << 32} for every entry (final outputs in v when depth == n);
+// out must be zeroed.
+// Returns the subtree height used.
+extern "C" int emu_frontier(int group, const uint8_t* k, int n, uint32_t depth, uint32_t count, uint64_t first,
+                            uint32_t min_roots, uint64_t* out) {
+  g_emu_lane = 0;
+  const Plan p{depth, count, first};
+  if (group == 0) frontier_all<0>(k, n, p, min_roots, out);
+  else frontier_all<1>(k, n, p, min_roots, out);
+  return expand_height(p, min_roots);
+}
+
+// Walk state after the top `depth` bits of `prefix` (given as a level-depth
+// prefix), or the final output when depth == n: the entry a frontier slot
+// must hold.
+extern "C" int emu_walk_prefix(int group, const uint8_t* k, int n, uint32_t depth, uint64_t prefix, uint64_t* e) {
+  g_emu_lane = 0;
+  const uint32_t lb = lane_base();
+  const uint32_t party = k[2];
+  Blk s;
+  std::memcpy(s.w, k + 8, 16);
+  s.w[3] &= 0x7FFFFFFFu;
+  uint32_t t = party;
+  uint64_t v = 0;
+  for (uint32_t lv = 0; lv < depth; lv++) {
+    const uint32_t xb = static_cast<uint32_t>((prefix >> (depth - 1 - lv)) & 1ull);
+    if (group == 0) walk_level<0>(g_prg, lb, s, t, v, xb, party, key_cw(k, static_cast<int>(lv)));
+    else walk_level<1>(g_prg, lb, s, t, v, xb, party, key_cw(k, static_cast<int>(lv)));
+  }
+  if (static_cast<int>(depth) == n) {
+    uint64_t np1;
+    std::memcpy(&np1, k + 24 + 33 * n, 8);
+    e[0] = e[1] = 0;
+    e[2] = group == 0 ? walk_finish<0>(s, t, v, party, np1) : walk_finish<1>(s, t, v, party, np1);
+    e[3] = 0;
+  } else {
+    e[0] = (static_cast<uint64_t>(s.w[1]) << 32) | s.w[0];
+    e[1] = (static_cast<uint64_t>(s.w[3]) << 32) | s.w[2];
+    e[2] = v;
+    e[3] = t;
+  }
+  return 0;
+}

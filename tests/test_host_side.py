@@ -146,6 +146,13 @@ def emu(tmp_path_factory):
                     str(ROOT / "tests" / "hostemu" / "emu_shim.cpp")], check=True)
     E = C.CDLL(str(out))
     E.emu_dcf_eval.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_uint64, C.c_int, C.POINTER(C.c_uint64)]
+    E.emu_frontier.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32,
+                               C.c_void_p]
+    E.emu_walk_prefix.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_uint32, C.c_uint64, C.c_void_p]
+    E.emu_make_plan.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p,
+                                C.c_void_p]
+    E.emu_plan_index.argtypes = [C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint64, C.c_int]
+    E.emu_plan_index.restype = C.c_uint32
     return E
 
 
@@ -188,3 +195,87 @@ def test_emulated_walk_matches_oracle(emu, oracle, prg_state, group):
                 v = C.c_uint64()
                 emu.emu_dcf_eval(group, k.ctypes.data, nb, C.c_uint64(int(x)), i % 32, C.byref(v))
                 assert v.value == int(ref[i])
+
+
+# ---- shared-prefix plan and frontier traversal (prefix.cuh) on the CPU ----
+
+def _plan(emu, pivot, mn, mx, n, kmax):
+    d, c, f = C.c_uint32(), C.c_uint32(), C.c_uint64()
+    emu.emu_make_plan(C.c_uint64(pivot), C.c_uint64((mn + 2**63) % 2**64), C.c_uint64((mx + 2**63) % 2**64),
+                      n, kmax, C.byref(d), C.byref(c), C.byref(f))
+    return d.value, c.value, f.value
+
+
+def test_plan_matches_brute_force(emu):
+    """make_plan picks the deepest D whose distinct D-bit prefixes over the
+    window fit kmax, and plan_index maps them one-to-one onto 0 .. count-1
+    (windows that wrap around 2^n, constant batches, full coverage)."""
+    emu.emu_plan_index.restype = C.c_uint32
+    rng = np.random.default_rng(21)
+    for trial in range(600):
+        n = int(rng.choice([6, 9, 12]))
+        M = 1 << n
+        pivot = int(rng.integers(0, 2**63)) * 2 + int(rng.integers(0, 2))
+        width = int(rng.integers(0, min(M, 1 << int(rng.integers(0, n + 1)))))
+        if trial % 50 == 0:
+            width = 0
+        mn = -int(rng.integers(0, width + 1))
+        mx = mn + width
+        kmax = int(rng.integers(1, 80))
+        d, c, f = _plan(emu, pivot, mn, mx, n, kmax)
+        vals = [((pivot + o) % 2**64) % M for o in range(mn, mx + 1)]
+        best = (0, 1)
+        for dd in range(n, 0, -1):
+            pres = {v >> (n - dd) for v in vals}
+            if len(pres) <= kmax:
+                best = (dd, len(pres))
+                break
+        assert (d, c) == best, (n, pivot, mn, mx, kmax)
+        if d:
+            idx = {}
+            for v in vals:
+                i = emu.emu_plan_index(d, c, C.c_uint64(f), C.c_uint64(v), n)
+                assert i < c
+                assert idx.setdefault(v >> (n - d), i) == i
+            assert len(set(idx.values())) == len(idx)
+
+
+@pytest.mark.parametrize("group", [GROUP_ADD, GROUP_XOR])
+def test_frontier_traversal_matches_prefix_walks(emu, oracle, prg_state, group):
+    """The frontier pass (subtree roots + depth-first expansion) stores, in
+    every slot exactly once, the state a walk of that slot's prefix from the
+    root reaches (the output itself at depth n)."""
+    emu.emu_prg_init(C.c_void_p(prg_state.ctypes.data))
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(31 + group)
+    heights = set()
+    for n, trials in ((10, 12), (16, 10), (64, 6)):
+        for trial in range(trials):
+            alpha = int(rng.integers(0, 2**63)) & ((1 << n) - 1)
+            s0, s1 = rng.integers(0, 256, (2, 16), dtype=np.uint8)
+            k0, _ = oracle.myl7_gen(group, n, alpha, rng.integers(0, 256, 8, dtype=np.uint8).tobytes(), s0, s1)
+            pivot = int(rng.integers(0, 2**63)) * 2
+            span = int(rng.integers(0, min(n, 60)))
+            width = int(rng.integers(0, 1 << span)) if span else 0
+            if trial == 0:
+                width = (1 << n) - 1 if n < 64 else 2**64 - 1  # the whole space
+            mn = -int(rng.integers(0, width + 1)) if width < 2**62 else -(width // 2)
+            if trial == 1:  # a window across 0 = 2^n
+                pivot, width = 2**64 - 3, 1 << min(n - 3, 40)
+                mn = -(width // 2)
+            mx = mn + width
+            kmax = int(rng.choice([1, 7, 40, 300])) if trial != 1 else 300
+            d, c, f = _plan(emu, pivot, mn, mx, n, kmax)
+            for min_roots in (1, 3, 16384):
+                out = np.zeros((c, 4), dtype=np.uint64)
+                h = emu.emu_frontier(group, k0.ctypes.data, n, d, c, C.c_uint64(f), min_roots, out.ctypes.data)
+                heights.add(h)
+                assert ((out[:, 3] >> np.uint64(32)) == 1).all(), (n, d, c, f, h)
+                for slot in range(c):
+                    e = np.zeros(4, dtype=np.uint64)
+                    pre = (f + slot) % (1 << d) if d < 64 else (f + slot) % 2**64
+                    emu.emu_walk_prefix(group, k0.ctypes.data, n, d, C.c_uint64(pre), e.ctypes.data)
+                    got = out[slot].copy()
+                    got[3] &= np.uint64(0xFFFFFFFF)
+                    assert (got == e).all(), (n, d, c, f, h, slot)
+    assert max(heights) >= 3 and 0 in heights
