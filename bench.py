@@ -144,7 +144,7 @@ def frontier_blocks(d: int, cnt: int, first: int) -> int:
     d - h walked from the root (2 blocks a level), then every child of each
     h-level subtree (2 blocks each) -- expand_height / root_count in prefix.cuh."""
     h = 0
-    while h < 5 and h < d and (cnt >> (h + 1)) >= 16384:
+    while h < 7 and h < d and (cnt >> (h + 1)) >= 8192:
         h += 1
     roots = (((first & ((1 << h) - 1)) + cnt - 1) >> h) + 1
     if d - h < 64:

@@ -63,6 +63,8 @@ constexpr size_t kAccBytes = 256;  // RangeAcc slot, keeps the frontier 256-byte
 struct HostIo {
   std::mutex mu;
   cudaStream_t stream = nullptr;
+  cudaStream_t copy = nullptr;    // device-to-host copies of finished chunks
+  cudaEvent_t chunk_done = nullptr;
   uint8_t* d_keys = nullptr;
   size_t keys_cap = 0;
   uint64_t* d_xs = nullptr;
@@ -104,6 +106,8 @@ void io_release(sufb200_ctx ctx) {
       if (io->d_xs) cudaFree(io->d_xs);
       if (io->d_out) cudaFree(io->d_out);
       if (io->stream) cudaStreamDestroy(io->stream);
+      if (io->copy) cudaStreamDestroy(io->copy);
+      if (io->chunk_done) cudaEventDestroy(io->chunk_done);
       delete io;
       g_io.erase(g_io.begin() + static_cast<long>(i));
       return;
@@ -388,9 +392,47 @@ int sufb200_trunc_gen(int kind, int frac_bits, uint64_t rng_seed, sufb200_trunc_
   return SUFB200_OK;
 }
 
+namespace {
+
+// Where the host entry point wants finished chunks: after the main kernel of
+// elements [i0, i1) the results are copied to the caller's host buffers on a
+// second stream, overlapping the next chunk's evaluation.
+struct ChunkSink {
+  cudaStream_t copy;
+  cudaEvent_t done;
+  uint64_t* y;      // host
+  uint64_t* bools;  // host or null
+  size_t chunk;     // elements per main-kernel launch
+};
+
+int enqueue_chunk_copy(const ChunkSink& k, cudaStream_t st, const uint64_t* d_y, const uint64_t* d_b, size_t i0,
+                       size_t i1) {
+  SUFB200_CHECK_CUDA(cudaEventRecord(k.done, st), "chunk event");
+  SUFB200_CHECK_CUDA(cudaStreamWaitEvent(k.copy, k.done, 0), "chunk wait");
+  SUFB200_CHECK_CUDA(cudaMemcpyAsync(k.y + i0, d_y + i0, (i1 - i0) * 8, cudaMemcpyDeviceToHost, k.copy), "D2H y");
+  if (k.bools)
+    SUFB200_CHECK_CUDA(cudaMemcpyAsync(k.bools + 3 * i0, d_b + 3 * i0, (i1 - i0) * 24, cudaMemcpyDeviceToHost, k.copy),
+                       "D2H bools");
+  return SUFB200_OK;
+}
+
+int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                      const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y, uint64_t* d_bools,
+                      void* stream, const ChunkSink* sink);
+
+}  // namespace
+
 int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
                               const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y,
                               uint64_t* d_bools, void* stream) {
+  return trunc_bundle_impl(ctx, desc, keys, key_bytes, d_xhat, n, d_y, d_bools, stream, nullptr);
+}
+
+namespace {
+
+int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                      const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y, uint64_t* d_bools,
+                      void* stream, const ChunkSink* sink) {
   if (int rc = check_ctx(ctx, true)) return rc;
   if (!desc || !keys || !key_bytes) return fail(SUFB200_ERR_INVALID, "null pointer");
   if (desc->nq < 0 || desc->nq > 4) return fail(SUFB200_ERR_UNSUPPORTED, "bundle has more than 4 queries");
@@ -452,14 +494,39 @@ int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, c
     }
     e = sufb200::launch_range(ctx, d_xhat, n, acc, st);
     if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
-    if (e == cudaSuccess) e = sufb200::launch_trunc_bundle_prefix(ctx, a, acc, kmax, F, st);
+    // the main pass, in chunks when a host sink streams results back (the
+    // kernel's outputs do not depend on the element index)
+    const size_t chunk = sink && sink->chunk ? sink->chunk : n;
+    for (size_t i0 = 0; i0 < n && e == cudaSuccess; i0 += chunk) {
+      const size_t i1 = n - i0 < chunk ? n : i0 + chunk;
+      sufb200::TruncLaunch c = a;
+      c.xhat = d_xhat + i0;
+      c.n = i1 - i0;
+      c.y = d_y + i0;
+      c.bools = d_bools ? d_bools + 3 * i0 : nullptr;
+      e = sufb200::launch_trunc_bundle_prefix(ctx, c, acc, kmax, F, st);
+      if (e == cudaSuccess && sink) {
+        if (int rc = enqueue_chunk_copy(*sink, st, d_y, d_bools, i0, i1)) {
+          cudaFreeAsync(scratch, st);
+          return rc;
+        }
+      }
+    }
   } else if (e == cudaSuccess) {
     e = sufb200::launch_trunc_bundle(ctx, a, st);
+    if (e == cudaSuccess && sink) {
+      if (int rc = enqueue_chunk_copy(*sink, st, d_y, d_bools, 0, n)) {
+        cudaFreeAsync(scratch, st);
+        return rc;
+      }
+    }
   }
   cudaFreeAsync(scratch, st);
   if (e != cudaSuccess) return cuda_fail(e, "trunc bundle launch");
   return SUFB200_OK;
 }
+
+}  // namespace
 
 int sufb200_trunc_bundle_eval_host(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
                                    const size_t* key_bytes, const uint64_t* xhat, size_t n, uint64_t* y,
@@ -473,13 +540,19 @@ int sufb200_trunc_bundle_eval_host(sufb200_ctx ctx, const sufb200_trunc_desc* de
   const size_t out_bytes = n * 8 * (bools ? 4 : 1);
   if (int rc = grow(reinterpret_cast<void**>(&io->d_xs), &io->xs_cap, n * 8)) return rc;
   if (int rc = grow(reinterpret_cast<void**>(&io->d_out), &io->out_cap, out_bytes)) return rc;
+  if (!io->copy) SUFB200_CHECK_CUDA(cudaStreamCreateWithFlags(&io->copy, cudaStreamNonBlocking), "copy stream");
+  if (!io->chunk_done)
+    SUFB200_CHECK_CUDA(cudaEventCreateWithFlags(&io->chunk_done, cudaEventDisableTiming), "chunk event");
   uint64_t* d_y = reinterpret_cast<uint64_t*>(io->d_out);
   uint64_t* d_b = bools ? d_y + n : nullptr;
   SUFB200_CHECK_CUDA(cudaMemcpyAsync(io->d_xs, xhat, n * 8, cudaMemcpyHostToDevice, io->stream), "H2D xhat");
-  if (int rc = sufb200_trunc_bundle_eval(ctx, desc, keys, key_bytes, io->d_xs, n, d_y, d_b, io->stream)) return rc;
-  SUFB200_CHECK_CUDA(cudaMemcpyAsync(y, d_y, n * 8, cudaMemcpyDeviceToHost, io->stream), "D2H y");
-  if (bools)
-    SUFB200_CHECK_CUDA(cudaMemcpyAsync(bools, d_b, n * 24, cudaMemcpyDeviceToHost, io->stream), "D2H bools");
+  // Eight main-kernel launches over large batches, each chunk's results
+  // copied back while the next one is evaluated.
+  const ChunkSink sink{io->copy, io->chunk_done, y, bools, n >= (1u << 20) ? (n + 7) / 8 : n};
+  const int rc = trunc_bundle_impl(ctx, desc, keys, key_bytes, io->d_xs, n, d_y, d_b, io->stream, &sink);
+  const cudaError_t ce = cudaStreamSynchronize(io->copy);
+  if (rc) return rc;
+  SUFB200_CHECK_CUDA(ce, "D2H chunk copies");
   return sufb200_ctx_sync(ctx, io->stream);
 }
 

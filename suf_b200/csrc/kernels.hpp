@@ -74,7 +74,7 @@ struct FrontierLaunch {
   uint32_t* status;
 };
 // The frontier tables of up to four keys over one batch, built in one launch
-// (blockIdx.y selects the key).
+// (all keys share the range accumulator and the status word of q[0]).
 struct FrontierBatch {
   FrontierLaunch q[4];
   int nq;

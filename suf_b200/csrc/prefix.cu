@@ -77,45 +77,101 @@ SUFB200_DEV void emit_entry(FrontierEntry* out, uint64_t slot, bool final_level,
   out[slot] = e;
 }
 
-// Frontier pass (blockIdx.y = key): one thread per subtree root
-// (frontier_root in prefix.cuh), roots dealt out round-robin over the blocks
-// so a small pass still spreads over all SMs.
+// Per-key parameters of a frontier pass, computed once per block.
+struct FrontierKey {
+  Plan plan;
+  FrontierEntry* out;
+  uint64_t roots;   // subtree roots (work items) of this key
+  int h;            // subtree height
+  int final_level;  // D == n: entries are outputs
+};
+
+// Staging area at the start of dynamic shared memory, below the AES tables
+// (no static shared memory: it would move the table window).
+struct FrontierStage {
+  BcastKeySmem key[4];
+  FrontierKey fk[4];
+  uint64_t first_item[5];
+  int order[4];
+};
+static_assert(sizeof(FrontierStage) < kTabBase - 4096, "staging must fit below the tables");
+
+// Frontier pass over all keys of a batch in one wave: every key is staged in
+// shared memory and the work items (subtree roots, frontier_root in
+// prefix.cuh) of all keys form one list, the most expensive keys' items
+// first, dealt out round-robin over the blocks so each SM gets a share of
+// each kind.
 template <int GROUP>
 __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParams prg, const FrontierBatch b) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const FrontierLaunch f = b.q[blockIdx.y];
   if (!aes_layout_ok()) {
-    if (threadIdx.x == 0) atomicOr(f.status, kStatusSmemLayout);
+    if (threadIdx.x == 0) atomicOr(b.q[0].status, kStatusSmemLayout);
     return;
   }
-  BcastKeySmem* ks = reinterpret_cast<BcastKeySmem*>(smem);
-  stage_bcast_key(ks, f.key, f.in_bits, f.out_bytes);
-  aes_fill_tables(f.t0);
+  const int nq = b.nq;
+  FrontierStage* fs = reinterpret_cast<FrontierStage*>(smem);
+  BcastKeySmem* ks = fs->key;
+  FrontierKey* fk = fs->fk;
+  int* order = fs->order;
+  uint64_t* first_item = fs->first_item;
+#pragma unroll
+  for (int q = 0; q < 4; q++)
+    if (q < nq) stage_bcast_key(&ks[q], b.q[q].key, b.q[q].in_bits, b.q[q].out_bytes);
+  aes_fill_tables(b.q[0].t0);
+  if (threadIdx.x == 0) {
+    uint64_t cost[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      if (q >= nq) continue;
+      const Plan p = make_plan(*b.q[q].acc, b.q[q].in_bits, b.q[q].kmax);
+      const int h = expand_height(p);
+      fk[q].plan = p;
+      fk[q].out = b.q[q].out;
+      fk[q].roots = root_count(p, h);
+      fk[q].h = h;
+      fk[q].final_level = static_cast<int>(p.depth) == b.q[q].in_bits;
+      cost[q] = 2ull * static_cast<uint64_t>(static_cast<int>(p.depth) - h) + 4ull * (1ull << h);
+      order[q] = q;
+    }
+    for (int i = 1; i < nq; i++)  // most expensive items first
+      for (int k = i; k > 0 && cost[order[k]] > cost[order[k - 1]]; k--) {
+        const int t = order[k];
+        order[k] = order[k - 1];
+        order[k - 1] = t;
+      }
+    first_item[0] = 0;
+    for (int r = 0; r < nq; r++) first_item[r + 1] = first_item[r] + fk[order[r]].roots;
+  }
   __syncthreads();
-  if (!ks->ok) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(f.status, kStatusBadKeyHeader);
-    return;
-  }
+  for (int q = 0; q < nq; q++)
+    if (!ks[q].ok) {
+      if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(b.q[0].status, kStatusBadKeyHeader);
+      return;
+    }
   const uint32_t lb = lane_base();
-  const Plan plan = make_plan(*f.acc, f.in_bits, f.kmax);
-  const int h = expand_height(plan);
-  const uint64_t roots = root_count(plan, h);
-  const uint32_t party = ks->party;
-  const bool final_level = static_cast<int>(plan.depth) == f.in_bits;
-  const uint64_t np1_lo = ks->np1_lo;
-  FrontierEntry* out = f.out;
-  Blk seed;
-  seed.w[0] = ks->seed.x;
-  seed.w[1] = ks->seed.y;
-  seed.w[2] = ks->seed.z;
-  seed.w[3] = ks->seed.w;
-  const auto cw_at = [ks](int lv) { return load_cw(ks, lv); };
-  const auto emit = [=](uint64_t slot, const Blk& s, uint32_t t, uint64_t v) {
-    emit_entry<GROUP>(out, slot, final_level, s, t, v, party, np1_lo);
-  };
+  const uint64_t total = first_item[nq];
   const uint64_t step = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-  for (uint64_t j = static_cast<uint64_t>(threadIdx.x) * gridDim.x + blockIdx.x; j < roots; j += step)
-    frontier_root<GROUP>(prg, lb, seed, party, plan, h, j, cw_at, emit);
+  for (uint64_t it = static_cast<uint64_t>(threadIdx.x) * gridDim.x + blockIdx.x; it < total; it += step) {
+    int r = 0;
+    while (r + 1 < nq && it >= first_item[r + 1]) r++;
+    const int q = order[r];
+    const BcastKeySmem* k = &ks[q];
+    const FrontierKey& f = fk[q];
+    Blk seed;
+    seed.w[0] = k->seed.x;
+    seed.w[1] = k->seed.y;
+    seed.w[2] = k->seed.z;
+    seed.w[3] = k->seed.w;
+    const uint32_t party = k->party;
+    const uint64_t np1_lo = k->np1_lo;
+    const bool final_level = f.final_level != 0;
+    FrontierEntry* out = f.out;
+    const auto cw_at = [k](int lv) { return load_cw(k, lv); };
+    const auto emit = [=](uint64_t slot, const Blk& s, uint32_t t, uint64_t v) {
+      emit_entry<GROUP>(out, slot, final_level, s, t, v, party, np1_lo);
+    };
+    frontier_root<GROUP>(prg, lb, seed, party, f.plan, f.h, it - first_item[r], cw_at, emit);
+  }
 }
 
 template <int GROUP>
@@ -221,9 +277,9 @@ cudaError_t launch_range(const sufb200_ctx_s* ctx, const uint64_t* xs, size_t n,
 
 cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st) {
   if (b.nq < 1 || b.nq > 4) return cudaErrorInvalidValue;
-  uint32_t work = 0;
-  for (int q = 0; q < b.nq; q++) work = b.q[q].kmax > work ? b.q[q].kmax : work;
-  const dim3 grid(static_cast<unsigned>(aes_grid(ctx, work)), static_cast<unsigned>(b.nq));
+  size_t work = 0;
+  for (int q = 0; q < b.nq; q++) work += b.q[q].kmax;
+  const int grid = aes_grid(ctx, work);
   cudaError_t e;
   if (group == SUFB200_GROUP_ADD) {
     if ((e = set_smem(frontier_kernel<SUFB200_GROUP_ADD>, ctx)) != cudaSuccess) return e;

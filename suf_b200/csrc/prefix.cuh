@@ -12,7 +12,7 @@
 //      covers the whole n-bit space): one thread walks from the root to a
 //      subtree root at level D - h, then expands the h levels below it
 //      depth-first, both children of every inner node, so a prefix costs
-//      about 4 + 2(D - h)/2^h AES blocks instead of 2D;
+//      about 4 + 2(D - h)/2^h AES blocks instead of 2D (h <= 7);
 //   4. the main pass resumes every element from its prefix's state at level D.
 // The outputs are the same bits as a walk from the root: step 4 replays the
 // identical level sequence, it only skips recomputing shared levels.
@@ -75,11 +75,12 @@ SUFB200_HD Plan make_plan(const RangeAcc& r, int n, uint32_t kmax) {
   return p;
 }
 
-// Subtree height h of the frontier pass: the largest h <= min(5, D) that still
+// Subtree height h of the frontier pass: the largest h <= min(7, D) that still
 // leaves at least kMinRoots subtree roots (so the pass fills the GPU).  It
-// only decides how the frontier work is split; the entries are the same.
-constexpr int kMaxExpand = 5;
-constexpr uint32_t kMinRoots = 16384;
+// only decides how the frontier work is split; the entries are the same.  At
+// h = 7 an entry costs about 4 + 2(D - 7)/128 AES blocks.
+constexpr int kMaxExpand = 7;
+constexpr uint32_t kMinRoots = 8192;
 
 SUFB200_HD int expand_height(const Plan& p, uint32_t min_roots = kMinRoots) {
   int h = 0;

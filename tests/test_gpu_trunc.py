@@ -109,3 +109,32 @@ def test_bundle_shared_prefix_path_bit_exact(ctx, torch_cuda, oracle, prg_state,
         ys.append(y)
     exp = (x >> np.uint64(16)) if kind == KIND_TR else (x.view(np.int64) >> 16).view(np.uint64)
     assert ((ys[0] + ys[1]) == exp).all()
+
+
+def test_host_entry_chunked_matches_device_entry(ctx, torch_cuda, oracle, prg_state):
+    """sufb200_trunc_bundle_eval_host above 2^20 elements runs the main pass
+    in eight chunks with the copies back overlapped: same y and bool shares
+    as the device entry, for a size that does not divide into eight, twice
+    in a row (reused host-io buffers)."""
+    oracle.prg_init(prg_state)
+    n = (1 << 20) + 13
+    rng = np.random.default_rng(4)
+    x = signed_fixed(rng, n, 40)
+    r_in, descs, keys = trunc_material(oracle, KIND_GAPARS, 12, 3)
+    xhat = x + np.uint64(r_in)
+    dx = to_dev(torch_cuda, xhat)
+    ys = []
+    for p in (0, 1):
+        d = to_product_desc(descs[p])
+        db = torch_cuda.zeros(3 * n, dtype=torch_cuda.int64, device="cuda")
+        dy = from_dev(ctx.trunc_bundle_eval(d, keys[p], dx, d_bools=db))
+        ctx.sync()
+        for _ in range(2):
+            hb = np.zeros(3 * n, dtype=np.uint64)
+            hy = ctx.trunc_bundle_eval_host(d, keys[p], xhat, bools=hb)
+            assert (hy == dy).all()
+            assert (hb == from_dev(db)).all()
+        ys.append(hy)
+    assert ((ys[0] + ys[1]) == (x.view(np.int64) >> 12).view(np.uint64)).all()
+    idx = rng.integers(0, n, 128)
+    assert (ys[1][idx] == oracle_trunc_eval(oracle, descs[1], keys[1], xhat[idx])).all()
