@@ -177,6 +177,8 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        if self.gpu is None:
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
@@ -235,6 +237,67 @@ def launches_per_call(desc, n: int) -> int:
     return 1
 
 
+def _max_over_ranks(ws: int, dev, v: float) -> float:
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed(args, ws, dev, stream, flush, step, ctx, local, sample_clocks=True):
+    """W untimed steps, then K steps bracketed by a barrier and a device
+    synchronize, each timed by CUDA events on the launch stream after a 256 MB
+    write (> 126 MB L2); returns (max over ranks of the mean step ms, this
+    rank's step times, the clock sampler)."""
+    import torch
+    import torch.distributed as dist
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    ctx.sync(stream)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clk = ClockSampler(local if sample_clocks else None)
+    with clk:
+        if sample_clocks:
+            time.sleep(0.3)
+        with torch.cuda.stream(stream):
+            for k in range(args.steps):
+                flush.fill_(k)
+                evs[k][0].record(stream)
+                step()
+                evs[k][1].record(stream)
+        torch.cuda.synchronize()
+        ctx.sync(stream)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms_steps = [a.elapsed_time(b) for a, b in evs]
+    return _max_over_ranks(ws, dev, sum(ms_steps) / len(ms_steps)), ms_steps, clk
+
+
+def _pair_check(ws: int, rank: int, dev, d_mine, want: np.ndarray) -> bool:
+    """Paired ranks j and j + N/2 swap their shares over NCCL and check
+    mine + theirs == want; the flag is reduced over all ranks."""
+    import torch
+    import torch.distributed as dist
+
+    peer = (rank + ws // 2) % ws
+    other = torch.empty_like(d_mine)
+    for r in dist.batch_isend_irecv([dist.P2POp(dist.isend, d_mine, peer), dist.P2POp(dist.irecv, other, peer)]):
+        r.wait()
+    ysum = d_mine.cpu().numpy().view(np.uint64) + other.cpu().numpy().view(np.uint64)
+    flag = torch.tensor([1 if bool((ysum == want).all()) else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return bool(flag.item())
+
+
 def run_ours(args, ws, rank, local):
     import torch
     import torch.distributed as dist
@@ -250,7 +313,7 @@ def run_ours(args, ws, rank, local):
     ctx.prg_init(prg_state())
     r_in, descs, keys = dealer(ctx)
     nq = int(descs[0].nq)
-    parties, n, shard = assignment(ws, rank, args.n_elem)
+    parties, n, shard = assignment(ws, rank, args.n_elem or N_ELEM)
     xhat_h = inputs(r_in, n, shard)
     stream = torch.cuda.Stream(device=dev)
     d_x = torch.from_numpy(xhat_h.view(np.int64)).to(dev)
@@ -262,34 +325,7 @@ def run_ours(args, ws, rank, local):
         for p in parties:
             ctx.trunc_bundle_eval(descs[p], keys[p], d_x, d_y=d_y[p], stream=stream)
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step()
-    ctx.sync(stream)
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    with ClockSampler(local) as clk:
-        time.sleep(0.3)
-        with torch.cuda.stream(stream):
-            for k in range(args.steps):
-                flush.fill_(k)  # write 256 MB (> 126 MB L2) between timed steps
-                evs[k][0].record(stream)
-                step()
-                evs[k][1].record(stream)
-        torch.cuda.synchronize()
-        ctx.sync(stream)
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ms_steps = [a.elapsed_time(b) for a, b in evs]
-    ms = sum(ms_steps) / len(ms_steps)
-    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if ws > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
+    ms_max, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
     units_per_rank = n * nq * len(parties)
     total_units = units_per_rank * ws
     value = total_units / (ms_max / 1e3)
@@ -311,34 +347,20 @@ def run_ours(args, ws, rank, local):
         for p in parties:
             ctx.trunc_bundle_eval_host(descs[p], keys[p], x_np, y=y_np[p])
         e2e_ms.append((time.perf_counter() - t0) * 1e3)
-    e2e_t = torch.tensor([sum(e2e_ms) / len(e2e_ms)], dtype=torch.float64, device=dev)
-    if ws > 1:
-        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-    e2e_ms_max = float(e2e_t.item())
+    e2e_ms_max = _max_over_ranks(ws, dev, sum(e2e_ms) / len(e2e_ms))
     e2e_value = total_units / (e2e_ms_max / 1e3)
 
     # correctness guard on the measured outputs: y0 + y1 == x >> f.  With both
     # parties local it is checked in place; across GPUs the paired ranks
     # (j, j + N/2) swap their shares over NCCL (outside the timed region).
     x = (xhat_h - np.uint64(r_in)).view(np.int64)
+    want = (x >> FRAC).view(np.uint64)
     if len(parties) == 2:
         y0 = d_y[0].cpu().numpy().view(np.uint64)
         y1 = d_y[1].cpu().numpy().view(np.uint64)
-        ok = bool(((y0 + y1) == (x >> FRAC).view(np.uint64)).all())
+        ok = bool(((y0 + y1) == want).all())
     else:
-        half = ws // 2
-        peer = (rank + half) % ws
-        other = torch.empty_like(d_y[parties[0]])
-        reqs = dist.batch_isend_irecv([dist.P2POp(dist.isend, d_y[parties[0]], peer),
-                                       dist.P2POp(dist.irecv, other, peer)])
-        for r in reqs:
-            r.wait()
-        ysum = d_y[parties[0]].cpu().numpy().view(np.uint64) + other.cpu().numpy().view(np.uint64)
-        ok = bool((ysum == (x >> FRAC).view(np.uint64)).all())
-    if ws > 1:
-        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
-        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-        ok = bool(flag.item())
+        ok = _pair_check(ws, rank, dev, d_y[parties[0]], want)
 
     peaks = measured_peaks()
     engine_peak = ctx.probe_aes_engine()  # AES-128 blocks/s of the T-table engine, measured now
@@ -451,13 +473,7 @@ def run_reference(args, ws, rank):
         return {"impl": "reference", "unavailable": "oracle/_ref (reference myl7 sources) was not built"}
     from suf_b200.engine import Context
 
-    ctx = Context.__new__(Context)  # dealer only: host context, no GPU work
-    import ctypes as C
-    from suf_b200 import _lib
-
-    h = C.c_void_p()
-    _lib.check(_lib.lib().sufb200_ctx_create(-1, C.byref(h)))
-    ctx._L, ctx.h, ctx.device = _lib.lib(), h, -1
+    ctx = Context(-1)  # dealer only (SUFB200_HOST_ONLY): no GPU work
     ctx.prg_init(prg_state())
     r_in, descs, keys = dealer(ctx)
     n = args.ref_sample
@@ -483,6 +499,203 @@ def run_reference(args, ws, rank):
                              "sample": f"{n} elements x {nq} queries x 2 parties per step"},
             "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
+# ---------------------------------------------------------------------------
+# batched single-predicate DCF compare, per-element keys
+# ---------------------------------------------------------------------------
+
+CMP_N = 1 << 20
+CMP_METRIC = "DCF pred-evals/sec (single-predicate compare 1[x^ < r_in], per-element myl7 keys)"
+
+
+def compare_material(ctx, n: int, shard: int):
+    """r_in[i] = successive mt19937_64(1) draws, x uniform with
+    |x| < 2^36 (|v| < 2^20 with 16 fractional bits) from the draws after the
+    masks, x^ = x + r_in; per-element myl7 keys for 1[x^ < r_in] with payload 1
+    (additive Z_2^64 shares), seeds from mt19937_64(1 ^ 0x5EED)."""
+    from suf_b200 import GROUP_ADD
+    from suf_b200.engine import host_mt19937_64
+
+    total = n * (shard + 1)
+    draws = host_mt19937_64(1, 2 * total)
+    r_in = draws[shard * n:(shard + 1) * n].copy()
+    x = ((draws[total + shard * n: total + (shard + 1) * n] >> np.uint64(27)).view(np.int64) - (1 << 36))
+    xhat = x.view(np.uint64) + r_in
+    seeds = host_mt19937_64(1 ^ 0x5EED, 4 * total).view(np.uint8).reshape(total, 2, 16)[shard * n:(shard + 1) * n]
+    k0, k1 = ctx.myl7_gen_batch(GROUP_ADD, 64, r_in, (1).to_bytes(8, "little"), seeds[:, 0].copy(),
+                                seeds[:, 1].copy())
+    return r_in, xhat, (k0, k1)
+
+
+def threshold_keys(alphas: np.ndarray, payload: int) -> np.ndarray:
+    """Per-element keys of the reference GPU backend's DcfKeyHeader format
+    (packed {u16 in_bits, u16 payload_len, u64 alpha} + 8-byte payload)."""
+    rec = np.zeros(alphas.size, dtype=np.dtype([("in_bits", "<u2"), ("plen", "<u2"), ("alpha", "<u8"),
+                                                 ("pay", "<u8")]))
+    rec["in_bits"] = 64
+    rec["plen"] = 8
+    rec["alpha"] = alphas
+    rec["pay"] = payload
+    return rec.view(np.uint8).reshape(alphas.size, 20)
+
+
+def run_compare(args, ws, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200 import GROUP_ADD
+    from suf_b200.engine import Context, thr_dcf_key
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    ctx = Context(local)
+    ctx.prg_init(prg_state())
+    parties, n, shard = assignment(ws, rank, args.n_elem or CMP_N)
+    r_in, xhat, keys = compare_material(ctx, n, shard)
+    kb = keys[0].shape[1]
+    stream = torch.cuda.Stream(device=dev)
+    d_x = torch.from_numpy(xhat.view(np.int64)).to(dev)
+    d_k = {p: torch.from_numpy(keys[p].reshape(-1)).to(dev) for p in parties}
+    d_y = {p: torch.empty(n, dtype=torch.int64, device=dev) for p in parties}
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+    torch.cuda.synchronize()
+
+    def step():
+        for p in parties:
+            ctx.myl7_eval(GROUP_ADD, 64, d_k[p], kb, False, d_x, 8, d_out=d_y[p], stream=stream)
+
+    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    units = n * len(parties) * ws
+    value = units / (ms / 1e3)
+
+    # reconstruction: y0 + y1 == 1[x^ < r_in]
+    want = (xhat < r_in).astype(np.uint64)
+    if len(parties) == 2:
+        ok = bool(((d_y[0].cpu().numpy().view(np.uint64) + d_y[1].cpu().numpy().view(np.uint64)) == want).all())
+    else:
+        ok = _pair_check(ws, rank, dev, d_y[parties[0]], want)
+
+    # e2e: the host-buffer entry point (keys, x^ in; shares out), copies timed
+    x_pin = torch.from_numpy(xhat.view(np.int64)).pin_memory().numpy().view(np.uint64)
+    k_pin = {p: torch.from_numpy(keys[p]).pin_memory().numpy() for p in parties}
+    o_pin = {p: torch.empty(n * 8, dtype=torch.uint8).pin_memory().numpy().reshape(n, 8) for p in parties}
+    for p in parties:
+        ctx.myl7_eval_host(GROUP_ADD, 64, k_pin[p], kb, False, x_pin, 8, outs=o_pin[p])
+    e2e = []
+    for _ in range(max(1, min(args.steps, 3))):
+        t0 = time.perf_counter()
+        for p in parties:
+            ctx.myl7_eval_host(GROUP_ADD, 64, k_pin[p], kb, False, x_pin, 8, outs=o_pin[p])
+        e2e.append((time.perf_counter() - t0) * 1e3)
+    e2e_ms = _max_over_ranks(ws, dev, sum(e2e) / len(e2e))
+
+    # the reference GPU backend's trivial threshold format (20-byte keys): HBM-bound
+    thr = {p: threshold_keys(r_in, 1 if p == 0 else 0) for p in parties}
+    for p in parties:  # the vectorised blobs are the library builder's bytes
+        for i in (0, n // 2, n - 1):
+            want_k = thr_dcf_key(64, int(r_in[i]), (1 if p == 0 else 0).to_bytes(8, "little"))
+            assert (thr[p][i] == want_k).all()
+    d_t = {p: torch.from_numpy(thr[p].reshape(-1)).to(dev) for p in parties}
+    d_o = {p: torch.empty(n, dtype=torch.int64, device=dev) for p in parties}
+
+    def thr_step():
+        for p in parties:
+            ctx.thr_dcf_eval(64, d_t[p], 20, False, d_x, 8, d_out=d_o[p], stream=stream)
+
+    thr_ms, _, _ = _timed(args, ws, dev, stream, flush, thr_step, ctx, local, sample_clocks=False)
+
+    peaks = measured_peaks()
+    engine_peak = ctx.probe_aes_engine()
+    kernel_ms = ms / len(parties)
+    blocks = n * 2 * 64  # two AES blocks (seed and value halves of the PRG) per level, 64 levels
+    hbm_bytes = n * (kb + 16)
+    roofline = {"bound": "lsu", "unit": "G AES-128 blocks/s",
+                "achieved": round(blocks / (kernel_ms / 1e3) / 1e9, 2), "peak": round(engine_peak / 1e9, 2),
+                "frac": round(blocks / (kernel_ms / 1e3) / engine_peak, 4), "traffic": hbm_bytes,
+                "kernel": "myl7_eval_elem_aligned_kernel",
+                "work_model": "128 AES blocks per element (2 per level x 64 levels)",
+                "hbm": {"achieved": round(hbm_bytes / (kernel_ms / 1e3) / 1e9, 1), "peak": peaks.get("hbm_gbs"),
+                        "unit": "GB/s", "bytes_per_element": kb + 16},
+                "kernel_ms": round(kernel_ms, 4)}
+    thr_gbs = n * 36 / (thr_ms / len(parties) / 1e3) / 1e9
+    out = None
+    if rank == 0:
+        cpu = cpu_compare_baseline(args, keys, xhat, kb) if (ws == 1 and not args.no_cpu) else None
+        out = {"metric": CMP_METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128", "data": "synthetic (seeded, configs[0] shapes)",
+               "config": {"workload": "configs[0]: DCF compare 1[x^ < r_in], per-element keys, seed 1",
+                          "n_elements_per_party_per_gpu": n, "parties_per_gpu": len(parties),
+                          "key_bytes": kb, "l2": "keys (2.2 GB per party) larger than L2; 256 MB flush as well",
+                          "parallelism": f"party x element shards on {ws} GPU(s)"},
+               "e2e": {"value": round(units / (e2e_ms / 1e3), 1), "unit": UNIT,
+                       "h2d_bytes_per_step": len(parties) * n * (kb + 8), "d2h_bytes_per_step": len(parties) * n * 8,
+                       "ms_per_step": round(e2e_ms, 3), "path": "sufb200_myl7_dcf_eval_host (pinned keys and x^)"},
+               "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
+               "gpu_launches": args.steps * len(parties), "reconstruction_ok": ok,
+               "reference_threshold_format": {
+                   "value": round(units / (thr_ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(thr_ms, 4),
+                   "hbm_gbs": round(thr_gbs, 1), "hbm_frac": round(thr_gbs / peaks.get("hbm_gbs", 6650.0), 3),
+                   "kernel": "thr_dcf_kernel (DcfKeyHeader keys, 20 B + 8 B x^ + 8 B out per element)"},
+               "ms_per_step_all": [round(v, 4) for v in ms_steps]}
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return out
+
+
+def cpu_compare_baseline(args, keys, xhat, kb):
+    """The reference's myl7 dcf_eval over a bounded sample of configs[0]
+    (per-element keys), OpenMP over elements, both parties."""
+    from oracle.oracle import GROUP_ADD, RefMyl7
+
+    if not RefMyl7.available():
+        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference", "sample": "oracle/_ref not built"}
+    ref = RefMyl7(GROUP_ADD)
+    ref.set_threads(host_threads())
+    ref.prg_init(prg_state())
+    n = min(args.cpu_sample, xhat.size, 1 << 18)
+    t0 = time.perf_counter()
+    for p in (0, 1):
+        ref.eval_omp(64, keys[p][:n], kb, False, xhat[:n], 8)
+    dt = time.perf_counter() - t0
+    return {"value": round(2 * n / dt, 1), "unit": UNIT, "cores": host_threads(), "kind": "reference",
+            "sample": f"{n} elements x 2 parties, reference myl7 dcf_eval (OpenMP over elements, "
+                      f"{host_threads()} threads); {dt:.2f} s"}
+
+
+def run_compare_reference(args, ws, rank):
+    from oracle.oracle import RefMyl7
+
+    if rank != 0:
+        return None
+    if not RefMyl7.available():
+        return {"impl": "reference", "unavailable": "oracle/_ref (reference myl7 sources) was not built"}
+    from suf_b200.engine import Context
+
+    ctx = Context(-1)
+    ctx.prg_init(prg_state())
+    n = min(args.ref_sample, CMP_N)
+    r_in, xhat, keys = compare_material(ctx, n, 0)
+    kb = keys[0].shape[1]
+    a = argparse.Namespace(cpu_sample=n)
+    for _ in range(args.warmup):
+        cpu_compare_baseline(argparse.Namespace(cpu_sample=max(1, n // 8)), keys, xhat, kb)
+    vals = [cpu_compare_baseline(a, keys, xhat, kb) for _ in range(args.steps)]
+    ctx.close()
+    v = sum(x["value"] for x in vals) / len(vals)
+    return {"metric": CMP_METRIC, "value": round(v, 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(2 * n / v * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128",
+            "data": "synthetic (seeded, configs[0] shapes)", "impl": "reference",
+            "config": {"workload": "configs[0]: DCF compare 1[x^ < r_in], per-element keys, seed 1",
+                       "sample_elements_per_step": n, "parties": 2},
+            "cpu_baseline": dict(vals[-1], value=round(v, 1)),
+            "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -495,11 +708,16 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=1 << 20,
                     help="elements per step of the --impl reference arm")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--n-elem", type=int, default=N_ELEM,
-                    help="elements per party at N=1 (default: the configs[1] size; smaller only for profiling)")
+    ap.add_argument("--n-elem", type=int, default=None,
+                    help="elements per party at N=1 (default: the workload's config size; smaller only for "
+                         "profiling)")
+    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare"],
+                    help="trunc: configs[1] (the headline line); compare: configs[0], per-element keys")
     args = ap.parse_args()
     ws, rank, local = dist_env()
-    if args.impl == "reference":
+    if args.workload == "compare":
+        out = run_compare_reference(args, ws, rank) if args.impl == "reference" else run_compare(args, ws, rank, local)
+    elif args.impl == "reference":
         out = run_reference(args, ws, rank)
     else:
         out = run_ours(args, ws, rank, local)

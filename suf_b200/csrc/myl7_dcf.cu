@@ -95,19 +95,30 @@ __global__ void __launch_bounds__(kAesThreads, 1)
     s.w[3] = static_cast<uint32_t>(s1 >> 32) & 0x7FFFFFFFu;
     uint32_t t = party;
     uint64_t v = 0;
+    const uintptr_t kaddr = reinterpret_cast<uintptr_t>(k);
     for (int lv = 0; lv < n; lv++) {
-      const uint32_t o = 24u + 33u * static_cast<uint32_t>(lv);
-      const uint64_t* q = k + (o >> 3);
-      const uint32_t r = o & 7u;
-      const uint64_t q0 = __ldg(q), q1 = __ldg(q + 1), q2 = __ldg(q + 2), q3 = __ldg(q + 3), q4 = __ldg(q + 4);
+      // The 33-byte record of level lv lies inside the three aligned 16-byte
+      // chunks from its address rounded down to 16 (offset <= 15, 15 + 33 <=
+      // 48; the last chunk ends at or before byte 38 + 33n of the 40 + 33n
+      // byte key): three 16-byte loads instead of five 8-byte ones.
+      const uintptr_t A = kaddr + 24u + 33u * static_cast<uint32_t>(lv);
+      const uint4* c = reinterpret_cast<const uint4*>(A & ~static_cast<uintptr_t>(15));
+      const uint4 c0 = __ldg(c), c1 = __ldg(c + 1), c2 = __ldg(c + 2);
+      const uint32_t r = static_cast<uint32_t>(A & 15u);
+      const bool hi = r >= 8u;
+      const uint32_t rb = r & 7u;
+      const uint64_t w0 = (static_cast<uint64_t>(c0.y) << 32) | c0.x, w1 = (static_cast<uint64_t>(c0.w) << 32) | c0.z;
+      const uint64_t w2 = (static_cast<uint64_t>(c1.y) << 32) | c1.x, w3 = (static_cast<uint64_t>(c1.w) << 32) | c1.z;
+      const uint64_t w4 = (static_cast<uint64_t>(c2.y) << 32) | c2.x, w5 = (static_cast<uint64_t>(c2.w) << 32) | c2.z;
+      const uint64_t q0 = hi ? w1 : w0, q1 = hi ? w2 : w1, q2 = hi ? w3 : w2, q3 = hi ? w4 : w3, q4 = hi ? w5 : w4;
       CwLevel cw;
-      const uint64_t slo = funnel64(q0, q1, r), shi = funnel64(q1, q2, r);
+      const uint64_t slo = funnel64(q0, q1, rb), shi = funnel64(q1, q2, rb);
       cw.s.w[0] = static_cast<uint32_t>(slo);
       cw.s.w[1] = static_cast<uint32_t>(slo >> 32);
       cw.s.w[2] = static_cast<uint32_t>(shi);
       cw.s.w[3] = static_cast<uint32_t>(shi >> 32);
-      cw.v = funnel64(q2, q3, r);
-      cw.t = static_cast<uint32_t>((q4 >> (8u * r)) & 0xFFu);
+      cw.v = funnel64(q2, q3, rb);
+      cw.t = static_cast<uint32_t>((q4 >> (8u * rb)) & 0xFFu);
       const uint32_t xb = static_cast<uint32_t>((x >> (n - 1 - lv)) & 1ull);
       walk_level<GROUP>(prg, lb, s, t, v, xb, party, cw);
     }

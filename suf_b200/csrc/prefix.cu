@@ -74,7 +74,10 @@ SUFB200_DEV void emit_entry(FrontierEntry* out, uint64_t slot, bool final_level,
     e.t = t;
   }
   e.pad = 0;
-  out[slot] = e;
+  // two 16-byte stores: one sector per entry instead of a partial write per field
+  uint4* o = reinterpret_cast<uint4*>(out + slot);
+  o[0] = make_uint4(e.s[0], e.s[1], e.s[2], e.s[3]);
+  o[1] = make_uint4(static_cast<uint32_t>(e.v), static_cast<uint32_t>(e.v >> 32), e.t, 0u);
 }
 
 // Per-key parameters of a frontier pass, computed once per block.

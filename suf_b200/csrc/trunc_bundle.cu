@@ -179,6 +179,18 @@ struct FrontierSet {
   const FrontierEntry* F[4];
 };
 
+// Per-query plan, frontier table and width, staged once per block after the
+// keys (the query loop index is uniform across a warp, so these are
+// broadcast reads instead of per-thread local-memory copies).
+struct QueryPlanSmem {
+  Plan plan;
+  const FrontierEntry* F;
+  int nb;
+  int pad;
+};
+static_assert(4 * sizeof(QueryKeySmem) + 4 * sizeof(QueryPlanSmem) < kTabBase - 4096,
+              "staging must fit below the tables");
+
 __global__ void __launch_bounds__(kAesThreads, 1)
     trunc_bundle_prefix_kernel(const PrgParams prg, const TruncLaunch a, const RangeAcc* acc, uint32_t kmax,
                                const FrontierSet fs) {
@@ -189,24 +201,33 @@ __global__ void __launch_bounds__(kAesThreads, 1)
   }
   const sufb200_trunc_desc& d = a.desc;
   QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);
-  if (!stage_bundle(ks, a)) return;
+  QueryPlanSmem* qp = reinterpret_cast<QueryPlanSmem*>(smem + 4 * sizeof(QueryKeySmem));
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int nb = d.q_bits[q];
+      qp[q].plan = q < d.nq ? make_plan(*acc, nb, kmax) : Plan{0, 1, 0};
+      qp[q].F = fs.F[q];
+      qp[q].nb = nb;
+      qp[q].pad = 0;
+    }
+  }
+  if (!stage_bundle(ks, a)) return;  // its barrier also publishes qp
   const uint32_t lb = lane_base();
   const uint32_t party = static_cast<uint32_t>(d.party);
-  Plan plan[4];
-  for (int q = 0; q < 4; q++) plan[q] = q < d.nq ? make_plan(*acc, d.q_bits[q], kmax) : Plan{0, 1, 0};
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
     const uint64_t xh = a.xhat[i];
     uint64_t pr[4] = {0, 0, 0, 0};
 #pragma unroll 1
     for (int q = 0; q < d.nq; q++) {
-      const int nb = d.q_bits[q];
+      const int nb = qp[q].nb;
       const uint64_t x = xh & nbit_mask(nb);
-      const Plan& P = plan[q];
+      const Plan P = qp[q].plan;
       const uint32_t idx = plan_index(P, x, nb);
       uint64_t v;
       if (idx < P.count) {
-        const FrontierEntry e = fs.F[q][idx];
+        const FrontierEntry e = qp[q].F[idx];
         if (P.depth == static_cast<uint32_t>(nb)) {
           v = e.v;
         } else {
