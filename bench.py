@@ -109,10 +109,11 @@ def inputs(r_in: int, n: int, shard: int) -> np.ndarray:
 # ---------------------------------------------------------------------------
 
 M64 = (1 << 64) - 1
-# DRAM bytes per element of one fused call, from the ncu capture summarised in
-# profiles/trunc_bundle_prefix_kernel_ars_f16.md (dram read + write per launch
-# divided by the elements of that launch).
-TRAFFIC_BYTES_PER_ELEMENT = 14.07
+# DRAM bytes per element of trunc_bundle_prefix_kernel, from the ncu capture
+# summarised in profiles/trunc_bundle_prefix_kernel_ars_f16.md (dram read +
+# write of one 4,194,304-element launch divided by its elements): 16 B of x^
+# and y plus the random 32-byte frontier-entry reads of the four queries.
+TRAFFIC_BYTES_PER_ELEMENT = 142.1
 
 
 def plan_for(xh: np.ndarray, nbits: int, kmax: int):
@@ -154,11 +155,12 @@ def frontier_blocks(d: int, cnt: int, first: int) -> int:
 
 def executed_aes_blocks(desc, xh: np.ndarray, n: int) -> float:
     kmax = prefix_budget(n)
+    prefix = n >= 16384 and os.environ.get("SUFB200_PREFIX", "1") != "0"  # else: a root walk per query
     total = 0
     for q in range(desc.nq):
         nb = int(desc.q_bits[q])
-        d, cnt, first = plan_for(xh, nb, kmax) if n >= 16384 else (0, 1, 0)
-        total += n * 2 * (nb - d) + (frontier_blocks(d, cnt, first) if n >= 16384 else 0)
+        d, cnt, first = plan_for(xh, nb, kmax) if prefix else (0, 1, 0)
+        total += n * 2 * (nb - d) + (frontier_blocks(d, cnt, first) if prefix else 0)
     return float(total)
 
 
@@ -372,8 +374,11 @@ def run_ours(args, ws, rank, local):
         "bound": "lsu", "unit": "G AES-128 blocks/s",
         "achieved": round(achieved / 1e9, 2), "peak": round(engine_peak / 1e9, 2),
         "frac": round(achieved / engine_peak, 4),
-        "traffic": (TRAFFIC_BYTES_PER_ELEMENT * n) if TRAFFIC_BYTES_PER_ELEMENT is not None else None,
-        "kernel": "trunc_bundle_prefix_kernel (+ frontier_kernel, range_kernel)",
+        "traffic": round(TRAFFIC_BYTES_PER_ELEMENT * n) if TRAFFIC_BYTES_PER_ELEMENT is not None else None,
+        "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size launch (caches "
+                          "flushed per pass), per element, times this call's elements",
+        "kernel": ("trunc_bundle_prefix_kernel (+ frontier_kernel, range_kernel)"
+                   if launches_per_call(descs[0], n) == 3 else "trunc_bundle_kernel"),
         "peak_source": "sufb200_probe_aes_engine: the DCF walk's two-block AES-128-MMO step on every SM, "
                        "measured in this run (the table-load (LSU) and integer (ALU) pipes it saturates are the "
                        "bound; see profiles/)",
@@ -504,6 +509,9 @@ def run_reference(args, ws, rank):
 # ---------------------------------------------------------------------------
 
 CMP_N = 1 << 20
+# DRAM bytes per element of myl7_eval_elem_aligned_kernel from its ncu capture
+# ((594.6 + 8.3) MB / 262,144): the 2,152-byte key, x^, y and some re-reads.
+CMP_TRAFFIC_BYTES_PER_ELEMENT = 2299.8
 CMP_METRIC = "DCF pred-evals/sec (single-predicate compare 1[x^ < r_in], per-element myl7 keys)"
 
 
@@ -612,7 +620,10 @@ def run_compare(args, ws, rank, local):
     hbm_bytes = n * (kb + 16)
     roofline = {"bound": "lsu", "unit": "G AES-128 blocks/s",
                 "achieved": round(blocks / (kernel_ms / 1e3) / 1e9, 2), "peak": round(engine_peak / 1e9, 2),
-                "frac": round(blocks / (kernel_ms / 1e3) / engine_peak, 4), "traffic": hbm_bytes,
+                "frac": round(blocks / (kernel_ms / 1e3) / engine_peak, 4),
+                "traffic": round(CMP_TRAFFIC_BYTES_PER_ELEMENT * n),
+                "traffic_source": "ncu dram read + write of one 262,144-element launch, per element "
+                                  "(profiles/myl7_eval_elem_aligned_kernel_compare.md), times this call's elements",
                 "kernel": "myl7_eval_elem_aligned_kernel",
                 "work_model": "128 AES blocks per element (2 per level x 64 levels)",
                 "hbm": {"achieved": round(hbm_bytes / (kernel_ms / 1e3) / 1e9, 1), "peak": peaks.get("hbm_gbs"),
