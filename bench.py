@@ -707,6 +707,88 @@ def run_compare_reference(args, ws, rank):
             "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ---------------------------------------------------------------------------
+# the paired-GPU open (configs[4] open traffic): N >= 2
+# ---------------------------------------------------------------------------
+
+OPEN_WORDS = 16_700_000   # words opened per layer per party (bert-base, measured by the reference)
+OPEN_FLUSHES = 120        # flushes per layer
+OPEN_METRIC = "opened words/sec (paired-GPU open, configs[4] layer: 120 flushes, 16.7 M words per party)"
+NVLINK_GBS = 770.0        # measured peer copy per direction on this pool
+
+
+def run_open(args, ws, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200.engine import Context, OpenComm, share_open_id
+
+    if ws < 2 or ws % 2:
+        if rank == 0:
+            return {"metric": OPEN_METRIC, "unavailable": "the open pairs GPU j with GPU j + N/2: run with N >= 2"}
+        return None
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    ctx = Context(local)
+    comm = OpenComm(ctx, share_open_id(rank), ws, rank, timeout_s=60.0)
+    peer = (rank + ws // 2) % ws
+    ring = args.ring_bits
+    eff = ring if ring <= 56 else 64  # SUF_OPEN_PACK_MAX_BITS default
+    per = (args.n_elem or OPEN_WORDS) // OPEN_FLUSHES
+    rng = np.random.default_rng([5, rank % (ws // 2)])
+    m = np.uint64((1 << ring) - 1) if ring < 64 else np.uint64(~np.uint64(0))
+    x = rng.integers(0, 2**63, per * OPEN_FLUSHES, dtype=np.uint64) & m
+    s0 = rng.integers(0, 2**63, x.size, dtype=np.uint64) & m
+    mine = s0 if rank < ws // 2 else (x - s0) & m
+    d_in = torch.from_numpy(mine.view(np.int64)).to(dev).view(OPEN_FLUSHES, per)
+    d_out = torch.empty_like(d_in)
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+
+    def step():
+        for f in range(OPEN_FLUSHES):
+            comm.exchange(peer, d_in[f], eff, ring, signed=True, d_out=d_out[f], stream=stream)
+
+    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    want = x.copy()
+    if ring < 64:
+        sign = (want >> np.uint64(ring - 1)) & np.uint64(1)
+        want |= (np.uint64(0) - sign) & ~m
+    ok = bool((d_out.cpu().numpy().reshape(-1).view(np.uint64) == want).all())
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    ok = bool(flag.item())
+    words = per * OPEN_FLUSHES
+    wire = -(-per * eff // 64) * 8 * OPEN_FLUSHES  # bytes each GPU sends per step
+    gbs = wire / (ms / 1e3) / 1e9
+    out = None
+    if rank == 0:
+        out = {"metric": OPEN_METRIC, "value": round(words * ws / (ms / 1e3), 1), "unit": "opened words/s",
+               "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": f"u64 (Z_2^{ring})",
+               "data": "synthetic (seeded shares)",
+               "config": {"workload": "configs[4] open traffic: one layer of flushes per step",
+                          "words_per_party_per_pair": words, "flushes": OPEN_FLUSHES, "ring_bits": ring,
+                          "eff_bits": eff, "pairs": ws // 2, "l2": "256 MB flush between steps",
+                          "parallelism": f"party 0 on GPUs 0..{ws // 2 - 1}, party 1 on the rest"},
+               "e2e": {"value": round(words * ws / (ms / 1e3), 1), "unit": "opened words/s",
+                       "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0,
+                       "note": "device-resident by design: the shares and the opened values stay in HBM"},
+               "roofline": {"bound": "nvlink", "unit": "GB/s", "achieved": round(gbs, 2), "peak": NVLINK_GBS,
+                            "frac": round(gbs / NVLINK_GBS, 4), "traffic": wire,
+                            "note": "bytes each GPU sends per step / step time, vs the measured peer copy per "
+                                    "direction; 120 flushes of 139 K words are latency-bound"},
+               "clocks": clk.summary(), "gpu_launches": args.steps * OPEN_FLUSHES * (2 if eff < 64 else 1),
+               "opened_ok": ok, "ms_per_flush": round(ms / OPEN_FLUSHES, 4),
+               "ms_per_step_all": [round(v, 4) for v in ms_steps]}
+    dist.barrier()
+    comm.close()
+    dist.destroy_process_group()
+    ctx.close()
+    return out
+
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -722,11 +804,19 @@ def main():
     ap.add_argument("--n-elem", type=int, default=None,
                     help="elements per party at N=1 (default: the workload's config size; smaller only for "
                          "profiling)")
-    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare"],
-                    help="trunc: configs[1] (the headline line); compare: configs[0], per-element keys")
+    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open"],
+                    help="trunc: configs[1] (the headline line); compare: configs[0], per-element keys; "
+                         "open: the paired-GPU open of a configs[4] layer (N >= 2)")
+    ap.add_argument("--ring-bits", type=int, default=37, help="ring of the open workload (37: the reference's "
+                                                                 "measured bert-base ring)")
     args = ap.parse_args()
     ws, rank, local = dist_env()
-    if args.workload == "compare":
+    if args.workload == "open":
+        out = ({"impl": "reference", "unavailable": "the reference's open runs through its host channel "
+                "(net::Chan); no stand-alone CPU implementation of the exchange to time"}
+               if args.impl == "reference" and rank == 0 else None) if args.impl == "reference" else \
+            run_open(args, ws, rank, local)
+    elif args.workload == "compare":
         out = run_compare_reference(args, ws, rank) if args.impl == "reference" else run_compare(args, ws, rank, local)
     elif args.impl == "reference":
         out = run_reference(args, ws, rank)

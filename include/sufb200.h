@@ -33,6 +33,7 @@ extern "C" {
 #define SUFB200_ERR_KEY (-3)          /* key blob header / size mismatch */
 #define SUFB200_ERR_UNSUPPORTED (-4)  /* valid but outside this engine's scope */
 #define SUFB200_ERR_NOT_READY (-5)    /* sufb200_prg_init not called yet */
+#define SUFB200_ERR_COMM (-6)         /* NCCL error or timeout in the paired-GPU open */
 
 #define SUFB200_GROUP_ADD 0 /* myl7 u128_le group: additive shares mod 2^64 (low 8 bytes) */
 #define SUFB200_GROUP_XOR 1 /* myl7 bytes group: XOR shares */
@@ -290,6 +291,33 @@ int sufb200_unpack_add_mod(const uint64_t* d_local, const uint64_t* d_packed_rem
  * (launch_unpack_add_to_signed_kernel). */
 int sufb200_unpack_add_to_signed(const uint64_t* d_local, const uint64_t* d_packed_remote, int eff_bits,
                                  uint64_t* d_out, size_t n, int ring_bits, void* stream);
+
+/* ---- paired-GPU open ------------------------------------------------------
+ * Replaces the exchange of OpenCollector::flush
+ * (src/runtime/open_collector.cpp:357-895), which packs a flush, moves it
+ * device -> host -> net::Chan -> host -> device and adds the peer's words:
+ * here the two parties' GPUs (party 0 on GPU j, party 1 on GPU j + N/2)
+ * swap the packed words over NVLink in one NCCL group call, enqueued with the
+ * pack and the add on the caller's stream.
+ *
+ * sufb200_open_unique_id writes the 128-byte NCCL id on one rank; the caller
+ * hands it to the others out of band.  sufb200_open_comm_create joins the
+ * communicator (all nranks ranks call it) and returns SUFB200_ERR_COMM if the
+ * peers have not all joined within timeout_s seconds.  sufb200_open_exchange:
+ * both ranks of a pair call it with the same n, eff_bits and ring_bits;
+ * d_out = local + peer (mod 2^ring_bits; sign-extended from ring_bits when
+ * signed_out) for the low eff_bits of every share (eff_bits = 64 sends the
+ * raw words).  If a peer stops calling, its partner's exchange never
+ * completes on the GPU: sufb200_open_comm_abort (from any thread) ends it. */
+#define SUFB200_OPEN_ID_BYTES 128
+typedef struct sufb200_open_comm_s* sufb200_open_comm;
+int sufb200_open_unique_id(uint8_t* id);
+int sufb200_open_comm_create(sufb200_ctx ctx, const uint8_t* id, int nranks, int rank, double timeout_s,
+                             sufb200_open_comm* out);
+int sufb200_open_comm_destroy(sufb200_open_comm comm);
+int sufb200_open_comm_abort(sufb200_open_comm comm);
+int sufb200_open_exchange(sufb200_open_comm comm, int peer, const uint64_t* d_local, size_t n, int eff_bits,
+                          int ring_bits, int signed_out, uint64_t* d_out, void* stream);
 
 /* local + remote, sign-extended to ring_bits (launch_open_add_to_signed_kernel). */
 int sufb200_open_add_to_signed(const uint64_t* d_local, const uint64_t* d_remote, uint64_t* d_out, size_t n,

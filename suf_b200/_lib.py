@@ -19,6 +19,7 @@ ERR_CUDA = -2
 ERR_KEY = -3
 ERR_UNSUPPORTED = -4
 ERR_NOT_READY = -5
+ERR_COMM = -6
 
 GROUP_ADD = 0
 GROUP_XOR = 1
@@ -94,6 +95,11 @@ _SIGS = {
     "sufb200_unpack_add_mod": (_i, [_vp, _vp, _i, _vp, _sz, _i, _vp]),
     "sufb200_unpack_add_to_signed": (_i, [_vp, _vp, _i, _vp, _sz, _i, _vp]),
     "sufb200_open_add_to_signed": (_i, [_vp, _vp, _vp, _sz, _i, _vp]),
+    "sufb200_open_unique_id": (_i, [_vp]),
+    "sufb200_open_comm_create": (_i, [_vp, _vp, _i, _i, C.c_double, C.POINTER(_vp)]),
+    "sufb200_open_comm_destroy": (_i, [_vp]),
+    "sufb200_open_comm_abort": (_i, [_vp]),
+    "sufb200_open_exchange": (_i, [_vp, _i, _vp, _sz, _i, _i, _i, _vp, _vp]),
     "sufb200_row_mean": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "sufb200_trunc_shift": (_i, [_vp, _vp, _i, _sz, _vp]),
     "sufb200_beaver_matmul2d": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, C.c_int64, _i, _vp, _vp]),

@@ -64,7 +64,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
             print(r.stderr, file=sys.stderr)
         objs.append(str(obj))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc, *ARCH, "-shared", "-Xcompiler", "-fopenmp", "-o", str(tmp), *objs, "-lgomp"]
+    cmd = [nvcc, *ARCH, "-shared", "-Xcompiler", "-fopenmp", "-o", str(tmp), *objs, "-lgomp", "-ldl"]
     if verbose:
         print(" ".join(cmd), flush=True)
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -213,6 +213,66 @@ class Context:
         return d_out
 
 
+# -- paired-GPU open ---------------------------------------------------------------
+
+OPEN_ID_BYTES = 128
+
+
+def open_unique_id() -> bytes:
+    """A fresh NCCL id for sufb200_open_comm_create (made on one rank)."""
+    buf = (C.c_uint8 * OPEN_ID_BYTES)()
+    check(_lib.lib().sufb200_open_unique_id(C.cast(buf, C.c_void_p)))
+    return bytes(buf)
+
+
+def share_open_id(rank: int, group=None) -> bytes:
+    """Rank 0 makes the id and every rank of the torch.distributed group gets
+    it (any backend: the id is 128 host bytes)."""
+    import torch.distributed as dist
+
+    box = [open_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0, group=group)
+    return box[0]
+
+
+class OpenComm:
+    """The communicator of the paired-GPU open (sufb200_open_*): party 0 on
+    GPU j and party 1 on GPU j + N/2 swap eff_bits-packed shares over NVLink
+    and add them, on the caller's stream."""
+
+    def __init__(self, ctx: Context, uid: bytes, nranks: int, rank: int, timeout_s: float = 60.0):
+        if len(uid) != OPEN_ID_BYTES:
+            raise ValueError("the NCCL id is 128 bytes")
+        self._L = ctx._L
+        self.ctx = ctx
+        self.rank = rank
+        self.nranks = nranks
+        h = C.c_void_p()
+        idb = (C.c_uint8 * OPEN_ID_BYTES).from_buffer_copy(uid)
+        check(self._L.sufb200_open_comm_create(ctx.h, C.cast(idb, C.c_void_p), nranks, rank, float(timeout_s),
+                                               C.byref(h)))
+        self.h = h
+
+    def exchange(self, peer: int, d_local, eff_bits: int, ring_bits: int, signed: bool = False, d_out=None,
+                 stream=None):
+        import torch
+
+        if d_out is None:
+            d_out = torch.empty_like(d_local)
+        check(self._L.sufb200_open_exchange(self.h, peer, _t_ptr(d_local), d_local.numel(), eff_bits, ring_bits,
+                                            int(signed), _t_ptr(d_out), _stream_ptr(stream)))
+        return d_out
+
+    def abort(self) -> None:
+        if self.h:
+            check(self._L.sufb200_open_comm_abort(self.h))
+
+    def close(self) -> None:
+        if self.h:
+            h, self.h = self.h, C.c_void_p()
+            check(self._L.sufb200_open_comm_destroy(h))
+
+
 # -- key builders for the reference formats (host) ---------------------------------
 
 def thr_dcf_key(in_bits: int, alpha: int, payload: bytes) -> np.ndarray:

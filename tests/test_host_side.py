@@ -5,6 +5,7 @@ from __future__ import annotations
 import ctypes as C
 import re
 import subprocess
+import sys
 from pathlib import Path
 
 import numpy as np
@@ -279,3 +280,34 @@ def test_frontier_traversal_matches_prefix_walks(emu, oracle, prg_state, group):
                     got[3] &= np.uint64(0xFFFFFFFF)
                     assert (got == e).all(), (n, d, c, f, h, slot)
     assert max(heights) >= 3 and 0 in heights
+
+
+# ---- paired-GPU open: host-side checks (no GPU) ----
+
+def test_open_rejects_host_only_context_and_null_comm():
+    import ctypes as C
+
+    from suf_b200 import _lib
+    from suf_b200.engine import Context
+
+    ctx = Context(-1)
+    try:
+        h = C.c_void_p()
+        uid = (C.c_uint8 * 128)()
+        rc = _lib.lib().sufb200_open_comm_create(ctx.h, C.cast(uid, C.c_void_p), 2, 0, 5.0, C.byref(h))
+        assert rc == _lib.ERR_INVALID and not h.value
+        assert b"GPU" in _lib.lib().sufb200_last_error()
+        rc = _lib.lib().sufb200_open_exchange(None, 1, None, 4, 64, 64, 0, None, None)
+        assert rc == _lib.ERR_INVALID
+    finally:
+        ctx.close()
+
+
+def test_open_unique_id_after_torch():
+    """The id comes from the NCCL the process already holds (torch's, when
+    torch is imported first): two ids, 128 bytes each, differ."""
+    code = ("import torch, sys; sys.path.insert(0, %r); from suf_b200.engine import open_unique_id; "
+            "a = open_unique_id(); b = open_unique_id(); assert len(a) == len(b) == 128 and a != b; print('ok')"
+            % str(ROOT))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]

@@ -96,3 +96,35 @@ def test_assignment_rules():
         assert all(v == {0, 1} for v in seen.values()) and len(seen) == ws // 2
     with pytest.raises(ValueError):
         bench.assignment(3, 0)
+
+
+def _id_worker(rank: int, port: int, q):
+    sys.path.insert(0, str(ROOT))
+    import torch.distributed as dist
+
+    from suf_b200.engine import share_open_id
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        q.put((rank, share_open_id(rank)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_open_id_shared_over_gloo():
+    """Rank 0 makes the NCCL id of the paired-GPU open; both ranks hold the
+    same 128 bytes afterwards (the hand-off the communicator needs)."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_id_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = dict(q.get(timeout=5) for _ in range(2))
+    assert len(got[0]) == 128 and got[0] == got[1]
