@@ -24,6 +24,16 @@ def test_adapter_compiles_against_mirror():
     subprocess.run(["g++", *FLAGS, "-fsyntax-only", str(ROOT / "suf_b200" / "host" / "make_backend.cpp")], check=True)
 
 
+def test_paired_open_handle_compiles(tmp_path):
+    src = tmp_path / "open_tu.cpp"
+    src.write_text('#include "sufb200_open.hpp"\n'
+                   'int f(sufb200_ctx c, cudaStream_t s, const uint64_t* a, uint64_t* b) {\n'
+                   '  sufb200::PairedOpen o(c, sufb200::PairedOpen::unique_id(), 2, 0, 1);\n'
+                   '  o.exchange(a, 8, sufb200::PairedOpen::eff_bits_for_ring(37), 37, true, b, s);\n'
+                   '  return sufb200::PairedOpen::eff_bits_for_ring(64); }\n')
+    subprocess.run(["g++", *FLAGS, "-fsyntax-only", str(src)], check=True)
+
+
 @pytest.mark.skipif(not (REF / "include" / "proto" / "backend_gpu.hpp").exists(), reason="reference checkout absent")
 def test_adapter_compiles_against_reference_headers():
     subprocess.run(["g++", *FLAGS, "-DSUFB200_WITH_REFERENCE_PROTO", "-DSUF_HAVE_CUDA", f"-I{REF / 'include'}",
