@@ -789,6 +789,152 @@ def run_open(args, ws, rank, local):
     return out
 
 
+# ---------------------------------------------------------------------------
+# the SiLU spline gate (interval-LUT coefficients, one pass)
+# ---------------------------------------------------------------------------
+
+SILU_N = 1 * 128 * 3072
+SILU_METRIC = "SiLU gate evals/sec (configs[2]: interval-LUT coefficients + output masks, one pass per party)"
+
+
+def silu_inputs(n: int, frac_bits: int, shard: int) -> np.ndarray:
+    """x ~ N(0, 4^2) quantised at frac_bits (numpy default_rng([3, shard]))."""
+    rng = np.random.default_rng([3, shard])
+    return np.rint(rng.normal(0.0, 4.0, n) * 2.0**frac_bits).astype(np.int64).view(np.uint64)
+
+
+def run_silu(args, ws, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200.engine import Context, coeff_lut_eval
+    from tests.helpers import silu_fixture, suf_table_eval
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    ctx = Context(local)
+    ctx.prg_init(prg_state())  # the engine-ceiling probe runs the PRG step
+    fx = silu_fixture()  # the reference's own dealer output (tests/golden/make_silu_fixture.py)
+    parties, n, shard = assignment(ws, rank, args.n_elem or SILU_N)
+    x = silu_inputs(n, fx["frac_bits"], shard)
+    xhat = x + np.uint64(fx["r_in"])
+    r = fx["r"]
+    stream = torch.cuda.Stream(device=dev)
+    d_x = torch.from_numpy(xhat.view(np.int64)).to(dev)
+    d_y = {p: torch.empty(n * r, dtype=torch.int64, device=dev) for p in parties}
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+
+    def step():
+        for p in parties:
+            coeff_lut_eval(ctx, fx["keys"][p], d_x, r, fx["degree"], r_out=fx[f"r_out_share{p}"], d_out=d_y[p],
+                           stream=stream)
+
+    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    units = n * len(parties) * ws
+    want = suf_table_eval(fx["alpha"], fx["pieces"], x)
+    if len(parties) == 2:
+        y = [d_y[p].cpu().numpy().view(np.uint64).reshape(n, r) for p in (0, 1)]
+        ok = bool(((y[0] + y[1] - fx["r_out"]) == want).all())
+    else:  # y0 + y1 = coefficients + r_out, checked across the paired GPUs
+        ok = _pair_check(ws, rank, dev, d_y[parties[0]], (want + fx["r_out"]).reshape(-1))
+
+    # e2e: pinned host x^ in, the r coefficient shares out, copies timed
+    x_pin = torch.from_numpy(xhat.view(np.int64)).pin_memory()
+    y_pin = {p: torch.empty(n * r, dtype=torch.int64).pin_memory() for p in parties}
+
+    def e2e_step():
+        d = x_pin.to(dev, non_blocking=True)
+        for p in parties:
+            y_pin[p].copy_(coeff_lut_eval(ctx, fx["keys"][p], d, r, fx["degree"], r_out=fx[f"r_out_share{p}"]),
+                           non_blocking=True)
+        torch.cuda.synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    e2e = []
+    for _ in range(max(args.steps, 5)):
+        t0 = time.perf_counter()
+        e2e_step()
+        e2e.append((time.perf_counter() - t0) * 1e3)
+    e2e_ms = _max_over_ranks(ws, dev, sum(e2e) / len(e2e))
+
+    peaks = measured_peaks()
+    engine_peak = ctx.probe_aes_engine()
+    kernel_ms = ms / len(parties)
+    blocks = n * ((fx["out_words"] + 1) // 2)  # one AES block per two coefficient words
+    hbm = n * (8 + 8 * r)
+    out = None
+    if rank == 0:
+        out = {"metric": SILU_METRIC, "value": round(units / (ms / 1e3), 1), "unit": "gate evals/s", "n_gpus": ws,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128",
+               "data": "synthetic x ~ N(0, 16) at f = 12; keys from the reference's own SiLU dealer",
+               "config": {"workload": "configs[2]: SiLU spline gate, 1x128x3072, f = 12, seed 3",
+                          "n_elements_per_party_per_gpu": n, "parties_per_gpu": len(parties),
+                          "intervals": int(fx["keys"][0][4:8].view(np.uint32)[0]), "coeff_words": r,
+                          "l2": "256 MB flush between steps", "parallelism": f"party x element shards on {ws} GPU(s)"},
+               "e2e": {"value": round(units / (e2e_ms / 1e3), 1), "unit": "gate evals/s",
+                       "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": len(parties) * n * r * 8,
+                       "ms_per_step": round(e2e_ms, 4), "path": "sufb200_coeff_lut_eval, pinned x^ in, shares out"},
+               "roofline": {"bound": "launch", "unit": "us per party call", "achieved": round(kernel_ms * 1e3, 2),
+                            "aes_floor_us": round(blocks / engine_peak * 1e6, 2),
+                            "hbm_floor_us": round(hbm / (peaks.get("hbm_gbs", 6650.0) * 1e9) * 1e6, 2),
+                            "frac": round((blocks / engine_peak * 1e6) / (kernel_ms * 1e3), 4),
+                            "peak": round(engine_peak / 1e9, 2), "traffic": hbm,
+                            "kernel": "coeff_lut_kernel",
+                            "note": "393 K elements x 2 AES blocks take about 14 us at the engine ceiling: the call "
+                                    "is bound by launch and key staging, frac = AES floor / measured time"},
+               "cpu_baseline": cpu_silu_baseline(args, fx, xhat) if (ws == 1 and not args.no_cpu) else None,
+               "clocks": clk.summary(), "gpu_launches": args.steps * len(parties), "reconstruction_ok": ok,
+               "ms_per_step_all": [round(v, 4) for v in ms_steps]}
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return out
+
+
+def run_silu_reference(args, ws, rank):
+    if rank != 0:
+        return None
+    from tests.helpers import silu_fixture
+
+    fx = silu_fixture()
+    n = min(args.n_elem or SILU_N, SILU_N)
+    xhat = silu_inputs(n, fx["frac_bits"], 0) + np.uint64(fx["r_in"])
+    a = argparse.Namespace(cpu_sample=n)
+    for _ in range(args.warmup):
+        cpu_silu_baseline(argparse.Namespace(cpu_sample=max(1, n // 8)), fx, xhat)
+    vals = [cpu_silu_baseline(a, fx, xhat)["value"] for _ in range(args.steps)]
+    v = sum(vals) / len(vals)
+    base = cpu_silu_baseline(argparse.Namespace(cpu_sample=min(n, 4096)), fx, xhat)
+    return {"metric": SILU_METRIC, "value": round(v, 1), "unit": "gate evals/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(2 * n / v * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128",
+            "data": "synthetic x ~ N(0, 16) at f = 12", "impl": "reference",
+            "config": {"workload": "configs[2]: SiLU spline gate, 1x128x3072, f = 12, seed 3", "parties": 2},
+            "cpu_baseline": dict(base, value=round(v, 1), sample=f"{n} elements x 2 parties per step"),
+            "e2e": {"value": round(v, 1), "unit": "gate evals/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def cpu_silu_baseline(args, fx, xhat):
+    """The oracle's restatement of the reference interval-LUT evaluation plus
+    the r_out add, both parties, OpenMP over elements (a port: the reference's
+    CPU composite path runs the same LUT through SigmaFastBackend)."""
+    from oracle.oracle import Oracle
+
+    orc = Oracle()
+    n = min(xhat.size, args.cpu_sample)
+    t0 = time.perf_counter()
+    for p in (0, 1):
+        orc.interval_eval(fx["keys"][p], fx["keys"][p].size, True, xhat[:n], fx["out_words"]) + fx[f"r_out_share{p}"]
+    dt = time.perf_counter() - t0
+    return {"value": round(2 * n / dt, 1), "unit": "gate evals/s", "cores": host_threads(), "kind": "port",
+            "sample": f"{n} elements x 2 parties, oracle interval LUT + r_out; {dt:.3f} s"}
+
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -804,7 +950,7 @@ def main():
     ap.add_argument("--n-elem", type=int, default=None,
                     help="elements per party at N=1 (default: the workload's config size; smaller only for "
                          "profiling)")
-    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open"],
+    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open", "silu"],
                     help="trunc: configs[1] (the headline line); compare: configs[0], per-element keys; "
                          "open: the paired-GPU open of a configs[4] layer (N >= 2)")
     ap.add_argument("--ring-bits", type=int, default=37, help="ring of the open workload (37: the reference's "
@@ -816,6 +962,8 @@ def main():
                 "(net::Chan); no stand-alone CPU implementation of the exchange to time"}
                if args.impl == "reference" and rank == 0 else None) if args.impl == "reference" else \
             run_open(args, ws, rank, local)
+    elif args.workload == "silu":
+        out = run_silu_reference(args, ws, rank) if args.impl == "reference" else run_silu(args, ws, rank, local)
     elif args.workload == "compare":
         out = run_compare_reference(args, ws, rank) if args.impl == "reference" else run_compare(args, ws, rank, local)
     elif args.impl == "reference":

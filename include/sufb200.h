@@ -230,6 +230,20 @@ int sufb200_interval_lut_eval(sufb200_ctx ctx, const uint8_t* d_keys, size_t key
                               const uint64_t* d_xs, size_t n, int out_words, uint64_t idx_base, uint64_t* d_out,
                               void* stream);
 
+/* Composite coefficient gate (ell = 0) in one pass: the coefficient words of
+ * the interval containing x^ from a broadcast interval-LUT key (reference
+ * IntervalKeyHeader blob, host memory, out_words = r * (degree + 1)), the
+ * polynomial of each output over the public x^, and this party's output-mask
+ * share: d_out[i*r + j] = sum_k c[j*(degree+1)+k] * x^^k + r_out[j] mod
+ * 2^ring_bits.  degree 0 is the interval-LUT fast path of
+ * composite_eval_batch_backend (include/gates/composite_fss.hpp:1253-1384:
+ * eval_interval_lut_many_device_broadcast, then the r_out loop or
+ * launch_add_rout_aos_kernel); degree > 0 its Horner-only path over x^
+ * (composite_fss.hpp:2066-2130).  r <= 8; r_out may be NULL (zero masks). */
+int sufb200_coeff_lut_eval(sufb200_ctx ctx, const uint8_t* key, size_t key_bytes, const uint64_t* d_xhat, size_t n,
+                           int r, int degree, const uint64_t* r_out, int ring_bits, uint64_t idx_base,
+                           uint64_t* d_out, void* stream);
+
 /* seed_from_id (pfss_backend_gpu.cu:189-194): 16 bytes from
  * mt19937_64(id ^ tweak * 0x9e3779b97f4a7c15). */
 int sufb200_seed_from_id(uint64_t id, uint64_t tweak, uint8_t* seed16);

@@ -12,7 +12,10 @@
 //                                                     with x^ staged on the device
 // with proto::SufB200Backend as the backend, and checks the reconstruction
 // against plaintext truncation and against the reference's ClearBackend run
-// of the same gate.  Prints "OK" on success.
+// of the same gate.  Then the SiLU spline gate: the reference's composite
+// eval of both parties (interval-LUT coefficients) checked against
+// eval_suf_ref, and against the fused sufb200_coeff_lut_eval per party.
+// Prints "OK" on success.
 #include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
@@ -23,6 +26,9 @@
 
 #include "gates/composite_fss.hpp"
 #include "gates/postproc_hooks.hpp"
+#include "gates/silu_spline_gate.hpp"
+#include "suf/ref_eval.hpp"
+#include "suf/suf_silu_builders.hpp"
 #include "proto/backend_clear.hpp"
 #include "proto/channel.hpp"
 #include "sufb200_backend.hpp"
@@ -97,6 +103,84 @@ std::vector<uint64_t> run_pair(proto::PfssBackendBatch& b0, proto::PfssBackendBa
   return rec;
 }
 
+// The SiLU spline gate (configs[2], f = 12): the reference's composite eval of
+// both parties on the adapter (interval-LUT coefficient mode), checked
+// against eval_suf_ref, and each party's output against the fused
+// sufb200_coeff_lut_eval on the same key, r_out share and device x^.
+bool run_silu(uint64_t seed, size_t n) {
+  auto spec = gates::make_silu_spec({12, 16});
+  auto F = suf::build_silu_suf_from_piecewise(spec);
+  proto::SufB200Backend::Options o;
+  o.deterministic = true;
+  o.seed = seed * 131;
+  proto::SufB200Backend gen(o), b0(o), b1(o);
+  std::mt19937_64 rng(seed);
+  const uint64_t r_in = rng();
+  std::vector<uint64_t> r_out(static_cast<size_t>(F.r_out));
+  for (auto& v : r_out) v = rng();
+  auto kp = gates::composite_gen_backend_with_masks(F, gen, rng, r_in, r_out, n, compiler::GateKind::SiLUSpline);
+  std::mt19937_64 xr(seed + 7);
+  std::normal_distribution<double> nd(0.0, 4.0);
+  std::vector<uint64_t> x(n), hatx(n);
+  for (size_t i = 0; i < n; i++) {
+    x[i] = static_cast<uint64_t>(static_cast<int64_t>(std::llround(nd(xr) * 4096.0)));
+    hatx[i] = x[i] + r_in;
+  }
+  uint64_t* d_hatx = nullptr;
+  uint64_t* d_y = nullptr;
+  if (cudaMalloc(&d_hatx, n * 8) != cudaSuccess || cudaMalloc(&d_y, n * 32) != cudaSuccess ||
+      cudaMemcpy(d_hatx, hatx.data(), n * 8, cudaMemcpyHostToDevice) != cudaSuccess) {
+    std::fprintf(stderr, "silu: cuda setup failed\n");
+    return false;
+  }
+  QueueChan::Shared sh;
+  QueueChan c0(&sh, 0), c1(&sh, 1);
+  gates::CompositeBatchInput in{hatx.data(), n, d_hatx};
+  gates::CompositeBatchOutput o0, o1;
+  std::exception_ptr err;
+  std::thread t([&] {
+    try {
+      o1 = gates::composite_eval_batch_backend(1, b1, c1, kp.k1, F, in);
+    } catch (...) {
+      err = std::current_exception();
+    }
+  });
+  o0 = gates::composite_eval_batch_backend(0, b0, c0, kp.k0, F, in);
+  t.join();
+  if (err) std::rethrow_exception(err);
+  bool ok = o0.haty_share.size() == n * 4 && o1.haty_share.size() == n * 4;
+  for (size_t i = 0; ok && i < n; i++) {
+    const auto ref = suf::eval_suf_ref(F, x[i]);
+    for (int j = 0; j < 4; j++) {
+      const uint64_t rec = o0.haty_share[i * 4 + j] + o1.haty_share[i * 4 + j] - r_out[static_cast<size_t>(j)];
+      if (rec != ref.arith[static_cast<size_t>(j)]) {
+        std::fprintf(stderr, "silu: reconstruction differs at %zu/%d\n", i, j);
+        ok = false;
+        break;
+      }
+    }
+  }
+  sufb200_ctx ctx = nullptr;
+  ok = ok && sufb200_ctx_create(0, &ctx) == SUFB200_OK;
+  for (int p = 0; ok && p < 2; p++) {
+    const auto& k = p ? kp.k1 : kp.k0;
+    const auto& out = p ? o1 : o0;
+    std::vector<uint64_t> y(n * 4);
+    ok = sufb200_coeff_lut_eval(ctx, k.coeff_keys[0].bytes.data(), k.coeff_keys[0].bytes.size(), d_hatx, n, 4, 0,
+                                k.r_out_share.data(), 64, 0, d_y, nullptr) == SUFB200_OK &&
+         sufb200_ctx_sync(ctx, nullptr) == SUFB200_OK &&
+         cudaMemcpy(y.data(), d_y, n * 32, cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (ok && y != out.haty_share) {
+      std::fprintf(stderr, "silu: fused kernel differs from the composite output (party %d)\n", p);
+      ok = false;
+    }
+  }
+  if (ctx) sufb200_ctx_destroy(ctx);
+  cudaFree(d_hatx);
+  cudaFree(d_y);
+  return ok;
+}
+
 }  // namespace
 
 int main() {
@@ -150,6 +234,9 @@ int main() {
         }
       }
     }
+  }
+  for (uint64_t seed : {3ull, 4ull}) {
+    if (!run_silu(seed, 5000)) return 1;
   }
   std::printf("OK\n");
   return 0;

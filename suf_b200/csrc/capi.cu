@@ -623,6 +623,47 @@ int sufb200_interval_lut_eval(sufb200_ctx ctx, const uint8_t* d_keys, size_t key
   return SUFB200_OK;
 }
 
+int sufb200_coeff_lut_eval(sufb200_ctx ctx, const uint8_t* key, size_t key_bytes, const uint64_t* d_xhat, size_t n,
+                           int r, int degree, const uint64_t* r_out, int ring_bits, uint64_t idx_base,
+                           uint64_t* d_out, void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  if (r < 1 || r > sufb200::kCoeffMaxOut || degree < 0 || degree > 15 || ring_bits < 1 || ring_bits > 64)
+    return fail(SUFB200_ERR_INVALID, "need 1 <= r <= 8, 0 <= degree <= 15, 1 <= ring_bits <= 64");
+  if (!key || key_bytes < 216 + 24) return fail(SUFB200_ERR_KEY, "interval key missing or too small");
+  uint64_t hdr;
+  std::memcpy(&hdr, key, 8);
+  const uint64_t ow = (hdr >> 16) & 0xFFFF, ivs = hdr >> 32, in_bits = hdr & 0xFFFF;
+  if (in_bits < 1 || in_bits > 64 || ivs < 1 || ow != static_cast<uint64_t>(r) * static_cast<uint64_t>(degree + 1))
+    return fail(SUFB200_ERR_KEY, "interval key header does not match r * (degree + 1) output words");
+  if (key_bytes < 216 + 8 * (ivs + 1 + ivs * ow)) return fail(SUFB200_ERR_KEY, "interval key shorter than its table");
+  if (n == 0) return SUFB200_OK;
+  if (!d_xhat || !d_out || !aligned8(d_xhat) || !aligned8(d_out))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  cudaStream_t st = as_stream(stream);
+  static thread_local sufb200::CoeffLutParams p;  // 4 KB: not on the stack
+  p.r = r;
+  p.degree = degree;
+  p.ring_mask = ring_bits >= 64 ? ~0ull : ((1ull << ring_bits) - 1ull);
+  for (int j = 0; j < sufb200::kCoeffMaxOut; j++) p.r_out[j] = (r_out && j < r) ? r_out[j] : 0ull;
+  p.key_in_params = key_bytes <= sufb200::kCoeffParamKeyBytes ? 1 : 0;
+  uint8_t* scratch = nullptr;
+  cudaError_t e = cudaSuccess;
+  if (p.key_in_params) {
+    std::memcpy(p.key, key, key_bytes);
+  } else {
+    SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), (key_bytes + 255) & ~size_t{255},
+                                               ctx->pool, st),
+                       "coefficient key staging");
+    e = cudaMemcpyAsync(scratch, key, key_bytes, cudaMemcpyHostToDevice, st);
+  }
+  sufb200::RefFmtLaunch a{scratch, key_bytes, 1, d_xhat, n, idx_base, d_out, 0, static_cast<int>(ow), 0, ctx->d_t0,
+                          ctx->d_status};
+  if (e == cudaSuccess) e = sufb200::launch_coeff_lut(ctx, a, p, st);
+  if (scratch) cudaFreeAsync(scratch, st);
+  if (e != cudaSuccess) return cuda_fail(e, "coefficient LUT launch");
+  return SUFB200_OK;
+}
+
 int sufb200_seed_from_id(uint64_t id, uint64_t tweak, uint8_t* seed16) {
   if (!seed16) return fail(SUFB200_ERR_INVALID, "null seed");
   sufb200::host::seed_from_id(id, tweak, seed16);

@@ -60,6 +60,21 @@ cudaError_t launch_thr_dcf(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cuda
 cudaError_t launch_packed_lt(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
 cudaError_t launch_interval_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
 
+// Interval-LUT coefficients, the polynomial over the public x^ and the output
+// masks in one pass (broadcast key, out_words = r * (degree + 1)).
+constexpr int kCoeffMaxOut = 8;
+constexpr size_t kCoeffParamKeyBytes = 4096;  // keys up to this size travel in the kernel parameters
+struct CoeffLutParams {
+  int r;                         // outputs per element
+  int degree;                    // coefficients per output = degree + 1
+  uint64_t ring_mask;            // results reduced mod 2^ring_bits
+  uint64_t r_out[kCoeffMaxOut];  // this party's output-mask shares
+  int key_in_params;             // the key is `key` below, not RefFmtLaunch::keys
+  alignas(16) uint8_t key[kCoeffParamKeyBytes];
+};
+cudaError_t launch_coeff_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, const CoeffLutParams& p,
+                             cudaStream_t st);
+
 // Shared-prefix evaluation of broadcast keys (prefix.cu, prefix.cuh).
 struct RangeAcc;
 struct FrontierEntry;

@@ -209,6 +209,93 @@ __global__ void __launch_bounds__(kAesThreads, 1) interval_lut_kernel(const RefF
   }
 }
 
+// ---- coefficient LUT + polynomial over x^ (composite eval, ell = 0) ------
+// Restates the two beaver-free branches of composite_eval_batch_backend for a
+// gate whose coefficient words come from one broadcast interval LUT:
+//   degree 0 (out_words = r): haty[j] = lut[j] + r_out[j]
+//     (interval-LUT fast path, include/gates/composite_fss.hpp:1253-1384);
+//   degree d > 0: haty[j] = sum_k lut[j*(d+1)+k] * x^^k + r_out[j]
+//     (Horner-only path over the public x^, composite_fss.hpp:2066-2130, with
+//     the coefficients the compiler shifted to the x^ domain).
+// The LUT share words are the reference kernel's (vector_lut_kernel_keyed,
+// cuda/pfss_kernels.cu:545-719: one AES block per two words, counter
+// nonce ^ (idx << 32) ^ (iv * out_words + w)).  Ring arithmetic mod 2^64,
+// reduced to ring_bits at the end (2^ring_bits divides 2^64).
+__global__ void __launch_bounds__(kAesThreads, 1)
+    coeff_lut_kernel(const RefFmtLaunch a0, const __grid_constant__ CoeffLutParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
+    return;
+  }
+  RefFmtLaunch a = a0;
+  if (p.key_in_params) a.keys = p.key;  // small keys ride in the parameter space: no staging copy
+  uint32_t* s_rk = reinterpret_cast<uint32_t*>(smem);
+  uint64_t* s_tab = reinterpret_cast<uint64_t*>(smem + 256);  // cuts then payload
+  const uint64_t h = *reinterpret_cast<const uint64_t*>(a.keys);
+  const int in_bits = static_cast<int>(h & 0xFFFF);
+  const int ow = static_cast<int>((h >> 16) & 0xFFFF);
+  const uint32_t ivs = static_cast<uint32_t>(h >> 32);
+  const size_t words = static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow;
+  const bool tab_in_smem = 8u * words <= kStageBytes;
+  for (int i = threadIdx.x; i < 44; i += blockDim.x) s_rk[i] = reinterpret_cast<const uint32_t*>(a.keys + 40)[i];
+  if (tab_in_smem)
+    for (size_t i = threadIdx.x; i < words; i += blockDim.x) s_tab[i] = reinterpret_cast<const uint64_t*>(a.keys + 216)[i];
+  aes_fill_tables(a.t0);
+  __syncthreads();
+  const int r = p.r, d1 = p.degree + 1;
+  if (ow != r * d1 || ivs == 0 || 216u + 8u * words > a.key_bytes) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.status, kStatusBadKeyHeader);
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+      for (int j = 0; j < r; j++) reinterpret_cast<uint64_t*>(a.out)[i * r + j] = 0;
+    return;
+  }
+  const uint32_t party = a.keys[8];
+  const uint64_t nonce = *reinterpret_cast<const uint64_t*>(a.keys + 16);
+  const uint64_t* cuts = tab_in_smem ? s_tab : reinterpret_cast<const uint64_t*>(a.keys + 216);
+  const uint64_t* pay = cuts + ivs + 1;
+  const uint64_t m = mask_bits(in_bits);
+  const uint32_t lb = lane_base();
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    const uint64_t xh = a.xs[i];
+    const uint64_t x = xh & m;
+    int iv = static_cast<int>(ivs) - 1;
+    if (ivs > 1) {
+      int lo = 0, hi = static_cast<int>(ivs);
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if ((cuts[mid] & m) <= x) lo = mid + 1; else hi = mid;
+      }
+      iv = lo - 1;
+      if (iv < 0) iv = 0;
+      if (iv >= static_cast<int>(ivs)) iv = static_cast<int>(ivs) - 1;
+    }
+    const uint64_t idx = a.idx_base + i;
+    const uint64_t* row = pay + static_cast<size_t>(iv) * ow;
+    uint64_t* out = reinterpret_cast<uint64_t*>(a.out) + i * static_cast<size_t>(r);
+    uint64_t ks0 = 0, ks1 = 0;
+    int w = 0;
+    for (int j = 0; j < r; j++) {
+      uint64_t acc = 0, pw = 1;
+      for (int k = 0; k < d1; k++, w++) {
+        if ((w & 1) == 0) {
+          const uint64_t ctr = nonce ^ (idx << 32) ^ (static_cast<uint64_t>(iv) * static_cast<uint64_t>(ow) + w);
+          const Blk ks = aes_encrypt_smem_rk(ctr_block(ctr), lb, s_rk);
+          ks0 = (static_cast<uint64_t>(ks.w[1]) << 32) | ks.w[0];
+          ks1 = (static_cast<uint64_t>(ks.w[3]) << 32) | ks.w[2];
+        }
+        const uint64_t ksw = (w & 1) ? ks1 : ks0;
+        const uint64_t c = party == 0 ? ksw : (row[w] - ksw);
+        acc += c * pw;
+        pw *= xh;
+      }
+      out[j] = (acc + p.r_out[j]) & p.ring_mask;
+    }
+  }
+}
+
 int grid_for(const sufb200_ctx_s* ctx, size_t n, int threads, int per_sm) {
   const size_t want = (n + threads - 1) / threads;
   const size_t cap = static_cast<size_t>(ctx->sm_count) * per_sm;
@@ -235,6 +322,15 @@ cudaError_t launch_interval_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a,
                                        static_cast<int>(ctx->aes_dyn_bytes));
   if (e != cudaSuccess) return e;
   interval_lut_kernel<<<grid_for(ctx, a.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_coeff_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, const CoeffLutParams& p,
+                             cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(coeff_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  coeff_lut_kernel<<<grid_for(ctx, a.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st>>>(a, p);
   return cudaGetLastError();
 }
 

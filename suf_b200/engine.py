@@ -213,6 +213,23 @@ class Context:
         return d_out
 
 
+def coeff_lut_eval(ctx: "Context", key: np.ndarray, d_xhat, r: int, degree: int, r_out=None, ring_bits: int = 64,
+                   idx_base: int = 0, d_out=None, stream=None):
+    """sufb200_coeff_lut_eval: the composite coefficient gate (interval-LUT
+    coefficients, polynomial over the public x^, output masks) in one pass."""
+    import torch
+
+    key = np.ascontiguousarray(key, dtype=np.uint8)
+    n = d_xhat.numel()
+    if d_out is None:
+        d_out = torch.empty(max(n * r, 1), dtype=torch.int64, device=d_xhat.device)
+    ro = None if r_out is None else np.ascontiguousarray(r_out, dtype=np.uint64)
+    check(ctx._L.sufb200_coeff_lut_eval(ctx.h, _np_ptr(key), key.size, _t_ptr(d_xhat), n, r, degree,
+                                        _np_ptr(ro) if ro is not None else None, ring_bits, C.c_uint64(idx_base),
+                                        _t_ptr(d_out), _stream_ptr(stream)))
+    return d_out
+
+
 # -- paired-GPU open ---------------------------------------------------------------
 
 OPEN_ID_BYTES = 128

@@ -44,16 +44,20 @@ class SufB200Backend final : public PfssIntervalLutExt, public PackedLtBackend, 
     std::vector<uint8_t> prg_state;  // >= 64 bytes; empty: the process-wide state
     bool deterministic = false;      // party seeds from mt19937_64(seed) instead of std::random_device
     uint64_t seed = 0;
+    bool dealer_only = false;        // keygen only, no GPU needed (evaluation calls throw)
   };
 
   SufB200Backend() : SufB200Backend(Options{}) {}
   explicit SufB200Backend(Options o) : opt_(std::move(o)), rng_(opt_.seed) {
-    int dev = opt_.device;
-    if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) throw std::runtime_error("SufB200Backend: no CUDA device");
+    int dev = SUFB200_HOST_ONLY;
+    if (!opt_.dealer_only) {
+      dev = opt_.device;
+      if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) throw std::runtime_error("SufB200Backend: no CUDA device");
+    }
     check(sufb200_ctx_create(dev, &ctx_), "sufb200_ctx_create");
     const std::vector<uint8_t>& st = opt_.prg_state.empty() ? process_prg_state() : opt_.prg_state;
     check(sufb200_prg_init(ctx_, st.data(), st.size()), "sufb200_prg_init");
-    if (cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess)
+    if (!opt_.dealer_only && cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess)
       throw std::runtime_error("SufB200Backend: cudaStreamCreate failed");
   }
 

@@ -59,3 +59,30 @@ def to_product_desc(d: OrcDesc):
     for i in range(4):
         p.q_bits[i] = d.q_bits[i]
     return p
+
+
+# ---- the SiLU gate fixture (tests/golden/make_silu_fixture.py) ----
+
+def silu_fixture() -> dict:
+    import json
+    from pathlib import Path
+
+    d = json.loads((Path(__file__).parent / "golden" / "silu_gate_f12_seed3.json").read_text())
+    u = lambda v: np.array([int(t) for t in v], dtype=np.uint64)  # noqa: E731
+    d["r_in"] = int(d["r_in"])
+    for k in ("r_out", "r_out_share0", "r_out_share1", "alpha"):
+        d[k] = u(d[k])
+    d["pieces"] = np.array([[int(t) for t in p] for p in d["pieces"]], dtype=np.uint64)
+    d["keys"] = [np.frombuffer(bytes.fromhex(d["key0"]), dtype=np.uint8).copy(),
+                 np.frombuffer(bytes.fromhex(d["key1"]), dtype=np.uint8).copy()]
+    d["x"] = u([s["x"] for s in d["samples"]])
+    d["expect"] = np.array([[int(t) for t in s["expect"]] for s in d["samples"]], dtype=np.uint64)
+    return d
+
+
+def suf_table_eval(alpha: np.ndarray, pieces: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """suf::eval_suf_ref (include/suf/ref_eval.hpp:47-77) for degree-0 pieces:
+    the piece whose [alpha_i, alpha_i+1) holds x, else the last piece."""
+    idx = np.searchsorted(alpha, x, side="right").astype(np.int64) - 1
+    idx[(idx < 0) | (idx > alpha.size - 2)] = alpha.size - 2
+    return pieces[idx]

@@ -155,3 +155,21 @@ def test_trunc_oracle_random_and_edges(oracle, prg_state, kind):
         y = oracle_trunc_eval(oracle, d0, k0, xhat) + oracle_trunc_eval(oracle, d1, k1, xhat)
         exp = (x.view(np.uint64) >> np.uint64(f)) if kind == KIND_TR else (x >> f).view(np.uint64)
         assert (y == exp).all()
+
+
+# ---- configs[2] SiLU gate fixture (the reference's own dealer) ----
+
+def test_silu_fixture_table_and_lut_semantics(oracle):
+    """The fixture's SUF table restated (select_interval + degree-0 piece)
+    reproduces the reference's eval_suf_ref on every sample; the compiled
+    interval LUT, evaluated by the oracle at x^ = x + r_in, reconstructs the
+    same coefficient words; the r_out shares add up to r_out."""
+    from tests.helpers import silu_fixture, suf_table_eval
+
+    d = silu_fixture()
+    assert (d["degree"], d["r"], d["out_words"]) == (0, 4, 4)
+    assert (suf_table_eval(d["alpha"], d["pieces"], d["x"]) == d["expect"]).all()
+    assert ((d["r_out_share0"] + d["r_out_share1"]) == d["r_out"]).all()
+    xhat = d["x"] + np.uint64(d["r_in"])
+    s = [oracle.interval_eval(k, k.size, True, xhat, 4) for k in d["keys"]]
+    assert ((s[0] + s[1]) == d["expect"]).all()
