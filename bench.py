@@ -515,6 +515,13 @@ CMP_TRAFFIC_BYTES_PER_ELEMENT = 2299.8
 CMP_METRIC = "DCF pred-evals/sec (single-predicate compare 1[x^ < r_in], per-element myl7 keys)"
 
 
+def compare_seeds(n: int, shard: int) -> np.ndarray:
+    from suf_b200.engine import host_mt19937_64
+
+    total = n * (shard + 1)
+    return host_mt19937_64(1 ^ 0x5EED, 4 * total).view(np.uint8).reshape(total, 2, 16)[shard * n:(shard + 1) * n]
+
+
 def compare_material(ctx, n: int, shard: int):
     """r_in[i] = successive mt19937_64(1) draws, x uniform with
     |x| < 2^36 (|v| < 2^20 with 16 fractional bits) from the draws after the
@@ -528,7 +535,7 @@ def compare_material(ctx, n: int, shard: int):
     r_in = draws[shard * n:(shard + 1) * n].copy()
     x = ((draws[total + shard * n: total + (shard + 1) * n] >> np.uint64(27)).view(np.int64) - (1 << 36))
     xhat = x.view(np.uint64) + r_in
-    seeds = host_mt19937_64(1 ^ 0x5EED, 4 * total).view(np.uint8).reshape(total, 2, 16)[shard * n:(shard + 1) * n]
+    seeds = compare_seeds(n, shard)
     k0, k1 = ctx.myl7_gen_batch(GROUP_ADD, 64, r_in, (1).to_bytes(8, "little"), seeds[:, 0].copy(),
                                 seeds[:, 1].copy())
     return r_in, xhat, (k0, k1)
@@ -560,8 +567,28 @@ def run_compare(args, ws, rank, local):
     ctx = Context(local)
     ctx.prg_init(prg_state())
     parties, n, shard = assignment(ws, rank, args.n_elem or CMP_N)
+    t0 = time.perf_counter()
     r_in, xhat, keys = compare_material(ctx, n, shard)
+    host_dealer_s = time.perf_counter() - t0
     kb = keys[0].shape[1]
+    # the same key pairs from the GPU dealer (sufb200_myl7_gen_batch_device)
+    from suf_b200 import GROUP_ADD as _GA
+
+    sd = torch.from_numpy(np.ascontiguousarray(compare_seeds(n, shard).transpose(1, 0, 2)).reshape(2, -1)).to(dev)
+    d_alpha = torch.from_numpy(r_in.view(np.int64)).to(dev)
+    s0d, s1d = sd[0].contiguous(), sd[1].contiguous()
+    g0 = torch.empty(n * kb, dtype=torch.uint8, device=dev)
+    g1 = torch.empty(n * kb, dtype=torch.uint8, device=dev)
+    ctx.myl7_gen_batch_device(_GA, 64, d_alpha, (1).to_bytes(8, "little"), s0d, s1d, g0, g1)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    ctx.myl7_gen_batch_device(_GA, 64, d_alpha, (1).to_bytes(8, "little"), s0d, s1d, g0, g1)
+    e1.record()
+    torch.cuda.synchronize()
+    dev_dealer_ms = e0.elapsed_time(e1)
+    dealer_same = bool((g0.cpu().numpy() == keys[0].reshape(-1)).all() and (g1.cpu().numpy() == keys[1].reshape(-1)).all())
+    del g0, g1, sd, s0d, s1d
     stream = torch.cuda.Stream(device=dev)
     d_x = torch.from_numpy(xhat.view(np.int64)).to(dev)
     d_k = {p: torch.from_numpy(keys[p].reshape(-1)).to(dev) for p in parties}
@@ -645,6 +672,11 @@ def run_compare(args, ws, rank, local):
                        "ms_per_step": round(e2e_ms, 3), "path": "sufb200_myl7_dcf_eval_host (pinned keys and x^)"},
                "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
                "gpu_launches": args.steps * len(parties), "reconstruction_ok": ok,
+               "dealer": {"device_ms": round(dev_dealer_ms, 3), "host_s": round(host_dealer_s, 3),
+                          "host_threads": host_threads(), "identical_keys": dealer_same,
+                          "device_key_pairs_per_s": round(n / (dev_dealer_ms / 1e3), 1),
+                          "device_aes_blocks_per_s": round(n * 8 * 64 / (dev_dealer_ms / 1e3), 1),
+                          "note": "sufb200_myl7_gen_batch_device vs the host dealer (OpenMP, AES-NI), same seeds"},
                "reference_threshold_format": {
                    "value": round(units / (thr_ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(thr_ms, 4),
                    "hbm_gbs": round(thr_gbs, 1), "hbm_frac": round(thr_gbs / peaks.get("hbm_gbs", 6650.0), 3),

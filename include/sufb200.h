@@ -230,6 +230,19 @@ int sufb200_interval_lut_eval(sufb200_ctx ctx, const uint8_t* d_keys, size_t key
                               const uint64_t* d_xs, size_t n, int out_words, uint64_t idx_base, uint64_t* d_out,
                               void* stream);
 
+/* myl7 DCF key pairs generated on the GPU, one per alpha: the same bytes as
+ * sufb200_myl7_gen_batch (the reference's dcf_gen,
+ * third_party/myl7_fss/src/dcf.c:42-142, in the adapter layout of
+ * Myl7FssBackend::gen_dcf, include/proto/myl7_fss_backend.hpp:131-213) for
+ * the same party seeds.  All arrays on the device: d_alphas [n],
+ * d_seeds0/1 [n][16] (16-byte aligned), d_keys0/1 [n][key_bytes] (8-byte
+ * aligned).  in_bits a multiple of 8 (8..64); payload 1..16 bytes, the same
+ * for every key.  No counterpart in the reference, whose keygen runs on the
+ * host. */
+int sufb200_myl7_gen_batch_device(sufb200_ctx ctx, int group, int in_bits, const uint64_t* d_alphas, size_t n,
+                                  const uint8_t* payload, int payload_len, const uint8_t* d_seeds0,
+                                  const uint8_t* d_seeds1, uint8_t* d_keys0, uint8_t* d_keys1, void* stream);
+
 /* Composite coefficient gate (ell = 0) in one pass: the coefficient words of
  * the interval containing x^ from a broadcast interval-LUT key (reference
  * IntervalKeyHeader blob, host memory, out_words = r * (degree + 1)), the

@@ -623,6 +623,40 @@ int sufb200_interval_lut_eval(sufb200_ctx ctx, const uint8_t* d_keys, size_t key
   return SUFB200_OK;
 }
 
+int sufb200_myl7_gen_batch_device(sufb200_ctx ctx, int group, int in_bits, const uint64_t* d_alphas, size_t n,
+                                  const uint8_t* payload, int payload_len, const uint8_t* d_seeds0,
+                                  const uint8_t* d_seeds1, uint8_t* d_keys0, uint8_t* d_keys1, void* stream) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (group != SUFB200_GROUP_ADD && group != SUFB200_GROUP_XOR) return fail(SUFB200_ERR_INVALID, "bad group");
+  if (in_bits < 8 || in_bits > 64 || in_bits % 8)
+    return fail(SUFB200_ERR_UNSUPPORTED, "device keygen needs in_bits in 8..64, a multiple of 8");
+  if (payload_len < 1 || payload_len > 16 || !payload)
+    return fail(SUFB200_ERR_UNSUPPORTED, "device keygen takes a payload of 1..16 bytes (one chunk)");
+  if (n == 0) return SUFB200_OK;
+  auto al = [](const void* p, uintptr_t a) { return p && (reinterpret_cast<uintptr_t>(p) % a) == 0; };
+  if (!al(d_alphas, 8) || !al(d_seeds0, 16) || !al(d_seeds1, 16) || !al(d_keys0, 8) || !al(d_keys1, 8))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer (seeds 16-byte, keys 8-byte aligned)");
+  uint8_t beta[16] = {0};
+  std::memcpy(beta, payload, static_cast<size_t>(payload_len));
+  beta[15] &= 0x7F;
+  sufb200::GenLaunch g{};
+  g.alphas = d_alphas;
+  g.seeds0 = d_seeds0;
+  g.seeds1 = d_seeds1;
+  g.keys0 = d_keys0;
+  g.keys1 = d_keys1;
+  g.n = n;
+  g.key_bytes = sufb200::host::myl7_key_bytes(in_bits, payload_len);
+  g.in_bits = in_bits;
+  g.payload_len = payload_len;
+  std::memcpy(&g.beta_lo, beta, 8);
+  std::memcpy(&g.beta_hi, beta + 8, 8);
+  g.t0 = ctx->d_t0;
+  g.status = ctx->d_status;
+  SUFB200_CHECK_CUDA(sufb200::launch_myl7_gen(ctx, group, g, as_stream(stream)), "myl7 keygen launch");
+  return SUFB200_OK;
+}
+
 int sufb200_coeff_lut_eval(sufb200_ctx ctx, const uint8_t* key, size_t key_bytes, const uint64_t* d_xhat, size_t n,
                            int r, int degree, const uint64_t* r_out, int ring_bits, uint64_t idx_base,
                            uint64_t* d_out, void* stream) {

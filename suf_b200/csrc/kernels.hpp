@@ -102,6 +102,23 @@ cudaError_t launch_myl7_bcast_prefix(const sufb200_ctx_s* ctx, int group, const 
 cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaunch& a, const RangeAcc* acc,
                                        uint32_t kmax, FrontierEntry* const F[4], cudaStream_t st);
 
+// myl7 DCF keygen on the GPU (keygen_dev.cu): one key pair per thread.
+struct GenLaunch {
+  const uint64_t* alphas;  // device [n]
+  const uint8_t* seeds0;   // device [n][16], 16-byte aligned
+  const uint8_t* seeds1;
+  uint8_t* keys0;          // device [n][key_bytes], 8-byte aligned
+  uint8_t* keys1;
+  size_t n;
+  size_t key_bytes;
+  int in_bits;             // multiple of 8
+  int payload_len;         // 1..16
+  uint64_t beta_lo, beta_hi;
+  const uint32_t* t0;
+  uint32_t* status;
+};
+cudaError_t launch_myl7_gen(const sufb200_ctx_s* ctx, int group, const GenLaunch& g, cudaStream_t st);
+
 // Measured AES-128 block rate of the shared-memory engine (probe.cu).
 cudaError_t probe_aes_engine(const sufb200_ctx_s* ctx, double* blocks_per_s);
 

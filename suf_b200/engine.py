@@ -115,6 +115,23 @@ class Context:
                                              _np_ptr(s0), _np_ptr(s1), _np_ptr(keys0), _np_ptr(keys1)))
         return keys0, keys1
 
+    def myl7_gen_batch_device(self, group: int, in_bits: int, d_alphas, payload: bytes, d_seeds0, d_seeds1,
+                              d_keys0=None, d_keys1=None, stream=None):
+        """Key pairs generated on the GPU (device tensors in and out)."""
+        import torch
+
+        n = d_alphas.numel()
+        kb = myl7_key_bytes(in_bits, len(payload))
+        if d_keys0 is None:
+            d_keys0 = torch.empty(n * kb, dtype=torch.uint8, device=d_alphas.device)
+        if d_keys1 is None:
+            d_keys1 = torch.empty(n * kb, dtype=torch.uint8, device=d_alphas.device)
+        pl = np.frombuffer(bytes(payload), dtype=np.uint8).copy()
+        check(self._L.sufb200_myl7_gen_batch_device(self.h, group, in_bits, _t_ptr(d_alphas), n, _np_ptr(pl),
+                                                    len(payload), _t_ptr(d_seeds0), _t_ptr(d_seeds1),
+                                                    _t_ptr(d_keys0), _t_ptr(d_keys1), _stream_ptr(stream)))
+        return d_keys0, d_keys1
+
     def myl7_eval(self, group: int, in_bits: int, d_keys, key_bytes: int, broadcast: bool, d_xs, out_bytes: int,
                   d_out=None, stream=None):
         import torch
