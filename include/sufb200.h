@@ -350,6 +350,26 @@ int sufb200_open_exchange(sufb200_open_comm comm, int peer, const uint64_t* d_lo
 int sufb200_open_add_to_signed(const uint64_t* d_local, const uint64_t* d_remote, uint64_t* d_out, size_t n,
                                int ring_bits, void* stream);
 
+/* ---- ring matmuls on the tensor cores -------------------------------------
+ * Exact Z_2^64 products by 8-bit limbs on tcgen05 (36 limb products per
+ * 32-deep step, int32 accumulators per limb diagonal in tensor memory);
+ * the contraction depth (2K for the Beaver form) must not exceed 8192.
+ * Both report a kernel-side timeout through sufb200_ctx_sync.
+ *
+ * sufb200_ring_matmul: matmul_publicW_gpu / matmul_publicW_tiled
+ * (src/nn/matmul_gpu.cu:21-117, 388-420): Y[b] = X[b] W (+ bias per column)
+ * mod 2^64, X [batch][M][K] shares, W [K][N] (or [N][K] when w_transposed)
+ * public int64, bias [N] or NULL.
+ * sufb200_beaver_matmul2d_tc: the same results as sufb200_beaver_matmul2d
+ * (launch_beaver_matmul2d[_batched]_kernel, cuda/cuda_primitives.cu:391-628),
+ * computed as one product [D | A] x [B (+ E for party 0) ; E] plus C. */
+int sufb200_ring_matmul(sufb200_ctx ctx, const uint64_t* d_x, const int64_t* d_w, const int64_t* d_bias,
+                        uint64_t* d_y, size_t batch, int M, int K, int N, int w_transposed, void* stream);
+int sufb200_beaver_matmul2d_tc(sufb200_ctx ctx, int party, const uint64_t* d_D_open, const uint64_t* d_E_open,
+                               const uint64_t* d_A, const uint64_t* d_B, const uint64_t* d_C, int batches, int M,
+                               int K, int N, int w_transposed, int has_scale, int64_t mul_const, int mul_shift,
+                               uint64_t* d_out, void* stream);
+
 /* Row mean = row sum / len, unsigned (launch_row_mean_kernel). */
 int sufb200_row_mean(const uint64_t* d_mat, int rows, int cols, const int* d_valid_lens, uint64_t* d_out_rows,
                      void* stream);

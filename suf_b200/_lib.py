@@ -96,6 +96,9 @@ _SIGS = {
     "sufb200_unpack_add_to_signed": (_i, [_vp, _vp, _i, _vp, _sz, _i, _vp]),
     "sufb200_open_add_to_signed": (_i, [_vp, _vp, _vp, _sz, _i, _vp]),
     "sufb200_myl7_gen_batch_device": (_i, [_vp, _i, _i, _vp, _sz, _vp, _i, _vp, _vp, _vp, _vp, _vp]),
+    "sufb200_ring_matmul": (_i, [_vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _i, _vp]),
+    "sufb200_beaver_matmul2d_tc": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, C.c_int64, _i, _vp,
+                                        _vp]),
     "sufb200_coeff_lut_eval": (_i, [_vp, _vp, _sz, _vp, _sz, _i, _i, _vp, _i, _u64, _vp, _vp]),
     "sufb200_open_unique_id": (_i, [_vp]),
     "sufb200_open_comm_create": (_i, [_vp, _vp, _i, _i, C.c_double, C.POINTER(_vp)]),

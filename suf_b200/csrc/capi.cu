@@ -256,6 +256,7 @@ int sufb200_ctx_sync(sufb200_ctx ctx, void* stream) {
     if (st & sufb200::kStatusSmemLayout) return fail(SUFB200_ERR_CUDA, "kernel found an unexpected shared-memory layout");
     if (st & sufb200::kStatusBadKeyHeader)
       return fail(SUFB200_ERR_KEY, "a key header did not match the call (in_bits / chunks / party / payload_len)");
+    if (st & sufb200::kStatusTimeout) return fail(SUFB200_ERR_CUDA, "a kernel's bounded wait gave up (results invalid)");
     return fail(SUFB200_ERR_INVALID, "device reported a bad argument");
   }
   return SUFB200_OK;
@@ -695,6 +696,68 @@ int sufb200_coeff_lut_eval(sufb200_ctx ctx, const uint8_t* key, size_t key_bytes
   if (e == cudaSuccess) e = sufb200::launch_coeff_lut(ctx, a, p, st);
   if (scratch) cudaFreeAsync(scratch, st);
   if (e != cudaSuccess) return cuda_fail(e, "coefficient LUT launch");
+  return SUFB200_OK;
+}
+
+// ---- ring matmuls on the tensor cores (ring_gemm_tc.cu) ---------------------
+// K' (summed over the product's pieces) up to 8192 keeps every limb diagonal
+// exact in its 32-bit accumulator.
+constexpr int kRingMaxK = 8192;
+
+int sufb200_ring_matmul(sufb200_ctx ctx, const uint64_t* d_x, const int64_t* d_w, const int64_t* d_bias,
+                        uint64_t* d_y, size_t batch, int M, int K, int N, int w_transposed, void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  if (batch == 0 || M == 0 || N == 0) return SUFB200_OK;
+  if (M < 0 || N < 0 || K < 1 || batch > 65535) return fail(SUFB200_ERR_INVALID, "bad shape");
+  if (K > kRingMaxK) return fail(SUFB200_ERR_UNSUPPORTED, "K above 8192 (split the contraction)");
+  if (!d_x || !d_w || !d_y || !aligned8(d_x) || !aligned8(d_w) || !aligned8(d_y) || (d_bias && !aligned8(d_bias)))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  sufb200::RingGemmLaunch g{};
+  g.piece[0] = sufb200::RingGemmPiece{d_x, reinterpret_cast<const uint64_t*>(d_w), nullptr,
+                                      static_cast<size_t>(M) * K, 0, 0};
+  g.npieces = 1;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.trans = w_transposed ? 1 : 0;
+  g.bias = d_bias;
+  g.out = d_y;
+  g.os = static_cast<size_t>(M) * N;
+  g.status = ctx->d_status;
+  SUFB200_CHECK_CUDA(sufb200::launch_ring_gemm_tc(g, static_cast<int>(batch), as_stream(stream)), "ring matmul launch");
+  return SUFB200_OK;
+}
+
+int sufb200_beaver_matmul2d_tc(sufb200_ctx ctx, int party, const uint64_t* d_D_open, const uint64_t* d_E_open,
+                               const uint64_t* d_A, const uint64_t* d_B, const uint64_t* d_C, int batches, int M,
+                               int K, int N, int w_transposed, int has_scale, int64_t mul_const, int mul_shift,
+                               uint64_t* d_out, void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  if (batches <= 0 || M <= 0 || N <= 0) return SUFB200_OK;
+  if (K < 1 || batches > 65535 || (party != 0 && party != 1)) return fail(SUFB200_ERR_INVALID, "bad shape or party");
+  if (2 * K > kRingMaxK) return fail(SUFB200_ERR_UNSUPPORTED, "K above 4096 (split the contraction)");
+  const void* ptrs[6] = {d_D_open, d_E_open, d_A, d_B, d_C, d_out};
+  for (const void* p : ptrs)
+    if (!p || !aligned8(p)) return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  const size_t mk = static_cast<size_t>(M) * K, kn = static_cast<size_t>(K) * N;
+  sufb200::RingGemmLaunch g{};
+  // [D | A] x [B (+ E for party 0) ; E]: one product of depth 2K
+  g.piece[0] = sufb200::RingGemmPiece{d_D_open, d_B, party == 0 ? d_E_open : nullptr, mk, 0, kn};
+  g.piece[1] = sufb200::RingGemmPiece{d_A, d_E_open, nullptr, 0, kn, 0};
+  g.npieces = 2;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.trans = w_transposed ? 1 : 0;
+  g.c = d_C;
+  g.cs = 0;
+  g.has_scale = has_scale;
+  g.mul_const = mul_const;
+  g.mul_shift = mul_shift;
+  g.out = d_out;
+  g.os = static_cast<size_t>(M) * N;
+  g.status = ctx->d_status;
+  SUFB200_CHECK_CUDA(sufb200::launch_ring_gemm_tc(g, batches, as_stream(stream)), "Beaver matmul launch");
   return SUFB200_OK;
 }
 

@@ -119,6 +119,33 @@ struct GenLaunch {
 };
 cudaError_t launch_myl7_gen(const sufb200_ctx_s* ctx, int group, const GenLaunch& g, cudaStream_t st);
 
+// Exact Z_2^64 matrix product on the tensor cores (ring_gemm_tc.cu):
+// out[b] = scale(C[b] + bias + sum_p X_p[b] (Y_p[b] + Y2_p[b])), X_p [M][K]
+// row-major, Y_p [K][N] (or [N][K] when trans), per-batch strides in elements
+// (0: shared across batches).
+struct RingGemmPiece {
+  const uint64_t* x;
+  const uint64_t* y;
+  const uint64_t* y2;  // optional, added to y element-wise
+  size_t xs, ys, y2s;
+};
+struct RingGemmLaunch {
+  RingGemmPiece piece[2];
+  int npieces;
+  int M, N, K;
+  int trans;
+  const uint64_t* c;  // optional [M][N]
+  size_t cs;
+  const int64_t* bias;  // optional [N]
+  int has_scale;
+  int64_t mul_const;
+  int mul_shift;
+  uint64_t* out;
+  size_t os;
+  uint32_t* status;
+};
+cudaError_t launch_ring_gemm_tc(const RingGemmLaunch& g, int batches, cudaStream_t st);
+
 // Measured AES-128 block rate of the shared-memory engine (probe.cu).
 cudaError_t probe_aes_engine(const sufb200_ctx_s* ctx, double* blocks_per_s);
 

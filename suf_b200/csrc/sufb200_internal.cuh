@@ -60,6 +60,7 @@ enum : uint32_t {
   kStatusBadKeyHeader = 1u << 0,
   kStatusSmemLayout = 1u << 1,
   kStatusBadArgument = 1u << 2,
+  kStatusTimeout = 1u << 3,  // a bounded wait inside a kernel gave up
 };
 
 SUFB200_HD uint32_t rotl32(uint32_t v, int r) { return (v << r) | (v >> ((32 - r) & 31)); }

@@ -311,3 +311,36 @@ def test_open_unique_id_after_torch():
             % str(ROOT))
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
+
+
+# ---- the limb identity behind the tensor-core ring matmul (ring_gemm_tc.cu) ----
+
+def _limb_product(x: np.ndarray, y: np.ndarray) -> np.ndarray:
+    """x @ y mod 2^64 the way the kernel forms it: byte planes, the 36 limb
+    products with i + j <= 7 summed per diagonal in a wrapping 32-bit
+    accumulator, then sum_s (P_s mod 2^32) << 8s mod 2^64."""
+    xb = [((x >> np.uint64(8 * i)) & np.uint64(0xFF)).astype(np.int64) for i in range(8)]
+    yb = [((y >> np.uint64(8 * j)) & np.uint64(0xFF)).astype(np.int64) for j in range(8)]
+    out = np.zeros((x.shape[0], y.shape[1]), dtype=np.uint64)
+    for s in range(8):
+        p = sum(xb[i] @ yb[s - i] for i in range(s + 1))  # exact in int64 here
+        out += (p.astype(np.uint64) & np.uint64(0xFFFFFFFF)) << np.uint64(8 * s)
+    return out
+
+
+def _exact_product(x: np.ndarray, y: np.ndarray) -> np.ndarray:
+    xo, yo = x.astype(object), y.astype(object)
+    return np.array((xo @ yo) % (1 << 64), dtype=np.uint64)
+
+
+@pytest.mark.parametrize("k", [1, 31, 32, 300, 8192])
+def test_limb_identity_is_exact(k):
+    """Worst case (all bytes 0xFF) and random words: the diagonal sums that
+    survive the shift fit the 32-bit accumulator up to depth 8192."""
+    rng = np.random.default_rng(k)
+    for x, y in ((np.full((3, k), 2**64 - 1, dtype=np.uint64), np.full((k, 4), 2**64 - 1, dtype=np.uint64)),
+                 (rng.integers(0, 2**63, (3, k), dtype=np.uint64) * np.uint64(2) + np.uint64(1),
+                  rng.integers(0, 2**63, (k, 4), dtype=np.uint64) * np.uint64(3))):
+        assert (_limb_product(x, y) == _exact_product(x, y)).all()
+    worst = 4 * 8192 * 255 * 255  # diagonal s = 3 at the maximum depth
+    assert worst < 2**31
