@@ -967,6 +967,97 @@ def cpu_silu_baseline(args, fx, xhat):
             "sample": f"{n} elements x 2 parties, oracle interval LUT + r_out; {dt:.3f} s"}
 
 
+# ---------------------------------------------------------------------------
+# one layer's Beaver matmuls on the tensor cores
+# ---------------------------------------------------------------------------
+
+LAYER_MATMULS = [("qkv", 128, 768, 2304), ("out", 128, 768, 768), ("ffn1", 128, 768, 3072), ("ffn2", 128, 3072, 768)]
+MATMUL_METRIC = "ring MACs/sec (configs[4] layer Beaver matmuls, Z_2^64, both parties)"
+
+
+def run_matmul(args, ws, rank, local):
+    import ctypes as C
+
+    import torch
+
+    from suf_b200 import _lib
+    from suf_b200.engine import Context
+
+    if ws > 1:
+        return {"metric": MATMUL_METRIC, "unavailable": "single-GPU microbenchmark"} if rank == 0 else None
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = Context(local)
+    L = _lib.lib()
+    rng = np.random.default_rng(5)
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+    mats = []
+    for name, M, K, N in LAYER_MATMULS:
+        t = {k: torch.from_numpy(rng.integers(-(2**62), 2**62, sz, dtype=np.int64)).to(dev)
+             for k, sz in (("D", M * K), ("E", K * N), ("A", M * K), ("B", K * N), ("C", M * N))}
+        t["out"] = {p: torch.empty(M * N, dtype=torch.int64, device=dev) for p in (0, 1)}
+        t["ref"] = torch.empty(M * N, dtype=torch.int64, device=dev)
+        mats.append((name, M, K, N, t))
+    sp = int(stream.cuda_stream)
+
+    def tc_step():
+        for name, M, K, N, t in mats:
+            for p in (0, 1):
+                _lib.check(L.sufb200_beaver_matmul2d_tc(ctx.h, p, t["D"].data_ptr(), t["E"].data_ptr(),
+                                                        t["A"].data_ptr(), t["B"].data_ptr(), t["C"].data_ptr(), 1, M,
+                                                        K, N, 0, 1, C.c_int64(4096), 12, t["out"][p].data_ptr(), sp))
+
+    def core_step():
+        for name, M, K, N, t in mats:
+            for p in (0, 1):
+                _lib.check(L.sufb200_beaver_matmul2d(p, t["D"].data_ptr(), t["E"].data_ptr(), t["A"].data_ptr(),
+                                                     t["B"].data_ptr(), t["C"].data_ptr(), 1, M, K, N, 0, 1, 4096, 12,
+                                                     t["ref"].data_ptr(), sp))
+
+    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, tc_step, ctx, local)
+    core_ms, _, _ = _timed(args, ws, dev, stream, flush, core_step, ctx, local, sample_clocks=False)
+    # bit-exact against the CUDA-core kernel (party 1 was the last written by both)
+    same = all(bool(torch.equal(t["out"][1], t["ref"])) for *_, t in mats)
+    macs = sum(2 * M * N * (2 * K) for _, M, K, N in LAYER_MATMULS)  # [D|A][B(+E);E], both parties
+    int8_macs = 36 * macs
+    peaks = measured_peaks()
+    int8_peak = 2 * peaks.get("bf16_tflops", 1590.0) * 1e12 / 2  # MAC/s: dense int8 = 2x bf16 rate
+    # per-matmul times
+    per = {}
+    for name, M, K, N, t in mats:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            flush.fill_(1)
+            e0.record(stream)
+            for _ in range(10):
+                _lib.check(L.sufb200_beaver_matmul2d_tc(ctx.h, 0, t["D"].data_ptr(), t["E"].data_ptr(),
+                                                        t["A"].data_ptr(), t["B"].data_ptr(), t["C"].data_ptr(), 1, M,
+                                                        K, N, 0, 1, C.c_int64(4096), 12, t["out"][0].data_ptr(), sp))
+            e1.record(stream)
+        torch.cuda.synchronize()
+        per[f"{name}_{M}x{K}x{N}_us"] = round(e0.elapsed_time(e1) / 10 * 1e3, 2)
+    ctx.sync(stream)
+    ctx.close()
+    return {"metric": MATMUL_METRIC, "value": round(macs / (ms / 1e3), 1), "unit": "ring MACs/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Z_2^64) via int8 limbs",
+            "data": "synthetic shares (seeded)",
+            "config": {"workload": "configs[4]: QKV, O, FFN1, FFN2 Beaver matmuls of one d=768 layer, L=128, "
+                                   "rescale by 4096 >> 12", "matmuls": [list(m[:4]) for m in mats],
+                       "l2": "256 MB flush between steps"},
+            "e2e": {"value": round(macs / (ms / 1e3), 1), "unit": "ring MACs/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0, "note": "device-resident operands by design (shares stay in HBM)"},
+            "roofline": {"bound": "tensor", "unit": "T int8 MAC/s", "achieved": round(int8_macs / (ms / 1e3) / 1e12, 1),
+                         "peak": round(int8_peak / 1e12, 1), "frac": round(int8_macs / (ms / 1e3) / int8_peak, 4),
+                         "traffic": None, "kernel": "ring_gemm_tc_kernel",
+                         "peak_source": "2x the measured dense bf16 rate (MEASURED_PEAKS.json) as the int8 rate"},
+            "cuda_core": {"ms_per_step": round(core_ms, 4), "speedup": round(core_ms / ms, 2),
+                          "kernel": "beaver_matmul_kernel (u64 MACs on the integer pipes)", "identical": same},
+            "per_matmul_us": per, "clocks": clk.summary(), "gpu_launches": args.steps * 8,
+            "ms_per_step_all": [round(v, 4) for v in ms_steps]}
+
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -982,7 +1073,7 @@ def main():
     ap.add_argument("--n-elem", type=int, default=None,
                     help="elements per party at N=1 (default: the workload's config size; smaller only for "
                          "profiling)")
-    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open", "silu"],
+    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open", "silu", "matmul"],
                     help="trunc: configs[1] (the headline line); compare: configs[0], per-element keys; "
                          "open: the paired-GPU open of a configs[4] layer (N >= 2)")
     ap.add_argument("--ring-bits", type=int, default=37, help="ring of the open workload (37: the reference's "
@@ -994,6 +1085,11 @@ def main():
                 "(net::Chan); no stand-alone CPU implementation of the exchange to time"}
                if args.impl == "reference" and rank == 0 else None) if args.impl == "reference" else \
             run_open(args, ws, rank, local)
+    elif args.workload == "matmul":
+        out = ({"impl": "reference", "metric": MATMUL_METRIC,
+                "unavailable": "the reference's Beaver matmul is a CUDA kernel; its CUDA-core equivalent is timed "
+                               "beside ours in the ours line (cuda_core)"}
+               if rank == 0 else None) if args.impl == "reference" else run_matmul(args, ws, rank, local)
     elif args.workload == "silu":
         out = run_silu_reference(args, ws, rank) if args.impl == "reference" else run_silu(args, ws, rank, local)
     elif args.workload == "compare":

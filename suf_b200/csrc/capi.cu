@@ -724,7 +724,7 @@ int sufb200_ring_matmul(sufb200_ctx ctx, const uint64_t* d_x, const int64_t* d_w
   g.out = d_y;
   g.os = static_cast<size_t>(M) * N;
   g.status = ctx->d_status;
-  SUFB200_CHECK_CUDA(sufb200::launch_ring_gemm_tc(g, static_cast<int>(batch), as_stream(stream)), "ring matmul launch");
+  SUFB200_CHECK_CUDA(sufb200::launch_ring_gemm_tc(ctx, g, static_cast<int>(batch), as_stream(stream)), "ring matmul launch");
   return SUFB200_OK;
 }
 
@@ -757,7 +757,7 @@ int sufb200_beaver_matmul2d_tc(sufb200_ctx ctx, int party, const uint64_t* d_D_o
   g.out = d_out;
   g.os = static_cast<size_t>(M) * N;
   g.status = ctx->d_status;
-  SUFB200_CHECK_CUDA(sufb200::launch_ring_gemm_tc(g, batches, as_stream(stream)), "Beaver matmul launch");
+  SUFB200_CHECK_CUDA(sufb200::launch_ring_gemm_tc(ctx, g, batches, as_stream(stream)), "Beaver matmul launch");
   return SUFB200_OK;
 }
 

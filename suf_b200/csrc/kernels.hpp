@@ -143,8 +143,35 @@ struct RingGemmLaunch {
   uint64_t* out;
   size_t os;
   uint32_t* status;
+  // set by the launcher
+  int batches;
+  int splits;        // contraction split across CTAs
+  uint64_t* ws;      // split partials [split][batch][M][N]
+  int steps;         // 32-deep steps over all pieces
+  int m_pad, n_pad;  // rows of the plane slabs (multiples of 128 / 64)
+  const uint8_t* xplanes;
+  size_t xps;  // per-batch stride in bytes (0: shared)
+  const uint8_t* yplanes;
+  size_t yps;
 };
-cudaError_t launch_ring_gemm_tc(const RingGemmLaunch& g, int batches, cudaStream_t st);
+
+// One operand's byte planes (ring_gemm_tc.cu::split_planes_kernel).
+struct PlanesPiece {
+  const uint64_t* src;
+  const uint64_t* add;  // optional element-wise addend
+  size_t ss, as;        // per-batch strides in elements
+};
+struct PlanesSplit {
+  PlanesPiece piece[2];
+  int R, K;  // rows (M or N) and depth per piece
+  int rows_pad;
+  int tile_rows;  // GEMM tile rows of this operand (128 for A, 64 for B)
+  int steps;
+  int k_contig;  // (row, k) at src[row * K + k]; else src[k * R + row]
+  uint8_t* dst;
+  size_t ds;  // per-batch stride in bytes
+};
+cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int batches, cudaStream_t st);
 
 // Measured AES-128 block rate of the shared-memory engine (probe.cu).
 cudaError_t probe_aes_engine(const sufb200_ctx_s* ctx, double* blocks_per_s);

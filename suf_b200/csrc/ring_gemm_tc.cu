@@ -5,20 +5,30 @@
 //   x * y mod 2^64 = sum_{i+j <= 7} 2^(8(i+j)) x_i y_j   (terms with i+j >= 8 vanish).
 // A 128 x 64 output tile keeps one int32 accumulator per diagonal s = i + j
 // in tensor memory (8 diagonals x 64 columns = all 512 TMEM columns); every
-// 32-deep K step issues the 36 unsigned 8-bit MMAs (128 x 64 x 32) of the
-// limb pairs into their diagonals, and the epilogue folds
+// 32-deep K step issues twelve unsigned 8-bit MMAs (128 x N x 32, N <= 256)
+// that together cover the 36 limb pairs (i, j), i + j <= 7, each landing in
+// its diagonal, and the epilogue folds
 //   acc = sum_s (P_s mod 2^32) << 8s  mod 2^64.
 // That is exact as long as P_s is exact wherever bits survive the shift:
 // for s <= 3 the diagonal sums stay below 2^31 while K' <= 8192 (P_s <=
 // (s+1) K' 255^2), and for s >= 4 only P_s mod 2^(64-8s) | 2^32 matters,
 // which the non-saturating accumulator keeps.
 //
-// Operands are split into byte planes while they are staged into shared
-// memory, in the canonical K-major no-swizzle layout of the UMMA shared-memory
+// A bandwidth-bound pre-pass writes each operand as 8 byte planes already in
+// the canonical K-major no-swizzle layout of the UMMA shared-memory
 // descriptor (8-row x 16-byte core matrices; leading byte offset 128 between
-// the two K halves, stride byte offset 256 between 8-row groups), two stages
-// deep; one elected thread issues the MMAs and commits each stage to an
-// mbarrier that the staging threads wait on (bounded) before reusing it.
+// the two K halves of a 32-deep step, stride byte offset 256 between 8-row
+// groups), tiled so that a CTA's plane block for one step is one contiguous
+// range.  The GEMM then runs a 4-stage pipeline: one warp issues two plain
+// bulk copies (cp.async.bulk, no multicast) per step, A and B plane blocks,
+// against a transaction-count mbarrier, one warp issues the 36 MMAs of the
+// step and commits them back to the stage's "empty" mbarrier (one lane of
+// each does the issuing), and all warps read the diagonals out of tensor
+// memory at the end.  Every wait is bounded.
+// Contractions too short to fill the GPU are split across CTAs: each stores
+// its partial tile (plain stores, no atomics), and a coalesced reduction
+// kernel adds the partials (addition mod 2^64 commutes), C and the bias and
+// applies the rescale.
 //
 // Serves the reference's Beaver matmul (cuda/cuda_primitives.cu:391-628,
 // out = C + D B + A E (+ D E for party 0) as ONE product [D | A] x [B (+E) ; E])
@@ -34,17 +44,16 @@ constexpr int kTM = 128;  // output rows per tile (TMEM lanes)
 constexpr int kTN = 64;   // output columns per tile (per diagonal)
 constexpr int kTK = 32;   // K per MMA (8-bit operands)
 constexpr int kThreads = 128;
-constexpr uint32_t kPlaneX = kTM * kTK;             // 4 KB
-constexpr uint32_t kPlaneY = kTN * kTK;             // 2 KB
+constexpr int kStages = 4;
+constexpr uint32_t kPlaneX = kTM * kTK;                    // 4 KB: one plane of the A tile
+constexpr uint32_t kPlaneY = kTN * kTK;                    // 2 KB: one plane of the B tile
 constexpr uint32_t kStageBytes = 8 * (kPlaneX + kPlaneY);  // 48 KB
-constexpr uint32_t kCtrlOffset = 2 * kStageBytes;   // mbarriers, TMEM slot
-// Requested dynamic shared memory: enough that two CTAs never share an SM,
-// so each can own all 512 TMEM columns.
-constexpr uint32_t kSmemBytes = 120 * 1024;
+constexpr uint32_t kCtrlOffset = kStages * kStageBytes;    // mbarriers, error flag, TMEM slot
+constexpr uint32_t kSmemBytes = kCtrlOffset + 256;         // 192 KB: one CTA per SM, all 512 TMEM columns
 constexpr uint32_t kTmemCols = 512;
-// idesc for kind::i8: D s32 (bits 4-5 = 2), A and B unsigned 8-bit, both
-// K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
-constexpr uint32_t kIdesc = (2u << 4) | (uint32_t(kTN >> 3) << 17) | (uint32_t(kTM >> 4) << 24);
+// idesc for kind::i8 with M = 128 and the given N: D s32 (bits 4-5 = 2), A
+// and B unsigned 8-bit, both K-major, N >> 3 at bits 17-22, M >> 4 at 24-28.
+__host__ __device__ constexpr uint32_t idesc_n(int n) { return (2u << 4) | (uint32_t(n >> 3) << 17) | (uint32_t(kTM >> 4) << 24); }
 constexpr uint32_t kWaitIters = 1u << 26;
 constexpr uint64_t kWaitNs = 2000000000ull;  // give up after 2 s of wall time
 
@@ -88,19 +97,21 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   return false;
 }
 
-__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
       :
-      : "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+      : "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
+// 16 columns of this warp's 32 lanes; the registers are valid after tmem_wait.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
@@ -108,47 +119,107 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Byte i of 16 consecutive words -> 16 bytes of plane i (one row half of a
-// core matrix), for all 8 planes.
-__device__ __forceinline__ void split_store(const uint64_t (&v)[16], uint32_t base, uint32_t plane_stride) {
-#pragma unroll
-  for (int i = 0; i < 8; i++) {
-    uint32_t w[4];
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const uint32_t a0 = static_cast<uint32_t>(v[4 * q + 0] >> (i < 4 ? 0 : 32));
-      const uint32_t a1 = static_cast<uint32_t>(v[4 * q + 1] >> (i < 4 ? 0 : 32));
-      const uint32_t a2 = static_cast<uint32_t>(v[4 * q + 2] >> (i < 4 ? 0 : 32));
-      const uint32_t a3 = static_cast<uint32_t>(v[4 * q + 3] >> (i < 4 ? 0 : 32));
-      const uint32_t sel = static_cast<uint32_t>(i & 3) | (static_cast<uint32_t>(4 + (i & 3)) << 4);
-      const uint32_t t01 = __byte_perm(a0, a1, sel);
-      const uint32_t t23 = __byte_perm(a2, a3, sel);
-      w[q] = __byte_perm(t01, t23, 0x5410);
-    }
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(base + static_cast<uint32_t>(i) * plane_stride),
-                 "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
-                 : "memory");
-  }
+// Waits for this thread's outstanding tensor-memory loads; taking the
+// registers as operands keeps every use of them after the wait.
+__device__ __forceinline__ void tmem_wait(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
 }
 
-// Shared-memory offset of (row r, K half h) inside a plane.
+// Offset of (row r, K half h) inside a plane slab (core-matrix order).
 __device__ __forceinline__ uint32_t core_off(int r, int h) {
   return static_cast<uint32_t>((r >> 3) * 256 + h * 128 + (r & 7) * 16);
 }
 
-template <bool TRANS>
+__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Byte planes of one operand, tiled for the GEMM: for step c and row tile
+// (tile rows T = 128 for A, 64 for B) the 8 planes of T rows x 32 bytes in
+// core-matrix order, contiguous (one bulk copy per operand per step).
+// Unit (c, h, r): 16 K-consecutive words of row r, K half h of step c.
+// k_contig: element (row, k) at src[row * K + k], else at src[k * R + row].
+__device__ __forceinline__ void split_planes(const PlanesSplit& p, int block, int nblocks, int b) {
+  const size_t units = static_cast<size_t>(p.steps) * 2 * static_cast<size_t>(p.rows_pad);
+  const int cpp = (p.K + kTK - 1) / kTK;
+  for (size_t u = static_cast<size_t>(block) * blockDim.x + threadIdx.x; u < units;
+       u += static_cast<size_t>(nblocks) * blockDim.x) {
+    const int r = static_cast<int>(u % static_cast<size_t>(p.rows_pad));
+    const int h = static_cast<int>((u / static_cast<size_t>(p.rows_pad)) & 1);
+    const int c = static_cast<int>(u / (2 * static_cast<size_t>(p.rows_pad)));
+    const bool second = c >= cpp;  // selects, not an indexed copy of the parameter
+    const uint64_t* src = (second ? p.piece[1].src : p.piece[0].src) +
+                          static_cast<size_t>(b) * (second ? p.piece[1].ss : p.piece[0].ss);
+    const uint64_t* add = second ? p.piece[1].add : p.piece[0].add;
+    if (add) add += static_cast<size_t>(b) * (second ? p.piece[1].as : p.piece[0].as);
+    const int k0 = (c % cpp) * kTK + 16 * h;
+    uint64_t v[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const int k = k0 + j;
+      uint64_t val = 0;
+      if (r < p.R && k < p.K) {
+        const size_t idx = p.k_contig ? static_cast<size_t>(r) * p.K + k : static_cast<size_t>(k) * p.R + r;
+        val = __ldg(src + idx);
+        if (add) val += __ldg(add + idx);
+      }
+      v[j] = val;
+    }
+    uint8_t* dst = p.dst + static_cast<size_t>(b) * p.ds;
+    const int tiles = p.rows_pad / p.tile_rows, tile = r / p.tile_rows, rr = r % p.tile_rows;
+    const size_t plane = static_cast<size_t>(p.tile_rows) * kTK;
+    uint8_t* blk = dst + ((static_cast<size_t>(c) * tiles + tile) * 8) * plane;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint32_t a0 = static_cast<uint32_t>(v[4 * q + 0] >> (i < 4 ? 0 : 32));
+        const uint32_t a1 = static_cast<uint32_t>(v[4 * q + 1] >> (i < 4 ? 0 : 32));
+        const uint32_t a2 = static_cast<uint32_t>(v[4 * q + 2] >> (i < 4 ? 0 : 32));
+        const uint32_t a3 = static_cast<uint32_t>(v[4 * q + 3] >> (i < 4 ? 0 : 32));
+        const uint32_t sel = static_cast<uint32_t>(i & 3) | (static_cast<uint32_t>(4 + (i & 3)) << 4);
+        w[q] = __byte_perm(__byte_perm(a0, a1, sel), __byte_perm(a2, a3, sel), 0x5410);
+      }
+      *reinterpret_cast<uint4*>(blk + i * plane + core_off(rr, h)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// Both operands in one launch: blocks [0, xblocks) split A, the rest split B
+// (blockIdx.y = batch, for an operand with per-batch planes).
+__global__ void split_planes_kernel(const PlanesSplit px, const PlanesSplit py, int xblocks, int xb, int yb) {
+  const int b = blockIdx.y;
+  if (static_cast<int>(blockIdx.x) < xblocks) {
+    if (b < xb) split_planes(px, blockIdx.x, xblocks, b);
+  } else if (b < yb) {
+    split_planes(py, blockIdx.x - xblocks, gridDim.x - xblocks, b);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGemmLaunch g) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int b = blockIdx.z;
+  const int b = blockIdx.z / g.splits, split = blockIdx.z % g.splits;
   const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
-  const int M = g.M, N = g.N, K = g.K;
+  const int M = g.M, N = g.N;
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar0 = sbase + kCtrlOffset, bar1 = bar0 + 8, slot = bar0 + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kCtrlOffset + 16);
+  const uint32_t full0 = sbase + kCtrlOffset, empty0 = full0 + 8 * kStages, done = empty0 + 8 * kStages;
+  const uint32_t slot = done + 8;
+  volatile uint32_t* err = reinterpret_cast<volatile uint32_t*>(smem + kCtrlOffset + 16 * kStages + 16);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kCtrlOffset + 16 * kStages + 8);
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(kTmemCols)
@@ -156,122 +227,134 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (t == 0) {
-    mbar_init(bar0, 1);
-    mbar_init(bar1, 1);
+    for (int i = 0; i < kStages; i++) {
+      mbar_init(full0 + 8 * i, 1);
+      mbar_init(empty0 + 8 * i, 1);
+    }
+    mbar_init(done, 1);
+    *err = 0;
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  const int cpp = (K + kTK - 1) / kTK;  // K steps per piece
-  const int steps = cpp * g.npieces;
-  bool ok = true;
-  for (int c = 0; c < steps; c++) {
-    const int st = c & 1;
-    // stage st was last read by the MMAs of step c - 2
-    const bool free_ok = c < 2 || mbar_wait(st ? bar1 : bar0, static_cast<uint32_t>(((c >> 1) - 1) & 1));
-    const RingGemmPiece& P = g.piece[c / cpp];
-    const int kc = (c % cpp) * kTK;
-    const uint32_t xs = sbase + static_cast<uint32_t>(st) * kStageBytes;
-    const uint32_t ys = xs + 8 * kPlaneX;
-    const uint64_t* X = P.x + static_cast<size_t>(b) * P.xs;
-    const bool x_vec = (K & 1) == 0 && (reinterpret_cast<uintptr_t>(X) & 15u) == 0;  // 16-byte row loads
-    // X tile: unit (row r = t, K half h), 16 words each
-#pragma unroll 1
-    for (int h = 0; h < 2; h++) {
-      const int m = m0 + t, k = kc + 16 * h;
-      uint64_t v[16];
-      if (m < M && k + 16 <= K && x_vec) {
-        const ulonglong2* src = reinterpret_cast<const ulonglong2*>(X + static_cast<size_t>(m) * K + k);
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-          const ulonglong2 q = __ldg(src + j);
-          v[2 * j] = q.x;
-          v[2 * j + 1] = q.y;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; j++) v[j] = (m < M && k + j < K) ? __ldg(X + static_cast<size_t>(m) * K + k + j) : 0ull;
-      }
-      split_store(v, xs + core_off(t, h), kPlaneX);
-    }
-    // Y tile: unit (row r = n, K half h)
-    {
-      const int r = t & 63, h = t >> 6;  // lanes on consecutive rows: coalesced, conflict-free
-      const int n = n0 + r, k = kc + 16 * h;
-      const uint64_t* Y = P.y + static_cast<size_t>(b) * P.ys;
-      const uint64_t* Y2 = P.y2 ? P.y2 + static_cast<size_t>(b) * P.y2s : nullptr;
-      uint64_t v[16];
-#pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const int kk = k + j;
-        uint64_t val = 0;
-        if (n < N && kk < K) {
-          const size_t idx = TRANS ? static_cast<size_t>(n) * K + kk : static_cast<size_t>(kk) * N + n;
-          val = __ldg(Y + idx);
-          if (Y2) val += __ldg(Y2 + idx);
-        }
-        v[j] = val;
-      }
-      split_store(v, ys + core_off(r, h), kPlaneY);
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    ok = __syncthreads_and(free_ok ? 1 : 0) != 0;  // one verdict for the whole block
-    if (!ok) break;
-    if (t == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const uint64_t ad = umma_desc(xs + static_cast<uint32_t>(i) * kPlaneX);
-#pragma unroll
-        for (int j = 0; j + i < 8; j++) {
-          const uint64_t bd = umma_desc(ys + static_cast<uint32_t>(j) * kPlaneY);
-          umma_i8(tmem + static_cast<uint32_t>((i + j) * kTN), ad, bd, (c > 0 || i > 0) ? 1u : 0u);
+  // this CTA's share of the contraction: steps [c0, c1)
+  const int per = (g.steps + g.splits - 1) / g.splits;
+  const int c0 = split * per, c1 = c0 + per < g.steps ? c0 + per : g.steps;
+  const int nsteps = c1 > c0 ? c1 - c0 : 0;
+  const uint8_t* xp = g.xplanes + static_cast<size_t>(b) * g.xps;
+  const uint8_t* yp = g.yplanes + static_cast<size_t>(b) * g.yps;
+  const int tiles_m = g.m_pad / kTM, tiles_n = g.n_pad / kTN;
+
+  // Roles are warp-uniform: lane 0 waits and issues while the other lanes of
+  // its warp sit at the warp's shuffle, so no lane of the issuing warp spins
+  // on a different barrier than the one lane 0 is serving.
+  if (warp == 0) {  // producer: one bulk copy per operand per step
+    for (int li = 0; li < nsteps; li++) {
+      const int st = li % kStages;
+      const uint32_t sb = sbase + static_cast<uint32_t>(st) * kStageBytes;
+      const uint32_t fb = full0 + 8 * st;
+      int go = 1;
+      if (lane == 0) {
+        go = li < kStages || mbar_wait(empty0 + 8 * st, static_cast<uint32_t>(((li / kStages) - 1) & 1));
+        if (go) {
+          mbar_expect_tx(fb, kStageBytes);
+          const size_t c = static_cast<size_t>(c0 + li);
+          bulk_copy(sb, xp + (c * tiles_m + blockIdx.y) * (8 * kPlaneX), 8 * kPlaneX, fb);
+          bulk_copy(sb + 8 * kPlaneX, yp + (c * tiles_n + blockIdx.x) * (8 * kPlaneY), 8 * kPlaneY, fb);
+        } else {
+          *err = 1;
         }
       }
-      umma_commit(st ? bar1 : bar0);
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
     }
+  } else if (warp == 1) {  // MMA issuer: the 36 limb MMAs of a step, then release the stage
+    // Stage 0's plane descriptors and the diagonals' column addresses, once:
+    // a stage's descriptors are these plus its byte offset >> 4 in the start
+    // field (shared-memory addresses stay below 2^18, so the field never
+    // carries), which leaves one instruction per MMA to issue.
+    uint64_t ad[8], bd[8];
+    uint32_t dt[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      ad[i] = umma_desc(sbase + static_cast<uint32_t>(i) * kPlaneX);
+      bd[i] = umma_desc(sbase + 8 * kPlaneX + static_cast<uint32_t>(i) * kPlaneY);
+      dt[i] = tmem + static_cast<uint32_t>(i * kTN);
+    }
+    for (int li = 0; li < nsteps; li++) {
+      const int st = li % kStages;
+      int go = 1;
+      if (lane == 0) {
+        go = mbar_wait(full0 + 8 * st, static_cast<uint32_t>((li / kStages) & 1));
+        if (go) {
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t so = static_cast<uint64_t>((static_cast<uint32_t>(st) * kStageBytes) >> 4);
+          uint64_t as[8], bs[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            as[i] = ad[i] + so;
+            bs[i] = bd[i] + so;
+          }
+          // The B planes of a stage are consecutive 64-row blocks in core-matrix
+          // order, so [y_0 | y_1 | y_2 | y_3] is one N = 256 operand.  x_i times
+          // it, accumulated at column 64 i, lands product (i, j) on column
+          // 64 (i + j): diagonal i + j.  Twelve MMAs (N = 256 except where the
+          // 512 columns end) cover the 36 limb pairs; the first two write all
+          // 512 columns, so on the first step they alone start from zero.
+          const uint32_t first = li > 0 ? 1u : 0u;
+          umma_i8(dt[0], as[0], bs[0], idesc_n(256), first);
+          umma_i8(dt[4], as[0], bs[4], idesc_n(256), first);
+#pragma unroll
+          for (int i = 1; i < 8; i++) umma_i8(dt[i], as[i], bs[0], idesc_n(i <= 4 ? 256 : 64 * (8 - i)), 1u);
+#pragma unroll
+          for (int i = 1; i < 4; i++) umma_i8(dt[i + 4], as[i], bs[4], idesc_n(256 - 64 * i), 1u);
+          umma_commit(empty0 + 8 * st);
+        } else {
+          *err = 1;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+    }
+    if (lane == 0) umma_commit(done);  // arrives once every MMA issued above has completed
+    __syncwarp();
   }
-  // every MMA issued so far has completed once the last commit arrives
-  if (ok && steps > 0) {
-    const int last = steps - 1;
-    ok = __syncthreads_and(mbar_wait((last & 1) ? bar1 : bar0, static_cast<uint32_t>((last >> 1) & 1)) ? 1 : 0) != 0;
-  }
+  bool ok = mbar_wait(done, 0);
+  ok = __syncthreads_and(ok ? 1 : 0) != 0 && *err == 0;
   if (!ok) {
     if (t == 0) atomicOr(g.status, kStatusTimeout);
-    // let whatever was issued drain before the columns are released
-    if (steps > 0) {
-      const int last = steps - 1;
-      mbar_wait((last & 1) ? bar1 : bar0, static_cast<uint32_t>((last >> 1) & 1));
-    }
-  } else {
+    mbar_wait(done, 0);  // let whatever was issued drain before the columns are released
+  } else if (nsteps > 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int m = m0 + warp * 32 + lane;
     const uint64_t* C = g.c ? g.c + static_cast<size_t>(b) * g.cs : nullptr;
     uint64_t* O = g.out + static_cast<size_t>(b) * g.os;
+    // a split CTA stores its raw partial; the reduction kernel finishes the sum
+    uint64_t* W = g.splits > 1 ? g.ws + (static_cast<size_t>(split) * g.batches + b) * M * N : nullptr;
 #pragma unroll 1
     for (int cb = 0; cb < kTN / 16; cb++) {
-      uint64_t acc[16];
+      uint32_t v[8][16];  // the 8 diagonals of 16 columns, loaded before one wait
 #pragma unroll
-      for (int j = 0; j < 16; j++) acc[j] = 0;
+      for (int s = 0; s < 8; s++)
+        tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(s * kTN + cb * 16), v[s]);
 #pragma unroll
-      for (int s = 0; s < 8; s++) {
-        uint32_t v[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(s * kTN + cb * 16), v);
-#pragma unroll
-        for (int j = 0; j < 16; j++) acc[j] += static_cast<uint64_t>(v[j]) << (8 * s);
-      }
+      for (int s = 0; s < 8; s++) tmem_wait(v[s]);
       if (m < M) {
 #pragma unroll
         for (int j = 0; j < 16; j++) {
+          uint64_t acc = 0;
+#pragma unroll
+          for (int s = 0; s < 8; s++) acc += static_cast<uint64_t>(v[s][j]) << (8 * s);
           const int n = n0 + cb * 16 + j;
           if (n < N) {
             const size_t o = static_cast<size_t>(m) * N + n;
-            uint64_t val = acc[j];
-            if (C) val += C[o];
-            if (g.bias) val += static_cast<uint64_t>(g.bias[n]);
-            O[o] = scaled_acc(val, g.has_scale, g.mul_const, g.mul_shift);
+            if (W) {
+              W[o] = acc;
+            } else {
+              if (C) acc += C[o];
+              if (g.bias) acc += static_cast<uint64_t>(g.bias[n]);
+              O[o] = scaled_acc(acc, g.has_scale, g.mul_const, g.mul_shift);
+            }
           }
         }
       }
@@ -285,23 +368,111 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
   }
 }
 
+// out = scale(sum of the split partials + C + bias), coalesced.
+__global__ void ring_gemm_reduce_kernel(const RingGemmLaunch g) {
+  const size_t mn = static_cast<size_t>(g.M) * g.N, total = mn * static_cast<size_t>(g.batches);
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t b = i / mn, o = i % mn;
+    uint64_t val = 0;
+#pragma unroll 4
+    for (int sp = 0; sp < g.splits; sp++) val += g.ws[(static_cast<size_t>(sp) * g.batches + b) * mn + o];
+    if (g.c) val += g.c[b * g.cs + o];
+    if (g.bias) val += static_cast<uint64_t>(g.bias[o % g.N]);
+    g.out[b * g.os + o] = scaled_acc(val, g.has_scale, g.mul_const, g.mul_shift);
+  }
+}
+
 }  // namespace
 
-cudaError_t launch_ring_gemm_tc(const RingGemmLaunch& g, int batches, cudaStream_t st) {
+cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int batches, cudaStream_t st) {
   if (g.npieces < 1 || g.npieces > 2 || g.M < 1 || g.N < 1 || g.K < 1 || batches < 1) return cudaErrorInvalidValue;
-  const dim3 grid(static_cast<unsigned>((g.N + kTN - 1) / kTN), static_cast<unsigned>((g.M + kTM - 1) / kTM),
-                  static_cast<unsigned>(batches));
-  cudaError_t e;
-  if (g.trans) {
-    e = cudaFuncSetAttribute(ring_gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    ring_gemm_tc_kernel<true><<<grid, kThreads, kSmemBytes, st>>>(g);
-  } else {
-    e = cudaFuncSetAttribute(ring_gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    ring_gemm_tc_kernel<false><<<grid, kThreads, kSmemBytes, st>>>(g);
+  const int tiles_n = (g.N + kTN - 1) / kTN, tiles_m = (g.M + kTM - 1) / kTM;
+  g.m_pad = tiles_m * kTM;
+  g.n_pad = tiles_n * kTN;
+  g.steps = ((g.K + kTK - 1) / kTK) * g.npieces;
+  const long long tiles = static_cast<long long>(tiles_n) * tiles_m * batches;
+  // split the contraction so one wave fills the SMs, keeping >= 8 steps per CTA
+  long long splits = ctx->sm_count / tiles;
+  if (splits > g.steps / 8) splits = g.steps / 8;
+  if (splits < 1) splits = 1;
+  if (static_cast<long long>(batches) * splits > 65535) splits = 1;
+  // every split non-empty: each one's arrival completes its tile's count
+  const long long per = (g.steps + splits - 1) / splits;
+  splits = (g.steps + per - 1) / per;
+  g.splits = static_cast<int>(splits);
+  // X planes per batch when any X piece varies per batch, else one copy; same for Y
+  bool x_per_batch = false, y_per_batch = false;
+  for (int p = 0; p < g.npieces; p++) {
+    x_per_batch |= g.piece[p].xs != 0;
+    y_per_batch |= g.piece[p].ys != 0 || (g.piece[p].y2 && g.piece[p].y2s != 0);
   }
-  return cudaGetLastError();
+  const size_t xbytes = static_cast<size_t>(g.steps) * 8 * g.m_pad * kTK;
+  const size_t ybytes = static_cast<size_t>(g.steps) * 8 * g.n_pad * kTK;
+  const int xb = x_per_batch ? batches : 1, yb = y_per_batch ? batches : 1;
+  g.batches = batches;
+  const size_t ws_bytes =
+      g.splits > 1 ? static_cast<size_t>(g.splits) * batches * static_cast<size_t>(g.M) * g.N * 8 : 0;
+  uint8_t* scratch = nullptr;
+  const size_t xoff = 0, yoff = (xbytes * xb + 255) & ~size_t{255};
+  const size_t woff = (yoff + ybytes * yb + 255) & ~size_t{255};
+  cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), woff + ws_bytes, ctx->pool, st);
+  if (e != cudaSuccess) return e;
+  g.xplanes = scratch + xoff;
+  g.xps = x_per_batch ? xbytes : 0;
+  g.yplanes = scratch + yoff;
+  g.yps = y_per_batch ? ybytes : 0;
+  g.ws = g.splits > 1 ? reinterpret_cast<uint64_t*>(scratch + woff) : nullptr;
+  // the operands as tiled byte planes
+  PlanesSplit px{};
+  PlanesSplit py{};
+  for (int p = 0; p < g.npieces; p++) {
+    px.piece[p] = PlanesPiece{g.piece[p].x, nullptr, g.piece[p].xs, 0};
+    py.piece[p] = PlanesPiece{g.piece[p].y, g.piece[p].y2, g.piece[p].ys, g.piece[p].y2s};
+  }
+  px.R = g.M;
+  px.K = g.K;
+  px.rows_pad = g.m_pad;
+  px.tile_rows = kTM;
+  px.steps = g.steps;
+  px.k_contig = 1;
+  px.dst = scratch + xoff;
+  px.ds = xbytes;
+  py.R = g.N;
+  py.K = g.K;
+  py.rows_pad = g.n_pad;
+  py.tile_rows = kTN;
+  py.steps = g.steps;
+  py.k_contig = g.trans ? 1 : 0;
+  py.dst = scratch + yoff;
+  py.ds = ybytes;
+  auto split_blocks = [](const PlanesSplit& q) {
+    const size_t units = static_cast<size_t>(q.steps) * 2 * q.rows_pad;
+    const size_t want = (units + 255) / 256;
+    return static_cast<int>(want < 8192 ? (want ? want : 1) : 8192);
+  };
+  const int xblocks = split_blocks(px), yblocks = split_blocks(py);
+  if (e == cudaSuccess) {
+    const dim3 sgrid(static_cast<unsigned>(xblocks + yblocks), static_cast<unsigned>(xb > yb ? xb : yb));
+    split_planes_kernel<<<sgrid, 256, 0, st>>>(px, py, xblocks, xb, yb);
+    e = cudaGetLastError();
+  }
+  const dim3 grid(static_cast<unsigned>(tiles_n), static_cast<unsigned>(tiles_m),
+                  static_cast<unsigned>(batches * g.splits));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(ring_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e == cudaSuccess) {
+    ring_gemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(g);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess && g.splits > 1) {
+    const size_t want = (static_cast<size_t>(batches) * g.M * g.N + 255) / 256;
+    const size_t cap = static_cast<size_t>(ctx->sm_count) * 8;
+    ring_gemm_reduce_kernel<<<static_cast<unsigned>(want < cap ? (want ? want : 1) : cap), 256, 0, st>>>(g);
+    e = cudaGetLastError();
+  }
+  cudaFreeAsync(scratch, st);
+  return e;
 }
 
 }  // namespace sufb200
