@@ -344,3 +344,54 @@ def test_limb_identity_is_exact(k):
         assert (_limb_product(x, y) == _exact_product(x, y)).all()
     worst = 4 * 8192 * 255 * 255  # diagonal s = 3 at the maximum depth
     assert worst < 2**31
+
+
+# The twelve MMAs of one step of ring_gemm_tc.cu: (TMEM column, x plane,
+# first y plane of the operand, N).  Operand y_b.. of width N covers the
+# planes b .. b + N/64 - 1, and product (i, j) lands on column 64 (i + j).
+def _ring_gemm_schedule():
+    sched = [(0, 0, 0, 256), (256, 0, 4, 256)]
+    sched += [(64 * i, i, 0, 256 if i <= 4 else 64 * (8 - i)) for i in range(1, 8)]
+    sched += [(64 * (i + 4), i, 4, 256 - 64 * i) for i in range(1, 4)]
+    return sched
+
+
+def test_ring_gemm_schedule_covers_every_limb_pair_once():
+    src = (Path(__file__).resolve().parents[1] / "suf_b200" / "csrc" / "ring_gemm_tc.cu").read_text()
+    for pat in (r"umma_i8\(dt\[0\], as\[0\], bs\[0\], idesc_n\(256\), first\)",
+                r"umma_i8\(dt\[4\], as\[0\], bs\[4\], idesc_n\(256\), first\)",
+                r"for \(int i = 1; i < 8; i\+\+\) umma_i8\(dt\[i\], as\[i\], bs\[0\], idesc_n\(i <= 4 \? 256 : 64 \* \(8 - i\)\), 1u\)",
+                r"for \(int i = 1; i < 4; i\+\+\) umma_i8\(dt\[i \+ 4\], as\[i\], bs\[4\], idesc_n\(256 - 64 \* i\), 1u\)"):
+        assert re.search(pat, src), pat
+    sched = _ring_gemm_schedule()
+    assert len(sched) == 12
+    seen = {}
+    for col, i, b, n in sched:
+        assert n % 16 == 0 and 16 <= n <= 256 and col + n <= 512 and b * 64 + n <= 512
+        for q in range(n // 64):
+            j = b + q
+            assert col + 64 * q == 64 * (i + j)  # lands on diagonal i + j
+            seen[(i, j)] = seen.get((i, j), 0) + 1
+    assert seen == {(i, j): 1 for i in range(8) for j in range(8) if i + j <= 7}
+    # the two MMAs that start from zero on the first step cover all 512 columns
+    assert sorted((c, c + n) for c, _, _, n in sched[:2]) == [(0, 256), (256, 512)]
+
+
+def test_ring_gemm_schedule_product_is_exact():
+    """Numpy emulation of the twelve MMAs (u8 planes, wrapping int32
+    columns) folded as the epilogue does, against the exact product."""
+    rng = np.random.default_rng(12)
+    M, K, N = 5, 96, 3
+    x = rng.integers(0, 2**63, (M, K), dtype=np.uint64) * np.uint64(2) + np.uint64(1)
+    y = rng.integers(0, 2**63, (K, N), dtype=np.uint64) * np.uint64(3)
+    xp = [((x >> np.uint64(8 * i)) & np.uint64(255)).astype(np.int64) for i in range(8)]
+    yp = [((y >> np.uint64(8 * j)) & np.uint64(255)).astype(np.int64) for j in range(8)]
+    tmem = np.zeros((M, 8, N), dtype=np.int64)  # column block s of width N stands for 64 columns
+    for col, i, b, n in _ring_gemm_schedule():
+        for q in range(n // 64):
+            tmem[:, col // 64 + q] = (tmem[:, col // 64 + q] + xp[i] @ yp[b + q]) % 2**32
+    acc = np.zeros((M, N), dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        for s in range(8):
+            acc += tmem[:, s].astype(np.uint64) << np.uint64(8 * s)
+    assert (acc == _exact_product(x, y)).all()
