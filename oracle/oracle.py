@@ -65,7 +65,7 @@ def build_oracle(quiet: bool = True) -> None:
     if Path(os.environ.get("SUF_REFERENCE", "/root/reference"), "third_party", "myl7_fss").is_dir():
         targets.append("ref")
         if (HERE.parent / "suf_b200" / "libsufb200.so").exists():
-            targets.append("drive")
+            targets += ["drive", "softmax"]
     subprocess.run(["make", "-C", str(HERE)] + targets, check=True,
                    stdout=subprocess.DEVNULL if quiet else None)
 
