@@ -48,6 +48,7 @@
 #include "nn/softmax_block_task.hpp"
 #include "proto/backend_gpu.hpp"
 #include "proto/reference_backend.hpp"
+#include "runtime/pfss_gpu_staging.hpp"
 #include "runtime/phase_executor.hpp"
 #include "runtime/pfss_superbatch.hpp"
 
@@ -179,6 +180,13 @@ Material deal(proto::PfssBackendBatch& be, const Workload& w, uint64_t seed) {
 std::vector<uint64_t> run_party(int party, proto::PfssBackendBatch& be, net::Chan& ch, const Workload& w,
                                 const Material& mat, runtime::RowBroadcastTripleProvider* rt,
                                 std::span<const uint64_t> t) {
+  // A GPU backend gets the reference's CUDA stager, as its bench does in device
+  // mode: the superbatch then stages x^ on the device and the composite driver
+  // takes the broadcast-key device path (pfss_superbatch.cpp:306-339).  It is
+  // declared before the executor, which holds a pointer to it.
+  std::unique_ptr<runtime::CudaPfssStager> stager;
+  if (auto* staged = dynamic_cast<proto::PfssGpuStagedEval*>(&be))
+    stager = std::make_unique<runtime::CudaPfssStager>(staged->device_stream());
   runtime::PhaseExecutor pe;
   runtime::PhaseResources R{};
   runtime::ProtoChanFromNet pch(ch);
@@ -189,6 +197,10 @@ std::vector<uint64_t> run_party(int party, proto::PfssBackendBatch& be, net::Cha
   R.pfss_coeff = &pe.pfss_coeff_batch();
   R.pfss_trunc = &pe.pfss_trunc_batch();
   R.opens = &pe.open_collector();
+  if (stager) {
+    pe.pfss_coeff_batch().set_gpu_stager(stager.get());
+    pe.pfss_trunc_batch().set_gpu_stager(stager.get());
+  }
 
   nn::SoftmaxPlan plan;
   plan.frac_bits = w.fb;

@@ -131,8 +131,9 @@ class SufB200Backend final : public PfssIntervalLutExt, public PackedLtBackend, 
   void eval_dcf_many_u64(int in_bits, size_t key_bytes, const uint8_t* keys_flat, const std::vector<u64>& xs,
                          int out_bytes, uint8_t* outs_flat) const override {
     if (xs.empty()) return;
+    const int bc = replicated(keys_flat, key_bytes, xs.size()) ? 1 : 0;
     std::lock_guard<std::mutex> lk(mu_);
-    check(sufb200_myl7_dcf_eval_host(ctx_, opt_.group, in_bits, keys_flat, key_bytes, 0, xs.data(), xs.size(),
+    check(sufb200_myl7_dcf_eval_host(ctx_, opt_.group, in_bits, keys_flat, key_bytes, bc, xs.data(), xs.size(),
                                      out_bytes, outs_flat),
           "eval_dcf_many_u64");
   }
@@ -308,6 +309,21 @@ class SufB200Backend final : public PfssIntervalLutExt, public PackedLtBackend, 
     }
   }
 
+  // True when all n keys of a per-element key block are byte-identical to the
+  // first.  The reference's composite driver, given host x^, copies its one
+  // broadcast key n times before calling the batch entry points
+  // (composite_fss.hpp:1515-1519); evaluating that block as one broadcast key
+  // gives the same shares (every format's per-element counter depends on the
+  // element index only) without uploading and walking n copies.
+  static bool replicated(const uint8_t* keys, size_t key_bytes, size_t n) {
+    if (n < 2 || key_bytes == 0) return false;
+    int same = 1;
+#pragma omp parallel for schedule(static) reduction(&& : same)
+    for (long long i = 1; i < static_cast<long long>(n); i++)
+      same = same && std::memcmp(keys + static_cast<size_t>(i) * key_bytes, keys, key_bytes) == 0;
+    return same != 0;
+  }
+
   const uint64_t* upload_xs(const u64* xs, size_t n) const {
     xs_buf_.ensure(n * 8);
     cuda(cudaMemcpyAsync(xs_buf_.ptr, xs, n * 8, cudaMemcpyHostToDevice, stream_), "H2D xs");
@@ -329,6 +345,7 @@ class SufB200Backend final : public PfssIntervalLutExt, public PackedLtBackend, 
                   int out_bytes, uint8_t* outs) const {
     if (N == 0) return;
     if (!keys || !xs) throw std::runtime_error("SufB200Backend: null keys / xs_device");
+    broadcast = broadcast || replicated(keys, key_bytes, N);
     const uint8_t* dk = upload_keys(keys, broadcast ? key_bytes : key_bytes * N);
     bool_buf_.ensure(N * static_cast<size_t>(out_bytes));
     check(sufb200_myl7_dcf_eval(ctx_, opt_.group, in_bits, dk, key_bytes, broadcast ? 1 : 0, xs, N, out_bytes,
@@ -341,6 +358,7 @@ class SufB200Backend final : public PfssIntervalLutExt, public PackedLtBackend, 
                      int out_words, uint64_t* outs) const {
     if (N == 0) return;
     if (!keys || !xs) throw std::runtime_error("SufB200Backend: null keys / xs");
+    broadcast = broadcast || replicated(keys, key_bytes, N);
     const uint8_t* dk = upload_keys(keys, broadcast ? key_bytes : key_bytes * N);
     bool_buf_.ensure(N * static_cast<size_t>(out_words) * 8);
     check(sufb200_packed_lt_eval(ctx_, dk, key_bytes, broadcast ? 1 : 0, xs, N, in_bits, out_words, 0,
@@ -353,6 +371,7 @@ class SufB200Backend final : public PfssIntervalLutExt, public PackedLtBackend, 
                   uint64_t* outs) const {
     if (N == 0) return;
     if (!keys || !xs) throw std::runtime_error("SufB200Backend: null keys / xs");
+    broadcast = broadcast || replicated(keys, key_bytes, N);
     const uint8_t* dk = upload_keys(keys, broadcast ? key_bytes : key_bytes * N);
     out_buf_.ensure(N * static_cast<size_t>(out_words) * 8);
     check(sufb200_interval_lut_eval(ctx_, dk, key_bytes, broadcast ? 1 : 0, xs, N, out_words, 0,
