@@ -26,8 +26,10 @@
 // (SUF_TRUNC_GPU, SUF_MUL_GPU, SUF_RECIP_GPU_KERNELS, SUF_HORNER_GPU,
 // SUF_PFSS_CACHE_KEYS/HATX), so its Beaver products, row sums and
 // truncations go through the cuda_primitives launchers, i.e. our kernels;
-// with --switches=0 only the PFSS gates run on the GPU.  Prints one JSON line with both wall times
-// per block and whether the reconstructed probabilities are identical.
+// with --switches=0 only the PFSS gates run on the GPU.  Prints one JSON line
+// with both wall times per block and whether the reconstructed probabilities
+// are identical; --dump=PATH also writes the input t and the CPU backend's
+// reconstruction (raw little-endian u64, rows*cols each).
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -268,6 +270,7 @@ double active_max_err(const Workload& w, const std::vector<uint64_t>& y) {
 int main(int argc, char** argv) {
   int heads = 12, len = 128, fb = 12, reps = 3, switches = 1;
   uint64_t seed = 4;
+  std::string dump;  // --dump=PATH: t[rows*cols] then the CPU reconstruction, little-endian u64
   for (int i = 1; i < argc; i++) {
     const std::string a(argv[i]);
     auto val = [&](const char* k) { return a.substr(std::strlen(k)); };
@@ -277,6 +280,7 @@ int main(int argc, char** argv) {
     else if (a.rfind("--reps=", 0) == 0) reps = std::stoi(val("--reps="));
     else if (a.rfind("--seed=", 0) == 0) seed = std::stoull(val("--seed="));
     else if (a.rfind("--switches=", 0) == 0) switches = std::stoi(val("--switches="));
+    else if (a.rfind("--dump=", 0) == 0) dump = val("--dump=");
   }
   const Workload w = make_workload(heads, len, fb, seed);
   const RowTriples trip(w.rows, w.cols, seed * 7 + 1);
@@ -291,6 +295,14 @@ int main(int argc, char** argv) {
   for (int i = 0; i < reps; i++) {
     yref = run_block(ref, ref, w, mref, trip, &ms);
     ref_ms = std::min(ref_ms, ms);
+  }
+  if (!dump.empty()) {
+    FILE* fp = std::fopen(dump.c_str(), "wb");
+    if (!fp || std::fwrite(w.t.data(), 8, w.t.size(), fp) != w.t.size() ||
+        std::fwrite(yref.data(), 8, yref.size(), fp) != yref.size() || std::fclose(fp) != 0) {
+      std::printf("{\"error\": \"cannot write %s\"}\n", dump.c_str());
+      return 1;
+    }
   }
 
   // the B200 engine behind the reference's GPU factory; with --switches=1 the

@@ -1,0 +1,53 @@
+// softmax_tables.cpp -- TEST INFRASTRUCTURE: dumps, as JSON, the SUF programs
+// the reference builds for the configs[4] softmax gates, so the device block
+// and the plaintext model of the block use the reference's own tables:
+//   nexp : gates::make_nexp_spec(NExpGateParams{f, 16}) (include/gates/
+//          nexp_gate.hpp:16, tables/nexp_piecewise_table.hpp) expanded by
+//          suf::build_silu_suf_from_piecewise, as dealer_make_nexp_task_material
+//          does (include/gates/nexp_composite.hpp:107-147);
+//   recip: gates::make_recip_affine_init_spec(f, 1024) (tables/
+//          recip_piecewise_affine_init.hpp:11) expanded the same way, as
+//          dealer_make_recip_task_material does (reciprocal_composite.hpp:55-105).
+// Built by oracle/Makefile (target `softmax`) into oracle/_ref/; run by
+// tests/golden/make_softmax_tables.py.  Usage: softmax_tables <frac_bits>.
+#include <cstdio>
+#include <cstdlib>
+
+#include "gates/nexp_composite.hpp"
+#include "gates/reciprocal_composite.hpp"
+
+namespace {
+
+void dump_suf(const char* name, const suf::SUF<uint64_t>& F, bool last) {
+  std::printf("  \"%s\": {\"n_bits\": %d, \"r_out\": %d, \"l_out\": %d, \"degree\": %d,\n", name, F.n_bits, F.r_out,
+              F.l_out, F.degree);
+  std::printf("    \"alpha\": [");
+  for (size_t i = 0; i < F.alpha.size(); i++) std::printf("%s\"%llu\"", i ? ", " : "", (unsigned long long)F.alpha[i]);
+  std::printf("],\n    \"pieces\": [");
+  for (size_t p = 0; p < F.pieces.size(); p++) {
+    std::printf("%s[", p ? ",\n      " : "\n      ");
+    const auto& polys = F.pieces[p].polys;
+    for (size_t j = 0; j < polys.size(); j++) {
+      std::printf("%s[", j ? ", " : "");
+      for (size_t k = 0; k < polys[j].coeffs.size(); k++)
+        std::printf("%s\"%llu\"", k ? ", " : "", (unsigned long long)polys[j].coeffs[k]);
+      std::printf("]");
+    }
+    std::printf("]");
+  }
+  std::printf("]}%s\n", last ? "" : ",");
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  const int f = argc > 1 ? std::atoi(argv[1]) : 12;
+  gates::NExpGateParams np{f, 16};
+  const auto nexp = suf::build_silu_suf_from_piecewise(gates::make_nexp_spec(np));
+  const auto recip = suf::build_silu_suf_from_piecewise(gates::make_recip_affine_init_spec(f, 1024.0));
+  std::printf("{\n  \"frac_bits\": %d,\n", f);
+  dump_suf("nexp", nexp, false);
+  dump_suf("recip", recip, true);
+  std::printf("}\n");
+  return 0;
+}
