@@ -387,6 +387,45 @@ int sufb200_beaver_matmul2d(int party, const uint64_t* d_D_open, const uint64_t*
                             int w_transposed, int has_scale, int64_t mul_const, int mul_shift, uint64_t* d_out,
                             void* stream);
 
+/* ---- configs[4] softmax block, device-resident --------------------------- */
+
+/* The six truncations of the block, in order: nExp T_f and T_2f, reciprocal
+ * init, Newton T_f(y s), Newton T_f(y d), probability T_f. */
+#define SUFB200_SOFTMAX_TRUNCS 6
+
+/* One party's dealer material for sufb200_softmax_block_pair.  Every triple
+ * array holds (a, b, c) words interleaved; the interval-LUT keys are device
+ * copies of broadcast IntervalKeyHeader blobs with 4 coefficient words per
+ * interval, built on the x^ = x + r_in domain of their gate. */
+typedef struct sufb200_softmax_party {
+  uint64_t nexp_rin, recip_rin;   /* this party's shares of the LUT gates' r_in */
+  const uint8_t* d_nexp_lut;      /* device */
+  size_t nexp_lut_bytes;
+  const uint8_t* d_recip_lut;     /* device */
+  size_t recip_lut_bytes;
+  const uint64_t* d_nexp_triples; /* device [3][n][3]: c3*t, u*t, q*t */
+  const uint64_t* d_recip_triples;/* device [3][rows][3]: a1*s, y*s, y*d */
+  const uint64_t* d_row_a;        /* device [n]   row-broadcast triple A */
+  const uint64_t* d_row_b;        /* device [rows] B */
+  const uint64_t* d_row_c;        /* device [n]   C = A * B[row] */
+  sufb200_trunc_desc trunc[SUFB200_SOFTMAX_TRUNCS];
+  uint64_t trunc_rin[SUFB200_SOFTMAX_TRUNCS];              /* shares of each truncation's r_in */
+  const uint8_t* trunc_keys[SUFB200_SOFTMAX_TRUNCS][4];    /* host: myl7 key of each query */
+  size_t trunc_key_bytes[SUFB200_SOFTMAX_TRUNCS][4];
+} sufb200_softmax_party;
+
+/* nn::SoftmaxBlockTask (include/nn/softmax_block_task.hpp) for BOTH parties
+ * on one GPU, every open computed on the device: nExp cubic gate
+ * (CubicPolyTask, include/runtime/phase_tasks.hpp:2670-3140), ragged row sums,
+ * reciprocal with one Newton step (RecipTask, :3140-3650), row-broadcast
+ * Beaver product and probability truncation.  t0/t1: the parties' shares of
+ * the packed active max-differences (Q frac_bits), n = row_off[rows];
+ * row_off: device [rows + 1].  prob0/prob1: shares of the packed
+ * probabilities.  Asynchronous on `stream`; 24 launches, no host sync. */
+int sufb200_softmax_block_pair(sufb200_ctx ctx, const sufb200_softmax_party* p0, const sufb200_softmax_party* p1,
+                               int rows, const int32_t* d_row_off, const uint64_t* d_t0, const uint64_t* d_t1,
+                               size_t n, int frac_bits, uint64_t* d_prob0, uint64_t* d_prob1, void* stream);
+
 /* ---- host utilities ----------------------------------------------------- */
 
 /* n successive draws of mt19937_64(seed) (the reference's mask / key RNG). */

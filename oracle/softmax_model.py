@@ -15,7 +15,7 @@ reconstruction does not depend on the masks):
 where T_k is the signed floor shift (the ARS / GapARS truncations) and
 LUT_g(x) the coefficient words of the SUF piece containing x (alpha[i] <=
 x < alpha[i+1]).  The tables are the reference's own SUF programs
-(tests/golden/softmax_tables_f12.json, from oracle/softmax_tables.cpp).
+(suf_b200/tables/softmax_suf_f12.json, from oracle/softmax_tables.cpp).
 """
 from __future__ import annotations
 
@@ -24,7 +24,7 @@ from pathlib import Path
 
 import numpy as np
 
-TABLES = Path(__file__).resolve().parents[1] / "tests" / "golden" / "softmax_tables_f12.json"
+TABLES = Path(__file__).resolve().parents[1] / "suf_b200" / "tables" / "softmax_suf_f12.json"
 
 
 def load_tables(path: Path = TABLES) -> dict:

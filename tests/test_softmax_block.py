@@ -1,0 +1,86 @@
+"""configs[4] softmax block on the device (sufb200_softmax_block_pair,
+suf_b200/softmax.py): the dealer's masked interval tables on the CPU, and on
+the GPU the reconstruction of both parties' outputs against the plaintext
+model pinned to the reference's SoftmaxBlockTask (oracle/softmax_model.py,
+tests/test_softmax_model.py) -- bit for bit -- and against the reference's
+own 64 x 64 reconstruction fixture."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle.softmax_model import softmax_block as model_block
+from suf_b200.softmax import load_tables, masked_lut_table
+
+GOLDEN = Path(__file__).parent / "golden"
+
+
+def _lut_search(cuts: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """The interval-LUT kernel's rule: the last cut <= x among cuts[0..iv-1],
+    clamped to interval 0."""
+    iv = len(cuts) - 1
+    return np.clip(np.searchsorted(cuts[:iv], x, side="right").astype(np.int64) - 1, 0, iv - 1)
+
+
+@pytest.mark.parametrize("gate", ["nexp", "recip"])
+def test_masked_table_returns_the_piece_of_x(gate):
+    alpha, coeffs = load_tables()[gate]
+    rng = np.random.default_rng(3)
+    for r_in in [0, 1, 2**64 - 1, 2**63, *[int(v) for v in rng.integers(0, 2**64, 20, dtype=np.uint64)]]:
+        cuts, rows = masked_lut_table(alpha, coeffs, r_in)
+        assert cuts[0] == 0 and (np.diff(cuts[:-1].astype(object)) > 0).all()
+        xs = np.concatenate([alpha[:-1], alpha[:-1] - np.uint64(1), rng.integers(0, 2**64, 2000, dtype=np.uint64),
+                             np.array([0, 2**64 - 1], dtype=np.uint64)])
+        with np.errstate(over="ignore"):
+            xh = xs + np.uint64(r_in)
+        got = rows[_lut_search(cuts, xh)]
+        piece = np.clip(np.searchsorted(alpha[:-1], xs, side="right").astype(np.int64) - 1, 0, len(coeffs) - 1)
+        assert (got == coeffs[piece]).all()
+
+
+def _shares(rng, v: np.ndarray):
+    s0 = rng.integers(0, 2**64, v.size, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        return s0, v - s0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("heads,length", [(1, 64), (12, 128), (2, 200)])
+def test_softmax_block_matches_model(ctx, torch_cuda, heads, length):
+    from suf_b200.softmax import SoftmaxBlock
+    from tests.conftest import from_dev, to_dev
+
+    rng = np.random.default_rng(heads * 1000 + length)
+    lens = np.arange(heads * length) % length + 1
+    off = np.concatenate([[0], np.cumsum(lens)])
+    t = rng.integers(0, 16 << 12, off[-1], dtype=np.uint64)
+    t[rng.random(t.size) < 0.05] = 0
+    t[rng.random(t.size) < 0.02] = 16 << 12
+    blk = SoftmaxBlock(ctx, lens, seed=heads + length)
+    t0, t1 = _shares(rng, t)
+    p0, p1 = blk.run(to_dev(torch_cuda, t0), to_dev(torch_cuda, t1))
+    ctx.sync()
+    with np.errstate(over="ignore"):
+        got = from_dev(p0, np.uint64) + from_dev(p1, np.uint64)
+    want = model_block(t, off, load_tables())
+    assert (got == want).all(), int((got != want).sum())
+
+
+@pytest.mark.gpu
+def test_softmax_block_matches_reference_fixture(ctx, torch_cuda):
+    """The reference's own SoftmaxBlockTask reconstruction (64 x 64 causal,
+    seed 4, its CPU backend) from the committed fixture."""
+    from suf_b200.softmax import SoftmaxBlock
+    from tests.conftest import from_dev, to_dev
+
+    g = np.load(GOLDEN / "softmax_ref_h1_l64.npz")
+    lens = np.arange(64) % 64 + 1
+    t = np.concatenate([g["t"].reshape(64, 64)[r, :lens[r]] for r in range(64)])
+    y = np.concatenate([g["y"].reshape(64, 64)[r, :lens[r]] for r in range(64)])
+    blk = SoftmaxBlock(ctx, lens, seed=9)
+    p0, p1 = blk.run(to_dev(torch_cuda, t), to_dev(torch_cuda, np.zeros_like(t)))
+    ctx.sync()
+    with np.errstate(over="ignore"):
+        assert ((from_dev(p0, np.uint64) + from_dev(p1, np.uint64)) == y).all()
