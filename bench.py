@@ -968,6 +968,171 @@ def cpu_silu_baseline(args, fx, xhat):
 
 
 # ---------------------------------------------------------------------------
+# the softmax block, device-resident, both parties on one GPU
+# ---------------------------------------------------------------------------
+
+SOFTMAX_HEADS, SOFTMAX_LEN = 12, 128
+SOFTMAX_METRIC = "softmax blocks/sec (configs[4]: 12 x 128 x 128 causal attention softmax, both parties)"
+# words each element's data moves through HBM in one block (reads + writes of
+# every stage's tensors, both parties; row-level tensors are negligible)
+SOFTMAX_WORDS_PER_ELEMENT = 70
+REF_SOFTMAX = ROOT / "oracle" / "_ref" / "ref_softmax_drive"
+
+
+def softmax_inputs(heads: int, length: int, frac_bits: int, seed: int = 4):
+    """Causal attention scores ~ N(0, 2^2) at f = 12 (seed 4): the packed
+    max-differences t = max - x clamped to [0, 16] (the SoftmaxBlockTask input),
+    the row lengths, and the double-precision softmax of the same scores."""
+    rng = np.random.default_rng(seed)
+    rows = heads * length
+    lens = np.arange(rows) % length + 1
+    x = np.round(rng.normal(0.0, 2.0, (rows, length)) * (1 << frac_bits)) / (1 << frac_bits)
+    ts, ref = [], []
+    for r in range(rows):
+        v = x[r, :lens[r]]
+        d = np.minimum(v.max() - v, 16.0)
+        ts.append(np.round(d * (1 << frac_bits)).astype(np.uint64))
+        e = np.exp(-d)
+        ref.append(e / e.sum())
+    return np.concatenate(ts), lens, np.concatenate(ref)
+
+
+def cpu_softmax_baseline(args):
+    """The reference's own nn::SoftmaxBlockTask on its CPU backend
+    (proto::ReferenceBackend), both parties on threads, driven by
+    oracle/_ref/ref_softmax_drive (built from the reference sources): ms per
+    block, best of the runs.  Without that build, the plaintext model of the
+    block (oracle/softmax_model.py, numpy) stands in as a port."""
+    if REF_SOFTMAX.exists():
+        r = subprocess.run([str(REF_SOFTMAX), f"--heads={SOFTMAX_HEADS}", f"--len={SOFTMAX_LEN}", "--reps=3",
+                            "--cpu-only"],
+                           capture_output=True, text=True, timeout=600)
+        line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+        if line:
+            j = json.loads(line[-1])
+            ms = float(j["ref_cpu_ms"])
+            return {"value": round(1e3 / ms, 3), "unit": "blocks/s", "cores": 2, "kind": "reference",
+                    "ms_per_block": round(ms, 3),
+                    "sample": "one configs[4] block, reference SoftmaxBlockTask on proto::ReferenceBackend, "
+                              "both parties on two threads, best of 3"}
+    from oracle.softmax_model import load_tables, softmax_block
+
+    t, lens, _ = softmax_inputs(SOFTMAX_HEADS, SOFTMAX_LEN, 12)
+    off = np.concatenate([[0], np.cumsum(lens)])
+    t0 = time.perf_counter()
+    softmax_block(t, off, load_tables())
+    ms = (time.perf_counter() - t0) * 1e3
+    return {"value": round(1e3 / ms, 3), "unit": "blocks/s", "cores": 1, "kind": "port", "ms_per_block": round(ms, 3),
+            "sample": "one configs[4] block, plaintext numpy model of the block (no shares)"}
+
+
+def run_softmax(args, ws, rank, local):
+    """One configs[4] softmax block per step on every GPU, both parties' shares
+    on the GPU (replicas: the block has no cross-GPU exchange when both
+    parties sit on one GPU)."""
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200.engine import Context
+    from suf_b200.softmax import SoftmaxBlock
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    ctx = Context(local)
+    ctx.prg_init(prg_state())
+    t, lens, ref = softmax_inputs(SOFTMAX_HEADS, SOFTMAX_LEN, 12)
+    n = t.size
+    blk = SoftmaxBlock(ctx, lens, seed=11 + rank)
+    rng = np.random.default_rng(5 + rank)
+    t0 = rng.integers(0, 2**63, n, dtype=np.uint64) * np.uint64(2)
+    with np.errstate(over="ignore"):
+        t1 = t - t0
+    d_t = [torch.from_numpy(v.view(np.int64)).to(dev) for v in (t0, t1)]
+    d_p = [torch.empty(n, dtype=torch.int64, device=dev) for _ in range(2)]
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+
+    def step():
+        blk.run(d_t[0], d_t[1], d_p[0], d_p[1], stream=stream)
+
+    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    ctx.sync()
+    with np.errstate(over="ignore"):
+        prob = (d_p[0].cpu().numpy().view(np.uint64) + d_p[1].cpu().numpy().view(np.uint64)).view(np.int64)
+    err = float(np.abs(prob / 4096.0 - ref).max())
+
+    # e2e: pinned host shares of t in, both parties' probability shares out
+    t_pin = [torch.from_numpy(v.view(np.int64)).pin_memory() for v in (t0, t1)]
+    p_pin = [torch.empty(n, dtype=torch.int64).pin_memory() for _ in range(2)]
+
+    def e2e_step():
+        d0, d1 = (v.to(dev, non_blocking=True) for v in t_pin)
+        p0, p1 = blk.run(d0, d1)
+        p_pin[0].copy_(p0, non_blocking=True)
+        p_pin[1].copy_(p1, non_blocking=True)
+        torch.cuda.synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    e2e = []
+    for _ in range(max(args.steps, 5)):
+        h0 = time.perf_counter()
+        e2e_step()
+        e2e.append((time.perf_counter() - h0) * 1e3)
+    e2e_ms = _max_over_ranks(ws, dev, sum(e2e) / len(e2e))
+
+    peaks = measured_peaks()
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    traffic = SOFTMAX_WORDS_PER_ELEMENT * 8 * n
+    gbs = traffic / (ms / 1e3) / 1e9
+    out = None
+    if rank == 0:
+        out = {"metric": SOFTMAX_METRIC, "value": round(ws / (ms / 1e3), 3), "unit": "blocks/s", "n_gpus": ws,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128",
+               "data": "synthetic causal scores ~ N(0, 4) at f = 12 (seed 4); gate tables from the reference",
+               "config": {"workload": "configs[4]: softmax block, 12 heads x 128 x 128 causal, f = 12, seed 4",
+                          "rows": int(lens.size), "active_elements": int(n), "parties_per_gpu": 2,
+                          "l2": "256 MB flush between steps", "parallelism": f"one block per GPU, {ws} GPU(s)"},
+               "e2e": {"value": round(ws / (e2e_ms / 1e3), 3), "unit": "blocks/s", "h2d_bytes_per_step": 2 * n * 8,
+                       "d2h_bytes_per_step": 2 * n * 8, "ms_per_step": round(e2e_ms, 4),
+                       "path": "sufb200_softmax_block_pair, pinned t shares in, probability shares out"},
+               "roofline": {"bound": "hbm", "unit": "GB/s", "achieved": round(gbs, 1), "peak": hbm_peak,
+                            "frac": round(gbs / hbm_peak, 4), "traffic": traffic,
+                            "per_block_us": round(ms * 1e3, 1),
+                            "note": "bytes = every stage's tensors read and written once (70 words per active "
+                                    "element); the block is a chain of 36 small launches, bound by their latency"},
+               "cpu_baseline": cpu_softmax_baseline(args) if (ws == 1 and not args.no_cpu) else None,
+               "clocks": clk.summary(), "gpu_launches": 36 * args.steps,
+               "max_err_vs_double_softmax": round(err, 6), "reconstruction_ok": err < 0.03,
+               "ms_per_step_all": [round(v, 4) for v in ms_steps]}
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return out
+
+
+def run_softmax_reference(args, ws, rank):
+    if rank != 0:
+        return None
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_softmax_baseline(args)
+    runs = [cpu_softmax_baseline(args) for _ in range(args.steps)]
+    ms = min(r["ms_per_block"] for r in runs)
+    v = round(1e3 / ms, 3)
+    return {"metric": SOFTMAX_METRIC, "value": v, "unit": "blocks/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64 (Z_2^64)", "data": "synthetic causal scores ~ N(0, 4) at f = 12",
+            "impl": "reference",
+            "config": {"workload": "configs[4]: softmax block, 12 heads x 128 x 128 causal, f = 12, seed 4"},
+            "cpu_baseline": dict(runs[0], value=v, ms_per_block=round(ms, 3)),
+            "e2e": {"value": v, "unit": "blocks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ---------------------------------------------------------------------------
 # configs[4]: one layer's Beaver matmuls on the tensor cores
 # ---------------------------------------------------------------------------
 
@@ -1073,9 +1238,10 @@ def main():
     ap.add_argument("--n-elem", type=int, default=None,
                     help="elements per party at N=1 (default: the workload's config size; smaller only for "
                          "profiling)")
-    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open", "silu", "matmul"],
+    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open", "silu", "matmul", "softmax"],
                     help="trunc: configs[1] (the headline line); compare: configs[0], per-element keys; "
-                         "open: the paired-GPU open of a configs[4] layer (N >= 2)")
+                         "open: the paired-GPU open of a configs[4] layer (N >= 2); softmax: the configs[4] "
+                         "softmax block")
     ap.add_argument("--ring-bits", type=int, default=37, help="ring of the open workload (37: the reference's "
                                                                  "measured bert-base ring)")
     args = ap.parse_args()
@@ -1090,6 +1256,8 @@ def main():
                 "unavailable": "the reference's Beaver matmul is a CUDA kernel; its CUDA-core equivalent is timed "
                                "beside ours in the ours line (cuda_core)"}
                if rank == 0 else None) if args.impl == "reference" else run_matmul(args, ws, rank, local)
+    elif args.workload == "softmax":
+        out = run_softmax_reference(args, ws, rank) if args.impl == "reference" else run_softmax(args, ws, rank, local)
     elif args.workload == "silu":
         out = run_silu_reference(args, ws, rank) if args.impl == "reference" else run_silu(args, ws, rank, local)
     elif args.workload == "compare":

@@ -162,6 +162,15 @@ int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, c
                               const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y,
                               uint64_t* d_bools, void* stream);
 
+/* Both parties' bundles over the same public x^ on one GPU (desc0 / keys0 of
+ * party 0, desc1 / keys1 of party 1): batches below the shared-prefix size
+ * run in ONE launch with one lane per (party, element, query); larger ones
+ * run sufb200_trunc_bundle_eval per party.  d_y0 / d_y1 are [n]. */
+int sufb200_trunc_bundle_eval_pair(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* keys0,
+                                   const size_t* key_bytes0, const sufb200_trunc_desc* desc1,
+                                   const uint8_t* const* keys1, const size_t* key_bytes1, const uint64_t* d_xhat,
+                                   size_t n, uint64_t* d_y0, uint64_t* d_y1, void* stream);
+
 /* Host-buffer form: xhat, y (and bools, may be NULL) in host memory; copies
  * in and out inside the call and returns when y is on the host.  Replaces
  * composite_eval_batch_backend with a host CompositeBatchInput::hatx

@@ -271,6 +271,7 @@ int main(int argc, char** argv) {
   int heads = 12, len = 128, fb = 12, reps = 3, switches = 1;
   uint64_t seed = 4;
   std::string dump;  // --dump=PATH: t[rows*cols] then the CPU reconstruction, little-endian u64
+  bool cpu_only = false;  // --cpu-only: the reference CPU leg alone (the B200 engine is not touched)
   for (int i = 1; i < argc; i++) {
     const std::string a(argv[i]);
     auto val = [&](const char* k) { return a.substr(std::strlen(k)); };
@@ -281,6 +282,7 @@ int main(int argc, char** argv) {
     else if (a.rfind("--seed=", 0) == 0) seed = std::stoull(val("--seed="));
     else if (a.rfind("--switches=", 0) == 0) switches = std::stoi(val("--switches="));
     else if (a.rfind("--dump=", 0) == 0) dump = val("--dump=");
+    else if (a == "--cpu-only") cpu_only = true;
   }
   const Workload w = make_workload(heads, len, fb, seed);
   const RowTriples trip(w.rows, w.cols, seed * 7 + 1);
@@ -312,6 +314,12 @@ int main(int argc, char** argv) {
     for (const char* k : {"SUF_PFSS_CACHE_KEYS", "SUF_PFSS_CACHE_HATX", "SUF_TRUNC_GPU", "SUF_MUL_GPU",
                           "SUF_RECIP_GPU_KERNELS", "SUF_HORNER_GPU"})
       setenv(k, "1", 0);
+  if (cpu_only) {
+    std::printf("{\"workload\": \"configs[4] softmax block\", \"rows\": %d, \"cols\": %d, \"active\": %zu, "
+                "\"ref_cpu_ms\": %.3f, \"ref_max_err_vs_double\": %.6f}\n",
+                w.rows, w.cols, active, ref_ms, active_max_err(w, yref));
+    return 0;
+  }
   std::unique_ptr<proto::PfssBackendBatch> g0, g1;
   try {
     g0 = proto::make_real_gpu_backend();

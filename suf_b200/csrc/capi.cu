@@ -431,10 +431,8 @@ int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, c
 
 namespace {
 
-int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
-                      const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y, uint64_t* d_bools,
-                      void* stream, const ChunkSink* sink) {
-  if (int rc = check_ctx(ctx, true)) return rc;
+// Descriptor checks of one bundle.
+int check_bundle_desc(const sufb200_trunc_desc* desc, const uint8_t* const* keys, const size_t* key_bytes) {
   if (!desc || !keys || !key_bytes) return fail(SUFB200_ERR_INVALID, "null pointer");
   if (desc->nq < 0 || desc->nq > 4) return fail(SUFB200_ERR_UNSUPPORTED, "bundle has more than 4 queries");
   if (desc->kind < 0 || desc->kind > 2 || desc->party < 0 || desc->party > 1)
@@ -445,26 +443,42 @@ int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uin
     if (v >= desc->nq) return fail(SUFB200_ERR_INVALID, "query index out of range");
   if ((desc->carry_a >= 0) != (desc->carry_b >= 0) || (desc->sign_a >= 0) != (desc->sign_b >= 0))
     return fail(SUFB200_ERR_INVALID, "rotation operands must come in pairs");
-  if (n == 0) return SUFB200_OK;
-  if (!d_xhat || !d_y || !aligned8(d_xhat) || !aligned8(d_y) || (d_bools && !aligned8(d_bools)))
-    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
-  std::vector<uint8_t> blob;
-  sufb200::TruncLaunch a{};
-  a.desc = *desc;
-  for (int q = 0; q < desc->nq; q++) {
-    const int nb = desc->q_bits[q];
+  return SUFB200_OK;
+}
+
+// Header checks of the bundle's query keys, appended to `blob` 16-byte
+// aligned; key_off[q] receives each key's offset in the blob.
+int pack_bundle_keys(const sufb200_trunc_desc& desc, const uint8_t* const* keys, const size_t* key_bytes,
+                     std::vector<uint8_t>& blob, uint32_t key_off[4]) {
+  for (int q = 0; q < desc.nq; q++) {
+    const int nb = desc.q_bits[q];
     if (nb < 1 || nb > 64) return fail(SUFB200_ERR_INVALID, "query in_bits out of range");
     if (!keys[q] || key_bytes[q] != sufb200::host::myl7_key_bytes(nb, 8))
       return fail(SUFB200_ERR_KEY, "query " + std::to_string(q) + ": key size does not match an 8-byte myl7 key");
     const uint8_t* k = keys[q];
     uint32_t pl;
     std::memcpy(&pl, k + 4, 4);
-    if (k[0] != nb || k[1] != 1 || k[2] != desc->party || pl != 8)
+    if (k[0] != nb || k[1] != 1 || k[2] != desc.party || pl != 8)
       return fail(SUFB200_ERR_KEY, "query " + std::to_string(q) + ": key header does not match the bundle");
-    a.key_off[q] = static_cast<uint32_t>(blob.size());
+    key_off[q] = static_cast<uint32_t>(blob.size());
     blob.insert(blob.end(), k, k + key_bytes[q]);
     while (blob.size() % 16) blob.push_back(0);
   }
+  return SUFB200_OK;
+}
+
+int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                      const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y, uint64_t* d_bools,
+                      void* stream, const ChunkSink* sink) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (int rc = check_bundle_desc(desc, keys, key_bytes)) return rc;
+  if (n == 0) return SUFB200_OK;
+  if (!d_xhat || !d_y || !aligned8(d_xhat) || !aligned8(d_y) || (d_bools && !aligned8(d_bools)))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  std::vector<uint8_t> blob;
+  sufb200::TruncLaunch a{};
+  a.desc = *desc;
+  if (int rc = pack_bundle_keys(*desc, keys, key_bytes, blob, a.key_off)) return rc;
   cudaStream_t st = as_stream(stream);
   const bool prefix = n >= prefix_min_n() && desc->nq > 0;
   const uint32_t kmax = sufb200::prefix_budget(n);
@@ -528,6 +542,49 @@ int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uin
 }
 
 }  // namespace
+
+int sufb200_trunc_bundle_eval_pair(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* keys0,
+                                   const size_t* key_bytes0, const sufb200_trunc_desc* desc1,
+                                   const uint8_t* const* keys1, const size_t* key_bytes1, const uint64_t* d_xhat,
+                                   size_t n, uint64_t* d_y0, uint64_t* d_y1, void* stream) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (int rc = check_bundle_desc(desc0, keys0, key_bytes0)) return rc;
+  if (int rc = check_bundle_desc(desc1, keys1, key_bytes1)) return rc;
+  if (desc0->party != 0 || desc1->party != 1) return fail(SUFB200_ERR_INVALID, "desc0 / desc1 must be parties 0 / 1");
+  if (n == 0) return SUFB200_OK;
+  if (n >= prefix_min_n()) {  // large batches: each party's bundle on the shared-prefix path
+    if (int rc = trunc_bundle_impl(ctx, desc0, keys0, key_bytes0, d_xhat, n, d_y0, nullptr, stream, nullptr))
+      return rc;
+    return trunc_bundle_impl(ctx, desc1, keys1, key_bytes1, d_xhat, n, d_y1, nullptr, stream, nullptr);
+  }
+  if (!d_xhat || !d_y0 || !d_y1 || !aligned8(d_xhat) || !aligned8(d_y0) || !aligned8(d_y1))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  std::vector<uint8_t> blob;
+  sufb200::TruncLaunch a0{}, a1{};
+  a0.desc = *desc0;
+  a1.desc = *desc1;
+  if (int rc = pack_bundle_keys(*desc0, keys0, key_bytes0, blob, a0.key_off)) return rc;
+  if (int rc = pack_bundle_keys(*desc1, keys1, key_bytes1, blob, a1.key_off)) return rc;
+  cudaStream_t st = as_stream(stream);
+  uint8_t* scratch = nullptr;
+  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), blob.size() + 256, ctx->pool, st),
+                     "pair bundle scratch allocation");
+  cudaError_t e = cudaMemcpyAsync(scratch, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
+  for (sufb200::TruncLaunch* a : {&a0, &a1}) {
+    a->keys = scratch;
+    a->xhat = d_xhat;
+    a->n = n;
+    a->bools = nullptr;
+    a->t0 = ctx->d_t0;
+    a->status = ctx->d_status;
+  }
+  a0.y = d_y0;
+  a1.y = d_y1;
+  if (e == cudaSuccess) e = sufb200::launch_trunc_bundle_pair(ctx, a0, a1, st);
+  cudaFreeAsync(scratch, st);
+  if (e != cudaSuccess) return cuda_fail(e, "pair bundle launch");
+  return SUFB200_OK;
+}
 
 int sufb200_trunc_bundle_eval_host(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
                                    const size_t* key_bytes, const uint64_t* xhat, size_t n, uint64_t* y,

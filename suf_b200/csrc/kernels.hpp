@@ -40,6 +40,10 @@ struct TruncLaunch {
   uint32_t* status;
 };
 cudaError_t launch_trunc_bundle(const sufb200_ctx_s* ctx, const TruncLaunch& a, cudaStream_t st);
+// Both parties' bundles over the same x^ (a0.xhat == a1.xhat, a0.n == a1.n),
+// one lane per (party, element, query): for batches too small to fill the GPU.
+cudaError_t launch_trunc_bundle_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
+                                     cudaStream_t st);
 
 // Reference GPU-backend key formats (ref_formats.cu).
 struct RefFmtLaunch {

@@ -20,7 +20,9 @@
 // bundle takes as its public input.  Each party's truncation bundle and LUT
 // evaluation runs on its own shares and keys, as it would on its own GPU.
 //
-// 8 fused kernels + 4 LUT launches + 12 truncation bundles per block.
+// 8 fused kernels, 4 LUT launches and 6 truncation stages per block: the
+// element-level stages run each party's bundle on the shared-prefix path, the
+// row-level ones both parties in one query-parallel launch.
 #include <string>
 
 #include "kernels.hpp"
@@ -198,11 +200,11 @@ int launch_rc(const char* what) {
                           : sufb200::record_error(SUFB200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-// One party's truncation bundle k over x^ (n words) into out.
-int trunc(sufb200_ctx ctx, const sufb200_softmax_party* p, int k, const uint64_t* xhat, size_t n, uint64_t* out,
-          cudaStream_t st) {
-  return sufb200_trunc_bundle_eval(ctx, &p->trunc[k], p->trunc_keys[k], p->trunc_key_bytes[k], xhat, n, out,
-                                   nullptr, st);
+// Both parties' truncation bundle k over x^ (n words) into out0 / out1.
+int trunc2(sufb200_ctx ctx, const sufb200_softmax_party* p0, const sufb200_softmax_party* p1, int k,
+           const uint64_t* xhat, size_t n, uint64_t* out0, uint64_t* out1, cudaStream_t st) {
+  return sufb200_trunc_bundle_eval_pair(ctx, &p0->trunc[k], p0->trunc_keys[k], p0->trunc_key_bytes[k], &p1->trunc[k],
+                                        p1->trunc_keys[k], p1->trunc_key_bytes[k], xhat, n, out0, out1, st);
 }
 
 }  // namespace
@@ -254,13 +256,13 @@ extern "C" int sufb200_softmax_block_pair(sufb200_ctx ctx, const sufb200_softmax
                                                p0->trunc_rin[0] + p1->trunc_rin[0], xh, n);
     run(launch_rc("softmax nExp Mul1/Mul2"));
   }
-  if (run(rc) && run(trunc(ctx, p0, 0, xh, n, p20, st))) run(trunc(ctx, p1, 0, xh, n, p21, st));
+  if (run(rc)) run(trunc2(ctx, p0, p1, 0, xh, n, p20, p21, st));
   if (rc == SUFB200_OK) {
     nexp_mul3_kernel<<<ge, kThreads, 0, st>>>(lut0, lut1, p20, p21, d_t0, d_t1, p0->d_nexp_triples,
                                               p1->d_nexp_triples, f, p0->trunc_rin[1] + p1->trunc_rin[1], xh, n);
     run(launch_rc("softmax nExp Mul3"));
   }
-  if (run(rc) && run(trunc(ctx, p0, 1, xh, n, y0, st))) run(trunc(ctx, p1, 1, xh, n, y1, st));
+  if (run(rc)) run(trunc2(ctx, p0, p1, 1, xh, n, y0, y1, st));
 
   // row sums and the reciprocal (one Newton step) on the rows
   if (rc == SUFB200_OK) {
@@ -275,19 +277,19 @@ extern "C" int sufb200_softmax_block_pair(sufb200_ctx ctx, const sufb200_softmax
                                                p0->trunc_rin[2] + p1->trunc_rin[2], xr, rows);
     run(launch_rc("softmax reciprocal init"));
   }
-  if (run(rc) && run(trunc(ctx, p0, 2, xr, R, z0, st))) run(trunc(ctx, p1, 2, xr, R, z1, st));
+  if (run(rc)) run(trunc2(ctx, p0, p1, 2, xr, R, z0, z1, st));
   if (rc == SUFB200_OK) {
     recip_nr1_kernel<<<gr, kThreads, 0, st>>>(z0, z1, lr0, lr1, s0, s1, p0->d_recip_triples, p1->d_recip_triples,
                                               p0->trunc_rin[3] + p1->trunc_rin[3], yr0, yr1, xr, rows);
     run(launch_rc("softmax Newton y*s"));
   }
-  if (run(rc) && run(trunc(ctx, p0, 3, xr, R, g0, st))) run(trunc(ctx, p1, 3, xr, R, g1, st));
+  if (run(rc)) run(trunc2(ctx, p0, p1, 3, xr, R, g0, g1, st));
   if (rc == SUFB200_OK) {
     recip_nr2_kernel<<<gr, kThreads, 0, st>>>(yr0, yr1, g0, g1, f, p0->d_recip_triples, p1->d_recip_triples,
                                               p0->trunc_rin[4] + p1->trunc_rin[4], xr, rows);
     run(launch_rc("softmax Newton y*d"));
   }
-  if (run(rc) && run(trunc(ctx, p0, 4, xr, R, v0, st))) run(trunc(ctx, p1, 4, xr, R, v1, st));
+  if (run(rc)) run(trunc2(ctx, p0, p1, 4, xr, R, v0, v1, st));
 
   // probabilities: row-broadcast product and its truncation
   if (rc == SUFB200_OK) {
@@ -296,7 +298,7 @@ extern "C" int sufb200_softmax_block_pair(sufb200_ctx ctx, const sufb200_softmax
                                                    p0->trunc_rin[5] + p1->trunc_rin[5], xh);
     run(launch_rc("softmax row-broadcast product"));
   }
-  if (run(rc) && run(trunc(ctx, p0, 5, xh, n, d_prob0, st))) run(trunc(ctx, p1, 5, xh, n, d_prob1, st));
+  if (run(rc)) run(trunc2(ctx, p0, p1, 5, xh, n, d_prob0, d_prob1, st));
   cudaFreeAsync(w, st);
   return rc;
 }

@@ -24,7 +24,7 @@ struct QueryKeySmem {
   uint32_t ok;
   uint32_t pad;
 };
-static_assert(4 * sizeof(QueryKeySmem) < kTabBase - 4096, "staging must fit below the tables");
+static_assert(8 * sizeof(QueryKeySmem) < kTabBase - 4096, "staging (two bundles) must fit below the tables");
 
 __device__ __forceinline__ uint32_t ldb32(const uint8_t* p) {
   return static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8) | (static_cast<uint32_t>(p[2]) << 16) |
@@ -85,9 +85,8 @@ __device__ __forceinline__ void combine_store(const sufb200_trunc_desc& d, uint6
   }
 }
 
-// Stage every query key of the bundle into shared memory, fill the AES
-// tables; false (status flagged) when a key header does not match.
-__device__ __forceinline__ bool stage_bundle(QueryKeySmem* ks, const TruncLaunch& a) {
+// Copy every query key of the bundle into shared memory (no barrier).
+__device__ __forceinline__ void stage_keys(QueryKeySmem* ks, const TruncLaunch& a) {
   const sufb200_trunc_desc& d = a.desc;
   for (int q = 0; q < d.nq; q++) {
     const uint8_t* k = a.keys + a.key_off[q];
@@ -107,15 +106,26 @@ __device__ __forceinline__ bool stage_bundle(QueryKeySmem* ks, const TruncLaunch
       ks[q].ok = ok ? 1u : 0u;
     }
   }
-  aes_fill_tables(a.t0);
-  __syncthreads();
-  for (int q = 0; q < d.nq; q++) {
+}
+
+// After the barrier: false (status flagged) when a key header did not match.
+__device__ __forceinline__ bool keys_ok(const QueryKeySmem* ks, const TruncLaunch& a) {
+  for (int q = 0; q < a.desc.nq; q++) {
     if (!ks[q].ok) {
       if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.status, kStatusBadKeyHeader);
       return false;
     }
   }
   return true;
+}
+
+// Stage every query key of the bundle into shared memory, fill the AES
+// tables; false (status flagged) when a key header does not match.
+__device__ __forceinline__ bool stage_bundle(QueryKeySmem* ks, const TruncLaunch& a) {
+  stage_keys(ks, a);
+  aes_fill_tables(a.t0);
+  __syncthreads();
+  return keys_ok(ks, a);
 }
 
 // Walk levels [from, n) of one query from state (s, t, v); returns the share.
@@ -173,6 +183,54 @@ __global__ void __launch_bounds__(kAesThreads, 1) trunc_bundle_kernel(const PrgP
   }
 }
 
+
+// Small batches of both parties' bundles over one x^: one lane per (party,
+// element, query), four lanes per element, so the queries of an element run
+// side by side instead of one after another and both parties fill one
+// launch; lane 0 of each quad gathers the quad's shares and folds the plan
+// and the postproc.  For batches too small to fill the GPU with one lane per
+// element (the row-level truncations of a softmax block).
+__global__ void __launch_bounds__(kAesThreads, 1)
+    trunc_bundle_pair_kernel(const PrgParams prg, const __grid_constant__ TruncLaunch a0,
+                             const __grid_constant__ TruncLaunch a1) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
+    return;
+  }
+  QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);  // party p, query q at ks[4 p + q]
+  stage_keys(ks, a0);
+  stage_keys(ks + 4, a1);
+  aes_fill_tables(a0.t0);
+  __syncthreads();
+  if (!keys_ok(ks, a0) || !keys_ok(ks + 4, a1)) return;
+  const uint32_t lb = lane_base();
+  const size_t n = a0.n, units = 8 * n;  // 2 parties x n elements x 4 lanes
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const int lane = static_cast<int>(threadIdx.x & 31u), quad = lane & ~3;
+  for (size_t g0 = static_cast<size_t>(blockIdx.x) * blockDim.x; g0 < units; g0 += stride) {
+    const size_t g = g0 + threadIdx.x;  // g0 is uniform across the block: every lane reaches the shuffles
+    const bool valid = g < units;
+    const size_t j = g >> 2;
+    const int q = static_cast<int>(g & 3u);
+    const uint32_t party = j >= n ? 1u : 0u;
+    const size_t i = party ? j - n : j;
+    const TruncLaunch* a = party ? &a1 : &a0;
+    const sufb200_trunc_desc& d = a->desc;
+    const uint64_t xh = valid ? a->xhat[i] : 0ull;
+    uint64_t v = 0;
+    if (valid && q < d.nq) {
+      const int nb = d.q_bits[q];
+      const uint64_t x = nb >= 64 ? xh : (xh & ((1ull << nb) - 1ull));
+      const QueryKeySmem& K = ks[4 * party + q];
+      v = walk_query(prg, lb, K, nb, x, party, seed_blk(K), party, 0, 0);
+    }
+    uint64_t pr[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) pr[k] = __shfl_sync(0xffffffffu, v, quad + k);
+    if (valid && q == 0) combine_store(d, xh, pr, a->y, a->bools, i);
+  }
+}
 
 // Large batches: every query resumes from its frontier entry (prefix.cuh).
 struct FrontierSet {
@@ -259,6 +317,18 @@ cudaError_t launch_trunc_bundle(const sufb200_ctx_s* ctx, const TruncLaunch& a, 
   const size_t want = (a.n + kAesThreads - 1) / kAesThreads;
   const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
   trunc_bundle_kernel<<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_trunc_bundle_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
+                                     cudaStream_t st) {
+  if (a0.n != a1.n || a0.xhat != a1.xhat) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(trunc_bundle_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  const size_t want = (8 * a0.n + kAesThreads - 1) / kAesThreads;
+  const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
+  trunc_bundle_pair_kernel<<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a0, a1);
   return cudaGetLastError();
 }
 

@@ -138,3 +138,33 @@ def test_host_entry_chunked_matches_device_entry(ctx, torch_cuda, oracle, prg_st
     assert ((ys[0] + ys[1]) == (x.view(np.int64) >> 12).view(np.uint64)).all()
     idx = rng.integers(0, n, 128)
     assert (ys[1][idx] == oracle_trunc_eval(oracle, descs[1], keys[1], xhat[idx])).all()
+
+
+@pytest.mark.parametrize("kind", [KIND_TR, KIND_ARS, KIND_GAPARS])
+@pytest.mark.parametrize("n", [1, 7, 1536, 20_000])
+def test_pair_entry_matches_per_party_entry(ctx, torch_cuda, oracle, prg_state, kind, n):
+    """sufb200_trunc_bundle_eval_pair (one query-parallel launch for both
+    parties below the shared-prefix size, the per-party path above it) gives
+    each party exactly the oracle's shares."""
+    import ctypes as C
+
+    from suf_b200 import _lib
+
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(900 + kind + n)
+    x = signed_fixed(rng, n, 40)
+    r_in, descs, keys = trunc_material(oracle, kind, 12, 17 + n)
+    xhat = x + np.uint64(r_in)
+    dx = to_dev(torch_cuda, xhat)
+    out = [torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda") for _ in (0, 1)]
+    pd = [to_product_desc(descs[p]) for p in (0, 1)]
+    karr = [[np.ascontiguousarray(k, dtype=np.uint8) for k in keys[p]] for p in (0, 1)]
+    ptrs = [(C.c_void_p * 4)(*[k.ctypes.data for k in karr[p]], *([None] * (4 - len(karr[p])))) for p in (0, 1)]
+    sizes = [(C.c_size_t * 4)(*[k.size for k in karr[p]], *([0] * (4 - len(karr[p])))) for p in (0, 1)]
+    _lib.check(_lib.lib().sufb200_trunc_bundle_eval_pair(
+        ctx.h, C.byref(pd[0]), C.cast(ptrs[0], C.c_void_p), C.cast(sizes[0], C.c_void_p), C.byref(pd[1]),
+        C.cast(ptrs[1], C.c_void_p), C.cast(sizes[1], C.c_void_p), dx.data_ptr(), n, out[0].data_ptr(),
+        out[1].data_ptr(), None))
+    ctx.sync()
+    for p in (0, 1):
+        assert (from_dev(out[p]) == oracle_trunc_eval(oracle, descs[p], keys[p], xhat)).all(), p
