@@ -1115,6 +1115,148 @@ def run_softmax(args, ws, rank, local):
     return out
 
 
+LN_ROWS, LN_COLS = 128, 768
+LN_METRIC = "layernorm blocks/sec (configs[4]: 128 x 768 LayerNorm, one Newton rsqrt step, both parties)"
+# words per element through HBM: x (2 r), d (2 w + 2 r), squares' triples (6 r),
+# x^ (1 w + 1 r per stage, 2 stages), row-broadcast triples (4 r), output (2 w)
+LN_WORDS_PER_ELEMENT = 22
+
+
+def ln_inputs(rows: int, cols: int, frac_bits: int, seed: int = 4):
+    rng = np.random.default_rng(seed)
+    return np.round(rng.normal(0.0, 1.0, rows * cols) * (1 << frac_bits)).astype(np.int64).view(np.uint64)
+
+
+def cpu_layernorm_baseline(args):
+    """The reference's own runtime::LayerNormTask on its CPU backend
+    (proto::ReferenceBackend, which by default reconstructs x and computes the
+    LayerNorm in plaintext), both parties on threads, via
+    oracle/_ref/ref_softmax_drive --block=ln.  Without that build the numpy
+    model of the block stands in as a port."""
+    if REF_SOFTMAX.exists():
+        r = subprocess.run([str(REF_SOFTMAX), "--block=ln", f"--rows={LN_ROWS}", f"--cols={LN_COLS}", "--reps=3",
+                            "--cpu-only"], capture_output=True, text=True, timeout=600)
+        line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+        if line:
+            ms = float(json.loads(line[-1])["ref_cpu_ms"])
+            return {"value": round(1e3 / ms, 3), "unit": "blocks/s", "cores": 2, "kind": "reference",
+                    "ms_per_block": round(ms, 3),
+                    "sample": "one configs[4] LayerNorm block, reference LayerNormTask on proto::ReferenceBackend, "
+                              "both parties on two threads, best of 3"}
+    from oracle.softmax_model import layernorm_block, load_tables
+
+    x = ln_inputs(LN_ROWS, LN_COLS, 12)
+    t0 = time.perf_counter()
+    layernorm_block(x, LN_ROWS, LN_COLS, load_tables())
+    ms = (time.perf_counter() - t0) * 1e3
+    return {"value": round(1e3 / ms, 3), "unit": "blocks/s", "cores": 1, "kind": "port", "ms_per_block": round(ms, 3),
+            "sample": "one configs[4] LayerNorm block, plaintext numpy model (no shares)"}
+
+
+def run_layernorm(args, ws, rank, local):
+    """One configs[4] LayerNorm block per step on every GPU, both parties'
+    shares on the GPU (replicas, as for the softmax block)."""
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200.engine import Context
+    from suf_b200.softmax import LayerNormBlock
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    ctx = Context(local)
+    ctx.prg_init(prg_state())
+    x = ln_inputs(LN_ROWS, LN_COLS, 12)
+    n = x.size
+    blk = LayerNormBlock(ctx, LN_ROWS, LN_COLS, seed=21 + rank)
+    rng = np.random.default_rng(6 + rank)
+    x0 = rng.integers(0, 2**63, n, dtype=np.uint64) * np.uint64(2)
+    with np.errstate(over="ignore"):
+        x1 = x - x0
+    d_x = [torch.from_numpy(v.view(np.int64)).to(dev) for v in (x0, x1)]
+    d_o = [torch.empty(n, dtype=torch.int64, device=dev) for _ in range(2)]
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+
+    def step():
+        blk.run(d_x[0], d_x[1], d_o[0], d_o[1], stream=stream)
+
+    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    ctx.sync()
+    with np.errstate(over="ignore"):
+        out = (d_o[0].cpu().numpy().view(np.uint64) + d_o[1].cpu().numpy().view(np.uint64)).view(np.int64)
+    inv = round(4096 / LN_COLS) / 4096.0
+    xr = x.view(np.int64).reshape(LN_ROWS, LN_COLS) / 4096.0
+    mu = xr.sum(1, keepdims=True) * inv
+    ref = (xr - mu) / np.sqrt(((xr - mu) ** 2).sum(1, keepdims=True) * inv + 1 / 1024)
+    err = float(np.abs(out.reshape(LN_ROWS, LN_COLS) / 4096.0 - ref).max())
+
+    x_pin = [torch.from_numpy(v.view(np.int64)).pin_memory() for v in (x0, x1)]
+    o_pin = [torch.empty(n, dtype=torch.int64).pin_memory() for _ in range(2)]
+
+    def e2e_step():
+        a, b = (v.to(dev, non_blocking=True) for v in x_pin)
+        o0, o1 = blk.run(a, b)
+        o_pin[0].copy_(o0, non_blocking=True)
+        o_pin[1].copy_(o1, non_blocking=True)
+        torch.cuda.synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    e2e = []
+    for _ in range(max(args.steps, 5)):
+        h0 = time.perf_counter()
+        e2e_step()
+        e2e.append((time.perf_counter() - h0) * 1e3)
+    e2e_ms = _max_over_ranks(ws, dev, sum(e2e) / len(e2e))
+
+    hbm_peak = measured_peaks().get("hbm_gbs", 6650.0)
+    traffic = LN_WORDS_PER_ELEMENT * 8 * n
+    gbs = traffic / (ms / 1e3) / 1e9
+    res = None
+    if rank == 0:
+        res = {"metric": LN_METRIC, "value": round(ws / (ms / 1e3), 3), "unit": "blocks/s", "n_gpus": ws,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128",
+               "data": "synthetic x ~ N(0, 1) at f = 12 (seed 4); rsqrt table from the reference",
+               "config": {"workload": "configs[4]: LayerNorm block, 128 x 768, f = 12, eps 1/1024, seed 4",
+                          "rows": LN_ROWS, "cols": LN_COLS, "parties_per_gpu": 2,
+                          "l2": "256 MB flush between steps", "parallelism": f"one block per GPU, {ws} GPU(s)"},
+               "e2e": {"value": round(ws / (e2e_ms / 1e3), 3), "unit": "blocks/s", "h2d_bytes_per_step": 2 * n * 8,
+                       "d2h_bytes_per_step": 2 * n * 8, "ms_per_step": round(e2e_ms, 4),
+                       "path": "sufb200_layernorm_block_pair, pinned x shares in, output shares out"},
+               "roofline": {"bound": "hbm", "unit": "GB/s", "achieved": round(gbs, 1), "peak": hbm_peak,
+                            "frac": round(gbs / hbm_peak, 4), "traffic": traffic, "per_block_us": round(ms * 1e3, 1),
+                            "note": "bytes = every stage's tensors read and written once (22 words per element); "
+                                    "a chain of about 30 small launches, bound by their latency"},
+               "cpu_baseline": cpu_layernorm_baseline(args) if (ws == 1 and not args.no_cpu) else None,
+               "clocks": clk.summary(), "gpu_launches": 30 * args.steps,
+               "max_err_vs_double_layernorm": round(err, 6), "reconstruction_ok": err < 0.02,
+               "ms_per_step_all": [round(v, 4) for v in ms_steps]}
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return res
+
+
+def run_layernorm_reference(args, ws, rank):
+    if rank != 0:
+        return None
+    runs = [cpu_layernorm_baseline(args) for _ in range(args.steps)]
+    ms = min(r["ms_per_block"] for r in runs)
+    v = round(1e3 / ms, 3)
+    return {"metric": LN_METRIC, "value": v, "unit": "blocks/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64 (Z_2^64)", "data": "synthetic x ~ N(0, 1) at f = 12",
+            "impl": "reference",
+            "config": {"workload": "configs[4]: LayerNorm block, 128 x 768, f = 12, eps 1/1024, seed 4"},
+            "cpu_baseline": dict(runs[0], value=v, ms_per_block=round(ms, 3)),
+            "e2e": {"value": v, "unit": "blocks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def run_softmax_reference(args, ws, rank):
     if rank != 0:
         return None
@@ -1238,10 +1380,11 @@ def main():
     ap.add_argument("--n-elem", type=int, default=None,
                     help="elements per party at N=1 (default: the workload's config size; smaller only for "
                          "profiling)")
-    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open", "silu", "matmul", "softmax"],
+    ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open", "silu", "matmul", "softmax",
+                                                          "layernorm"],
                     help="trunc: configs[1] (the headline line); compare: configs[0], per-element keys; "
                          "open: the paired-GPU open of a configs[4] layer (N >= 2); softmax: the configs[4] "
-                         "softmax block")
+                         "softmax block; layernorm: the configs[4] LayerNorm block")
     ap.add_argument("--ring-bits", type=int, default=37, help="ring of the open workload (37: the reference's "
                                                                  "measured bert-base ring)")
     args = ap.parse_args()
@@ -1256,6 +1399,9 @@ def main():
                 "unavailable": "the reference's Beaver matmul is a CUDA kernel; its CUDA-core equivalent is timed "
                                "beside ours in the ours line (cuda_core)"}
                if rank == 0 else None) if args.impl == "reference" else run_matmul(args, ws, rank, local)
+    elif args.workload == "layernorm":
+        out = (run_layernorm_reference(args, ws, rank) if args.impl == "reference"
+               else run_layernorm(args, ws, rank, local))
     elif args.workload == "softmax":
         out = run_softmax_reference(args, ws, rank) if args.impl == "reference" else run_softmax(args, ws, rank, local)
     elif args.workload == "silu":

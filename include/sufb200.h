@@ -435,6 +435,46 @@ int sufb200_softmax_block_pair(sufb200_ctx ctx, const sufb200_softmax_party* p0,
                                int rows, const int32_t* d_row_off, const uint64_t* d_t0, const uint64_t* d_t1,
                                size_t n, int frac_bits, uint64_t* d_prob0, uint64_t* d_prob1, void* stream);
 
+/* The eight truncations of the LayerNorm block, in order: mean T_f, variance
+ * T_2f, rsqrt init T_f(c1 v), T_f(y y), T_f(v y2), the halving T_1(x y2),
+ * the Newton update T_f(y t), the normalised output T_f(d y). */
+#define SUFB200_LAYERNORM_TRUNCS 8
+
+/* One party's dealer material for sufb200_layernorm_block_pair (rows x cols,
+ * dense).  Triple arrays hold (a, b, c) interleaved. */
+typedef struct sufb200_layernorm_party {
+  uint64_t rsqrt_rin;              /* this party's share of the rsqrt LUT gate's r_in */
+  const uint8_t* d_rsqrt_lut;      /* device: broadcast IntervalKeyHeader blob, 4 words per interval */
+  size_t rsqrt_lut_bytes;
+  const uint64_t* d_sq_triples;    /* device [rows*cols][3]: d * d */
+  const uint64_t* d_row_triples;   /* device [4][rows][3]: c1*v, y*y, v*y2, y*t */
+  const uint64_t* d_norm_a;        /* device [rows*cols] row-broadcast triple A */
+  const uint64_t* d_norm_b;        /* device [rows] B */
+  const uint64_t* d_norm_c;        /* device [rows*cols] C = A * B[row] */
+  sufb200_trunc_desc trunc[SUFB200_LAYERNORM_TRUNCS];
+  uint64_t trunc_rin[SUFB200_LAYERNORM_TRUNCS];
+  const uint8_t* trunc_keys[SUFB200_LAYERNORM_TRUNCS][4]; /* host */
+  size_t trunc_key_bytes[SUFB200_LAYERNORM_TRUNCS][4];
+} sufb200_layernorm_party;
+
+/* runtime::LayerNormTask with RsqrtTask (include/runtime/phase_tasks.hpp:
+ * 1383-1700, 2186-2600; one Newton step, no affine) for BOTH parties on one
+ * GPU, every open on the device, computed with Beaver products and
+ * truncation bundles throughout:
+ *   mu = T_f(sum x * inv_len), d = x - mu, v = T_2f(sum d^2 * inv_len) + eps,
+ *   y = c0 + T_f(c1 v) with (c0, c1) = LUT_rsqrt(v),
+ *   y = T_f(y (3 2^(f-1) - T_1(T_f(v T_f(y y))))), out = T_f(d y[row]).
+ * (The reference's RsqrtTask forms its initial guess from the opened input
+ * and halves x y^2 with a local shift of each share; on additive shares both
+ * are replaced here by the secure steps above, which compute the same
+ * fixed-point function.)  inv_len and eps are public Q(frac_bits) constants;
+ * eps is added once.  x0/x1: [rows*cols] shares; out0/out1 likewise.
+ * Asynchronous on `stream`. */
+int sufb200_layernorm_block_pair(sufb200_ctx ctx, const sufb200_layernorm_party* p0,
+                                 const sufb200_layernorm_party* p1, int rows, int cols, const uint64_t* d_x0,
+                                 const uint64_t* d_x1, int frac_bits, uint64_t inv_len, uint64_t eps,
+                                 uint64_t* d_out0, uint64_t* d_out1, void* stream);
+
 /* ---- host utilities ----------------------------------------------------- */
 
 /* n successive draws of mt19937_64(seed) (the reference's mask / key RNG). */

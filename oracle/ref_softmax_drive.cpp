@@ -53,6 +53,7 @@
 #include "runtime/pfss_gpu_staging.hpp"
 #include "runtime/phase_executor.hpp"
 #include "runtime/pfss_superbatch.hpp"
+#include "rsqrt_affine_suf.hpp"
 
 namespace {
 
@@ -255,6 +256,152 @@ std::vector<uint64_t> run_block(proto::PfssBackendBatch& be0, proto::PfssBackend
   return y;
 }
 
+// ---- LayerNorm (configs[4] second half): the reference's runtime::LayerNormTask
+
+struct LnWorkload {
+  int rows, cols, fb;
+  std::vector<uint64_t> x;  // Q(fb), two's complement
+  std::vector<double> ref;  // double-precision LayerNorm (eps 1/1024, no affine)
+};
+
+LnWorkload make_ln_workload(int rows, int cols, int fb, uint64_t seed) {
+  LnWorkload w{rows, cols, fb, {}, {}};
+  std::mt19937_64 g(seed);
+  std::normal_distribution<double> nd(0.0, 1.0);
+  w.x.resize(static_cast<size_t>(rows) * cols);
+  w.ref.resize(w.x.size());
+  for (int r = 0; r < rows; r++) {
+    double s = 0, s2 = 0;
+    for (int c = 0; c < cols; c++) {
+      const int64_t q = std::llround(std::ldexp(nd(g), fb));
+      w.x[static_cast<size_t>(r) * cols + c] = static_cast<uint64_t>(q);
+      s += std::ldexp(static_cast<double>(q), -fb);
+    }
+    const double mu = s / cols;
+    for (int c = 0; c < cols; c++) {
+      const double d = std::ldexp(static_cast<double>(static_cast<int64_t>(w.x[static_cast<size_t>(r) * cols + c])), -fb) - mu;
+      s2 += d * d;
+    }
+    const double inv = 1.0 / std::sqrt(s2 / cols + 1.0 / 1024.0);
+    for (int c = 0; c < cols; c++) {
+      const size_t k = static_cast<size_t>(r) * cols + c;
+      w.ref[k] = (std::ldexp(static_cast<double>(static_cast<int64_t>(w.x[k])), -fb) - mu) * inv;
+    }
+  }
+  return w;
+}
+
+struct LnMaterial {
+  gates::PiecewisePolySpec spec;
+  suf::SUF<uint64_t> suf;
+  gates::CompositeKeyPair keys;
+  compiler::TruncationLoweringResult trunc_f, trunc_2f, mean_t, var_t, norm_t;
+  std::vector<proto::BeaverTriple64Share> mul[2];
+};
+
+compiler::TruncationLoweringResult lower(proto::PfssBackendBatch& be, std::mt19937_64& g, compiler::GateKind kind,
+                                         int f, size_t n) {
+  compiler::GateParams p;
+  p.kind = kind;
+  p.frac_bits = f;
+  return compiler::lower_truncation_gate(be, g, p, n);
+}
+
+// Signed truncations throughout: the inputs are Gaussian (negative values),
+// where a logical shift (FaithfulTR) of the mean or the normalised value
+// would be wrong.
+std::unique_ptr<LnMaterial> deal_ln(proto::PfssBackendBatch& be, const LnWorkload& w, uint64_t seed) {
+  auto m = std::make_unique<LnMaterial>();
+  std::mt19937_64 g(seed);
+  const size_t R = static_cast<size_t>(w.rows), N = R * w.cols;
+  m->spec = gates::make_rsqrt_affine_init_spec(w.fb, 1.0 / 1024.0, 16.0);
+  m->suf = oracle_ref::rsqrt_affine_suf(m->spec);
+  std::vector<uint64_t> r_out(2, 0ull);
+  m->keys = gates::composite_gen_backend_with_masks(m->suf, be, g, g(), r_out, R, compiler::GateKind::Rsqrt);
+  m->keys.k0.compiled.gate_kind = compiler::GateKind::Rsqrt;
+  m->keys.k1.compiled.gate_kind = compiler::GateKind::Rsqrt;
+  gates::ensure_beaver_triples(m->keys, 3 * R, g);  // RsqrtTask: y*y, x*y2, y*t per Newton step
+  m->trunc_f = lower(be, g, compiler::GateKind::FaithfulARS, w.fb, R);
+  m->trunc_2f = lower(be, g, compiler::GateKind::GapARS, 2 * w.fb, R);
+  m->mean_t = lower(be, g, compiler::GateKind::FaithfulARS, w.fb, R);
+  m->var_t = lower(be, g, compiler::GateKind::GapARS, 2 * w.fb, R);
+  m->norm_t = lower(be, g, compiler::GateKind::FaithfulARS, w.fb, N);
+  for (size_t i = 0; i < N; i++) {  // Beaver triples of diff^2
+    const uint64_t a = g(), b = g(), c = a * b, a0 = g(), b0 = g(), c0 = g();
+    m->mul[0].push_back({a0, b0, c0});
+    m->mul[1].push_back({a - a0, b - b0, c - c0});
+  }
+  return m;
+}
+
+std::vector<uint64_t> run_ln_party(int party, proto::PfssBackendBatch& be, net::Chan& ch, const LnWorkload& w,
+                                   const LnMaterial& m, runtime::RowBroadcastTripleProvider* rt,
+                                   std::span<const uint64_t> x) {
+  std::unique_ptr<runtime::CudaPfssStager> stager;
+  if (auto* staged = dynamic_cast<proto::PfssGpuStagedEval*>(&be))
+    stager = std::make_unique<runtime::CudaPfssStager>(staged->device_stream());
+  runtime::PhaseExecutor pe;
+  runtime::PhaseResources R{};
+  runtime::ProtoChanFromNet pch(ch);
+  R.party = party;
+  R.pfss_backend = &be;
+  R.pfss_chan = &pch;
+  R.net_chan = &ch;
+  R.pfss_coeff = &pe.pfss_coeff_batch();
+  R.pfss_trunc = &pe.pfss_trunc_batch();
+  R.opens = &pe.open_collector();
+  if (stager) {
+    pe.pfss_coeff_batch().set_gpu_stager(stager.get());
+    pe.pfss_trunc_batch().set_gpu_stager(stager.get());
+  }
+  runtime::LayerNormTaskBundle b{};
+  b.mean_trunc = {nullptr, &m.mean_t, w.fb, true};
+  b.var_trunc = {nullptr, &m.var_t, 2 * w.fb, true};
+  b.norm_trunc = {nullptr, &m.norm_t, w.fb, true};
+  b.rsqrt = runtime::RsqrtTaskBundle{&m.suf, &m.keys.k0, &m.keys.k1, &m.trunc_f, &m.trunc_2f, &m.spec, w.fb, 1};
+  b.inv_len_qf = static_cast<uint64_t>(std::llround(std::ldexp(1.0 / w.cols, w.fb)));
+  b.eps_qf = static_cast<uint64_t>(std::llround(std::ldexp(1.0 / 1024.0, w.fb)));
+  b.frac_bits = w.fb;
+  b.mul_triples = std::span<const proto::BeaverTriple64Share>(m.mul[party]);
+  b.row_triples = rt;
+  std::vector<uint64_t> out(x.size(), 0);
+  pe.add_task(std::make_unique<runtime::LayerNormTask>(b, x, std::span<uint64_t>(out), w.rows, w.cols));
+  pe.run(R);
+  return out;
+}
+
+std::vector<uint64_t> run_ln_block(proto::PfssBackendBatch& be0, proto::PfssBackendBatch& be1, const LnWorkload& w,
+                                   const LnMaterial& m, const RowTriples& trip, double* ms) {
+  WordPipes pipes;
+  PipeChan c0(&pipes, 0), c1(&pipes, 1);
+  RowTripleSource s0(trip, 0), s1(trip, 1);
+  const std::vector<uint64_t> zeros(w.x.size(), 0);
+  std::vector<uint64_t> y0, y1;
+  std::exception_ptr e1;
+  const auto t0 = std::chrono::steady_clock::now();
+  std::thread th([&] {
+    try {
+      y1 = run_ln_party(1, be1, c1, w, m, &s1, std::span<const uint64_t>(zeros));
+    } catch (...) {
+      e1 = std::current_exception();
+    }
+  });
+  y0 = run_ln_party(0, be0, c0, w, m, &s0, std::span<const uint64_t>(w.x));
+  th.join();
+  if (e1) std::rethrow_exception(e1);
+  *ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  std::vector<uint64_t> y(y0.size());
+  for (size_t i = 0; i < y.size(); i++) y[i] = y0[i] + y1[i];
+  return y;
+}
+
+double ln_max_err(const LnWorkload& w, const std::vector<uint64_t>& y) {
+  double e = 0.0;
+  for (size_t k = 0; k < y.size(); k++)
+    e = std::max(e, std::fabs(std::ldexp(static_cast<double>(static_cast<int64_t>(y[k])), -w.fb) - w.ref[k]));
+  return e;
+}
+
 double active_max_err(const Workload& w, const std::vector<uint64_t>& y) {
   double e = 0.0;
   for (int r = 0; r < w.rows; r++)
@@ -267,8 +414,72 @@ double active_max_err(const Workload& w, const std::vector<uint64_t>& y) {
 
 }  // namespace
 
+void set_gpu_switches() {
+  for (const char* k : {"SUF_PFSS_CACHE_KEYS", "SUF_PFSS_CACHE_HATX", "SUF_TRUNC_GPU", "SUF_MUL_GPU",
+                        "SUF_RECIP_GPU_KERNELS", "SUF_HORNER_GPU"})
+    setenv(k, "1", 0);
+}
+
+bool write_dump(const std::string& path, const std::vector<uint64_t>& a, const std::vector<uint64_t>& b) {
+  FILE* fp = std::fopen(path.c_str(), "wb");
+  return fp && std::fwrite(a.data(), 8, a.size(), fp) == a.size() && std::fwrite(b.data(), 8, b.size(), fp) == b.size() &&
+         std::fclose(fp) == 0;
+}
+
+// --block=ln: the LayerNorm block, same legs and output as the softmax block.
+int main_ln(int rows, int cols, int fb, int reps, uint64_t seed, const std::string& dump, bool cpu_only,
+            bool switches) {
+  const LnWorkload w = make_ln_workload(rows, cols, fb, seed);
+  const RowTriples trip(rows, cols, seed * 7 + 1);
+  proto::ReferenceBackend ref;
+  const auto mref = deal_ln(ref, w, seed * 31 + 5);
+  double ms = 0.0, ref_ms = 1e30;
+  std::vector<uint64_t> yref;
+  for (int i = 0; i < reps; i++) {
+    yref = run_ln_block(ref, ref, w, *mref, trip, &ms);
+    ref_ms = std::min(ref_ms, ms);
+  }
+  if (!dump.empty() && !write_dump(dump, w.x, yref)) {
+    std::printf("{\"error\": \"cannot write %s\"}\n", dump.c_str());
+    return 1;
+  }
+  if (cpu_only) {
+    std::printf("{\"workload\": \"configs[4] layernorm block\", \"rows\": %d, \"cols\": %d, \"ref_cpu_ms\": %.3f, "
+                "\"ref_max_err_vs_double\": %.6f}\n",
+                rows, cols, ref_ms, ln_max_err(w, yref));
+    return 0;
+  }
+  if (switches) set_gpu_switches();
+  std::unique_ptr<proto::PfssBackendBatch> g0, g1;
+  try {
+    g0 = proto::make_real_gpu_backend();
+    g1 = proto::make_real_gpu_backend();
+  } catch (const std::exception& e) {
+    std::printf("{\"workload\": \"configs[4] layernorm block\", \"rows\": %d, \"cols\": %d, \"ref_cpu_ms\": %.3f, "
+                "\"ref_max_err_vs_double\": %.6f, \"sufb200\": \"%s\"}\n",
+                rows, cols, ref_ms, ln_max_err(w, yref), e.what());
+    return 3;
+  }
+  const auto mgpu = deal_ln(*g0, w, seed * 31 + 5);
+  double gpu_ms = 1e30;
+  std::vector<uint64_t> ygpu;
+  for (int i = 0; i < reps + 1; i++) {
+    ygpu = run_ln_block(*g0, *g1, w, *mgpu, trip, &ms);
+    if (i > 0) gpu_ms = std::min(gpu_ms, ms);
+  }
+  size_t diff = 0;
+  for (size_t k = 0; k < ygpu.size(); k++) diff += ygpu[k] != yref[k];
+  std::printf("{\"workload\": \"configs[4] layernorm block\", \"rows\": %d, \"cols\": %d, \"ref_cpu_ms\": %.3f, "
+              "\"sufb200_ms\": %.3f, \"identical\": %s, \"mismatches\": %zu, \"max_err_vs_double\": %.6f, "
+              "\"ref_max_err_vs_double\": %.6f}\n",
+              rows, cols, ref_ms, gpu_ms, diff == 0 ? "true" : "false", diff, ln_max_err(w, ygpu),
+              ln_max_err(w, yref));
+  return diff == 0 ? 0 : 2;
+}
+
 int main(int argc, char** argv) {
-  int heads = 12, len = 128, fb = 12, reps = 3, switches = 1;
+  int heads = 12, len = 128, fb = 12, reps = 3, switches = 1, rows = 128, cols = 768;
+  bool ln = false;
   uint64_t seed = 4;
   std::string dump;  // --dump=PATH: t[rows*cols] then the CPU reconstruction, little-endian u64
   bool cpu_only = false;  // --cpu-only: the reference CPU leg alone (the B200 engine is not touched)
@@ -283,7 +494,11 @@ int main(int argc, char** argv) {
     else if (a.rfind("--switches=", 0) == 0) switches = std::stoi(val("--switches="));
     else if (a.rfind("--dump=", 0) == 0) dump = val("--dump=");
     else if (a == "--cpu-only") cpu_only = true;
+    else if (a == "--block=ln") ln = true;
+    else if (a.rfind("--rows=", 0) == 0) rows = std::stoi(val("--rows="));
+    else if (a.rfind("--cols=", 0) == 0) cols = std::stoi(val("--cols="));
   }
+  if (ln) return main_ln(rows, cols, fb, reps, seed, dump, cpu_only, switches != 0);
   const Workload w = make_workload(heads, len, fb, seed);
   const RowTriples trip(w.rows, w.cols, seed * 7 + 1);
   size_t active = 0;

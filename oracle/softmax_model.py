@@ -30,7 +30,9 @@ TABLES = Path(__file__).resolve().parents[1] / "suf_b200" / "tables" / "softmax_
 def load_tables(path: Path = TABLES) -> dict:
     d = json.loads(Path(path).read_text())
     out = {"frac_bits": int(d["frac_bits"])}
-    for g in ("nexp", "recip"):
+    for g in ("nexp", "recip", "rsqrt"):
+        if g not in d:
+            continue
         alpha = np.array([int(v) for v in d[g]["alpha"]], dtype=np.uint64)
         coeffs = np.zeros((len(d[g]["pieces"]), 4), dtype=np.uint64)
         for i, piece in enumerate(d[g]["pieces"]):
@@ -69,3 +71,29 @@ def softmax_block(t: np.ndarray, row_offsets: np.ndarray, tables: dict) -> np.nd
         y = tshift(y * (np.uint64(2 << f) - tshift(y * s, f)), f)
         row_of = np.repeat(np.arange(rows), lens)
         return tshift(e * y[row_of], f)
+
+
+def layernorm_block(x: np.ndarray, rows: int, cols: int, tables: dict, eps_qf: int | None = None) -> np.ndarray:
+    """The configs[4] LayerNorm block (runtime::LayerNormTask with RsqrtTask,
+    include/runtime/phase_tasks.hpp:1383-1700, 2186-2600; one Newton step, no
+    affine), with signed truncations:
+      mu = T_f(sum_row(x) invL)            d = x - mu
+      v  = T_2f(sum_row(d^2) invL) + eps
+      y  = c0 + T_f(c1 v)                  (c0, c1 = LUT_rsqrt(v))
+      y  = T_f(y (3 2^(f-1) - floor(T_f(v T_f(y y)) / 2)))
+      out = T_f(d y_row)
+    invL = round(2^f / cols), eps = round(2^f / 1024)."""
+    f = tables["frac_bits"]
+    inv_len = np.uint64(round((1 << f) / cols))
+    eps = np.uint64(round((1 << f) / 1024) if eps_qf is None else eps_qf)
+    x = x.astype(np.uint64).reshape(rows, cols)
+    with np.errstate(over="ignore"):
+        mu = tshift(x.sum(axis=1, dtype=np.uint64) * inv_len, f)
+        d = x - mu[:, None]
+        v = tshift((d * d).sum(axis=1, dtype=np.uint64) * inv_len, 2 * f) + eps
+        c = lut(tables["rsqrt"], v)
+        y = c[:, 0] + tshift(c[:, 1] * v, f)
+        xy2 = tshift(v * tshift(y * y, f), f)
+        t = np.uint64(3 << (f - 1)) - (xy2 >> np.uint64(1))
+        y = tshift(y * t, f)
+        return tshift(d * y[:, None], f).reshape(-1)

@@ -7,7 +7,10 @@
 //          does (include/gates/nexp_composite.hpp:107-147);
 //   recip: gates::make_recip_affine_init_spec(f, 1024) (tables/
 //          recip_piecewise_affine_init.hpp:11) expanded the same way, as
-//          dealer_make_recip_task_material does (reciprocal_composite.hpp:55-105).
+//          dealer_make_recip_task_material does (reciprocal_composite.hpp:55-105);
+//   rsqrt: gates::make_rsqrt_affine_init_spec(f, 1/1024, 16) (tables/
+//          rsqrt_piecewise_affine_init.hpp) as the affine SUF of
+//          oracle/rsqrt_affine_suf.hpp (the LayerNorm block's RsqrtTask init).
 // Built by oracle/Makefile (target `softmax`) into oracle/_ref/; run by
 // tests/golden/make_softmax_tables.py.  Usage: softmax_tables <frac_bits>.
 #include <cstdio>
@@ -15,6 +18,8 @@
 
 #include "gates/nexp_composite.hpp"
 #include "gates/reciprocal_composite.hpp"
+#include "gates/tables/rsqrt_piecewise_affine_init.hpp"
+#include "rsqrt_affine_suf.hpp"
 
 namespace {
 
@@ -45,9 +50,11 @@ int main(int argc, char** argv) {
   gates::NExpGateParams np{f, 16};
   const auto nexp = suf::build_silu_suf_from_piecewise(gates::make_nexp_spec(np));
   const auto recip = suf::build_silu_suf_from_piecewise(gates::make_recip_affine_init_spec(f, 1024.0));
+  const auto rsqrt = oracle_ref::rsqrt_affine_suf(gates::make_rsqrt_affine_init_spec(f, 1.0 / 1024.0, 16.0));
   std::printf("{\n  \"frac_bits\": %d,\n", f);
   dump_suf("nexp", nexp, false);
-  dump_suf("recip", recip, true);
+  dump_suf("recip", recip, false);
+  dump_suf("rsqrt", rsqrt, true);
   std::printf("}\n");
   return 0;
 }

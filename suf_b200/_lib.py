@@ -112,6 +112,7 @@ _SIGS = {
     "sufb200_beaver_matmul2d": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, C.c_int64, _i, _vp, _vp]),
     "sufb200_host_mt19937_64": (_i, [_u64, _vp, _sz]),
     "sufb200_softmax_block_pair": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _sz, _i, _vp, _vp, _vp]),
+    "sufb200_layernorm_block_pair": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _i, _u64, _u64, _vp, _vp, _vp]),
 }
 
 

@@ -54,7 +54,9 @@ def load_tables(path: Path = TABLES) -> dict:
     """{'frac_bits': f, 'nexp': (alpha [m+1] u64, coeffs [m][4] u64), 'recip': ...}"""
     d = json.loads(Path(path).read_text())
     out = {"frac_bits": int(d["frac_bits"])}
-    for g in ("nexp", "recip"):
+    for g in ("nexp", "recip", "rsqrt"):
+        if g not in d:
+            continue
         alpha = np.array([int(v) for v in d[g]["alpha"]], dtype=np.uint64)
         coeffs = np.zeros((len(d[g]["pieces"]), 4), dtype=np.uint64)
         for i, piece in enumerate(d[g]["pieces"]):
@@ -197,3 +199,116 @@ class SoftmaxBlock:
                                            _t_ptr(self.d_row_off), _t_ptr(d_t0), _t_ptr(d_t1), self.n,
                                            self.frac_bits, _t_ptr(d_prob0), _t_ptr(d_prob1), _stream_ptr(stream)))
         return d_prob0, d_prob1
+
+
+# ---------------------------------------------------------------------------
+# configs[4] LayerNorm block (sufb200_layernorm_block_pair)
+# ---------------------------------------------------------------------------
+
+N_LN_TRUNCS = 8
+
+
+class LayerNormParty(C.Structure):
+    """Mirror of sufb200_layernorm_party."""
+
+    _fields_ = [
+        ("rsqrt_rin", C.c_uint64),
+        ("d_rsqrt_lut", C.c_void_p), ("rsqrt_lut_bytes", C.c_size_t),
+        ("d_sq_triples", C.c_void_p), ("d_row_triples", C.c_void_p),
+        ("d_norm_a", C.c_void_p), ("d_norm_b", C.c_void_p), ("d_norm_c", C.c_void_p),
+        ("trunc", TruncDesc * N_LN_TRUNCS),
+        ("trunc_rin", C.c_uint64 * N_LN_TRUNCS),
+        ("trunc_keys", (C.c_void_p * 4) * N_LN_TRUNCS),
+        ("trunc_key_bytes", (C.c_size_t * 4) * N_LN_TRUNCS),
+    ]
+
+
+class LayerNormBlock:
+    """Dealer material for one LayerNorm block (rows x cols, dense) for both
+    parties on the context's device, and the block call.  All eight
+    truncations are GapARS bundles (signed floors; the reference's bench uses
+    logical shifts for the mean and the output, which are wrong for the
+    negative values of Gaussian inputs, and FaithfulARS for the Newton steps,
+    which floors identically in this range)."""
+
+    def __init__(self, ctx: Context, rows: int, cols: int, seed: int = 1, tables: dict | None = None):
+        import torch
+
+        self.ctx = ctx
+        self.tables = tables or load_tables()
+        f = self.frac_bits = int(self.tables["frac_bits"])
+        self.rows, self.cols = int(rows), int(cols)
+        n = self.n = self.rows * self.cols
+        self.inv_len = int(round((1 << f) / cols))
+        self.eps = int(round((1 << f) / 1024))
+        dev = torch.device("cuda", ctx.device)
+        self._keep = []
+
+        def dcopy(a: np.ndarray):
+            t = torch.from_numpy(np.ascontiguousarray(a).view(np.int64) if a.dtype == np.uint64 else a).to(dev)
+            self._keep.append(t)
+            return t
+
+        rng = np.random.default_rng(seed)
+        parts = [LayerNormParty(), LayerNormParty()]
+        r_in = int(rng.integers(0, 2**64, dtype=np.uint64))
+        r0 = int(rng.integers(0, 2**64, dtype=np.uint64))
+        cuts, payload = masked_lut_table(*self.tables["rsqrt"], r_in)
+        nonce = int(rng.integers(1, 2**62))
+        sd = seed_from_id(nonce, 7)
+        for p in (0, 1):
+            key = interval_lut_key(p, nonce, 64, 4, cuts, payload.reshape(-1), sd)
+            parts[p].rsqrt_rin = r0 if p == 0 else (r_in - r0) & M64
+            parts[p].d_rsqrt_lut = dcopy(key).data_ptr()
+            parts[p].rsqrt_lut_bytes = key.size
+        for field, count in (("d_sq_triples", n), ("d_row_triples", 4 * self.rows)):
+            sh = _triples(rng, count)
+            for p in (0, 1):
+                setattr(parts[p], field, dcopy(sh[p]).data_ptr())
+        A = rng.integers(0, 2**64, n, dtype=np.uint64)
+        B = rng.integers(0, 2**64, self.rows, dtype=np.uint64)
+        with np.errstate(over="ignore"):
+            Cm = A * np.repeat(B, self.cols)
+        for field, v in (("d_norm_a", A), ("d_norm_b", B), ("d_norm_c", Cm)):
+            sh = _split(rng, v)
+            for p in (0, 1):
+                setattr(parts[p], field, dcopy(sh[p]).data_ptr())
+        payload1 = (1).to_bytes(8, "little")
+        # every value truncated here stays below 2^40 in magnitude, far inside
+        # GapARS's exactness bound, where it floors exactly like FaithfulARS with
+        # two f-bit queries instead of two 64-bit ones
+        kinds = [(TRUNC_GAPARS, fk) for fk in (f, 2 * f, f, f, f, 1, f, f)]
+        for k, (kind, fk) in enumerate(kinds):
+            r_t, d0, d1, thetas = Context.trunc_gen(kind, fk, int(rng.integers(1, 2**63)))
+            rr = int(rng.integers(0, 2**64, dtype=np.uint64))
+            for p, d in ((0, d0), (1, d1)):
+                parts[p].trunc[k] = d
+                parts[p].trunc_rin[k] = rr if p == 0 else (r_t - rr) & M64
+            for q in range(int(d0.nq)):
+                s0 = rng.integers(0, 256, 16, dtype=np.uint8)
+                s1 = rng.integers(0, 256, 16, dtype=np.uint8)
+                k0, k1 = ctx.myl7_gen(GROUP_ADD, int(d0.q_bits[q]), int(thetas[q]), payload1, s0, s1)
+                for p, key in ((0, k0), (1, k1)):
+                    self._keep.append(key)
+                    parts[p].trunc_keys[k][q] = key.ctypes.data
+                    parts[p].trunc_key_bytes[k][q] = key.size
+        self.parts = parts
+
+    def run(self, d_x0, d_x1, d_out0=None, d_out1=None, stream=None):
+        """Both parties' shares of x (rows * cols, Q f, int64 tensors on the
+        device) -> shares of the normalised values.  Asynchronous."""
+        import torch
+
+        from .engine import _stream_ptr, _t_ptr
+
+        if d_x0.numel() != self.n or d_x1.numel() != self.n:
+            raise ValueError(f"layernorm block: expected {self.n} elements")
+        if d_out0 is None:
+            d_out0 = torch.empty_like(d_x0)
+        if d_out1 is None:
+            d_out1 = torch.empty_like(d_x1)
+        check(_lib.lib().sufb200_layernorm_block_pair(
+            self.ctx.h, C.byref(self.parts[0]), C.byref(self.parts[1]), self.rows, self.cols, _t_ptr(d_x0),
+            _t_ptr(d_x1), self.frac_bits, C.c_uint64(self.inv_len), C.c_uint64(self.eps), _t_ptr(d_out0),
+            _t_ptr(d_out1), _stream_ptr(stream)))
+        return d_out0, d_out1

@@ -84,3 +84,29 @@ def test_softmax_block_matches_reference_fixture(ctx, torch_cuda):
     ctx.sync()
     with np.errstate(over="ignore"):
         assert ((from_dev(p0, np.uint64) + from_dev(p1, np.uint64)) == y).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,cols", [(128, 768), (7, 100), (64, 64)])
+def test_layernorm_block_matches_model(ctx, torch_cuda, rows, cols):
+    from oracle.softmax_model import layernorm_block
+    from suf_b200.softmax import LayerNormBlock
+    from tests.conftest import from_dev, to_dev
+
+    rng = np.random.default_rng(rows * 7 + cols)
+    x = np.round(rng.normal(0.0, 1.0, rows * cols) * 4096).astype(np.int64).view(np.uint64)
+    blk = LayerNormBlock(ctx, rows, cols, seed=rows + cols)
+    x0, x1 = _shares(rng, x)
+    o0, o1 = blk.run(to_dev(torch_cuda, x0), to_dev(torch_cuda, x1))
+    ctx.sync()
+    with np.errstate(over="ignore"):
+        got = from_dev(o0, np.uint64) + from_dev(o1, np.uint64)
+    want = layernorm_block(x, rows, cols, load_tables())
+    assert (got == want).all(), int((got != want).sum())
+    # double-precision LayerNorm with the block's public 1/L = round(2^f / cols) / 2^f
+    # (the reference's inv_len_qf), against which only rounding remains
+    inv = round(4096 / cols) / 4096.0
+    xr = x.view(np.int64).reshape(rows, cols) / 4096.0
+    mu = xr.sum(1, keepdims=True) * inv
+    ref = (xr - mu) / np.sqrt(((xr - mu) ** 2).sum(1, keepdims=True) * inv + 1 / 1024)
+    assert np.abs(got.view(np.int64).reshape(rows, cols) / 4096.0 - ref).max() < 0.02
