@@ -162,6 +162,16 @@ int sufb200_trunc_bundle_eval(sufb200_ctx ctx, const sufb200_trunc_desc* desc, c
                               const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y,
                               uint64_t* d_bools, void* stream);
 
+/* One party's bundle over a bucket of jobs that share its keys (the bucket
+ * step of PfssSuperBatch::flush_eval, src/runtime/pfss_superbatch.cpp:
+ * 251-975, which concatenates the jobs' x^ with one device memcpy per job,
+ * :801-845): job j's x^ is d_xhat[j][0..n[j]) and its result goes to
+ * d_y[j].  One gather launch, one bundle evaluation over the whole bucket,
+ * one scatter launch (per 48 jobs).  Host arrays of device pointers. */
+int sufb200_trunc_bundle_eval_jobs(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                                   const size_t* key_bytes, const uint64_t* const* d_xhat, const size_t* n,
+                                   uint64_t* const* d_y, int njobs, void* stream);
+
 /* Both parties' bundles over the same public x^ on one GPU (desc0 / keys0 of
  * party 0, desc1 / keys1 of party 1): batches below the shared-prefix size
  * run in ONE launch with one lane per (party, element, query); larger ones

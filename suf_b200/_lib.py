@@ -72,6 +72,7 @@ _SIGS = {
     "sufb200_myl7_dcf_eval_host": (_i, [_vp, _i, _i, _vp, _sz, _i, _vp, _sz, _i, _vp]),
     "sufb200_trunc_gen": (_i, [_i, _i, _u64, C.POINTER(TruncDesc), C.POINTER(TruncDesc), _vp, _vp]),
     "sufb200_trunc_bundle_eval": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
+    "sufb200_trunc_bundle_eval_jobs": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _vp, _vp, _i, _vp]),
     "sufb200_trunc_bundle_eval_pair": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, C.POINTER(TruncDesc), _vp, _vp, _vp,
                                             _sz, _vp, _vp, _vp]),
     "sufb200_trunc_bundle_eval_host": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp]),

@@ -586,6 +586,52 @@ int sufb200_trunc_bundle_eval_pair(sufb200_ctx ctx, const sufb200_trunc_desc* de
   return SUFB200_OK;
 }
 
+int sufb200_trunc_bundle_eval_jobs(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                                   const size_t* key_bytes, const uint64_t* const* d_xhat, const size_t* n,
+                                   uint64_t* const* d_y, int njobs, void* stream) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (int rc = check_bundle_desc(desc, keys, key_bytes)) return rc;
+  if (njobs < 0 || (njobs > 0 && (!d_xhat || !n || !d_y))) return fail(SUFB200_ERR_INVALID, "bad job list");
+  size_t total = 0;
+  for (int j = 0; j < njobs; j++) {
+    if (n[j] && (!d_xhat[j] || !d_y[j] || !aligned8(d_xhat[j]) || !aligned8(d_y[j])))
+      return fail(SUFB200_ERR_INVALID, "job " + std::to_string(j) + ": null or misaligned device pointer");
+    total += n[j];
+  }
+  if (total == 0) return SUFB200_OK;
+  if (njobs == 1) return trunc_bundle_impl(ctx, desc, keys, key_bytes, d_xhat[0], n[0], d_y[0], nullptr, stream, nullptr);
+  cudaStream_t st = as_stream(stream);
+  uint64_t* batch = nullptr;
+  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&batch), 2 * total * 8, ctx->pool, st),
+                     "job bucket allocation");
+  auto copy_all = [&](bool to_batch, uint64_t* buf) {
+    size_t base = 0;
+    for (int j0 = 0; j0 < njobs; j0 += sufb200::kJobsPerLaunch) {
+      sufb200::JobTable t{};
+      t.njobs = std::min(sufb200::kJobsPerLaunch, njobs - j0);
+      t.base = base;
+      t.off[0] = 0;
+      for (int k = 0; k < t.njobs; k++) {
+        t.src[k] = d_xhat[j0 + k];
+        t.dst[k] = d_y[j0 + k];
+        t.off[k + 1] = t.off[k] + n[j0 + k];
+      }
+      const cudaError_t e = sufb200::launch_jobs_copy(ctx, t, buf, to_batch, st);
+      if (e != cudaSuccess) return e;
+      base += t.off[t.njobs];
+    }
+    return cudaSuccess;
+  };
+  cudaError_t e = copy_all(true, batch);
+  int rc = SUFB200_OK;
+  if (e == cudaSuccess)
+    rc = trunc_bundle_impl(ctx, desc, keys, key_bytes, batch, total, batch + total, nullptr, stream, nullptr);
+  if (e == cudaSuccess && rc == SUFB200_OK) e = copy_all(false, batch + total);
+  cudaFreeAsync(batch, st);
+  if (e != cudaSuccess) return cuda_fail(e, "job bucket gather / scatter");
+  return rc;
+}
+
 int sufb200_trunc_bundle_eval_host(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
                                    const size_t* key_bytes, const uint64_t* xhat, size_t n, uint64_t* y,
                                    uint64_t* bools) {

@@ -40,6 +40,19 @@ struct TruncLaunch {
   uint32_t* status;
 };
 cudaError_t launch_trunc_bundle(const sufb200_ctx_s* ctx, const TruncLaunch& a, cudaStream_t st);
+// A chunk of a job bucket (jobs.cu): job j's words are src[j][0..off[j+1]-off[j])
+// (gather) or dst[j][...] (scatter), at batch[base + off[j] ...].
+constexpr int kJobsPerLaunch = 48;
+struct JobTable {
+  const uint64_t* src[kJobsPerLaunch];
+  uint64_t* dst[kJobsPerLaunch];
+  size_t off[kJobsPerLaunch + 1];
+  size_t base;
+  int njobs;
+};
+cudaError_t launch_jobs_copy(const sufb200_ctx_s* ctx, const JobTable& t, uint64_t* batch, bool to_batch,
+                             cudaStream_t st);
+
 // Both parties' bundles over the same x^ (a0.xhat == a1.xhat, a0.n == a1.n),
 // one lane per (party, element, query): for batches too small to fill the GPU.
 cudaError_t launch_trunc_bundle_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,

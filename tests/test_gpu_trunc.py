@@ -168,3 +168,37 @@ def test_pair_entry_matches_per_party_entry(ctx, torch_cuda, oracle, prg_state, 
     ctx.sync()
     for p in (0, 1):
         assert (from_dev(out[p]) == oracle_trunc_eval(oracle, descs[p], keys[p], xhat)).all(), p
+
+
+@pytest.mark.parametrize("lens", [[5, 0, 20_000, 1, 37], [300] * 61 + [0, 17_000]])
+def test_jobs_bucket_matches_per_job(ctx, torch_cuda, oracle, prg_state, lens):
+    """sufb200_trunc_bundle_eval_jobs over a bucket of jobs sharing one key
+    (ragged, empty, more than one gather launch): each job's result equals the
+    oracle's evaluation of that job alone."""
+    import ctypes as C
+
+    from suf_b200 import _lib
+
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(sum(lens))
+    r_in, descs, keys = trunc_material(oracle, KIND_GAPARS, 12, 33)
+    xs = [signed_fixed(rng, n, 40) + np.uint64(r_in) for n in lens]
+    dx = [to_dev(torch_cuda, x) if x.size else torch_cuda.zeros(1, dtype=torch_cuda.int64, device="cuda") for x in xs]
+    dy = [torch_cuda.full((max(n, 1),), -1, dtype=torch_cuda.int64, device="cuda") for n in lens]
+    pd = to_product_desc(descs[0])
+    karr = [np.ascontiguousarray(k, dtype=np.uint8) for k in keys[0]]
+    ptrs = (C.c_void_p * 4)(*[k.ctypes.data for k in karr], *([None] * (4 - len(karr))))
+    sizes = (C.c_size_t * 4)(*[k.size for k in karr], *([0] * (4 - len(karr))))
+    J = len(lens)
+    xp = (C.c_void_p * J)(*[t.data_ptr() for t in dx])
+    yp = (C.c_void_p * J)(*[t.data_ptr() for t in dy])
+    ns = (C.c_size_t * J)(*lens)
+    _lib.check(_lib.lib().sufb200_trunc_bundle_eval_jobs(ctx.h, C.byref(pd), C.cast(ptrs, C.c_void_p),
+                                                         C.cast(sizes, C.c_void_p), C.cast(xp, C.c_void_p),
+                                                         C.cast(ns, C.c_void_p), C.cast(yp, C.c_void_p), J, None))
+    ctx.sync()
+    for j, n in enumerate(lens):
+        if n:
+            assert (from_dev(dy[j])[:n] == oracle_trunc_eval(oracle, descs[0], keys[0], xs[j])).all(), j
+        else:
+            assert int(dy[j].cpu()[0]) == -1  # untouched
