@@ -21,10 +21,13 @@
 // groups), tiled so that a CTA's plane block for one step is one contiguous
 // range.  The GEMM then runs a 4-stage pipeline: one warp issues two plain
 // bulk copies (cp.async.bulk, no multicast) per step, A and B plane blocks,
-// against a transaction-count mbarrier, one warp issues the 36 MMAs of the
-// step and commits them back to the stage's "empty" mbarrier (one lane of
+// against a transaction-count mbarrier, one warp issues the twelve MMAs of
+// the step and commits them back to the stage's "empty" mbarrier (one lane of
 // each does the issuing), and all warps read the diagonals out of tensor
-// memory at the end.  Every wait is bounded.
+// memory at the end.  Every wait is bounded.  When B is row-major with
+// 16-byte rows, B's planes are instead made inside the GEMM from raw rows
+// bulk-copied four steps ahead (ring_gemm_tc_fused_kernel), so B crosses HBM
+// once, as words.
 // Contractions too short to fill the GPU are split across CTAs: each stores
 // its partial tile (plain stores, no atomics), and a coalesced reduction
 // kernel adds the partials (addition mod 2^64 commutes), C and the bias and
@@ -33,6 +36,8 @@
 // Serves the reference's Beaver matmul (cuda/cuda_primitives.cu:391-628,
 // out = C + D B + A E (+ D E for party 0) as ONE product [D | A] x [B (+E) ; E])
 // and the public-weight matmul (src/nn/matmul_gpu.cu:21-117, Y = X W + bias).
+#include <cuda.h>  // CUtensorMap and its enums (the encoder comes from cudaGetDriverEntryPoint)
+
 #include "kernels.hpp"
 #include "ring_common.cuh"
 
@@ -144,6 +149,82 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
 
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Plane i (byte i of every word) of 16 K-consecutive words: 16 bytes.
+__device__ __forceinline__ uint4 plane_bytes(const uint64_t (&v)[16], int i) {
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    const uint32_t a0 = static_cast<uint32_t>(v[4 * q + 0] >> (i < 4 ? 0 : 32));
+    const uint32_t a1 = static_cast<uint32_t>(v[4 * q + 1] >> (i < 4 ? 0 : 32));
+    const uint32_t a2 = static_cast<uint32_t>(v[4 * q + 2] >> (i < 4 ? 0 : 32));
+    const uint32_t a3 = static_cast<uint32_t>(v[4 * q + 3] >> (i < 4 ? 0 : 32));
+    const uint32_t sel = static_cast<uint32_t>(i & 3) | (static_cast<uint32_t>(4 + (i & 3)) << 4);
+    w[q] = __byte_perm(__byte_perm(a0, a1, sel), __byte_perm(a2, a3, sel), 0x5410);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// The B planes of a stage are consecutive 64-row blocks in core-matrix
+// order, so [y_0 | y_1 | y_2 | y_3] is one N = 256 operand.  x_i times it,
+// accumulated at column 64 i, lands product (i, j) on column 64 (i + j):
+// diagonal i + j.  Twelve MMAs (N = 256 except where the 512 columns end)
+// cover the 36 limb pairs; the first two write all 512 columns, so on the
+// first step (accumulate = 0) they alone start from zero.
+__device__ __forceinline__ void mma_step(const uint32_t (&dt)[8], const uint64_t (&as)[8], const uint64_t (&bs)[8],
+                                         uint32_t accumulate) {
+  umma_i8(dt[0], as[0], bs[0], idesc_n(256), accumulate);
+  umma_i8(dt[4], as[0], bs[4], idesc_n(256), accumulate);
+#pragma unroll
+  for (int i = 1; i < 8; i++) umma_i8(dt[i], as[i], bs[0], idesc_n(i <= 4 ? 256 : 64 * (8 - i)), 1u);
+#pragma unroll
+  for (int i = 1; i < 4; i++) umma_i8(dt[i + 4], as[i], bs[4], idesc_n(256 - 64 * i), 1u);
+}
+
+// Warps 0-3 (TMEM lane quarter = warp): fold the 8 diagonals of the tile's
+// 128 x 64 accumulators and store the result (or a split's raw partial).
+__device__ __forceinline__ void epilogue(const RingGemmLaunch& g, uint32_t tmem, int warp, int lane, int b, int split,
+                                         int m0, int n0) {
+  const int M = g.M, N = g.N;
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const int m = m0 + warp * 32 + lane;
+  const uint64_t* C = g.c ? g.c + static_cast<size_t>(b) * g.cs : nullptr;
+  uint64_t* O = g.out + static_cast<size_t>(b) * g.os;
+  // a split CTA stores its raw partial; the reduction kernel finishes the sum
+  uint64_t* W = g.splits > 1 ? g.ws + (static_cast<size_t>(split) * g.batches + b) * M * N : nullptr;
+#pragma unroll 1
+  for (int cb = 0; cb < kTN / 16; cb++) {
+    uint32_t v[8][16];  // the 8 diagonals of 16 columns, loaded before one wait
+#pragma unroll
+    for (int s = 0; s < 8; s++)
+      tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(s * kTN + cb * 16), v[s]);
+#pragma unroll
+    for (int s = 0; s < 8; s++) tmem_wait(v[s]);
+    if (m < M) {
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        uint64_t acc = 0;
+#pragma unroll
+        for (int s = 0; s < 8; s++) acc += static_cast<uint64_t>(v[s][j]) << (8 * s);
+        const int n = n0 + cb * 16 + j;
+        if (n < N) {
+          const size_t o = static_cast<size_t>(m) * N + n;
+          if (W) {
+            W[o] = acc;
+          } else {
+            if (C) acc += C[o];
+            if (g.bias) acc += static_cast<uint64_t>(g.bias[n]);
+            O[o] = scaled_acc(acc, g.has_scale, g.mul_const, g.mul_shift);
+          }
+        }
+      }
+    }
+  }
 }
 
 // Byte planes of one operand, tiled for the GEMM: for step c and row tile
@@ -296,19 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
             as[i] = ad[i] + so;
             bs[i] = bd[i] + so;
           }
-          // The B planes of a stage are consecutive 64-row blocks in core-matrix
-          // order, so [y_0 | y_1 | y_2 | y_3] is one N = 256 operand.  x_i times
-          // it, accumulated at column 64 i, lands product (i, j) on column
-          // 64 (i + j): diagonal i + j.  Twelve MMAs (N = 256 except where the
-          // 512 columns end) cover the 36 limb pairs; the first two write all
-          // 512 columns, so on the first step they alone start from zero.
-          const uint32_t first = li > 0 ? 1u : 0u;
-          umma_i8(dt[0], as[0], bs[0], idesc_n(256), first);
-          umma_i8(dt[4], as[0], bs[4], idesc_n(256), first);
-#pragma unroll
-          for (int i = 1; i < 8; i++) umma_i8(dt[i], as[i], bs[0], idesc_n(i <= 4 ? 256 : 64 * (8 - i)), 1u);
-#pragma unroll
-          for (int i = 1; i < 4; i++) umma_i8(dt[i + 4], as[i], bs[4], idesc_n(256 - 64 * i), 1u);
+          mma_step(dt, as, bs, li > 0 ? 1u : 0u);
           umma_commit(empty0 + 8 * st);
         } else {
           *err = 1;
@@ -325,40 +394,215 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
     if (t == 0) atomicOr(g.status, kStatusTimeout);
     mbar_wait(done, 0);  // let whatever was issued drain before the columns are released
   } else if (nsteps > 0) {
+    epilogue(g, tmem, warp, lane, b, split, m0, n0);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int m = m0 + warp * 32 + lane;
-    const uint64_t* C = g.c ? g.c + static_cast<size_t>(b) * g.cs : nullptr;
-    uint64_t* O = g.out + static_cast<size_t>(b) * g.os;
-    // a split CTA stores its raw partial; the reduction kernel finishes the sum
-    uint64_t* W = g.splits > 1 ? g.ws + (static_cast<size_t>(split) * g.batches + b) * M * N : nullptr;
-#pragma unroll 1
-    for (int cb = 0; cb < kTN / 16; cb++) {
-      uint32_t v[8][16];  // the 8 diagonals of 16 columns, loaded before one wait
-#pragma unroll
-      for (int s = 0; s < 8; s++)
-        tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(s * kTN + cb * 16), v[s]);
-#pragma unroll
-      for (int s = 0; s < 8; s++) tmem_wait(v[s]);
-      if (m < M) {
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-          uint64_t acc = 0;
-#pragma unroll
-          for (int s = 0; s < 8; s++) acc += static_cast<uint64_t>(v[s][j]) << (8 * s);
-          const int n = n0 + cb * 16 + j;
-          if (n < N) {
-            const size_t o = static_cast<size_t>(m) * N + n;
-            if (W) {
-              W[o] = acc;
-            } else {
-              if (C) acc += C[o];
-              if (g.bias) acc += static_cast<uint64_t>(g.bias[n]);
-              O[o] = scaled_acc(acc, g.has_scale, g.mul_const, g.mul_shift);
-            }
-          }
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---- B split inside the GEMM --------------------------------------------
+// For a row-major B (K x N words, N even, 16-byte base) the byte planes of B
+// are made inside the GEMM instead of by the pre-pass: warp 0 loads each
+// step's raw 32 x 64 words of B (and of the Beaver addend) with one tiled
+// tensor-map load per matrix (no multicast; x = n0 is a multiple of 64 words,
+// out-of-range rows and columns read as zero) into one of four raw stages,
+// four steps ahead; warps 4-7 split a landed
+// raw stage into the B planes of one of two plane stages and fence them to
+// the async proxy; warp 2 bulk-copies the step's A planes into the same plane
+// stage; warp 1 issues the twelve MMAs.  B crosses HBM once as words instead
+// of being read, written as planes and read again.
+constexpr int kFThreads = 256;
+constexpr int kFPlaneStages = 2;
+constexpr int kFRawStages = 4;
+constexpr uint32_t kFRawHalf = kTK * kTN * 8;                          // 16 KB: 32 rows x 64 words
+constexpr uint32_t kFRawStage = 2 * kFRawHalf;                         // B words, then the addend's
+constexpr uint32_t kFRawOffset = kFPlaneStages * kStageBytes;           // 96 KB of plane stages
+constexpr uint32_t kFCtrl = kFRawOffset + kFRawStages * kFRawStage;     // 224 KB
+constexpr uint32_t kFSmemBytes = kFCtrl + 256;
+
+// Tensor maps of B and the addend per piece: m[2 p] = B_p, m[2 p + 1] = its
+// addend; 3-D {N, K, batch} u64, box {64, 32, 1}, zero fill out of range.
+struct alignas(64) BMaps {
+  CUtensorMap m[4];
+};
+
+// One box of 32 K-rows x 64 words at (n0, k0, batch) into shared memory.
+__device__ __forceinline__ void tma_load_box(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kFThreads, 1)
+    ring_gemm_tc_fused_kernel(const __grid_constant__ RingGemmLaunch g, const __grid_constant__ BMaps bm) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int b = blockIdx.z / g.splits, split = blockIdx.z % g.splits;
+  const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t ctrl = sbase + kFCtrl;
+  const uint32_t pfull0 = ctrl, pempty0 = ctrl + 16, rfull0 = ctrl + 32, rempty0 = ctrl + 64, done = ctrl + 96;
+  const uint32_t slot = ctrl + 104;
+  volatile uint32_t* err = reinterpret_cast<volatile uint32_t*>(smem + kFCtrl + 112);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kFCtrl + 104);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (t == 0) {
+    for (int i = 0; i < kFPlaneStages; i++) {
+      mbar_init(pfull0 + 8 * i, 1 + 4);  // the A copy's arrival + the four converter warps
+      mbar_init(pempty0 + 8 * i, 1);
+    }
+    for (int i = 0; i < kFRawStages; i++) {
+      mbar_init(rfull0 + 8 * i, 1);
+      mbar_init(rempty0 + 8 * i, 4);
+    }
+    mbar_init(done, 1);
+    *err = 0;
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  const int per = (g.steps + g.splits - 1) / g.splits;
+  const int c0 = split * per, c1 = c0 + per < g.steps ? c0 + per : g.steps;
+  const int nsteps = c1 > c0 ? c1 - c0 : 0;
+  const uint8_t* xp = g.xplanes + static_cast<size_t>(b) * g.xps;
+  const int tiles_m = g.m_pad / kTM;
+  const int K = g.K, N = g.N, cpp = (K + kTK - 1) / kTK;
+  const int cnt = N - n0 < kTN ? N - n0 : kTN;  // valid words of each raw row (the rest read as zero)
+
+  if (warp == 0) {  // raw B (and addend) rows of each step
+    for (int li = 0; li < nsteps; li++) {
+      const int rs = li % kFRawStages;
+      int go = 1;
+      if (lane == 0) {
+        go = li < kFRawStages || mbar_wait(rempty0 + 8 * rs, static_cast<uint32_t>(((li / kFRawStages) - 1) & 1));
+        if (go) {
+          const int c = c0 + li;
+          const int p = c >= cpp ? 1 : 0;
+          const bool add = (p ? g.piece[1].y2 : g.piece[0].y2) != nullptr;
+          const int zb = (p ? g.piece[1].ys : g.piece[0].ys) ? b : 0;
+          const int za = (p ? g.piece[1].y2s : g.piece[0].y2s) ? b : 0;
+          const int k0 = (c % cpp) * kTK;
+          const uint32_t rb = sbase + kFRawOffset + static_cast<uint32_t>(rs) * kFRawStage;
+          mbar_expect_tx(rfull0 + 8 * rs, add ? kFRawStage : kFRawHalf);
+          tma_load_box(rb, &bm.m[2 * p], n0, k0, zb, rfull0 + 8 * rs);
+          if (add) tma_load_box(rb + kFRawHalf, &bm.m[2 * p + 1], n0, k0, za, rfull0 + 8 * rs);
+        } else {
+          *err = 1;
         }
       }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
     }
+  } else if (warp == 2) {  // A planes of each step
+    for (int li = 0; li < nsteps; li++) {
+      const int ps = li % kFPlaneStages;
+      int go = 1;
+      if (lane == 0) {
+        go = li < kFPlaneStages ||
+             mbar_wait(pempty0 + 8 * ps, static_cast<uint32_t>(((li / kFPlaneStages) - 1) & 1));
+        if (go) {
+          mbar_expect_tx(pfull0 + 8 * ps, 8 * kPlaneX);
+          const size_t c = static_cast<size_t>(c0 + li);
+          bulk_copy(sbase + static_cast<uint32_t>(ps) * kStageBytes, xp + (c * tiles_m + blockIdx.y) * (8 * kPlaneX),
+                    8 * kPlaneX, pfull0 + 8 * ps);
+        } else {
+          *err = 1;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+    }
+  } else if (warp == 1) {  // MMA issuer
+    uint64_t ad[8], bd[8];
+    uint32_t dt[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      ad[i] = umma_desc(sbase + static_cast<uint32_t>(i) * kPlaneX);
+      bd[i] = umma_desc(sbase + 8 * kPlaneX + static_cast<uint32_t>(i) * kPlaneY);
+      dt[i] = tmem + static_cast<uint32_t>(i * kTN);
+    }
+    for (int li = 0; li < nsteps; li++) {
+      const int ps = li % kFPlaneStages;
+      int go = 1;
+      if (lane == 0) {
+        go = mbar_wait(pfull0 + 8 * ps, static_cast<uint32_t>((li / kFPlaneStages) & 1));
+        if (go) {
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t so = static_cast<uint64_t>((static_cast<uint32_t>(ps) * kStageBytes) >> 4);
+          uint64_t as[8], bs[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            as[i] = ad[i] + so;
+            bs[i] = bd[i] + so;
+          }
+          mma_step(dt, as, bs, li > 0 ? 1u : 0u);
+          umma_commit(pempty0 + 8 * ps);
+        } else {
+          *err = 1;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+    }
+    if (lane == 0) umma_commit(done);
+    __syncwarp();
+  } else if (warp >= 4) {  // converters: a landed raw stage into the B planes of a plane stage
+    const int ct = (warp - 4) * 32 + lane;
+    const int r = ct % kTN, h = ct / kTN;  // B-tile row (output column n0 + r) and K half
+    for (int li = 0; li < nsteps; li++) {
+      const int rs = li % kFRawStages, ps = li % kFPlaneStages;
+      int go = 1;
+      if (lane == 0)
+        go = mbar_wait(rfull0 + 8 * rs, static_cast<uint32_t>((li / kFRawStages) & 1)) &&
+             (li < kFPlaneStages ||
+              mbar_wait(pempty0 + 8 * ps, static_cast<uint32_t>(((li / kFPlaneStages) - 1) & 1)));
+      if (!__shfl_sync(0xffffffffu, go, 0)) {
+        if (lane == 0) *err = 1;
+        break;
+      }
+      const int c = c0 + li;
+      const bool add = (c >= cpp ? g.piece[1].y2 : g.piece[0].y2) != nullptr;
+      const int k0 = (c % cpp) * kTK;
+      const uint64_t* raw = reinterpret_cast<const uint64_t*>(smem + kFRawOffset + rs * kFRawStage);
+      uint64_t v[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const int kk = 16 * h + j;
+        uint64_t val = 0;
+        if (k0 + kk < K && r < cnt) {
+          val = raw[kk * kTN + r];
+          if (add) val += raw[kFRawHalf / 8 + kk * kTN + r];
+        }
+        v[j] = val;
+      }
+      uint8_t* yt = smem + static_cast<size_t>(ps) * kStageBytes + 8 * kPlaneX + core_off(r, h);
+#pragma unroll
+      for (int i = 0; i < 8; i++) *reinterpret_cast<uint4*>(yt + i * kPlaneY) = plane_bytes(v, i);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(rempty0 + 8 * rs);
+        mbar_arrive(pfull0 + 8 * ps);
+      }
+    }
+  }
+  bool ok = mbar_wait(done, 0);
+  ok = __syncthreads_and(ok ? 1 : 0) != 0 && *err == 0;
+  if (!ok) {
+    if (t == 0) atomicOr(g.status, kStatusTimeout);
+    mbar_wait(done, 0);
+  } else if (nsteps > 0 && warp < 4) {
+    epilogue(g, tmem, warp, lane, b, split, m0, n0);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -381,6 +625,38 @@ __global__ void ring_gemm_reduce_kernel(const RingGemmLaunch g) {
     if (g.bias) val += static_cast<uint64_t>(g.bias[o % g.N]);
     g.out[b * g.os + o] = scaled_acc(val, g.has_scale, g.mul_const, g.mul_shift);
   }
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_tiled() {
+  static const EncodeTiled fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiled>(nullptr);
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+// B (K x N u64, row-major; per-batch stride ys words, 0 = shared) as a 3-D
+// tensor map with 32 x 64-word boxes; false when it cannot be encoded.
+bool make_b_map(CUtensorMap* m, const uint64_t* y, size_t ys, int N, int K, int batches) {
+  const EncodeTiled enc = encode_tiled();
+  if (!enc || !y) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K),
+                              static_cast<cuuint64_t>(ys ? batches : 1)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(N) * 8,
+                                 static_cast<cuuint64_t>(ys ? ys : static_cast<size_t>(N) * K) * 8};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTN), static_cast<cuuint32_t>(kTK), 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint64_t*>(y), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -409,7 +685,19 @@ cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int 
   }
   const size_t xbytes = static_cast<size_t>(g.steps) * 8 * g.m_pad * kTK;
   const size_t ybytes = static_cast<size_t>(g.steps) * 8 * g.n_pad * kTK;
-  const int xb = x_per_batch ? batches : 1, yb = y_per_batch ? batches : 1;
+  // B split inside the GEMM when its rows can be bulk-copied: row-major,
+  // N even (16-byte row starts), 16-byte bases and even per-batch strides
+  bool fused = !g.trans && g.N % 2 == 0 && g.N >= kTN && g.K >= kTK;
+  for (int p = 0; p < g.npieces; p++) {
+    fused = fused && (reinterpret_cast<uintptr_t>(g.piece[p].y) & 15u) == 0 && g.piece[p].ys % 2 == 0;
+    if (g.piece[p].y2) fused = fused && (reinterpret_cast<uintptr_t>(g.piece[p].y2) & 15u) == 0 && g.piece[p].y2s % 2 == 0;
+  }
+  BMaps bm{};
+  for (int p = 0; p < g.npieces && fused; p++) {
+    fused = make_b_map(&bm.m[2 * p], g.piece[p].y, g.piece[p].ys, g.N, g.K, batches);
+    if (fused && g.piece[p].y2) fused = make_b_map(&bm.m[2 * p + 1], g.piece[p].y2, g.piece[p].y2s, g.N, g.K, batches);
+  }
+  const int xb = x_per_batch ? batches : 1, yb = fused ? 0 : (y_per_batch ? batches : 1);
   g.batches = batches;
   const size_t ws_bytes =
       g.splits > 1 ? static_cast<size_t>(g.splits) * batches * static_cast<size_t>(g.M) * g.N * 8 : 0;
@@ -451,7 +739,7 @@ cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int 
     const size_t want = (units + 255) / 256;
     return static_cast<int>(want < 8192 ? (want ? want : 1) : 8192);
   };
-  const int xblocks = split_blocks(px), yblocks = split_blocks(py);
+  const int xblocks = split_blocks(px), yblocks = fused ? 0 : split_blocks(py);
   if (e == cudaSuccess) {
     const dim3 sgrid(static_cast<unsigned>(xblocks + yblocks), static_cast<unsigned>(xb > yb ? xb : yb));
     split_planes_kernel<<<sgrid, 256, 0, st>>>(px, py, xblocks, xb, yb);
@@ -459,11 +747,20 @@ cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int 
   }
   const dim3 grid(static_cast<unsigned>(tiles_n), static_cast<unsigned>(tiles_m),
                   static_cast<unsigned>(batches * g.splits));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(ring_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e == cudaSuccess) {
-    ring_gemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(g);
-    e = cudaGetLastError();
+  if (fused) {
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ring_gemm_tc_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmemBytes);
+    if (e == cudaSuccess) {
+      ring_gemm_tc_fused_kernel<<<grid, kFThreads, kFSmemBytes, st>>>(g, bm);
+      e = cudaGetLastError();
+    }
+  } else {
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ring_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e == cudaSuccess) {
+      ring_gemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(g);
+      e = cudaGetLastError();
+    }
   }
   if (e == cudaSuccess && g.splits > 1) {
     const size_t want = (static_cast<size_t>(batches) * g.M * g.N + 255) / 256;

@@ -358,8 +358,8 @@ def _ring_gemm_schedule():
 
 def test_ring_gemm_schedule_covers_every_limb_pair_once():
     src = (Path(__file__).resolve().parents[1] / "suf_b200" / "csrc" / "ring_gemm_tc.cu").read_text()
-    for pat in (r"umma_i8\(dt\[0\], as\[0\], bs\[0\], idesc_n\(256\), first\)",
-                r"umma_i8\(dt\[4\], as\[0\], bs\[4\], idesc_n\(256\), first\)",
+    for pat in (r"umma_i8\(dt\[0\], as\[0\], bs\[0\], idesc_n\(256\), accumulate\)",
+                r"umma_i8\(dt\[4\], as\[0\], bs\[4\], idesc_n\(256\), accumulate\)",
                 r"for \(int i = 1; i < 8; i\+\+\) umma_i8\(dt\[i\], as\[i\], bs\[0\], idesc_n\(i <= 4 \? 256 : 64 \* \(8 - i\)\), 1u\)",
                 r"for \(int i = 1; i < 4; i\+\+\) umma_i8\(dt\[i \+ 4\], as\[i\], bs\[4\], idesc_n\(256 - 64 \* i\), 1u\)"):
         assert re.search(pat, src), pat
