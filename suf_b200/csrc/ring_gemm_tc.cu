@@ -25,8 +25,8 @@
 // the step and commits them back to the stage's "empty" mbarrier (one lane of
 // each does the issuing), and all warps read the diagonals out of tensor
 // memory at the end.  Every wait is bounded.  When B is row-major with
-// 16-byte rows, B's planes are instead made inside the GEMM from raw rows
-// bulk-copied four steps ahead (ring_gemm_tc_fused_kernel), so B crosses HBM
+// 16-byte rows, B's planes are instead made inside the GEMM from raw boxes
+// loaded by tensor-map TMA (ring_gemm_tc_fused_kernel), so B crosses HBM
 // once, as words.
 // Contractions too short to fill the GPU are split across CTAs: each stores
 // its partial tile (plain stores, no atomics), and a coalesced reduction
@@ -409,19 +409,21 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
 // are made inside the GEMM instead of by the pre-pass: warp 0 loads each
 // step's raw 32 x 64 words of B (and of the Beaver addend) with one tiled
 // tensor-map load per matrix (no multicast; x = n0 is a multiple of 64 words,
-// out-of-range rows and columns read as zero) into one of four raw stages,
-// four steps ahead; warps 4-7 split a landed
-// raw stage into the B planes of one of two plane stages and fence them to
-// the async proxy; warp 2 bulk-copies the step's A planes into the same plane
-// stage; warp 1 issues the twelve MMAs.  B crosses HBM once as words instead
-// of being read, written as planes and read again.
+// out-of-range rows and columns read as zero) into one of two raw stages;
+// warps 4-7 split a landed raw stage into the B planes of one of three plane
+// stages and fence them to the async proxy; warp 2 bulk-copies the step's A
+// planes into the same plane stage; warp 1 issues the twelve MMAs.  B crosses
+// HBM once as words instead of being read, written as planes and read again.
+// (Three plane stages decouple the conversion of step i from the MMAs of
+// step i - 2; two were 2 % slower, and one bulk copy per 512-byte row instead
+// of one tensor-map load per box cost 34 us per FFN1 call in issue overhead.)
 constexpr int kFThreads = 256;
-constexpr int kFPlaneStages = 2;
-constexpr int kFRawStages = 4;
+constexpr int kFPlaneStages = 3;
+constexpr int kFRawStages = 2;
 constexpr uint32_t kFRawHalf = kTK * kTN * 8;                          // 16 KB: 32 rows x 64 words
 constexpr uint32_t kFRawStage = 2 * kFRawHalf;                         // B words, then the addend's
-constexpr uint32_t kFRawOffset = kFPlaneStages * kStageBytes;           // 96 KB of plane stages
-constexpr uint32_t kFCtrl = kFRawOffset + kFRawStages * kFRawStage;     // 224 KB
+constexpr uint32_t kFRawOffset = kFPlaneStages * kStageBytes;           // 144 KB of plane stages
+constexpr uint32_t kFCtrl = kFRawOffset + kFRawStages * kFRawStage;     // 208 KB
 constexpr uint32_t kFSmemBytes = kFCtrl + 256;
 
 // Tensor maps of B and the addend per piece: m[2 p] = B_p, m[2 p + 1] = its
@@ -446,11 +448,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
   const int b = blockIdx.z / g.splits, split = blockIdx.z % g.splits;
   const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
   const uint32_t sbase = smem_u32(smem);
+  constexpr uint32_t kOffPE = 8 * kFPlaneStages, kOffRF = 16 * kFPlaneStages, kOffRE = kOffRF + 8 * kFRawStages,
+                     kOffDone = kOffRE + 8 * kFRawStages;
+  static_assert(kOffDone + 24 <= 256, "control block");
   const uint32_t ctrl = sbase + kFCtrl;
-  const uint32_t pfull0 = ctrl, pempty0 = ctrl + 16, rfull0 = ctrl + 32, rempty0 = ctrl + 64, done = ctrl + 96;
-  const uint32_t slot = ctrl + 104;
-  volatile uint32_t* err = reinterpret_cast<volatile uint32_t*>(smem + kFCtrl + 112);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kFCtrl + 104);
+  const uint32_t pfull0 = ctrl, pempty0 = ctrl + kOffPE, rfull0 = ctrl + kOffRF, rempty0 = ctrl + kOffRE;
+  const uint32_t done = ctrl + kOffDone, slot = done + 8;
+  volatile uint32_t* err = reinterpret_cast<volatile uint32_t*>(smem + kFCtrl + kOffDone + 16);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kFCtrl + kOffDone + 8);
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(kTmemCols)
