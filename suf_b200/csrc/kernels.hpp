@@ -162,8 +162,7 @@ struct RingGemmLaunch {
   uint32_t* status;
   // set by the launcher
   int batches;
-  int splits;        // contraction split across CTAs
-  uint64_t* ws;      // split partials [split][batch][M][N]
+  int splits;        // contraction split across the CTAs of one cluster
   int steps;         // 32-deep steps over all pieces
   int m_pad, n_pad;  // rows of the plane slabs (multiples of 128 / 64)
   const uint8_t* xplanes;

@@ -28,14 +28,15 @@
 // 16-byte rows, B's planes are instead made inside the GEMM from raw boxes
 // loaded by tensor-map TMA (ring_gemm_tc_fused_kernel), so B crosses HBM
 // once, as words.
-// Contractions too short to fill the GPU are split across CTAs: each stores
-// its partial tile (plain stores, no atomics), and a coalesced reduction
-// kernel adds the partials (addition mod 2^64 commutes), C and the bias and
-// applies the rescale.
+// Contractions too short to fill the GPU are split across the CTAs of one
+// thread-block cluster per output tile, which sum their partial tiles through
+// distributed shared memory and store the result once.
 //
 // Serves the reference's Beaver matmul (cuda/cuda_primitives.cu:391-628,
 // out = C + D B + A E (+ D E for party 0) as ONE product [D | A] x [B (+E) ; E])
 // and the public-weight matmul (src/nn/matmul_gpu.cu:21-117, Y = X W + bias).
+#include <atomic>
+
 #include <cuda.h>  // CUtensorMap and its enums (the encoder comes from cudaGetDriverEntryPoint)
 
 #include "kernels.hpp"
@@ -186,17 +187,55 @@ __device__ __forceinline__ void mma_step(const uint32_t (&dt)[8], const uint64_t
   for (int i = 1; i < 4; i++) umma_i8(dt[i + 4], as[i], bs[4], idesc_n(256 - 64 * i), 1u);
 }
 
-// Warps 0-3 (TMEM lane quarter = warp): fold the 8 diagonals of the tile's
-// 128 x 64 accumulators and store the result (or a split's raw partial).
-__device__ __forceinline__ void epilogue(const RingGemmLaunch& g, uint32_t tmem, int warp, int lane, int b, int split,
-                                         int m0, int n0) {
-  const int M = g.M, N = g.N;
+// ---- Epilogue: the K-split CTAs of a tile are one thread-block cluster ----
+// Every CTA folds its 8 diagonals into a 128 x 64 word tile in its own shared
+// memory (the pipeline stages are idle by then); after a cluster barrier each
+// of the S ranks sums a 1/S share of the tile's 16-byte chunks over all S
+// tiles through distributed shared memory, adds C and the bias, rescales and
+// stores it with coalesced rows.  A second barrier keeps every rank's tile
+// alive until its readers are done.  S = 1 takes the same path.  (Split
+// partials through global memory cost an 8 us epilogue of one-row-per-thread
+// stores plus a 6 us reduction kernel per FFN1 call.)
+constexpr int kChunks = kTM * kTN / 2;  // 16-byte chunks of a tile
+
+// Chunk c (words 2c, 2c+1) of tile row `row`; chunks XOR-swizzled by row so
+// both the row-per-thread fold and the chunk-per-thread reduction are free
+// of bank conflicts.
+__device__ __forceinline__ uint32_t tile_chunk(int row, int c) {
+  return static_cast<uint32_t>(row * (kTN * 8) + ((c ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+// 16 bytes at the same shared-memory offset in cluster rank `rank`.
+__device__ __forceinline__ void ld_rank16(uint32_t saddr, uint32_t rank, uint64_t& x, uint64_t& y) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(saddr), "r"(rank));
+  asm volatile("ld.shared::cluster.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "r"(a) : "memory");
+}
+
+// Warps 0-3 (TMEM lane quarter = warp): the folded tile, sum_s (P_s mod
+// 2^32) << 8s per word, into this CTA's shared memory.
+__device__ __forceinline__ void fold_tile(uint32_t tmem, int warp, int lane, uint8_t* tile) {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const int m = m0 + warp * 32 + lane;
-  const uint64_t* C = g.c ? g.c + static_cast<size_t>(b) * g.cs : nullptr;
-  uint64_t* O = g.out + static_cast<size_t>(b) * g.os;
-  // a split CTA stores its raw partial; the reduction kernel finishes the sum
-  uint64_t* W = g.splits > 1 ? g.ws + (static_cast<size_t>(split) * g.batches + b) * M * N : nullptr;
+  const int row = warp * 32 + lane;
 #pragma unroll 1
   for (int cb = 0; cb < kTN / 16; cb++) {
     uint32_t v[8][16];  // the 8 diagonals of 16 columns, loaded before one wait
@@ -205,25 +244,72 @@ __device__ __forceinline__ void epilogue(const RingGemmLaunch& g, uint32_t tmem,
       tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(s * kTN + cb * 16), v[s]);
 #pragma unroll
     for (int s = 0; s < 8; s++) tmem_wait(v[s]);
-    if (m < M) {
 #pragma unroll
-      for (int j = 0; j < 16; j++) {
-        uint64_t acc = 0;
+    for (int q = 0; q < 8; q++) {
+      uint64_t a0 = 0, a1 = 0;
 #pragma unroll
-        for (int s = 0; s < 8; s++) acc += static_cast<uint64_t>(v[s][j]) << (8 * s);
-        const int n = n0 + cb * 16 + j;
-        if (n < N) {
-          const size_t o = static_cast<size_t>(m) * N + n;
-          if (W) {
-            W[o] = acc;
-          } else {
-            if (C) acc += C[o];
-            if (g.bias) acc += static_cast<uint64_t>(g.bias[n]);
-            O[o] = scaled_acc(acc, g.has_scale, g.mul_const, g.mul_shift);
-          }
-        }
+      for (int s = 0; s < 8; s++) {
+        a0 += static_cast<uint64_t>(v[s][2 * q]) << (8 * s);
+        a1 += static_cast<uint64_t>(v[s][2 * q + 1]) << (8 * s);
       }
+      *reinterpret_cast<ulonglong2*>(tile + tile_chunk(row, cb * 8 + q)) = make_ulonglong2(a0, a1);
     }
+  }
+}
+
+// All threads: this rank's share of the tile, summed over the cluster's
+// tiles (addition mod 2^64 commutes), plus C and the bias, rescaled, stored.
+__device__ __forceinline__ void reduce_tile(const RingGemmLaunch& g, int b, int m0, int n0, uint32_t tile, int t,
+                                            int nthr) {
+  const uint32_t S = cluster_size(), q = cluster_rank();
+  const int lo = static_cast<int>(q * kChunks / S), hi = static_cast<int>((q + 1) * kChunks / S);
+  const uint64_t* C = g.c ? g.c + static_cast<size_t>(b) * g.cs : nullptr;
+  uint64_t* O = g.out + static_cast<size_t>(b) * g.os;
+  for (int ch = lo + t; ch < hi; ch += nthr) {
+    const int row = ch / (kTN / 2), c = ch % (kTN / 2);
+    const int m = m0 + row, n = n0 + 2 * c;
+    if (m >= g.M || n >= g.N) continue;
+    const uint32_t a = tile + tile_chunk(row, c);
+    uint64_t s0 = 0, s1 = 0;
+#pragma unroll 4
+    for (uint32_t r = 0; r < S; r++) {
+      uint64_t x, y;
+      ld_rank16(a, r, x, y);
+      s0 += x;
+      s1 += y;
+    }
+    const size_t o = static_cast<size_t>(m) * g.N + n;
+    if (C) s0 += C[o];
+    if (g.bias) s0 += static_cast<uint64_t>(g.bias[n]);
+    O[o] = scaled_acc(s0, g.has_scale, g.mul_const, g.mul_shift);
+    if (n + 1 < g.N) {
+      if (C) s1 += C[o + 1];
+      if (g.bias) s1 += static_cast<uint64_t>(g.bias[n + 1]);
+      O[o + 1] = scaled_acc(s1, g.has_scale, g.mul_const, g.mul_shift);
+    }
+  }
+}
+
+// The common tail of both GEMM kernels: fold, reduce over the cluster, free
+// the tensor memory.  Every thread of every rank reaches both cluster
+// barriers, on the error path too.
+__device__ __forceinline__ void finish_tile(const RingGemmLaunch& g, uint8_t* smem, uint32_t tmem, bool ok, int nsteps,
+                                            int warp, int lane, int t, int b, int m0, int n0) {
+  if (ok && warp < 4) {
+    if (nsteps > 0) {
+      fold_tile(tmem, warp, lane, smem);
+    } else {
+      for (int c = 0; c < kTN / 2; c++)
+        *reinterpret_cast<ulonglong2*>(smem + tile_chunk(warp * 32 + lane, c)) = make_ulonglong2(0, 0);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  cluster_sync_all();  // every rank's tile is in its shared memory
+  reduce_tile(g, b, m0, n0, smem_u32(smem), t, static_cast<int>(blockDim.x));
+  cluster_sync_all();  // every reader of this CTA's tile is done
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
 }
 
@@ -281,7 +367,11 @@ __device__ __forceinline__ void split_planes(const PlanesSplit& p, int block, in
 
 // Both operands in one launch: blocks [0, xblocks) split A, the rest split B
 // (blockIdx.y = batch, for an operand with per-batch planes).
+// The GEMM after it is launched as its programmatic dependent: it may start
+// its prologue and B loads at once and waits (griddepcontrol.wait) only
+// before it reads the planes written here.
 __global__ void split_planes_kernel(const PlanesSplit px, const PlanesSplit py, int xblocks, int xb, int yb) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int b = blockIdx.y;
   if (static_cast<int>(blockIdx.x) < xblocks) {
     if (b < xb) split_planes(px, blockIdx.x, xblocks, b);
@@ -332,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
   // its warp sit at the warp's shuffle, so no lane of the issuing warp spins
   // on a different barrier than the one lane 0 is serving.
   if (warp == 0) {  // producer: one bulk copy per operand per step
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the planes of the pre-pass
     for (int li = 0; li < nsteps; li++) {
       const int st = li % kStages;
       const uint32_t sb = sbase + static_cast<uint32_t>(st) * kStageBytes;
@@ -393,15 +484,8 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
   if (!ok) {
     if (t == 0) atomicOr(g.status, kStatusTimeout);
     mbar_wait(done, 0);  // let whatever was issued drain before the columns are released
-  } else if (nsteps > 0) {
-    epilogue(g, tmem, warp, lane, b, split, m0, n0);
   }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  if (warp == 0) {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
-  }
+  finish_tile(g, smem, tmem, ok, nsteps, warp, lane, t, b, m0, n0);
 }
 
 // ---- B split inside the GEMM --------------------------------------------
@@ -409,22 +493,29 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
 // are made inside the GEMM instead of by the pre-pass: warp 0 loads each
 // step's raw 32 x 64 words of B (and of the Beaver addend) with one tiled
 // tensor-map load per matrix (no multicast; x = n0 is a multiple of 64 words,
-// out-of-range rows and columns read as zero) into one of two raw stages;
-// warps 4-7 split a landed raw stage into the B planes of one of three plane
-// stages and fence them to the async proxy; warp 2 bulk-copies the step's A
-// planes into the same plane stage; warp 1 issues the twelve MMAs.  B crosses
-// HBM once as words instead of being read, written as planes and read again.
-// (Three plane stages decouple the conversion of step i from the MMAs of
-// step i - 2; two were 2 % slower, and one bulk copy per 512-byte row instead
-// of one tensor-map load per box cost 34 us per FFN1 call in issue overhead.)
+// out-of-range rows and columns read as zero) into one of three raw stages;
+// warps 4-7 split a landed raw stage into one of two B-plane stages and fence
+// them to the async proxy; warp 2 bulk-copies the step's A planes into one of
+// three A stages; warp 1 issues the twelve MMAs and commits the A and B stages
+// back.  B crosses HBM once as words instead of being read, written as planes
+// and read again.  The three kinds of stage are separate rings so that the
+// raw stage is free again as soon as it is split: the main loop is bound by
+// the latency of the raw loads (about 2 us per load with all SMs loading),
+// so the smem goes to keeping more of them in flight.
 constexpr int kFThreads = 256;
-constexpr int kFPlaneStages = 3;
-constexpr int kFRawStages = 2;
-constexpr uint32_t kFRawHalf = kTK * kTN * 8;                          // 16 KB: 32 rows x 64 words
-constexpr uint32_t kFRawStage = 2 * kFRawHalf;                         // B words, then the addend's
-constexpr uint32_t kFRawOffset = kFPlaneStages * kStageBytes;           // 144 KB of plane stages
-constexpr uint32_t kFCtrl = kFRawOffset + kFRawStages * kFRawStage;     // 208 KB
+constexpr int kFAStages = 3;
+constexpr int kFBStages = 2;
+constexpr int kFRawStages = 3;
+constexpr uint32_t kFAStage = 8 * kPlaneX;                            // 32 KB of A planes
+constexpr uint32_t kFBStage = 8 * kPlaneY;                            // 16 KB of B planes
+constexpr uint32_t kFRawHalf = kTK * kTN * 8;                         // 16 KB: 32 rows x 64 words
+constexpr uint32_t kFRawStage = 2 * kFRawHalf;                        // B words, then the addend's
+constexpr uint32_t kFBOffset = kFAStages * kFAStage;                  // 96 KB
+constexpr uint32_t kFRawOffset = kFBOffset + kFBStages * kFBStage;    // 128 KB
+constexpr uint32_t kFCtrl = kFRawOffset + kFRawStages * kFRawStage;   // 224 KB
 constexpr uint32_t kFSmemBytes = kFCtrl + 256;
+static_assert(kFSmemBytes <= 227 * 1024, "dynamic shared memory per CTA");
+static_assert(kFCtrl >= kTM * kTN * 8, "the epilogue tile reuses the stages");
 
 // Tensor maps of B and the addend per piece: m[2 p] = B_p, m[2 p + 1] = its
 // addend; 3-D {N, K, batch} u64, box {64, 32, 1}, zero fill out of range.
@@ -448,11 +539,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
   const int b = blockIdx.z / g.splits, split = blockIdx.z % g.splits;
   const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
   const uint32_t sbase = smem_u32(smem);
-  constexpr uint32_t kOffPE = 8 * kFPlaneStages, kOffRF = 16 * kFPlaneStages, kOffRE = kOffRF + 8 * kFRawStages,
+  // control block: full/empty mbarriers of the A, B-plane and raw rings
+  constexpr uint32_t kOffAE = 8 * kFAStages, kOffBF = 16 * kFAStages, kOffBE = kOffBF + 8 * kFBStages,
+                     kOffRF = kOffBE + 8 * kFBStages, kOffRE = kOffRF + 8 * kFRawStages,
                      kOffDone = kOffRE + 8 * kFRawStages;
   static_assert(kOffDone + 24 <= 256, "control block");
   const uint32_t ctrl = sbase + kFCtrl;
-  const uint32_t pfull0 = ctrl, pempty0 = ctrl + kOffPE, rfull0 = ctrl + kOffRF, rempty0 = ctrl + kOffRE;
+  const uint32_t afull0 = ctrl, aempty0 = ctrl + kOffAE, bfull0 = ctrl + kOffBF, bempty0 = ctrl + kOffBE;
+  const uint32_t rfull0 = ctrl + kOffRF, rempty0 = ctrl + kOffRE;
   const uint32_t done = ctrl + kOffDone, slot = done + 8;
   volatile uint32_t* err = reinterpret_cast<volatile uint32_t*>(smem + kFCtrl + kOffDone + 16);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kFCtrl + kOffDone + 8);
@@ -463,9 +557,13 @@ __global__ void __launch_bounds__(kFThreads, 1)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (t == 0) {
-    for (int i = 0; i < kFPlaneStages; i++) {
-      mbar_init(pfull0 + 8 * i, 1 + 4);  // the A copy's arrival + the four converter warps
-      mbar_init(pempty0 + 8 * i, 1);
+    for (int i = 0; i < kFAStages; i++) {
+      mbar_init(afull0 + 8 * i, 1);  // the A copy's arrival (with its transaction bytes)
+      mbar_init(aempty0 + 8 * i, 1);
+    }
+    for (int i = 0; i < kFBStages; i++) {
+      mbar_init(bfull0 + 8 * i, 4);  // the four converter warps
+      mbar_init(bempty0 + 8 * i, 1);
     }
     for (int i = 0; i < kFRawStages; i++) {
       mbar_init(rfull0 + 8 * i, 1);
@@ -511,17 +609,17 @@ __global__ void __launch_bounds__(kFThreads, 1)
       if (!__shfl_sync(0xffffffffu, go, 0)) break;
     }
   } else if (warp == 2) {  // A planes of each step
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // written by the pre-pass
     for (int li = 0; li < nsteps; li++) {
-      const int ps = li % kFPlaneStages;
+      const int as = li % kFAStages;
       int go = 1;
       if (lane == 0) {
-        go = li < kFPlaneStages ||
-             mbar_wait(pempty0 + 8 * ps, static_cast<uint32_t>(((li / kFPlaneStages) - 1) & 1));
+        go = li < kFAStages || mbar_wait(aempty0 + 8 * as, static_cast<uint32_t>(((li / kFAStages) - 1) & 1));
         if (go) {
-          mbar_expect_tx(pfull0 + 8 * ps, 8 * kPlaneX);
+          mbar_expect_tx(afull0 + 8 * as, kFAStage);
           const size_t c = static_cast<size_t>(c0 + li);
-          bulk_copy(sbase + static_cast<uint32_t>(ps) * kStageBytes, xp + (c * tiles_m + blockIdx.y) * (8 * kPlaneX),
-                    8 * kPlaneX, pfull0 + 8 * ps);
+          bulk_copy(sbase + static_cast<uint32_t>(as) * kFAStage, xp + (c * tiles_m + blockIdx.y) * kFAStage,
+                    kFAStage, afull0 + 8 * as);
         } else {
           *err = 1;
         }
@@ -534,25 +632,30 @@ __global__ void __launch_bounds__(kFThreads, 1)
 #pragma unroll
     for (int i = 0; i < 8; i++) {
       ad[i] = umma_desc(sbase + static_cast<uint32_t>(i) * kPlaneX);
-      bd[i] = umma_desc(sbase + 8 * kPlaneX + static_cast<uint32_t>(i) * kPlaneY);
+      bd[i] = umma_desc(sbase + kFBOffset + static_cast<uint32_t>(i) * kPlaneY);
       dt[i] = tmem + static_cast<uint32_t>(i * kTN);
     }
     for (int li = 0; li < nsteps; li++) {
-      const int ps = li % kFPlaneStages;
+      const int as = li % kFAStages, bs = li % kFBStages;
       int go = 1;
       if (lane == 0) {
-        go = mbar_wait(pfull0 + 8 * ps, static_cast<uint32_t>((li / kFPlaneStages) & 1));
+        go = mbar_wait(afull0 + 8 * as, static_cast<uint32_t>((li / kFAStages) & 1)) &&
+             mbar_wait(bfull0 + 8 * bs, static_cast<uint32_t>((li / kFBStages) & 1));
         if (go) {
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint64_t so = static_cast<uint64_t>((static_cast<uint32_t>(ps) * kStageBytes) >> 4);
-          uint64_t as[8], bs[8];
+          // descriptors of stage 0 plus the stage's byte offset >> 4 (addresses
+          // stay below 2^18, so the start field never carries)
+          const uint64_t ao = static_cast<uint64_t>((static_cast<uint32_t>(as) * kFAStage) >> 4);
+          const uint64_t bo = static_cast<uint64_t>((static_cast<uint32_t>(bs) * kFBStage) >> 4);
+          uint64_t a[8], bb[8];
 #pragma unroll
           for (int i = 0; i < 8; i++) {
-            as[i] = ad[i] + so;
-            bs[i] = bd[i] + so;
+            a[i] = ad[i] + ao;
+            bb[i] = bd[i] + bo;
           }
-          mma_step(dt, as, bs, li > 0 ? 1u : 0u);
-          umma_commit(pempty0 + 8 * ps);
+          mma_step(dt, a, bb, li > 0 ? 1u : 0u);
+          umma_commit(aempty0 + 8 * as);
+          umma_commit(bempty0 + 8 * bs);
         } else {
           *err = 1;
         }
@@ -561,16 +664,15 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
     if (lane == 0) umma_commit(done);
     __syncwarp();
-  } else if (warp >= 4) {  // converters: a landed raw stage into the B planes of a plane stage
+  } else if (warp >= 4) {  // converters: a landed raw stage into a B-plane stage
     const int ct = (warp - 4) * 32 + lane;
     const int r = ct % kTN, h = ct / kTN;  // B-tile row (output column n0 + r) and K half
     for (int li = 0; li < nsteps; li++) {
-      const int rs = li % kFRawStages, ps = li % kFPlaneStages;
+      const int rs = li % kFRawStages, bs = li % kFBStages;
       int go = 1;
       if (lane == 0)
         go = mbar_wait(rfull0 + 8 * rs, static_cast<uint32_t>((li / kFRawStages) & 1)) &&
-             (li < kFPlaneStages ||
-              mbar_wait(pempty0 + 8 * ps, static_cast<uint32_t>(((li / kFPlaneStages) - 1) & 1)));
+             (li < kFBStages || mbar_wait(bempty0 + 8 * bs, static_cast<uint32_t>(((li / kFBStages) - 1) & 1)));
       if (!__shfl_sync(0xffffffffu, go, 0)) {
         if (lane == 0) *err = 1;
         break;
@@ -590,14 +692,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
         }
         v[j] = val;
       }
-      uint8_t* yt = smem + static_cast<size_t>(ps) * kStageBytes + 8 * kPlaneX + core_off(r, h);
+      uint8_t* yt = smem + kFBOffset + static_cast<size_t>(bs) * kFBStage + core_off(r, h);
 #pragma unroll
       for (int i = 0; i < 8; i++) *reinterpret_cast<uint4*>(yt + i * kPlaneY) = plane_bytes(v, i);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(rempty0 + 8 * rs);
-        mbar_arrive(pfull0 + 8 * ps);
+        mbar_arrive(bfull0 + 8 * bs);
       }
     }
   }
@@ -606,30 +708,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
   if (!ok) {
     if (t == 0) atomicOr(g.status, kStatusTimeout);
     mbar_wait(done, 0);
-  } else if (nsteps > 0 && warp < 4) {
-    epilogue(g, tmem, warp, lane, b, split, m0, n0);
   }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  if (warp == 0) {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
-  }
-}
-
-// out = scale(sum of the split partials + C + bias), coalesced.
-__global__ void ring_gemm_reduce_kernel(const RingGemmLaunch g) {
-  const size_t mn = static_cast<size_t>(g.M) * g.N, total = mn * static_cast<size_t>(g.batches);
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t b = i / mn, o = i % mn;
-    uint64_t val = 0;
-#pragma unroll 4
-    for (int sp = 0; sp < g.splits; sp++) val += g.ws[(static_cast<size_t>(sp) * g.batches + b) * mn + o];
-    if (g.c) val += g.c[b * g.cs + o];
-    if (g.bias) val += static_cast<uint64_t>(g.bias[o % g.N]);
-    g.out[b * g.os + o] = scaled_acc(val, g.has_scale, g.mul_const, g.mul_shift);
-  }
+  finish_tile(g, smem, tmem, ok, nsteps, warp, lane, t, b, m0, n0);
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -664,6 +744,96 @@ bool make_b_map(CUtensorMap* m, const uint64_t* y, size_t ys, int N, int K, int 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+constexpr int kMaxSplits = 16;  // cluster size; above 8 needs the non-portable opt-in
+constexpr int kMaxDevices = 64;
+// Fixed cost of one wave of tiles (prologue, first loads, epilogue) in
+// pipeline steps, for choosing the split.
+constexpr int kWaveSteps = 6;
+
+// Kernel attributes, once per kernel and device: the dynamic shared memory
+// and the non-portable cluster sizes.
+cudaError_t prepare_kernel(const void* kernel, int which, int device, uint32_t smem) {
+  static std::atomic<int> done[kMaxDevices][2];
+  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (done[device][which].load(std::memory_order_acquire)) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) done[device][which].store(1, std::memory_order_release);
+  return e;
+}
+
+// How many clusters of S CTAs of the kernel are resident at once (clusters
+// stay inside one GPC, so this is below SMs / S where GPCs do not divide
+// evenly); 0 when S does not fit.  Cached per kernel, device and S.
+int resident_clusters(const void* kernel, int which, int device, int threads, uint32_t smem, int S) {
+  static std::atomic<int> cache[kMaxDevices][2][kMaxSplits + 1];
+  const int hit = cache[device][which][S].load(std::memory_order_relaxed);
+  if (hit) return hit - 1;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = static_cast<unsigned>(S);
+  cfg.gridDim = dim3(1, 1, static_cast<unsigned>(S));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  cache[device][which][S].store(n + 1, std::memory_order_relaxed);
+  return n;
+}
+
+// The split S (cluster size) with the least estimated time: waves of
+// resident clusters x (steps per CTA + a wave's fixed cost), keeping at least
+// 4 steps per CTA and every split non-empty.
+int choose_splits(const void* kernel, int which, int device, int threads, uint32_t smem, long long tiles, int steps,
+                  int batches) {
+  int best = 1;
+  long long best_cost = -1;
+  const int smax = steps / 4 < kMaxSplits ? steps / 4 : kMaxSplits;
+  for (int S = 1; S <= (smax > 1 ? smax : 1); S++) {
+    const int per = (steps + S - 1) / S;
+    if ((steps + per - 1) / per != S) continue;  // normalizes to a smaller S
+    if (static_cast<long long>(batches) * S > 65535) break;
+    const int rc = resident_clusters(kernel, which, device, threads, smem, S);
+    if (rc <= 0) continue;
+    const long long waves = (tiles + rc - 1) / rc;
+    const long long cost = waves * (per + kWaveSteps);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = S;
+    }
+  }
+  return best;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_clustered(void (*kernel)(KArgs...), dim3 grid, int threads, uint32_t smem, int S, cudaStream_t st,
+                             const Args&... args) {
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[2]{};
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = static_cast<unsigned>(S);
+  // programmatic dependent of the pre-pass launched just before it
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 }  // namespace
 
 cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int batches, cudaStream_t st) {
@@ -673,15 +843,6 @@ cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int 
   g.n_pad = tiles_n * kTN;
   g.steps = ((g.K + kTK - 1) / kTK) * g.npieces;
   const long long tiles = static_cast<long long>(tiles_n) * tiles_m * batches;
-  // split the contraction so one wave fills the SMs, keeping >= 8 steps per CTA
-  long long splits = ctx->sm_count / tiles;
-  if (splits > g.steps / 8) splits = g.steps / 8;
-  if (splits < 1) splits = 1;
-  if (static_cast<long long>(batches) * splits > 65535) splits = 1;
-  // every split non-empty: each one's arrival completes its tile's count
-  const long long per = (g.steps + splits - 1) / splits;
-  splits = (g.steps + per - 1) / per;
-  g.splits = static_cast<int>(splits);
   // X planes per batch when any X piece varies per batch, else one copy; same for Y
   bool x_per_batch = false, y_per_batch = false;
   for (int p = 0; p < g.npieces; p++) {
@@ -704,18 +865,21 @@ cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int 
   }
   const int xb = x_per_batch ? batches : 1, yb = fused ? 0 : (y_per_batch ? batches : 1);
   g.batches = batches;
-  const size_t ws_bytes =
-      g.splits > 1 ? static_cast<size_t>(g.splits) * batches * static_cast<size_t>(g.M) * g.N * 8 : 0;
+  const void* kernel = fused ? reinterpret_cast<const void*>(ring_gemm_tc_fused_kernel)
+                             : reinterpret_cast<const void*>(ring_gemm_tc_kernel);
+  const int which = fused ? 1 : 0, threads = fused ? kFThreads : kThreads;
+  const uint32_t smem = fused ? kFSmemBytes : kSmemBytes;
+  cudaError_t e = prepare_kernel(kernel, which, ctx->device, smem);
+  if (e != cudaSuccess) return e;
+  g.splits = choose_splits(kernel, which, ctx->device, threads, smem, tiles, g.steps, batches);
   uint8_t* scratch = nullptr;
   const size_t xoff = 0, yoff = (xbytes * xb + 255) & ~size_t{255};
-  const size_t woff = (yoff + ybytes * yb + 255) & ~size_t{255};
-  cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), woff + ws_bytes, ctx->pool, st);
+  e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), yoff + ybytes * yb, ctx->pool, st);
   if (e != cudaSuccess) return e;
   g.xplanes = scratch + xoff;
   g.xps = x_per_batch ? xbytes : 0;
   g.yplanes = scratch + yoff;
   g.yps = y_per_batch ? ybytes : 0;
-  g.ws = g.splits > 1 ? reinterpret_cast<uint64_t*>(scratch + woff) : nullptr;
   // the operands as tiled byte planes
   PlanesSplit px{};
   PlanesSplit py{};
@@ -752,26 +916,11 @@ cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int 
   }
   const dim3 grid(static_cast<unsigned>(tiles_n), static_cast<unsigned>(tiles_m),
                   static_cast<unsigned>(batches * g.splits));
-  if (fused) {
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(ring_gemm_tc_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmemBytes);
-    if (e == cudaSuccess) {
-      ring_gemm_tc_fused_kernel<<<grid, kFThreads, kFSmemBytes, st>>>(g, bm);
-      e = cudaGetLastError();
-    }
-  } else {
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(ring_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e == cudaSuccess) {
-      ring_gemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(g);
-      e = cudaGetLastError();
-    }
-  }
-  if (e == cudaSuccess && g.splits > 1) {
-    const size_t want = (static_cast<size_t>(batches) * g.M * g.N + 255) / 256;
-    const size_t cap = static_cast<size_t>(ctx->sm_count) * 8;
-    ring_gemm_reduce_kernel<<<static_cast<unsigned>(want < cap ? (want ? want : 1) : cap), 256, 0, st>>>(g);
-    e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    const RingGemmLaunch& gc = g;
+    const BMaps& bc = bm;
+    e = fused ? launch_clustered(ring_gemm_tc_fused_kernel, grid, kFThreads, kFSmemBytes, g.splits, st, gc, bc)
+              : launch_clustered(ring_gemm_tc_kernel, grid, kThreads, kSmemBytes, g.splits, st, gc);
   }
   cudaFreeAsync(scratch, st);
   return e;
