@@ -1282,9 +1282,9 @@ LAYER_MATMULS = [("qkv", 128, 768, 2304), ("out", 128, 768, 768), ("ffn1", 128, 
 MATMUL_METRIC = "ring MACs/sec (configs[4] layer Beaver matmuls, Z_2^64, both parties)"
 
 
-# A-plane pre-pass, fused GEMM and split reduction per Beaver call (all four
-# layer shapes take the fused path and split their contraction)
-LAUNCHES_PER_TC_CALL = 3
+# A-plane pre-pass and fused GEMM per Beaver call (all four layer shapes take
+# the fused path; the split contraction is reduced inside the GEMM's cluster)
+LAUNCHES_PER_TC_CALL = 2
 
 
 def run_matmul(args, ws, rank, local):

@@ -224,24 +224,28 @@ __device__ __forceinline__ uint32_t cluster_size() {
   return r;
 }
 
-// 16 bytes at the same shared-memory offset in cluster rank `rank`.
-__device__ __forceinline__ void ld_rank16(uint32_t saddr, uint32_t rank, uint64_t& x, uint64_t& y) {
-  uint32_t a;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(saddr), "r"(rank));
-  asm volatile("ld.shared::cluster.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "r"(a) : "memory");
+// Generic pointer to the same shared-memory object in cluster rank `rank`
+// (plain loads through it, so the compiler can keep many in flight; they
+// are ordered after the cluster barrier by its memory clobber).
+__device__ __forceinline__ const ulonglong2* rank_ptr(const void* p, uint32_t rank) {
+  uint64_t a;
+  asm("mapa.u64 %0, %1, %2;" : "=l"(a) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+  return reinterpret_cast<const ulonglong2*>(a);
 }
 
-// Warps 0-3 (TMEM lane quarter = warp): the folded tile, sum_s (P_s mod
-// 2^32) << 8s per word, into this CTA's shared memory.
-__device__ __forceinline__ void fold_tile(uint32_t tmem, int warp, int lane, uint8_t* tile) {
+// The folded tile, sum_s (P_s mod 2^32) << 8s per word, into this CTA's
+// shared memory.  A warp reads the TMEM lanes of its quarter (warp % 4);
+// the groups of four warps deal the 16-column blocks among themselves.
+__device__ __forceinline__ void fold_tile(uint32_t tmem, int warp, int lane, int nwarps, uint8_t* tile) {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const int row = warp * 32 + lane;
+  const int quarter = warp & 3, row = quarter * 32 + lane;
+  const int groups = nwarps / 4 < kTN / 16 ? nwarps / 4 : kTN / 16;
 #pragma unroll 1
-  for (int cb = 0; cb < kTN / 16; cb++) {
+  for (int cb = warp >> 2; cb < kTN / 16; cb += groups) {
     uint32_t v[8][16];  // the 8 diagonals of 16 columns, loaded before one wait
 #pragma unroll
     for (int s = 0; s < 8; s++)
-      tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(s * kTN + cb * 16), v[s]);
+      tmem_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(s * kTN + cb * 16), v[s]);
 #pragma unroll
     for (int s = 0; s < 8; s++) tmem_wait(v[s]);
 #pragma unroll
@@ -257,35 +261,83 @@ __device__ __forceinline__ void fold_tile(uint32_t tmem, int warp, int lane, uin
   }
 }
 
+// Chunks [lo, hi) of the tile are this rank's share of the reduction.
+__device__ __forceinline__ void rank_share(int& lo, int& hi) {
+  const uint32_t S = cluster_size(), q = cluster_rank();
+  lo = static_cast<int>(q * kChunks / S);
+  hi = static_cast<int>((q + 1) * kChunks / S);
+}
+
+// One warp, during the main loop: the rows of C under this rank's share
+// into L2, so the reduction's C loads do not wait on HBM.
+__device__ __forceinline__ void prefetch_c_share(const RingGemmLaunch& g, int b, int m0, int n0, int lane) {
+  if (!g.c) return;
+  int lo, hi;
+  rank_share(lo, hi);
+  if (hi <= lo) return;
+  const int r0 = lo / (kTN / 2), r1 = (hi - 1) / (kTN / 2);
+  const uint64_t* C = g.c + static_cast<size_t>(b) * g.cs;
+  for (int u = lane; u < (r1 - r0 + 1) * 4; u += 32) {
+    const int m = m0 + r0 + u / 4, n = n0 + 16 * (u % 4);  // 128-byte lines of the row
+    if (m < g.M && n < g.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(C + static_cast<size_t>(m) * g.N + n));
+  }
+}
+
 // All threads: this rank's share of the tile, summed over the cluster's
 // tiles (addition mod 2^64 commutes), plus C and the bias, rescaled, stored.
-__device__ __forceinline__ void reduce_tile(const RingGemmLaunch& g, int b, int m0, int n0, uint32_t tile, int t,
+// Four chunks per thread at a time, their loads all issued before the first
+// use, so the loop pays the load latency once per four chunks.
+__device__ __forceinline__ void reduce_tile(const RingGemmLaunch& g, int b, int m0, int n0, const uint8_t* tile, int t,
                                             int nthr) {
-  const uint32_t S = cluster_size(), q = cluster_rank();
-  const int lo = static_cast<int>(q * kChunks / S), hi = static_cast<int>((q + 1) * kChunks / S);
+  constexpr int kBatch = 4;
+  const uint32_t S = cluster_size();
+  int lo, hi;
+  rank_share(lo, hi);
   const uint64_t* C = g.c ? g.c + static_cast<size_t>(b) * g.cs : nullptr;
   uint64_t* O = g.out + static_cast<size_t>(b) * g.os;
-  for (int ch = lo + t; ch < hi; ch += nthr) {
-    const int row = ch / (kTN / 2), c = ch % (kTN / 2);
-    const int m = m0 + row, n = n0 + 2 * c;
-    if (m >= g.M || n >= g.N) continue;
-    const uint32_t a = tile + tile_chunk(row, c);
-    uint64_t s0 = 0, s1 = 0;
-#pragma unroll 4
-    for (uint32_t r = 0; r < S; r++) {
-      uint64_t x, y;
-      ld_rank16(a, r, x, y);
-      s0 += x;
-      s1 += y;
+  for (int base = lo + t; base < hi; base += kBatch * nthr) {
+    uint64_t s0[kBatch], s1[kBatch];
+    size_t o[kBatch];
+    int n[kBatch];
+    bool ok[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; u++) {
+      const int ch = base + u * nthr;
+      const int row = ch / (kTN / 2), c = ch % (kTN / 2);
+      const int m = m0 + row;
+      n[u] = n0 + 2 * c;
+      ok[u] = ch < hi && m < g.M && n[u] < g.N;
+      o[u] = static_cast<size_t>(m) * g.N + n[u];
+      s0[u] = 0;
+      s1[u] = 0;
+      if (ok[u]) {
+        if (C) {
+          s0[u] = C[o[u]];
+          if (n[u] + 1 < g.N) s1[u] = C[o[u] + 1];
+        }
+        if (g.bias) {
+          s0[u] += static_cast<uint64_t>(g.bias[n[u]]);
+          if (n[u] + 1 < g.N) s1[u] += static_cast<uint64_t>(g.bias[n[u] + 1]);
+        }
+      }
     }
-    const size_t o = static_cast<size_t>(m) * g.N + n;
-    if (C) s0 += C[o];
-    if (g.bias) s0 += static_cast<uint64_t>(g.bias[n]);
-    O[o] = scaled_acc(s0, g.has_scale, g.mul_const, g.mul_shift);
-    if (n + 1 < g.N) {
-      if (C) s1 += C[o + 1];
-      if (g.bias) s1 += static_cast<uint64_t>(g.bias[n + 1]);
-      O[o + 1] = scaled_acc(s1, g.has_scale, g.mul_const, g.mul_shift);
+#pragma unroll
+    for (int u = 0; u < kBatch; u++) {
+      if (!ok[u]) continue;
+      const int ch = base + u * nthr;
+      const uint8_t* a = tile + tile_chunk(ch / (kTN / 2), ch % (kTN / 2));
+#pragma unroll 4
+      for (uint32_t r = 0; r < S; r++) {
+        const ulonglong2 xy = *rank_ptr(a, r);
+        s0[u] += xy.x;
+        s1[u] += xy.y;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; u++) {
+      if (!ok[u]) continue;
+      O[o[u]] = scaled_acc(s0[u], g.has_scale, g.mul_const, g.mul_shift);
+      if (n[u] + 1 < g.N) O[o[u] + 1] = scaled_acc(s1[u], g.has_scale, g.mul_const, g.mul_shift);
     }
   }
 }
@@ -295,17 +347,18 @@ __device__ __forceinline__ void reduce_tile(const RingGemmLaunch& g, int b, int 
 // barriers, on the error path too.
 __device__ __forceinline__ void finish_tile(const RingGemmLaunch& g, uint8_t* smem, uint32_t tmem, bool ok, int nsteps,
                                             int warp, int lane, int t, int b, int m0, int n0) {
-  if (ok && warp < 4) {
+  const int nwarps = static_cast<int>(blockDim.x) / 32;
+  if (ok) {
     if (nsteps > 0) {
-      fold_tile(tmem, warp, lane, smem);
-    } else {
+      fold_tile(tmem, warp, lane, nwarps, smem);
+    } else if (warp < 4) {
       for (int c = 0; c < kTN / 2; c++)
         *reinterpret_cast<ulonglong2*>(smem + tile_chunk(warp * 32 + lane, c)) = make_ulonglong2(0, 0);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   cluster_sync_all();  // every rank's tile is in its shared memory
-  reduce_tile(g, b, m0, n0, smem_u32(smem), t, static_cast<int>(blockDim.x));
+  reduce_tile(g, b, m0, n0, smem, t, static_cast<int>(blockDim.x));
   cluster_sync_all();  // every reader of this CTA's tile is done
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -316,25 +369,30 @@ __device__ __forceinline__ void finish_tile(const RingGemmLaunch& g, uint8_t* sm
 // Byte planes of one operand, tiled for the GEMM: for step c and row tile
 // (tile rows T = 128 for A, 64 for B) the 8 planes of T rows x 32 bytes in
 // core-matrix order, contiguous (one bulk copy per operand per step).
-// Unit (c, h, r): 16 K-consecutive words of row r, K half h of step c.
+// Unit (c, h, r, q): words 4q..4q+3 of the 16 K-consecutive words of row r,
+// K half h of step c; it writes 4 bytes of each plane, and the four units of
+// a 16-byte core-matrix row are adjacent threads (short load chains, many
+// threads: the pass is latency-bound at configs[4] sizes).
 // k_contig: element (row, k) at src[row * K + k], else at src[k * R + row].
 __device__ __forceinline__ void split_planes(const PlanesSplit& p, int block, int nblocks, int b) {
-  const size_t units = static_cast<size_t>(p.steps) * 2 * static_cast<size_t>(p.rows_pad);
+  const size_t units = static_cast<size_t>(p.steps) * 2 * static_cast<size_t>(p.rows_pad) * 4;
   const int cpp = (p.K + kTK - 1) / kTK;
   for (size_t u = static_cast<size_t>(block) * blockDim.x + threadIdx.x; u < units;
        u += static_cast<size_t>(nblocks) * blockDim.x) {
-    const int r = static_cast<int>(u % static_cast<size_t>(p.rows_pad));
-    const int h = static_cast<int>((u / static_cast<size_t>(p.rows_pad)) & 1);
-    const int c = static_cast<int>(u / (2 * static_cast<size_t>(p.rows_pad)));
+    const int q = static_cast<int>(u & 3);
+    const size_t w = u >> 2;
+    const int r = static_cast<int>(w % static_cast<size_t>(p.rows_pad));
+    const int h = static_cast<int>((w / static_cast<size_t>(p.rows_pad)) & 1);
+    const int c = static_cast<int>(w / (2 * static_cast<size_t>(p.rows_pad)));
     const bool second = c >= cpp;  // selects, not an indexed copy of the parameter
     const uint64_t* src = (second ? p.piece[1].src : p.piece[0].src) +
                           static_cast<size_t>(b) * (second ? p.piece[1].ss : p.piece[0].ss);
     const uint64_t* add = second ? p.piece[1].add : p.piece[0].add;
     if (add) add += static_cast<size_t>(b) * (second ? p.piece[1].as : p.piece[0].as);
-    const int k0 = (c % cpp) * kTK + 16 * h;
-    uint64_t v[16];
+    const int k0 = (c % cpp) * kTK + 16 * h + 4 * q;
+    uint64_t v[4];
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
+    for (int j = 0; j < 4; j++) {
       const int k = k0 + j;
       uint64_t val = 0;
       if (r < p.R && k < p.K) {
@@ -347,26 +405,20 @@ __device__ __forceinline__ void split_planes(const PlanesSplit& p, int block, in
     uint8_t* dst = p.dst + static_cast<size_t>(b) * p.ds;
     const int tiles = p.rows_pad / p.tile_rows, tile = r / p.tile_rows, rr = r % p.tile_rows;
     const size_t plane = static_cast<size_t>(p.tile_rows) * kTK;
-    uint8_t* blk = dst + ((static_cast<size_t>(c) * tiles + tile) * 8) * plane;
+    uint8_t* blk = dst + ((static_cast<size_t>(c) * tiles + tile) * 8) * plane + core_off(rr, h) + 4 * q;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-      uint32_t w[4];
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const uint32_t a0 = static_cast<uint32_t>(v[4 * q + 0] >> (i < 4 ? 0 : 32));
-        const uint32_t a1 = static_cast<uint32_t>(v[4 * q + 1] >> (i < 4 ? 0 : 32));
-        const uint32_t a2 = static_cast<uint32_t>(v[4 * q + 2] >> (i < 4 ? 0 : 32));
-        const uint32_t a3 = static_cast<uint32_t>(v[4 * q + 3] >> (i < 4 ? 0 : 32));
-        const uint32_t sel = static_cast<uint32_t>(i & 3) | (static_cast<uint32_t>(4 + (i & 3)) << 4);
-        w[q] = __byte_perm(__byte_perm(a0, a1, sel), __byte_perm(a2, a3, sel), 0x5410);
-      }
-      *reinterpret_cast<uint4*>(blk + i * plane + core_off(rr, h)) = make_uint4(w[0], w[1], w[2], w[3]);
+      const uint32_t a0 = static_cast<uint32_t>(v[0] >> (i < 4 ? 0 : 32));
+      const uint32_t a1 = static_cast<uint32_t>(v[1] >> (i < 4 ? 0 : 32));
+      const uint32_t a2 = static_cast<uint32_t>(v[2] >> (i < 4 ? 0 : 32));
+      const uint32_t a3 = static_cast<uint32_t>(v[3] >> (i < 4 ? 0 : 32));
+      const uint32_t sel = static_cast<uint32_t>(i & 3) | (static_cast<uint32_t>(4 + (i & 3)) << 4);
+      *reinterpret_cast<uint32_t*>(blk + i * plane) =
+          __byte_perm(__byte_perm(a0, a1, sel), __byte_perm(a2, a3, sel), 0x5410);
     }
   }
 }
 
-// Both operands in one launch: blocks [0, xblocks) split A, the rest split B
-// (blockIdx.y = batch, for an operand with per-batch planes).
 // The GEMM after it is launched as its programmatic dependent: it may start
 // its prologue and B loads at once and waits (griddepcontrol.wait) only
 // before it reads the planes written here.
@@ -441,6 +493,8 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
       }
       if (!__shfl_sync(0xffffffffu, go, 0)) break;
     }
+  } else if (warp == 3) {  // idle in the main loop: C of the epilogue into L2
+    prefetch_c_share(g, b, m0, n0, lane);
   } else if (warp == 1) {  // MMA issuer: the 36 limb MMAs of a step, then release the stage
     // Stage 0's plane descriptors and the diagonals' column addresses, once:
     // a stage's descriptors are these plus its byte offset >> 4 in the start
@@ -494,25 +548,43 @@ __global__ void __launch_bounds__(kThreads, 1) ring_gemm_tc_kernel(const RingGem
 // step's raw 32 x 64 words of B (and of the Beaver addend) with one tiled
 // tensor-map load per matrix (no multicast; x = n0 is a multiple of 64 words,
 // out-of-range rows and columns read as zero) into one of three raw stages;
-// warps 4-7 split a landed raw stage into one of two B-plane stages and fence
-// them to the async proxy; warp 2 bulk-copies the step's A planes into one of
-// three A stages; warp 1 issues the twelve MMAs and commits the A and B stages
-// back.  B crosses HBM once as words instead of being read, written as planes
-// and read again.  The three kinds of stage are separate rings so that the
-// raw stage is free again as soon as it is split: the main loop is bound by
-// the latency of the raw loads (about 2 us per load with all SMs loading),
-// so the smem goes to keeping more of them in flight.
-constexpr int kFThreads = 256;
-constexpr int kFAStages = 3;
-constexpr int kFBStages = 2;
-constexpr int kFRawStages = 3;
+// warps 4-11 split a landed raw stage into one of two B-plane stages and
+// fence them to the async proxy; warp 2 bulk-copies the step's A planes into
+// one of three A stages; warp 1 issues the twelve MMAs and commits the A and
+// B stages back; warp 3 prefetches the epilogue's C into L2.  B crosses HBM
+// once as words instead of being read, written as planes and read again.
+// The main loop is bound by the chain raw stage landed -> split -> B planes
+// ready -> MMAs: with four converter warps a step took 1.28 us against
+// 0.87 us for its MMAs alone; eight (two per SM sub-partition, eight K words
+// per thread) took 16 % off the configs[4] layer's four calls, while the
+// stage counts (3/2/3, 3/3/2, 3/4/2, 2/3/3) changed them by 1 % at most.
+// The counts and the converter warps are compile-time parameters.
+#ifndef SUFB200_F_CONV_WARPS
+#define SUFB200_F_CONV_WARPS 8
+#endif
+#ifndef SUFB200_F_A_STAGES
+#define SUFB200_F_A_STAGES 3
+#endif
+#ifndef SUFB200_F_B_STAGES
+#define SUFB200_F_B_STAGES 2
+#endif
+#ifndef SUFB200_F_RAW_STAGES
+#define SUFB200_F_RAW_STAGES 3
+#endif
+constexpr int kFConvWarps = SUFB200_F_CONV_WARPS;  // converter warps (4 or 8)
+constexpr int kFThreads = 128 + 32 * kFConvWarps;
+constexpr int kFAStages = SUFB200_F_A_STAGES;      // A-plane stages
+constexpr int kFBStages = SUFB200_F_B_STAGES;      // B-plane stages
+constexpr int kFRawStages = SUFB200_F_RAW_STAGES;  // raw B (+ addend) stages
+constexpr int kFConvK = kTK * kTN / (32 * kFConvWarps);  // K words one converter thread splits per step
+static_assert(kFConvWarps == 4 || kFConvWarps == 8, "converter split");
 constexpr uint32_t kFAStage = 8 * kPlaneX;                            // 32 KB of A planes
 constexpr uint32_t kFBStage = 8 * kPlaneY;                            // 16 KB of B planes
 constexpr uint32_t kFRawHalf = kTK * kTN * 8;                         // 16 KB: 32 rows x 64 words
 constexpr uint32_t kFRawStage = 2 * kFRawHalf;                        // B words, then the addend's
-constexpr uint32_t kFBOffset = kFAStages * kFAStage;                  // 96 KB
-constexpr uint32_t kFRawOffset = kFBOffset + kFBStages * kFBStage;    // 128 KB
-constexpr uint32_t kFCtrl = kFRawOffset + kFRawStages * kFRawStage;   // 224 KB
+constexpr uint32_t kFBOffset = kFAStages * kFAStage;
+constexpr uint32_t kFRawOffset = kFBOffset + kFBStages * kFBStage;
+constexpr uint32_t kFCtrl = kFRawOffset + kFRawStages * kFRawStage;
 constexpr uint32_t kFSmemBytes = kFCtrl + 256;
 static_assert(kFSmemBytes <= 227 * 1024, "dynamic shared memory per CTA");
 static_assert(kFCtrl >= kTM * kTN * 8, "the epilogue tile reuses the stages");
@@ -555,6 +627,9 @@ __global__ void __launch_bounds__(kFThreads, 1)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  } else if (warp == 3 && lane < 2 * g.npieces) {  // the tensor maps this CTA will load through
+    if (lane % 2 == 0 || g.piece[lane / 2].y2)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bm.m[lane])) : "memory");
   }
   if (t == 0) {
     for (int i = 0; i < kFAStages; i++) {
@@ -562,12 +637,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
       mbar_init(aempty0 + 8 * i, 1);
     }
     for (int i = 0; i < kFBStages; i++) {
-      mbar_init(bfull0 + 8 * i, 4);  // the four converter warps
+      mbar_init(bfull0 + 8 * i, kFConvWarps);  // the converter warps
       mbar_init(bempty0 + 8 * i, 1);
     }
     for (int i = 0; i < kFRawStages; i++) {
       mbar_init(rfull0 + 8 * i, 1);
-      mbar_init(rempty0 + 8 * i, 4);
+      mbar_init(rempty0 + 8 * i, kFConvWarps);
     }
     mbar_init(done, 1);
     *err = 0;
@@ -626,6 +701,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
       }
       if (!__shfl_sync(0xffffffffu, go, 0)) break;
     }
+  } else if (warp == 3) {  // idle in the main loop: C of the epilogue into L2
+    prefetch_c_share(g, b, m0, n0, lane);
   } else if (warp == 1) {  // MMA issuer
     uint64_t ad[8], bd[8];
     uint32_t dt[8];
@@ -666,7 +743,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     __syncwarp();
   } else if (warp >= 4) {  // converters: a landed raw stage into a B-plane stage
     const int ct = (warp - 4) * 32 + lane;
-    const int r = ct % kTN, h = ct / kTN;  // B-tile row (output column n0 + r) and K half
+    const int r = ct % kTN, kq = (ct / kTN) * kFConvK;  // B-tile row (output column n0 + r), first K word
     for (int li = 0; li < nsteps; li++) {
       const int rs = li % kFRawStages, bs = li % kFBStages;
       int go = 1;
@@ -684,17 +761,24 @@ __global__ void __launch_bounds__(kFThreads, 1)
       uint64_t v[16];
 #pragma unroll
       for (int j = 0; j < 16; j++) {
-        const int kk = 16 * h + j;
+        const int kk = kq + j;
         uint64_t val = 0;
-        if (k0 + kk < K && r < cnt) {
+        if (j < kFConvK && k0 + kk < K && r < cnt) {
           val = raw[kk * kTN + r];
           if (add) val += raw[kFRawHalf / 8 + kk * kTN + r];
         }
         v[j] = val;
       }
-      uint8_t* yt = smem + kFBOffset + static_cast<size_t>(bs) * kFBStage + core_off(r, h);
+      // kFConvK bytes of each plane: a whole 16-byte core-matrix row, or its half
+      uint8_t* yt = smem + kFBOffset + static_cast<size_t>(bs) * kFBStage + core_off(r, kq / 16) + (kq % 16);
 #pragma unroll
-      for (int i = 0; i < 8; i++) *reinterpret_cast<uint4*>(yt + i * kPlaneY) = plane_bytes(v, i);
+      for (int i = 0; i < 8; i++) {
+        const uint4 pb = plane_bytes(v, i);
+        if (kFConvK == 16)
+          *reinterpret_cast<uint4*>(yt + i * kPlaneY) = pb;
+        else
+          *reinterpret_cast<uint2*>(yt + i * kPlaneY) = make_uint2(pb.x, pb.y);
+      }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
       __syncwarp();
       if (lane == 0) {
@@ -904,7 +988,7 @@ cudaError_t launch_ring_gemm_tc(const sufb200_ctx_s* ctx, RingGemmLaunch g, int 
   py.dst = scratch + yoff;
   py.ds = ybytes;
   auto split_blocks = [](const PlanesSplit& q) {
-    const size_t units = static_cast<size_t>(q.steps) * 2 * q.rows_pad;
+    const size_t units = static_cast<size_t>(q.steps) * 2 * q.rows_pad * 4;
     const size_t want = (units + 255) / 256;
     return static_cast<int>(want < 8192 ? (want ? want : 1) : 8192);
   };

@@ -80,6 +80,26 @@ def test_beaver_matmul_tc_matches_cuda_core(ctx, torch_cuda, L, trans, scale):
             assert (from_dev(out) == from_dev(ref)).all(), (batches, M, K, N, party)
 
 
+def test_beaver_matmul_tc_layer_shapes(ctx, torch_cuda, L):
+    """The four Beaver matmuls of a configs[4] layer (QKV, O, FFN1, FFN2),
+    whose contractions split into clusters of 3, 8, 2 and 9 CTAs (the last
+    one a non-portable cluster size): identical to the CUDA-core kernel."""
+    rng = np.random.default_rng(91)
+    for M, K, N in ((128, 768, 2304), (128, 768, 768), (128, 768, 3072), (128, 3072, 768)):
+        D, E, A, B = (rand_u64(rng, n) for n in (M * K, K * N, M * K, K * N))
+        Cm = rand_u64(rng, M * N)
+        k = Keep(torch_cuda)
+        args = [k.dev(D), k.dev(E), k.dev(A), k.dev(B), k.dev(Cm)]
+        ref = torch_cuda.empty(M * N, dtype=torch_cuda.int64, device="cuda")
+        out = torch_cuda.empty_like(ref)
+        for party in (0, 1):
+            L.check(L.lib().sufb200_beaver_matmul2d(party, *args, 1, M, K, N, 0, 1, 4096, 12, _p(ref), None))
+            L.check(L.lib().sufb200_beaver_matmul2d_tc(ctx.h, party, *args, 1, M, K, N, 0, 1, C.c_int64(4096), 12,
+                                                       _p(out), None))
+            ctx.sync()
+            assert (from_dev(out) == from_dev(ref)).all(), (M, K, N, party)
+
+
 def test_ring_matmul_rejects(ctx, torch_cuda, L):
     from suf_b200 import _lib
 
