@@ -172,4 +172,30 @@ SUFB200_DEV Blk aes_encrypt_smem_rk(const Blk& in, uint32_t lb, const uint32_t* 
   return o;
 }
 
+// Two independent blocks under the same 44 round-key words held in
+// registers, their rounds interleaved (two table-lookup chains in flight per
+// thread, no round-key loads) -- the CTR keystream of a short coefficient row.
+SUFB200_DEV void aes_encrypt2_rk(const Blk& in0, const Blk& in1, uint32_t lb, const uint32_t (&rk)[44], Blk& o0,
+                                 Blk& o1) {
+  Blk a, b;
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    a.w[c] = in0.w[c] ^ rk[c];
+    b.w[c] = in1.w[c] ^ rk[c];
+  }
+#pragma unroll
+  for (int r = 1; r < 10; r++) {
+    a = aes_round(a, lb, rk[4 * r + 0], rk[4 * r + 1], rk[4 * r + 2], rk[4 * r + 3]);
+    b = aes_round(b, lb, rk[4 * r + 0], rk[4 * r + 1], rk[4 * r + 2], rk[4 * r + 3]);
+  }
+  o0.w[0] = aes_last_col<0>(a, lb, rk[40]);
+  o0.w[1] = aes_last_col<1>(a, lb, rk[41]);
+  o0.w[2] = aes_last_col<2>(a, lb, rk[42]);
+  o0.w[3] = aes_last_col<3>(a, lb, rk[43]);
+  o1.w[0] = aes_last_col<0>(b, lb, rk[40]);
+  o1.w[1] = aes_last_col<1>(b, lb, rk[41]);
+  o1.w[2] = aes_last_col<2>(b, lb, rk[42]);
+  o1.w[3] = aes_last_col<3>(b, lb, rk[43]);
+}
+
 }  // namespace sufb200

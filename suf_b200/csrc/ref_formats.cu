@@ -258,6 +258,45 @@ __global__ void __launch_bounds__(kAesThreads, 1)
   const uint64_t m = mask_bits(in_bits);
   const uint32_t lb = lane_base();
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  if (ow <= 4) {
+    // Rows of at most four words (configs[2]'s SiLU gate: r = 4, degree 0):
+    // both CTR blocks of an element at once, round keys in registers.
+    uint32_t rk[44];
+#pragma unroll
+    for (int k = 0; k < 44; k++) rk[k] = s_rk[k];
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+      const uint64_t xh = a.xs[i];
+      const uint64_t x = xh & m;
+      int lo = 0, hi = static_cast<int>(ivs);
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if ((cuts[mid] & m) <= x) lo = mid + 1; else hi = mid;
+      }
+      const int iv = lo - 1 < 0 ? 0 : (lo - 1 >= static_cast<int>(ivs) ? static_cast<int>(ivs) - 1 : lo - 1);
+      const uint64_t base = nonce ^ ((a.idx_base + i) << 32);
+      const uint64_t w0 = static_cast<uint64_t>(iv) * static_cast<uint64_t>(ow);
+      Blk k0, k1;
+      aes_encrypt2_rk(ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2)), lb, rk, k0, k1);
+      const uint64_t ks0 = (static_cast<uint64_t>(k0.w[1]) << 32) | k0.w[0];
+      const uint64_t ks1 = (static_cast<uint64_t>(k0.w[3]) << 32) | k0.w[2];
+      const uint64_t ks2 = (static_cast<uint64_t>(k1.w[1]) << 32) | k1.w[0];
+      const uint64_t ks3 = (static_cast<uint64_t>(k1.w[3]) << 32) | k1.w[2];
+      const uint64_t* row = pay + static_cast<size_t>(iv) * ow;
+      uint64_t* out = reinterpret_cast<uint64_t*>(a.out) + i * static_cast<size_t>(r);
+      int w = 0;
+      for (int j = 0; j < r; j++) {
+        uint64_t acc = 0, pw = 1;
+        for (int k = 0; k < d1; k++, w++) {
+          const uint64_t ksw = w == 0 ? ks0 : (w == 1 ? ks1 : (w == 2 ? ks2 : ks3));
+          const uint64_t c = party == 0 ? ksw : (row[w] - ksw);
+          acc += c * pw;
+          pw *= xh;
+        }
+        out[j] = (acc + p.r_out[j]) & p.ring_mask;
+      }
+    }
+    return;
+  }
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
     const uint64_t xh = a.xs[i];
     const uint64_t x = xh & m;
