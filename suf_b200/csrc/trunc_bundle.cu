@@ -185,14 +185,15 @@ __global__ void __launch_bounds__(kAesThreads, 1) trunc_bundle_kernel(const PrgP
 
 
 // Small batches of both parties' bundles over one x^: one lane per (party,
-// element, query), four lanes per element, so the queries of an element run
-// side by side instead of one after another and both parties fill one
-// launch; lane 0 of each quad gathers the quad's shares and folds the plan
-// and the postproc.  For batches too small to fill the GPU with one lane per
-// element (the row-level truncations of a softmax block).
+// element, query), `lanes` (1, 2 or 4: the bundle's query count rounded up)
+// lanes per element, so the queries of an element run side by side instead
+// of one after another and both parties fill one launch; lane 0 of each
+// group gathers the group's shares and folds the plan and the postproc.  For
+// batches too small to fill the GPU with one lane per element (the row-level
+// truncations of the softmax and LayerNorm blocks).
 __global__ void __launch_bounds__(kAesThreads, 1)
     trunc_bundle_pair_kernel(const PrgParams prg, const __grid_constant__ TruncLaunch a0,
-                             const __grid_constant__ TruncLaunch a1) {
+                             const __grid_constant__ TruncLaunch a1, int lanes) {
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
     if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
@@ -205,14 +206,15 @@ __global__ void __launch_bounds__(kAesThreads, 1)
   __syncthreads();
   if (!keys_ok(ks, a0) || !keys_ok(ks + 4, a1)) return;
   const uint32_t lb = lane_base();
-  const size_t n = a0.n, units = 8 * n;  // 2 parties x n elements x 4 lanes
+  const int lsh = lanes >= 4 ? 2 : (lanes >= 2 ? 1 : 0);  // lanes per element = 1 << lsh
+  const size_t n = a0.n, units = (2 * n) << lsh;           // 2 parties x n elements x lanes
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-  const int lane = static_cast<int>(threadIdx.x & 31u), quad = lane & ~3;
+  const int lane = static_cast<int>(threadIdx.x & 31u), grp = lane & ~((1 << lsh) - 1);
   for (size_t g0 = static_cast<size_t>(blockIdx.x) * blockDim.x; g0 < units; g0 += stride) {
     const size_t g = g0 + threadIdx.x;  // g0 is uniform across the block: every lane reaches the shuffles
     const bool valid = g < units;
-    const size_t j = g >> 2;
-    const int q = static_cast<int>(g & 3u);
+    const size_t j = g >> lsh;
+    const int q = static_cast<int>(g & ((1u << lsh) - 1u));
     const uint32_t party = j >= n ? 1u : 0u;
     const size_t i = party ? j - n : j;
     const TruncLaunch* a = party ? &a1 : &a0;
@@ -227,7 +229,10 @@ __global__ void __launch_bounds__(kAesThreads, 1)
     }
     uint64_t pr[4];
 #pragma unroll
-    for (int k = 0; k < 4; k++) pr[k] = __shfl_sync(0xffffffffu, v, quad + k);
+    for (int k = 0; k < 4; k++) {
+      const uint64_t w = __shfl_sync(0xffffffffu, v, grp + (k < (1 << lsh) ? k : 0));
+      pr[k] = k < (1 << lsh) ? w : 0ull;
+    }
     if (valid && q == 0) combine_store(d, xh, pr, a->y, a->bools, i);
   }
 }
@@ -326,9 +331,20 @@ cudaError_t launch_trunc_bundle_pair(const sufb200_ctx_s* ctx, const TruncLaunch
   cudaError_t e = cudaFuncSetAttribute(trunc_bundle_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(ctx->aes_dyn_bytes));
   if (e != cudaSuccess) return e;
-  const size_t want = (8 * a0.n + kAesThreads - 1) / kAesThreads;
-  const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
-  trunc_bundle_pair_kernel<<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a0, a1);
+  if (a0.desc.nq != a1.desc.nq || a0.desc.nq < 0 || a0.desc.nq > 4) return cudaErrorInvalidValue;  // 0: no query
+  const int lanes = a0.desc.nq <= 1 ? 1 : (a0.desc.nq <= 2 ? 2 : 4);
+  const size_t units = 2 * a0.n * static_cast<size_t>(lanes);
+  // A tree level is about 1,200 instructions per lane and the levels are
+  // sequential: a small batch is bound by how many warps share an SM's issue
+  // slots, so it is spread over as many SMs as it can use (at least 128
+  // threads per CTA, so the table fill stays short).
+  const size_t sms = static_cast<size_t>(ctx->sm_count);
+  size_t threads = ((units + sms - 1) / sms + 31) / 32 * 32;
+  threads = threads < 128 ? 128 : (threads > static_cast<size_t>(kAesThreads) ? kAesThreads : threads);
+  const size_t want = (units + threads - 1) / threads;
+  const int grid = static_cast<int>(want < sms ? (want ? want : 1) : sms);
+  trunc_bundle_pair_kernel<<<grid, static_cast<unsigned>(threads), ctx->aes_dyn_bytes, st>>>(ctx->prg, a0, a1,
+                                                                                            lanes);
   return cudaGetLastError();
 }
 
