@@ -1027,6 +1027,15 @@ def cpu_softmax_baseline(args):
             "sample": "one configs[4] block, plaintext numpy model of the block (no shares)"}
 
 
+# Our kernels per block (from the ncu launch list): softmax = 3 element-level
+# truncations x (range, frontier, main) + 3 row-level pair truncations + 4
+# interval-LUT gates + 8 elementwise stages; LayerNorm = 1 element-level
+# truncation x 3 + 7 row-level pair truncations + 2 LUT gates + 9 row and
+# elementwise stages.
+SOFTMAX_LAUNCHES = 24
+LAYERNORM_LAUNCHES = 21
+
+
 def run_softmax(args, ws, rank, local):
     """One configs[4] softmax block per step on every GPU, both parties' shares
     on the GPU (replicas: the block has no cross-GPU exchange when both
@@ -1104,9 +1113,9 @@ def run_softmax(args, ws, rank, local):
                             "frac": round(gbs / hbm_peak, 4), "traffic": traffic,
                             "per_block_us": round(ms * 1e3, 1),
                             "note": "bytes = every stage's tensors read and written once (70 words per active "
-                                    "element); the block is a chain of 36 small launches, bound by their latency"},
+                                    "element); the block is a chain of 24 small launches, bound by their latency"},
                "cpu_baseline": cpu_softmax_baseline(args) if (ws == 1 and not args.no_cpu) else None,
-               "clocks": clk.summary(), "gpu_launches": 36 * args.steps,
+               "clocks": clk.summary(), "gpu_launches": SOFTMAX_LAUNCHES * args.steps,
                "max_err_vs_double_softmax": round(err, 6), "reconstruction_ok": err < 0.03,
                "ms_per_step_all": [round(v, 4) for v in ms_steps]}
     if ws > 1:
@@ -1231,9 +1240,9 @@ def run_layernorm(args, ws, rank, local):
                "roofline": {"bound": "hbm", "unit": "GB/s", "achieved": round(gbs, 1), "peak": hbm_peak,
                             "frac": round(gbs / hbm_peak, 4), "traffic": traffic, "per_block_us": round(ms * 1e3, 1),
                             "note": "bytes = every stage's tensors read and written once (22 words per element); "
-                                    "a chain of about 30 small launches, bound by their latency"},
+                                    "a chain of 21 small launches, bound by their latency"},
                "cpu_baseline": cpu_layernorm_baseline(args) if (ws == 1 and not args.no_cpu) else None,
-               "clocks": clk.summary(), "gpu_launches": 30 * args.steps,
+               "clocks": clk.summary(), "gpu_launches": LAYERNORM_LAUNCHES * args.steps,
                "max_err_vs_double_layernorm": round(err, 6), "reconstruction_ok": err < 0.02,
                "ms_per_step_all": [round(v, 4) for v in ms_steps]}
     if ws > 1:

@@ -420,6 +420,10 @@ int enqueue_chunk_copy(const ChunkSink& k, cudaStream_t st, const uint64_t* d_y,
 int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
                       const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y, uint64_t* d_bools,
                       void* stream, const ChunkSink* sink);
+int trunc_bundle_pair_prefix(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* keys0,
+                             const size_t* key_bytes0, const sufb200_trunc_desc* desc1, const uint8_t* const* keys1,
+                             const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
+                             uint64_t* d_y1, void* stream);
 
 }  // namespace
 
@@ -541,6 +545,62 @@ int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uin
   return SUFB200_OK;
 }
 
+// Both parties' bundles over one x^ on the shared-prefix path: one range
+// pass (x^ is common), one frontier launch over both parties' query keys and
+// one main pass over both parties' elements.
+int trunc_bundle_pair_prefix(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* keys0,
+                             const size_t* key_bytes0, const sufb200_trunc_desc* desc1, const uint8_t* const* keys1,
+                             const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
+                             uint64_t* d_y1, void* stream) {
+  if (!d_xhat || !d_y0 || !d_y1 || !aligned8(d_xhat) || !aligned8(d_y0) || !aligned8(d_y1))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  std::vector<uint8_t> blob;
+  sufb200::TruncLaunch a0{}, a1{};
+  a0.desc = *desc0;
+  a1.desc = *desc1;
+  if (int rc = pack_bundle_keys(*desc0, keys0, key_bytes0, blob, a0.key_off)) return rc;
+  if (int rc = pack_bundle_keys(*desc1, keys1, key_bytes1, blob, a1.key_off)) return rc;
+  cudaStream_t st = as_stream(stream);
+  const uint32_t kmax = sufb200::prefix_budget(n);
+  const size_t blob_bytes = (blob.size() + 255) & ~static_cast<size_t>(255);
+  const size_t nqt = static_cast<size_t>(desc0->nq + desc1->nq);
+  uint8_t* scratch = nullptr;
+  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch),
+                                             blob_bytes + kAccBytes + 32ull * kmax * nqt + 256, ctx->pool, st),
+                     "pair bundle scratch allocation");
+  cudaError_t e = cudaMemcpyAsync(scratch, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
+  for (sufb200::TruncLaunch* a : {&a0, &a1}) {
+    a->keys = scratch;
+    a->xhat = d_xhat;
+    a->n = n;
+    a->bools = nullptr;
+    a->t0 = ctx->d_t0;
+    a->status = ctx->d_status;
+  }
+  a0.y = d_y0;
+  a1.y = d_y1;
+  auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch + blob_bytes);
+  sufb200::FrontierEntry* F[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  sufb200::FrontierBatch fb{};
+  fb.nq = static_cast<int>(nqt);
+  int k = 0;
+  for (int p = 0; p < 2; p++) {
+    const sufb200_trunc_desc* d = p ? desc1 : desc0;
+    const sufb200::TruncLaunch& a = p ? a1 : a0;
+    for (int q = 0; q < d->nq; q++, k++) {
+      F[4 * p + q] = reinterpret_cast<sufb200::FrontierEntry*>(scratch + blob_bytes + kAccBytes + 32ull * kmax * k);
+      fb.q[k] = sufb200::FrontierLaunch{scratch + a.key_off[q], d->q_bits[q], 8, acc, kmax, F[4 * p + q],
+                                        ctx->d_t0, ctx->d_status};
+    }
+  }
+  if (e == cudaSuccess) e = sufb200::launch_range(ctx, d_xhat, n, acc, st);
+  if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
+  if (e == cudaSuccess) e = sufb200::launch_trunc_bundle_prefix_pair(ctx, a0, a1, acc, kmax, F, st);
+  cudaFreeAsync(scratch, st);
+  if (e != cudaSuccess) return cuda_fail(e, "pair bundle launch");
+  return SUFB200_OK;
+}
+
 }  // namespace
 
 int sufb200_trunc_bundle_eval_pair(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* keys0,
@@ -552,7 +612,10 @@ int sufb200_trunc_bundle_eval_pair(sufb200_ctx ctx, const sufb200_trunc_desc* de
   if (int rc = check_bundle_desc(desc1, keys1, key_bytes1)) return rc;
   if (desc0->party != 0 || desc1->party != 1) return fail(SUFB200_ERR_INVALID, "desc0 / desc1 must be parties 0 / 1");
   if (n == 0) return SUFB200_OK;
-  if (n >= prefix_min_n()) {  // large batches: each party's bundle on the shared-prefix path
+  if (n >= prefix_min_n() && desc0->nq > 0 && desc1->nq > 0)  // large batches: both bundles, shared-prefix path
+    return trunc_bundle_pair_prefix(ctx, desc0, keys0, key_bytes0, desc1, keys1, key_bytes1, d_xhat, n, d_y0, d_y1,
+                                    stream);
+  if (n >= prefix_min_n()) {  // large batches of query-free bundles: each party on its own
     if (int rc = trunc_bundle_impl(ctx, desc0, keys0, key_bytes0, d_xhat, n, d_y0, nullptr, stream, nullptr))
       return rc;
     return trunc_bundle_impl(ctx, desc1, keys1, key_bytes1, d_xhat, n, d_y1, nullptr, stream, nullptr);

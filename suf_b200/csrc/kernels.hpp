@@ -105,10 +105,12 @@ struct FrontierLaunch {
   const uint32_t* t0;
   uint32_t* status;
 };
-// The frontier tables of up to four keys over one batch, built in one launch
-// (all keys share the range accumulator and the status word of q[0]).
+// The frontier tables of up to eight keys over one batch (one bundle's
+// queries, or both parties' bundles), built in one launch (all keys share
+// the range accumulator and the status word of q[0]).
+constexpr int kFrontierMaxKeys = 8;
 struct FrontierBatch {
-  FrontierLaunch q[4];
+  FrontierLaunch q[kFrontierMaxKeys];
   int nq;
 };
 uint32_t prefix_budget(size_t n);
@@ -118,6 +120,11 @@ cudaError_t launch_myl7_bcast_prefix(const sufb200_ctx_s* ctx, int group, const 
                                      uint32_t kmax, const FrontierEntry* F, cudaStream_t st);
 cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaunch& a, const RangeAcc* acc,
                                        uint32_t kmax, FrontierEntry* const F[4], cudaStream_t st);
+// Both parties' bundles over one x^ in one main pass: F[0..3] party 0's
+// queries, F[4..7] party 1's.
+cudaError_t launch_trunc_bundle_prefix_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
+                                            const RangeAcc* acc, uint32_t kmax, FrontierEntry* const F[8],
+                                            cudaStream_t st);
 
 // myl7 DCF keygen on the GPU (keygen_dev.cu): one key pair per thread.
 struct GenLaunch {

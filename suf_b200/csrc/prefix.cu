@@ -92,10 +92,10 @@ struct FrontierKey {
 // Staging area at the start of dynamic shared memory, below the AES tables
 // (no static shared memory: it would move the table window).
 struct FrontierStage {
-  BcastKeySmem key[4];
-  FrontierKey fk[4];
-  uint64_t first_item[5];
-  int order[4];
+  BcastKeySmem key[kFrontierMaxKeys];
+  FrontierKey fk[kFrontierMaxKeys];
+  uint64_t first_item[kFrontierMaxKeys + 1];
+  int order[kFrontierMaxKeys];
 };
 static_assert(sizeof(FrontierStage) < kTabBase - 4096, "staging must fit below the tables");
 
@@ -118,13 +118,13 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
   int* order = fs->order;
   uint64_t* first_item = fs->first_item;
 #pragma unroll
-  for (int q = 0; q < 4; q++)
+  for (int q = 0; q < kFrontierMaxKeys; q++)
     if (q < nq) stage_bcast_key(&ks[q], b.q[q].key, b.q[q].in_bits, b.q[q].out_bytes);
   aes_fill_tables(b.q[0].t0);
   if (threadIdx.x == 0) {
-    uint64_t cost[4];
+    uint64_t cost[kFrontierMaxKeys];
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
+    for (int q = 0; q < kFrontierMaxKeys; q++) {
       if (q >= nq) continue;
       const Plan p = make_plan(*b.q[q].acc, b.q[q].in_bits, b.q[q].kmax);
       const int h = expand_height(p);
@@ -279,7 +279,7 @@ cudaError_t launch_range(const sufb200_ctx_s* ctx, const uint64_t* xs, size_t n,
 }
 
 cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st) {
-  if (b.nq < 1 || b.nq > 4) return cudaErrorInvalidValue;
+  if (b.nq < 1 || b.nq > kFrontierMaxKeys) return cudaErrorInvalidValue;
   size_t work = 0;
   for (int q = 0; q < b.nq; q++) work += b.q[q].kmax;
   const int grid = aes_grid(ctx, work);

@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kAesThreads, 1)
 
 // Large batches: every query resumes from its frontier entry (prefix.cuh).
 struct FrontierSet {
-  const FrontierEntry* F[4];
+  const FrontierEntry* F[8];  // F[4 p + q]: party slot p's query q
 };
 
 // Per-query plan, frontier table and width, staged once per block after the
@@ -251,46 +251,66 @@ struct QueryPlanSmem {
   int nb;
   int pad;
 };
-static_assert(4 * sizeof(QueryKeySmem) + 4 * sizeof(QueryPlanSmem) < kTabBase - 4096,
+static_assert(8 * sizeof(QueryKeySmem) + 8 * sizeof(QueryPlanSmem) < kTabBase - 4096,
               "staging must fit below the tables");
 
+// NP = 1: one party's bundle; NP = 2: both parties' bundles over one x^ in
+// one pass (elements [0, n) party 0, [n, 2n) party 1), so a pair of
+// element-level truncations costs one range, one frontier and one main
+// launch instead of two of each.
+template <int NP>
 __global__ void __launch_bounds__(kAesThreads, 1)
-    trunc_bundle_prefix_kernel(const PrgParams prg, const TruncLaunch a, const RangeAcc* acc, uint32_t kmax,
+    trunc_bundle_prefix_kernel(const PrgParams prg, const __grid_constant__ TruncLaunch a0,
+                               const __grid_constant__ TruncLaunch a1, const RangeAcc* acc, uint32_t kmax,
                                const FrontierSet fs) {
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
-    if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
     return;
   }
-  const sufb200_trunc_desc& d = a.desc;
   QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);
-  QueryPlanSmem* qp = reinterpret_cast<QueryPlanSmem*>(smem + 4 * sizeof(QueryKeySmem));
+  QueryPlanSmem* qp = reinterpret_cast<QueryPlanSmem*>(smem + 8 * sizeof(QueryKeySmem));
   if (threadIdx.x == 0) {
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int nb = d.q_bits[q];
-      qp[q].plan = q < d.nq ? make_plan(*acc, nb, kmax) : Plan{0, 1, 0};
-      qp[q].F = fs.F[q];
-      qp[q].nb = nb;
-      qp[q].pad = 0;
+    for (int p = 0; p < NP; p++) {
+      const sufb200_trunc_desc& dp = p ? a1.desc : a0.desc;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int nb = dp.q_bits[q];
+        qp[4 * p + q].plan = q < dp.nq ? make_plan(*acc, nb, kmax) : Plan{0, 1, 0};
+        qp[4 * p + q].F = fs.F[4 * p + q];
+        qp[4 * p + q].nb = nb;
+        qp[4 * p + q].pad = 0;
+      }
     }
   }
-  if (!stage_bundle(ks, a)) return;  // its barrier also publishes qp
+  stage_keys(ks, a0);
+  if (NP == 2) stage_keys(ks + 4, a1);
+  aes_fill_tables(a0.t0);
+  __syncthreads();  // also publishes qp
+  if (!keys_ok(ks, a0) || (NP == 2 && !keys_ok(ks + 4, a1))) return;
   const uint32_t lb = lane_base();
-  const uint32_t party = static_cast<uint32_t>(d.party);
+  const size_t n = a0.n, total = static_cast<size_t>(NP) * n;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+  for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total; g += stride) {
+    const int slot = (NP == 2 && g >= n) ? 1 : 0;
+    const size_t i = slot ? g - n : g;
+    const TruncLaunch& a = slot ? a1 : a0;
+    const sufb200_trunc_desc& d = a.desc;
+    const uint32_t party = static_cast<uint32_t>(d.party);
+    const QueryKeySmem* kq = ks + 4 * slot;
+    const QueryPlanSmem* pq = qp + 4 * slot;
     const uint64_t xh = a.xhat[i];
     uint64_t pr[4] = {0, 0, 0, 0};
 #pragma unroll 1
     for (int q = 0; q < d.nq; q++) {
-      const int nb = qp[q].nb;
+      const int nb = pq[q].nb;
       const uint64_t x = xh & nbit_mask(nb);
-      const Plan P = qp[q].plan;
+      const Plan P = pq[q].plan;
       const uint32_t idx = plan_index(P, x, nb);
       uint64_t v;
       if (idx < P.count) {
-        const FrontierEntry e = qp[q].F[idx];
+        const FrontierEntry e = pq[q].F[idx];
         if (P.depth == static_cast<uint32_t>(nb)) {
           v = e.v;
         } else {
@@ -299,10 +319,10 @@ __global__ void __launch_bounds__(kAesThreads, 1)
           s.w[1] = e.s[1];
           s.w[2] = e.s[2];
           s.w[3] = e.s[3];
-          v = walk_query(prg, lb, ks[q], nb, x, party, s, e.t, e.v, static_cast<int>(P.depth));
+          v = walk_query(prg, lb, kq[q], nb, x, party, s, e.t, e.v, static_cast<int>(P.depth));
         }
       } else {
-        v = walk_query(prg, lb, ks[q], nb, x, party, seed_blk(ks[q]), party, 0, 0);
+        v = walk_query(prg, lb, kq[q], nb, x, party, seed_blk(kq[q]), party, 0, 0);
       }
       if (q == 0) pr[0] = v;
       else if (q == 1) pr[1] = v;
@@ -350,13 +370,27 @@ cudaError_t launch_trunc_bundle_pair(const sufb200_ctx_s* ctx, const TruncLaunch
 
 cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaunch& a, const RangeAcc* acc,
                                        uint32_t kmax, FrontierEntry* const F[4], cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(trunc_bundle_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(trunc_bundle_prefix_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(ctx->aes_dyn_bytes));
   if (e != cudaSuccess) return e;
-  FrontierSet fs{{F[0], F[1], F[2], F[3]}};
+  FrontierSet fs{{F[0], F[1], F[2], F[3], nullptr, nullptr, nullptr, nullptr}};
   const size_t want = (a.n + kAesThreads - 1) / kAesThreads;
   const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
-  trunc_bundle_prefix_kernel<<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a, acc, kmax, fs);
+  trunc_bundle_prefix_kernel<1><<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a, a, acc, kmax, fs);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_trunc_bundle_prefix_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
+                                            const RangeAcc* acc, uint32_t kmax, FrontierEntry* const F[8],
+                                            cudaStream_t st) {
+  if (a0.n != a1.n || a0.xhat != a1.xhat) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(trunc_bundle_prefix_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  FrontierSet fs{{F[0], F[1], F[2], F[3], F[4], F[5], F[6], F[7]}};
+  const size_t want = (2 * a0.n + kAesThreads - 1) / kAesThreads;
+  const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
+  trunc_bundle_prefix_kernel<2><<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a0, a1, acc, kmax, fs);
   return cudaGetLastError();
 }
 

@@ -141,7 +141,7 @@ def test_host_entry_chunked_matches_device_entry(ctx, torch_cuda, oracle, prg_st
 
 
 @pytest.mark.parametrize("kind", [KIND_TR, KIND_ARS, KIND_GAPARS])
-@pytest.mark.parametrize("n", [1, 7, 1536, 20_000])
+@pytest.mark.parametrize("n", [1, 7, 1536, 20_000, 99_072])
 def test_pair_entry_matches_per_party_entry(ctx, torch_cuda, oracle, prg_state, kind, n):
     """sufb200_trunc_bundle_eval_pair (one query-parallel launch for both
     parties below the shared-prefix size, the per-party path above it) gives
