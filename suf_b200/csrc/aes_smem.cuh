@@ -155,6 +155,29 @@ SUFB200_DEV void prg_level(const PrgParams& P, uint32_t lb, const Blk& s, uint32
   b1 = aes_last_col<1>(b, lb, SUFB200_PRG_KEY(P, 1, 10, 1, xm)) ^ s.w[1];
 }
 
+// Key word of half h (hm = 0 - h) for round r, column c: the per-lane
+// choice between the two halves of prg_level, without indexing the
+// parameter block by a register.
+#define SUFB200_PRG_KEY_H(P, R, C, XM, HM) \
+  ((SUFB200_PRG_KEY(P, 0, R, C, XM) & ~(HM)) | (SUFB200_PRG_KEY(P, 1, R, C, XM) & (HM)))
+
+// One of the two MMO blocks of prg_level: out = AES_{K_{2x+h}}(s) ^ s, the
+// full block (h = 0 gives prg_level's A, h = 1 its B).
+SUFB200_DEV void prg_half(const PrgParams& P, uint32_t lb, const Blk& s, uint32_t xm, uint32_t h, Blk& out) {
+  const uint32_t hm = 0u - h;
+  Blk a;
+#pragma unroll
+  for (int c = 0; c < 4; c++) a.w[c] = s.w[c] ^ SUFB200_PRG_KEY_H(P, 0, c, xm, hm);
+#pragma unroll
+  for (int r = 1; r < 10; r++)
+    a = aes_round(a, lb, SUFB200_PRG_KEY_H(P, r, 0, xm, hm), SUFB200_PRG_KEY_H(P, r, 1, xm, hm),
+                  SUFB200_PRG_KEY_H(P, r, 2, xm, hm), SUFB200_PRG_KEY_H(P, r, 3, xm, hm));
+  out.w[0] = aes_last_col<0>(a, lb, SUFB200_PRG_KEY_H(P, 10, 0, xm, hm)) ^ s.w[0];
+  out.w[1] = aes_last_col<1>(a, lb, SUFB200_PRG_KEY_H(P, 10, 1, xm, hm)) ^ s.w[1];
+  out.w[2] = aes_last_col<2>(a, lb, SUFB200_PRG_KEY_H(P, 10, 2, xm, hm)) ^ s.w[2];
+  out.w[3] = aes_last_col<3>(a, lb, SUFB200_PRG_KEY_H(P, 10, 3, xm, hm)) ^ s.w[3];
+}
+
 // Plain AES-128 of one block under 44 round-key words read from shared
 // memory (uniform address across the warp) -- the CTR keystream of the
 // reference key formats.

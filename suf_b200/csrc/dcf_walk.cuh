@@ -53,6 +53,45 @@ SUFB200_DEV void walk_level(const PrgParams& P, uint32_t lb, Blk& s, uint32_t& t
   t = tc;
 }
 
+// walk_level split over a lane pair (lanes 2k, 2k+1 of the warp, pmask =
+// both lanes' bits, h = lane & 1): each lane computes one of the level's two
+// MMO blocks and the pair swaps them, so a level costs one AES block per lane
+// instead of two.  Both lanes leave with the same s, t, v as walk_level.
+#if !defined(SUFB200_HOST_EMU)
+template <int GROUP>
+SUFB200_DEV void walk_level_split(const PrgParams& P, uint32_t lb, Blk& s, uint32_t& t, uint64_t& v, uint32_t x_bit,
+                                  uint32_t party, const CwLevel& cw, uint32_t h, uint32_t pmask) {
+  const uint32_t xm = 0u - x_bit;
+  Blk o, e;
+  prg_half(P, lb, s, xm, h, o);
+#pragma unroll
+  for (int c = 0; c < 4; c++) e.w[c] = __shfl_xor_sync(pmask, o.w[c], 1);
+  Blk a;
+#pragma unroll
+  for (int c = 0; c < 4; c++) a.w[c] = h ? e.w[c] : o.w[c];  // block A (half 0)
+  const uint32_t b0 = h ? o.w[0] : e.w[0], b1 = h ? o.w[1] : e.w[1];  // low half of block B
+  uint32_t tc = a.w[3] >> 31;
+  a.w[3] &= 0x7FFFFFFFu;
+  const uint32_t tm = 0u - t;
+  a.w[0] ^= cw.s.w[0] & tm;
+  a.w[1] ^= cw.s.w[1] & tm;
+  a.w[2] ^= cw.s.w[2] & tm;
+  a.w[3] ^= cw.s.w[3] & tm;
+  tc ^= t & ((cw.t >> (1u - x_bit)) & 1u);
+  uint64_t vc = (static_cast<uint64_t>(b1) << 32) | b0;
+  const uint64_t tm64 = 0ull - static_cast<uint64_t>(t);
+  if (GROUP == SUFB200_GROUP_ADD) {
+    vc += cw.v & tm64;
+    v += party ? (0ull - vc) : vc;
+  } else {
+    vc ^= cw.v & tm64;
+    v ^= vc;
+  }
+  s = a;
+  t = tc;
+}
+#endif  // !SUFB200_HOST_EMU
+
 // Final correction: v += (-1)^b (s + t * cw_np1) on the low 64 bits.
 template <int GROUP>
 SUFB200_DEV uint64_t walk_finish(const Blk& s, uint32_t t, uint64_t v, uint32_t party, uint64_t np1_lo) {

@@ -145,6 +145,26 @@ __device__ __forceinline__ uint64_t walk_query(const PrgParams& prg, uint32_t lb
   return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, K.np1_lo);
 }
 
+// walk_query over a lane pair (walk_level_split): lanes 2k and 2k+1 of the
+// warp walk the same query together; both return the share.
+__device__ __forceinline__ uint64_t walk_query_split(const PrgParams& prg, uint32_t lb, const QueryKeySmem& K, int n,
+                                                     uint64_t x, uint32_t party, Blk s, uint32_t t, uint64_t v,
+                                                     uint32_t h, uint32_t pmask) {
+  for (int lv = 0; lv < n; lv++) {
+    CwLevel cw;
+    const uint4 cs = K.cw_s[lv];
+    cw.s.w[0] = cs.x;
+    cw.s.w[1] = cs.y;
+    cw.s.w[2] = cs.z;
+    cw.s.w[3] = cs.w;
+    cw.v = K.cw_v[lv];
+    cw.t = K.cw_t[lv];
+    walk_level_split<SUFB200_GROUP_ADD>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (n - 1 - lv)) & 1ull), party,
+                                        cw, h, pmask);
+  }
+  return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, K.np1_lo);
+}
+
 __device__ __forceinline__ Blk seed_blk(const QueryKeySmem& K) {
   Blk s;
   s.w[0] = K.seed.x;
@@ -184,13 +204,15 @@ __global__ void __launch_bounds__(kAesThreads, 1) trunc_bundle_kernel(const PrgP
 }
 
 
-// Small batches of both parties' bundles over one x^: one lane per (party,
-// element, query), `lanes` (1, 2 or 4: the bundle's query count rounded up)
-// lanes per element, so the queries of an element run side by side instead
-// of one after another and both parties fill one launch; lane 0 of each
-// group gathers the group's shares and folds the plan and the postproc.  For
-// batches too small to fill the GPU with one lane per element (the row-level
-// truncations of the softmax and LayerNorm blocks).
+// Small batches of both parties' bundles over one x^: a lane pair per (party,
+// element, query) -- each lane computes one of a tree level's two MMO blocks
+// and the pair swaps them (walk_level_split) -- and `lanes` (2, 4 or 8: twice
+// the bundle's query count rounded up) lanes per element, so the queries of
+// an element run side by side instead of one after another and both parties
+// fill one launch; lane 0 of each group gathers the group's shares and folds
+// the plan and the postproc.  For batches too small to fill the GPU with one
+// lane per element (the row-level truncations of the softmax and LayerNorm
+// blocks), which are bound by the latency of the sequential tree levels.
 __global__ void __launch_bounds__(kAesThreads, 1)
     trunc_bundle_pair_kernel(const PrgParams prg, const __grid_constant__ TruncLaunch a0,
                              const __grid_constant__ TruncLaunch a1, int lanes) {
@@ -206,7 +228,7 @@ __global__ void __launch_bounds__(kAesThreads, 1)
   __syncthreads();
   if (!keys_ok(ks, a0) || !keys_ok(ks + 4, a1)) return;
   const uint32_t lb = lane_base();
-  const int lsh = lanes >= 4 ? 2 : (lanes >= 2 ? 1 : 0);  // lanes per element = 1 << lsh
+  const int lsh = lanes >= 8 ? 3 : (lanes >= 4 ? 2 : 1);  // lanes per element = 1 << lsh
   const size_t n = a0.n, units = (2 * n) << lsh;           // 2 parties x n elements x lanes
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   const int lane = static_cast<int>(threadIdx.x & 31u), grp = lane & ~((1 << lsh) - 1);
@@ -214,7 +236,9 @@ __global__ void __launch_bounds__(kAesThreads, 1)
     const size_t g = g0 + threadIdx.x;  // g0 is uniform across the block: every lane reaches the shuffles
     const bool valid = g < units;
     const size_t j = g >> lsh;
-    const int q = static_cast<int>(g & ((1u << lsh) - 1u));
+    const int u = static_cast<int>(g & ((1u << lsh) - 1u));
+    const int q = u >> 1;                      // query of the lane pair
+    const uint32_t h = static_cast<uint32_t>(u & 1);  // which MMO block of a level this lane computes
     const uint32_t party = j >= n ? 1u : 0u;
     const size_t i = party ? j - n : j;
     const TruncLaunch* a = party ? &a1 : &a0;
@@ -225,15 +249,15 @@ __global__ void __launch_bounds__(kAesThreads, 1)
       const int nb = d.q_bits[q];
       const uint64_t x = nb >= 64 ? xh : (xh & ((1ull << nb) - 1ull));
       const QueryKeySmem& K = ks[4 * party + q];
-      v = walk_query(prg, lb, K, nb, x, party, seed_blk(K), party, 0, 0);
+      v = walk_query_split(prg, lb, K, nb, x, party, seed_blk(K), party, 0, h, 3u << (lane & ~1));
     }
     uint64_t pr[4];
 #pragma unroll
     for (int k = 0; k < 4; k++) {
-      const uint64_t w = __shfl_sync(0xffffffffu, v, grp + (k < (1 << lsh) ? k : 0));
-      pr[k] = k < (1 << lsh) ? w : 0ull;
+      const uint64_t w = __shfl_sync(0xffffffffu, v, grp + (2 * k < (1 << lsh) ? 2 * k : 0));
+      pr[k] = 2 * k < (1 << lsh) ? w : 0ull;
     }
-    if (valid && q == 0) combine_store(d, xh, pr, a->y, a->bools, i);
+    if (valid && u == 0) combine_store(d, xh, pr, a->y, a->bools, i);
   }
 }
 
@@ -352,12 +376,12 @@ cudaError_t launch_trunc_bundle_pair(const sufb200_ctx_s* ctx, const TruncLaunch
                                        static_cast<int>(ctx->aes_dyn_bytes));
   if (e != cudaSuccess) return e;
   if (a0.desc.nq != a1.desc.nq || a0.desc.nq < 0 || a0.desc.nq > 4) return cudaErrorInvalidValue;  // 0: no query
-  const int lanes = a0.desc.nq <= 1 ? 1 : (a0.desc.nq <= 2 ? 2 : 4);
+  const int lanes = 2 * (a0.desc.nq <= 1 ? 1 : (a0.desc.nq <= 2 ? 2 : 4));  // a lane pair per query
   const size_t units = 2 * a0.n * static_cast<size_t>(lanes);
-  // A tree level is about 1,200 instructions per lane and the levels are
-  // sequential: a small batch is bound by how many warps share an SM's issue
-  // slots, so it is spread over as many SMs as it can use (at least 128
-  // threads per CTA, so the table fill stays short).
+  // The tree levels are sequential and each is hundreds of instructions per
+  // lane: a small batch is bound by how many warps share an SM's issue slots,
+  // so it is spread over as many SMs as it can use (at least 128 threads per
+  // CTA, so the table fill stays short).
   const size_t sms = static_cast<size_t>(ctx->sm_count);
   size_t threads = ((units + sms - 1) / sms + 31) / 32 * 32;
   threads = threads < 128 ? 128 : (threads > static_cast<size_t>(kAesThreads) ? kAesThreads : threads);
