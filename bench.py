@@ -1028,12 +1028,12 @@ def cpu_softmax_baseline(args):
 
 
 # Our kernels per block (from the ncu launch list): softmax = 3 element-level
-# truncations x (range, frontier, main) + 3 row-level pair truncations + 4
-# interval-LUT gates + 8 elementwise stages; LayerNorm = 1 element-level
-# truncation x 3 + 7 row-level pair truncations + 2 LUT gates + 9 row and
-# elementwise stages.
-SOFTMAX_LAUNCHES = 24
-LAYERNORM_LAUNCHES = 21
+# truncations x (range, frontier, main) + 3 row-level pair truncations + 2
+# interval-LUT gates (both parties per launch) + 8 elementwise stages;
+# LayerNorm = 1 element-level truncation x 3 + 7 row-level pair truncations
+# + 1 LUT gate + 9 row and elementwise stages.
+SOFTMAX_LAUNCHES = 22
+LAYERNORM_LAUNCHES = 20
 
 
 def run_softmax(args, ws, rank, local):
@@ -1113,7 +1113,7 @@ def run_softmax(args, ws, rank, local):
                             "frac": round(gbs / hbm_peak, 4), "traffic": traffic,
                             "per_block_us": round(ms * 1e3, 1),
                             "note": "bytes = every stage's tensors read and written once (70 words per active "
-                                    "element); the block is a chain of 24 small launches, bound by their latency"},
+                                    "element); the block is a chain of 22 small launches, bound by their latency"},
                "cpu_baseline": cpu_softmax_baseline(args) if (ws == 1 and not args.no_cpu) else None,
                "clocks": clk.summary(), "gpu_launches": SOFTMAX_LAUNCHES * args.steps,
                "max_err_vs_double_softmax": round(err, 6), "reconstruction_ok": err < 0.03,
@@ -1240,7 +1240,7 @@ def run_layernorm(args, ws, rank, local):
                "roofline": {"bound": "hbm", "unit": "GB/s", "achieved": round(gbs, 1), "peak": hbm_peak,
                             "frac": round(gbs / hbm_peak, 4), "traffic": traffic, "per_block_us": round(ms * 1e3, 1),
                             "note": "bytes = every stage's tensors read and written once (22 words per element); "
-                                    "a chain of 21 small launches, bound by their latency"},
+                                    "a chain of 20 small launches, bound by their latency"},
                "cpu_baseline": cpu_layernorm_baseline(args) if (ws == 1 and not args.no_cpu) else None,
                "clocks": clk.summary(), "gpu_launches": LAYERNORM_LAUNCHES * args.steps,
                "max_err_vs_double_layernorm": round(err, 6), "reconstruction_ok": err < 0.02,

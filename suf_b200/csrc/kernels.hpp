@@ -76,6 +76,15 @@ struct RefFmtLaunch {
 cudaError_t launch_thr_dcf(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
 cudaError_t launch_packed_lt(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
 cudaError_t launch_interval_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, cudaStream_t st);
+// Both parties' broadcast keys over one x^ (a0 party 0, a1 party 1), one launch.
+cudaError_t launch_interval_lut_pair(const sufb200_ctx_s* ctx, const RefFmtLaunch& a0, const RefFmtLaunch& a1,
+                                     cudaStream_t st);
+// Checked form for the device blocks: both parties' broadcast interval-LUT
+// keys (device) over x^, out_words each; a status code (record_error on
+// failure).
+int interval_lut_pair_eval(const sufb200_ctx_s* ctx, const uint8_t* key0, size_t key_bytes0, const uint8_t* key1,
+                           size_t key_bytes1, const uint64_t* xs, size_t n, int out_words, uint64_t* out0,
+                           uint64_t* out1, cudaStream_t st);
 
 // Interval-LUT coefficients, the polynomial over the public x^ and the output
 // masks in one pass (broadcast key, out_words = r * (degree + 1)).

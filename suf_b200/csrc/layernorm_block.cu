@@ -235,8 +235,9 @@ extern "C" int sufb200_layernorm_block_pair(sufb200_ctx ctx, const sufb200_layer
     ln_rsqrt_open_kernel<<<gr, kThreads, 0, st>>>(v0, v1, eps, p0->rsqrt_rin + p1->rsqrt_rin, xr, rows);
     run(ln_launch_rc("layernorm rsqrt open"));
   }
-  if (run(rc) && run(sufb200_interval_lut_eval(ctx, p0->d_rsqrt_lut, p0->rsqrt_lut_bytes, 1, xr, R, 4, 0, lut0, st)))
-    run(sufb200_interval_lut_eval(ctx, p1->d_rsqrt_lut, p1->rsqrt_lut_bytes, 1, xr, R, 4, 0, lut1, st));
+  if (run(rc))
+    run(sufb200::interval_lut_pair_eval(ctx, p0->d_rsqrt_lut, p0->rsqrt_lut_bytes, p1->d_rsqrt_lut,
+                                        p1->rsqrt_lut_bytes, xr, R, 4, lut0, lut1, st));
   stage(0, nullptr, nullptr, 2);  // c1 * v
   if (run(rc)) run(ln_trunc2(ctx, p0, p1, 2, xr, R, z0, z1, st));
   stage(1, z0, z1, 3);  // y = c0 + T_f(c1 v); y * y

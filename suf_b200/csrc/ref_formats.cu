@@ -142,6 +142,65 @@ __global__ void __launch_bounds__(kAesThreads, 1) packed_lt_kernel(const RefFmtL
 }
 
 // ---- interval LUT --------------------------------------------------------
+// Round keys and (when it fits `cap` bytes) the cut/payload table of a
+// broadcast key into shared memory; true when the table was staged.
+__device__ __forceinline__ bool stage_lut_key(const RefFmtLaunch& a, uint32_t* s_rk, uint64_t* s_tab, uint32_t cap) {
+  const uint64_t h = *reinterpret_cast<const uint64_t*>(a.keys);
+  const uint32_t ivs = static_cast<uint32_t>(h >> 32), ow = static_cast<uint32_t>((h >> 16) & 0xFFFF);
+  const size_t words = static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow;
+  const bool tab_in_smem = 216u + 8u * words <= a.key_bytes && 8u * words <= cap;
+  for (int i = threadIdx.x; i < 44; i += blockDim.x) s_rk[i] = reinterpret_cast<const uint32_t*>(a.keys + 40)[i];
+  if (tab_in_smem)
+    for (size_t i = threadIdx.x; i < words; i += blockDim.x) s_tab[i] = reinterpret_cast<const uint64_t*>(a.keys + 216)[i];
+  return tab_in_smem;
+}
+
+// Element i of one interval-LUT launch: interval by binary search over the
+// cuts, then the row's share words, one AES-CTR block per two words.
+__device__ __forceinline__ void lut_element(const RefFmtLaunch& a, size_t i, const uint32_t* s_rk, const uint64_t* s_tab,
+                                            bool tab_in_smem, uint32_t lb) {
+  const uint8_t* k = a.keys + (a.broadcast ? 0 : i * a.key_bytes);
+  const uint64_t h = *reinterpret_cast<const uint64_t*>(k);
+  const int in_bits = static_cast<int>(h & 0xFFFF);
+  const int ow = static_cast<int>((h >> 16) & 0xFFFF);
+  const uint32_t ivs = static_cast<uint32_t>(h >> 32);
+  const uint32_t party = k[8];
+  uint64_t* out = reinterpret_cast<uint64_t*>(a.out) + i * static_cast<size_t>(a.out_words);
+  const size_t need = 216u + 8u * (static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow);
+  if (ow != a.out_words || ivs == 0 || need > a.key_bytes) {
+    atomicOr(a.status, kStatusBadKeyHeader);
+    for (int w = 0; w < a.out_words; w++) out[w] = 0;
+    return;
+  }
+  const uint64_t nonce = *reinterpret_cast<const uint64_t*>(k + 16);
+  const uint32_t* rk = a.broadcast ? s_rk : reinterpret_cast<const uint32_t*>(k + 40);
+  const uint64_t* cuts = (a.broadcast && tab_in_smem) ? s_tab : reinterpret_cast<const uint64_t*>(k + 216);
+  const uint64_t* pay = cuts + ivs + 1;
+  const uint64_t m = mask_bits(in_bits);
+  const uint64_t x = a.xs[i] & m;
+  int iv = static_cast<int>(ivs) - 1;
+  if (ivs > 1) {
+    int lo = 0, hi = static_cast<int>(ivs);
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if ((cuts[mid] & m) <= x) lo = mid + 1; else hi = mid;
+    }
+    iv = lo - 1;
+    if (iv < 0) iv = 0;
+    if (iv >= static_cast<int>(ivs)) iv = static_cast<int>(ivs) - 1;
+  }
+  const uint64_t idx = a.idx_base + i;
+  const uint64_t* row = pay + static_cast<size_t>(iv) * ow;
+  for (int w = 0; w < ow; w += 2) {
+    const uint64_t ctr = nonce ^ (idx << 32) ^ (static_cast<uint64_t>(iv) * static_cast<uint64_t>(ow) + w);
+    const Blk ks = aes_encrypt_smem_rk(ctr_block(ctr), lb, rk);
+    const uint64_t ks0 = (static_cast<uint64_t>(ks.w[1]) << 32) | ks.w[0];
+    const uint64_t ks1 = (static_cast<uint64_t>(ks.w[3]) << 32) | ks.w[2];
+    out[w] = party == 0 ? ks0 : (row[w] - ks0);
+    if (w + 1 < ow) out[w + 1] = party == 0 ? ks1 : (row[w + 1] - ks1);
+  }
+}
+
 __global__ void __launch_bounds__(kAesThreads, 1) interval_lut_kernel(const RefFmtLaunch a) {
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
@@ -150,62 +209,41 @@ __global__ void __launch_bounds__(kAesThreads, 1) interval_lut_kernel(const RefF
   }
   uint32_t* s_rk = reinterpret_cast<uint32_t*>(smem);
   uint64_t* s_tab = reinterpret_cast<uint64_t*>(smem + 256);  // cuts then payload
-  bool tab_in_smem = false;
-  if (a.broadcast) {
-    const uint64_t h = *reinterpret_cast<const uint64_t*>(a.keys);
-    const uint32_t ivs = static_cast<uint32_t>(h >> 32), ow = static_cast<uint32_t>((h >> 16) & 0xFFFF);
-    const size_t words = static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow;
-    tab_in_smem = 216u + 8u * words <= a.key_bytes && 8u * words <= kStageBytes;
-    for (int i = threadIdx.x; i < 44; i += blockDim.x) s_rk[i] = reinterpret_cast<const uint32_t*>(a.keys + 40)[i];
-    if (tab_in_smem)
-      for (size_t i = threadIdx.x; i < words; i += blockDim.x)
-        s_tab[i] = reinterpret_cast<const uint64_t*>(a.keys + 216)[i];
-  }
+  const bool tab_in_smem = a.broadcast ? stage_lut_key(a, s_rk, s_tab, kStageBytes) : false;
   aes_fill_tables(a.t0);
   __syncthreads();
   const uint32_t lb = lane_base();
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
-    const uint8_t* k = a.keys + (a.broadcast ? 0 : i * a.key_bytes);
-    const uint64_t h = *reinterpret_cast<const uint64_t*>(k);
-    const int in_bits = static_cast<int>(h & 0xFFFF);
-    const int ow = static_cast<int>((h >> 16) & 0xFFFF);
-    const uint32_t ivs = static_cast<uint32_t>(h >> 32);
-    const uint32_t party = k[8];
-    uint64_t* out = reinterpret_cast<uint64_t*>(a.out) + i * static_cast<size_t>(a.out_words);
-    const size_t need = 216u + 8u * (static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow);
-    if (ow != a.out_words || ivs == 0 || need > a.key_bytes) {
-      atomicOr(a.status, kStatusBadKeyHeader);
-      for (int w = 0; w < a.out_words; w++) out[w] = 0;
-      continue;
-    }
-    const uint64_t nonce = *reinterpret_cast<const uint64_t*>(k + 16);
-    const uint32_t* rk = a.broadcast ? s_rk : reinterpret_cast<const uint32_t*>(k + 40);
-    const uint64_t* cuts = (a.broadcast && tab_in_smem) ? s_tab : reinterpret_cast<const uint64_t*>(k + 216);
-    const uint64_t* pay = cuts + ivs + 1;
-    const uint64_t m = mask_bits(in_bits);
-    const uint64_t x = a.xs[i] & m;
-    int iv = static_cast<int>(ivs) - 1;
-    if (ivs > 1) {
-      int lo = 0, hi = static_cast<int>(ivs);
-      while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if ((cuts[mid] & m) <= x) lo = mid + 1; else hi = mid;
-      }
-      iv = lo - 1;
-      if (iv < 0) iv = 0;
-      if (iv >= static_cast<int>(ivs)) iv = static_cast<int>(ivs) - 1;
-    }
-    const uint64_t idx = a.idx_base + i;
-    const uint64_t* row = pay + static_cast<size_t>(iv) * ow;
-    for (int w = 0; w < ow; w += 2) {
-      const uint64_t ctr = nonce ^ (idx << 32) ^ (static_cast<uint64_t>(iv) * static_cast<uint64_t>(ow) + w);
-      const Blk ks = aes_encrypt_smem_rk(ctr_block(ctr), lb, rk);
-      const uint64_t ks0 = (static_cast<uint64_t>(ks.w[1]) << 32) | ks.w[0];
-      const uint64_t ks1 = (static_cast<uint64_t>(ks.w[3]) << 32) | ks.w[2];
-      out[w] = party == 0 ? ks0 : (row[w] - ks0);
-      if (w + 1 < ow) out[w + 1] = party == 0 ? ks1 : (row[w + 1] - ks1);
-    }
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride)
+    lut_element(a, i, s_rk, s_tab, tab_in_smem, lb);
+}
+
+// Both parties' broadcast-key gates over one x^ in one launch (elements
+// [0, n) party 0's key, [n, 2n) party 1's), spread over as many SMs as the
+// batch can use: the softmax and LayerNorm blocks' gates on 128 to 99,072
+// values, where one launch per party was latency-bound.
+__global__ void __launch_bounds__(kAesThreads, 1) interval_lut_pair_kernel(const RefFmtLaunch a0, const RefFmtLaunch a1) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
+    return;
+  }
+  uint32_t* s_rk0 = reinterpret_cast<uint32_t*>(smem);
+  uint32_t* s_rk1 = reinterpret_cast<uint32_t*>(smem + 256);
+  uint64_t* s_tab0 = reinterpret_cast<uint64_t*>(smem + 512);
+  uint64_t* s_tab1 = reinterpret_cast<uint64_t*>(smem + 512 + kStageBytes / 2);
+  const bool tab0 = stage_lut_key(a0, s_rk0, s_tab0, kStageBytes / 2);
+  const bool tab1 = stage_lut_key(a1, s_rk1, s_tab1, kStageBytes / 2);
+  aes_fill_tables(a0.t0);
+  __syncthreads();
+  const uint32_t lb = lane_base();
+  const size_t n = a0.n;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < 2 * n; g += stride) {
+    if (g < n)
+      lut_element(a0, g, s_rk0, s_tab0, tab0, lb);
+    else
+      lut_element(a1, g - n, s_rk1, s_tab1, tab1, lb);
   }
 }
 
@@ -362,6 +400,39 @@ cudaError_t launch_interval_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a,
   if (e != cudaSuccess) return e;
   interval_lut_kernel<<<grid_for(ctx, a.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st>>>(a);
   return cudaGetLastError();
+}
+
+cudaError_t launch_interval_lut_pair(const sufb200_ctx_s* ctx, const RefFmtLaunch& a0, const RefFmtLaunch& a1,
+                                     cudaStream_t st) {
+  if (!a0.broadcast || !a1.broadcast || a0.n != a1.n || a0.xs != a1.xs || a0.out_words != a1.out_words)
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(interval_lut_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  const size_t units = 2 * a0.n, sms = static_cast<size_t>(ctx->sm_count);
+  size_t threads = ((units + sms - 1) / sms + 31) / 32 * 32;  // as many SMs as the batch can use
+  threads = threads < 128 ? 128 : (threads > static_cast<size_t>(kAesThreads) ? kAesThreads : threads);
+  const size_t want = (units + threads - 1) / threads;
+  const int grid = static_cast<int>(want < sms ? (want ? want : 1) : sms);
+  interval_lut_pair_kernel<<<grid, static_cast<unsigned>(threads), ctx->aes_dyn_bytes, st>>>(a0, a1);
+  return cudaGetLastError();
+}
+
+int interval_lut_pair_eval(const sufb200_ctx_s* ctx, const uint8_t* key0, size_t key_bytes0, const uint8_t* key1,
+                           size_t key_bytes1, const uint64_t* xs, size_t n, int out_words, uint64_t* out0,
+                           uint64_t* out1, cudaStream_t st) {
+  if (n == 0) return SUFB200_OK;
+  if (out_words < 1) return record_error(SUFB200_ERR_INVALID, "out_words must be >= 1");
+  for (size_t kb : {key_bytes0, key_bytes1})
+    if (kb < 216 + 24 || kb % 8) return record_error(SUFB200_ERR_KEY, "interval key_bytes too small or not 8k");
+  const void* ptrs[5] = {key0, key1, xs, out0, out1};
+  for (const void* q : ptrs)
+    if (!q || reinterpret_cast<uintptr_t>(q) % 8) return record_error(SUFB200_ERR_INVALID, "null or misaligned pointer");
+  const RefFmtLaunch a0{key0, key_bytes0, 1, xs, n, 0, out0, 0, out_words, 0, ctx->d_t0, ctx->d_status};
+  const RefFmtLaunch a1{key1, key_bytes1, 1, xs, n, 0, out1, 0, out_words, 0, ctx->d_t0, ctx->d_status};
+  const cudaError_t e = launch_interval_lut_pair(ctx, a0, a1, st);
+  return e == cudaSuccess ? SUFB200_OK
+                          : record_error(SUFB200_ERR_CUDA, std::string("interval LUT pair launch: ") + cudaGetErrorString(e));
 }
 
 cudaError_t launch_coeff_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, const CoeffLutParams& p,

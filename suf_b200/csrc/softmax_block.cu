@@ -249,8 +249,9 @@ extern "C" int sufb200_softmax_block_pair(sufb200_ctx ctx, const sufb200_softmax
   // nExp: open t + r, coefficient LUT per party, Horner with two truncations
   open_masked_kernel<<<ge, kThreads, 0, st>>>(d_t0, d_t1, p0->nexp_rin + p1->nexp_rin, xh, n);
   run(launch_rc("softmax open"));
-  if (run(sufb200_interval_lut_eval(ctx, p0->d_nexp_lut, p0->nexp_lut_bytes, 1, xh, n, 4, 0, lut0, st)))
-    run(sufb200_interval_lut_eval(ctx, p1->d_nexp_lut, p1->nexp_lut_bytes, 1, xh, n, 4, 0, lut1, st));
+  if (run(rc))
+    run(sufb200::interval_lut_pair_eval(ctx, p0->d_nexp_lut, p0->nexp_lut_bytes, p1->d_nexp_lut, p1->nexp_lut_bytes,
+                                        xh, n, 4, lut0, lut1, st));
   if (rc == SUFB200_OK) {
     nexp_mul12_kernel<<<ge, kThreads, 0, st>>>(lut0, lut1, d_t0, d_t1, p0->d_nexp_triples, p1->d_nexp_triples, f,
                                                p0->trunc_rin[0] + p1->trunc_rin[0], xh, n);
@@ -270,8 +271,9 @@ extern "C" int sufb200_softmax_block_pair(sufb200_ctx ctx, const sufb200_softmax
                                                      e0, e1, s0, s1, sh);
     run(launch_rc("softmax row sums"));
   }
-  if (run(rc) && run(sufb200_interval_lut_eval(ctx, p0->d_recip_lut, p0->recip_lut_bytes, 1, sh, R, 4, 0, lr0, st)))
-    run(sufb200_interval_lut_eval(ctx, p1->d_recip_lut, p1->recip_lut_bytes, 1, sh, R, 4, 0, lr1, st));
+  if (run(rc))
+    run(sufb200::interval_lut_pair_eval(ctx, p0->d_recip_lut, p0->recip_lut_bytes, p1->d_recip_lut,
+                                        p1->recip_lut_bytes, sh, R, 4, lr0, lr1, st));
   if (rc == SUFB200_OK) {
     recip_init_kernel<<<gr, kThreads, 0, st>>>(lr0, lr1, s0, s1, p0->d_recip_triples, p1->d_recip_triples,
                                                p0->trunc_rin[2] + p1->trunc_rin[2], xr, rows);
