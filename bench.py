@@ -337,18 +337,46 @@ def run_ours(args, ws, rank, local):
     y_pin = {p: torch.empty(n, dtype=torch.int64).pin_memory() for p in parties}
     x_np = x_pin.numpy().view(np.uint64)
     y_np = {p: y_pin[p].numpy().view(np.uint64) for p in parties}
+    # One backend instance per party, as in the reference (each party's
+    # adapter binds its own context); with both parties on this GPU they
+    # call from their own host threads, so one party's copies overlap the
+    # other's kernels.  ctypes releases the GIL inside the C-ABI call.
+    import threading
+
+    pctx = {parties[0]: ctx}
+    for p in parties[1:]:
+        pctx[p] = Context(local)
+        pctx[p].prg_init(prg_state())
+
+    def e2e_step():
+        errs = []
+
+        def one(p):
+            try:
+                pctx[p].trunc_bundle_eval_host(descs[p], keys[p], x_np, y=y_np[p])
+            except Exception as ex:  # re-raised below, on the bench thread
+                errs.append(ex)
+
+        ths = [threading.Thread(target=one, args=(p,)) for p in parties]
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        if errs:
+            raise errs[0]
+
     for _ in range(max(1, args.warmup // 2)):
-        for p in parties:
-            ctx.trunc_bundle_eval_host(descs[p], keys[p], x_np, y=y_np[p])
+        e2e_step()
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e2e_ms = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        for p in parties:
-            ctx.trunc_bundle_eval_host(descs[p], keys[p], x_np, y=y_np[p])
+        e2e_step()
         e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    for p in parties[1:]:
+        pctx[p].close()
     e2e_ms_max = _max_over_ranks(ws, dev, sum(e2e_ms) / len(e2e_ms))
     e2e_value = total_units / (e2e_ms_max / 1e3)
 
@@ -361,6 +389,7 @@ def run_ours(args, ws, rank, local):
         y0 = d_y[0].cpu().numpy().view(np.uint64)
         y1 = d_y[1].cpu().numpy().view(np.uint64)
         ok = bool(((y0 + y1) == want).all())
+        ok = ok and bool(((y_np[0] + y_np[1]) == want).all())  # the e2e leg's host outputs too
     else:
         ok = _pair_check(ws, rank, dev, d_y[parties[0]], want)
 
@@ -402,7 +431,8 @@ def run_ours(args, ws, rank, local):
                        "l2": "256 MB buffer written between timed steps", "parallelism": f"party x element shards on {ws} GPU(s)"},
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": 8 * n * len(parties),
                     "d2h_bytes_per_step": 8 * n * len(parties), "ms_per_step": round(e2e_ms_max, 3),
-                    "path": "sufb200_trunc_bundle_eval_host (pinned host x^ in, y out)"},
+                    "path": "sufb200_trunc_bundle_eval_host (pinned host x^ in, y out; one context and "
+                            "host thread per party)"},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
