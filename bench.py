@@ -8,18 +8,26 @@ PRG), the additive boolean plan and the ARS postproc, all in one fused
 launch per party.  Metric: DCF pred-evals per second (one pred-eval = one
 (element, query, party) evaluation), whole job.
 
-At N = 1 the GPU evaluates both parties on the 4,194,304 elements (the
-reference's setting: both parties on one GPU).  At N >= 2, ranks
-[0, N/2) are party 0 and [N/2, N) party 1; each rank evaluates its party on
-its own shard of 2 x 4,194,304 elements, so per-GPU work is the same at every
-N (weak scaling) and no data-path collective is involved.
+One step is the protocol's truncation round: each party holds its masked
+share m_p = x_p + r_p of the input, the parties open x^ = m_0 + m_1 (the
+open of OpenCollector::flush), and each party evaluates its bundle on x^.
+At N = 1 the GPU holds both parties (the reference's setting) and the open
+is the local add of the two shares.  At N >= 2, ranks [0, N/2) are party 0
+and [N/2, N) party 1; paired ranks j and j + N/2 hold the same shard of
+2 x 4,194,304 elements, swap their masked shares over NVLink
+(sufb200_open_exchange: an NCCL send/recv pair, 64-bit words) and evaluate
+their party's bundle, so per-GPU work is the same at every N (weak scaling)
+and the one collective is the open between paired GPUs.
 
 Legs: `value` (inputs resident in HBM, CUDA events on the launch stream,
-L2 flushed between steps), `e2e` (host-buffer C-ABI call from pinned memory,
-copies inside the timed region), the roofline of the fused kernel, a bounded
-CPU baseline (the reference's own myl7 dcf_eval, OpenMP over elements) and
-the clocks sampled during the timed region.  `--impl reference` times only
-the reference CPU implementation on the same workload.
+L2 flushed between steps), `e2e` (host buffers, copies inside the timed
+region), the roofline of the fused kernel, a bounded CPU baseline (the
+reference's own myl7 dcf_eval, OpenMP over elements, in a child process
+that runs exactly the `--impl reference` code) and the clocks sampled during
+the timed region.  `--impl reference` times only the reference CPU
+implementation on the same workload, with keys dealt by test infrastructure
+(the oracle's truncation dealer and the reference's own dcf_gen): the
+product library is not loaded in that arm.
 """
 from __future__ import annotations
 
@@ -109,10 +117,10 @@ def inputs(r_in: int, n: int, shard: int) -> np.ndarray:
 # ---------------------------------------------------------------------------
 
 M64 = (1 << 64) - 1
-# DRAM bytes per element of trunc_bundle_prefix_kernel, from the ncu capture
-# summarised in profiles/trunc_bundle_prefix_kernel_ars_f16.md (dram read +
-# write of one 4,194,304-element launch divided by its elements): 16 B of x^
-# and y plus the random 32-byte frontier-entry reads of the four queries.
+# DRAM bytes per element of trunc_bundle_prefix_kernel, from an ncu capture
+# of one 4,194,304-element launch (dram read + write divided by its
+# elements): 16 B of x^ and y plus the random 32-byte frontier-entry reads of
+# the four queries.
 TRAFFIC_BYTES_PER_ELEMENT = 142.1
 
 
@@ -249,22 +257,28 @@ def _max_over_ranks(ws: int, dev, v: float) -> float:
     return float(t.item())
 
 
-def _timed(args, ws, dev, stream, flush, step, ctx, local, sample_clocks=True):
+def _timed(args, ws, dev, stream, flush, step, ctx, local, sample_clocks=True, mids=False):
     """W untimed steps, then K steps bracketed by a barrier and a device
     synchronize, each timed by CUDA events on the launch stream after a 256 MB
     write (> 126 MB L2); returns (max over ranks of the mean step ms, this
-    rank's step times, the clock sampler)."""
+    rank's step times, the clock sampler[, this rank's step-start -> mid-event
+    times]).  With mids=True the step is called as step(mid) and records
+    `mid` on the stream at the point whose share of the step is wanted."""
     import torch
     import torch.distributed as dist
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            step()
+            if mids:
+                step(torch.cuda.Event(enable_timing=True))
+            else:
+                step()
     ctx.sync(stream)
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    mid_evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] if mids else None
     clk = ClockSampler(local if sample_clocks else None)
     with clk:
         if sample_clocks:
@@ -273,7 +287,10 @@ def _timed(args, ws, dev, stream, flush, step, ctx, local, sample_clocks=True):
             for k in range(args.steps):
                 flush.fill_(k)
                 evs[k][0].record(stream)
-                step()
+                if mids:
+                    step(mid_evs[k])
+                else:
+                    step()
                 evs[k][1].record(stream)
         torch.cuda.synchronize()
         ctx.sync(stream)
@@ -281,7 +298,10 @@ def _timed(args, ws, dev, stream, flush, step, ctx, local, sample_clocks=True):
         dist.barrier()
     torch.cuda.synchronize()
     ms_steps = [a.elapsed_time(b) for a, b in evs]
-    return _max_over_ranks(ws, dev, sum(ms_steps) / len(ms_steps)), ms_steps, clk
+    ms_max = _max_over_ranks(ws, dev, sum(ms_steps) / len(ms_steps))
+    if mids:
+        return ms_max, ms_steps, clk, [evs[k][0].elapsed_time(mid_evs[k]) for k in range(args.steps)]
+    return ms_max, ms_steps, clk
 
 
 def _pair_check(ws: int, rank: int, dev, d_mine, want: np.ndarray) -> bool:
@@ -300,12 +320,34 @@ def _pair_check(ws: int, rank: int, dev, d_mine, want: np.ndarray) -> bool:
     return bool(flag.item())
 
 
+def masked_shares(xhat: np.ndarray, shard: int) -> tuple[np.ndarray, np.ndarray]:
+    """The two parties' masked shares of x^ = x + r_in: party p holds
+    m_p = x_p + r_p, where x = x_0 + x_1 is the secret-shared input and
+    r_in = r_0 + r_1 the dealer's split of the mask (TruncTask's masked
+    value before its open); m_0 is uniform and m_1 = x^ - m_0 mod 2^64."""
+    rng = np.random.default_rng([SEED, shard, 0x0FE4])
+    m0 = rng.integers(0, 2**64 - 1, xhat.size, dtype=np.uint64, endpoint=True)
+    return m0, xhat - m0
+
+
+def trunc_config(ws: int, n: int, parties: int, nq: int, q_bits) -> dict:
+    """The workload description both arms print (the reference arm times the
+    work one GPU of ours does at this N)."""
+    return {"workload": "configs[1]: FaithfulARS trunc bundle, f=16, |x|<2^40, seed 2",
+            "n_elements_per_party_per_gpu": n, "queries_per_element": nq, "query_bits": list(q_bits),
+            "parties_per_gpu": parties, "keys": "broadcast myl7 (AES-128-MMO PRG)",
+            "step": "open of the masked input (local add at N=1, paired-GPU exchange at N>=2) + fused bundle",
+            "l2": "256 MB buffer written between timed steps",
+            "parallelism": ("both parties on one GPU" if ws <= 1 else
+                            f"party 0 on GPUs 0..{ws // 2 - 1}, party 1 on GPUs {ws // 2}..{ws - 1}, "
+                            f"element shards, open between GPU j and j+{ws // 2}")}
+
+
 def run_ours(args, ws, rank, local):
     import torch
     import torch.distributed as dist
 
-    from suf_b200.engine import Context
-    from suf_b200 import _lib
+    from suf_b200.engine import Context, OpenComm, open_add_local, share_open_id
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -317,53 +359,95 @@ def run_ours(args, ws, rank, local):
     nq = int(descs[0].nq)
     parties, n, shard = assignment(ws, rank, args.n_elem or N_ELEM)
     xhat_h = inputs(r_in, n, shard)
+    m_h = masked_shares(xhat_h, shard)
     stream = torch.cuda.Stream(device=dev)
-    d_x = torch.from_numpy(xhat_h.view(np.int64)).to(dev)
+    d_m = {p: torch.from_numpy(m_h[p].view(np.int64)).to(dev) for p in parties}
+    d_x = torch.empty(n, dtype=torch.int64, device=dev)
     d_y = {p: torch.empty(n, dtype=torch.int64, device=dev) for p in parties}
     flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+    comm, peer = None, None
+    if ws > 1:
+        comm = OpenComm(ctx, share_open_id(rank), ws, rank, timeout_s=60.0)
+        peer = (rank + ws // 2) % ws
     torch.cuda.synchronize()
 
-    def step():
+    def open_step(d_in, d_out, st):
+        """x^ from this GPU's masked share(s): the local add with both parties
+        here, else the exchange with the paired GPU (64-bit ring, raw words)."""
+        if comm is None:
+            open_add_local(d_in[0], d_in[1], 64, d_out=d_out, stream=st)
+        else:
+            comm.exchange(peer, d_in[parties[0]], 64, 64, signed=False, d_out=d_out, stream=st)
+
+    def step(mid):
+        open_step(d_m, d_x, stream)
+        mid.record(stream)
         for p in parties:
             ctx.trunc_bundle_eval(descs[p], keys[p], d_x, d_y=d_y[p], stream=stream)
 
-    ms_max, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    ms_max, ms_steps, clk, open_ms = _timed(args, ws, dev, stream, flush, step, ctx, local, mids=True)
+    opened_ok = bool((d_x.cpu().numpy().view(np.uint64) == xhat_h).all())
+    open_ms_max = _max_over_ranks(ws, dev, sum(open_ms) / len(open_ms))
     units_per_rank = n * nq * len(parties)
     total_units = units_per_rank * ws
     value = total_units / (ms_max / 1e3)
 
-    # ---- e2e: host-buffer C-ABI entry point, pinned host memory, copies timed ----
-    x_pin = torch.from_numpy(xhat_h.view(np.int64)).pin_memory()
-    y_pin = {p: torch.empty(n, dtype=torch.int64).pin_memory() for p in parties}
-    x_np = x_pin.numpy().view(np.uint64)
-    y_np = {p: y_pin[p].numpy().view(np.uint64) for p in parties}
-    # One backend instance per party, as in the reference (each party's
-    # adapter binds its own context); with both parties on this GPU they
-    # call from their own host threads, so one party's copies overlap the
-    # other's kernels.  ctypes releases the GIL inside the C-ABI call.
+    # ---- e2e: host buffers, copies inside the timed region ----
     import threading
 
+    y_pin = {p: torch.empty(n, dtype=torch.int64).pin_memory() for p in parties}
+    y_np = {p: y_pin[p].numpy().view(np.uint64) for p in parties}
     pctx = {parties[0]: ctx}
-    for p in parties[1:]:
-        pctx[p] = Context(local)
-        pctx[p].prg_init(prg_state())
+    if ws <= 1:
+        # Both parties here: the reference-facing host call (x^ in, y out) per
+        # party, one backend instance (context) and host thread per party as
+        # in the reference, so one party's copies overlap the other's kernels.
+        x_pin = torch.from_numpy(xhat_h.view(np.int64)).pin_memory()
+        x_np = x_pin.numpy().view(np.uint64)
+        for p in parties[1:]:
+            pctx[p] = Context(local)
+            pctx[p].prg_init(prg_state())
 
-    def e2e_step():
-        errs = []
+        def e2e_step():
+            errs = []
 
-        def one(p):
-            try:
-                pctx[p].trunc_bundle_eval_host(descs[p], keys[p], x_np, y=y_np[p])
-            except Exception as ex:  # re-raised below, on the bench thread
-                errs.append(ex)
+            def one(p):
+                try:
+                    pctx[p].trunc_bundle_eval_host(descs[p], keys[p], x_np, y=y_np[p])
+                except Exception as ex:  # re-raised below, on the bench thread
+                    errs.append(ex)
 
-        ths = [threading.Thread(target=one, args=(p,)) for p in parties]
-        for th in ths:
-            th.start()
-        for th in ths:
-            th.join()
-        if errs:
-            raise errs[0]
+            ths = [threading.Thread(target=one, args=(p,)) for p in parties]
+            for th in ths:
+                th.start()
+            for th in ths:
+                th.join()
+            if errs:
+                raise errs[0]
+
+        e2e_path = ("sufb200_trunc_bundle_eval_host (pinned host x^ in, y out; one context and host thread per "
+                    "party)")
+        h2d = 8 * n * len(parties)
+    else:
+        # One party here: its masked share crosses PCIe, the open crosses
+        # NVLink, the bundle runs, y comes back.
+        p0 = parties[0]
+        m_pin = torch.from_numpy(m_h[p0].view(np.int64)).pin_memory()
+        d_me = torch.empty(n, dtype=torch.int64, device=dev)
+        d_xe = torch.empty(n, dtype=torch.int64, device=dev)
+        d_ye = torch.empty(n, dtype=torch.int64, device=dev)
+
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                d_me.copy_(m_pin, non_blocking=True)
+                comm.exchange(peer, d_me, 64, 64, signed=False, d_out=d_xe, stream=stream)
+                ctx.trunc_bundle_eval(descs[p0], keys[p0], d_xe, d_y=d_ye, stream=stream)
+                y_pin[p0].copy_(d_ye, non_blocking=True)
+            stream.synchronize()
+
+        e2e_path = ("pinned host masked share -> device, sufb200_open_exchange with the paired GPU, "
+                    "sufb200_trunc_bundle_eval, y -> pinned host")
+        h2d = 8 * n
 
     for _ in range(max(1, args.warmup // 2)):
         e2e_step()
@@ -375,6 +459,7 @@ def run_ours(args, ws, rank, local):
         t0 = time.perf_counter()
         e2e_step()
         e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    ctx.sync(stream)
     for p in parties[1:]:
         pctx[p].close()
     e2e_ms_max = _max_over_ranks(ws, dev, sum(e2e_ms) / len(e2e_ms))
@@ -392,10 +477,15 @@ def run_ours(args, ws, rank, local):
         ok = ok and bool(((y_np[0] + y_np[1]) == want).all())  # the e2e leg's host outputs too
     else:
         ok = _pair_check(ws, rank, dev, d_y[parties[0]], want)
+        ok = ok and bool((y_np[parties[0]] == d_y[parties[0]].cpu().numpy().view(np.uint64)).all())
+    if ws > 1:
+        flag = torch.tensor([1 if (ok and opened_ok) else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = bool(flag.item())
 
     peaks = measured_peaks()
     engine_peak = ctx.probe_aes_engine()  # AES-128 blocks/s of the T-table engine, measured now
-    kernel_ms = ms_max / len(parties)      # one fused call (range + frontiers + main) per party
+    kernel_ms = (ms_max - open_ms_max) / len(parties)  # one fused call (range + frontiers + main) per party
     blocks = executed_aes_blocks(descs[0], xhat_h, n)
     achieved = blocks / (kernel_ms / 1e3)
     hbm_gbs = 16.0 * n / (kernel_ms / 1e3) / 1e9  # x^ read + y written per element
@@ -410,37 +500,47 @@ def run_ours(args, ws, rank, local):
                    if launches_per_call(descs[0], n) == 3 else "trunc_bundle_kernel"),
         "peak_source": "sufb200_probe_aes_engine: the DCF walk's two-block AES-128-MMO step on every SM, "
                        "measured in this run (the table-load (LSU) and integer (ALU) pipes it saturates are the "
-                       "bound; see profiles/)",
+                       "bound)",
         "work_model": "executed AES blocks = N * sum_q 2*(n_q - D_q) + frontier sum_q roots_q * (2*(D_q - h_q) "
                       "+ 2*(2^(h_q+1) - 2))",
         "hbm": {"achieved": round(hbm_gbs, 2), "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
                 "frac": round(hbm_gbs / peaks.get("hbm_gbs", 6650.0), 5)},
         "kernel_ms": round(kernel_ms, 4),
     }
+    open_bytes = 8 * n  # 64-bit words each GPU sends (N >= 2) or the add reads twice and writes (N = 1)
+    open_info = {
+        "what": ("local add of both parties' masked shares (open_add_to_signed_kernel)" if ws <= 1 else
+                 "sufb200_open_exchange: NCCL send/recv of 64-bit words between GPU j (party 0) and GPU j+N/2 "
+                 "(party 1), then open_add_to_signed_kernel"),
+        "ms": round(open_ms_max, 4), "share_of_step": round(open_ms_max / ms_max, 4),
+        "bytes_per_gpu": open_bytes,
+        "gbs_per_gpu": round(open_bytes / (open_ms_max / 1e3) / 1e9, 1),
+        "opened_ok": opened_ok,
+    }
     out = None
     if rank == 0:
-        cpu = cpu_baseline(args, descs, keys, r_in, ws) if (ws == 1 and not args.no_cpu) else None
+        cpu = cpu_baseline(args, ws) if (ws == 1 and not args.no_cpu) else None
         out = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128", "data": "synthetic (seeded, configs[1] shapes)",
-            "config": {"workload": "configs[1]: FaithfulARS trunc bundle, f=16, |x|<2^40, seed 2",
-                       "n_elements_per_party_per_gpu": n, "queries_per_element": nq,
-                       "query_bits": [int(descs[0].q_bits[q]) for q in range(nq)],
-                       "parties_per_gpu": len(parties), "keys": "broadcast myl7 (AES-128-MMO PRG)",
-                       "l2": "256 MB buffer written between timed steps", "parallelism": f"party x element shards on {ws} GPU(s)"},
-            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": 8 * n * len(parties),
+            "config": trunc_config(ws, n, len(parties), nq, [int(descs[0].q_bits[q]) for q in range(nq)]),
+            "open": open_info,
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 8 * n * len(parties), "ms_per_step": round(e2e_ms_max, 3),
-                    "path": "sufb200_trunc_bundle_eval_host (pinned host x^ in, y out; one context and "
-                            "host thread per party)"},
+                    "path": e2e_path},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
-            # per fused call: range_kernel + frontier_kernel + the main kernel
-            "gpu_launches": args.steps * len(parties) * (launches_per_call(descs[0], n)),
+            # per step: the open's add kernel, then per party range_kernel +
+            # frontier_kernel + the main kernel (NCCL's own kernel not counted)
+            "gpu_launches": args.steps * (1 + len(parties) * launches_per_call(descs[0], n)),
             "reconstruction_ok": ok,
             "ms_per_step_all": [round(v, 4) for v in ms_steps],
         }
+    if comm is not None:
+        dist.barrier()
+        comm.close()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -460,16 +560,41 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_eval_bundle(descs, keys, xhat, parties):
+def ref_prg_state() -> np.ndarray:
+    """prg_state() computed by the oracle's mt19937_64 (no product library)."""
+    from oracle.oracle import Oracle
+
+    return Oracle().mt64(0x5EED_0002, 16).view(np.uint8).copy()
+
+
+def ref_dealer():
+    """The configs[1] bundle material dealt by test infrastructure alone: the
+    oracle's truncation dealer (composite_gen_trunc_gate's masks and query
+    rewrite, include/gates/composite_fss.hpp:645-833) and the reference's own
+    myl7 dcf_gen (oracle/_ref) with the seeds dealer() uses -- byte-identical
+    to the product dealer's material, without loading the product library."""
+    from oracle.oracle import GROUP_ADD, Oracle, RefMyl7
+
+    orc = Oracle()
+    r_in, d0, d1 = orc.trunc_gen(KIND_ARS, FRAC, SEED)
+    words = orc.mt64(SEED ^ 0x6D796C37, 4 * max(d0.nq, 1)).view(np.uint8).reshape(-1, 2, 16)
+    ref = RefMyl7(GROUP_ADD)
+    ref.prg_init(ref_prg_state())
+    keys0, keys1 = [], []
+    for q in range(d0.nq):
+        k0, k1 = ref.gen_seeded(int(d0.q_bits[q]), int(d0.q_theta[q]), (1).to_bytes(8, "little"), words[q, 0],
+                                words[q, 1])
+        keys0.append(k0)
+        keys1.append(k1)
+    return r_in, (d0, d1), (keys0, keys1)
+
+
+def cpu_eval_bundle(ref, orc, descs, keys, xhat, parties):
     """The reference CPU path of the bundle: per query, the reference's own
     myl7 dcf_eval over all elements (OpenMP in the harness), then the
     composite boolean plan + ARS postproc (oracle restatement)."""
-    from oracle.oracle import GROUP_ADD, Oracle, RefMyl7, desc_from_fields
+    from oracle.oracle import desc_from_fields
 
-    ref = RefMyl7(GROUP_ADD)
-    ref.set_threads(host_threads())
-    ref.prg_init(prg_state())
-    orc = Oracle()
     ys = []
     for p in parties:
         d = descs[p]
@@ -481,58 +606,78 @@ def cpu_eval_bundle(descs, keys, xhat, parties):
     return ys
 
 
-def cpu_baseline(args, descs, keys, r_in, ws):
-    from oracle.oracle import RefMyl7
-
-    if not RefMyl7.available():
-        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
-                "sample": "oracle/_ref not built (needs the reference checkout at build time)"}
-    n = args.cpu_sample
-    xhat = inputs(r_in, n, 0)
-    t0 = time.perf_counter()
-    cpu_eval_bundle(descs, keys, xhat, [0, 1])
-    dt = time.perf_counter() - t0
-    nq = int(descs[0].nq)
-    return {"value": round(n * nq * 2 / dt, 1), "unit": UNIT, "cores": host_threads(), "kind": "reference",
-            "sample": f"{n} elements x {nq} queries x 2 parties (the whole configs[1] batch when n = 4194304), "
-                      f"reference myl7 dcf_eval (OpenMP over elements, {host_threads()} threads) + composite "
-                      f"plan/postproc; {dt:.2f} s"}
+def cpu_baseline(args, ws):
+    """One step of the --impl reference arm on the whole batch, run in a
+    child process exactly as that arm runs (same code, same thread count, no
+    CUDA context or bench threads beside it), so the two CPU figures agree."""
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "ROLE_RANK",
+                        "MASTER_ADDR", "MASTER_PORT", "TORCHELASTIC_RUN_ID")}
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "1"]
+    if args.n_elem:
+        cmd += ["--n-elem", str(args.n_elem)]
+    try:
+        r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+        line = json.loads(r.stdout.strip().splitlines()[-1])
+    except (subprocess.TimeoutExpired, ValueError, IndexError) as ex:
+        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference", "sample": f"failed: {ex}"}
+    if "unavailable" in line:
+        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference", "sample": line["unavailable"]}
+    cb = dict(line["cpu_baseline"])
+    cb["sample"] += " (one step of the --impl reference arm, in a child process)"
+    return cb
 
 
 def run_reference(args, ws, rank):
-    from oracle.oracle import RefMyl7
+    """The reference's CPU implementation of the step on the box's host
+    cores: the reference's myl7 dcf_eval (oracle/_ref, OpenMP over elements,
+    all host threads) plus the composite plan/postproc, on the same elements
+    one GPU of our arm evaluates at this N (the open is an add and is left
+    out).  Warm-up steps run on an eighth of the batch; every timed step is
+    the whole batch.  Keys come from ref_dealer(): nothing here loads the
+    product library."""
+    from oracle.oracle import Oracle, RefMyl7
 
     if rank != 0:
         return None
     if not RefMyl7.available():
         return {"impl": "reference", "unavailable": "oracle/_ref (reference myl7 sources) was not built"}
-    from suf_b200.engine import Context
+    from oracle.oracle import GROUP_ADD
 
-    ctx = Context(-1)  # dealer only (SUFB200_HOST_ONLY): no GPU work
-    ctx.prg_init(prg_state())
-    r_in, descs, keys = dealer(ctx)
-    n = args.ref_sample
-    xhat = inputs(r_in, n, 0)
+    r_in, descs, keys = ref_dealer()
+    parties, n, shard = assignment(ws, 0, args.n_elem or N_ELEM)
+    xhat = inputs(r_in, n, shard)
     nq = int(descs[0].nq)
+    ref = RefMyl7(GROUP_ADD)
+    threads = ref.set_threads(host_threads())
+    ref.prg_init(ref_prg_state())
+    orc = Oracle()
     for _ in range(args.warmup):
-        cpu_eval_bundle(descs, keys, xhat[: max(1, n // 8)], [0, 1])
+        cpu_eval_bundle(ref, orc, descs, keys, xhat[: max(1, n // 8)], parties)
     times = []
+    ys = None
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        cpu_eval_bundle(descs, keys, xhat, [0, 1])
+        ys = cpu_eval_bundle(ref, orc, descs, keys, xhat, parties)
         times.append(time.perf_counter() - t0)
-    ctx.close()
+    ok = None
+    if len(parties) == 2:
+        x = (xhat - np.uint64(r_in)).view(np.int64)
+        ok = bool(((ys[0] + ys[1]) == (x >> FRAC).view(np.uint64)).all())
     dt = sum(times) / len(times)
-    v = n * nq * 2 / dt
+    v = n * nq * len(parties) / dt
+    sample = (f"{n} elements x {nq} queries x {len(parties)} part{'ies' if len(parties) == 2 else 'y'} per step "
+              f"(the work of one GPU of the GPU arm at N={ws}), reference myl7 dcf_eval (OpenMP over elements, "
+              f"{threads} threads) + composite plan/postproc")
     return {"metric": METRIC, "value": round(v, 1), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128", "data": "synthetic (seeded, configs[1] shapes)",
             "impl": "reference",
-            "config": {"workload": "configs[1]: FaithfulARS trunc bundle, f=16, |x|<2^40, seed 2",
-                       "sample_elements_per_step": n, "queries_per_element": nq, "parties": 2},
-            "cpu_baseline": {"value": round(v, 1), "unit": UNIT, "cores": host_threads(), "kind": "reference",
-                             "sample": f"{n} elements x {nq} queries x 2 parties per step"},
-            "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "config": trunc_config(ws, n, len(parties), nq, [int(descs[0].q_bits[q]) for q in range(nq)]),
+            "cpu_baseline": {"value": round(v, 1), "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "reconstruction_ok": ok, "s_per_step_all": [round(t, 3) for t in times]}
 
 # ---------------------------------------------------------------------------
 # configs[0]: batched single-predicate DCF compare, per-element keys
@@ -679,8 +824,8 @@ def run_compare(args, ws, rank, local):
                 "achieved": round(blocks / (kernel_ms / 1e3) / 1e9, 2), "peak": round(engine_peak / 1e9, 2),
                 "frac": round(blocks / (kernel_ms / 1e3) / engine_peak, 4),
                 "traffic": round(CMP_TRAFFIC_BYTES_PER_ELEMENT * n),
-                "traffic_source": "ncu dram read + write of one 262,144-element launch, per element "
-                                  "(profiles/myl7_eval_elem_aligned_kernel_compare.md), times this call's elements",
+                "traffic_source": "ncu dram read + write of one 262,144-element launch of this kernel, per "
+                                  "element, times this call's elements",
                 "kernel": "myl7_eval_elem_aligned_kernel",
                 "work_model": "128 AES blocks per element (2 per level x 64 levels)",
                 "hbm": {"achieved": round(hbm_bytes / (kernel_ms / 1e3) / 1e9, 1), "peak": peaks.get("hbm_gbs"),
@@ -1430,9 +1575,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=N_ELEM,
-                    help="elements of the one-pass cpu_baseline leg (default: the whole configs[1] batch)")
+                    help="elements of the compare / silu workloads' cpu_baseline leg")
     ap.add_argument("--ref-sample", type=int, default=1 << 20,
-                    help="elements per step of the --impl reference arm")
+                    help="elements per step of the compare workload's --impl reference arm")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--n-elem", type=int, default=None,
                     help="elements per party at N=1 (default: the workload's config size; smaller only for "

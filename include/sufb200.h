@@ -197,16 +197,24 @@ int sufb200_trunc_bundle_eval_host(sufb200_ctx ctx, const sufb200_trunc_desc* de
  * they evaluate -- a runtime that owns all device memory through its own
  * arena, or code that must not re-enter or grow the CUDA allocator).  The
  * bundle's keys are staged in one fixed array of SUFB200_NOALLOC_KEY_BYTES
- * (16 KiB, room for four 64-bit-input keys) that every device loading the
- * library holds until exit; the call makes no cudaMalloc / cudaFree or other
- * allocating call, and rejects (SUFB200_ERR_INVALID) a bundle whose keys,
- * each padded to 16 bytes, exceed that size.  The first call on each device
- * looks up the array's device address (cudaGetSymbolAddress) with that
- * device current, so make it before any stream capture.  All calls on a
- * device share the array and it keeps the last call's contents: calls whose
- * copies and kernels overlap on the GPU (different streams, no ordering)
- * race with each other.  Arguments, checks and outputs are otherwise those
- * of sufb200_trunc_bundle_eval. */
+ * (16 KiB; a valid bundle of four 64-bit-input keys needs 8640 bytes) that
+ * every device loading the library holds until exit; the call makes no
+ * cudaMalloc / cudaFree or other allocating call, and rejects
+ * (SUFB200_ERR_INVALID) a bundle whose keys, each padded to 16 bytes, exceed
+ * that size.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current, and with CUDA's
+ * lazy module loading it also loads the library's kernels, which allocates
+ * device memory: make one call at set-up, before the phase that must not
+ * allocate and before any stream capture.  The address stays cached for the
+ * process: after cudaDeviceReset (or a re-created primary context) do not
+ * call this entry point again.  All calls on a device share the array and it
+ * keeps the last call's contents: calls whose copies and kernels overlap on
+ * the GPU (different streams, no ordering) race with each other.  It always
+ * runs the one-pass bundle kernel (the shared-prefix path of
+ * sufb200_trunc_bundle_eval for n >= 16384 needs scratch sized by n), so it
+ * is slower than that entry point on large batches; the outputs are the
+ * same.  Arguments, checks and outputs are otherwise those of
+ * sufb200_trunc_bundle_eval. */
 int sufb200_trunc_bundle_eval_noalloc(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
                                       const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y,
                                       uint64_t* d_bools, void* stream);

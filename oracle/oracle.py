@@ -57,16 +57,35 @@ def desc_from_fields(src) -> TruncDesc:
     return d
 
 
+def reference_root() -> Path | None:
+    """The reference checkout, if this machine has one: $SUF_REFERENCE, else
+    the `reference_path` that BASELINE.json at the repository root records.
+    None when neither names an existing directory (as on a GPU box, which
+    only uses the prebuilt oracle/_ref files)."""
+    cand = os.environ.get("SUF_REFERENCE")
+    if not cand:
+        import json
+
+        try:
+            cand = json.loads((HERE.parent / "BASELINE.json").read_text()).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    return Path(cand) if cand and Path(cand).is_dir() else None
+
+
 def build_oracle(quiet: bool = True) -> None:
     """Compile liboracle.so (and oracle/_ref when the reference is present)."""
     import subprocess
 
     targets = ["oracle"]
-    if Path(os.environ.get("SUF_REFERENCE", "/root/reference"), "third_party", "myl7_fss").is_dir():
+    ref = reference_root()
+    extra = []
+    if ref is not None and (ref / "third_party" / "myl7_fss").is_dir():
+        extra = [f"REF={ref}"]
         targets.append("ref")
         if (HERE.parent / "suf_b200" / "libsufb200.so").exists():
             targets += ["drive", "softmax"]
-    subprocess.run(["make", "-C", str(HERE)] + targets, check=True,
+    subprocess.run(["make", "-C", str(HERE)] + extra + targets, check=True,
                    stdout=subprocess.DEVNULL if quiet else None)
 
 

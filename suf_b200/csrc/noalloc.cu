@@ -11,9 +11,19 @@
 // call itself allocates nothing on the device or the host.
 //
 // The array below is g_noalloc_keys: SUFB200_NOALLOC_KEY_BYTES (16 KiB)
-// bytes, enough for four 64-bit-input keys of the myl7 layout (2152 bytes
-// each, padded to 16).  Every GPU that loads the library holds these 16 KiB
-// until the process exits.
+// bytes.  A bundle has at most four keys of the myl7 layout, each at most
+// 2152 bytes (64-bit input, 8-byte payload; 2160 padded to 16), so 8640
+// bytes is the most a valid bundle needs: the size check below is a guard
+// with headroom, not a limit a valid bundle reaches.  Every GPU that loads
+// the library holds these 16 KiB until the process exits.
+//
+// Two things on the first call per device are not allocation-free: the
+// address lookup, and (with CUDA's lazy module loading, the default since
+// CUDA 12.2) loading this library's kernels into the context, which
+// allocates device memory.  A caller makes one call at set-up.  The cached
+// address is only valid for the context it was looked up in: after
+// cudaDeviceReset, or a release and re-creation of the primary context, the
+// entry point must not be called again in this process.
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -51,7 +61,7 @@ int noalloc_keys_address(int device, uint8_t** out) {
   return SUFB200_OK;
 }
 
-int noalloc_fail(int code, const char* msg) { return sufb200::record_error(code, msg); }
+int noalloc_fail(int code, const std::string& msg) { return sufb200::record_error(code, msg); }
 
 }  // namespace
 
@@ -100,7 +110,7 @@ extern "C" int sufb200_trunc_bundle_eval_noalloc(sufb200_ctx ctx, const sufb200_
       (d_bools && (reinterpret_cast<uintptr_t>(d_bools) & 7)))
     return noalloc_fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
   cudaError_t e = cudaSetDevice(ctx->device);
-  if (e != cudaSuccess) return noalloc_fail(SUFB200_ERR_CUDA, "cudaSetDevice failed");
+  if (e != cudaSuccess) return noalloc_fail(SUFB200_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
   uint8_t* base = nullptr;
   if (int rc = noalloc_keys_address(ctx->device, &base)) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -109,7 +119,9 @@ extern "C" int sufb200_trunc_bundle_eval_noalloc(sufb200_ctx ctx, const sufb200_
   // overwritten (padding, space past this bundle) are never read.
   for (int q = 0; q < desc->nq; q++) {
     e = cudaMemcpyAsync(base + a.key_off[q], keys[q], key_bytes[q], cudaMemcpyHostToDevice, st);
-    if (e != cudaSuccess) return noalloc_fail(SUFB200_ERR_CUDA, "copy of the bundle keys into the staging array failed");
+    if (e != cudaSuccess)
+      return noalloc_fail(SUFB200_ERR_CUDA,
+                          std::string("copy of the bundle keys into the staging array: ") + cudaGetErrorString(e));
   }
   a.keys = base;
   a.xhat = d_xhat;
@@ -119,6 +131,7 @@ extern "C" int sufb200_trunc_bundle_eval_noalloc(sufb200_ctx ctx, const sufb200_
   a.t0 = ctx->d_t0;
   a.status = ctx->d_status;
   e = sufb200::launch_trunc_bundle(ctx, a, st);
-  if (e != cudaSuccess) return noalloc_fail(SUFB200_ERR_CUDA, "trunc bundle launch failed");
+  if (e != cudaSuccess)
+    return noalloc_fail(SUFB200_ERR_CUDA, std::string("trunc bundle launch: ") + cudaGetErrorString(e));
   return SUFB200_OK;
 }

@@ -259,6 +259,22 @@ def open_unique_id() -> bytes:
     return bytes(buf)
 
 
+def open_add_local(d_share0, d_share1, ring_bits: int = 64, d_out=None, stream=None):
+    """The open when both parties' shares live on this GPU: d_out = share0 +
+    share1 mod 2^ring_bits, sign-extended from ring_bits (the add step of
+    OpenCollector::flush, src/runtime/open_collector.cpp:357-895, with no
+    exchange)."""
+    import torch
+
+    if d_share0.numel() != d_share1.numel():
+        raise ValueError("the two shares differ in length")
+    if d_out is None:
+        d_out = torch.empty_like(d_share0)
+    check(_lib.lib().sufb200_open_add_to_signed(_t_ptr(d_share0), _t_ptr(d_share1), _t_ptr(d_out),
+                                                d_share0.numel(), ring_bits, _stream_ptr(stream)))
+    return d_out
+
+
 def share_open_id(rank: int, group=None) -> bytes:
     """Rank 0 makes the id and every rank of the torch.distributed group gets
     it (any backend: the id is 128 host bytes)."""

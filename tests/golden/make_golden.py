@@ -1,5 +1,6 @@
 """Regenerate the golden fixtures in tests/golden/ (run in a checkout that has
-the reference at $SUF_REFERENCE, default /root/reference, and oracle/_ref built).
+the reference checkout, found by oracle.reference_root(): $SUF_REFERENCE or
+BASELINE.json's reference_path, and oracle/_ref built).
 
 * myl7_{add,xor}.npz -- key pairs made by the reference's own dcf_gen
   (oracle/_ref, third_party/myl7_fss/src/dcf.c) from fixed seeds, and both

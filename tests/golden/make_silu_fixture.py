@@ -2,7 +2,8 @@
 for the SiLU spline gate (configs[2]: f = 12, 16 segments, seed 3), run by
 oracle/_ref/silu_fixture (oracle/silu_fixture.cpp, built from the reference
 headers and src/compiler/suf_to_pfss.cpp with the adapter in dealer-only
-mode; needs the reference checkout at $SUF_REFERENCE, default /root/reference).
+mode; needs the reference checkout, found by oracle.reference_root():
+$SUF_REFERENCE or BASELINE.json's reference_path).
 
 The fixture holds the compiled coefficient program's shape (interval-LUT
 mode, degree 0, r = 4 coefficient words c0..c3), r_in, the output masks and
@@ -23,7 +24,13 @@ ROOT = HERE.parents[1]
 
 
 def main() -> None:
-    subprocess.run(["make", "-C", str(ROOT / "oracle"), "silu"], check=True)
+    sys.path.insert(0, str(ROOT))
+    from oracle.oracle import reference_root
+
+    ref = reference_root()
+    if ref is None:
+        raise SystemExit("no reference checkout: set SUF_REFERENCE")
+    subprocess.run(["make", "-C", str(ROOT / "oracle"), f"REF={ref}", "silu"], check=True)
     out = subprocess.run([str(ROOT / "oracle" / "_ref" / "silu_fixture"), "12", "3", "256"], check=True,
                          capture_output=True, text=True).stdout
     data = json.loads(out)

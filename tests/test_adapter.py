@@ -14,8 +14,10 @@ from pathlib import Path
 
 import pytest
 
+from oracle.oracle import reference_root
+
 ROOT = Path(__file__).resolve().parents[1]
-REF = Path(os.environ.get("SUF_REFERENCE", "/root/reference"))
+REF = reference_root() or Path("/nonexistent")
 CUDA_INC = "/usr/local/cuda/include"
 FLAGS = ["-std=c++17", f"-I{ROOT / 'include'}", f"-I{ROOT / 'suf_b200' / 'host'}", f"-I{CUDA_INC}"]
 

@@ -395,3 +395,42 @@ def test_ring_gemm_schedule_product_is_exact():
         for s in range(8):
             acc += tmem[:, s].astype(np.uint64) << np.uint64(8 * s)
     assert (acc == _exact_product(x, y)).all()
+
+
+def test_bench_reference_dealer_matches_product_dealer():
+    """bench.py's reference arm deals the configs[1] bundle with the oracle's
+    truncation dealer and the reference's own dcf_gen (no product library);
+    its material must equal the product dealer's byte for byte, so both arms
+    evaluate the same keys."""
+    import bench
+    from oracle.oracle import RefMyl7
+    from suf_b200.engine import Context
+
+    if not RefMyl7.available():
+        pytest.skip("oracle/_ref not built")
+    ctx = Context(-1)
+    try:
+        ctx.prg_init(bench.prg_state())
+        r1, d1, k1 = bench.dealer(ctx)
+    finally:
+        ctx.close()
+    r2, d2, k2 = bench.ref_dealer()
+    assert r1 == r2
+    assert (bench.ref_prg_state() == bench.prg_state()).all()
+    for p in (0, 1):
+        for f in ("kind", "frac_bits", "party", "nq", "carry_a", "carry_b", "sign_a", "sign_b", "wrap_q", "carry_w",
+                  "sign_w", "haty", "r_hi", "m"):
+            assert getattr(d1[p], f) == getattr(d2[p], f), f
+        assert len(k1[p]) == len(k2[p])
+        for a, b in zip(k1[p], k2[p]):
+            assert a.tobytes() == b.tobytes()
+
+
+def test_bench_masked_shares_open_to_xhat():
+    """The bench step opens x^ from the parties' masked shares."""
+    import bench
+
+    xh = np.arange(1000, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15)
+    m0, m1 = bench.masked_shares(xh, 3)
+    assert ((m0 + m1) == xh).all()
+    assert not (m0 == xh).all()

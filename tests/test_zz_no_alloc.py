@@ -54,3 +54,32 @@ def test_noalloc_matches_allocating_entry_point_twice(ctx, torch_cuda, oracle, p
         ctx.sync()
         assert (from_dev(y_na) == from_dev(y_ref)).all()
         assert (from_dev(b_na) == from_dev(b_ref)).all()
+
+
+def test_noalloc_rejects_bad_keys_before_staging(ctx, torch_cuda, oracle, prg_state):
+    """A key of the wrong size or with a header that does not match the
+    bundle is refused (SUFB200_ERR_KEY) by the host-side checks, before the
+    shared staging array is written; a valid call afterwards still matches
+    the allocating entry point."""
+    from suf_b200 import _lib
+
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(77)
+    n = 4096
+    r_in, descs, keys = trunc_material(oracle, KIND_ARS, 16, 2)
+    dx = to_dev(torch_cuda, signed_fixed(rng, n, 40) + np.uint64(r_in))
+    desc = to_product_desc(descs[0])
+    y = torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda")
+    b = torch_cuda.empty(3 * n, dtype=torch_cuda.int64, device="cuda")
+    short = [k.copy() for k in keys[0]]
+    short[0] = short[0][:-1]
+    wrong_party = [k.copy() for k in keys[0]]
+    wrong_party[1][2] ^= 1
+    for bad in (short, wrong_party):
+        with pytest.raises(_lib.SufB200Error) as ei:
+            _eval_noalloc(ctx, desc, bad, dx, y, b)
+        assert ei.value.code == _lib.ERR_KEY
+    y_ref = ctx.trunc_bundle_eval(desc, keys[0], dx)
+    _eval_noalloc(ctx, desc, keys[0], dx, y, b)
+    ctx.sync()
+    assert (from_dev(y) == from_dev(y_ref)).all()
