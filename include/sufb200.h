@@ -495,6 +495,46 @@ int sufb200_layernorm_block_pair(sufb200_ctx ctx, const sufb200_layernorm_party*
 
 /* ---- host utilities ----------------------------------------------------- */
 
+/* ---- glue of the device-resident transformer layer (both parties, one GPU) --
+ * Every party's share is computed from that party's own material; where the
+ * protocol opens a masked value, the open is the sum of both parties'
+ * masked shares (OpenCollector::flush, src/runtime/open_collector.cpp:357-895,
+ * with both shares at hand).
+ *
+ * sufb200_open_masked_pair: x^ = (a0 + r0) + (a1 + r1), the masked input of
+ * the gate after a local product (TruncTask / CubicPolyTask open of x + r_in,
+ * include/runtime/phase_tasks.hpp).
+ * sufb200_add_pair: out_p = a_p + b_p (residual adds).
+ * sufb200_relu_open_pair / sufb200_relu_update_pair: one round of the row-max
+ * tournament of nn::RowMaxDiffTask (include/nn/row_maxdiff_task.hpp):
+ * x^[r][j] = sum_p (c_p[r][2j] - c_p[r][2j+1] + r_p) opens the difference for
+ * the ReLU gate; next_p[r][j] = c_p[r][2j+1] + relu_p[r][j] = max in shares.
+ * sufb200_maxdiff_pair: t_p[r][c] = max_p[r] - x_p[r][c].
+ * sufb200_beaver_open_pair: per head h < heads, both parties' Beaver matmul
+ * shares Z_p = C_p + D B_p + A_p E (+ D E for party 0), D = X - A and E = Y - B
+ * opened from the parties' shares (nn::matmul_beaver, launch_beaver_matmul2d_kernel,
+ * cuda/cuda_primitives.cu:391-628), written as the open of the masked result
+ * out(h, m, n) = sum_p (Z_p + r[p]).  d_x[p], d_y[p], d_a[p], d_b[p], d_c[p] are
+ * two-entry host arrays of device pointers; X (h, m, k) at x + h*sx + m*ldx + k,
+ * Y (h, k, n) at y + h*sy + k*ldy + n (y_transposed: n*ldy + k), A [heads][M][K],
+ * B [heads][K][N] ([heads][N][K] transposed), C [heads][M][N] contiguous; out
+ * (h, m, n) at d_out + h*so + m*ldo + n. */
+int sufb200_open_masked_pair(const uint64_t* d_a0, const uint64_t* d_a1, uint64_t r0, uint64_t r1, uint64_t* d_xhat,
+                             size_t n, void* stream);
+int sufb200_add_pair(const uint64_t* d_a0, const uint64_t* d_b0, const uint64_t* d_a1, const uint64_t* d_b1,
+                     uint64_t* d_out0, uint64_t* d_out1, size_t n, void* stream);
+int sufb200_relu_open_pair(const uint64_t* d_c0, const uint64_t* d_c1, int rows, int width, uint64_t r0, uint64_t r1,
+                           uint64_t* d_xhat, void* stream);
+int sufb200_relu_update_pair(const uint64_t* d_c0, const uint64_t* d_c1, const uint64_t* d_relu0,
+                             const uint64_t* d_relu1, int rows, int width, uint64_t* d_next0, uint64_t* d_next1,
+                             void* stream);
+int sufb200_maxdiff_pair(const uint64_t* d_max0, const uint64_t* d_max1, const uint64_t* d_x0, const uint64_t* d_x1,
+                         int rows, int cols, uint64_t* d_t0, uint64_t* d_t1, void* stream);
+int sufb200_beaver_open_pair(const uint64_t* const* d_x, size_t sx, int ldx, const uint64_t* const* d_y, size_t sy,
+                             int ldy, int y_transposed, const uint64_t* const* d_a, const uint64_t* const* d_b,
+                             const uint64_t* const* d_c, const uint64_t* r, int heads, int M, int K, int N,
+                             uint64_t* d_out, size_t so, int ldo, void* stream);
+
 /* n successive draws of mt19937_64(seed) (the reference's mask / key RNG). */
 int sufb200_host_mt19937_64(uint64_t seed, uint64_t* out, size_t n);
 

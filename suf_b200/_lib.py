@@ -114,6 +114,13 @@ _SIGS = {
     "sufb200_host_mt19937_64": (_i, [_u64, _vp, _sz]),
     "sufb200_softmax_block_pair": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _sz, _i, _vp, _vp, _vp]),
     "sufb200_layernorm_block_pair": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _i, _u64, _u64, _vp, _vp, _vp]),
+    "sufb200_open_masked_pair": (_i, [_vp, _vp, _u64, _u64, _vp, _sz, _vp]),
+    "sufb200_add_pair": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "sufb200_relu_open_pair": (_i, [_vp, _vp, _i, _i, _u64, _u64, _vp, _vp]),
+    "sufb200_relu_update_pair": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
+    "sufb200_maxdiff_pair": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
+    "sufb200_beaver_open_pair": (_i, [_vp, _sz, _i, _vp, _sz, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz,
+                                      _i, _vp]),
 }
 
 

@@ -40,29 +40,44 @@ def _stale() -> bool:
     return any(p.stat().st_mtime > t for p in deps)
 
 
+def _compile(nvcc: str, src: Path, obj: Path, verbose: bool, ptxas_info: bool) -> str:
+    cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
+    if ptxas_info and src.suffix == ".cu":
+        cmd += ["-Xptxas", "-v"]
+    if src.suffix == ".cpp":
+        cmd = [nvcc, "-x", "cu", *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
+    return r.stderr if ptxas_info else ""
+
+
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
-    """Compile the library if any source changed; return its path."""
+    """Compile the library if any source changed; return its path.  Sources
+    compile in parallel; an object is rebuilt when its source, a shared
+    header or this recipe is newer than it."""
+    from concurrent.futures import ThreadPoolExecutor
+
     if not force and not _stale():
         return LIB
     nvcc = _nvcc()
     objdir = HERE / "_build"
     objdir.mkdir(exist_ok=True)
+    shared = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.hpp")) + [INCLUDE / "sufb200.h", Path(__file__)]
+    t_shared = max(p.stat().st_mtime for p in shared)
+    jobs = []
     objs = []
     for src in sources():
         obj = objdir / (src.name + ".o")
-        cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
-        if ptxas_info and src.suffix == ".cu":
-            cmd += ["-Xptxas", "-v"]
-        if src.suffix == ".cpp":
-            cmd = [nvcc, "-x", "cu", *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
-        if verbose:
-            print(" ".join(cmd), flush=True)
-        r = subprocess.run(cmd, capture_output=True, text=True)
-        if r.returncode != 0:
-            raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
-        if ptxas_info and r.stderr:
-            print(r.stderr, file=sys.stderr)
         objs.append(str(obj))
+        if force or ptxas_info or not obj.exists() or obj.stat().st_mtime < max(src.stat().st_mtime, t_shared):
+            jobs.append((src, obj))
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
+        for err in ex.map(lambda j: _compile(nvcc, j[0], j[1], verbose, ptxas_info), jobs):
+            if err:
+                print(err, file=sys.stderr)
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH, "-shared", "-Xcompiler", "-fopenmp", "-o", str(tmp), *objs, "-lgomp", "-ldl"]
     if verbose:

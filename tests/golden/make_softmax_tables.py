@@ -3,6 +3,9 @@ here, where the reference checkout and oracle/_ref are built):
   suf_b200/tables/softmax_suf_f12.json -- the nExp / reciprocal SUF tables
                               the reference builds (oracle/_ref/softmax_tables
                               12); the device block's dealer reads them
+  suf_b200/tables/layer_suf_f12.json -- the ReLU (row max) and 256-segment
+                              constant GeLU SUF tables of the device layer
+                              (oracle/_ref/softmax_tables 12 layer)
   softmax_ref_h1_l64.npz   -- a causal 64 x 64 block (seed 4): the input t and
                               the reference's own reconstruction of the
                               SoftmaxBlockTask output on its CPU backend
@@ -29,6 +32,9 @@ REF = HERE.parents[1] / "oracle" / "_ref"
 def main() -> None:
     js = subprocess.run([str(REF / "softmax_tables"), "12"], check=True, capture_output=True, text=True).stdout
     (HERE.parents[1] / "suf_b200" / "tables" / "softmax_suf_f12.json").write_text(js)
+    js = subprocess.run([str(REF / "softmax_tables"), "12", "layer"], check=True, capture_output=True,
+                        text=True).stdout
+    (HERE.parents[1] / "suf_b200" / "tables" / "layer_suf_f12.json").write_text(js)
     with tempfile.TemporaryDirectory() as d:
         out = Path(d) / "dump.bin"
         subprocess.run([str(REF / "ref_softmax_drive"), "--heads=1", "--len=64", "--reps=1", f"--dump={out}"],
