@@ -1460,6 +1460,209 @@ def run_softmax_reference(args, ws, rank):
 
 
 # ---------------------------------------------------------------------------
+# the 2PC transformer layer (and the 12-layer stack)
+# ---------------------------------------------------------------------------
+
+LAYER_METRIC = "2PC transformer-layer latency (configs[4]: d 768, 12 heads, d_ff 3072, seq 128, Z_2^64, f 12)"
+LAYER_STACK = 12
+HARNESS_B200 = ROOT / "suf_b200" / "_refrt" / "layer_harness_b200"
+HARNESS_REF = ROOT / "oracle" / "_ref" / "refgpu" / "layer_harness_ref"
+
+
+def _run_harness(path: Path, args_list, timeout: int = 900) -> dict:
+    """One run of a layer_harness binary; its JSON line, or {'error': ...}."""
+    if not path.exists():
+        return {"error": f"{path.relative_to(ROOT)} not built (needs the reference checkout at build time)"}
+    env = dict(os.environ)
+    env.pop("OMP_NUM_THREADS", None)  # the harness picks the reference bench's per-party thread count
+    try:
+        r = subprocess.run([str(path), *args_list], capture_output=True, text=True, timeout=timeout, env=env)
+    except subprocess.TimeoutExpired:
+        return {"error": f"timed out after {timeout} s"}
+    try:
+        return json.loads(r.stdout.strip().splitlines()[-1])
+    except (ValueError, IndexError):
+        return {"error": f"rc={r.returncode}: {r.stderr.strip()[-300:]}"}
+
+
+def _layer_float64(X, W, dims):
+    """The same pre-LN layer in float64 on the dequantised values (exact
+    LayerNorm with eps 1/1024, softmax and GeLU): the accuracy yardstick."""
+    from math import erf, sqrt
+
+    S, D, H, Dh, f = dims.S, dims.D, dims.H, dims.Dh, dims.f
+    x = X.view(np.int64).reshape(S, D) / float(1 << f)
+    w = {n: W[n].astype(np.float64) / float(1 << f) for n in W}
+
+    def ln(z):
+        mu = z.mean(axis=1, keepdims=True)
+        return (z - mu) / np.sqrt(((z - mu) ** 2).mean(axis=1, keepdims=True) + 1.0 / 1024)
+
+    qkv = ln(x) @ w["qkv"]
+    outs = []
+    for h in range(H):
+        q, k, v = (qkv[:, o + h * Dh:o + (h + 1) * Dh] for o in (0, D, 2 * D))
+        s = q @ k.T / np.sqrt(Dh)
+        e = np.exp(s - s.max(axis=1, keepdims=True))
+        outs.append(e / e.sum(axis=1, keepdims=True) @ v)
+    x2 = x + np.concatenate(outs, axis=1) @ w["o"]
+    f1 = ln(x2) @ w["ff1"]
+    g = np.vectorize(lambda z: 0.5 * z * (1.0 + erf(z / sqrt(2.0))))(f1)
+    return x2 + g @ w["ff2"]
+
+
+def run_layer(args, ws, rank, local):
+    """One configs[4] transformer layer per step on the device (both parties'
+    shares on one GPU, suf_b200.layer.TransformerLayerPair), the 12-layer
+    stack timed beside it; at N > 1 every GPU runs its own replica (the
+    layer has no cross-GPU step).  Beside it, the reference's own layer
+    runtime (nn::transformer_layer_forward on its phase executor) with this
+    engine as its PFSS backend (the drop-in, suf_b200/_refrt)."""
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200.engine import Context
+    from suf_b200.layer import LayerDims, TransformerLayerPair, synthetic_layer
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
+    ctx = Context(local)
+    ctx.prg_init(prg_state())
+    dims = LayerDims()
+    X, W = synthetic_layer(dims, seed=5)
+    lay = TransformerLayerPair(ctx, W, dims, seed=11 + rank)
+    rng = np.random.default_rng([5, rank])
+    x0 = rng.integers(0, 2**64, X.size, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        x1 = X.ravel() - x0
+    d_x = [torch.from_numpy(v.view(np.int64)).to(dev) for v in (x0, x1)]
+    d_y = [torch.empty(X.size, dtype=torch.int64, device=dev) for _ in range(2)]
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+
+    def step():
+        lay.run(d_x[0], d_x[1], d_y[0], d_y[1], stream=stream)
+
+    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    ctx.sync(stream)
+    y = (d_y[0].cpu().numpy().view(np.uint64) + d_y[1].cpu().numpy().view(np.uint64)).view(np.int64) / 4096.0
+
+    # the 12-layer stack: each layer's output shares feed the next
+    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    stack = []
+    for _ in range(2):
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            flush.fill_(0)
+            ev[0].record(stream)
+            a, b = d_x
+            for _ in range(LAYER_STACK):
+                a, b = lay.run(a, b, stream=stream)
+            ev[1].record(stream)
+        torch.cuda.synchronize()
+        stack.append(ev[0].elapsed_time(ev[1]))
+    ctx.sync(stream)
+    stack_ms = _max_over_ranks(ws, dev, min(stack))
+
+    x_pin = [torch.from_numpy(v.view(np.int64)).pin_memory() for v in (x0, x1)]
+    y_pin = [torch.empty(X.size, dtype=torch.int64).pin_memory() for _ in range(2)]
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            a, b = (v.to(dev, non_blocking=True) for v in x_pin)
+            o0, o1 = lay.run(a, b, stream=stream)
+            y_pin[0].copy_(o0, non_blocking=True)
+            y_pin[1].copy_(o1, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(2):
+        e2e_step()
+    e2e = []
+    for _ in range(max(args.steps, 5)):
+        h0 = time.perf_counter()
+        e2e_step()
+        e2e.append((time.perf_counter() - h0) * 1e3)
+    ctx.sync(stream)
+    e2e_ms = _max_over_ranks(ws, dev, sum(e2e) / len(e2e))
+    ok_e2e = bool((y_pin[0].numpy() + y_pin[1].numpy() == d_y[0].cpu().numpy() + d_y[1].cpu().numpy()).all())
+
+    res = None
+    if rank == 0:
+        acc = None
+        try:  # accuracy of the fixed-point layer against float64, off the timed path
+            yf = _layer_float64(X, W, dims)
+            acc = {"max_abs_err": round(float(np.abs(y.reshape(yf.shape) - yf).max()), 5),
+                   "mean_abs_err": round(float(np.abs(y.reshape(yf.shape) - yf).mean()), 5),
+                   "max_abs_output": round(float(np.abs(yf).max()), 4)}
+        except Exception as ex:  # noqa: BLE001 -- a report, not a gate
+            acc = {"error": str(ex)[:200]}
+        dropin = _run_harness(HARNESS_B200, ["--backend=gpu", "--layers=1", f"--iters={max(3, args.steps // 2)}"])
+        cpu = None
+        if ws == 1 and not args.no_cpu:
+            c = _run_harness(HARNESS_B200, ["--backend=cpu", "--layers=1", "--iters=2"], timeout=600)
+            cpu = ({"value": c["ms_per_layer"], "unit": "ms/layer", "cores": os.cpu_count(), "kind": "reference",
+                    "sample": "one configs[4] layer of the reference's own runtime on its OpenMP CPU backend "
+                              "(SigmaFast, SUF_FORCE_PFSS), both parties as threads, online iteration after the "
+                              f"dealer's; {c.get('omp_threads_per_party')} OpenMP threads per party"}
+                   if "ms_per_layer" in c else {"value": None, "unit": "ms/layer", "cores": 0, "kind": "reference",
+                                                "sample": c.get("error", "failed")})
+        res = {"metric": LAYER_METRIC, "value": round(ms, 4), "unit": "ms/layer", "n_gpus": ws, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False,
+               "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128",
+               "data": "synthetic: weights N(0, 0.02^2), inputs N(0, 1), quantised at f = 12 (seed 5)",
+               "config": {"workload": "configs[4]: one 2PC transformer encoder layer, pre-LN, GeLU (256-segment "
+                                      "constant SUF), 64-bit ring", "d_model": dims.D, "heads": dims.H,
+                          "d_ff": dims.Dff, "seq_len": dims.S, "batch": 1, "frac_bits": dims.f,
+                          "parties_per_gpu": 2, "stack_layers": LAYER_STACK,
+                          "l2": "256 MB flush between steps",
+                          "parallelism": "both parties on one GPU" + (f"; {ws} replicas" if ws > 1 else "")},
+               "stack_ms": round(stack_ms, 3),
+               "e2e": {"value": round(e2e_ms, 4), "unit": "ms/layer", "h2d_bytes_per_step": 2 * X.size * 8,
+                       "d2h_bytes_per_step": 2 * X.size * 8, "ms_per_step": round(e2e_ms, 4),
+                       "path": "TransformerLayerPair.run from pinned host shares of X to pinned host shares of Y",
+                       "outputs_match_device_leg": ok_e2e},
+               "accuracy_vs_float64": acc,
+               "dropin_reference_runtime": dropin,
+               "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": lay.launches() * args.steps,
+               "ms_per_step_all": [round(v, 4) for v in ms_steps]}
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return res
+
+
+def run_layer_reference(args, ws, rank):
+    """The reference's GPU build (its cuda_pfss backend and nn runtime,
+    compiled for sm_100a by oracle/Makefile's refgpu recipe) running the same
+    configs[4] layer: nn::transformer_layer_forward for both parties on
+    threads, as its bench_suf_transformer does, 64-bit ring."""
+    if rank != 0:
+        return None
+    r = _run_harness(HARNESS_REF, ["--backend=gpu", "--layers=1", f"--iters={args.steps + 1}"])
+    if "ms_per_layer" not in r:
+        return {"impl": "reference", "metric": LAYER_METRIC, "unavailable": r.get("error", "layer harness failed")}
+    st = _run_harness(HARNESS_REF, ["--backend=gpu", f"--layers={LAYER_STACK}", "--iters=2"])
+    v = r["ms_per_layer"]
+    return {"metric": LAYER_METRIC, "value": v, "unit": "ms/layer", "n_gpus": ws, "steps": args.steps,
+            "warmup": 1, "ms_per_step": v, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u64 (Z_2^64)", "data": "synthetic: weights N(0, 0.02^2), inputs N(0, 1), quantised at f = 12",
+            "impl": "reference",
+            "config": {"workload": "configs[4]: one 2PC transformer encoder layer (the reference's "
+                                   "transformer_layer_forward, bert-base shape), GeLU (256-segment constant SUF), "
+                                   "64-bit ring", "d_model": 768, "heads": 12, "d_ff": 3072, "seq_len": 128,
+                       "batch": 1, "frac_bits": 12, "parties_per_gpu": 2, "stack_layers": LAYER_STACK},
+            "stack_ms": st.get("online_ms"),
+            "cpu_baseline": {"value": v, "unit": "ms/layer", "cores": os.cpu_count(), "kind": "reference",
+                             "sample": "the reference GPU build's layer, host-orchestrated (wall clock per online "
+                                       "iteration, as its bench measures)"},
+            "e2e": {"value": v, "unit": "ms/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "harness": r}
+
+
+# ---------------------------------------------------------------------------
 # configs[4]: one layer's Beaver matmuls on the tensor cores
 # ---------------------------------------------------------------------------
 
@@ -1583,9 +1786,10 @@ def main():
                     help="elements per party at N=1 (default: the workload's config size; smaller only for "
                          "profiling)")
     ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open", "silu", "matmul", "softmax",
-                                                          "layernorm"],
+                                                          "layernorm", "layer"],
                     help="trunc: configs[1] (the headline line); compare: configs[0], per-element keys; "
-                         "open: the paired-GPU open of a configs[4] layer (N >= 2); softmax: the configs[4] "
+                         "open: the paired-GPU open of a configs[4] layer (N >= 2); layer: the configs[4] "
+                         "transformer layer (ms/layer, lower is better); softmax: the configs[4] "
                          "softmax block; layernorm: the configs[4] LayerNorm block")
     ap.add_argument("--ring-bits", type=int, default=37, help="ring of the open workload (37: the reference's "
                                                                  "measured bert-base ring)")
@@ -1601,6 +1805,8 @@ def main():
                 "unavailable": "the reference's Beaver matmul is a CUDA kernel; its CUDA-core equivalent is timed "
                                "beside ours in the ours line (cuda_core)"}
                if rank == 0 else None) if args.impl == "reference" else run_matmul(args, ws, rank, local)
+    elif args.workload == "layer":
+        out = run_layer_reference(args, ws, rank) if args.impl == "reference" else run_layer(args, ws, rank, local)
     elif args.workload == "layernorm":
         out = (run_layernorm_reference(args, ws, rank) if args.impl == "reference"
                else run_layernorm(args, ws, rank, local))

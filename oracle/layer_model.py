@@ -109,6 +109,8 @@ def layer(X: np.ndarray, W: dict, dims: Dims, sm_tables: dict | None = None, tab
         s2 = scores.reshape(H * S, S)
         m = rowmax(s2, tables["relu"])
         t = m[:, None] - s2
+        if trace is not None:
+            trace["t"] = t
         offs = np.arange(0, H * S * S + 1, S, dtype=np.int64)
         p = softmax_block(t.ravel(), offs, sm_tables).reshape(H, S, S)
         o = np.concatenate([tshift(np.matmul(p[h], v[:, h * Dh:(h + 1) * Dh]), f) for h in range(H)], axis=1)
@@ -120,7 +122,7 @@ def layer(X: np.ndarray, W: dict, dims: Dims, sm_tables: dict | None = None, tab
         f2 = tshift(matmul(g, W["ff2"]), f)
         y = x2 + f2
     if trace is not None:
-        trace.update(h1=h1, qkv=qkv, scores=scores, rowmax=m, probs=p, attn=a, x2=x2, h2=h2, f1=f1, gelu=g, f2=f2)
+        trace.update(h1=h1, qkv=qkv, scores=scores, rowmax=m, probs=p, o=o, attn=a, x2=x2, h2=h2, f1=f1, gelu=g, f2=f2)
     return y
 
 

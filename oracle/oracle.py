@@ -84,9 +84,9 @@ def build_oracle(quiet: bool = True) -> None:
         extra = [f"REF={ref}"]
         targets.append("ref")
         if (HERE.parent / "suf_b200" / "libsufb200.so").exists():
-            targets += ["drive", "softmax"]
-    subprocess.run(["make", "-C", str(HERE)] + extra + targets, check=True,
-                   stdout=subprocess.DEVNULL if quiet else None)
+            targets += ["drive", "softmax", "refgpu"]
+    subprocess.run(["make", "-C", str(HERE), f"-j{os.cpu_count() or 1}"] + extra + targets, check=True,
+                   stdout=subprocess.DEVNULL if quiet else None, stderr=subprocess.DEVNULL if quiet else None)
 
 
 class Oracle:

@@ -84,6 +84,14 @@ def load_layer_tables(path: Path = LAYER_TABLES) -> dict:
     return out
 
 
+class _nullctx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
 def _rand64(rng) -> int:
     return int(rng.integers(0, 2**64, dtype=np.uint64))
 
@@ -207,8 +215,9 @@ class TransformerLayerPair:
         def buf(n):
             return torch.empty(n, dtype=torch.int64, device=dev)
 
+        wide = max(S * 3 * D, S * Dff)  # the widest public-weight product
         self.b = {
-            "h": (buf(S * D), buf(S * D)), "acc": (buf(S * Dff), buf(S * Dff)), "xhat": buf(max(S * Dff, H * S * S)),
+            "h": (buf(S * D), buf(S * D)), "acc": (buf(wide), buf(wide)), "xhat": buf(max(wide, H * S * S)),
             "qkv": (buf(S * 3 * D), buf(S * 3 * D)), "s": (buf(H * S * S), buf(H * S * S)),
             "c": (buf(H * S * S // 2), buf(H * S * S // 2)), "c2": (buf(H * S * S // 4), buf(H * S * S // 4)),
             "relu": (buf(H * S * S // 2), buf(H * S * S // 2)), "t": (buf(H * S * S), buf(H * S * S)),
@@ -227,6 +236,8 @@ class TransformerLayerPair:
             check(L.sufb200_ring_matmul(self.ctx.h, _t_ptr(x[p]), _t_ptr(self.W[wname]), None, _t_ptr(acc[p]), 1, S,
                                         K, N, 0, _stream_ptr(stream)))
         n = S * N
+        if acc[0].numel() < n or self.b["xhat"].numel() < n or out[0].numel() < n or x[0].numel() < S * K:
+            raise ValueError("layer: a staging buffer is smaller than the product")
         xh = self.b["xhat"][:n]
         check(L.sufb200_open_masked_pair(_t_ptr(acc[0]), _t_ptr(acc[1]), C.c_uint64(tr.r[0]), C.c_uint64(tr.r[1]),
                                          _t_ptr(xh), n, _stream_ptr(stream)))
@@ -236,6 +247,8 @@ class TransformerLayerPair:
                       tr: _Trunc, out, stream):
         H = self.dims.H
         n = H * M * N
+        if self.b["xhat"].numel() < n or out[0].numel() < n:
+            raise ValueError("layer: a staging buffer is smaller than the product")
         xh = self.b["xhat"][:n]
         xs = (C.c_void_p * 2)(*[x[p].data_ptr() + 8 * off_x for p in (0, 1)])
         ys = (C.c_void_p * 2)(*[y[p].data_ptr() + 8 * off_y for p in (0, 1)])
@@ -269,10 +282,17 @@ class TransformerLayerPair:
         check(L.sufb200_maxdiff_pair(_t_ptr(cur[0]), _t_ptr(cur[1]), _t_ptr(s[0]), _t_ptr(s[1]), rows, d.S,
                                      _t_ptr(t[0]), _t_ptr(t[1]), _stream_ptr(stream)))
 
-    def run(self, d_x0, d_x1, d_y0=None, d_y1=None, stream=None):
+    def run(self, d_x0, d_x1, d_y0=None, d_y1=None, stream=None, trace: dict | None = None):
         """Both parties' shares of X ([S, D] Q f, int64 tensors on the device)
-        -> shares of the layer output.  Asynchronous on `stream`."""
+        -> shares of the layer output.  Asynchronous on `stream`.  With a
+        `trace` dict, copies of both parties' shares after each stage are
+        stored in it (for stage-by-stage checks)."""
         import torch
+
+        def keep(name, pair, n):
+            if trace is not None:
+                with torch.cuda.stream(stream) if stream is not None else _nullctx():
+                    trace[name] = (pair[0][:n].clone(), pair[1][:n].clone())
 
         d = self.dims
         S, D, H, Dh, Dff = d.S, d.D, d.H, d.Dh, d.Dff
@@ -287,19 +307,28 @@ class TransformerLayerPair:
         x = (d_x0, d_x1)
         # attention
         h = self.ln1.run(x[0], x[1], b["h"][0], b["h"][1], stream=stream)
+        keep("h1", h, S * D)
         self._matmul_trunc(h, "qkv", D, 3 * D, self.tr["qkv"], b["qkv"], stream)
+        keep("qkv", b["qkv"], S * 3 * D)
         self._beaver_trunc(b["qkv"], 0, Dh, 3 * D, b["qkv"], D, Dh, 3 * D, True, self.trip_s, S, Dh, S, S * S, S,
                            self.tr["scores"], b["s"], stream)
+        keep("scores", b["s"], H * S * S)
         self._rowmax_diff(b["s"], b["t"], stream)
+        keep("t", b["t"], H * S * S)
         self.softmax.run(b["t"][0], b["t"][1], b["p"][0], b["p"][1], stream=stream)
+        keep("probs", b["p"], H * S * S)
         self._beaver_trunc(b["p"], 0, S * S, S, b["qkv"], 2 * D, Dh, 3 * D, False, self.trip_pv, S, S, Dh, Dh, D,
                            self.tr["pv"], b["o"], stream)
+        keep("o", b["o"], S * D)
         self._matmul_trunc(b["o"], "o", D, D, self.tr["o"], b["a"], stream)
+        keep("attn", b["a"], S * D)
         check(L.sufb200_add_pair(_t_ptr(x[0]), _t_ptr(b["a"][0]), _t_ptr(x[1]), _t_ptr(b["a"][1]),
                                  _t_ptr(b["x2"][0]), _t_ptr(b["x2"][1]), S * D, _stream_ptr(stream)))
         # MLP
         h = self.ln2.run(b["x2"][0], b["x2"][1], b["h"][0], b["h"][1], stream=stream)
+        keep("h2", h, S * D)
         self._matmul_trunc(h, "ff1", D, Dff, self.tr["ff1"], b["f1"], stream)
+        keep("f1", b["f1"], S * Dff)
         n = S * Dff
         xh = b["xhat"][:n]
         g = self.gelu
@@ -307,7 +336,9 @@ class TransformerLayerPair:
                                          C.c_uint64(g.r[1]), _t_ptr(xh), n, _stream_ptr(stream)))
         for p in (0, 1):
             g.eval(self.ctx, p, xh, b["g"][p], stream)
+        keep("gelu", b["g"], S * Dff)
         self._matmul_trunc(b["g"], "ff2", Dff, D, self.tr["ff2"], b["a"], stream)
+        keep("f2", b["a"], S * D)
         check(L.sufb200_add_pair(_t_ptr(b["x2"][0]), _t_ptr(b["a"][0]), _t_ptr(b["x2"][1]), _t_ptr(b["a"][1]),
                                  _t_ptr(d_y0), _t_ptr(d_y1), S * D, _stream_ptr(stream)))
         return d_y0, d_y1
