@@ -1598,7 +1598,8 @@ def run_layer(args, ws, rank, local):
                    "max_abs_output": round(float(np.abs(yf).max()), 4)}
         except Exception as ex:  # noqa: BLE001 -- a report, not a gate
             acc = {"error": str(ex)[:200]}
-        dropin = _run_harness(HARNESS_B200, ["--backend=gpu", "--layers=1", f"--iters={max(3, args.steps // 2)}"])
+        dropin = (None if args.no_dropin else
+                  _run_harness(HARNESS_B200, ["--backend=gpu", "--layers=1", f"--iters={max(3, args.steps // 2)}"]))
         cpu = None
         if ws == 1 and not args.no_cpu:
             c = _run_harness(HARNESS_B200, ["--backend=cpu", "--layers=1", "--iters=2"], timeout=600)
@@ -1782,6 +1783,8 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=1 << 20,
                     help="elements per step of the compare workload's --impl reference arm")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-dropin", action="store_true",
+                    help="layer workload: skip the reference-runtime (drop-in) harness run beside the device layer")
     ap.add_argument("--n-elem", type=int, default=None,
                     help="elements per party at N=1 (default: the workload's config size; smaller only for "
                          "profiling)")
