@@ -15,8 +15,10 @@ At N = 1 the GPU holds both parties (the reference's setting) and the open
 is the local add of the two shares.  At N >= 2, ranks [0, N/2) are party 0
 and [N/2, N) party 1; paired ranks j and j + N/2 hold the same shard of
 2 x 4,194,304 elements, swap their masked shares over NVLink
-(sufb200_open_exchange: an NCCL send/recv pair, 64-bit words) and evaluate
-their party's bundle, so per-GPU work is the same at every N (weak scaling)
+(sufb200_p2p_open: one kernel per GPU stores its 64-bit words into the
+paired GPU's landing buffer, flags it and adds the peer's words; the NCCL
+form sufb200_open_exchange with --open-impl nccl) and evaluate their
+party's bundle, so per-GPU work is the same at every N (weak scaling)
 and the one collective is the open between paired GPUs.
 
 Legs: `value` (inputs resident in HBM, CUDA events on the launch stream,
@@ -365,17 +367,26 @@ def run_ours(args, ws, rank, local):
     d_x = torch.empty(n, dtype=torch.int64, device=dev)
     d_y = {p: torch.empty(n, dtype=torch.int64, device=dev) for p in parties}
     flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
-    comm, peer = None, None
+    comm, peer, ep = None, None, None
     if ws > 1:
-        comm = OpenComm(ctx, share_open_id(rank), ws, rank, timeout_s=60.0)
         peer = (rank + ws // 2) % ws
+        if args.open_impl == "p2p":
+            from suf_b200.engine import P2POpen, share_p2p_handles
+
+            ep = P2POpen(ctx, max_words=(n + 63) // 64 * 64)
+            ep.connect(share_p2p_handles(ep)[peer])
+        else:
+            comm = OpenComm(ctx, share_open_id(rank), ws, rank, timeout_s=60.0)
     torch.cuda.synchronize()
 
     def open_step(d_in, d_out, st):
         """x^ from this GPU's masked share(s): the local add with both parties
-        here, else the exchange with the paired GPU (64-bit ring, raw words)."""
-        if comm is None:
+        here, else the exchange with the paired GPU (64-bit ring, raw words):
+        one fused peer-store kernel (p2p) or NCCL send/recv plus an add."""
+        if ws <= 1:
             open_add_local(d_in[0], d_in[1], 64, d_out=d_out, stream=st)
+        elif ep is not None:
+            ep.exchange(d_in[parties[0]], 64, 64, signed=False, d_out=d_out, timeout_s=5.0, stream=st)
         else:
             comm.exchange(peer, d_in[parties[0]], 64, 64, signed=False, d_out=d_out, stream=st)
 
@@ -440,13 +451,14 @@ def run_ours(args, ws, rank, local):
         def e2e_step():
             with torch.cuda.stream(stream):
                 d_me.copy_(m_pin, non_blocking=True)
-                comm.exchange(peer, d_me, 64, 64, signed=False, d_out=d_xe, stream=stream)
+                open_step({p0: d_me}, d_xe, stream)
                 ctx.trunc_bundle_eval(descs[p0], keys[p0], d_xe, d_y=d_ye, stream=stream)
                 y_pin[p0].copy_(d_ye, non_blocking=True)
             stream.synchronize()
 
-        e2e_path = ("pinned host masked share -> device, sufb200_open_exchange with the paired GPU, "
-                    "sufb200_trunc_bundle_eval, y -> pinned host")
+        e2e_path = ("pinned host masked share -> device, the open with the paired GPU ("
+                    + ("sufb200_p2p_open" if ep is not None else "sufb200_open_exchange")
+                    + "), sufb200_trunc_bundle_eval, y -> pinned host")
         h2d = 8 * n
 
     for _ in range(max(1, args.warmup // 2)):
@@ -510,8 +522,10 @@ def run_ours(args, ws, rank, local):
     open_bytes = 8 * n  # 64-bit words each GPU sends (N >= 2) or the add reads twice and writes (N = 1)
     open_info = {
         "what": ("local add of both parties' masked shares (open_add_to_signed_kernel)" if ws <= 1 else
-                 "sufb200_open_exchange: NCCL send/recv of 64-bit words between GPU j (party 0) and GPU j+N/2 "
-                 "(party 1), then open_add_to_signed_kernel"),
+                 ("sufb200_p2p_open: one kernel per GPU stores its 64-bit words into the paired GPU's landing "
+                  "buffer over NVLink, flags it, waits (bounded) for the peer's flag and adds" if ep is not None else
+                  "sufb200_open_exchange: NCCL send/recv of 64-bit words between GPU j (party 0) and GPU j+N/2 "
+                  "(party 1), then open_add_to_signed_kernel")),
         "ms": round(open_ms_max, 4), "share_of_step": round(open_ms_max / ms_max, 4),
         "bytes_per_gpu": open_bytes,
         "gbs_per_gpu": round(open_bytes / (open_ms_max / 1e3) / 1e9, 1),
@@ -538,9 +552,12 @@ def run_ours(args, ws, rank, local):
             "reconstruction_ok": ok,
             "ms_per_step_all": [round(v, 4) for v in ms_steps],
         }
-    if comm is not None:
+    if comm is not None or ep is not None:
         dist.barrier()
-        comm.close()
+        if comm is not None:
+            comm.close()
+        if ep is not None:
+            ep.close()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -941,6 +958,13 @@ def run_open(args, ws, rank, local):
     comm = OpenComm(ctx, share_open_id(rank), ws, rank, timeout_s=60.0)
     peer = (rank + ws // 2) % ws
     ring = args.ring_bits
+    ep = None
+    if args.open_impl == "p2p":
+        from suf_b200.engine import P2POpen, share_p2p_handles
+
+        per0 = (args.n_elem or OPEN_WORDS) // OPEN_FLUSHES
+        ep = P2POpen(ctx, max_words=(per0 + 63) // 64 * 64 + 64)
+        ep.connect(share_p2p_handles(ep)[peer])
     eff = ring if ring <= 56 else 64  # SUF_OPEN_PACK_MAX_BITS default
     per = (args.n_elem or OPEN_WORDS) // OPEN_FLUSHES
     rng = np.random.default_rng([5, rank % (ws // 2)])
@@ -955,7 +979,10 @@ def run_open(args, ws, rank, local):
 
     def step():
         for f in range(OPEN_FLUSHES):
-            comm.exchange(peer, d_in[f], eff, ring, signed=True, d_out=d_out[f], stream=stream)
+            if ep is not None:
+                ep.exchange(d_in[f], eff, ring, signed=True, d_out=d_out[f], timeout_s=5.0, stream=stream)
+            else:
+                comm.exchange(peer, d_in[f], eff, ring, signed=True, d_out=d_out[f], stream=stream)
 
     ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
     want = x.copy()
@@ -986,10 +1013,15 @@ def run_open(args, ws, rank, local):
                             "frac": round(gbs / NVLINK_GBS, 4), "traffic": wire,
                             "note": "bytes each GPU sends per step / step time, vs the measured peer copy per "
                                     "direction; 120 flushes of 139 K words are latency-bound"},
-               "clocks": clk.summary(), "gpu_launches": args.steps * OPEN_FLUSHES * (2 if eff < 64 else 1),
+               "open_impl": ("sufb200_p2p_open: pack, peer stores over NVLink, flag, bounded wait, add in one "
+                             "kernel" if ep is not None else "sufb200_open_exchange: pack, NCCL send/recv, add"),
+               "clocks": clk.summary(),
+               "gpu_launches": args.steps * OPEN_FLUSHES * (1 if ep is not None else (2 if eff < 64 else 1)),
                "opened_ok": ok, "ms_per_flush": round(ms / OPEN_FLUSHES, 4),
                "ms_per_step_all": [round(v, 4) for v in ms_steps]}
     dist.barrier()
+    if ep is not None:
+        ep.close()
     comm.close()
     dist.destroy_process_group()
     ctx.close()
@@ -1794,6 +1826,9 @@ def main():
                          "open: the paired-GPU open of a configs[4] layer (N >= 2); layer: the configs[4] "
                          "transformer layer (ms/layer, lower is better); softmax: the configs[4] "
                          "softmax block; layernorm: the configs[4] LayerNorm block")
+    ap.add_argument("--open-impl", default="p2p", choices=["nccl", "p2p"],
+                    help="the open between paired GPUs (N >= 2; headline and open workloads): the one-kernel "
+                         "peer-store open (sufb200_p2p_open, default) or NCCL send/recv (sufb200_open_exchange)")
     ap.add_argument("--ring-bits", type=int, default=37, help="ring of the open workload (37: the reference's "
                                                                  "measured bert-base ring)")
     args = ap.parse_args()

@@ -373,6 +373,30 @@ int sufb200_open_comm_abort(sufb200_open_comm comm);
 int sufb200_open_exchange(sufb200_open_comm comm, int peer, const uint64_t* d_local, size_t n, int eff_bits,
                           int ring_bits, int signed_out, uint64_t* d_out, void* stream);
 
+/* ---- paired-GPU open in one kernel (peer stores over NVLink) ---------------
+ * The same exchange as sufb200_open_exchange, fused: one kernel packs this
+ * rank's shares to eff_bits-wide words (the pack_eff_bits wire format of
+ * OpenCollector::flush, src/runtime/open_collector.cpp:357-895,
+ * cuda/pfss_kernels.cu:722-812), stores them straight into the paired GPU's
+ * landing buffer, raises a per-CTA flag there, waits for the peer's flag and
+ * writes d_out = local + peer (mod 2^ring_bits, sign-extended when
+ * signed_out).  sufb200_p2p_open_create allocates this rank's landing buffer
+ * (room for max_words packed words per call, cudaMalloc) and writes the
+ * SUFB200_P2P_HANDLE_BYTES blob the peer passes to sufb200_p2p_open_connect
+ * (out of band).  Both ranks call exchange with the same n / eff_bits /
+ * ring_bits, on one stream each, in the same order.  Waits are bounded by
+ * timeout_s: a peer that does not call ends the kernel with
+ * SUFB200_ERR_CUDA from sufb200_ctx_sync (status: timeout) and d_out
+ * undefined.  The two ranks must be on different GPUs (connect refuses a
+ * peer on the same device). */
+#define SUFB200_P2P_HANDLE_BYTES 128
+typedef struct sufb200_p2p_open_s* sufb200_p2p_open;
+int sufb200_p2p_open_create(sufb200_ctx ctx, size_t max_words, sufb200_p2p_open* out, uint8_t* handle_out);
+int sufb200_p2p_open_connect(sufb200_p2p_open h, const uint8_t* peer_handle);
+int sufb200_p2p_open_exchange(sufb200_p2p_open h, const uint64_t* d_local, size_t n, int eff_bits, int ring_bits,
+                              int signed_out, uint64_t* d_out, double timeout_s, void* stream);
+int sufb200_p2p_open_destroy(sufb200_p2p_open h);
+
 /* local + remote, sign-extended to ring_bits (launch_open_add_to_signed_kernel). */
 int sufb200_open_add_to_signed(const uint64_t* d_local, const uint64_t* d_remote, uint64_t* d_out, size_t n,
                                int ring_bits, void* stream);

@@ -323,6 +323,52 @@ class OpenComm:
             check(self._L.sufb200_open_comm_destroy(h))
 
 
+class P2POpen:
+    """The paired-GPU open in one kernel (sufb200_p2p_open_*): this rank's
+    landing buffer, mapped by the peer, receives the peer's packed shares by
+    direct peer stores over NVLink.  `handles` is every rank's export blob
+    (share_p2p_handles gathers them); the endpoint connects to `peer`'s."""
+
+    HANDLE_BYTES = 128
+
+    def __init__(self, ctx: Context, max_words: int):
+        self._L = ctx._L
+        self.ctx = ctx
+        h = C.c_void_p()
+        buf = (C.c_uint8 * self.HANDLE_BYTES)()
+        check(self._L.sufb200_p2p_open_create(ctx.h, int(max_words), C.byref(h), C.cast(buf, C.c_void_p)))
+        self.h = h
+        self.handle = bytes(buf)
+
+    def connect(self, peer_handle: bytes) -> None:
+        buf = (C.c_uint8 * self.HANDLE_BYTES).from_buffer_copy(peer_handle)
+        check(self._L.sufb200_p2p_open_connect(self.h, C.cast(buf, C.c_void_p)))
+
+    def exchange(self, d_local, eff_bits: int, ring_bits: int, signed: bool = False, d_out=None, timeout_s=2.0,
+                 stream=None):
+        import torch
+
+        if d_out is None:
+            d_out = torch.empty_like(d_local)
+        check(self._L.sufb200_p2p_open_exchange(self.h, _t_ptr(d_local), d_local.numel(), eff_bits, ring_bits,
+                                                int(signed), _t_ptr(d_out), float(timeout_s), _stream_ptr(stream)))
+        return d_out
+
+    def close(self) -> None:
+        if self.h:
+            h, self.h = self.h, C.c_void_p()
+            check(self._L.sufb200_p2p_open_destroy(h))
+
+
+def share_p2p_handles(ep: P2POpen, group=None) -> list:
+    """Every rank's P2P export blob, gathered over torch.distributed (any backend)."""
+    import torch.distributed as dist
+
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, ep.handle, group=group)
+    return out
+
+
 # -- key builders for the reference formats (host) ---------------------------------
 
 def thr_dcf_key(in_bits: int, alpha: int, payload: bytes) -> np.ndarray:

@@ -141,3 +141,112 @@ def test_open_comm_create_times_out_without_peer():
     assert procs[0].exitcode == 0
     what, dt = q.get(timeout=5)
     assert what == "error" and dt < 60, (what, dt)
+
+
+# ---- the open in one kernel: peer stores over NVLink (sufb200_p2p_open_*) ----
+
+def _p2p_worker(rank: int, port: int, q):
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200.engine import Context, OpenComm, P2POpen, share_open_id, share_p2p_handles
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    torch.cuda.set_device(rank)
+    ctx = Context(rank)
+    ep = P2POpen(ctx, max_words=(1 << 20) + 64)
+    comm = OpenComm(ctx, share_open_id(rank), 2, rank, timeout_s=60.0)
+    try:
+        ep.connect(share_p2p_handles(ep)[1 - rank])
+        stream = torch.cuda.Stream()
+        results = []
+        for ci, (n, eff, ring, signed) in enumerate(CASES):
+            rng = np.random.default_rng([9, ci])  # same values on both ranks
+            x = rng.integers(0, 2**63, n, dtype=np.uint64) * np.uint64(2) + rng.integers(0, 2, n, dtype=np.uint64)
+            s0 = rng.integers(0, 2**63, n, dtype=np.uint64) * np.uint64(3)
+            m = np.uint64((1 << ring) - 1) if ring < 64 else np.uint64(~np.uint64(0))
+            s0 &= m
+            s1 = (x - s0) & m
+            d = torch.from_numpy((s0 if rank == 0 else s1).view(np.int64)).cuda()
+            outs = []
+            for _ in range(3):  # three calls in a row: both landing halves, flags of rising value
+                outs.append(ep.exchange(d, eff, ring, signed=signed, timeout_s=10.0, stream=stream))
+            ref = comm.exchange(1 - rank, d, eff, ring, signed=signed, stream=stream)
+            ctx.sync(stream)
+            want = _expected(x, ring, signed)
+            ok = all(bool((o.cpu().numpy().view(np.uint64) == want).all()) for o in outs)
+            ok = ok and bool((ref.cpu().numpy() == outs[-1].cpu().numpy()).all())  # same words as the NCCL path
+            results.append(ok)
+        dist.barrier()
+        q.put((rank, results))
+    finally:
+        ep.close()
+        comm.close()
+        ctx.close()
+        dist.destroy_process_group()
+
+
+def test_p2p_open_two_gpus():
+    """The fused open equals the plain Z_2^ring arithmetic and the NCCL path,
+    word for word, for packed and raw flushes, three calls in a row."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    port = _free_port()
+    procs, q = _run(_p2p_worker, lambda r, q: (r, port, q))
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert res[0] == res[1] == [True] * len(CASES), res
+
+
+def _p2p_silent_peer_worker(rank: int, port: int, q):
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200 import SufB200Error
+    from suf_b200.engine import Context, P2POpen, share_p2p_handles
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    torch.cuda.set_device(rank)
+    ctx = Context(rank)
+    ep = P2POpen(ctx, max_words=4096)
+    try:
+        ep.connect(share_p2p_handles(ep)[1 - rank])
+        dist.barrier()
+        what, dt = "idle", 0.0
+        if rank == 0:  # rank 1 never calls: rank 0's wait must end by itself
+            d = torch.arange(1000, dtype=torch.int64, device="cuda")
+            t0 = time.time()
+            ep.exchange(d, 37, 37, timeout_s=0.5)
+            try:
+                ctx.sync()
+                what = "completed"
+            except SufB200Error as e:
+                what = "timeout" if "bounded wait" in str(e) else f"other: {e}"
+            dt = time.time() - t0
+            ctx.sync()  # the status was cleared: the context stays usable
+        dist.barrier()
+        q.put((rank, what, dt))
+    finally:
+        ep.close()
+        ctx.close()
+        dist.destroy_process_group()
+
+
+def test_p2p_open_times_out_when_the_peer_never_calls():
+    """A peer that never calls ends the waiting kernel after its bounded wait
+    (the kernel returns; sufb200_ctx_sync reports the timeout)."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    port = _free_port()
+    procs, q = _run(_p2p_silent_peer_worker, lambda r, q: (r, port, q), timeout=180)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = {r: (w, dt) for r, w, dt in (q.get(timeout=5) for _ in range(2))}
+    assert res[0][0] == "timeout" and res[0][1] < 30, res
