@@ -697,6 +697,141 @@ def run_reference(args, ws, rank):
             "reconstruction_ok": ok, "s_per_step_all": [round(t, 3) for t in times]}
 
 # ---------------------------------------------------------------------------
+# configs[1] secondary case: per-element masks (SUF_PER_ELEMENT_MASKS=1)
+# ---------------------------------------------------------------------------
+
+ELEM_METRIC = ("DCF pred-evals/sec (FaithfulARS trunc bundle with per-element masks: every element its own gate and "
+               "keys, 4 queries/element)")
+
+
+def elem_material(ctx, n: int, shard: int, dev):
+    """Per-element configs[1] gates (seed 2) and both parties' per-element
+    keys, made on the device (sufb200_myl7_gen_batch_device), one array per
+    query slot."""
+    import torch
+
+    from suf_b200.engine import Context, host_mt19937_64, myl7_key_bytes
+
+    r_in, s0, s1, w0, w1, th = Context.trunc_gen_elem(KIND_ARS, FRAC, SEED + (shard << 40), n)
+    nq = int(s0.nq)
+    keys = ([], [])
+    kb = []
+    for q in range(nq):
+        nb = int(s0.q_bits[q])
+        kb.append(myl7_key_bytes(nb, 8))
+        seeds = torch.from_numpy(host_mt19937_64((SEED << 8) ^ (shard << 4) ^ q, 4 * n).view(np.uint8)).to(dev)
+        seeds = seeds.view(n, 2, 16)
+        d_alpha = torch.from_numpy(np.ascontiguousarray(th[:, q]).view(np.int64)).to(dev)
+        k0, k1 = ctx.myl7_gen_batch_device(0, nb, d_alpha, (1).to_bytes(8, "little"), seeds[:, 0].contiguous(),
+                                           seeds[:, 1].contiguous())
+        keys[0].append(k0)
+        keys[1].append(k1)
+        del seeds, d_alpha
+    words = tuple(torch.from_numpy(w.view(np.int64).ravel()).to(dev) for w in (w0, w1))
+    return r_in, (s0, s1), keys, kb, words
+
+
+def run_trunc_elem(args, ws, rank, local):
+    """Both parties' per-element configs[1] gates on one GPU per step
+    (replicas at N > 1: per-element gates have no shared state to exchange
+    beyond the open, which the headline line measures)."""
+    import torch
+    import torch.distributed as dist
+
+    from suf_b200.engine import Context
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
+    ctx = Context(local)
+    ctx.prg_init(prg_state())
+    n = args.n_elem or N_ELEM
+    r_in, shapes, keys, kb, words = elem_material(ctx, n, rank, dev)
+    nq = int(shapes[0].nq)
+    rng = np.random.default_rng([SEED, rank, 0xE1])
+    x = rng.integers(-(2**40) + 1, 2**40, n, dtype=np.int64).view(np.uint64)
+    xhat_h = x + r_in
+    d_x = torch.from_numpy(xhat_h.view(np.int64)).to(dev)
+    d_y = [torch.empty(n, dtype=torch.int64, device=dev) for _ in range(2)]
+    stream = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+    torch.cuda.synchronize()
+
+    def step():
+        for p in (0, 1):
+            ctx.trunc_bundle_eval_elem(shapes[p], keys[p], kb, words[p], d_x, d_y=d_y[p], stream=stream)
+
+    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    want = (x.view(np.int64) >> FRAC).view(np.uint64)
+    ok = bool(((d_y[0].cpu().numpy().view(np.uint64) + d_y[1].cpu().numpy().view(np.uint64)) == want).all())
+
+    x_pin = torch.from_numpy(xhat_h.view(np.int64)).pin_memory()
+    y_pin = [torch.empty(n, dtype=torch.int64).pin_memory() for _ in range(2)]
+    d_xe = torch.empty_like(d_x)
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            d_xe.copy_(x_pin, non_blocking=True)
+            for p in (0, 1):
+                ctx.trunc_bundle_eval_elem(shapes[p], keys[p], kb, words[p], d_xe, d_y=d_y[p], stream=stream)
+                y_pin[p].copy_(d_y[p], non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(2):
+        e2e_step()
+    e2e = []
+    for _ in range(args.steps):
+        h0 = time.perf_counter()
+        e2e_step()
+        e2e.append((time.perf_counter() - h0) * 1e3)
+    ctx.sync(stream)
+    e2e_ms = _max_over_ranks(ws, dev, sum(e2e) / len(e2e))
+    ok = ok and bool(((y_pin[0].numpy().view(np.uint64) + y_pin[1].numpy().view(np.uint64)) == want).all())
+
+    units = n * nq * 2
+    engine_peak = ctx.probe_aes_engine()
+    bits = [int(shapes[0].q_bits[q]) for q in range(nq)]
+    blocks = n * 2 * sum(bits)  # one party's call: two AES blocks per level, every level of every key
+    kernel_ms = ms / 2
+    key_bytes = n * sum(kb)
+    hbm = (key_bytes + n * (8 + 48 + 8)) / (kernel_ms / 1e3) / 1e9  # keys + x^ + words + y per party call
+    peaks = measured_peaks()
+    res = None
+    if rank == 0:
+        res = {"metric": ELEM_METRIC, "value": round(units * ws / (ms / 1e3), 1), "unit": UNIT, "n_gpus": ws,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Z_2^64), AES-128",
+               "data": "synthetic (seeded, configs[1] shapes; per-element gates from seed 2)",
+               "config": {"workload": "configs[1] secondary: FaithfulARS, f=16, |x|<2^40, per-element masks "
+                                      "(SUF_PER_ELEMENT_MASKS=1)", "n_elements_per_party_per_gpu": n,
+                          "query_bits": bits, "key_bytes_per_element_per_party": sum(kb), "parties_per_gpu": 2,
+                          "l2": "256 MB flush between steps (the 45 GB of keys exceed L2 anyway)",
+                          "parallelism": "both parties on one GPU" + (f"; {ws} replicas" if ws > 1 else "")},
+               "e2e": {"value": round(units * ws / (e2e_ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": 8 * n,
+                       "d2h_bytes_per_step": 16 * n, "ms_per_step": round(e2e_ms, 3),
+                       "path": "pinned host x^ in, both parties' y out; the per-element keys are dealer material "
+                               "resident on the device (offline phase)"},
+               "roofline": {"bound": "lsu", "unit": "G AES-128 blocks/s",
+                            "achieved": round(blocks / (kernel_ms / 1e3) / 1e9, 2),
+                            "peak": round(engine_peak / 1e9, 2),
+                            "frac": round(blocks / (kernel_ms / 1e3) / engine_peak, 4),
+                            "kernel": "trunc_bundle_elem_kernel<true>", "traffic": None,
+                            "work_model": "every element walks every level of its own four keys: 2 AES blocks per "
+                                          "level, 160 levels per element per party",
+                            "hbm": {"achieved": round(hbm, 1), "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
+                                    "frac": round(hbm / peaks.get("hbm_gbs", 6650.0), 4),
+                                    "bytes_per_element_per_party": sum(kb) + 64}},
+               "cpu_baseline": None, "clocks": clk.summary(), "gpu_launches": 2 * args.steps,
+               "reconstruction_ok": ok, "ms_per_step_all": [round(v, 4) for v in ms_steps]}
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return res
+
+
+# ---------------------------------------------------------------------------
 # configs[0]: batched single-predicate DCF compare, per-element keys
 # ---------------------------------------------------------------------------
 
@@ -1821,7 +1956,7 @@ def main():
                     help="elements per party at N=1 (default: the workload's config size; smaller only for "
                          "profiling)")
     ap.add_argument("--workload", default="trunc", choices=["trunc", "compare", "open", "silu", "matmul", "softmax",
-                                                          "layernorm", "layer"],
+                                                          "layernorm", "layer", "trunc_elem"],
                     help="trunc: configs[1] (the headline line); compare: configs[0], per-element keys; "
                          "open: the paired-GPU open of a configs[4] layer (N >= 2); layer: the configs[4] "
                          "transformer layer (ms/layer, lower is better); softmax: the configs[4] "
@@ -1843,6 +1978,11 @@ def main():
                 "unavailable": "the reference's Beaver matmul is a CUDA kernel; its CUDA-core equivalent is timed "
                                "beside ours in the ours line (cuda_core)"}
                if rank == 0 else None) if args.impl == "reference" else run_matmul(args, ws, rank, local)
+    elif args.workload == "trunc_elem":
+        out = ({"impl": "reference", "metric": ELEM_METRIC,
+                "unavailable": "the reference's per-element path evaluates one composite gate per element on its "
+                               "host runtime; no batch CPU implementation to time at this size"}
+               if rank == 0 else None) if args.impl == "reference" else run_trunc_elem(args, ws, rank, local)
     elif args.workload == "layer":
         out = run_layer_reference(args, ws, rank) if args.impl == "reference" else run_layer(args, ws, rank, local)
     elif args.workload == "layernorm":

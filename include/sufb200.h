@@ -189,6 +189,31 @@ int sufb200_trunc_bundle_eval_host(sufb200_ctx ctx, const sufb200_trunc_desc* de
                                    const size_t* key_bytes, const uint64_t* xhat, size_t n, uint64_t* y,
                                    uint64_t* bools);
 
+/* Per-element masks (the reference's SUF_PER_ELEMENT_MASKS=1: one whole gate
+ * per element, compiler::lower_truncation_gate with per_element_masks,
+ * include/compiler/truncation_lowering.hpp:91-125, evaluated element by
+ * element by TruncTask).  sufb200_trunc_gen_elem deals n such gates: element
+ * i is sufb200_trunc_gen(kind, frac_bits, rng_seed + i * 0x9E3779B97F4A7C15);
+ * shape0/1 get the fixed query slots (64-bit queries first, then the two
+ * f-bit carry queries: TR [64, f, f], ARS [64, 64, f, f], GapARS [f, f]);
+ * thetas[4 i + q] is element i's threshold for slot q (an element without
+ * carry queries, r_low = 0, gets 0 in the f-bit slots and its plan marks the
+ * carry absent); words[6 i ..] per party = carry_w, sign_w, haty, r_hi, m
+ * and the plan (query indices carry_a, carry_b, sign_a, sign_b, wrap_q, 4
+ * bits each, 0xF = absent); r_in[i] is element i's mask.  The caller makes
+ * slot q's per-element keys (myl7, in_bits q_bits[q], alpha thetas[4 i + q],
+ * payload u64 1).
+ * sufb200_trunc_bundle_eval_elem evaluates one party's n gates in one
+ * launch, one element per thread: d_keys[q] (device) is slot q's key array
+ * [n][key_bytes[q]], d_words (device) the party's words; d_y [n], d_bools
+ * [n][3] or NULL. */
+int sufb200_trunc_gen_elem(int kind, int frac_bits, uint64_t rng_seed, size_t n, sufb200_trunc_desc* shape0,
+                           sufb200_trunc_desc* shape1, uint64_t* words0, uint64_t* words1, uint64_t* thetas,
+                           uint64_t* r_in);
+int sufb200_trunc_bundle_eval_elem(sufb200_ctx ctx, const sufb200_trunc_desc* shape, const uint8_t* const* d_keys,
+                                   const size_t* key_bytes, const uint64_t* d_words, const uint64_t* d_xhat, size_t n,
+                                   uint64_t* d_y, uint64_t* d_bools, void* stream);
+
 /* Size of the fixed key staging array of sufb200_trunc_bundle_eval_noalloc. */
 #define SUFB200_NOALLOC_KEY_BYTES 16384
 

@@ -393,6 +393,53 @@ int sufb200_trunc_gen(int kind, int frac_bits, uint64_t rng_seed, sufb200_trunc_
   return SUFB200_OK;
 }
 
+int sufb200_trunc_gen_elem(int kind, int frac_bits, uint64_t rng_seed, size_t n, sufb200_trunc_desc* shape0,
+                           sufb200_trunc_desc* shape1, uint64_t* words0, uint64_t* words1, uint64_t* thetas,
+                           uint64_t* r_in) {
+  if (!shape0 || !shape1 || (n && (!words0 || !words1 || !thetas || !r_in))) return fail(SUFB200_ERR_INVALID, "null pointer");
+  if (sufb200::host::trunc_gen_elem(kind, frac_bits, rng_seed, n, shape0, shape1, words0, words1, thetas, r_in))
+    return fail(SUFB200_ERR_INVALID, "bad truncation kind / frac_bits");
+  return SUFB200_OK;
+}
+
+int sufb200_trunc_bundle_eval_elem(sufb200_ctx ctx, const sufb200_trunc_desc* shape, const uint8_t* const* d_keys,
+                                   const size_t* key_bytes, const uint64_t* d_words, const uint64_t* d_xhat, size_t n,
+                                   uint64_t* d_y, uint64_t* d_bools, void* stream) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (!shape || !d_keys || !key_bytes) return fail(SUFB200_ERR_INVALID, "null pointer");
+  if (shape->nq < 0 || shape->nq > 4) return fail(SUFB200_ERR_UNSUPPORTED, "bundle has more than 4 slots");
+  if (shape->kind < 0 || shape->kind > 2 || shape->party < 0 || shape->party > 1 || shape->frac_bits < 0 ||
+      shape->frac_bits > 64)
+    return fail(SUFB200_ERR_INVALID, "bad kind / party / frac_bits");
+  if (n == 0) return SUFB200_OK;
+  if (!d_words || !d_xhat || !d_y || !aligned8(d_words) || !aligned8(d_xhat) || !aligned8(d_y) ||
+      (d_bools && !aligned8(d_bools)))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  sufb200::TruncElemLaunch a{};
+  a.shape = *shape;
+  bool aligned = true;
+  for (int q = 0; q < shape->nq; q++) {
+    const int nb = shape->q_bits[q];
+    if (nb < 1 || nb > 64) return fail(SUFB200_ERR_INVALID, "slot in_bits out of range");
+    if (!d_keys[q]) return fail(SUFB200_ERR_INVALID, "null key array");
+    if (key_bytes[q] != sufb200::host::myl7_key_bytes(nb, 8))
+      return fail(SUFB200_ERR_KEY, "key size does not match an 8-byte myl7 key of the slot's width");
+    a.keys[q] = d_keys[q];
+    a.key_bytes[q] = key_bytes[q];
+    aligned = aligned && (key_bytes[q] % 8 == 0) && (reinterpret_cast<uintptr_t>(d_keys[q]) % 8 == 0);
+  }
+  a.words = d_words;
+  a.xhat = d_xhat;
+  a.n = n;
+  a.y = d_y;
+  a.bools = d_bools;
+  a.t0 = ctx->d_t0;
+  a.status = ctx->d_status;
+  const cudaError_t e = sufb200::launch_trunc_bundle_elem(ctx, a, aligned, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "per-element bundle launch");
+  return SUFB200_OK;
+}
+
 namespace {
 
 // Where the host entry point wants finished chunks: after the main kernel of

@@ -40,6 +40,22 @@ struct TruncLaunch {
   uint32_t* status;
 };
 cudaError_t launch_trunc_bundle(const sufb200_ctx_s* ctx, const TruncLaunch& a, cudaStream_t st);
+// Per-element masks: element i's keys for slot q at keys[q] + i * key_bytes[q]
+// (device), its words [carry_w, sign_w, haty, r_hi, m, plan] at words[6 i].
+struct TruncElemLaunch {
+  sufb200_trunc_desc shape;  // kind, frac_bits, party, nq slots, q_bits
+  const uint8_t* keys[4];
+  uint64_t key_bytes[4];
+  const uint64_t* words;
+  const uint64_t* xhat;
+  size_t n;
+  uint64_t* y;
+  uint64_t* bools;
+  const uint32_t* t0;
+  uint32_t* status;
+};
+cudaError_t launch_trunc_bundle_elem(const sufb200_ctx_s* ctx, const TruncElemLaunch& a, bool aligned,
+                                     cudaStream_t st);
 // A chunk of a job bucket (jobs.cu): job j's words are src[j][0..off[j+1]-off[j])
 // (gather) or dst[j][...] (scatter), at batch[base + off[j] ...].
 constexpr int kJobsPerLaunch = 48;

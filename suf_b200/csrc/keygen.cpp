@@ -256,6 +256,70 @@ int trunc_gen(int kind, int f, uint64_t seed, sufb200_trunc_desc* d0, sufb200_tr
   return 0;
 }
 
+// Per-element masks (SUF_PER_ELEMENT_MASKS=1): every element gets a gate of
+// its own, as compiler::lower_truncation_gate does with per_element_masks
+// (include/compiler/truncation_lowering.hpp:91-125: one
+// composite_gen_trunc_gate per element).  Element i's gate is
+// trunc_gen(kind, f, seed_i) with seed_i = seed + i * 0x9E3779B97F4A7C15.
+// Its queries fill fixed slots: the 64-bit queries first, then the two f-bit
+// carry queries, as trunc_gen sorts them; when an element has no carry
+// queries (r_low = 0: the carry is the constant 0 and the reference drops
+// the queries) its f-bit slots get keys for threshold 0 and its plan marks
+// the carry absent.  Per element and party, words[6] = carry_w, sign_w,
+// haty, r_hi, m and the plan: the five query indices carry_a, carry_b,
+// sign_a, sign_b, wrap_q, 4 bits each (0xF = absent).  shape gets kind, f,
+// party, the slot count and slot widths.
+int trunc_gen_elem(int kind, int f, uint64_t seed, size_t n, sufb200_trunc_desc* shape0, sufb200_trunc_desc* shape1,
+                   uint64_t* words0, uint64_t* words1, uint64_t* thetas, uint64_t* r_in) {
+  if (kind < 0 || kind > 2 || f < 0 || f > 64) return -1;
+  const int wide = kind == SUFB200_TRUNC_FAITHFUL_ARS ? 2 : (kind == SUFB200_TRUNC_FAITHFUL_TR ? 1 : 0);
+  const int low = (f > 0 && f < 64) ? 2 : 0;
+  const int slots = wide + low;
+  sufb200_trunc_desc* sh[2] = {shape0, shape1};
+  for (int p = 0; p < 2; p++) {
+    std::memset(sh[p], 0, sizeof(sufb200_trunc_desc));
+    sh[p]->kind = kind;
+    sh[p]->frac_bits = f;
+    sh[p]->party = p;
+    sh[p]->nq = slots;
+    for (int q = 0; q < slots; q++) sh[p]->q_bits[q] = q < wide ? 64 : f;
+    sh[p]->carry_a = sh[p]->carry_b = sh[p]->sign_a = sh[p]->sign_b = sh[p]->wrap_q = -1;
+  }
+  int err = 0;
+#pragma omp parallel for schedule(static, 4096) reduction(| : err)
+  for (long long ii = 0; ii < static_cast<long long>(n); ii++) {
+    const size_t i = static_cast<size_t>(ii);
+    sufb200_trunc_desc e0, e1;
+    uint64_t th[4], r = 0;
+    if (trunc_gen(kind, f, seed + static_cast<uint64_t>(i) * 0x9E3779B97F4A7C15ull, &e0, &e1, th, &r)) {
+      err |= 1;
+      continue;
+    }
+    // the element's queries are the first e0.nq slots; missing carry slots
+    // (r_low = 0) get threshold 0
+    if (e0.nq != slots && e0.nq != wide) {
+      err |= 2;
+      continue;
+    }
+    for (int q = 0; q < 4; q++) thetas[4 * i + q] = q < e0.nq ? th[q] : 0ull;
+    auto nib = [](int32_t v) -> uint64_t { return v < 0 ? 0xFull : static_cast<uint64_t>(v); };
+    const uint64_t plan = nib(e0.carry_a) | (nib(e0.carry_b) << 4) | (nib(e0.sign_a) << 8) | (nib(e0.sign_b) << 12) |
+                          (nib(e0.wrap_q) << 16);
+    const sufb200_trunc_desc* e[2] = {&e0, &e1};
+    uint64_t* w[2] = {words0 + 6 * i, words1 + 6 * i};
+    for (int p = 0; p < 2; p++) {
+      w[p][0] = e[p]->carry_w;
+      w[p][1] = e[p]->sign_w;
+      w[p][2] = e[p]->haty;
+      w[p][3] = e[p]->r_hi;
+      w[p][4] = e[p]->m;
+      w[p][5] = plan;
+    }
+    r_in[i] = r;
+  }
+  return err ? -1 : 0;
+}
+
 // ---- reference GPU-backend blobs ------------------------------------------
 
 void seed_from_id(uint64_t id, uint64_t tweak, uint8_t seed[16]) {

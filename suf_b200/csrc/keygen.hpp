@@ -24,6 +24,8 @@ int myl7_gen_batch(const PrgHostKeys& prg, bool add_group, int in_bits, const ui
                    uint8_t* keys0, uint8_t* keys1);
 int trunc_gen(int kind, int f, uint64_t seed, sufb200_trunc_desc* d0, sufb200_trunc_desc* d1, uint64_t thetas[4],
               uint64_t* r_in_out);
+int trunc_gen_elem(int kind, int f, uint64_t seed, size_t n, sufb200_trunc_desc* shape0, sufb200_trunc_desc* shape1,
+                   uint64_t* words0, uint64_t* words1, uint64_t* thetas, uint64_t* r_in);
 void seed_from_id(uint64_t id, uint64_t tweak, uint8_t seed[16]);
 size_t thr_dcf_build(int in_bits, uint64_t alpha, const uint8_t* payload, int payload_len, uint8_t* out);
 size_t packed_lt_build(int party, uint64_t nonce, int in_bits, const uint64_t* thr, int num_thr,

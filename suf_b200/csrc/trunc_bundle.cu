@@ -359,6 +359,155 @@ __global__ void __launch_bounds__(kAesThreads, 1)
 
 }  // namespace
 
+namespace {
+
+// One per-element myl7 key (adapter layout, ADD group, 8-byte payload) walked
+// from global memory for input x.  ALIGNED: the key starts 8-byte aligned
+// (every key of the array is a multiple of 8 bytes long), so each level's
+// 33-byte record comes in three 16-byte loads re-aligned by funnel shifts;
+// otherwise byte loads.  A header that does not match flags the status and
+// yields 0.
+template <bool ALIGNED>
+__device__ __forceinline__ uint64_t walk_elem_key(const PrgParams& prg, uint32_t lb, const uint8_t* k, int nb,
+                                                  uint64_t x, uint32_t party, uint32_t* status) {
+  const uint64_t hdr = ALIGNED ? __ldg(reinterpret_cast<const uint64_t*>(k)) : ldb64(k);
+  if ((hdr & 0xFF) != static_cast<uint64_t>(nb) || ((hdr >> 8) & 0xFF) != 1 || ((hdr >> 16) & 0xFF) != party ||
+      (hdr >> 32) != 8) {
+    atomicOr(status, kStatusBadKeyHeader);
+    return 0;
+  }
+  Blk s;
+  if (ALIGNED) {
+    const uint64_t s0 = __ldg(reinterpret_cast<const uint64_t*>(k) + 1), s1 = __ldg(reinterpret_cast<const uint64_t*>(k) + 2);
+    s.w[0] = static_cast<uint32_t>(s0);
+    s.w[1] = static_cast<uint32_t>(s0 >> 32);
+    s.w[2] = static_cast<uint32_t>(s1);
+    s.w[3] = static_cast<uint32_t>(s1 >> 32);
+  } else {
+    s.w[0] = ldb32(k + 8);
+    s.w[1] = ldb32(k + 12);
+    s.w[2] = ldb32(k + 16);
+    s.w[3] = ldb32(k + 20);
+  }
+  s.w[3] &= 0x7FFFFFFFu;
+  uint32_t t = party;
+  uint64_t v = 0;
+  const uintptr_t kaddr = reinterpret_cast<uintptr_t>(k);
+  for (int lv = 0; lv < nb; lv++) {
+    CwLevel cw;
+    if (ALIGNED) {
+      // the record lies inside the three aligned 16-byte chunks from its
+      // address rounded down to 16 (offset <= 15, 15 + 33 <= 48), all inside
+      // the 40 + 33 nb byte key
+      const uintptr_t A = kaddr + 24u + 33u * static_cast<uint32_t>(lv);
+      const uint4* c = reinterpret_cast<const uint4*>(A & ~static_cast<uintptr_t>(15));
+      const uint4 c0 = __ldg(c), c1 = __ldg(c + 1), c2 = __ldg(c + 2);
+      const uint32_t r = static_cast<uint32_t>(A & 15u);
+      const bool hi = r >= 8u;
+      const uint32_t rb = r & 7u;
+      const uint64_t w0 = (static_cast<uint64_t>(c0.y) << 32) | c0.x, w1 = (static_cast<uint64_t>(c0.w) << 32) | c0.z;
+      const uint64_t w2 = (static_cast<uint64_t>(c1.y) << 32) | c1.x, w3 = (static_cast<uint64_t>(c1.w) << 32) | c1.z;
+      const uint64_t w4 = (static_cast<uint64_t>(c2.y) << 32) | c2.x, w5 = (static_cast<uint64_t>(c2.w) << 32) | c2.z;
+      const uint64_t q0 = hi ? w1 : w0, q1 = hi ? w2 : w1, q2 = hi ? w3 : w2, q3 = hi ? w4 : w3, q4 = hi ? w5 : w4;
+      const uint64_t slo = funnel64(q0, q1, rb), shi = funnel64(q1, q2, rb);
+      cw.s.w[0] = static_cast<uint32_t>(slo);
+      cw.s.w[1] = static_cast<uint32_t>(slo >> 32);
+      cw.s.w[2] = static_cast<uint32_t>(shi);
+      cw.s.w[3] = static_cast<uint32_t>(shi >> 32);
+      cw.v = funnel64(q2, q3, rb);
+      cw.t = static_cast<uint32_t>((q4 >> (8u * rb)) & 0xFFu);
+    } else {
+      const uint8_t* c = k + 24 + 33 * lv;
+      cw.s.w[0] = ldb32(c);
+      cw.s.w[1] = ldb32(c + 4);
+      cw.s.w[2] = ldb32(c + 8);
+      cw.s.w[3] = ldb32(c + 12);
+      cw.v = ldb64(c + 16);
+      cw.t = c[32];
+    }
+    walk_level<SUFB200_GROUP_ADD>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (nb - 1 - lv)) & 1ull), party, cw);
+  }
+  const uint32_t onp = 24u + 33u * static_cast<uint32_t>(nb);
+  const uint64_t np1 = ALIGNED ? funnel64(__ldg(reinterpret_cast<const uint64_t*>(k) + (onp >> 3)),
+                                          __ldg(reinterpret_cast<const uint64_t*>(k) + (onp >> 3) + 1), onp & 7u)
+                               : ldb64(k + onp);
+  return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, np1);
+}
+
+// Per-element masks: element i has its own keys (slot q at keys[q] + i *
+// key_bytes[q]), its own descriptor words and plan (words[6 i ..]); one
+// thread per element walks every slot and folds the element's plan and
+// postproc (the per-element path of compiler::lower_truncation_gate,
+// include/compiler/truncation_lowering.hpp:91-125, evaluated by one
+// composite_eval_batch_backend per element in the reference).
+template <bool ALIGNED>
+__global__ void __launch_bounds__(kAesThreads, 1)
+    trunc_bundle_elem_kernel(const PrgParams prg, const __grid_constant__ TruncElemLaunch a) {
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    return;
+  }
+  aes_fill_tables(a.t0);
+  __syncthreads();
+  const uint32_t lb = lane_base();
+  const uint32_t party = static_cast<uint32_t>(a.shape.party);
+  const int nq = a.shape.nq;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    const uint64_t xh = a.xhat[i];
+    uint64_t pr[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      if (q < nq) {
+        const int nb = a.shape.q_bits[q];
+        const uint64_t x = nb >= 64 ? xh : (xh & ((1ull << nb) - 1ull));
+        pr[q] = walk_elem_key<ALIGNED>(prg, lb, a.keys[q] + i * a.key_bytes[q], nb, x, party, a.status);
+      }
+    }
+    const uint64_t* w = a.words + 6 * i;
+    sufb200_trunc_desc d = a.shape;
+    d.carry_w = w[0];
+    d.sign_w = w[1];
+    d.haty = w[2];
+    d.r_hi = w[3];
+    d.m = w[4];
+    const uint64_t plan = w[5];
+    int32_t idx[5];
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < 5; j++) {
+      const int32_t v = static_cast<int32_t>((plan >> (4 * j)) & 0xFu);
+      idx[j] = v == 0xF ? -1 : v;
+      ok = ok && idx[j] < nq;
+    }
+    d.carry_a = idx[0];
+    d.carry_b = idx[1];
+    d.sign_a = idx[2];
+    d.sign_b = idx[3];
+    d.wrap_q = idx[4];
+    if (!ok || (d.carry_a >= 0) != (d.carry_b >= 0) || (d.sign_a >= 0) != (d.sign_b >= 0)) {
+      atomicOr(a.status, kStatusBadArgument);
+      a.y[i] = 0;
+      continue;
+    }
+    combine_store(d, xh, pr, a.y, a.bools, i);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_trunc_bundle_elem(const sufb200_ctx_s* ctx, const TruncElemLaunch& a, bool aligned,
+                                     cudaStream_t st) {
+  const auto kernel = aligned ? trunc_bundle_elem_kernel<true> : trunc_bundle_elem_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  const size_t want = (a.n + kAesThreads - 1) / kAesThreads;
+  const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
+  kernel<<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_trunc_bundle(const sufb200_ctx_s* ctx, const TruncLaunch& a, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(trunc_bundle_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(ctx->aes_dyn_bytes));

@@ -180,6 +180,37 @@ class Context:
                                                 _stream_ptr(stream)))
         return d_y
 
+    @staticmethod
+    def trunc_gen_elem(kind: int, frac_bits: int, seed: int, n: int):
+        """Per-element gates (sufb200_trunc_gen_elem): (r_in [n], shape0,
+        shape1, words0 [n][6], words1 [n][6], thetas [n][4])."""
+        s0, s1 = TruncDesc(), TruncDesc()
+        w0 = np.zeros((n, 6), dtype=np.uint64)
+        w1 = np.zeros((n, 6), dtype=np.uint64)
+        th = np.zeros((n, 4), dtype=np.uint64)
+        r = np.zeros(n, dtype=np.uint64)
+        check(_lib.lib().sufb200_trunc_gen_elem(kind, frac_bits, C.c_uint64(seed), n, C.byref(s0), C.byref(s1),
+                                                _np_ptr(w0), _np_ptr(w1), _np_ptr(th), _np_ptr(r)))
+        return r, s0, s1, w0, w1, th
+
+    def trunc_bundle_eval_elem(self, shape: TruncDesc, d_keys: Sequence, key_bytes: Sequence[int], d_words, d_xhat,
+                               d_y=None, d_bools=None, stream=None):
+        """One party's per-element gates: d_keys[q] is slot q's [n][key_bytes[q]]
+        device key array, d_words the party's [n][6] device words."""
+        import torch
+
+        n = d_xhat.numel()
+        if d_y is None:
+            d_y = torch.empty(n, dtype=torch.int64, device=d_xhat.device)
+        nq = int(shape.nq)
+        ptrs = (C.c_void_p * 4)(*[_t_ptr(k) for k in d_keys[:nq]], *([None] * (4 - nq)))
+        sizes = (C.c_size_t * 4)(*[int(b) for b in key_bytes[:nq]], *([0] * (4 - nq)))
+        check(self._L.sufb200_trunc_bundle_eval_elem(self.h, C.byref(shape), C.cast(ptrs, C.c_void_p),
+                                                     C.cast(sizes, C.c_void_p), _t_ptr(d_words), _t_ptr(d_xhat), n,
+                                                     _t_ptr(d_y), _t_ptr(d_bools) if d_bools is not None else None,
+                                                     _stream_ptr(stream)))
+        return d_y
+
     def trunc_bundle_eval_host(self, desc: TruncDesc, keys: Sequence[np.ndarray], xhat: np.ndarray,
                                y: np.ndarray | None = None, bools: np.ndarray | None = None) -> np.ndarray:
         """Host buffers in and out (pinned memory makes the copies true DMA)."""

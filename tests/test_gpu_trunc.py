@@ -202,3 +202,63 @@ def test_jobs_bucket_matches_per_job(ctx, torch_cuda, oracle, prg_state, lens):
             assert (from_dev(dy[j])[:n] == oracle_trunc_eval(oracle, descs[0], keys[0], xs[j])).all(), j
         else:
             assert int(dy[j].cpu()[0]) == -1  # untouched
+
+
+def _elem_desc(shape, words_row):
+    """The oracle descriptor of one per-element gate: the shape's kind, f,
+    party and slot widths, the element's words and plan."""
+    from oracle.oracle import TruncDesc as OrcDesc
+
+    d = OrcDesc()
+    for name in ("kind", "frac_bits", "party", "nq"):
+        setattr(d, name, getattr(shape, name))
+    for q in range(4):
+        d.q_bits[q] = shape.q_bits[q]
+    d.carry_w, d.sign_w, d.haty, d.r_hi, d.m = (int(v) for v in words_row[:5])
+    plan = int(words_row[5])
+    idx = [(plan >> (4 * j)) & 0xF for j in range(5)]
+    d.carry_a, d.carry_b, d.sign_a, d.sign_b, d.wrap_q = (-1 if v == 0xF else v for v in idx)
+    return d
+
+
+@pytest.mark.parametrize("kind,f,n", [(KIND_ARS, 16, 4096), (KIND_TR, 12, 16384), (KIND_GAPARS, 12, 16384)])
+def test_per_element_bundles_bit_exact(ctx, torch_cuda, oracle, prg_state, kind, f, n):
+    """Per-element masks (SUF_PER_ELEMENT_MASKS=1): every element has its own
+    gate and keys.  Each party's shares equal the oracle's per-element
+    composite eval + postproc word for word, and y0 + y1 is the truncation;
+    the f = 12 cases hold elements whose gate has no carry queries (r_low =
+    0), which the slot layout marks absent."""
+    from suf_b200.engine import Context, host_mt19937_64, myl7_key_bytes
+    from tests.helpers import ONE_LE
+
+    oracle.prg_init(prg_state)
+    r_in, s0, s1, w0, w1, th = Context.trunc_gen_elem(kind, f, 77, n)
+    nq = int(s0.nq)
+    if f == 12:
+        assert ((r_in & np.uint64((1 << f) - 1)) == 0).any()  # the carry-free elements are exercised
+    seeds = host_mt19937_64(0xE1E1, 4 * n * nq).view(np.uint8).reshape(nq, n, 2, 16)
+    keys = []
+    for q in range(nq):
+        k0, k1 = ctx.myl7_gen_batch(0, int(s0.q_bits[q]), th[:, q], ONE_LE, np.ascontiguousarray(seeds[q, :, 0]),
+                                    np.ascontiguousarray(seeds[q, :, 1]))
+        keys.append((k0, k1))
+    rng = np.random.default_rng(5)
+    x = signed_fixed(rng, n, 40)
+    xhat = x + r_in
+    dx = to_dev(torch_cuda, xhat)
+    ys = []
+    for p, shape, words in ((0, s0, w0), (1, s1, w1)):
+        kb = [myl7_key_bytes(int(shape.q_bits[q]), 8) for q in range(nq)]
+        dk = [to_dev(torch_cuda, keys[q][p].ravel()) for q in range(nq)]
+        db = torch_cuda.zeros(3 * n, dtype=torch_cuda.int64, device="cuda")
+        dy = ctx.trunc_bundle_eval_elem(shape, dk, kb, to_dev(torch_cuda, words.ravel()), dx, d_bools=db)
+        ctx.sync()
+        got = from_dev(dy)
+        pred = np.stack([oracle.myl7_eval(0, keys[q][p], kb[q], False, xhat, 8).view(np.uint64).ravel()
+                         for q in range(nq)])
+        exp = np.array([oracle.trunc_combine(_elem_desc(shape, words[i]), xhat[i:i + 1], pred[:, i].copy())[0]
+                        for i in range(n)], dtype=np.uint64)
+        assert (got == exp).all(), int((got != exp).sum())
+        ys.append(got)
+    want = (x >> np.uint64(f)) if kind == KIND_TR else (x.view(np.int64) >> f).view(np.uint64)
+    assert ((ys[0] + ys[1]) == want).all()

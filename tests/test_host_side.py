@@ -434,3 +434,29 @@ def test_bench_masked_shares_open_to_xhat():
     m0, m1 = bench.masked_shares(xh, 3)
     assert ((m0 + m1) == xh).all()
     assert not (m0 == xh).all()
+
+
+def test_per_element_dealer_matches_oracle_gates():
+    """sufb200_trunc_gen_elem: element i is the oracle's trunc_gen(kind, f,
+    seed + i * 0x9E3779B97F4A7C15) -- same mask, thresholds in the fixed
+    slots, descriptor words -- for every kind, carry-free elements included."""
+    from oracle.oracle import Oracle
+    from suf_b200.engine import Context
+
+    orc = Oracle()
+    for kind, f in ((KIND_ARS, 16), (KIND_TR, 12), (KIND_GAPARS, 12)):
+        n = 8192
+        r, s0, s1, w0, w1, th = Context.trunc_gen_elem(kind, f, 77, n)
+        assert s0.nq == {KIND_ARS: 4, KIND_TR: 3, KIND_GAPARS: 2}[kind]
+        for i in [*range(0, n, 97), *np.flatnonzero((r & np.uint64((1 << f) - 1)) == 0).tolist()]:
+            ro, d0, d1 = orc.trunc_gen(kind, f, (77 + i * 0x9E3779B97F4A7C15) & (2**64 - 1))
+            assert ro == int(r[i])
+            for q in range(d0.nq):
+                assert int(d0.q_theta[q]) == int(th[i, q]) and d0.q_bits[q] == s0.q_bits[q]
+            for q in range(d0.nq, s0.nq):  # carry-free element: threshold 0 in the f-bit slots
+                assert int(th[i, q]) == 0
+            plan = int(w0[i, 5])
+            idx = [(plan >> (4 * j)) & 0xF for j in range(5)]
+            assert [(-1 if v == 0xF else v) for v in idx] == [d0.carry_a, d0.carry_b, d0.sign_a, d0.sign_b, d0.wrap_q]
+            for d, w in ((d0, w0), (d1, w1)):
+                assert [d.carry_w, d.sign_w, d.haty, d.r_hi, d.m] == [int(v) for v in w[i, :5]]
