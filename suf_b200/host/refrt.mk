@@ -6,6 +6,8 @@
 # cuda_primitives ABI and libsufb200.so.  Output: suf_b200/_refrt/.
 #   make -f suf_b200/host/refrt.mk REF=<reference checkout> [-j8]
 #   _refrt/layer_harness_b200  layer_harness.cpp on the B200 engine
+#   _refrt/ops_harness_b200    ops_harness.cpp (the hot-path operations through
+#                              the reference's backend interfaces) on it
 # suf_b200.build runs it when a reference checkout is present.
 REF ?=
 HOSTDIR := $(dir $(abspath $(lastword $(MAKEFILE_LIST))))
@@ -29,7 +31,7 @@ RT_OBJ := $(patsubst %,$(OUT)/rt/%.o,$(RT))
 OURS := $(OUT)/ours/make_backend.o $(OUT)/ours/cuda_primitives_shim.o $(OUT)/ours/matmul_gpu.o
 
 .PHONY: all need-ref
-all: need-ref $(OUT)/layer_harness_b200
+all: need-ref $(OUT)/layer_harness_b200 $(OUT)/ops_harness_b200
 
 need-ref:
 	@test -n "$(REF)" -a -d "$(REF)/src/nn" || { echo "set REF=<reference checkout>" >&2; exit 2; }
@@ -50,4 +52,8 @@ $(OUT)/ours/matmul_gpu.o: $(REF)/src/nn/matmul_gpu.cu
 
 $(OUT)/layer_harness_b200: $(OUT)/ours/layer_harness.o $(RT_OBJ) $(OURS) $(PKG)/libsufb200.so
 	g++ -fopenmp -o $@ $(OUT)/ours/layer_harness.o $(RT_OBJ) $(OURS) -L$(PKG) -lsufb200 \
+	    -L$(CUDA)/lib64 -lcudart -lcrypto -Wl,-rpath,'$$ORIGIN/..'
+
+$(OUT)/ops_harness_b200: $(OUT)/ours/ops_harness.o $(RT_OBJ) $(OURS) $(PKG)/libsufb200.so
+	g++ -fopenmp -o $@ $(OUT)/ours/ops_harness.o $(RT_OBJ) $(OURS) -L$(PKG) -lsufb200 \
 	    -L$(CUDA)/lib64 -lcudart -lcrypto -Wl,-rpath,'$$ORIGIN/..'

@@ -215,6 +215,7 @@ class TransformerLayerPair:
         def buf(n):
             return torch.empty(n, dtype=torch.int64, device=dev)
 
+        self._side = self._fork = self._join = None  # party 1's stream (created on first use)
         wide = max(S * 3 * D, S * Dff)  # the widest public-weight product
         self.b = {
             "h": (buf(S * D), buf(S * D)), "acc": (buf(wide), buf(wide)), "xhat": buf(max(wide, H * S * S)),
@@ -226,15 +227,33 @@ class TransformerLayerPair:
         }
 
     # -- steps ---------------------------------------------------------------
+    def _both_parties(self, stream, fn):
+        """fn(p, stream_p) for both parties, party 1 on a side stream forked
+        from and joined back to `stream`: the parties' independent launches
+        (their matmuls, their gate evaluations) overlap on the GPU, as two
+        party processes sharing it would."""
+        import torch
+
+        main = stream if stream is not None else torch.cuda.current_stream(self.dev)
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=self.dev)
+            self._fork = torch.cuda.Event()
+            self._join = torch.cuda.Event()
+        self._fork.record(main)
+        self._side.wait_event(self._fork)
+        fn(0, main)
+        fn(1, self._side)
+        self._join.record(self._side)
+        main.wait_event(self._join)
+
     def _matmul_trunc(self, x, wname, K, N, tr: _Trunc, out, stream):
         """out_p = T(x_p W): each party's public-weight product, the open of
         the masked products and the truncation bundle of both parties."""
         L = _lib.lib()
         S = self.dims.S
         acc = self.b["acc"]
-        for p in (0, 1):
-            check(L.sufb200_ring_matmul(self.ctx.h, _t_ptr(x[p]), _t_ptr(self.W[wname]), None, _t_ptr(acc[p]), 1, S,
-                                        K, N, 0, _stream_ptr(stream)))
+        self._both_parties(stream, lambda p, st: check(L.sufb200_ring_matmul(
+            self.ctx.h, _t_ptr(x[p]), _t_ptr(self.W[wname]), None, _t_ptr(acc[p]), 1, S, K, N, 0, _stream_ptr(st))))
         n = S * N
         if acc[0].numel() < n or self.b["xhat"].numel() < n or out[0].numel() < n or x[0].numel() < S * K:
             raise ValueError("layer: a staging buffer is smaller than the product")
@@ -272,8 +291,7 @@ class TransformerLayerPair:
             check(L.sufb200_relu_open_pair(_t_ptr(cur[0]), _t_ptr(cur[1]), rows, w, C.c_uint64(g.r[0]),
                                            C.c_uint64(g.r[1]), _t_ptr(xh), _stream_ptr(stream)))
             rl = self.b["relu"]
-            for p in (0, 1):
-                g.eval(self.ctx, p, xh, rl[p][:half], stream)
+            self._both_parties(stream, lambda p, st: g.eval(self.ctx, p, xh, rl[p][:half], st))
             nxt = bufs[i % 2]
             check(L.sufb200_relu_update_pair(_t_ptr(cur[0]), _t_ptr(cur[1]), _t_ptr(rl[0]), _t_ptr(rl[1]), rows, w,
                                              _t_ptr(nxt[0]), _t_ptr(nxt[1]), _stream_ptr(stream)))
@@ -334,8 +352,7 @@ class TransformerLayerPair:
         g = self.gelu
         check(L.sufb200_open_masked_pair(_t_ptr(b["f1"][0]), _t_ptr(b["f1"][1]), C.c_uint64(g.r[0]),
                                          C.c_uint64(g.r[1]), _t_ptr(xh), n, _stream_ptr(stream)))
-        for p in (0, 1):
-            g.eval(self.ctx, p, xh, b["g"][p], stream)
+        self._both_parties(stream, lambda p, st: g.eval(self.ctx, p, xh, b["g"][p], st))
         keep("gelu", b["g"], S * Dff)
         self._matmul_trunc(b["g"], "ff2", Dff, D, self.tr["ff2"], b["a"], stream)
         keep("f2", b["a"], S * D)
