@@ -294,7 +294,9 @@ __global__ void __launch_bounds__(kAesThreads, 1)
   }
   QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);
   QueryPlanSmem* qp = reinterpret_cast<QueryPlanSmem*>(smem + 8 * sizeof(QueryKeySmem));
+  __shared__ int s_walks;  // 1 when some query resumes above its last level (needs the AES tables)
   if (threadIdx.x == 0) {
+    int walks = 0;
 #pragma unroll
     for (int p = 0; p < NP; p++) {
       const sufb200_trunc_desc& dp = p ? a1.desc : a0.desc;
@@ -305,12 +307,19 @@ __global__ void __launch_bounds__(kAesThreads, 1)
         qp[4 * p + q].F = fs.F[4 * p + q];
         qp[4 * p + q].nb = nb;
         qp[4 * p + q].pad = 0;
+        if (q < dp.nq && qp[4 * p + q].plan.depth != static_cast<uint32_t>(nb)) walks = 1;
       }
     }
+    s_walks = walks;
   }
   stage_keys(ks, a0);
   if (NP == 2) stage_keys(ks + 4, a1);
-  aes_fill_tables(a0.t0);
+  __syncthreads();
+  // With every query planned at its full depth the pass is table lookups
+  // (the plan's window holds every element of the batch), so the AES tables
+  // are filled only when some query resumes a walk.
+  const bool walks = s_walks != 0;
+  if (walks) aes_fill_tables(a0.t0);
   __syncthreads();  // also publishes qp
   if (!keys_ok(ks, a0) || (NP == 2 && !keys_ok(ks + 4, a1))) return;
   const uint32_t lb = lane_base();
@@ -345,8 +354,14 @@ __global__ void __launch_bounds__(kAesThreads, 1)
           s.w[3] = e.s[3];
           v = walk_query(prg, lb, kq[q], nb, x, party, s, e.t, e.v, static_cast<int>(P.depth));
         }
-      } else {
+      } else if (walks) {
         v = walk_query(prg, lb, kq[q], nb, x, party, seed_blk(kq[q]), party, 0, 0);
+      } else {
+        // outside the window of a lookup-only pass: cannot happen for the
+        // batch the range was taken over; flagged rather than walked without
+        // tables
+        atomicOr(a.status, kStatusBadArgument);
+        v = 0;
       }
       if (q == 0) pr[0] = v;
       else if (q == 1) pr[1] = v;

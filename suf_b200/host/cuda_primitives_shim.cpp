@@ -8,7 +8,11 @@
 // signatures are the reference's; where the reference launchers return
 // silently on a failed launch, these throw std::runtime_error with the engine's
 // message (the callers are C++).
+#include <cuda_runtime.h>
+
 #include <cstddef>
+#include <map>
+#include <mutex>
 #include <cstdint>
 #include <stdexcept>
 #include <string>
@@ -18,6 +22,22 @@
 namespace {
 void ok(int rc, const char* what) {
   if (rc != SUFB200_OK) throw std::runtime_error(std::string(what) + ": " + sufb200_last_error());
+}
+
+// One engine context per device for the launchers that need one (made at
+// the first call on the current device, kept until exit).
+sufb200_ctx device_ctx() {
+  static std::mutex mu;
+  static std::map<int, sufb200_ctx> ctxs;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = ctxs.find(dev);
+  if (it != ctxs.end()) return it->second;
+  sufb200_ctx c = nullptr;
+  ok(sufb200_ctx_create(dev, &c), "sufb200_ctx_create");
+  ctxs.emplace(dev, c);
+  return c;
 }
 }  // namespace
 
@@ -76,23 +96,32 @@ void launch_row_sum_ragged_kernel(const uint64_t* d_vals, const int* d_row_offse
   ok(sufb200_row_sum_ragged(d_vals, d_row_offsets, rows, d_out_rows, stream), "launch_row_sum_ragged_kernel");
 }
 
-void launch_beaver_matmul2d_kernel(int party, const uint64_t* d_D_open, const uint64_t* d_E_open,
-                                   const uint64_t* d_A_tri_share, const uint64_t* d_B_tri_share,
-                                   const uint64_t* d_C_tri_share, int M, int K, int N, int w_transposed,
-                                   int has_scale, int64_t mul_const, int mul_shift, uint64_t* d_out, void* stream) {
-  ok(sufb200_beaver_matmul2d(party, d_D_open, d_E_open, d_A_tri_share, d_B_tri_share, d_C_tri_share, 1, M, K, N,
-                             w_transposed, has_scale, mul_const, mul_shift, d_out, stream),
-     "launch_beaver_matmul2d_kernel");
-}
-
 void launch_beaver_matmul2d_batched_kernel(int party, const uint64_t* d_D_open, const uint64_t* d_E_open,
                                            const uint64_t* d_A_tri_share, const uint64_t* d_B_tri_share,
                                            const uint64_t* d_C_tri_share, int batches, int M, int K, int N,
                                            int w_transposed, int has_scale, int64_t mul_const, int mul_shift,
                                            uint64_t* d_out, void* stream) {
+  // The tensor-core form (tcgen05, exact up to contraction depth 2K = 8192)
+  // needs an engine context; the launchers have none in their signature, so
+  // one per device is made at the first call and kept for the process.  A
+  // deeper contraction takes the CUDA-core kernel.
+  if (sufb200_ctx ctx = (2 * static_cast<long long>(K) <= 8192) ? device_ctx() : nullptr) {
+    ok(sufb200_beaver_matmul2d_tc(ctx, party, d_D_open, d_E_open, d_A_tri_share, d_B_tri_share, d_C_tri_share, batches,
+                                  M, K, N, w_transposed, has_scale, mul_const, mul_shift, d_out, stream),
+       "launch_beaver_matmul2d_kernel");
+    return;
+  }
   ok(sufb200_beaver_matmul2d(party, d_D_open, d_E_open, d_A_tri_share, d_B_tri_share, d_C_tri_share, batches, M, K,
                              N, w_transposed, has_scale, mul_const, mul_shift, d_out, stream),
-     "launch_beaver_matmul2d_batched_kernel");
+     "launch_beaver_matmul2d_kernel");
+}
+
+void launch_beaver_matmul2d_kernel(int party, const uint64_t* d_D_open, const uint64_t* d_E_open,
+                                   const uint64_t* d_A_tri_share, const uint64_t* d_B_tri_share,
+                                   const uint64_t* d_C_tri_share, int M, int K, int N, int w_transposed,
+                                   int has_scale, int64_t mul_const, int mul_shift, uint64_t* d_out, void* stream) {
+  launch_beaver_matmul2d_batched_kernel(party, d_D_open, d_E_open, d_A_tri_share, d_B_tri_share, d_C_tri_share, 1, M,
+                                        K, N, w_transposed, has_scale, mul_const, mul_shift, d_out, stream);
 }
 
 void launch_row_mean_kernel(const uint64_t* d_mat, int rows, int cols, const int* d_valid_lens, uint64_t* d_out_rows,
