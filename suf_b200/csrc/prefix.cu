@@ -153,8 +153,11 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
     }
   const uint32_t lb = lane_base();
   const uint64_t total = first_item[nq];
-  const uint64_t step = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-  for (uint64_t it = static_cast<uint64_t>(threadIdx.x) * gridDim.x + blockIdx.x; it < total; it += step) {
+  // A lane pair per work item (frontier_root_pair): the items are dealt
+  // round-robin over the blocks, pair by pair.
+  const uint32_t lane = threadIdx.x & 31u, hsel = lane & 1u, pmask = 3u << (lane & ~1u);
+  const uint64_t step = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 1);
+  for (uint64_t it = static_cast<uint64_t>(threadIdx.x >> 1) * gridDim.x + blockIdx.x; it < total; it += step) {
     int r = 0;
     while (r + 1 < nq && it >= first_item[r + 1]) r++;
     const int q = order[r];
@@ -173,7 +176,7 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
     const auto emit = [=](uint64_t slot, const Blk& s, uint32_t t, uint64_t v) {
       emit_entry<GROUP>(out, slot, final_level, s, t, v, party, np1_lo);
     };
-    frontier_root<GROUP>(prg, lb, seed, party, f.plan, f.h, it - first_item[r], cw_at, emit);
+    frontier_root_pair<GROUP>(prg, lb, seed, party, f.plan, f.h, it - first_item[r], cw_at, emit, hsel, pmask);
   }
 }
 
@@ -282,7 +285,7 @@ cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierB
   if (b.nq < 1 || b.nq > kFrontierMaxKeys) return cudaErrorInvalidValue;
   size_t work = 0;
   for (int q = 0; q < b.nq; q++) work += b.q[q].kmax;
-  const int grid = aes_grid(ctx, work);
+  const int grid = aes_grid(ctx, 2 * work);  // two lanes per work item
   cudaError_t e;
   if (group == SUFB200_GROUP_ADD) {
     if ((e = set_smem(frontier_kernel<SUFB200_GROUP_ADD>, ctx)) != cudaSuccess) return e;

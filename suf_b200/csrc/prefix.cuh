@@ -175,4 +175,63 @@ SUFB200_DEV void frontier_root(const PrgParams& prg, uint32_t lb, const Blk& see
   }
 }
 
+#if !defined(SUFB200_HOST_EMU)
+// frontier_root over a lane pair (lanes 2k and 2k + 1 of a warp, hsel = lane
+// & 1, pmask = both lanes' bits): every level is walk_level_split, each lane
+// computing one of the level's two MMO blocks, so the serial chain of a work
+// item is one AES block per level instead of two.  Both lanes hold the same
+// states throughout; lane hsel = 0 emits.
+template <int GROUP, typename CwAt, typename Emit>
+__device__ __forceinline__ void frontier_root_pair(const PrgParams& prg, uint32_t lb, const Blk& seed,
+                                                   uint32_t party, const Plan& plan, int h, uint64_t j,
+                                                   const CwAt& cw_at, const Emit& emit, uint32_t hsel,
+                                                   uint32_t pmask) {
+  const int D = static_cast<int>(plan.depth);
+  const int d0 = D - h;
+  const uint64_t dmask = nbit_mask(D);
+  const uint64_t R = ((plan.first >> h) + j) & nbit_mask(d0);
+  Blk s = seed;
+  uint32_t t = party;
+  uint64_t v = 0;
+  for (int lv = 0; lv < d0; lv++)
+    walk_level_split<GROUP>(prg, lb, s, t, v, static_cast<uint32_t>((R >> (d0 - 1 - lv)) & 1ull), party, cw_at(lv),
+                            hsel, pmask);
+  if (h == 0) {
+    if (hsel == 0) emit((R - plan.first) & dmask, s, t, v);
+    return;
+  }
+  uint32_t st[kMaxExpand][8];
+  st[0][0] = s.w[0];
+  st[0][1] = s.w[1];
+  st[0][2] = s.w[2];
+  st[0][3] = s.w[3];
+  st[0][4] = t;
+  st[0][5] = static_cast<uint32_t>(v);
+  st[0][6] = static_cast<uint32_t>(v >> 32);
+  for (uint32_t k = 0; k < (1u << h); k++) {
+    const int l0 = k ? (h - 1 - high_bit(k ^ (k - 1u))) : 0;
+    s.w[0] = st[l0][0];
+    s.w[1] = st[l0][1];
+    s.w[2] = st[l0][2];
+    s.w[3] = st[l0][3];
+    t = st[l0][4];
+    v = (static_cast<uint64_t>(st[l0][6]) << 32) | st[l0][5];
+    for (int l = l0; l < h; l++) {
+      walk_level_split<GROUP>(prg, lb, s, t, v, (k >> (h - 1 - l)) & 1u, party, cw_at(d0 + l), hsel, pmask);
+      if (l + 1 < h) {
+        st[l + 1][0] = s.w[0];
+        st[l + 1][1] = s.w[1];
+        st[l + 1][2] = s.w[2];
+        st[l + 1][3] = s.w[3];
+        st[l + 1][4] = t;
+        st[l + 1][5] = static_cast<uint32_t>(v);
+        st[l + 1][6] = static_cast<uint32_t>(v >> 32);
+      }
+    }
+    const uint64_t slot = ((((R << h) | k) & dmask) - plan.first) & dmask;
+    if (hsel == 0 && slot < plan.count) emit(slot, s, t, v);
+  }
+}
+#endif  // !SUFB200_HOST_EMU
+
 }  // namespace sufb200
