@@ -465,9 +465,14 @@ int sufb200_beaver_matmul2d(int party, const uint64_t* d_D_open, const uint64_t*
 
 /* ---- configs[4] softmax block, device-resident --------------------------- */
 
-/* The six truncations of the block, in order: nExp T_f and T_2f, reciprocal
- * init, Newton T_f(y s), Newton T_f(y d), probability T_f. */
-#define SUFB200_SOFTMAX_TRUNCS 6
+/* The seven truncations of the block, in order: nExp T_f(p), the first T_f
+ * of the nExp T_2f(r), reciprocal init, Newton T_f(y s), Newton T_f(y d),
+ * probability T_f, and the second T_f of T_2f(r).  CubicPolyTask's T_2f is
+ * done as T_f(T_f(r)): floor(floor(r / 2^f) / 2^f) = floor(r / 2^2f), so the
+ * result is the same word, and each half is an f-bit GapARS bundle (a
+ * full-domain table lookup) instead of a 2f-bit one (a walk of f levels per
+ * element past the shared prefix). */
+#define SUFB200_SOFTMAX_TRUNCS 7
 
 /* One party's dealer material for sufb200_softmax_block_pair.  Every triple
  * array holds (a, b, c) words interleaved; the interval-LUT keys are device

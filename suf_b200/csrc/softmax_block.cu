@@ -7,7 +7,8 @@
 // floor shift done by a truncation bundle, LUT = interval-LUT coefficient gate):
 //   x^ = open(t + r)             c0..c3 = LUT_nexp(x^)
 //   p  = (c3 t + c2 2^f) t       p2 = T_f(p)          (CubicPolyTask Mul1, Mul2, Trunc1)
-//   r  = (p2 + c1 2^f) t         e  = T_2f(r) + c0    (Mul3, Trunc2)
+//   r  = (p2 + c1 2^f) t         e  = T_2f(r) + c0    (Mul3, Trunc2; T_2f done
+//                                                      as T_f(T_f(r)), the same floor)
 //   s  = row sums of e           s^ = open(s + r')    a0, a1 = LUT_recip(s^)
 //   y  = T_f(a1 s) + a0                               (RecipTask init)
 //   y  = T_f(y (2 2^f - T_f(y s)))                    (one Newton step)
@@ -20,7 +21,7 @@
 // bundle takes as its public input.  Each party's truncation bundle and LUT
 // evaluation runs on its own shares and keys, as it would on its own GPU.
 //
-// 8 fused kernels, 4 LUT launches and 6 truncation stages per block: the
+// 9 fused kernels, 4 LUT launches and 7 truncation stages per block: the
 // element-level stages run each party's bundle on the shared-prefix path, the
 // row-level ones both parties in one query-parallel launch.
 #include <string>
@@ -226,16 +227,18 @@ extern "C" int sufb200_softmax_block_pair(sufb200_ctx ctx, const sufb200_softmax
       return record_error(SUFB200_ERR_INVALID, "softmax block: incomplete material");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t R = static_cast<size_t>(rows);
-  // scratch words: per element 8 (LUT) + 1 (x^) + 2 (p2) + 2 (T_2f) + 2 (e);
-  // per row 2 (s) + 1 (s^) + 8 (LUT) + 1 (x^) + 2 x 4 (z, y, T(y s), inv)
-  const size_t words = 15 * n + 20 * R;
+  // scratch words: per element 8 (LUT) + 1 (x^) + 2 (p2) + 2 (T_f(r)) +
+  // 2 (T_2f) + 2 (e); per row 2 (s) + 1 (s^) + 8 (LUT) + 1 (x^) + 2 x 4 (z, y,
+  // T(y s), inv)
+  const size_t words = 17 * n + 20 * R;
   uint64_t* w = nullptr;
   cudaError_t ce = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&w), words * 8, ctx->pool, st);
   if (ce != cudaSuccess)
     return record_error(SUFB200_ERR_CUDA, std::string("softmax block scratch: ") + cudaGetErrorString(ce));
   uint64_t *lut0 = w, *lut1 = lut0 + 4 * n, *xh = lut1 + 4 * n, *p20 = xh + n, *p21 = p20 + n, *y0 = p21 + n,
            *y1 = y0 + n, *e0 = y1 + n, *e1 = e0 + n;
-  uint64_t *s0 = e1 + n, *s1 = s0 + R, *sh = s1 + R, *lr0 = sh + R, *lr1 = lr0 + 4 * R, *xr = lr1 + 4 * R,
+  uint64_t *h0 = e1 + n, *h1 = h0 + n;  // T_f(r), the first half of T_2f(r)
+  uint64_t *s0 = h1 + n, *s1 = s0 + R, *sh = s1 + R, *lr0 = sh + R, *lr1 = lr0 + 4 * R, *xr = lr1 + 4 * R,
            *z0 = xr + R, *z1 = z0 + R, *yr0 = z1 + R, *yr1 = yr0 + R, *g0 = yr1 + R, *g1 = g0 + R, *v0 = g1 + R,
            *v1 = v0 + R;
   const int f = frac_bits;
@@ -263,7 +266,12 @@ extern "C" int sufb200_softmax_block_pair(sufb200_ctx ctx, const sufb200_softmax
                                               p1->d_nexp_triples, f, p0->trunc_rin[1] + p1->trunc_rin[1], xh, n);
     run(launch_rc("softmax nExp Mul3"));
   }
-  if (run(rc)) run(trunc2(ctx, p0, p1, 1, xh, n, y0, y1, st));
+  if (run(rc)) run(trunc2(ctx, p0, p1, 1, xh, n, h0, h1, st));
+  if (rc == SUFB200_OK) {
+    open_masked_kernel<<<ge, kThreads, 0, st>>>(h0, h1, p0->trunc_rin[6] + p1->trunc_rin[6], xh, n);
+    run(launch_rc("softmax T_2f second half open"));
+  }
+  if (run(rc)) run(trunc2(ctx, p0, p1, 6, xh, n, y0, y1, st));
 
   // row sums and the reciprocal (one Newton step) on the rows
   if (rc == SUFB200_OK) {

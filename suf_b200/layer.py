@@ -366,7 +366,7 @@ class TransformerLayerPair:
     def launches(self) -> int:
         d = self.dims
         lf = 20 * 2  # two LayerNorm blocks
-        sm = 22
+        sm = 26  # the softmax block (see bench.py's SOFTMAX_LAUNCHES)
         def trunc(n):
             return 6 if n >= 16384 else 1
         mm = 0

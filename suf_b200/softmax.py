@@ -11,7 +11,8 @@ tests/golden/make_softmax_tables.py):
   nexp : make_nexp_spec(NExpGateParams{f, 16}) via build_silu_suf_from_piecewise
   recip: make_recip_affine_init_spec(f, 1024) via build_silu_suf_from_piecewise
 Every truncation is a GapARS bundle, as dealer_make_nexp_task_material and the
-reciprocal's AutoTrunc choose for these ranges.  The dealer's masks are its
+reciprocal's AutoTrunc choose for these ranges; CubicPolyTask's T_2f is done
+as two f-bit bundles (the same floor).  The dealer's masks are its
 own draws: the reconstruction of every step is exact in Z_2^64 and does not
 depend on them.
 """
@@ -28,7 +29,7 @@ from ._lib import TruncDesc, check
 from .engine import Context, interval_lut_key, seed_from_id
 
 TABLES = Path(__file__).resolve().parent / "tables" / "softmax_suf_f12.json"
-N_TRUNCS = 6
+N_TRUNCS = 7
 TRUNC_GAPARS = 2  # SUFB200_TRUNC_GAPARS
 GROUP_ADD = 0
 M64 = (1 << 64) - 1
@@ -162,9 +163,12 @@ class SoftmaxBlock:
             for p in (0, 1):
                 setattr(parts[p], field, dcopy(sh[p]).data_ptr())
 
-        # the six GapARS truncations: nExp T_f, T_2f; reciprocal init, Newton x2; probabilities
+        # the seven GapARS truncations: nExp T_f(p), the first T_f of T_2f(r);
+        # reciprocal init, Newton x2; probabilities; the second T_f of T_2f(r)
+        # (floor(floor(r / 2^f) / 2^f) = floor(r / 2^2f): two f-bit bundles,
+        # each a full-domain table lookup, in place of one 2f-bit bundle)
         payload1 = (1).to_bytes(8, "little")
-        for k, fk in enumerate((f, 2 * f, f, f, f, f)):
+        for k, fk in enumerate((f, f, f, f, f, f, f)):
             r_in, d0, d1, thetas = Context.trunc_gen(TRUNC_GAPARS, fk, int(rng.integers(1, 2**63)))
             r0 = int(rng.integers(0, 2**64, dtype=np.uint64))
             for p, d in ((0, d0), (1, d1)):
