@@ -1112,12 +1112,24 @@ def run_open(args, ws, rank, local):
     stream = torch.cuda.Stream(device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
 
+    # The flushes' device pointers are taken once, so a step is 120 calls of
+    # the C ABI (as a C++ runtime would make them), not 120 tensor slicings.
+    from suf_b200 import _lib as L_
+
+    lib_ = L_.lib()
+    sp = int(stream.cuda_stream)
+    ins = [int(d_in[f].data_ptr()) for f in range(OPEN_FLUSHES)]
+    outs = [int(d_out[f].data_ptr()) for f in range(OPEN_FLUSHES)]
+
     def step():
-        for f in range(OPEN_FLUSHES):
-            if ep is not None:
-                ep.exchange(d_in[f], eff, ring, signed=True, d_out=d_out[f], timeout_s=5.0, stream=stream)
-            else:
-                comm.exchange(peer, d_in[f], eff, ring, signed=True, d_out=d_out[f], stream=stream)
+        if ep is not None:
+            h = ep.h
+            for f in range(OPEN_FLUSHES):
+                L_.check(lib_.sufb200_p2p_open_exchange(h, ins[f], per, eff, ring, 1, outs[f], 5.0, sp))
+        else:
+            h = comm.h
+            for f in range(OPEN_FLUSHES):
+                L_.check(lib_.sufb200_open_exchange(h, peer, ins[f], per, eff, ring, 1, outs[f], sp))
 
     ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
     want = x.copy()
