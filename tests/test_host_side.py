@@ -460,3 +460,39 @@ def test_per_element_dealer_matches_oracle_gates():
             assert [(-1 if v == 0xF else v) for v in idx] == [d0.carry_a, d0.carry_b, d0.sign_a, d0.sign_b, d0.wrap_q]
             for d, w in ((d0, w0), (d1, w1)):
                 assert [d.carry_w, d.sign_w, d.haty, d.r_hi, d.m] == [int(v) for v in w[i, :5]]
+
+
+def test_ctypes_mirrors_match_the_c_structs(tmp_path):
+    """The Python mirrors of the C-ABI structs (TruncDesc, SoftmaxParty,
+    LayerNormParty) have the C header's size and field offsets: a mismatch
+    would hand the library shifted fields."""
+    import ctypes as C
+
+    from suf_b200._lib import TruncDesc
+    from suf_b200.softmax import LayerNormParty, SoftmaxParty
+
+    fields = {
+        "sufb200_trunc_desc": (TruncDesc, ["frac_bits", "q_bits", "carry_a", "wrap_q", "carry_w", "haty", "m"]),
+        "sufb200_softmax_party": (SoftmaxParty, ["recip_rin", "d_recip_lut", "d_row_c", "trunc", "trunc_rin",
+                                                 "trunc_keys", "trunc_key_bytes"]),
+        "sufb200_layernorm_party": (LayerNormParty, ["d_rsqrt_lut", "d_norm_c", "trunc", "trunc_rin", "trunc_keys",
+                                                     "trunc_key_bytes"]),
+    }
+    src = ['#include <stdio.h>', '#include <stddef.h>', '#include "sufb200.h"', "int main(void) {"]
+    for name, (_, fs) in fields.items():
+        src.append(f'  printf("{name} %zu\\n", sizeof({name}));')
+        for f in fs:
+            src.append(f'  printf("{name}.{f} %zu\\n", offsetof({name}, {f}));')
+    src.append("  return 0; }")
+    c = tmp_path / "layout.c"
+    c.write_text("\n".join(src))
+    exe = tmp_path / "layout"
+    root = Path(__file__).resolve().parents[1]
+    subprocess.run(["gcc", "-std=c11", f"-I{root / 'include'}", "-I/usr/local/cuda/include", str(c), "-o", str(exe)],
+                   check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                        text=True).stdout.splitlines())
+    for name, (cls, fs) in fields.items():
+        assert int(got[name]) == C.sizeof(cls), name
+        for f in fs:
+            assert int(got[f"{name}.{f}"]) == getattr(cls, f).offset, f"{name}.{f}"
