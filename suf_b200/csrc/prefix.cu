@@ -153,11 +153,9 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
     }
   const uint32_t lb = lane_base();
   const uint64_t total = first_item[nq];
-  // A lane pair per work item (frontier_root_pair): the items are dealt
-  // round-robin over the blocks, pair by pair.
-  const uint32_t lane = threadIdx.x & 31u, hsel = lane & 1u, pmask = 3u << (lane & ~1u);
-  const uint64_t step = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 1);
-  for (uint64_t it = static_cast<uint64_t>(threadIdx.x >> 1) * gridDim.x + blockIdx.x; it < total; it += step) {
+  // The work item `it` of the merged list, walked by one lane, or by a lane
+  // pair (frontier_root_pair) when hsel <= 1.
+  const auto item = [&](uint64_t it, uint32_t hsel, uint32_t pmask) {
     int r = 0;
     while (r + 1 < nq && it >= first_item[r + 1]) r++;
     const int q = order[r];
@@ -176,7 +174,24 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
     const auto emit = [=](uint64_t slot, const Blk& s, uint32_t t, uint64_t v) {
       emit_entry<GROUP>(out, slot, final_level, s, t, v, party, np1_lo);
     };
-    frontier_root_pair<GROUP>(prg, lb, seed, party, f.plan, f.h, it - first_item[r], cw_at, emit, hsel, pmask);
+    if (hsel <= 1u)
+      frontier_root_pair<GROUP>(prg, lb, seed, party, f.plan, f.h, it - first_item[r], cw_at, emit, hsel, pmask);
+    else
+      frontier_root<GROUP>(prg, lb, seed, party, f.plan, f.h, it - first_item[r], cw_at, emit);
+  };
+  const uint64_t lanes = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  if (2 * total <= lanes) {
+    // Fewer items than lane pairs (small batches): a lane pair per item
+    // halves the serial chain of AES blocks.  Items are dealt round-robin
+    // over the blocks, pair by pair; the branch is uniform over the grid.
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint64_t it = static_cast<uint64_t>(threadIdx.x >> 1) * gridDim.x + blockIdx.x;
+    if (it < total) item(it, lane & 1u, 3u << (lane & ~1u));
+  } else {
+    // Enough items to fill every lane: a lane per item, round-robin over
+    // the blocks (the AES tables' throughput, not the chain, bounds this).
+    for (uint64_t it = static_cast<uint64_t>(threadIdx.x) * gridDim.x + blockIdx.x; it < total; it += lanes)
+      item(it, 2u, 0u);
   }
 }
 
@@ -285,7 +300,7 @@ cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierB
   if (b.nq < 1 || b.nq > kFrontierMaxKeys) return cudaErrorInvalidValue;
   size_t work = 0;
   for (int q = 0; q < b.nq; q++) work += b.q[q].kmax;
-  const int grid = aes_grid(ctx, 2 * work);  // two lanes per work item
+  const int grid = aes_grid(ctx, 2 * work);  // up to two lanes per work item
   cudaError_t e;
   if (group == SUFB200_GROUP_ADD) {
     if ((e = set_smem(frontier_kernel<SUFB200_GROUP_ADD>, ctx)) != cudaSuccess) return e;
