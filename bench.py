@@ -816,7 +816,10 @@ def run_trunc_elem(args, ws, rank, local):
                             "achieved": round(blocks / (kernel_ms / 1e3) / 1e9, 2),
                             "peak": round(engine_peak / 1e9, 2),
                             "frac": round(blocks / (kernel_ms / 1e3) / engine_peak, 4),
-                            "kernel": "trunc_bundle_elem_kernel<true>", "traffic": None,
+                            "kernel": "trunc_bundle_elem_kernel<true>",
+                            "traffic": round(ELEM_TRAFFIC_BYTES_PER_ELEMENT * n),
+                            "traffic_source": "ncu dram read + write of two 262,144-element launches of this "
+                                              "kernel, per element, times one launch's elements",
                             "work_model": "every element walks every level of its own four keys: 2 AES blocks per "
                                           "level, 160 levels per element per party",
                             "hbm": {"achieved": round(hbm, 1), "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
@@ -836,6 +839,10 @@ def run_trunc_elem(args, ws, rank, local):
 # ---------------------------------------------------------------------------
 
 CMP_N = 1 << 20
+# DRAM bytes per element and party of trunc_bundle_elem_kernel from its ncu
+# capture (two 262,144-element launches: 1,497.1 MB read and 1.9 - 5.3 MB
+# written each): the 5,440 bytes of keys, the six plan words, x^ and y.
+ELEM_TRAFFIC_BYTES_PER_ELEMENT = 5724.9
 # DRAM bytes per element of myl7_eval_elem_aligned_kernel from its ncu capture
 # ((594.6 + 8.3) MB / 262,144): the 2,152-byte key, x^, y and some re-reads.
 CMP_TRAFFIC_BYTES_PER_ELEMENT = 2299.8

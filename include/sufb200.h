@@ -413,11 +413,16 @@ int sufb200_open_exchange(sufb200_open_comm comm, int peer, const uint64_t* d_lo
  * timeout_s: a peer that does not call ends the kernel with
  * SUFB200_ERR_CUDA from sufb200_ctx_sync (status: timeout) and d_out
  * undefined.  The two ranks must be on different GPUs (connect refuses a
- * peer on the same device). */
+ * peer on the same device).
+ * sufb200_p2p_open_connect_self instead makes the endpoint its own peer (a
+ * single-device check of the whole kernel: each CTA waits only on the flag
+ * it raised itself); exchange then writes d_out = local + (local mod
+ * 2^eff_bits), reduced and sign-extended as above. */
 #define SUFB200_P2P_HANDLE_BYTES 128
 typedef struct sufb200_p2p_open_s* sufb200_p2p_open;
 int sufb200_p2p_open_create(sufb200_ctx ctx, size_t max_words, sufb200_p2p_open* out, uint8_t* handle_out);
 int sufb200_p2p_open_connect(sufb200_p2p_open h, const uint8_t* peer_handle);
+int sufb200_p2p_open_connect_self(sufb200_p2p_open h);
 int sufb200_p2p_open_exchange(sufb200_p2p_open h, const uint64_t* d_local, size_t n, int eff_bits, int ring_bits,
                               int signed_out, uint64_t* d_out, double timeout_s, void* stream);
 int sufb200_p2p_open_destroy(sufb200_p2p_open h);

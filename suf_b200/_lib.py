@@ -120,6 +120,7 @@ _SIGS = {
     "sufb200_open_masked_pair": (_i, [_vp, _vp, _u64, _u64, _vp, _sz, _vp]),
     "sufb200_p2p_open_create": (_i, [_vp, _sz, C.POINTER(_vp), _vp]),
     "sufb200_p2p_open_connect": (_i, [_vp, _vp]),
+    "sufb200_p2p_open_connect_self": (_i, [_vp]),
     "sufb200_p2p_open_exchange": (_i, [_vp, _vp, _sz, _i, _i, _i, _vp, C.c_double, _vp]),
     "sufb200_p2p_open_destroy": (_i, [_vp]),
     "sufb200_add_pair": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -28,7 +28,10 @@
 // kStatusTimeout in the context's status word (sufb200_ctx_sync reports
 // it), skips its additions and returns, so a peer that never calls ends the
 // kernel instead of hanging the GPU.  Two ranks on one GPU are refused: the
-// kernels wait on each other and must run on different devices.
+// kernels wait on each other and must run on different devices.  The
+// loopback form (sufb200_p2p_open_connect_self) makes an endpoint its own
+// peer, so the whole kernel -- pack, stores, flag, wait, unpack and add --
+// runs on one device with each CTA waiting only on its own flag.
 #include <cstring>
 #include <string>
 
@@ -212,6 +215,7 @@ struct sufb200_p2p_open_s {
   uint64_t peer_max_words = 0;
   int grid_cap = 0;
   uint64_t seq = 0;
+  bool loopback = false;  // peer_area is this endpoint's own area
   char pci[40] = {};
 };
 
@@ -273,6 +277,17 @@ int sufb200_p2p_open_connect(sufb200_p2p_open h, const uint8_t* peer_handle) {
   return SUFB200_OK;
 }
 
+int sufb200_p2p_open_connect_self(sufb200_p2p_open h) {
+  if (!h) return fail(SUFB200_ERR_INVALID, "null endpoint");
+  if (h->peer_area) return fail(SUFB200_ERR_INVALID, "already connected");
+  // CTA c stores into its own landing half, raises its own flag c and waits
+  // for that flag: every wait is on a store the same CTA made before it.
+  h->peer_area = h->area;
+  h->peer_max_words = h->max_words;
+  h->loopback = true;
+  return SUFB200_OK;
+}
+
 int sufb200_p2p_open_exchange(sufb200_p2p_open h, const uint64_t* d_local, size_t n, int eff_bits, int ring_bits,
                               int signed_out, uint64_t* d_out, double timeout_s, void* stream) {
   if (!h) return fail(SUFB200_ERR_INVALID, "null endpoint");
@@ -315,7 +330,7 @@ int sufb200_p2p_open_destroy(sufb200_p2p_open h) {
   if (!h) return SUFB200_OK;
   cudaSetDevice(h->ctx->device);
   cudaError_t e = cudaDeviceSynchronize();
-  if (h->peer_area) cudaIpcCloseMemHandle(h->peer_area);
+  if (h->peer_area && !h->loopback) cudaIpcCloseMemHandle(h->peer_area);
   if (h->area) cudaFree(h->area);
   delete h;
   return e == cudaSuccess ? SUFB200_OK : fail(SUFB200_ERR_CUDA, std::string("p2p open teardown: ") + cudaGetErrorString(e));

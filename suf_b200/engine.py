@@ -375,6 +375,11 @@ class P2POpen:
         buf = (C.c_uint8 * self.HANDLE_BYTES).from_buffer_copy(peer_handle)
         check(self._L.sufb200_p2p_open_connect(self.h, C.cast(buf, C.c_void_p)))
 
+    def connect_self(self) -> None:
+        """Loopback: this endpoint becomes its own peer (one-device check of
+        the exchange kernel; exchange gives local + (local mod 2^eff_bits))."""
+        check(self._L.sufb200_p2p_open_connect_self(self.h))
+
     def exchange(self, d_local, eff_bits: int, ring_bits: int, signed: bool = False, d_out=None, timeout_s=2.0,
                  stream=None):
         import torch

@@ -2,8 +2,9 @@
 per GPU like the runtime (party 0 on GPU 0, party 1 on GPU 1), against the
 plain arithmetic of OpenCollector::flush's packed path
 (src/runtime/open_collector.cpp:357-895): opened = s0 + s1 mod 2^ring,
-optionally sign-extended, for flushes packed to eff_bits.  Skipped with
-fewer than two GPUs."""
+optionally sign-extended, for flushes packed to eff_bits.  The two-GPU
+tests are skipped with fewer than two GPUs; the loopback test runs the fused
+kernel (sufb200_p2p_open_*) on one."""
 from __future__ import annotations
 
 import os
@@ -250,3 +251,38 @@ def test_p2p_open_times_out_when_the_peer_never_calls():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = {r: (w, dt) for r, w, dt in (q.get(timeout=5) for _ in range(2))}
     assert res[0][0] == "timeout" and res[0][1] < 30, res
+
+
+def test_p2p_open_loopback_one_gpu():
+    """The whole fused-open kernel on one device: an endpoint connected to
+    itself packs, stores, raises and waits on its own per-CTA flags, unpacks
+    and adds -- out = local + (local mod 2^eff_bits), reduced to the ring and
+    sign-extended -- over both landing halves; connecting to the endpoint's
+    own handle as a peer is refused (the paired kernels need two devices)."""
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from suf_b200 import SufB200Error
+    from suf_b200.engine import Context, P2POpen
+
+    ctx = Context(0)
+    ep = P2POpen(ctx, max_words=(1 << 20) + 64)
+    try:
+        with pytest.raises(SufB200Error):
+            ep.connect(ep.handle)
+        ep.connect_self()
+        stream = torch.cuda.Stream()
+        for ci, (n, eff, ring, signed) in enumerate(CASES):
+            rng = np.random.default_rng([11, ci])
+            s = rng.integers(0, 2**63, n, dtype=np.uint64) * np.uint64(2) + rng.integers(0, 2, n, dtype=np.uint64)
+            d = torch.from_numpy(s.view(np.int64)).cuda()
+            emask = np.uint64((1 << eff) - 1) if eff < 64 else np.uint64(~np.uint64(0))
+            want = _expected(s + (s & emask), ring, signed)
+            outs = [ep.exchange(d, eff, ring, signed=signed, timeout_s=5.0, stream=stream) for _ in range(3)]
+            ctx.sync(stream)
+            for o in outs:
+                assert (o.cpu().numpy().view(np.uint64) == want).all(), (n, eff, ring, signed)
+    finally:
+        ep.close()
+        ctx.close()
