@@ -214,6 +214,41 @@ int sufb200_trunc_bundle_eval_elem(sufb200_ctx ctx, const sufb200_trunc_desc* sh
                                    const size_t* key_bytes, const uint64_t* d_words, const uint64_t* d_xhat, size_t n,
                                    uint64_t* d_y, uint64_t* d_bools, void* stream);
 
+/* ---- composite tapes of truncation gates ----------------------------------
+ * The serialized CompositePartyKey of gates::write_composite_tape /
+ * read_composite_tape (include/gates/composite_fss.hpp:2458-2608), byte for
+ * byte, for the gates composite_gen_trunc_gate deals (:645-833).
+ * sufb200_trunc_write_tapes: composite_write_tapes (:2610) of the gate
+ * sufb200_trunc_gen(kind, frac_bits, rng_seed) deals, keys0/keys1[q] the
+ * parties' myl7 keys of its nkeys queries (sizes key_bytes[q]); bit_order is
+ * the dealing backend's (proto::BitOrder: 0 MSB_FIRST, 1 LSB_FIRST).  Both
+ * tapes have the same length, written to *len_out; tape0 = tape1 = NULL
+ * queries it.  Either tape pointer may be NULL.
+ * sufb200_trunc_read_tape: one party's tape of a gate of `kind` with mask
+ * r_in (the compiled gate's, CompiledSUFGate::r_in) into a bundle descriptor
+ * for sufb200_trunc_bundle_eval: desc gets the query plan and the shares,
+ * key_off[q] / key_bytes[q] locate query q's key inside the tape (up to 4),
+ * *r_in_share (may be NULL) the party's r_in share.  A tape that is not a
+ * truncation gate's of that kind and mask returns SUFB200_ERR_KEY.
+ * Per-element gates (sufb200_trunc_gen_elem material, on the device):
+ * sufb200_trunc_write_tapes_elem writes element i's tape of one party at
+ * d_out + i * stride (stride >= sufb200_trunc_tape_elem_stride) and its
+ * length to d_len[i], one warp per element; d_r_in [n] are the elements'
+ * masks (trunc_gen_elem's r_in), d_r_in_share [n] the party's r_in shares:
+ * sufb200_trunc_gen_elem_rin_shares gives party 0's (party 1's = r_in -
+ * party 0's). */
+int sufb200_trunc_write_tapes(int kind, int frac_bits, uint64_t rng_seed, int bit_order, const uint8_t* const* keys0,
+                              const uint8_t* const* keys1, const size_t* key_bytes, int nkeys, uint8_t* tape0,
+                              uint8_t* tape1, size_t cap, size_t* len_out);
+int sufb200_trunc_read_tape(const uint8_t* tape, size_t len, int kind, uint64_t r_in, int party,
+                            sufb200_trunc_desc* desc, size_t* key_off, size_t* key_bytes, uint64_t* r_in_share);
+int sufb200_trunc_gen_elem_rin_shares(int kind, int frac_bits, uint64_t rng_seed, size_t n, uint64_t* share0);
+size_t sufb200_trunc_tape_elem_stride(const sufb200_trunc_desc* shape, const size_t* key_bytes);
+int sufb200_trunc_write_tapes_elem(sufb200_ctx ctx, const sufb200_trunc_desc* shape, const uint8_t* const* d_keys,
+                                   const size_t* key_bytes, const uint64_t* d_words, const uint64_t* d_r_in,
+                                   const uint64_t* d_r_in_share, size_t n, int bit_order, uint8_t* d_out,
+                                   size_t stride, uint64_t* d_len, void* stream);
+
 /* Size of the fixed key staging array of sufb200_trunc_bundle_eval_noalloc. */
 #define SUFB200_NOALLOC_KEY_BYTES 16384
 

@@ -80,6 +80,12 @@ _SIGS = {
     "sufb200_trunc_gen_elem": (_i, [_i, _i, _u64, _sz, C.POINTER(TruncDesc), C.POINTER(TruncDesc), _vp, _vp, _vp,
                                     _vp]),
     "sufb200_trunc_bundle_eval_elem": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
+    "sufb200_trunc_write_tapes": (_i, [_i, _i, _u64, _i, _vp, _vp, _vp, _i, _vp, _vp, _sz, _vp]),
+    "sufb200_trunc_read_tape": (_i, [_vp, _sz, _i, _u64, _i, C.POINTER(TruncDesc), _vp, _vp, _vp]),
+    "sufb200_trunc_gen_elem_rin_shares": (_i, [_i, _i, _u64, _sz, _vp]),
+    "sufb200_trunc_tape_elem_stride": (_sz, [C.POINTER(TruncDesc), _vp]),
+    "sufb200_trunc_write_tapes_elem": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _vp, _vp, _sz, _i, _vp, _sz,
+                                            _vp, _vp]),
     "sufb200_thr_dcf_build": (_sz, [_i, _u64, _vp, _i, _vp]),
     "sufb200_thr_dcf_eval": (_i, [_vp, _i, _vp, _sz, _i, _vp, _sz, _i, _vp, _vp]),
     "sufb200_packed_lt_build": (_sz, [_i, _u64, _i, _vp, _i, _vp, _vp]),

@@ -150,14 +150,11 @@ int myl7_gen_batch(const PrgHostKeys& prg, bool add_group, int in_bits, const ui
 
 // ---- truncation bundles ---------------------------------------------------
 
-int trunc_gen(int kind, int f, uint64_t seed, sufb200_trunc_desc* d0, sufb200_trunc_desc* d1, uint64_t thetas[4],
-              uint64_t* r_in_out) {
+int trunc_plan(int kind, int f, uint64_t r, sufb200_trunc_desc* d0, sufb200_trunc_desc* d1, uint64_t thetas[4],
+               TruncWraps* wraps) {
   if (kind < 0 || kind > 2 || f < 0 || f > 64) return -1;
-  std::mt19937_64 rng(seed);
   const uint64_t fmask = f >= 64 ? ~0ull : ((1ull << f) - 1ull);
-  const uint64_t r = rng();
   const uint64_t r_low = r & fmask;
-  const uint64_t r_hi = f >= 64 ? 0ull : (r >> f);
   struct Q {
     int kind;  // 0 = LtU64, 1 = LtLow (RawPredKind order)
     int bits;
@@ -165,24 +162,24 @@ int trunc_gen(int kind, int f, uint64_t seed, sufb200_trunc_desc* d0, sufb200_tr
     int tag;  // 0 carry.a 1 carry.b 2 sign.a 3 sign.b 4 wrap
   };
   std::vector<Q> raw;
-  std::vector<uint64_t> wrap_bits;
-  int carry_wi = -1, sign_wi = -1;
+  TruncWraps w{};
+  w.carry = w.sign = -1;
   // carry = NOT(1[x_low < 2^f - r_low]), rewritten by rewrite_ltlow
   if (f > 0 && f < 64 && r_low != 0) {
     const uint64_t gamma = (1ull << f) - r_low;
     const uint64_t th0 = r_low, th1 = (r_low + gamma) & fmask;
     raw.push_back({1, f, th0, 0});
     raw.push_back({1, f, th1, 1});
-    carry_wi = static_cast<int>(wrap_bits.size());
-    wrap_bits.push_back(th1 < th0 ? 1u : 0u);
+    w.carry = w.count;
+    w.bit[w.count++] = th1 < th0 ? 1u : 0u;
   }
   // sign = MSB(x), rewritten by rewrite_msb_add(r, 0)
   if (kind == SUFB200_TRUNC_FAITHFUL_ARS) {
     const uint64_t th0 = r + (1ull << 63), th1 = th0 + (1ull << 63);
     raw.push_back({0, 64, th0, 2});
     raw.push_back({0, 64, th1, 3});
-    sign_wi = static_cast<int>(wrap_bits.size());
-    wrap_bits.push_back(th1 < th0 ? 1u : 0u);
+    w.sign = w.count;
+    w.bit[w.count++] = th1 < th0 ? 1u : 0u;
   }
   // wrap = 1[x^ < r_in] for the faithful kinds
   if (kind != SUFB200_TRUNC_GAPARS) raw.push_back({0, 64, r, 4});
@@ -228,18 +225,30 @@ int trunc_gen(int kind, int f, uint64_t seed, sufb200_trunc_desc* d0, sufb200_tr
     d[p]->wrap_q = q_of_tag[4];
   }
   for (int i = 0; i < 4; i++) thetas[i] = i < static_cast<int>(order.size()) ? uq[order[i]].theta : 0ull;
+  if (wraps) *wraps = w;
+  return 0;
+}
+
+int trunc_gen(int kind, int f, uint64_t seed, sufb200_trunc_desc* d0, sufb200_trunc_desc* d1, uint64_t thetas[4],
+              uint64_t* r_in_out, uint64_t* r_in_share0) {
+  if (kind < 0 || kind > 2 || f < 0 || f > 64) return -1;
+  std::mt19937_64 rng(seed);
+  const uint64_t r = rng();
+  const uint64_t r_hi = f >= 64 ? 0ull : (r >> f);
+  TruncWraps w;
+  if (trunc_plan(kind, f, r, d0, d1, thetas, &w)) return -1;
   // share splits in composite_gen_trunc_gate order: r_in, r_out, wrap bits, r_hi, m
-  (void)rng();  // r_in share (party 0); party 1 = r - share
+  const uint64_t rin0 = rng();  // r_in share of party 0; party 1 holds r - rin0
   const uint64_t rout0 = rng();
   d0->haty = rout0;  // base coefficient 0, r_out = 0
   d1->haty = 0ull - rout0;
-  for (size_t w = 0; w < wrap_bits.size(); w++) {
-    const uint64_t w0 = rng(), w1 = wrap_bits[w] - w0;
-    if (static_cast<int>(w) == carry_wi) {
+  for (int k = 0; k < w.count; k++) {
+    const uint64_t w0 = rng(), w1 = w.bit[k] - w0;
+    if (k == w.carry) {
       d0->carry_w = w0;
       d1->carry_w = w1;
     }
-    if (static_cast<int>(w) == sign_wi) {
+    if (k == w.sign) {
       d0->sign_w = w0;
       d1->sign_w = w1;
     }
@@ -253,6 +262,7 @@ int trunc_gen(int kind, int f, uint64_t seed, sufb200_trunc_desc* d0, sufb200_tr
   d0->m = kind == SUFB200_TRUNC_GAPARS ? m0 : 0ull;
   d1->m = kind == SUFB200_TRUNC_GAPARS ? (m - m0) : 0ull;
   if (r_in_out) *r_in_out = r;
+  if (r_in_share0) *r_in_share0 = rin0;
   return 0;
 }
 

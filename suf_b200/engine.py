@@ -211,6 +211,69 @@ class Context:
                                                      _stream_ptr(stream)))
         return d_y
 
+    # -- composite tapes (gates::write_composite_tape format) -------------------
+    @staticmethod
+    def trunc_write_tapes(kind: int, frac_bits: int, seed: int, keys0: Sequence[np.ndarray],
+                          keys1: Sequence[np.ndarray], bit_order: int = 1) -> tuple[bytes, bytes]:
+        """Both parties' composite tapes of the gate trunc_gen(kind, frac_bits,
+        seed) deals, with its queries' myl7 keys (composite_write_tapes)."""
+        L = _lib.lib()
+        nk = len(keys0)
+        k0 = [np.ascontiguousarray(k, dtype=np.uint8) for k in keys0]
+        k1 = [np.ascontiguousarray(k, dtype=np.uint8) for k in keys1]
+        p0 = (C.c_void_p * max(nk, 1))(*[_np_ptr(k) for k in k0])
+        p1 = (C.c_void_p * max(nk, 1))(*[_np_ptr(k) for k in k1])
+        sizes = (C.c_size_t * max(nk, 1))(*[k.size for k in k0])
+        n = C.c_size_t()
+        args = (kind, frac_bits, C.c_uint64(seed), bit_order, C.cast(p0, C.c_void_p), C.cast(p1, C.c_void_p),
+                C.cast(sizes, C.c_void_p), nk)
+        check(L.sufb200_trunc_write_tapes(*args, None, None, 0, C.byref(n)))
+        t0 = np.zeros(n.value, dtype=np.uint8)
+        t1 = np.zeros(n.value, dtype=np.uint8)
+        check(L.sufb200_trunc_write_tapes(*args, _np_ptr(t0), _np_ptr(t1), n.value, C.byref(n)))
+        return t0.tobytes(), t1.tobytes()
+
+    @staticmethod
+    def trunc_read_tape(tape: bytes, kind: int, r_in: int, party: int):
+        """(desc, [key arrays], r_in share) of one party's composite tape of a
+        truncation gate of `kind` with mask r_in (read_composite_tape)."""
+        buf = np.frombuffer(bytes(tape), dtype=np.uint8).copy()
+        d = TruncDesc()
+        off = (C.c_size_t * 4)()
+        kb = (C.c_size_t * 4)()
+        share = C.c_uint64()
+        check(_lib.lib().sufb200_trunc_read_tape(_np_ptr(buf), buf.size, kind, C.c_uint64(r_in), party, C.byref(d),
+                                                 C.cast(off, C.c_void_p), C.cast(kb, C.c_void_p), C.byref(share)))
+        keys = [buf[off[q]:off[q] + kb[q]].copy() for q in range(int(d.nq))]
+        return d, keys, int(share.value)
+
+    @staticmethod
+    def trunc_gen_elem_rin_shares(kind: int, frac_bits: int, seed: int, n: int) -> np.ndarray:
+        """Party 0's r_in shares of trunc_gen_elem's n gates (party 1's: r_in - these)."""
+        out = np.zeros(n, dtype=np.uint64)
+        check(_lib.lib().sufb200_trunc_gen_elem_rin_shares(kind, frac_bits, C.c_uint64(seed), n, _np_ptr(out)))
+        return out
+
+    def trunc_write_tapes_elem(self, shape: TruncDesc, d_keys: Sequence, key_bytes: Sequence[int], d_words, d_r_in,
+                               d_r_in_share, bit_order: int = 1, stream=None):
+        """One party's per-element tapes on the device: ([n][stride] uint8, [n] lengths)."""
+        import torch
+
+        n = d_r_in.numel()
+        nq = int(shape.nq)
+        sizes = (C.c_size_t * 4)(*[int(b) for b in key_bytes[:nq]], *([0] * (4 - nq)))
+        stride = int(self._L.sufb200_trunc_tape_elem_stride(C.byref(shape), C.cast(sizes, C.c_void_p)))
+        if stride == 0:
+            raise SufB200Error(_lib.ERR_INVALID, "bad per-element shape")
+        out = torch.empty((n, stride), dtype=torch.uint8, device=d_r_in.device)
+        lens = torch.empty(n, dtype=torch.int64, device=d_r_in.device)
+        ptrs = (C.c_void_p * 4)(*[_t_ptr(k) for k in d_keys[:nq]], *([None] * (4 - nq)))
+        check(self._L.sufb200_trunc_write_tapes_elem(self.h, C.byref(shape), C.cast(ptrs, C.c_void_p),
+                                                     C.cast(sizes, C.c_void_p), _t_ptr(d_words), _t_ptr(d_r_in),
+                                                     _t_ptr(d_r_in_share), n, bit_order, _t_ptr(out), stride,
+                                                     _t_ptr(lens), _stream_ptr(stream)))
+        return out, lens
+
     def trunc_bundle_eval_host(self, desc: TruncDesc, keys: Sequence[np.ndarray], xhat: np.ndarray,
                                y: np.ndarray | None = None, bools: np.ndarray | None = None) -> np.ndarray:
         """Host buffers in and out (pinned memory makes the copies true DMA)."""
