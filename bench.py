@@ -260,31 +260,32 @@ def _max_over_ranks(ws: int, dev, v: float) -> float:
 
 
 def _timed(args, ws, dev, stream, flush, step, ctx, local, sample_clocks=True, mids=False):
-    """W untimed steps, then K steps bracketed by a barrier and a device
-    synchronize, each timed by CUDA events on the launch stream after a 256 MB
-    write (> 126 MB L2); returns (max over ranks of the mean step ms, this
+    """W untimed steps (after the clock sampler has started, so an idle GPU's
+    clocks are back up before timing), then K steps bracketed by a barrier
+    and a device synchronize, each timed by CUDA events on the launch stream
+    after a 256 MB write (> 126 MB L2); returns (max over ranks of the mean step ms, this
     rank's step times, the clock sampler[, this rank's step-start -> mid-event
     times]).  With mids=True the step is called as step(mid) and records
     `mid` on the stream at the point whose share of the step is wanted."""
     import torch
     import torch.distributed as dist
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            if mids:
-                step(torch.cuda.Event(enable_timing=True))
-            else:
-                step()
-    ctx.sync(stream)
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     mid_evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] if mids else None
     clk = ClockSampler(local if sample_clocks else None)
     with clk:
         if sample_clocks:
-            time.sleep(0.3)
+            time.sleep(0.3)  # the sampler's first readings; the warm-up then brings the clocks back up
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                if mids:
+                    step(torch.cuda.Event(enable_timing=True))
+                else:
+                    step()
+        ctx.sync(stream)
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             for k in range(args.steps):
                 flush.fill_(k)
@@ -1200,7 +1201,7 @@ def run_silu(args, ws, rank, local):
     import torch
     import torch.distributed as dist
 
-    from suf_b200.engine import Context, coeff_lut_eval
+    from suf_b200.engine import Context, coeff_lut_eval, coeff_lut_eval_pair
     from tests.helpers import silu_fixture, suf_table_eval
 
     torch.cuda.set_device(local)
@@ -1219,7 +1220,13 @@ def run_silu(args, ws, rank, local):
     d_y = {p: torch.empty(n * r, dtype=torch.int64, device=dev) for p in parties}
     flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
 
+    pair = len(parties) == 2
+
     def step():
+        if pair:  # both parties on this GPU: one launch (sufb200_coeff_lut_eval_pair)
+            coeff_lut_eval_pair(ctx, fx["keys"], d_x, r, fx["degree"], r_outs=(fx["r_out_share0"], fx["r_out_share1"]),
+                                d_outs=(d_y[0], d_y[1]), stream=stream)
+            return
         for p in parties:
             coeff_lut_eval(ctx, fx["keys"][p], d_x, r, fx["degree"], r_out=fx[f"r_out_share{p}"], d_out=d_y[p],
                            stream=stream)
@@ -1239,9 +1246,15 @@ def run_silu(args, ws, rank, local):
 
     def e2e_step():
         d = x_pin.to(dev, non_blocking=True)
-        for p in parties:
-            y_pin[p].copy_(coeff_lut_eval(ctx, fx["keys"][p], d, r, fx["degree"], r_out=fx[f"r_out_share{p}"]),
-                           non_blocking=True)
+        if pair:
+            ys = coeff_lut_eval_pair(ctx, fx["keys"], d, r, fx["degree"],
+                                     r_outs=(fx["r_out_share0"], fx["r_out_share1"]))
+            for p in parties:
+                y_pin[p].copy_(ys[p], non_blocking=True)
+        else:
+            for p in parties:
+                y_pin[p].copy_(coeff_lut_eval(ctx, fx["keys"][p], d, r, fx["degree"], r_out=fx[f"r_out_share{p}"]),
+                               non_blocking=True)
         torch.cuda.synchronize()
 
     for _ in range(3):
@@ -1255,9 +1268,10 @@ def run_silu(args, ws, rank, local):
 
     peaks = measured_peaks()
     engine_peak = ctx.probe_aes_engine()
-    kernel_ms = ms / len(parties)
-    blocks = n * ((fx["out_words"] + 1) // 2)  # one AES block per two coefficient words
-    hbm = n * (8 + 8 * r)
+    launches = 1 if pair else len(parties)
+    kernel_ms = ms / launches
+    blocks = n * (len(parties) // launches) * ((fx["out_words"] + 1) // 2)  # one AES block per two words
+    hbm = n * (8 + 8 * r * (len(parties) // launches))
     out = None
     if rank == 0:
         out = {"metric": SILU_METRIC, "value": round(units / (ms / 1e3), 1), "unit": "gate evals/s", "n_gpus": ws,
@@ -1270,18 +1284,20 @@ def run_silu(args, ws, rank, local):
                           "l2": "256 MB flush between steps", "parallelism": f"party x element shards on {ws} GPU(s)"},
                "e2e": {"value": round(units / (e2e_ms / 1e3), 1), "unit": "gate evals/s",
                        "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": len(parties) * n * r * 8,
-                       "ms_per_step": round(e2e_ms, 4), "path": "sufb200_coeff_lut_eval, pinned x^ in, shares out"},
-               "roofline": {"bound": "lsu", "unit": "us per party call", "achieved": round(kernel_ms * 1e3, 2),
+                       "ms_per_step": round(e2e_ms, 4),
+                       "path": ("sufb200_coeff_lut_eval_pair" if pair else "sufb200_coeff_lut_eval")
+                               + ", pinned x^ in, shares out"},
+               "roofline": {"bound": "lsu", "unit": "us per launch", "achieved": round(kernel_ms * 1e3, 2),
                             "aes_floor_us": round(blocks / engine_peak * 1e6, 2),
                             "hbm_floor_us": round(hbm / (peaks.get("hbm_gbs", 6650.0) * 1e9) * 1e6, 2),
                             "frac": round((blocks / engine_peak * 1e6) / (kernel_ms * 1e3), 4),
                             "peak": round(engine_peak / 1e9, 2), "traffic": hbm,
-                            "kernel": "coeff_lut_kernel",
-                            "note": "393 K elements x 2 AES blocks take about 14 us at the engine ceiling; the "
-                                    "kernel issues the table lookups at 56 % of peak with 16 warps per SM (ncu), "
-                                    "frac = AES floor / measured time"},
+                            "kernel": "coeff_lut_pair_kernel" if pair else "coeff_lut_kernel",
+                            "work_model": f"{len(parties) // launches} x 393,216 elements per launch, one AES "
+                                          "block per two coefficient words (2 per element)",
+                            "note": "frac = AES-engine floor of the launch's blocks / measured launch time"},
                "cpu_baseline": cpu_silu_baseline(args, fx, xhat) if (ws == 1 and not args.no_cpu) else None,
-               "clocks": clk.summary(), "gpu_launches": args.steps * len(parties), "reconstruction_ok": ok,
+               "clocks": clk.summary(), "gpu_launches": args.steps * launches, "reconstruction_ok": ok,
                "ms_per_step_all": [round(v, 4) for v in ms_steps]}
     if ws > 1:
         dist.barrier()

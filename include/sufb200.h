@@ -343,6 +343,14 @@ int sufb200_myl7_gen_batch_device(sufb200_ctx ctx, int group, int in_bits, const
 int sufb200_coeff_lut_eval(sufb200_ctx ctx, const uint8_t* key, size_t key_bytes, const uint64_t* d_xhat, size_t n,
                            int r, int degree, const uint64_t* r_out, int ring_bits, uint64_t idx_base,
                            uint64_t* d_out, void* stream);
+/* Both parties' coefficient gates over the same public x^ in one launch (one
+ * GPU holding both parties, as the reference's single-GPU runs do): party
+ * 0's key / r_out0 / d_out0 and party 1's, the same r, degree and ring; each
+ * output equals sufb200_coeff_lut_eval's for that party. */
+int sufb200_coeff_lut_eval_pair(sufb200_ctx ctx, const uint8_t* key0, size_t key_bytes0, const uint8_t* key1,
+                                size_t key_bytes1, const uint64_t* d_xhat, size_t n, int r, int degree,
+                                const uint64_t* r_out0, const uint64_t* r_out1, int ring_bits, uint64_t idx_base,
+                                uint64_t* d_out0, uint64_t* d_out1, void* stream);
 
 /* seed_from_id (pfss_backend_gpu.cu:189-194): 16 bytes from
  * mt19937_64(id ^ tweak * 0x9e3779b97f4a7c15). */

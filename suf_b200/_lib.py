@@ -112,6 +112,8 @@ _SIGS = {
     "sufb200_beaver_matmul2d_tc": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, C.c_int64, _i, _vp,
                                         _vp]),
     "sufb200_coeff_lut_eval": (_i, [_vp, _vp, _sz, _vp, _sz, _i, _i, _vp, _i, _u64, _vp, _vp]),
+    "sufb200_coeff_lut_eval_pair": (_i, [_vp, _vp, _sz, _vp, _sz, _vp, _sz, _i, _i, _vp, _vp, _i, _u64, _vp, _vp,
+                                         _vp]),
     "sufb200_open_unique_id": (_i, [_vp]),
     "sufb200_open_comm_create": (_i, [_vp, _vp, _i, _i, C.c_double, C.POINTER(_vp)]),
     "sufb200_open_comm_destroy": (_i, [_vp]),

@@ -871,10 +871,14 @@ int sufb200_myl7_gen_batch_device(sufb200_ctx ctx, int group, int in_bits, const
   return SUFB200_OK;
 }
 
-int sufb200_coeff_lut_eval(sufb200_ctx ctx, const uint8_t* key, size_t key_bytes, const uint64_t* d_xhat, size_t n,
-                           int r, int degree, const uint64_t* r_out, int ring_bits, uint64_t idx_base,
-                           uint64_t* d_out, void* stream) {
-  if (int rc = check_ctx(ctx, false)) return rc;
+// Checks one party's coefficient-gate key against r / degree and fills the
+// launch parameters (the key rides in them when it fits, else it is staged
+// in a pool buffer returned through *scratch, freed by the caller after the
+// launch).
+static int coeff_prepare(sufb200_ctx ctx, const uint8_t* key, size_t key_bytes, int r, int degree,
+                         const uint64_t* r_out, int ring_bits, sufb200::CoeffLutParams& p, uint8_t** scratch,
+                         cudaStream_t st) {
+  *scratch = nullptr;
   if (r < 1 || r > sufb200::kCoeffMaxOut || degree < 0 || degree > 15 || ring_bits < 1 || ring_bits > 64)
     return fail(SUFB200_ERR_INVALID, "need 1 <= r <= 8, 0 <= degree <= 15, 1 <= ring_bits <= 64");
   if (!key || key_bytes < 216 + 24) return fail(SUFB200_ERR_KEY, "interval key missing or too small");
@@ -884,31 +888,75 @@ int sufb200_coeff_lut_eval(sufb200_ctx ctx, const uint8_t* key, size_t key_bytes
   if (in_bits < 1 || in_bits > 64 || ivs < 1 || ow != static_cast<uint64_t>(r) * static_cast<uint64_t>(degree + 1))
     return fail(SUFB200_ERR_KEY, "interval key header does not match r * (degree + 1) output words");
   if (key_bytes < 216 + 8 * (ivs + 1 + ivs * ow)) return fail(SUFB200_ERR_KEY, "interval key shorter than its table");
-  if (n == 0) return SUFB200_OK;
-  if (!d_xhat || !d_out || !aligned8(d_xhat) || !aligned8(d_out))
-    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
-  cudaStream_t st = as_stream(stream);
-  static thread_local sufb200::CoeffLutParams p;  // 4 KB: not on the stack
   p.r = r;
   p.degree = degree;
   p.ring_mask = ring_bits >= 64 ? ~0ull : ((1ull << ring_bits) - 1ull);
   for (int j = 0; j < sufb200::kCoeffMaxOut; j++) p.r_out[j] = (r_out && j < r) ? r_out[j] : 0ull;
   p.key_in_params = key_bytes <= sufb200::kCoeffParamKeyBytes ? 1 : 0;
-  uint8_t* scratch = nullptr;
-  cudaError_t e = cudaSuccess;
   if (p.key_in_params) {
     std::memcpy(p.key, key, key_bytes);
-  } else {
-    SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), (key_bytes + 255) & ~size_t{255},
-                                               ctx->pool, st),
-                       "coefficient key staging");
-    e = cudaMemcpyAsync(scratch, key, key_bytes, cudaMemcpyHostToDevice, st);
+    return SUFB200_OK;
   }
-  sufb200::RefFmtLaunch a{scratch, key_bytes, 1, d_xhat, n, idx_base, d_out, 0, static_cast<int>(ow), 0, ctx->d_t0,
+  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(scratch), (key_bytes + 255) & ~size_t{255},
+                                             ctx->pool, st),
+                     "coefficient key staging");
+  SUFB200_CHECK_CUDA(cudaMemcpyAsync(*scratch, key, key_bytes, cudaMemcpyHostToDevice, st), "coefficient key H2D");
+  return SUFB200_OK;
+}
+
+int sufb200_coeff_lut_eval(sufb200_ctx ctx, const uint8_t* key, size_t key_bytes, const uint64_t* d_xhat, size_t n,
+                           int r, int degree, const uint64_t* r_out, int ring_bits, uint64_t idx_base,
+                           uint64_t* d_out, void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  cudaStream_t st = as_stream(stream);
+  static thread_local sufb200::CoeffLutParams p;  // 4 KB: not on the stack
+  uint8_t* scratch = nullptr;
+  if (n == 0) {
+    if (int rc = coeff_prepare(ctx, key, key_bytes, r, degree, r_out, ring_bits, p, &scratch, nullptr)) return rc;
+    return SUFB200_OK;
+  }
+  if (!d_xhat || !d_out || !aligned8(d_xhat) || !aligned8(d_out))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  if (int rc = coeff_prepare(ctx, key, key_bytes, r, degree, r_out, ring_bits, p, &scratch, st)) {
+    if (scratch) cudaFreeAsync(scratch, st);
+    return rc;
+  }
+  sufb200::RefFmtLaunch a{scratch, key_bytes, 1, d_xhat, n, idx_base, d_out, 0, r * (degree + 1), 0, ctx->d_t0,
                           ctx->d_status};
-  if (e == cudaSuccess) e = sufb200::launch_coeff_lut(ctx, a, p, st);
+  cudaError_t e = sufb200::launch_coeff_lut(ctx, a, p, st);
   if (scratch) cudaFreeAsync(scratch, st);
   if (e != cudaSuccess) return cuda_fail(e, "coefficient LUT launch");
+  return SUFB200_OK;
+}
+
+int sufb200_coeff_lut_eval_pair(sufb200_ctx ctx, const uint8_t* key0, size_t key_bytes0, const uint8_t* key1,
+                                size_t key_bytes1, const uint64_t* d_xhat, size_t n, int r, int degree,
+                                const uint64_t* r_out0, const uint64_t* r_out1, int ring_bits, uint64_t idx_base,
+                                uint64_t* d_out0, uint64_t* d_out1, void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  cudaStream_t st = as_stream(stream);
+  static thread_local sufb200::CoeffLutParams p[2];
+  uint8_t* scratch[2] = {nullptr, nullptr};
+  const uint8_t* keys[2] = {key0, key1};
+  const size_t kb[2] = {key_bytes0, key_bytes1};
+  const uint64_t* ro[2] = {r_out0, r_out1};
+  if (n != 0 && (!d_xhat || !d_out0 || !d_out1 || !aligned8(d_xhat) || !aligned8(d_out0) || !aligned8(d_out1)))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  int rc = SUFB200_OK;
+  for (int q = 0; q < 2 && rc == SUFB200_OK; q++)
+    rc = coeff_prepare(ctx, keys[q], kb[q], r, degree, ro[q], ring_bits, p[q], &scratch[q], n ? st : nullptr);
+  cudaError_t e = cudaSuccess;
+  if (rc == SUFB200_OK && n != 0) {
+    sufb200::RefFmtLaunch a0{scratch[0], kb[0], 1, d_xhat, n, idx_base, d_out0, 0, r * (degree + 1), 0, ctx->d_t0,
+                             ctx->d_status};
+    sufb200::RefFmtLaunch a1{scratch[1], kb[1], 1, d_xhat, n, idx_base, d_out1, 0, r * (degree + 1), 0, ctx->d_t0,
+                             ctx->d_status};
+    e = sufb200::launch_coeff_lut_pair(ctx, a0, p[0], a1, p[1], st);
+  }
+  for (int q = 0; q < 2; q++)
+    if (scratch[q]) cudaFreeAsync(scratch[q], st);
+  if (rc != SUFB200_OK) return rc;
+  if (e != cudaSuccess) return cuda_fail(e, "coefficient LUT pair launch");
   return SUFB200_OK;
 }
 

@@ -116,6 +116,9 @@ struct CoeffLutParams {
 };
 cudaError_t launch_coeff_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, const CoeffLutParams& p,
                              cudaStream_t st);
+// Both parties' gates over one x^ (a0.xs == a1.xs, equal n) in one launch.
+cudaError_t launch_coeff_lut_pair(const sufb200_ctx_s* ctx, const RefFmtLaunch& a0, const CoeffLutParams& p0,
+                                  const RefFmtLaunch& a1, const CoeffLutParams& p1, cudaStream_t st);
 
 // Shared-prefix evaluation of broadcast keys (prefix.cu, prefix.cuh).
 struct RangeAcc;

@@ -247,6 +247,160 @@ __global__ void __launch_bounds__(kAesThreads, 1) interval_lut_pair_kernel(const
   }
 }
 
+// One party's gate of a coefficient launch, laid out once per block in
+// shared memory.
+struct CoeffSide {
+  const uint64_t* cuts;  // the interval starts (shared memory when they fit)
+  const uint64_t* pay;   // ivs rows of ow words
+  uint64_t* out;
+  uint64_t nonce, m, ring_mask, idx_base;
+  uint64_t r_out[kCoeffMaxOut];
+  uint32_t party, ivs;
+  int ow, r, d1, ok;
+};
+
+// Stage side q's round keys (s_rk, 44 words), its cut/payload table when it
+// fits `cap` bytes (s_tab) and its scalars (S, by thread 0).
+__device__ __forceinline__ void stage_coeff_side(const RefFmtLaunch& a, const CoeffLutParams& p, uint32_t* s_rk,
+                                                 uint64_t* s_tab, uint32_t cap, CoeffSide* S) {
+  const uint8_t* key = p.key_in_params ? p.key : a.keys;
+  const uint64_t h = *reinterpret_cast<const uint64_t*>(key);
+  const int in_bits = static_cast<int>(h & 0xFFFF);
+  const int ow = static_cast<int>((h >> 16) & 0xFFFF);
+  const uint32_t ivs = static_cast<uint32_t>(h >> 32);
+  const size_t words = static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow;
+  const bool tab_in_smem = 8u * words <= cap;
+  for (int i = threadIdx.x; i < 44; i += blockDim.x) s_rk[i] = reinterpret_cast<const uint32_t*>(key + 40)[i];
+  if (tab_in_smem)
+    for (size_t i = threadIdx.x; i < words; i += blockDim.x) s_tab[i] = reinterpret_cast<const uint64_t*>(key + 216)[i];
+  if (threadIdx.x == 0) {
+    const uint64_t* cuts = tab_in_smem ? s_tab : reinterpret_cast<const uint64_t*>(key + 216);
+    S->cuts = cuts;
+    S->pay = cuts + ivs + 1;
+    S->out = reinterpret_cast<uint64_t*>(a.out);
+    S->nonce = *reinterpret_cast<const uint64_t*>(key + 16);
+    S->m = mask_bits(in_bits);
+    S->ring_mask = p.ring_mask;
+    S->idx_base = a.idx_base;
+    for (int j = 0; j < kCoeffMaxOut; j++) S->r_out[j] = p.r_out[j];
+    S->party = key[8];
+    S->ivs = ivs;
+    S->ow = ow;
+    S->r = p.r;
+    S->d1 = p.degree + 1;
+    S->ok = ow == p.r * (p.degree + 1) && ivs != 0 && 216u + 8u * words <= a.key_bytes;
+  }
+}
+
+__device__ __forceinline__ int coeff_interval(const CoeffSide& S, uint64_t xh) {
+  const uint64_t x = xh & S.m;
+  int lo = 0, hi = static_cast<int>(S.ivs);
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if ((S.cuts[mid] & S.m) <= x) lo = mid + 1; else hi = mid;
+  }
+  return lo - 1 < 0 ? 0 : (lo - 1 >= static_cast<int>(S.ivs) ? static_cast<int>(S.ivs) - 1 : lo - 1);
+}
+
+// Elements of NP gates over one x^ (NP = 2: both parties; items [0, n) are
+// party 0's, [n, 2n) party 1's).  Warps take 32-item chunks dealt
+// round-robin over the blocks (chunk = warp-in-block * grid + block), so the
+// last partial wave spreads over every SM while each warp's x^ loads stay
+// coalesced, and each lane loads its next item's x^ before working on the
+// current one.
+template <int NP>
+__device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const CoeffLutParams& p0,
+                                               const RefFmtLaunch& a1, const CoeffLutParams& p1) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if (!aes_layout_ok()) {
+    if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
+    return;
+  }
+  const size_t n = a0.n, total = NP * n;
+  const uint64_t* xs = a0.xs;
+  const uint32_t lane = threadIdx.x & 31u;
+  const size_t step = static_cast<size_t>(gridDim.x) * (blockDim.x >> 5) * 32;
+  const size_t first = ((static_cast<size_t>(threadIdx.x >> 5) * gridDim.x + blockIdx.x) << 5) + lane;
+  uint64_t xh_next = first < total ? __ldg(xs + (first < n ? first : first - n)) : 0ull;  // before the table fill
+  uint32_t* s_rk = reinterpret_cast<uint32_t*>(smem);                 // [NP][44]
+  CoeffSide* s_side = reinterpret_cast<CoeffSide*>(smem + 512);       // [NP]
+  uint64_t* s_tab = reinterpret_cast<uint64_t*>(smem + 1024);         // [NP][kStageBytes / NP]
+  stage_coeff_side(a0, p0, s_rk, s_tab, kStageBytes / NP, &s_side[0]);
+  if (NP == 2) stage_coeff_side(a1, p1, s_rk + 44, s_tab + kStageBytes / 16, kStageBytes / 2, &s_side[1]);
+  aes_fill_tables(a0.t0);
+  __syncthreads();
+  if (threadIdx.x == 0 && blockIdx.x == 0)
+    for (int q = 0; q < NP; q++)
+      if (!s_side[q].ok) atomicOr(a0.status, kStatusBadKeyHeader);
+  const uint32_t lb = lane_base();
+  uint32_t rk[44];
+  int cur = -1;
+  for (size_t g = first; g < total; g += step) {
+    const uint64_t xh = xh_next;
+    const size_t gn = g + step;
+    xh_next = gn < total ? __ldg(xs + (gn < n ? gn : gn - n)) : 0ull;
+    const int q = (NP == 2 && g >= n) ? 1 : 0;
+    const size_t i = q ? g - n : g;
+    const CoeffSide& S = s_side[q];
+    const int r = S.r;
+    uint64_t* out = S.out + i * static_cast<size_t>(r);
+    if (!S.ok) {
+      for (int j = 0; j < r; j++) out[j] = 0;
+      continue;
+    }
+    const int iv = coeff_interval(S, xh);
+    const uint64_t base = S.nonce ^ ((S.idx_base + i) << 32);
+    const uint64_t w0 = static_cast<uint64_t>(iv) * static_cast<uint64_t>(S.ow);
+    const uint64_t* row = S.pay + static_cast<size_t>(iv) * S.ow;
+    const uint32_t party = S.party;
+    const int d1 = S.d1;
+    if (S.ow <= 4) {
+      // Rows of at most four words (configs[2]'s SiLU gate: r = 4, degree 0):
+      // both CTR blocks of an element at once, round keys in registers.
+      if (q != cur) {
+#pragma unroll
+        for (int k = 0; k < 44; k++) rk[k] = s_rk[44 * q + k];
+        cur = q;
+      }
+      Blk k0, k1;
+      aes_encrypt2_rk(ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2)), lb, rk, k0, k1);
+      const uint64_t ks[4] = {(static_cast<uint64_t>(k0.w[1]) << 32) | k0.w[0],
+                              (static_cast<uint64_t>(k0.w[3]) << 32) | k0.w[2],
+                              (static_cast<uint64_t>(k1.w[1]) << 32) | k1.w[0],
+                              (static_cast<uint64_t>(k1.w[3]) << 32) | k1.w[2]};
+      int w = 0;
+      for (int j = 0; j < r; j++) {
+        uint64_t acc = 0, pw = 1;
+        for (int k = 0; k < d1; k++, w++) {
+          const uint64_t ksw = w == 0 ? ks[0] : (w == 1 ? ks[1] : (w == 2 ? ks[2] : ks[3]));
+          const uint64_t c = party == 0 ? ksw : (row[w] - ksw);
+          acc += c * pw;
+          pw *= xh;
+        }
+        out[j] = (acc + S.r_out[j]) & S.ring_mask;
+      }
+      continue;
+    }
+    uint64_t ks0 = 0, ks1 = 0;
+    int w = 0;
+    for (int j = 0; j < r; j++) {
+      uint64_t acc = 0, pw = 1;
+      for (int k = 0; k < d1; k++, w++) {
+        if ((w & 1) == 0) {
+          const Blk ks = aes_encrypt_smem_rk(ctr_block(base ^ (w0 + w)), lb, s_rk + 44 * q);
+          ks0 = (static_cast<uint64_t>(ks.w[1]) << 32) | ks.w[0];
+          ks1 = (static_cast<uint64_t>(ks.w[3]) << 32) | ks.w[2];
+        }
+        const uint64_t ksw = (w & 1) ? ks1 : ks0;
+        const uint64_t c = party == 0 ? ksw : (row[w] - ksw);
+        acc += c * pw;
+        pw *= xh;
+      }
+      out[j] = (acc + S.r_out[j]) & S.ring_mask;
+    }
+  }
+}
+
 // ---- coefficient LUT + polynomial over x^ (composite eval, ell = 0) ------
 // Restates the two beaver-free branches of composite_eval_batch_backend for a
 // gate whose coefficient words come from one broadcast interval LUT:
@@ -260,117 +414,16 @@ __global__ void __launch_bounds__(kAesThreads, 1) interval_lut_pair_kernel(const
 // nonce ^ (idx << 32) ^ (iv * out_words + w)).  Ring arithmetic mod 2^64,
 // reduced to ring_bits at the end (2^ring_bits divides 2^64).
 __global__ void __launch_bounds__(kAesThreads, 1)
-    coeff_lut_kernel(const RefFmtLaunch a0, const __grid_constant__ CoeffLutParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  if (!aes_layout_ok()) {
-    if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
-    return;
-  }
-  RefFmtLaunch a = a0;
-  if (p.key_in_params) a.keys = p.key;  // small keys ride in the parameter space: no staging copy
-  uint32_t* s_rk = reinterpret_cast<uint32_t*>(smem);
-  uint64_t* s_tab = reinterpret_cast<uint64_t*>(smem + 256);  // cuts then payload
-  const uint64_t h = *reinterpret_cast<const uint64_t*>(a.keys);
-  const int in_bits = static_cast<int>(h & 0xFFFF);
-  const int ow = static_cast<int>((h >> 16) & 0xFFFF);
-  const uint32_t ivs = static_cast<uint32_t>(h >> 32);
-  const size_t words = static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow;
-  const bool tab_in_smem = 8u * words <= kStageBytes;
-  for (int i = threadIdx.x; i < 44; i += blockDim.x) s_rk[i] = reinterpret_cast<const uint32_t*>(a.keys + 40)[i];
-  if (tab_in_smem)
-    for (size_t i = threadIdx.x; i < words; i += blockDim.x) s_tab[i] = reinterpret_cast<const uint64_t*>(a.keys + 216)[i];
-  aes_fill_tables(a.t0);
-  __syncthreads();
-  const int r = p.r, d1 = p.degree + 1;
-  if (ow != r * d1 || ivs == 0 || 216u + 8u * words > a.key_bytes) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.status, kStatusBadKeyHeader);
-    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x)
-      for (int j = 0; j < r; j++) reinterpret_cast<uint64_t*>(a.out)[i * r + j] = 0;
-    return;
-  }
-  const uint32_t party = a.keys[8];
-  const uint64_t nonce = *reinterpret_cast<const uint64_t*>(a.keys + 16);
-  const uint64_t* cuts = tab_in_smem ? s_tab : reinterpret_cast<const uint64_t*>(a.keys + 216);
-  const uint64_t* pay = cuts + ivs + 1;
-  const uint64_t m = mask_bits(in_bits);
-  const uint32_t lb = lane_base();
-  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-  if (ow <= 4) {
-    // Rows of at most four words (configs[2]'s SiLU gate: r = 4, degree 0):
-    // both CTR blocks of an element at once, round keys in registers.
-    uint32_t rk[44];
-#pragma unroll
-    for (int k = 0; k < 44; k++) rk[k] = s_rk[k];
-    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
-      const uint64_t xh = a.xs[i];
-      const uint64_t x = xh & m;
-      int lo = 0, hi = static_cast<int>(ivs);
-      while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if ((cuts[mid] & m) <= x) lo = mid + 1; else hi = mid;
-      }
-      const int iv = lo - 1 < 0 ? 0 : (lo - 1 >= static_cast<int>(ivs) ? static_cast<int>(ivs) - 1 : lo - 1);
-      const uint64_t base = nonce ^ ((a.idx_base + i) << 32);
-      const uint64_t w0 = static_cast<uint64_t>(iv) * static_cast<uint64_t>(ow);
-      Blk k0, k1;
-      aes_encrypt2_rk(ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2)), lb, rk, k0, k1);
-      const uint64_t ks0 = (static_cast<uint64_t>(k0.w[1]) << 32) | k0.w[0];
-      const uint64_t ks1 = (static_cast<uint64_t>(k0.w[3]) << 32) | k0.w[2];
-      const uint64_t ks2 = (static_cast<uint64_t>(k1.w[1]) << 32) | k1.w[0];
-      const uint64_t ks3 = (static_cast<uint64_t>(k1.w[3]) << 32) | k1.w[2];
-      const uint64_t* row = pay + static_cast<size_t>(iv) * ow;
-      uint64_t* out = reinterpret_cast<uint64_t*>(a.out) + i * static_cast<size_t>(r);
-      int w = 0;
-      for (int j = 0; j < r; j++) {
-        uint64_t acc = 0, pw = 1;
-        for (int k = 0; k < d1; k++, w++) {
-          const uint64_t ksw = w == 0 ? ks0 : (w == 1 ? ks1 : (w == 2 ? ks2 : ks3));
-          const uint64_t c = party == 0 ? ksw : (row[w] - ksw);
-          acc += c * pw;
-          pw *= xh;
-        }
-        out[j] = (acc + p.r_out[j]) & p.ring_mask;
-      }
-    }
-    return;
-  }
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
-    const uint64_t xh = a.xs[i];
-    const uint64_t x = xh & m;
-    int iv = static_cast<int>(ivs) - 1;
-    if (ivs > 1) {
-      int lo = 0, hi = static_cast<int>(ivs);
-      while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if ((cuts[mid] & m) <= x) lo = mid + 1; else hi = mid;
-      }
-      iv = lo - 1;
-      if (iv < 0) iv = 0;
-      if (iv >= static_cast<int>(ivs)) iv = static_cast<int>(ivs) - 1;
-    }
-    const uint64_t idx = a.idx_base + i;
-    const uint64_t* row = pay + static_cast<size_t>(iv) * ow;
-    uint64_t* out = reinterpret_cast<uint64_t*>(a.out) + i * static_cast<size_t>(r);
-    uint64_t ks0 = 0, ks1 = 0;
-    int w = 0;
-    for (int j = 0; j < r; j++) {
-      uint64_t acc = 0, pw = 1;
-      for (int k = 0; k < d1; k++, w++) {
-        if ((w & 1) == 0) {
-          const uint64_t ctr = nonce ^ (idx << 32) ^ (static_cast<uint64_t>(iv) * static_cast<uint64_t>(ow) + w);
-          const Blk ks = aes_encrypt_smem_rk(ctr_block(ctr), lb, s_rk);
-          ks0 = (static_cast<uint64_t>(ks.w[1]) << 32) | ks.w[0];
-          ks1 = (static_cast<uint64_t>(ks.w[3]) << 32) | ks.w[2];
-        }
-        const uint64_t ksw = (w & 1) ? ks1 : ks0;
-        const uint64_t c = party == 0 ? ksw : (row[w] - ksw);
-        acc += c * pw;
-        pw *= xh;
-      }
-      out[j] = (acc + p.r_out[j]) & p.ring_mask;
-    }
-  }
+    coeff_lut_kernel(const RefFmtLaunch a, const __grid_constant__ CoeffLutParams p) {
+  coeff_lut_body<1>(a, p, a, p);
+}
+
+// Both parties' gates over one x^ in one launch (the parties' halves of one
+// GPU's work: one table fill and one launch for the pair).
+__global__ void __launch_bounds__(kAesThreads, 1)
+    coeff_lut_pair_kernel(const RefFmtLaunch a0, const __grid_constant__ CoeffLutParams p0, const RefFmtLaunch a1,
+                          const __grid_constant__ CoeffLutParams p1) {
+  coeff_lut_body<2>(a0, p0, a1, p1);
 }
 
 int grid_for(const sufb200_ctx_s* ctx, size_t n, int threads, int per_sm) {
@@ -441,6 +494,17 @@ cudaError_t launch_coeff_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, co
                                        static_cast<int>(ctx->aes_dyn_bytes));
   if (e != cudaSuccess) return e;
   coeff_lut_kernel<<<grid_for(ctx, a.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st>>>(a, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_coeff_lut_pair(const sufb200_ctx_s* ctx, const RefFmtLaunch& a0, const CoeffLutParams& p0,
+                                  const RefFmtLaunch& a1, const CoeffLutParams& p1, cudaStream_t st) {
+  if (a0.n != a1.n || a0.xs != a1.xs) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(coeff_lut_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(ctx->aes_dyn_bytes));
+  if (e != cudaSuccess) return e;
+  coeff_lut_pair_kernel<<<grid_for(ctx, 2 * a0.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st>>>(a0, p0, a1,
+                                                                                                         p1);
   return cudaGetLastError();
 }
 

@@ -341,6 +341,26 @@ def coeff_lut_eval(ctx: "Context", key: np.ndarray, d_xhat, r: int, degree: int,
     return d_out
 
 
+def coeff_lut_eval_pair(ctx: "Context", keys, d_xhat, r: int, degree: int, r_outs=(None, None), ring_bits: int = 64,
+                        idx_base: int = 0, d_outs=(None, None), stream=None):
+    """sufb200_coeff_lut_eval_pair: both parties' coefficient gates over one
+    x^ in one launch; returns (party 0's, party 1's) outputs."""
+    import torch
+
+    ks = [np.ascontiguousarray(k, dtype=np.uint8) for k in keys]
+    n = d_xhat.numel()
+    outs = [d if d is not None else torch.empty(max(n * r, 1), dtype=torch.int64, device=d_xhat.device)
+            for d in d_outs]
+    ro = [None if v is None else np.ascontiguousarray(v, dtype=np.uint64) for v in r_outs]
+    check(ctx._L.sufb200_coeff_lut_eval_pair(ctx.h, _np_ptr(ks[0]), ks[0].size, _np_ptr(ks[1]), ks[1].size,
+                                             _t_ptr(d_xhat), n, r, degree,
+                                             _np_ptr(ro[0]) if ro[0] is not None else None,
+                                             _np_ptr(ro[1]) if ro[1] is not None else None, ring_bits,
+                                             C.c_uint64(idx_base), _t_ptr(outs[0]), _t_ptr(outs[1]),
+                                             _stream_ptr(stream)))
+    return outs[0], outs[1]
+
+
 # -- paired-GPU open ---------------------------------------------------------------
 
 OPEN_ID_BYTES = 128

@@ -156,6 +156,14 @@ class _CoeffGate:
                                             self.degree, ro.ctypes.data, 64, C.c_uint64(0), _t_ptr(d_out),
                                             _stream_ptr(stream)))
 
+    def eval_pair(self, ctx: Context, d_xhat, d_out0, d_out1, stream):
+        """Both parties in one launch (sufb200_coeff_lut_eval_pair)."""
+        k0, k1 = self.keys
+        check(ctx._L.sufb200_coeff_lut_eval_pair(ctx.h, k0.ctypes.data, k0.size, k1.ctypes.data, k1.size,
+                                                 _t_ptr(d_xhat), d_xhat.numel(), 1, self.degree,
+                                                 self.r_out[0].ctypes.data, self.r_out[1].ctypes.data, 64,
+                                                 C.c_uint64(0), _t_ptr(d_out0), _t_ptr(d_out1), _stream_ptr(stream)))
+
 
 class _Triples:
     """Beaver matmul triples, one per head: A [H][M][K], B [H][K][N] (or
@@ -291,7 +299,7 @@ class TransformerLayerPair:
             check(L.sufb200_relu_open_pair(_t_ptr(cur[0]), _t_ptr(cur[1]), rows, w, C.c_uint64(g.r[0]),
                                            C.c_uint64(g.r[1]), _t_ptr(xh), _stream_ptr(stream)))
             rl = self.b["relu"]
-            self._both_parties(stream, lambda p, st: g.eval(self.ctx, p, xh, rl[p][:half], st))
+            g.eval_pair(self.ctx, xh, rl[0][:half], rl[1][:half], stream)
             nxt = bufs[i % 2]
             check(L.sufb200_relu_update_pair(_t_ptr(cur[0]), _t_ptr(cur[1]), _t_ptr(rl[0]), _t_ptr(rl[1]), rows, w,
                                              _t_ptr(nxt[0]), _t_ptr(nxt[1]), _stream_ptr(stream)))
@@ -352,7 +360,7 @@ class TransformerLayerPair:
         g = self.gelu
         check(L.sufb200_open_masked_pair(_t_ptr(b["f1"][0]), _t_ptr(b["f1"][1]), C.c_uint64(g.r[0]),
                                          C.c_uint64(g.r[1]), _t_ptr(xh), n, _stream_ptr(stream)))
-        self._both_parties(stream, lambda p, st: g.eval(self.ctx, p, xh, b["g"][p], st))
+        g.eval_pair(self.ctx, xh, b["g"][0], b["g"][1], stream)
         keep("gelu", b["g"], S * Dff)
         self._matmul_trunc(b["g"], "ff2", Dff, D, self.tr["ff2"], b["a"], stream)
         keep("f2", b["a"], S * D)
@@ -373,6 +381,6 @@ class TransformerLayerPair:
         for n in (d.S * 3 * d.D, d.S * d.D, d.S * d.Dff, d.S * d.D):  # qkv, o, ff1, ff2
             mm += 2 * 2 + 1 + trunc(n)  # two ring matmuls (pre-pass + GEMM each), open, truncation
         bv = 2 * (1 + trunc(d.H * d.S * d.S))  # scores, pv (the pv truncation is S*D elements)
-        relu = self.rounds * 4 + 1
-        gelu = 1 + 2
+        relu = self.rounds * 3 + 1  # open, the pair gate launch, update per round; the final max-difference
+        gelu = 1 + 1  # open, the pair gate launch
         return lf + sm + mm + bv + relu + gelu + 2

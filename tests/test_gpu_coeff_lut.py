@@ -89,3 +89,29 @@ def test_coeff_lut_rejects_shape_mismatch(ctx, torch_cuda, oracle):
         coeff_lut_eval(ctx, d["keys"][0], dx, 2, 0)  # the key has 4 words per interval, not 2
     with pytest.raises(SufB200Error):
         coeff_lut_eval(ctx, d["keys"][0][:300], dx, 4, 0)  # shorter than its table
+
+
+@pytest.mark.parametrize("r,degree,n", [(4, 0, 393_216), (1, 1, 20_001), (3, 2, 1), (8, 0, 77_777)])
+def test_coeff_lut_pair_equals_per_party(ctx, torch_cuda, oracle, r, degree, n):
+    """sufb200_coeff_lut_eval_pair: both parties in one launch give each
+    party's sufb200_coeff_lut_eval output word for word (item counts that
+    split a warp chunk between the parties, a single element, several waves)."""
+    from suf_b200.engine import coeff_lut_eval_pair
+
+    rng = np.random.default_rng(7 * r + n)
+    ow = r * (degree + 1)
+    ivs = 20
+    cuts = np.sort(rng.integers(0, 2**63, ivs - 1, dtype=np.uint64) * np.uint64(2))
+    cuts = np.concatenate([[np.uint64(0)], cuts, [np.uint64(0)]]).astype(np.uint64)
+    pay = rng.integers(0, 2**63, ivs * ow, dtype=np.uint64) * np.uint64(2)
+    seed = oracle.seed_from_id(55 + r, 7)
+    keys = [oracle.interval_key(p, 55 + r, 64, ow, cuts, pay, seed) for p in (0, 1)]
+    xh = rng.integers(0, 2**63, n, dtype=np.uint64) * np.uint64(2) + rng.integers(0, 2, n, dtype=np.uint64)
+    dx = to_dev(torch_cuda, xh)
+    r_out = rng.integers(0, 2**63, (2, r), dtype=np.uint64)
+    y0, y1 = coeff_lut_eval_pair(ctx, keys, dx, r, degree, r_outs=(r_out[0], r_out[1]), idx_base=3)
+    ctx.sync()
+    for p, y in ((0, y0), (1, y1)):
+        want = coeff_lut_eval(ctx, keys[p], dx, r, degree, r_out=r_out[p], idx_base=3)
+        ctx.sync()
+        assert (from_dev(y)[:n * r] == from_dev(want)[:n * r]).all(), p
