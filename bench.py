@@ -287,6 +287,10 @@ def _timed(args, ws, dev, stream, flush, step, ctx, local, sample_clocks=True, m
             dist.barrier()
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
+            # a ~1 ms device-side wait first, so the host has enqueued the first
+            # steps before the GPU reaches them (the events then time the
+            # device's work, not the host's enqueue of step 0)
+            torch.cuda._sleep(2_000_000)
             for k in range(args.steps):
                 flush.fill_(k)
                 evs[k][0].record(stream)

@@ -292,14 +292,19 @@ __device__ __forceinline__ void stage_coeff_side(const RefFmtLaunch& a, const Co
   }
 }
 
+// The interval of x^: the last cut <= x (the first interval below cut 0),
+// by a search whose steps depend only on the cut count (the same trip count
+// and no branches in every lane; a select per step).
 __device__ __forceinline__ int coeff_interval(const CoeffSide& S, uint64_t xh) {
   const uint64_t x = xh & S.m;
-  int lo = 0, hi = static_cast<int>(S.ivs);
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if ((S.cuts[mid] & S.m) <= x) lo = mid + 1; else hi = mid;
+  int base = 0, len = static_cast<int>(S.ivs);
+  while (len > 1) {
+    const int half = len >> 1;
+    base = (S.cuts[base + half] & S.m) <= x ? base + half : base;
+    len -= half;
   }
-  return lo - 1 < 0 ? 0 : (lo - 1 >= static_cast<int>(S.ivs) ? static_cast<int>(S.ivs) - 1 : lo - 1);
+  const int ub = base + ((S.cuts[base] & S.m) <= x ? 1 : 0);  // cuts <= x
+  return ub - 1 < 0 ? 0 : (ub - 1 >= static_cast<int>(S.ivs) ? static_cast<int>(S.ivs) - 1 : ub - 1);
 }
 
 // Elements of NP gates over one x^ (NP = 2: both parties; items [0, n) are
