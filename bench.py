@@ -1772,13 +1772,49 @@ def run_layer(args, ws, rank, local):
     ctx.sync(stream)
     stack_ms = _max_over_ranks(ws, dev, min(stack))
 
+    # the same layer as a CUDA graph (TransformerLayerPair.capture): one
+    # replay per step launches all of the layer's kernels with no host work
+    eager_ms, eager_stack_ms = ms, stack_ms
+    gx = [t.clone() for t in d_x]
+    gy = [torch.empty_like(t) for t in d_x]
+    g1 = lay.capture(gx[0], gx[1], gy[0], gy[1], layers=1)
+
+    def gstep():
+        g1.replay()
+
+    gms, gms_steps, gclk = _timed(args, ws, dev, stream, flush, gstep, ctx, local)
+    ctx.sync(stream)
+    graph_ok = bool((gy[0].cpu().numpy() == d_y[0].cpu().numpy()).all()
+                    and (gy[1].cpu().numpy() == d_y[1].cpu().numpy()).all())
+    gs = lay.capture(gx[0], gx[1], gy[0], gy[1], layers=LAYER_STACK)
+    gstack = []
+    for _ in range(2):
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            flush.fill_(0)
+            ev[0].record(stream)
+            gs.replay()
+            ev[1].record(stream)
+        torch.cuda.synchronize()
+        gstack.append(ev[0].elapsed_time(ev[1]))
+    ctx.sync(stream)
+    graph_stack_ms = _max_over_ranks(ws, dev, min(gstack))
+    if graph_ok:
+        ms, ms_steps, clk, stack_ms = gms, gms_steps, gclk, graph_stack_ms
+
     x_pin = [torch.from_numpy(v.view(np.int64)).pin_memory() for v in (x0, x1)]
     y_pin = [torch.empty(X.size, dtype=torch.int64).pin_memory() for _ in range(2)]
 
     def e2e_step():
         with torch.cuda.stream(stream):
-            a, b = (v.to(dev, non_blocking=True) for v in x_pin)
-            o0, o1 = lay.run(a, b, stream=stream)
+            if graph_ok:  # pinned shares into the graph's input buffers, replay, shares out
+                gx[0].copy_(x_pin[0], non_blocking=True)
+                gx[1].copy_(x_pin[1], non_blocking=True)
+                g1.replay()
+                o0, o1 = gy
+            else:
+                a, b = (v.to(dev, non_blocking=True) for v in x_pin)
+                o0, o1 = lay.run(a, b, stream=stream)
             y_pin[0].copy_(o0, non_blocking=True)
             y_pin[1].copy_(o1, non_blocking=True)
         stream.synchronize()
@@ -1828,8 +1864,12 @@ def run_layer(args, ws, rank, local):
                "stack_ms": round(stack_ms, 3),
                "e2e": {"value": round(e2e_ms, 4), "unit": "ms/layer", "h2d_bytes_per_step": 2 * X.size * 8,
                        "d2h_bytes_per_step": 2 * X.size * 8, "ms_per_step": round(e2e_ms, 4),
-                       "path": "TransformerLayerPair.run from pinned host shares of X to pinned host shares of Y",
+                       "path": ("TransformerLayerPair.capture's graph replayed" if graph_ok else
+                                "TransformerLayerPair.run") + " from pinned host shares of X to pinned host shares of Y",
                        "outputs_match_device_leg": ok_e2e},
+               "graph": {"used_for_value": graph_ok, "outputs_match_eager": graph_ok, "ms_per_layer": round(gms, 4),
+                         "stack_ms": round(graph_stack_ms, 3), "eager_ms_per_layer": round(eager_ms, 4),
+                         "eager_stack_ms": round(eager_stack_ms, 3)},
                "accuracy_vs_float64": acc,
                "dropin_reference_runtime": dropin,
                "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": lay.launches() * args.steps,

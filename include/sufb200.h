@@ -180,6 +180,16 @@ int sufb200_trunc_bundle_eval_pair(sufb200_ctx ctx, const sufb200_trunc_desc* de
                                    const size_t* key_bytes0, const sufb200_trunc_desc* desc1,
                                    const uint8_t* const* keys1, const size_t* key_bytes1, const uint64_t* d_xhat,
                                    size_t n, uint64_t* d_y0, uint64_t* d_y1, void* stream);
+/* The same with every query key already in device memory (d_keys0[q],
+ * d_keys1[q]: dealer material kept resident, any alignment; sizes on the
+ * host): nothing is copied from the host, so a sequence of these calls can be
+ * captured in a CUDA graph.  Key headers are checked on the device (status:
+ * bad key header through sufb200_ctx_sync). */
+int sufb200_trunc_bundle_eval_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0,
+                                       const uint8_t* const* d_keys0, const size_t* key_bytes0,
+                                       const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
+                                       const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
+                                       uint64_t* d_y1, void* stream);
 
 /* Host-buffer form: xhat, y (and bools, may be NULL) in host memory; copies
  * in and out inside the call and returns when y is on the host.  Replaces
@@ -539,8 +549,9 @@ typedef struct sufb200_softmax_party {
   const uint64_t* d_row_c;        /* device [n]   C = A * B[row] */
   sufb200_trunc_desc trunc[SUFB200_SOFTMAX_TRUNCS];
   uint64_t trunc_rin[SUFB200_SOFTMAX_TRUNCS];              /* shares of each truncation's r_in */
-  const uint8_t* trunc_keys[SUFB200_SOFTMAX_TRUNCS][4];    /* host: myl7 key of each query */
+  const uint8_t* trunc_keys[SUFB200_SOFTMAX_TRUNCS][4];    /* myl7 key of each query: host, or device */
   size_t trunc_key_bytes[SUFB200_SOFTMAX_TRUNCS][4];
+  int32_t trunc_keys_device;  /* nonzero: trunc_keys are device pointers (resident; no copy per call) */
 } sufb200_softmax_party;
 
 /* nn::SoftmaxBlockTask (include/nn/softmax_block_task.hpp) for BOTH parties
@@ -573,8 +584,9 @@ typedef struct sufb200_layernorm_party {
   const uint64_t* d_norm_c;        /* device [rows*cols] C = A * B[row] */
   sufb200_trunc_desc trunc[SUFB200_LAYERNORM_TRUNCS];
   uint64_t trunc_rin[SUFB200_LAYERNORM_TRUNCS];
-  const uint8_t* trunc_keys[SUFB200_LAYERNORM_TRUNCS][4]; /* host */
+  const uint8_t* trunc_keys[SUFB200_LAYERNORM_TRUNCS][4]; /* host, or device (trunc_keys_device) */
   size_t trunc_key_bytes[SUFB200_LAYERNORM_TRUNCS][4];
+  int32_t trunc_keys_device;  /* nonzero: trunc_keys are device pointers */
 } sufb200_layernorm_party;
 
 /* runtime::LayerNormTask with RsqrtTask (include/runtime/phase_tasks.hpp:

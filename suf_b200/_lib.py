@@ -75,6 +75,8 @@ _SIGS = {
     "sufb200_trunc_bundle_eval_jobs": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _vp, _vp, _i, _vp]),
     "sufb200_trunc_bundle_eval_pair": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, C.POINTER(TruncDesc), _vp, _vp, _vp,
                                             _sz, _vp, _vp, _vp]),
+    "sufb200_trunc_bundle_eval_pair_dev": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, C.POINTER(TruncDesc), _vp, _vp,
+                                                _vp, _sz, _vp, _vp, _vp]),
     "sufb200_trunc_bundle_eval_host": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp]),
     "sufb200_trunc_bundle_eval_noalloc": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "sufb200_trunc_gen_elem": (_i, [_i, _i, _u64, _sz, C.POINTER(TruncDesc), C.POINTER(TruncDesc), _vp, _vp, _vp,

@@ -467,10 +467,8 @@ int enqueue_chunk_copy(const ChunkSink& k, cudaStream_t st, const uint64_t* d_y,
 int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
                       const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y, uint64_t* d_bools,
                       void* stream, const ChunkSink* sink);
-int trunc_bundle_pair_prefix(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* keys0,
-                             const size_t* key_bytes0, const sufb200_trunc_desc* desc1, const uint8_t* const* keys1,
-                             const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
-                             uint64_t* d_y1, void* stream);
+int trunc_pair_core(sufb200_ctx ctx, sufb200::TruncLaunch a0, sufb200::TruncLaunch a1, const uint64_t* d_xhat,
+                    size_t n, uint64_t* d_y0, uint64_t* d_y1, cudaStream_t st);
 
 }  // namespace
 
@@ -518,70 +516,55 @@ int pack_bundle_keys(const sufb200_trunc_desc& desc, const uint8_t* const* keys,
   return SUFB200_OK;
 }
 
-int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
-                      const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y, uint64_t* d_bools,
-                      void* stream, const ChunkSink* sink) {
-  if (int rc = check_ctx(ctx, true)) return rc;
-  if (int rc = check_bundle_desc(desc, keys, key_bytes)) return rc;
-  if (n == 0) return SUFB200_OK;
-  if (!d_xhat || !d_y || !aligned8(d_xhat) || !aligned8(d_y) || (d_bools && !aligned8(d_bools)))
-    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
-  std::vector<uint8_t> blob;
-  sufb200::TruncLaunch a{};
-  a.desc = *desc;
-  if (int rc = pack_bundle_keys(*desc, keys, key_bytes, blob, a.key_off)) return rc;
-  cudaStream_t st = as_stream(stream);
-  const bool prefix = n >= prefix_min_n() && desc->nq > 0;
-  const uint32_t kmax = sufb200::prefix_budget(n);
-  const size_t blob_bytes = (blob.size() + 255) & ~static_cast<size_t>(255);
-  const size_t scratch_bytes =
-      blob_bytes + (prefix ? kAccBytes + 32ull * kmax * static_cast<size_t>(desc->nq) : 0) + 256;
-  uint8_t* scratch = nullptr;
-  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), scratch_bytes, ctx->pool, st),
-                     "bundle scratch allocation");
-  cudaError_t e = cudaSuccess;
-  if (!blob.empty()) e = cudaMemcpyAsync(scratch, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
-  a.keys = scratch;
-  a.xhat = d_xhat;
-  a.n = n;
-  a.y = d_y;
-  a.bools = d_bools;
+// One party's bundle with its keys already on the device (a.key, xhat, n,
+// y, bools set): range + frontier + the resuming main pass at shared-prefix
+// sizes (scratch for the range and the frontier tables from the pool,
+// stream-ordered), else the one-pass kernel.  No host copies.
+int single_core(sufb200_ctx ctx, sufb200::TruncLaunch a, cudaStream_t st, const ChunkSink* sink) {
+  const size_t n = a.n;
+  const sufb200_trunc_desc* desc = &a.desc;
+  uint64_t* d_y = a.y;
+  uint64_t* d_bools = a.bools;
   a.t0 = ctx->d_t0;
   a.status = ctx->d_status;
-  if (e == cudaSuccess && prefix) {
-    auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch + blob_bytes);
-    sufb200::FrontierEntry* F[4] = {nullptr, nullptr, nullptr, nullptr};
-    sufb200::FrontierBatch fb{};
-    fb.nq = desc->nq;
-    for (int q = 0; q < desc->nq; q++) {
-      F[q] = reinterpret_cast<sufb200::FrontierEntry*>(scratch + blob_bytes + kAccBytes + 32ull * kmax * q);
-      fb.q[q] = sufb200::FrontierLaunch{scratch + a.key_off[q], desc->q_bits[q], 8, acc, kmax, F[q], ctx->d_t0,
-                                        ctx->d_status};
-    }
-    e = sufb200::launch_range(ctx, d_xhat, n, acc, st);
-    if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
-    // the main pass, in chunks when a host sink streams results back (the
-    // kernel's outputs do not depend on the element index)
-    const size_t chunk = sink && sink->chunk ? sink->chunk : n;
-    for (size_t i0 = 0; i0 < n && e == cudaSuccess; i0 += chunk) {
-      const size_t i1 = n - i0 < chunk ? n : i0 + chunk;
-      sufb200::TruncLaunch c = a;
-      c.xhat = d_xhat + i0;
-      c.n = i1 - i0;
-      c.y = d_y + i0;
-      c.bools = d_bools ? d_bools + 3 * i0 : nullptr;
-      e = sufb200::launch_trunc_bundle_prefix(ctx, c, acc, kmax, F, st);
-      if (e == cudaSuccess && sink) {
-        if (int rc = enqueue_chunk_copy(*sink, st, d_y, d_bools, i0, i1)) {
-          cudaFreeAsync(scratch, st);
-          return rc;
-        }
-      }
-    }
-  } else if (e == cudaSuccess) {
+  const bool prefix = n >= prefix_min_n() && desc->nq > 0;
+  cudaError_t e = cudaSuccess;
+  if (!prefix) {
     e = sufb200::launch_trunc_bundle(ctx, a, st);
+    if (e == cudaSuccess && sink)
+      if (int rc = enqueue_chunk_copy(*sink, st, d_y, d_bools, 0, n)) return rc;
+    if (e != cudaSuccess) return cuda_fail(e, "trunc bundle launch");
+    return SUFB200_OK;
+  }
+  const uint32_t kmax = sufb200::prefix_budget(n);
+  uint8_t* scratch = nullptr;
+  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch),
+                                             kAccBytes + 32ull * kmax * static_cast<size_t>(desc->nq) + 256,
+                                             ctx->pool, st),
+                     "bundle scratch allocation");
+  auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch);
+  sufb200::FrontierEntry* F[4] = {nullptr, nullptr, nullptr, nullptr};
+  sufb200::FrontierBatch fb{};
+  fb.nq = desc->nq;
+  for (int q = 0; q < desc->nq; q++) {
+    F[q] = reinterpret_cast<sufb200::FrontierEntry*>(scratch + kAccBytes + 32ull * kmax * q);
+    fb.q[q] = sufb200::FrontierLaunch{a.key[q], desc->q_bits[q], 8, acc, kmax, F[q], ctx->d_t0, ctx->d_status};
+  }
+  e = sufb200::launch_range(ctx, a.xhat, n, acc, st);
+  if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
+  // the main pass, in chunks when a host sink streams results back (the
+  // kernel's outputs do not depend on the element index)
+  const size_t chunk = sink && sink->chunk ? sink->chunk : n;
+  for (size_t i0 = 0; i0 < n && e == cudaSuccess; i0 += chunk) {
+    const size_t i1 = n - i0 < chunk ? n : i0 + chunk;
+    sufb200::TruncLaunch c = a;
+    c.xhat = a.xhat + i0;
+    c.n = i1 - i0;
+    c.y = d_y + i0;
+    c.bools = d_bools ? d_bools + 3 * i0 : nullptr;
+    e = sufb200::launch_trunc_bundle_prefix(ctx, c, acc, kmax, F, st);
     if (e == cudaSuccess && sink) {
-      if (int rc = enqueue_chunk_copy(*sink, st, d_y, d_bools, 0, n)) {
+      if (int rc = enqueue_chunk_copy(*sink, st, d_y, d_bools, i0, i1)) {
         cudaFreeAsync(scratch, st);
         return rc;
       }
@@ -592,32 +575,56 @@ int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uin
   return SUFB200_OK;
 }
 
-// Both parties' bundles over one x^ on the shared-prefix path: one range
-// pass (x^ is common), one frontier launch over both parties' query keys and
-// one main pass over both parties' elements.
-int trunc_bundle_pair_prefix(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* keys0,
-                             const size_t* key_bytes0, const sufb200_trunc_desc* desc1, const uint8_t* const* keys1,
-                             const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
-                             uint64_t* d_y1, void* stream) {
-  if (!d_xhat || !d_y0 || !d_y1 || !aligned8(d_xhat) || !aligned8(d_y0) || !aligned8(d_y1))
-    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+// Host keys of the given bundles into one pool buffer (one H2D copy); the
+// caller frees *scratch after its launches.
+int upload_bundle_keys(sufb200_ctx ctx, const sufb200_trunc_desc* const* desc, const uint8_t* const* const* keys,
+                       const size_t* const* key_bytes, int nb, sufb200::TruncLaunch* const* a, cudaStream_t st,
+                       uint8_t** scratch) {
+  *scratch = nullptr;
   std::vector<uint8_t> blob;
-  sufb200::TruncLaunch a0{}, a1{};
-  a0.desc = *desc0;
-  a1.desc = *desc1;
-  if (int rc = pack_bundle_keys(*desc0, keys0, key_bytes0, blob, a0.key_off)) return rc;
-  if (int rc = pack_bundle_keys(*desc1, keys1, key_bytes1, blob, a1.key_off)) return rc;
+  uint32_t off[2][4] = {};
+  for (int b = 0; b < nb; b++)
+    if (int rc = pack_bundle_keys(*desc[b], keys[b], key_bytes[b], blob, off[b])) return rc;
+  if (blob.empty()) return SUFB200_OK;
+  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(scratch), blob.size() + 256, ctx->pool, st),
+                     "bundle key staging");
+  SUFB200_CHECK_CUDA(cudaMemcpyAsync(*scratch, blob.data(), blob.size(), cudaMemcpyHostToDevice, st), "bundle keys H2D");
+  for (int b = 0; b < nb; b++)
+    for (int q = 0; q < desc[b]->nq; q++) a[b]->key[q] = *scratch + off[b][q];
+  return SUFB200_OK;
+}
+
+int trunc_bundle_impl(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,
+                      const size_t* key_bytes, const uint64_t* d_xhat, size_t n, uint64_t* d_y, uint64_t* d_bools,
+                      void* stream, const ChunkSink* sink) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (int rc = check_bundle_desc(desc, keys, key_bytes)) return rc;
+  if (n == 0) return SUFB200_OK;
+  if (!d_xhat || !d_y || !aligned8(d_xhat) || !aligned8(d_y) || (d_bools && !aligned8(d_bools)))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
   cudaStream_t st = as_stream(stream);
-  const uint32_t kmax = sufb200::prefix_budget(n);
-  const size_t blob_bytes = (blob.size() + 255) & ~static_cast<size_t>(255);
-  const size_t nqt = static_cast<size_t>(desc0->nq + desc1->nq);
+  sufb200::TruncLaunch a{};
+  a.desc = *desc;
+  a.xhat = d_xhat;
+  a.n = n;
+  a.y = d_y;
+  a.bools = d_bools;
+  sufb200::TruncLaunch* pa[1] = {&a};
   uint8_t* scratch = nullptr;
-  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch),
-                                             blob_bytes + kAccBytes + 32ull * kmax * nqt + 256, ctx->pool, st),
-                     "pair bundle scratch allocation");
-  cudaError_t e = cudaMemcpyAsync(scratch, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
+  int rc = upload_bundle_keys(ctx, &desc, &keys, &key_bytes, 1, pa, st, &scratch);
+  if (rc == SUFB200_OK) rc = single_core(ctx, a, st, sink);
+  if (scratch) cudaFreeAsync(scratch, st);
+  return rc;
+}
+
+// Both parties' bundles over one x^ with their keys on the device: batches
+// below the shared-prefix size in one launch (a lane per party, element and
+// query); larger ones on the shared-prefix path with one range pass (x^ is
+// common), one frontier launch over both parties' query keys and one main
+// pass over both parties' elements; query-free bundles party by party.
+int trunc_pair_core(sufb200_ctx ctx, sufb200::TruncLaunch a0, sufb200::TruncLaunch a1, const uint64_t* d_xhat,
+                    size_t n, uint64_t* d_y0, uint64_t* d_y1, cudaStream_t st) {
   for (sufb200::TruncLaunch* a : {&a0, &a1}) {
-    a->keys = scratch;
     a->xhat = d_xhat;
     a->n = n;
     a->bools = nullptr;
@@ -626,21 +633,35 @@ int trunc_bundle_pair_prefix(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, c
   }
   a0.y = d_y0;
   a1.y = d_y1;
-  auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch + blob_bytes);
+  if (n < prefix_min_n()) {
+    cudaError_t e = sufb200::launch_trunc_bundle_pair(ctx, a0, a1, st);
+    if (e != cudaSuccess) return cuda_fail(e, "pair bundle launch");
+    return SUFB200_OK;
+  }
+  if (a0.desc.nq == 0 || a1.desc.nq == 0) {
+    if (int rc = single_core(ctx, a0, st, nullptr)) return rc;
+    return single_core(ctx, a1, st, nullptr);
+  }
+  const uint32_t kmax = sufb200::prefix_budget(n);
+  const size_t nqt = static_cast<size_t>(a0.desc.nq + a1.desc.nq);
+  uint8_t* scratch = nullptr;
+  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), kAccBytes + 32ull * kmax * nqt + 256,
+                                             ctx->pool, st),
+                     "pair bundle scratch allocation");
+  auto* acc = reinterpret_cast<sufb200::RangeAcc*>(scratch);
   sufb200::FrontierEntry* F[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   sufb200::FrontierBatch fb{};
   fb.nq = static_cast<int>(nqt);
   int k = 0;
   for (int p = 0; p < 2; p++) {
-    const sufb200_trunc_desc* d = p ? desc1 : desc0;
     const sufb200::TruncLaunch& a = p ? a1 : a0;
-    for (int q = 0; q < d->nq; q++, k++) {
-      F[4 * p + q] = reinterpret_cast<sufb200::FrontierEntry*>(scratch + blob_bytes + kAccBytes + 32ull * kmax * k);
-      fb.q[k] = sufb200::FrontierLaunch{scratch + a.key_off[q], d->q_bits[q], 8, acc, kmax, F[4 * p + q],
-                                        ctx->d_t0, ctx->d_status};
+    for (int q = 0; q < a.desc.nq; q++, k++) {
+      F[4 * p + q] = reinterpret_cast<sufb200::FrontierEntry*>(scratch + kAccBytes + 32ull * kmax * k);
+      fb.q[k] = sufb200::FrontierLaunch{a.key[q], a.desc.q_bits[q], 8, acc, kmax, F[4 * p + q], ctx->d_t0,
+                                        ctx->d_status};
     }
   }
-  if (e == cudaSuccess) e = sufb200::launch_range(ctx, d_xhat, n, acc, st);
+  cudaError_t e = sufb200::launch_range(ctx, d_xhat, n, acc, st);
   if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
   if (e == cudaSuccess) e = sufb200::launch_trunc_bundle_prefix_pair(ctx, a0, a1, acc, kmax, F, st);
   cudaFreeAsync(scratch, st);
@@ -659,41 +680,51 @@ int sufb200_trunc_bundle_eval_pair(sufb200_ctx ctx, const sufb200_trunc_desc* de
   if (int rc = check_bundle_desc(desc1, keys1, key_bytes1)) return rc;
   if (desc0->party != 0 || desc1->party != 1) return fail(SUFB200_ERR_INVALID, "desc0 / desc1 must be parties 0 / 1");
   if (n == 0) return SUFB200_OK;
-  if (n >= prefix_min_n() && desc0->nq > 0 && desc1->nq > 0)  // large batches: both bundles, shared-prefix path
-    return trunc_bundle_pair_prefix(ctx, desc0, keys0, key_bytes0, desc1, keys1, key_bytes1, d_xhat, n, d_y0, d_y1,
-                                    stream);
-  if (n >= prefix_min_n()) {  // large batches of query-free bundles: each party on its own
-    if (int rc = trunc_bundle_impl(ctx, desc0, keys0, key_bytes0, d_xhat, n, d_y0, nullptr, stream, nullptr))
-      return rc;
-    return trunc_bundle_impl(ctx, desc1, keys1, key_bytes1, d_xhat, n, d_y1, nullptr, stream, nullptr);
-  }
   if (!d_xhat || !d_y0 || !d_y1 || !aligned8(d_xhat) || !aligned8(d_y0) || !aligned8(d_y1))
     return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
-  std::vector<uint8_t> blob;
+  cudaStream_t st = as_stream(stream);
   sufb200::TruncLaunch a0{}, a1{};
   a0.desc = *desc0;
   a1.desc = *desc1;
-  if (int rc = pack_bundle_keys(*desc0, keys0, key_bytes0, blob, a0.key_off)) return rc;
-  if (int rc = pack_bundle_keys(*desc1, keys1, key_bytes1, blob, a1.key_off)) return rc;
-  cudaStream_t st = as_stream(stream);
+  const sufb200_trunc_desc* descs[2] = {desc0, desc1};
+  const uint8_t* const* keys[2] = {keys0, keys1};
+  const size_t* kbs[2] = {key_bytes0, key_bytes1};
+  sufb200::TruncLaunch* pa[2] = {&a0, &a1};
   uint8_t* scratch = nullptr;
-  SUFB200_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&scratch), blob.size() + 256, ctx->pool, st),
-                     "pair bundle scratch allocation");
-  cudaError_t e = cudaMemcpyAsync(scratch, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
-  for (sufb200::TruncLaunch* a : {&a0, &a1}) {
-    a->keys = scratch;
-    a->xhat = d_xhat;
-    a->n = n;
-    a->bools = nullptr;
-    a->t0 = ctx->d_t0;
-    a->status = ctx->d_status;
+  int rc = upload_bundle_keys(ctx, descs, keys, kbs, 2, pa, st, &scratch);
+  if (rc == SUFB200_OK) rc = trunc_pair_core(ctx, a0, a1, d_xhat, n, d_y0, d_y1, st);
+  if (scratch) cudaFreeAsync(scratch, st);
+  return rc;
+}
+
+int sufb200_trunc_bundle_eval_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0,
+                                       const uint8_t* const* d_keys0, const size_t* key_bytes0,
+                                       const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
+                                       const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
+                                       uint64_t* d_y1, void* stream) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (int rc = check_bundle_desc(desc0, d_keys0, key_bytes0)) return rc;
+  if (int rc = check_bundle_desc(desc1, d_keys1, key_bytes1)) return rc;
+  if (desc0->party != 0 || desc1->party != 1) return fail(SUFB200_ERR_INVALID, "desc0 / desc1 must be parties 0 / 1");
+  sufb200::TruncLaunch a0{}, a1{};
+  a0.desc = *desc0;
+  a1.desc = *desc1;
+  for (int p = 0; p < 2; p++) {
+    const sufb200_trunc_desc* d = p ? desc1 : desc0;
+    const uint8_t* const* dk = p ? d_keys1 : d_keys0;
+    const size_t* kb = p ? key_bytes1 : key_bytes0;
+    for (int q = 0; q < d->nq; q++) {
+      const int nb = d->q_bits[q];
+      if (nb < 1 || nb > 64) return fail(SUFB200_ERR_INVALID, "query in_bits out of range");
+      if (!dk[q] || kb[q] != sufb200::host::myl7_key_bytes(nb, 8))
+        return fail(SUFB200_ERR_KEY, "query " + std::to_string(q) + ": key size does not match an 8-byte myl7 key");
+      (p ? a1 : a0).key[q] = dk[q];
+    }
   }
-  a0.y = d_y0;
-  a1.y = d_y1;
-  if (e == cudaSuccess) e = sufb200::launch_trunc_bundle_pair(ctx, a0, a1, st);
-  cudaFreeAsync(scratch, st);
-  if (e != cudaSuccess) return cuda_fail(e, "pair bundle launch");
-  return SUFB200_OK;
+  if (n == 0) return SUFB200_OK;
+  if (!d_xhat || !d_y0 || !d_y1 || !aligned8(d_xhat) || !aligned8(d_y0) || !aligned8(d_y1))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  return trunc_pair_core(ctx, a0, a1, d_xhat, n, d_y0, d_y1, as_stream(stream));
 }
 
 int sufb200_trunc_bundle_eval_jobs(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,

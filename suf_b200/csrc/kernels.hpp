@@ -30,8 +30,7 @@ cudaError_t launch_myl7_eval(const sufb200_ctx_s* ctx, int group, const DcfLaunc
 // Fused truncation bundle (trunc_bundle.cu).
 struct TruncLaunch {
   sufb200_trunc_desc desc;
-  const uint8_t* keys;       // device: concatenated per-query broadcast keys
-  uint32_t key_off[4];       // byte offset of query q's key inside `keys`
+  const uint8_t* key[4];     // device: query q's broadcast myl7 key (any alignment)
   const uint64_t* xhat;      // device [n]
   size_t n;
   uint64_t* y;               // device [n]

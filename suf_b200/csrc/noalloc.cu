@@ -88,7 +88,7 @@ extern "C" int sufb200_trunc_bundle_eval_noalloc(sufb200_ctx ctx, const sufb200_
   // rejected before anything is written to the shared array.
   sufb200::TruncLaunch a{};
   a.desc = *desc;
-  size_t total = 0;
+  size_t total = 0, off[4] = {0, 0, 0, 0};
   for (int q = 0; q < desc->nq; q++) {
     const int nb = desc->q_bits[q];
     if (nb < 1 || nb > 64) return noalloc_fail(SUFB200_ERR_INVALID, "query in_bits out of range");
@@ -99,7 +99,7 @@ extern "C" int sufb200_trunc_bundle_eval_noalloc(sufb200_ctx ctx, const sufb200_
     std::memcpy(&pl, k + 4, 4);
     if (k[0] != nb || k[1] != 1 || k[2] != desc->party || pl != 8)
       return noalloc_fail(SUFB200_ERR_KEY, "key header does not match the bundle");
-    a.key_off[q] = static_cast<uint32_t>(total);
+    off[q] = total;
     total += (key_bytes[q] + 15) & ~static_cast<size_t>(15);
   }
   if (total > SUFB200_NOALLOC_KEY_BYTES)
@@ -118,12 +118,12 @@ extern "C" int sufb200_trunc_bundle_eval_noalloc(sufb200_ctx ctx, const sufb200_
   // the array has to start at zero; bytes of an earlier call that are not
   // overwritten (padding, space past this bundle) are never read.
   for (int q = 0; q < desc->nq; q++) {
-    e = cudaMemcpyAsync(base + a.key_off[q], keys[q], key_bytes[q], cudaMemcpyHostToDevice, st);
+    e = cudaMemcpyAsync(base + off[q], keys[q], key_bytes[q], cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess)
       return noalloc_fail(SUFB200_ERR_CUDA,
                           std::string("copy of the bundle keys into the staging array: ") + cudaGetErrorString(e));
   }
-  a.keys = base;
+  for (int q = 0; q < desc->nq; q++) a.key[q] = base + off[q];
   a.xhat = d_xhat;
   a.n = n;
   a.y = d_y;

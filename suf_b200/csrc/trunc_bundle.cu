@@ -89,7 +89,7 @@ __device__ __forceinline__ void combine_store(const sufb200_trunc_desc& d, uint6
 __device__ __forceinline__ void stage_keys(QueryKeySmem* ks, const TruncLaunch& a) {
   const sufb200_trunc_desc& d = a.desc;
   for (int q = 0; q < d.nq; q++) {
-    const uint8_t* k = a.keys + a.key_off[q];
+    const uint8_t* k = a.key[q];
     const int nb = d.q_bits[q];
     for (int i = threadIdx.x; i < nb; i += blockDim.x) {
       const uint8_t* c = k + 24 + 33 * i;

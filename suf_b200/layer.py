@@ -100,24 +100,26 @@ class _Trunc:
     """One GapARS truncation bundle for both parties: descriptors, myl7 keys
     (host) and the split of its input mask r_in = r[0] + r[1]."""
 
-    def __init__(self, ctx: Context, rng, frac_bits: int):
+    def __init__(self, ctx: Context, rng, frac_bits: int, dev=None):
+        import torch
+
         r_in, d0, d1, thetas = Context.trunc_gen(TRUNC_GAPARS, frac_bits, int(rng.integers(1, 2**63)))
         r0 = _rand64(rng)
         self.r = (r0, (r_in - r0) & M64)
         self.desc = (d0, d1)
-        self.keys = ([], [])
+        self.keys = ([], [])  # device copies: the bundle's keys stay resident
         for q in range(int(d0.nq)):
             s0 = rng.integers(0, 256, 16, dtype=np.uint8)
             s1 = rng.integers(0, 256, 16, dtype=np.uint8)
             k0, k1 = ctx.myl7_gen(GROUP_ADD, int(d0.q_bits[q]), int(thetas[q]), (1).to_bytes(8, "little"), s0, s1)
-            self.keys[0].append(k0)
-            self.keys[1].append(k1)
+            self.keys[0].append(torch.from_numpy(k0).to(dev))
+            self.keys[1].append(torch.from_numpy(k1).to(dev))
         nq = int(d0.nq)
-        self.kptr = [(C.c_void_p * 4)(*[k.ctypes.data for k in ks], *([None] * (4 - nq))) for ks in self.keys]
-        self.ksz = [(C.c_size_t * 4)(*[k.size for k in ks], *([0] * (4 - nq))) for ks in self.keys]
+        self.kptr = [(C.c_void_p * 4)(*[k.data_ptr() for k in ks], *([None] * (4 - nq))) for ks in self.keys]
+        self.ksz = [(C.c_size_t * 4)(*[k.numel() for k in ks], *([0] * (4 - nq))) for ks in self.keys]
 
     def eval_pair(self, ctx: Context, d_xhat, d_y0, d_y1, stream):
-        check(_lib.lib().sufb200_trunc_bundle_eval_pair(
+        check(_lib.lib().sufb200_trunc_bundle_eval_pair_dev(
             ctx.h, C.byref(self.desc[0]), C.cast(self.kptr[0], C.c_void_p), C.cast(self.ksz[0], C.c_void_p),
             C.byref(self.desc[1]), C.cast(self.kptr[1], C.c_void_p), C.cast(self.ksz[1], C.c_void_p), _t_ptr(d_xhat),
             d_xhat.numel(), _t_ptr(d_y0), _t_ptr(d_y1), _stream_ptr(stream)))
@@ -212,8 +214,8 @@ class TransformerLayerPair:
         self.ln1 = LayerNormBlock(ctx, S, D, seed=int(rng.integers(1, 2**62)), tables=sm_tab)
         self.ln2 = LayerNormBlock(ctx, S, D, seed=int(rng.integers(1, 2**62)), tables=sm_tab)
         self.softmax = SoftmaxBlock(ctx, [S] * (H * S), seed=int(rng.integers(1, 2**62)), tables=sm_tab)
-        self.tr = {name: _Trunc(ctx, rng, fk) for name, fk in (("qkv", f), ("scores", f + 3), ("pv", f), ("o", f),
-                                                                ("ff1", f), ("ff2", f))}
+        self.tr = {name: _Trunc(ctx, rng, fk, dev) for name, fk in (("qkv", f), ("scores", f + 3), ("pv", f),
+                                                                     ("o", f), ("ff1", f), ("ff2", f))}
         self.trip_s = _Triples(rng, dev, H, S, Dh, S, transposed=True)
         self.trip_pv = _Triples(rng, dev, H, S, S, Dh, transposed=False)
         self.rounds = S.bit_length() - 1
@@ -367,6 +369,37 @@ class TransformerLayerPair:
         check(L.sufb200_add_pair(_t_ptr(b["x2"][0]), _t_ptr(b["a"][0]), _t_ptr(b["x2"][1]), _t_ptr(b["a"][1]),
                                  _t_ptr(d_y0), _t_ptr(d_y1), S * D, _stream_ptr(stream)))
         return d_y0, d_y1
+
+    def capture(self, d_x0, d_x1, d_y0, d_y1, layers: int = 1):
+        """A CUDA graph of `layers` runs of this layer, each layer's output
+        shares feeding the next and the last one's written to d_y0 / d_y1;
+        replay() reads d_x0 / d_x1 as they are at replay time and launches
+        the whole sequence (about 150 kernels a layer) with no host work.
+        Everything the calls use stays resident on the device (keys, triples,
+        tables); the scratch the calls allocate becomes graph memory."""
+        import torch
+
+        d = self.dims
+        tmp = [(torch.empty(d.S * d.D, dtype=torch.int64, device=self.dev),
+                torch.empty(d.S * d.D, dtype=torch.int64, device=self.dev)) for _ in range(2 if layers > 1 else 0)]
+
+        def chain(stream):
+            a, b = d_x0, d_x1
+            for i in range(layers):
+                o = (d_y0, d_y1) if i == layers - 1 else tmp[i % 2]
+                self.run(a, b, o[0], o[1], stream=stream)
+                a, b = o
+
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        chain(s)  # warm-up outside the capture: lazily made streams, events and pool memory
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.ctx.sync(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s, capture_error_mode="relaxed"):
+            chain(s)
+        g._sufb200_keep = tmp  # the graph's intermediate buffers live as long as it does
+        return g
 
     # launches of our kernels per layer (counted from the calls above; the
     # truncations take the shared-prefix path: range, frontier and main

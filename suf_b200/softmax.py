@@ -48,6 +48,7 @@ class SoftmaxParty(C.Structure):
         ("trunc_rin", C.c_uint64 * N_TRUNCS),
         ("trunc_keys", (C.c_void_p * 4) * N_TRUNCS),
         ("trunc_key_bytes", (C.c_size_t * 4) * N_TRUNCS),
+        ("trunc_keys_device", C.c_int32),
     ]
 
 
@@ -178,10 +179,11 @@ class SoftmaxBlock:
                 s0 = rng.integers(0, 256, 16, dtype=np.uint8)
                 s1 = rng.integers(0, 256, 16, dtype=np.uint8)
                 k0, k1 = ctx.myl7_gen(GROUP_ADD, int(d0.q_bits[q]), int(thetas[q]), payload1, s0, s1)
-                for p, key in ((0, k0), (1, k1)):
-                    self._keep.append(key)
-                    parts[p].trunc_keys[k][q] = key.ctypes.data
+                for p, key in ((0, k0), (1, k1)):  # resident on the device, like the rest of the material
+                    parts[p].trunc_keys[k][q] = dcopy(key).data_ptr()
                     parts[p].trunc_key_bytes[k][q] = key.size
+        for p in (0, 1):
+            parts[p].trunc_keys_device = 1
         self.parts = parts
 
     def run(self, d_t0, d_t1, d_prob0=None, d_prob1=None, stream=None):
@@ -224,6 +226,7 @@ class LayerNormParty(C.Structure):
         ("trunc_rin", C.c_uint64 * N_LN_TRUNCS),
         ("trunc_keys", (C.c_void_p * 4) * N_LN_TRUNCS),
         ("trunc_key_bytes", (C.c_size_t * 4) * N_LN_TRUNCS),
+        ("trunc_keys_device", C.c_int32),
     ]
 
 
@@ -292,10 +295,11 @@ class LayerNormBlock:
                 s0 = rng.integers(0, 256, 16, dtype=np.uint8)
                 s1 = rng.integers(0, 256, 16, dtype=np.uint8)
                 k0, k1 = ctx.myl7_gen(GROUP_ADD, int(d0.q_bits[q]), int(thetas[q]), payload1, s0, s1)
-                for p, key in ((0, k0), (1, k1)):
-                    self._keep.append(key)
-                    parts[p].trunc_keys[k][q] = key.ctypes.data
+                for p, key in ((0, k0), (1, k1)):  # resident on the device, like the rest of the material
+                    parts[p].trunc_keys[k][q] = dcopy(key).data_ptr()
                     parts[p].trunc_key_bytes[k][q] = key.size
+        for p in (0, 1):
+            parts[p].trunc_keys_device = 1
         self.parts = parts
 
     def run(self, d_x0, d_x1, d_out0=None, d_out1=None, stream=None):
