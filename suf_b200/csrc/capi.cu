@@ -18,6 +18,18 @@
 #include "primitives.hpp"
 #include "sufb200_internal.cuh"
 
+namespace sufb200 {
+
+bool pdl_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("SUFB200_PDL");
+    return !(e && std::string(e) == "0");
+  }();
+  return v;
+}
+
+}  // namespace sufb200
+
 namespace {
 
 thread_local std::string g_err;

@@ -5,12 +5,33 @@
 #include <cstddef>
 #include <cstdint>
 #include <string>
+#include <utility>
 
 #include <cuda_runtime.h>
 
 #include "sufb200_internal.cuh"
 
 namespace sufb200 {
+
+// Programmatic dependent launch of kernel k (see pdl_wait in
+// sufb200_internal.cuh): the attribute is set unless SUFB200_PDL=0 in the
+// environment.  Every kernel launched this way calls pdl_wait() before it
+// reads anything an earlier kernel of the stream may still be writing.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
 
 struct DcfLaunch {
   const uint8_t* keys;  // device: [n][key_bytes] or one key (broadcast)

@@ -48,12 +48,14 @@ int grid_for(size_t n) {
 
 __global__ void open_masked_pair_kernel(const uint64_t* __restrict__ a0, const uint64_t* __restrict__ a1, uint64_t r0,
                                         uint64_t r1, uint64_t* __restrict__ xhat, size_t n) {
+  sufb200::pdl_trigger();  // a following programmatic launch may start its set-up
   LAYER_GRID_LOOP(i, n) xhat[i] = (a0[i] + r0) + (a1[i] + r1);
 }
 
 __global__ void add_pair_kernel(const uint64_t* __restrict__ a0, const uint64_t* __restrict__ b0,
                                 const uint64_t* __restrict__ a1, const uint64_t* __restrict__ b1,
                                 uint64_t* __restrict__ o0, uint64_t* __restrict__ o1, size_t n) {
+  sufb200::pdl_trigger();  // a following programmatic launch may start its set-up
   LAYER_GRID_LOOP(i, n) {
     o0[i] = a0[i] + b0[i];
     o1[i] = a1[i] + b1[i];
@@ -64,6 +66,7 @@ __global__ void add_pair_kernel(const uint64_t* __restrict__ a0, const uint64_t*
 // (c_p[r][2j] - c_p[r][2j+1] + r_p).
 __global__ void relu_open_pair_kernel(const uint64_t* __restrict__ c0, const uint64_t* __restrict__ c1, int rows,
                                       int w, uint64_t r0, uint64_t r1, uint64_t* __restrict__ xhat) {
+  sufb200::pdl_trigger();  // a following programmatic launch may start its set-up
   const size_t half = static_cast<size_t>(w / 2), n = static_cast<size_t>(rows) * half;
   LAYER_GRID_LOOP(i, n) {
     const size_t r = i / half, j = i % half, at = r * w + 2 * j;
@@ -75,6 +78,7 @@ __global__ void relu_open_pair_kernel(const uint64_t* __restrict__ c0, const uin
 __global__ void relu_update_pair_kernel(const uint64_t* __restrict__ c0, const uint64_t* __restrict__ c1,
                                         const uint64_t* __restrict__ relu0, const uint64_t* __restrict__ relu1,
                                         int rows, int w, uint64_t* __restrict__ n0, uint64_t* __restrict__ n1) {
+  sufb200::pdl_trigger();  // a following programmatic launch may start its set-up
   const size_t half = static_cast<size_t>(w / 2), n = static_cast<size_t>(rows) * half;
   LAYER_GRID_LOOP(i, n) {
     const size_t r = i / half, j = i % half, at = r * w + 2 * j + 1;
@@ -86,6 +90,7 @@ __global__ void relu_update_pair_kernel(const uint64_t* __restrict__ c0, const u
 __global__ void maxdiff_pair_kernel(const uint64_t* __restrict__ m0, const uint64_t* __restrict__ m1,
                                     const uint64_t* __restrict__ x0, const uint64_t* __restrict__ x1, int rows,
                                     int cols, uint64_t* __restrict__ t0, uint64_t* __restrict__ t1) {
+  sufb200::pdl_trigger();  // a following programmatic launch may start its set-up
   const size_t n = static_cast<size_t>(rows) * cols;
   LAYER_GRID_LOOP(i, n) {
     const size_t r = i / cols;
@@ -111,6 +116,7 @@ struct BeaverPairArgs {
 // E = Y - B are formed while staging.  Sums mod 2^64 are order-free.
 template <bool TRANS>
 __global__ void __launch_bounds__(256) beaver_open_pair_kernel(const BeaverPairArgs p) {
+  sufb200::pdl_trigger();  // a following programmatic launch may start its set-up
   __shared__ uint64_t sD[kMT][kKT + 1], sA0[kMT][kKT + 1], sA1[kMT][kKT + 1];
   __shared__ uint64_t sE[kKT][kMT + 1], sB0[kKT][kMT + 1], sB1[kKT][kMT + 1];
   const int h = blockIdx.z;

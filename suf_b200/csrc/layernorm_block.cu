@@ -67,6 +67,7 @@ __device__ __forceinline__ void block_sum2(uint64_t& a, uint64_t& b) {
 // Row sums times invL, opened with the mean truncation's mask.  One block per row.
 __global__ void ln_mean_open_kernel(const uint64_t* __restrict__ x0, const uint64_t* __restrict__ x1, int cols,
                                     uint64_t inv_len, uint64_t rM, uint64_t* __restrict__ xhat) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   const size_t base = static_cast<size_t>(blockIdx.x) * cols;
   uint64_t a = 0, b = 0;
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
@@ -84,6 +85,7 @@ __global__ void ln_var_open_kernel(const uint64_t* __restrict__ x0, const uint64
                                    const uint64_t* __restrict__ tr0, const uint64_t* __restrict__ tr1,
                                    uint64_t inv_len, uint64_t rV, uint64_t* __restrict__ d0,
                                    uint64_t* __restrict__ d1, uint64_t* __restrict__ xhat) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   const int r = blockIdx.x;
   const size_t base = static_cast<size_t>(r) * cols;
   const uint64_t m0 = mu0[r], m1 = mu1[r];
@@ -104,6 +106,7 @@ __global__ void ln_var_open_kernel(const uint64_t* __restrict__ x0, const uint64
 // v += eps (party 0), opened with the rsqrt LUT gate's mask.
 __global__ void ln_rsqrt_open_kernel(uint64_t* __restrict__ v0, const uint64_t* __restrict__ v1, uint64_t eps,
                                      uint64_t rR, uint64_t* __restrict__ xhat, int rows) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
     const uint64_t a = v0[r] + eps;
     v0[r] = a;
@@ -119,6 +122,7 @@ __global__ void ln_row_stage_kernel(int stage, const uint64_t* __restrict__ in0,
                                     uint64_t* __restrict__ y0, uint64_t* __restrict__ y1,
                                     const uint64_t* __restrict__ tr0, const uint64_t* __restrict__ tr1, int f,
                                     uint64_t rmask, uint64_t* __restrict__ xhat, int rows) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
     const uint64_t* t0 = tr0 + 3 * (static_cast<size_t>(stage < 3 ? stage : 3) * rows + r);
     const uint64_t* t1 = tr1 + 3 * (static_cast<size_t>(stage < 3 ? stage : 3) * rows + r);
@@ -149,6 +153,7 @@ __global__ void ln_norm_kernel(const uint64_t* __restrict__ d0, const uint64_t* 
                                const uint64_t* __restrict__ B0, const uint64_t* __restrict__ B1,
                                const uint64_t* __restrict__ C0, const uint64_t* __restrict__ C1, int cols,
                                uint64_t rN, uint64_t* __restrict__ xhat) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   const int r = blockIdx.x;
   const size_t base = static_cast<size_t>(r) * cols;
   const uint64_t b0 = B0[r], b1 = B1[r];

@@ -28,6 +28,8 @@ __device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
 // Signed offsets from the pivot xs[0], biased by flipping the sign bit so
 // unsigned order is signed order; one atomic pair per warp.
 __global__ void range_kernel(const uint64_t* __restrict__ xs, size_t n, RangeAcc* acc) {
+  pdl_wait();
+  pdl_trigger();
   const uint64_t pivot = xs[0];
   uint64_t mn = ~0ull, mx = 0ull;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
@@ -109,6 +111,7 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
     if (threadIdx.x == 0) atomicOr(b.q[0].status, kStatusSmemLayout);
+    pdl_wait();
     return;
   }
   const int nq = b.nq;
@@ -117,10 +120,12 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
   FrontierKey* fk = fs->fk;
   int* order = fs->order;
   uint64_t* first_item = fs->first_item;
+  aes_fill_tables(b.q[0].t0);
+  pdl_wait();  // the plans read the range pass's result
+  pdl_trigger();
 #pragma unroll
   for (int q = 0; q < kFrontierMaxKeys; q++)
     if (q < nq) stage_bcast_key(&ks[q], b.q[q].key, b.q[q].in_bits, b.q[q].out_bytes);
-  aes_fill_tables(b.q[0].t0);
   if (threadIdx.x == 0) {
     uint64_t cost[kFrontierMaxKeys];
 #pragma unroll
@@ -292,8 +297,7 @@ cudaError_t launch_range(const sufb200_ctx_s* ctx, const uint64_t* xs, size_t n,
   if (e != cudaSuccess) return e;
   const size_t want = (n + 255) / 256;
   const size_t cap = static_cast<size_t>(ctx->sm_count) * 4;
-  range_kernel<<<static_cast<int>(want < cap ? (want ? want : 1) : cap), 256, 0, st>>>(xs, n, acc);
-  return cudaGetLastError();
+  return launch_pdl(range_kernel, static_cast<int>(want < cap ? (want ? want : 1) : cap), 256, 0, st, xs, n, acc);
 }
 
 cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st) {
@@ -304,12 +308,10 @@ cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierB
   cudaError_t e;
   if (group == SUFB200_GROUP_ADD) {
     if ((e = set_smem(frontier_kernel<SUFB200_GROUP_ADD>, ctx)) != cudaSuccess) return e;
-    frontier_kernel<SUFB200_GROUP_ADD><<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, b);
-  } else {
-    if ((e = set_smem(frontier_kernel<SUFB200_GROUP_XOR>, ctx)) != cudaSuccess) return e;
-    frontier_kernel<SUFB200_GROUP_XOR><<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, b);
+    return launch_pdl(frontier_kernel<SUFB200_GROUP_ADD>, grid, kAesThreads, ctx->aes_dyn_bytes, st, ctx->prg, b);
   }
-  return cudaGetLastError();
+  if ((e = set_smem(frontier_kernel<SUFB200_GROUP_XOR>, ctx)) != cudaSuccess) return e;
+  return launch_pdl(frontier_kernel<SUFB200_GROUP_XOR>, grid, kAesThreads, ctx->aes_dyn_bytes, st, ctx->prg, b);
 }
 
 cudaError_t launch_myl7_bcast_prefix(const sufb200_ctx_s* ctx, int group, const DcfLaunch& a, const RangeAcc* acc,

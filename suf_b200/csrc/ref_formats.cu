@@ -226,15 +226,18 @@ __global__ void __launch_bounds__(kAesThreads, 1) interval_lut_pair_kernel(const
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
     if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
+    pdl_wait();
     return;
   }
   uint32_t* s_rk0 = reinterpret_cast<uint32_t*>(smem);
   uint32_t* s_rk1 = reinterpret_cast<uint32_t*>(smem + 256);
   uint64_t* s_tab0 = reinterpret_cast<uint64_t*>(smem + 512);
   uint64_t* s_tab1 = reinterpret_cast<uint64_t*>(smem + 512 + kStageBytes / 2);
+  aes_fill_tables(a0.t0);
+  pdl_wait();
+  pdl_trigger();
   const bool tab0 = stage_lut_key(a0, s_rk0, s_tab0, kStageBytes / 2);
   const bool tab1 = stage_lut_key(a1, s_rk1, s_tab1, kStageBytes / 2);
-  aes_fill_tables(a0.t0);
   __syncthreads();
   const uint32_t lb = lane_base();
   const size_t n = a0.n;
@@ -319,6 +322,7 @@ __device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const Coe
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
     if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
+    pdl_wait();
     return;
   }
   const size_t n = a0.n, total = NP * n;
@@ -326,13 +330,19 @@ __device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const Coe
   const uint32_t lane = threadIdx.x & 31u;
   const size_t step = static_cast<size_t>(gridDim.x) * (blockDim.x >> 5) * 32;
   const size_t first = ((static_cast<size_t>(threadIdx.x >> 5) * gridDim.x + blockIdx.x) << 5) + lane;
-  uint64_t xh_next = first < total ? __ldg(xs + (first < n ? first : first - n)) : 0ull;  // before the table fill
+  aes_fill_tables(a0.t0);
+  pdl_wait();  // x^ may come from the previous kernel
+  pdl_trigger();
+  // Items in flight per lane: the current one (x^ and interval known), the
+  // next (x^ loaded a step ago; its interval is searched while the current
+  // one's AES runs) and the one after (x^ load issued).
+  const auto xload = [&](size_t g) { return g < total ? __ldg(xs + (g < n ? g : g - n)) : 0ull; };
+  uint64_t xh_cur = xload(first), xh_next = xload(first + step);
   uint32_t* s_rk = reinterpret_cast<uint32_t*>(smem);                 // [NP][44]
   CoeffSide* s_side = reinterpret_cast<CoeffSide*>(smem + 512);       // [NP]
   uint64_t* s_tab = reinterpret_cast<uint64_t*>(smem + 1024);         // [NP][kStageBytes / NP]
   stage_coeff_side(a0, p0, s_rk, s_tab, kStageBytes / NP, &s_side[0]);
   if (NP == 2) stage_coeff_side(a1, p1, s_rk + 44, s_tab + kStageBytes / 16, kStageBytes / 2, &s_side[1]);
-  aes_fill_tables(a0.t0);
   __syncthreads();
   if (threadIdx.x == 0 && blockIdx.x == 0)
     for (int q = 0; q < NP; q++)
@@ -340,10 +350,21 @@ __device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const Coe
   const uint32_t lb = lane_base();
   uint32_t rk[44];
   int cur = -1;
+  // The interval of item g's x^ (0 for an item past the end or a side whose key failed its checks).
+  const auto search = [&](size_t g, uint64_t xh) {
+    if (g >= total) return 0;
+    const CoeffSide& S = s_side[(NP == 2 && g >= n) ? 1 : 0];
+    return S.ok ? coeff_interval(S, xh) : 0;
+  };
+  int iv_cur = search(first, xh_cur);
   for (size_t g = first; g < total; g += step) {
-    const uint64_t xh = xh_next;
+    const uint64_t xh = xh_cur;
+    const int iv = iv_cur;
     const size_t gn = g + step;
-    xh_next = gn < total ? __ldg(xs + (gn < n ? gn : gn - n)) : 0ull;
+    const uint64_t xh_after = xload(gn + step);
+    iv_cur = search(gn, xh_next);
+    xh_cur = xh_next;
+    xh_next = xh_after;
     const int q = (NP == 2 && g >= n) ? 1 : 0;
     const size_t i = q ? g - n : g;
     const CoeffSide& S = s_side[q];
@@ -353,7 +374,6 @@ __device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const Coe
       for (int j = 0; j < r; j++) out[j] = 0;
       continue;
     }
-    const int iv = coeff_interval(S, xh);
     const uint64_t base = S.nonce ^ ((S.idx_base + i) << 32);
     const uint64_t w0 = static_cast<uint64_t>(iv) * static_cast<uint64_t>(S.ow);
     const uint64_t* row = S.pay + static_cast<size_t>(iv) * S.ow;
@@ -472,8 +492,7 @@ cudaError_t launch_interval_lut_pair(const sufb200_ctx_s* ctx, const RefFmtLaunc
   threads = threads < 128 ? 128 : (threads > static_cast<size_t>(kAesThreads) ? kAesThreads : threads);
   const size_t want = (units + threads - 1) / threads;
   const int grid = static_cast<int>(want < sms ? (want ? want : 1) : sms);
-  interval_lut_pair_kernel<<<grid, static_cast<unsigned>(threads), ctx->aes_dyn_bytes, st>>>(a0, a1);
-  return cudaGetLastError();
+  return launch_pdl(interval_lut_pair_kernel, grid, static_cast<unsigned>(threads), ctx->aes_dyn_bytes, st, a0, a1);
 }
 
 int interval_lut_pair_eval(const sufb200_ctx_s* ctx, const uint8_t* key0, size_t key_bytes0, const uint8_t* key1,
@@ -498,8 +517,7 @@ cudaError_t launch_coeff_lut(const sufb200_ctx_s* ctx, const RefFmtLaunch& a, co
   cudaError_t e = cudaFuncSetAttribute(coeff_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(ctx->aes_dyn_bytes));
   if (e != cudaSuccess) return e;
-  coeff_lut_kernel<<<grid_for(ctx, a.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st>>>(a, p);
-  return cudaGetLastError();
+  return launch_pdl(coeff_lut_kernel, grid_for(ctx, a.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st, a, p);
 }
 
 cudaError_t launch_coeff_lut_pair(const sufb200_ctx_s* ctx, const RefFmtLaunch& a0, const CoeffLutParams& p0,
@@ -508,9 +526,8 @@ cudaError_t launch_coeff_lut_pair(const sufb200_ctx_s* ctx, const RefFmtLaunch& 
   cudaError_t e = cudaFuncSetAttribute(coeff_lut_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(ctx->aes_dyn_bytes));
   if (e != cudaSuccess) return e;
-  coeff_lut_pair_kernel<<<grid_for(ctx, 2 * a0.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes, st>>>(a0, p0, a1,
-                                                                                                         p1);
-  return cudaGetLastError();
+  return launch_pdl(coeff_lut_pair_kernel, grid_for(ctx, 2 * a0.n, kAesThreads, 1), kAesThreads, ctx->aes_dyn_bytes,
+                    st, a0, p0, a1, p1);
 }
 
 }  // namespace sufb200

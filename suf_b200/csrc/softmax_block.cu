@@ -51,6 +51,7 @@ __device__ __forceinline__ Prod beaver(uint64_t x0, uint64_t x1, uint64_t y0, ui
 // x^ = t0 + t1 + r (the open of the nExp input, masked by its r_in).
 __global__ void open_masked_kernel(const uint64_t* __restrict__ a0, const uint64_t* __restrict__ a1, uint64_t r,
                                    uint64_t* __restrict__ out, size_t n) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
     out[i] = a0[i] + a1[i] + r;
@@ -61,6 +62,7 @@ __global__ void nexp_mul12_kernel(const uint64_t* __restrict__ c0, const uint64_
                                   const uint64_t* __restrict__ t0, const uint64_t* __restrict__ t1,
                                   const uint64_t* __restrict__ tr0, const uint64_t* __restrict__ tr1, int f,
                                   uint64_t rA, uint64_t* __restrict__ xhat, size_t n) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const uint64_t x0 = t0[i], x1 = t1[i];
@@ -77,6 +79,7 @@ __global__ void nexp_mul3_kernel(const uint64_t* __restrict__ c0, const uint64_t
                                  const uint64_t* __restrict__ t0, const uint64_t* __restrict__ t1,
                                  const uint64_t* __restrict__ tr0, const uint64_t* __restrict__ tr1, int f,
                                  uint64_t rB, uint64_t* __restrict__ xhat, size_t n) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const uint64_t q0 = p20[i] + (c0[4 * i + 1] << f), q1 = p21[i] + (c1[4 * i + 1] << f);
@@ -92,6 +95,7 @@ __global__ void rowsum_open_kernel(const uint64_t* __restrict__ y0, const uint64
                                    const int32_t* __restrict__ row_off, uint64_t rR, uint64_t* __restrict__ e0,
                                    uint64_t* __restrict__ e1, uint64_t* __restrict__ s0, uint64_t* __restrict__ s1,
                                    uint64_t* __restrict__ shat) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   __shared__ uint64_t red[2][kRowThreads / 32];
   const int r = blockIdx.x;
   const int beg = row_off[r], end = row_off[r + 1];
@@ -130,6 +134,7 @@ __global__ void recip_init_kernel(const uint64_t* __restrict__ a0, const uint64_
                                   const uint64_t* __restrict__ s0, const uint64_t* __restrict__ s1,
                                   const uint64_t* __restrict__ tr0, const uint64_t* __restrict__ tr1, uint64_t rC,
                                   uint64_t* __restrict__ xhat, int rows) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
     const Prod z = beaver(a0[4 * r + 1], a1[4 * r + 1], s0[r], s1[r], tr0 + 3 * r, tr1 + 3 * r);
     xhat[r] = z.z0 + z.z1 + rC;
@@ -143,6 +148,7 @@ __global__ void recip_nr1_kernel(const uint64_t* __restrict__ z0, const uint64_t
                                  const uint64_t* __restrict__ tr0, const uint64_t* __restrict__ tr1, uint64_t rD,
                                  uint64_t* __restrict__ y0, uint64_t* __restrict__ y1, uint64_t* __restrict__ xhat,
                                  int rows) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
     const uint64_t v0 = z0[r] + a0[4 * r], v1 = z1[r] + a1[4 * r];
     y0[r] = v0;
@@ -157,6 +163,7 @@ __global__ void recip_nr2_kernel(const uint64_t* __restrict__ y0, const uint64_t
                                  const uint64_t* __restrict__ g0, const uint64_t* __restrict__ g1, int f,
                                  const uint64_t* __restrict__ tr0, const uint64_t* __restrict__ tr1, uint64_t rE,
                                  uint64_t* __restrict__ xhat, int rows) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
     const uint64_t d0 = (uint64_t{2} << f) - g0[r], d1 = 0ull - g1[r];
     const Prod v = beaver(y0[r], y1[r], d0, d1, tr0 + 3 * (2 * rows + r), tr1 + 3 * (2 * rows + r));
@@ -172,6 +179,7 @@ __global__ void row_bcast_kernel(const uint64_t* __restrict__ e0, const uint64_t
                                  const uint64_t* __restrict__ B0, const uint64_t* __restrict__ B1,
                                  const uint64_t* __restrict__ C0, const uint64_t* __restrict__ C1,
                                  const int32_t* __restrict__ row_off, uint64_t rF, uint64_t* __restrict__ xhat) {
+  pdl_trigger();  // a following programmatic launch may start its set-up
   const int r = blockIdx.x;
   const int beg = row_off[r], end = row_off[r + 1];
   const uint64_t b0 = B0[r], b1 = B1[r];

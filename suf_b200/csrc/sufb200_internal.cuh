@@ -81,6 +81,28 @@ SUFB200_HD uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 #endif
 }
 
+// Programmatic dependent launch.  A kernel launched with the
+// programmatic-stream-serialization attribute (launch_pdl) may be scheduled
+// while the kernel before it in the stream is still running: pdl_wait()
+// blocks until that kernel has completed and its writes are visible (a no-op
+// when the kernel was launched without the attribute), so code before it may
+// read only constant or resident data (the AES tables' source, resident keys)
+// and write only shared memory.  pdl_trigger() lets the next such kernel in
+// the stream be scheduled onto SMs as this one's CTAs finish: its table fill
+// and set-up then overlap this kernel's last wave.
+#if defined(__CUDACC__)
+__device__ __forceinline__ void pdl_wait() {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 900)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+__device__ __forceinline__ void pdl_trigger() {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 900)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
+#endif
+
 }  // namespace sufb200
 
 // Host-side context (definition shared by the .cu translation units).

@@ -52,6 +52,9 @@ struct TapeFields {
   uint8_t bit_order;
 };
 
+// Called with host lambdas by the host writer and device lambdas by the
+// kernel; the execution-space check does not apply to either instantiation.
+#pragma nv_exec_check_disable
 template <typename Put, typename Keys>
 SUFB200_HD void emit_tape(const TapeFields& t, int nq, const size_t* key_bytes, const Put& put, const Keys& keys) {
   put(t.r_in_share, 8);

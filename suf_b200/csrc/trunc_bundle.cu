@@ -122,8 +122,10 @@ __device__ __forceinline__ bool keys_ok(const QueryKeySmem* ks, const TruncLaunc
 // Stage every query key of the bundle into shared memory, fill the AES
 // tables; false (status flagged) when a key header does not match.
 __device__ __forceinline__ bool stage_bundle(QueryKeySmem* ks, const TruncLaunch& a) {
-  stage_keys(ks, a);
   aes_fill_tables(a.t0);
+  pdl_wait();  // the tables overlap the previous kernel's tail; its outputs are read below
+  pdl_trigger();
+  stage_keys(ks, a);
   __syncthreads();
   return keys_ok(ks, a);
 }
@@ -178,6 +180,7 @@ __global__ void __launch_bounds__(kAesThreads, 1) trunc_bundle_kernel(const PrgP
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
     if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    pdl_wait();
     return;
   }
   const sufb200_trunc_desc& d = a.desc;
@@ -219,12 +222,15 @@ __global__ void __launch_bounds__(kAesThreads, 1)
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
     if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
+    pdl_wait();
     return;
   }
   QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);  // party p, query q at ks[4 p + q]
+  aes_fill_tables(a0.t0);
+  pdl_wait();
+  pdl_trigger();
   stage_keys(ks, a0);
   stage_keys(ks + 4, a1);
-  aes_fill_tables(a0.t0);
   __syncthreads();
   if (!keys_ok(ks, a0) || !keys_ok(ks + 4, a1)) return;
   const uint32_t lb = lane_base();
@@ -290,11 +296,14 @@ __global__ void __launch_bounds__(kAesThreads, 1)
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
     if (threadIdx.x == 0) atomicOr(a0.status, kStatusSmemLayout);
+    pdl_wait();
     return;
   }
   QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);
   QueryPlanSmem* qp = reinterpret_cast<QueryPlanSmem*>(smem + 8 * sizeof(QueryKeySmem));
   __shared__ int s_walks;  // 1 when some query resumes above its last level (needs the AES tables)
+  pdl_wait();  // the plan reads the range pass's result
+  pdl_trigger();
   if (threadIdx.x == 0) {
     int walks = 0;
 #pragma unroll
@@ -460,6 +469,7 @@ __global__ void __launch_bounds__(kAesThreads, 1)
     trunc_bundle_elem_kernel(const PrgParams prg, const __grid_constant__ TruncElemLaunch a) {
   if (!aes_layout_ok()) {
     if (threadIdx.x == 0) atomicOr(a.status, kStatusSmemLayout);
+    pdl_wait();
     return;
   }
   aes_fill_tables(a.t0);
@@ -529,8 +539,7 @@ cudaError_t launch_trunc_bundle(const sufb200_ctx_s* ctx, const TruncLaunch& a, 
   if (e != cudaSuccess) return e;
   const size_t want = (a.n + kAesThreads - 1) / kAesThreads;
   const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
-  trunc_bundle_kernel<<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a);
-  return cudaGetLastError();
+  return launch_pdl(trunc_bundle_kernel, grid, kAesThreads, ctx->aes_dyn_bytes, st, ctx->prg, a);
 }
 
 cudaError_t launch_trunc_bundle_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
@@ -551,9 +560,8 @@ cudaError_t launch_trunc_bundle_pair(const sufb200_ctx_s* ctx, const TruncLaunch
   threads = threads < 128 ? 128 : (threads > static_cast<size_t>(kAesThreads) ? kAesThreads : threads);
   const size_t want = (units + threads - 1) / threads;
   const int grid = static_cast<int>(want < sms ? (want ? want : 1) : sms);
-  trunc_bundle_pair_kernel<<<grid, static_cast<unsigned>(threads), ctx->aes_dyn_bytes, st>>>(ctx->prg, a0, a1,
-                                                                                            lanes);
-  return cudaGetLastError();
+  return launch_pdl(trunc_bundle_pair_kernel, grid, static_cast<unsigned>(threads), ctx->aes_dyn_bytes, st, ctx->prg,
+                    a0, a1, lanes);
 }
 
 cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaunch& a, const RangeAcc* acc,
@@ -564,8 +572,8 @@ cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaun
   FrontierSet fs{{F[0], F[1], F[2], F[3], nullptr, nullptr, nullptr, nullptr}};
   const size_t want = (a.n + kAesThreads - 1) / kAesThreads;
   const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
-  trunc_bundle_prefix_kernel<1><<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a, a, acc, kmax, fs);
-  return cudaGetLastError();
+  return launch_pdl(trunc_bundle_prefix_kernel<1>, grid, kAesThreads, ctx->aes_dyn_bytes, st, ctx->prg, a, a, acc,
+                    kmax, fs);
 }
 
 cudaError_t launch_trunc_bundle_prefix_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
@@ -578,8 +586,8 @@ cudaError_t launch_trunc_bundle_prefix_pair(const sufb200_ctx_s* ctx, const Trun
   FrontierSet fs{{F[0], F[1], F[2], F[3], F[4], F[5], F[6], F[7]}};
   const size_t want = (2 * a0.n + kAesThreads - 1) / kAesThreads;
   const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
-  trunc_bundle_prefix_kernel<2><<<grid, kAesThreads, ctx->aes_dyn_bytes, st>>>(ctx->prg, a0, a1, acc, kmax, fs);
-  return cudaGetLastError();
+  return launch_pdl(trunc_bundle_prefix_kernel<2>, grid, kAesThreads, ctx->aes_dyn_bytes, st, ctx->prg, a0, a1, acc,
+                    kmax, fs);
 }
 
 }  // namespace sufb200

@@ -145,7 +145,8 @@ def test_host_entry_chunked_matches_device_entry(ctx, torch_cuda, oracle, prg_st
 def test_pair_entry_matches_per_party_entry(ctx, torch_cuda, oracle, prg_state, kind, n):
     """sufb200_trunc_bundle_eval_pair (one query-parallel launch for both
     parties below the shared-prefix size, the per-party path above it) gives
-    each party exactly the oracle's shares."""
+    each party exactly the oracle's shares, and sufb200_trunc_bundle_eval_pair_dev
+    (keys resident on the device) the same words."""
     import ctypes as C
 
     from suf_b200 import _lib
@@ -168,6 +169,18 @@ def test_pair_entry_matches_per_party_entry(ctx, torch_cuda, oracle, prg_state, 
     ctx.sync()
     for p in (0, 1):
         assert (from_dev(out[p]) == oracle_trunc_eval(oracle, descs[p], keys[p], xhat)).all(), p
+    # the same bundles with their keys resident on the device (no host copy;
+    # the layer's capturable path), at odd device offsets
+    dkeys = [[to_dev(torch_cuda, np.concatenate([np.zeros(3, np.uint8), k]))[3:] for k in karr[p]] for p in (0, 1)]
+    dptrs = [(C.c_void_p * 4)(*[k.data_ptr() for k in dkeys[p]], *([None] * (4 - len(dkeys[p])))) for p in (0, 1)]
+    out2 = [torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda") for _ in (0, 1)]
+    _lib.check(_lib.lib().sufb200_trunc_bundle_eval_pair_dev(
+        ctx.h, C.byref(pd[0]), C.cast(dptrs[0], C.c_void_p), C.cast(sizes[0], C.c_void_p), C.byref(pd[1]),
+        C.cast(dptrs[1], C.c_void_p), C.cast(sizes[1], C.c_void_p), dx.data_ptr(), n, out2[0].data_ptr(),
+        out2[1].data_ptr(), None))
+    ctx.sync()
+    for p in (0, 1):
+        assert (from_dev(out2[p]) == from_dev(out[p])).all(), p
 
 
 @pytest.mark.parametrize("lens", [[5, 0, 20_000, 1, 37], [300] * 61 + [0, 17_000]])
