@@ -277,11 +277,18 @@ def _timed(args, ws, dev, stream, flush, step, ctx, local, sample_clocks=True, m
         if sample_clocks:
             time.sleep(0.3)  # the sampler's first readings; the warm-up then brings the clocks back up
         with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
+            # the warm-up steps are the timed steps' exact sequence (L2 flush,
+            # events, step): the first flush and event records of a process
+            # run long once, and they belong here, not in step 0
+            for k in range(args.warmup):
+                flush.fill_(k)
+                wev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                wev[0].record(stream)
                 if mids:
                     step(torch.cuda.Event(enable_timing=True))
                 else:
                     step()
+                wev[1].record(stream)
         ctx.sync(stream)
         if ws > 1:
             dist.barrier()

@@ -333,11 +333,7 @@ __device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const Coe
   aes_fill_tables(a0.t0);
   pdl_wait();  // x^ may come from the previous kernel
   pdl_trigger();
-  // Items in flight per lane: the current one (x^ and interval known), the
-  // next (x^ loaded a step ago; its interval is searched while the current
-  // one's AES runs) and the one after (x^ load issued).
-  const auto xload = [&](size_t g) { return g < total ? __ldg(xs + (g < n ? g : g - n)) : 0ull; };
-  uint64_t xh_cur = xload(first), xh_next = xload(first + step);
+  uint64_t xh_next = first < total ? __ldg(xs + (first < n ? first : first - n)) : 0ull;
   uint32_t* s_rk = reinterpret_cast<uint32_t*>(smem);                 // [NP][44]
   CoeffSide* s_side = reinterpret_cast<CoeffSide*>(smem + 512);       // [NP]
   uint64_t* s_tab = reinterpret_cast<uint64_t*>(smem + 1024);         // [NP][kStageBytes / NP]
@@ -350,21 +346,10 @@ __device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const Coe
   const uint32_t lb = lane_base();
   uint32_t rk[44];
   int cur = -1;
-  // The interval of item g's x^ (0 for an item past the end or a side whose key failed its checks).
-  const auto search = [&](size_t g, uint64_t xh) {
-    if (g >= total) return 0;
-    const CoeffSide& S = s_side[(NP == 2 && g >= n) ? 1 : 0];
-    return S.ok ? coeff_interval(S, xh) : 0;
-  };
-  int iv_cur = search(first, xh_cur);
   for (size_t g = first; g < total; g += step) {
-    const uint64_t xh = xh_cur;
-    const int iv = iv_cur;
+    const uint64_t xh = xh_next;
     const size_t gn = g + step;
-    const uint64_t xh_after = xload(gn + step);
-    iv_cur = search(gn, xh_next);
-    xh_cur = xh_next;
-    xh_next = xh_after;
+    xh_next = gn < total ? __ldg(xs + (gn < n ? gn : gn - n)) : 0ull;
     const int q = (NP == 2 && g >= n) ? 1 : 0;
     const size_t i = q ? g - n : g;
     const CoeffSide& S = s_side[q];
@@ -374,6 +359,7 @@ __device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const Coe
       for (int j = 0; j < r; j++) out[j] = 0;
       continue;
     }
+    const int iv = coeff_interval(S, xh);
     const uint64_t base = S.nonce ^ ((S.idx_base + i) << 32);
     const uint64_t w0 = static_cast<uint64_t>(iv) * static_cast<uint64_t>(S.ow);
     const uint64_t* row = S.pay + static_cast<size_t>(iv) * S.ow;
