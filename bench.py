@@ -770,13 +770,27 @@ def run_trunc_elem(args, ws, rank, local):
     flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
     torch.cuda.synchronize()
 
-    def step():
+    def step_adapter():
         for p in (0, 1):
             ctx.trunc_bundle_eval_elem(shapes[p], keys[p], kb, words[p], d_x, d_y=d_y[p], stream=stream)
 
-    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    ms_adapter, _, _ = _timed(args, ws, dev, stream, flush, step_adapter, ctx, local)
     want = (x.view(np.int64) >> FRAC).view(np.uint64)
     ok = bool(((d_y[0].cpu().numpy().view(np.uint64) + d_y[1].cpu().numpy().view(np.uint64)) == want).all())
+    # the keys rearranged level by level (dealer-side, once; the adapter
+    # layout is dropped), the layout the product path evaluates
+    soa = [[ctx.elem_keys_to_soa(int(shapes[p].q_bits[q]), p, keys[p][q], n, stream=stream) for q in range(nq)]
+           for p in (0, 1)]
+    ctx.sync(stream)
+    del keys
+    torch.cuda.empty_cache()
+
+    def step():
+        for p in (0, 1):
+            ctx.trunc_bundle_eval_elem_soa(shapes[p], soa[p], words[p], d_x, d_y=d_y[p], stream=stream)
+
+    ms, ms_steps, clk = _timed(args, ws, dev, stream, flush, step, ctx, local)
+    ok = ok and bool(((d_y[0].cpu().numpy().view(np.uint64) + d_y[1].cpu().numpy().view(np.uint64)) == want).all())
 
     x_pin = torch.from_numpy(xhat_h.view(np.int64)).pin_memory()
     y_pin = [torch.empty(n, dtype=torch.int64).pin_memory() for _ in range(2)]
@@ -786,7 +800,7 @@ def run_trunc_elem(args, ws, rank, local):
         with torch.cuda.stream(stream):
             d_xe.copy_(x_pin, non_blocking=True)
             for p in (0, 1):
-                ctx.trunc_bundle_eval_elem(shapes[p], keys[p], kb, words[p], d_xe, d_y=d_y[p], stream=stream)
+                ctx.trunc_bundle_eval_elem_soa(shapes[p], soa[p], words[p], d_xe, d_y=d_y[p], stream=stream)
                 y_pin[p].copy_(d_y[p], non_blocking=True)
         stream.synchronize()
 
@@ -806,7 +820,8 @@ def run_trunc_elem(args, ws, rank, local):
     bits = [int(shapes[0].q_bits[q]) for q in range(nq)]
     blocks = n * 2 * sum(bits)  # one party's call: two AES blocks per level, every level of every key
     kernel_ms = ms / 2
-    key_bytes = n * sum(kb)
+    soa_kb = [25 * b + 24 for b in bits]  # bytes per key in the level-major layout
+    key_bytes = n * sum(soa_kb)
     hbm = (key_bytes + n * (8 + 48 + 8)) / (kernel_ms / 1e3) / 1e9  # keys + x^ + words + y per party call
     peaks = measured_peaks()
     res = None
@@ -828,15 +843,17 @@ def run_trunc_elem(args, ws, rank, local):
                             "achieved": round(blocks / (kernel_ms / 1e3) / 1e9, 2),
                             "peak": round(engine_peak / 1e9, 2),
                             "frac": round(blocks / (kernel_ms / 1e3) / engine_peak, 4),
-                            "kernel": "trunc_bundle_elem_kernel<true>",
-                            "traffic": round(ELEM_TRAFFIC_BYTES_PER_ELEMENT * n),
-                            "traffic_source": "ncu dram read + write of two 262,144-element launches of this "
-                                              "kernel, per element, times one launch's elements",
+                            "kernel": "trunc_bundle_elem_kernel<2> (level-major keys)",
+                            "traffic": None,
+                            "traffic_adapter_layout": round(ELEM_TRAFFIC_BYTES_PER_ELEMENT * n),
+                            "traffic_source": "ncu dram read + write of two 262,144-element launches of the "
+                                              "adapter-layout kernel, per element, times one launch's elements",
+                            "adapter_layout_ms_per_step": round(ms_adapter, 4),
                             "work_model": "every element walks every level of its own four keys: 2 AES blocks per "
                                           "level, 160 levels per element per party",
                             "hbm": {"achieved": round(hbm, 1), "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
                                     "frac": round(hbm / peaks.get("hbm_gbs", 6650.0), 4),
-                                    "bytes_per_element_per_party": sum(kb) + 64}},
+                                    "bytes_per_element_per_party": sum(soa_kb) + 64}},
                "cpu_baseline": None, "clocks": clk.summary(), "gpu_launches": 2 * args.steps,
                "reconstruction_ok": ok, "ms_per_step_all": [round(v, 4) for v in ms_steps]}
     if ws > 1:

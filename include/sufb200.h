@@ -224,6 +224,25 @@ int sufb200_trunc_bundle_eval_elem(sufb200_ctx ctx, const sufb200_trunc_desc* sh
                                    const size_t* key_bytes, const uint64_t* d_words, const uint64_t* d_xhat, size_t n,
                                    uint64_t* d_y, uint64_t* d_bools, void* stream);
 
+/* The per-element keys of one slot rearranged level by level for the
+ * evaluation kernel (an engine-internal device layout, made once per batch
+ * of dealt keys): the n keys' seeds, per-level correction words and final
+ * words as arrays over the elements, so a warp reads one level of its 32
+ * elements' keys as one coalesced run instead of 32 records 33 in_bits + 40
+ * bytes apart, and each key takes 25 in_bits + 24 bytes.
+ * sufb200_elem_keys_soa_bytes gives the layout's size (0 for a bad width);
+ * sufb200_elem_keys_to_soa fills it from d_keys [n][key_bytes] (adapter
+ * layout, in_bits, party; d_soa 16-byte aligned; a key whose header does not
+ * match is flagged through sufb200_ctx_sync and evaluates to 0);
+ * sufb200_trunc_bundle_eval_elem_soa is sufb200_trunc_bundle_eval_elem over
+ * those layouts (d_soa[q] per slot), with the same outputs. */
+size_t sufb200_elem_keys_soa_bytes(int in_bits, size_t n);
+int sufb200_elem_keys_to_soa(sufb200_ctx ctx, int in_bits, int party, const uint8_t* d_keys, size_t key_bytes,
+                             size_t n, uint8_t* d_soa, void* stream);
+int sufb200_trunc_bundle_eval_elem_soa(sufb200_ctx ctx, const sufb200_trunc_desc* shape, const uint8_t* const* d_soa,
+                                       const uint64_t* d_words, const uint64_t* d_xhat, size_t n, uint64_t* d_y,
+                                       uint64_t* d_bools, void* stream);
+
 /* ---- composite tapes of truncation gates ----------------------------------
  * The serialized CompositePartyKey of gates::write_composite_tape /
  * read_composite_tape (include/gates/composite_fss.hpp:2458-2608), byte for

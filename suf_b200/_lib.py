@@ -82,6 +82,9 @@ _SIGS = {
     "sufb200_trunc_gen_elem": (_i, [_i, _i, _u64, _sz, C.POINTER(TruncDesc), C.POINTER(TruncDesc), _vp, _vp, _vp,
                                     _vp]),
     "sufb200_trunc_bundle_eval_elem": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
+    "sufb200_elem_keys_soa_bytes": (_sz, [_i, _sz]),
+    "sufb200_elem_keys_to_soa": (_i, [_vp, _i, _i, _vp, _sz, _sz, _vp, _vp]),
+    "sufb200_trunc_bundle_eval_elem_soa": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "sufb200_trunc_write_tapes": (_i, [_i, _i, _u64, _i, _vp, _vp, _vp, _i, _vp, _vp, _sz, _vp]),
     "sufb200_trunc_read_tape": (_i, [_vp, _sz, _i, _u64, _i, C.POINTER(TruncDesc), _vp, _vp, _vp]),
     "sufb200_trunc_gen_elem_rin_shares": (_i, [_i, _i, _u64, _sz, _vp]),

@@ -447,7 +447,63 @@ int sufb200_trunc_bundle_eval_elem(sufb200_ctx ctx, const sufb200_trunc_desc* sh
   a.bools = d_bools;
   a.t0 = ctx->d_t0;
   a.status = ctx->d_status;
-  const cudaError_t e = sufb200::launch_trunc_bundle_elem(ctx, a, aligned, as_stream(stream));
+  const cudaError_t e = sufb200::launch_trunc_bundle_elem(ctx, a, aligned ? 1 : 0, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "per-element bundle launch");
+  return SUFB200_OK;
+}
+
+size_t sufb200_elem_keys_soa_bytes(int in_bits, size_t n) {
+  if (in_bits < 1 || in_bits > 64) return 0;
+  return sufb200::elem_soa_bytes(in_bits, n);
+}
+
+int sufb200_elem_keys_to_soa(sufb200_ctx ctx, int in_bits, int party, const uint8_t* d_keys, size_t key_bytes,
+                             size_t n, uint8_t* d_soa, void* stream) {
+  if (int rc = check_ctx(ctx, false)) return rc;
+  if (in_bits < 1 || in_bits > 64 || (party != 0 && party != 1))
+    return fail(SUFB200_ERR_INVALID, "in_bits must be 1..64 and party 0 or 1");
+  if (key_bytes != sufb200::host::myl7_key_bytes(in_bits, 8))
+    return fail(SUFB200_ERR_KEY, "key size does not match an 8-byte myl7 key of this width");
+  if (n == 0) return SUFB200_OK;
+  if (!d_keys || !d_soa || (reinterpret_cast<uintptr_t>(d_soa) & 15u))
+    return fail(SUFB200_ERR_INVALID, "null keys, or a layout buffer that is not 16-byte aligned");
+  SUFB200_CHECK_CUDA(sufb200::launch_elem_keys_to_soa(ctx, d_keys, key_bytes, in_bits, party, n, d_soa,
+                                                      as_stream(stream)),
+                     "per-element key rearrangement launch");
+  return SUFB200_OK;
+}
+
+int sufb200_trunc_bundle_eval_elem_soa(sufb200_ctx ctx, const sufb200_trunc_desc* shape, const uint8_t* const* d_soa,
+                                       const uint64_t* d_words, const uint64_t* d_xhat, size_t n, uint64_t* d_y,
+                                       uint64_t* d_bools, void* stream) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (!shape || !d_soa) return fail(SUFB200_ERR_INVALID, "null pointer");
+  if (shape->nq < 0 || shape->nq > 4) return fail(SUFB200_ERR_UNSUPPORTED, "bundle has more than 4 slots");
+  if (shape->kind < 0 || shape->kind > 2 || shape->party < 0 || shape->party > 1 || shape->frac_bits < 0 ||
+      shape->frac_bits > 64)
+    return fail(SUFB200_ERR_INVALID, "bad kind / party / frac_bits");
+  if (n == 0) return SUFB200_OK;
+  if (!d_words || !d_xhat || !d_y || !aligned8(d_words) || !aligned8(d_xhat) || !aligned8(d_y) ||
+      (d_bools && !aligned8(d_bools)))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  sufb200::TruncElemLaunch a{};
+  a.shape = *shape;
+  for (int q = 0; q < shape->nq; q++) {
+    const int nb = shape->q_bits[q];
+    if (nb < 1 || nb > 64) return fail(SUFB200_ERR_INVALID, "slot in_bits out of range");
+    if (!d_soa[q] || (reinterpret_cast<uintptr_t>(d_soa[q]) & 15u))
+      return fail(SUFB200_ERR_INVALID, "null or unaligned key layout");
+    a.keys[q] = d_soa[q];
+    a.key_bytes[q] = 0;
+  }
+  a.words = d_words;
+  a.xhat = d_xhat;
+  a.n = n;
+  a.y = d_y;
+  a.bools = d_bools;
+  a.t0 = ctx->d_t0;
+  a.status = ctx->d_status;
+  const cudaError_t e = sufb200::launch_trunc_bundle_elem(ctx, a, 2, as_stream(stream));
   if (e != cudaSuccess) return cuda_fail(e, "per-element bundle launch");
   return SUFB200_OK;
 }

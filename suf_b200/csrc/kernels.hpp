@@ -74,8 +74,16 @@ struct TruncElemLaunch {
   const uint32_t* t0;
   uint32_t* status;
 };
-cudaError_t launch_trunc_bundle_elem(const sufb200_ctx_s* ctx, const TruncElemLaunch& a, bool aligned,
+// mode: 0 adapter-layout keys (bytewise), 1 adapter-layout keys (aligned
+// loads), 2 level-major keys (launch_elem_keys_to_soa's layout).
+cudaError_t launch_trunc_bundle_elem(const sufb200_ctx_s* ctx, const TruncElemLaunch& a, int mode,
                                      cudaStream_t st);
+// One slot's n adapter-layout keys (key_bytes each, in_bits nb, party) into
+// the level-major layout of elem_soa_bytes(nb, n) bytes at soa (device,
+// 16-byte aligned); a key whose header does not match is flagged.
+cudaError_t launch_elem_keys_to_soa(const sufb200_ctx_s* ctx, const uint8_t* keys, size_t kb, int nb, int party,
+                                    size_t n, uint8_t* soa, cudaStream_t st);
+size_t elem_soa_bytes(int nb, size_t n);
 // A chunk of a job bucket (jobs.cu): job j's words are src[j][0..off[j+1]-off[j])
 // (gather) or dst[j][...] (scatter), at batch[base + off[j] ...].
 constexpr int kJobsPerLaunch = 48;

@@ -458,13 +458,102 @@ __device__ __forceinline__ uint64_t walk_elem_key(const PrgParams& prg, uint32_t
   return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, np1);
 }
 
+// Level-major layout of one slot's n per-element keys (n in_bits-level keys):
+//   cws [nb][n] uint4   the seed correction word of each level
+//   seed [n] uint4      the key's seed (bit 127 set: the key's header failed)
+//   cwv [nb][n] u64     the low word of each level's value correction
+//   np1 [n] u64         the low word of the final correction
+//   cwt [nb][n] u8      each level's two t-bit corrections
+// Lanes of a warp (consecutive elements) read one level's words as one
+// coalesced run, where the adapter layout spreads them over 32 records
+// 33 nb + 40 bytes apart; 25 nb + 24 bytes per key.
+struct ElemSoa {
+  const uint4* cws;
+  const uint4* seed;
+  const uint64_t* cwv;
+  const uint64_t* np1;
+  const uint8_t* cwt;
+};
+
+__host__ __device__ __forceinline__ ElemSoa elem_soa_view(const uint8_t* base, int nb, size_t n) {
+  ElemSoa v;
+  const size_t L = static_cast<size_t>(nb) * n;
+  v.cws = reinterpret_cast<const uint4*>(base);
+  v.seed = v.cws + L;
+  v.cwv = reinterpret_cast<const uint64_t*>(v.seed + n);
+  v.np1 = v.cwv + L;
+  v.cwt = reinterpret_cast<const uint8_t*>(v.np1 + n);
+  return v;
+}
+
+__device__ __forceinline__ uint64_t walk_elem_soa(const PrgParams& prg, uint32_t lb, const uint8_t* base, size_t i,
+                                                  size_t n, int nb, uint64_t x, uint32_t party) {
+  const ElemSoa K = elem_soa_view(base, nb, n);
+  const uint4 sd = __ldg(K.seed + i);
+  if (sd.w & 0x80000000u) return 0;  // its header failed at the rearrangement (status flagged there)
+  Blk s;
+  s.w[0] = sd.x;
+  s.w[1] = sd.y;
+  s.w[2] = sd.z;
+  s.w[3] = sd.w;
+  uint32_t t = party;
+  uint64_t v = 0;
+  for (int lv = 0; lv < nb; lv++) {
+    const size_t j = static_cast<size_t>(lv) * n + i;
+    const uint4 c = __ldg(K.cws + j);
+    CwLevel cw;
+    cw.s.w[0] = c.x;
+    cw.s.w[1] = c.y;
+    cw.s.w[2] = c.z;
+    cw.s.w[3] = c.w;
+    cw.v = __ldg(K.cwv + j);
+    cw.t = __ldg(K.cwt + j);
+    walk_level<SUFB200_GROUP_ADD>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (nb - 1 - lv)) & 1ull), party, cw);
+  }
+  return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, __ldg(K.np1 + i));
+}
+
+// Adapter-layout keys [n][key_bytes] of one slot -> the level-major layout;
+// one thread per (element, level) record (and the seed / final word at
+// level 0), writes coalesced across threads.
+__global__ void elem_keys_to_soa_kernel(const uint8_t* __restrict__ keys, size_t kb, int nb, uint32_t party, size_t n,
+                                        uint8_t* __restrict__ soa, uint32_t* status) {
+  const ElemSoa K = elem_soa_view(soa, nb, n);
+  uint4* cws = const_cast<uint4*>(K.cws);
+  uint4* seed = const_cast<uint4*>(K.seed);
+  uint64_t* cwv = const_cast<uint64_t*>(K.cwv);
+  uint64_t* np1 = const_cast<uint64_t*>(K.np1);
+  uint8_t* cwt = const_cast<uint8_t*>(K.cwt);
+  const size_t total = static_cast<size_t>(nb) * n;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total; g += stride) {
+    const size_t lv = g / n, i = g - lv * n;
+    const uint8_t* k = keys + i * kb;
+    const uint8_t* c = k + 24 + 33 * lv;
+    cws[g] = make_uint4(ldb32(c), ldb32(c + 4), ldb32(c + 8), ldb32(c + 12));
+    cwv[g] = ldb64(c + 16);
+    cwt[g] = c[32];
+    if (lv == 0) {
+      const uint64_t hdr = ldb64(k);
+      const bool ok = (hdr & 0xFF) == static_cast<uint64_t>(nb) && ((hdr >> 8) & 0xFF) == 1 &&
+                      ((hdr >> 16) & 0xFF) == party && (hdr >> 32) == 8;
+      if (!ok) atomicOr(status, kStatusBadKeyHeader);
+      seed[i] = make_uint4(ldb32(k + 8), ldb32(k + 12), ldb32(k + 16),
+                           (ldb32(k + 20) & 0x7FFFFFFFu) | (ok ? 0u : 0x80000000u));
+      np1[i] = ldb64(k + 24 + 33 * static_cast<size_t>(nb));
+    }
+  }
+}
+
 // Per-element masks: element i has its own keys (slot q at keys[q] + i *
 // key_bytes[q]), its own descriptor words and plan (words[6 i ..]); one
 // thread per element walks every slot and folds the element's plan and
 // postproc (the per-element path of compiler::lower_truncation_gate,
 // include/compiler/truncation_lowering.hpp:91-125, evaluated by one
 // composite_eval_batch_backend per element in the reference).
-template <bool ALIGNED>
+// MODE: 0 adapter-layout keys read bytewise, 1 adapter-layout keys with
+// aligned 16-byte loads, 2 level-major keys (keys[q] = the slot's layout).
+template <int MODE>
 __global__ void __launch_bounds__(kAesThreads, 1)
     trunc_bundle_elem_kernel(const PrgParams prg, const __grid_constant__ TruncElemLaunch a) {
   if (!aes_layout_ok()) {
@@ -486,7 +575,9 @@ __global__ void __launch_bounds__(kAesThreads, 1)
       if (q < nq) {
         const int nb = a.shape.q_bits[q];
         const uint64_t x = nb >= 64 ? xh : (xh & ((1ull << nb) - 1ull));
-        pr[q] = walk_elem_key<ALIGNED>(prg, lb, a.keys[q] + i * a.key_bytes[q], nb, x, party, a.status);
+        pr[q] = MODE == 2 ? walk_elem_soa(prg, lb, a.keys[q], i, a.n, nb, x, party)
+                          : walk_elem_key<MODE == 1>(prg, lb, a.keys[q] + i * a.key_bytes[q], nb, x, party,
+                                                     a.status);
       }
     }
     const uint64_t* w = a.words + 6 * i;
@@ -521,9 +612,21 @@ __global__ void __launch_bounds__(kAesThreads, 1)
 
 }  // namespace
 
-cudaError_t launch_trunc_bundle_elem(const sufb200_ctx_s* ctx, const TruncElemLaunch& a, bool aligned,
+cudaError_t launch_elem_keys_to_soa(const sufb200_ctx_s* ctx, const uint8_t* keys, size_t kb, int nb, int party,
+                                    size_t n, uint8_t* soa, cudaStream_t st) {
+  const size_t total = static_cast<size_t>(nb) * n;
+  const size_t want = (total + 255) / 256, cap = static_cast<size_t>(ctx->sm_count) * 8;
+  elem_keys_to_soa_kernel<<<static_cast<int>(want < cap ? (want ? want : 1) : cap), 256, 0, st>>>(
+      keys, kb, nb, static_cast<uint32_t>(party), n, soa, ctx->d_status);
+  return cudaGetLastError();
+}
+
+size_t elem_soa_bytes(int nb, size_t n) { return n * (25 * static_cast<size_t>(nb) + 24); }
+
+cudaError_t launch_trunc_bundle_elem(const sufb200_ctx_s* ctx, const TruncElemLaunch& a, int mode,
                                      cudaStream_t st) {
-  const auto kernel = aligned ? trunc_bundle_elem_kernel<true> : trunc_bundle_elem_kernel<false>;
+  const auto kernel = mode == 2 ? trunc_bundle_elem_kernel<2>
+                                : (mode == 1 ? trunc_bundle_elem_kernel<1> : trunc_bundle_elem_kernel<0>);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(ctx->aes_dyn_bytes));
   if (e != cudaSuccess) return e;

@@ -274,6 +274,33 @@ class Context:
                                                      _t_ptr(lens), _stream_ptr(stream)))
         return out, lens
 
+    def elem_keys_to_soa(self, in_bits: int, party: int, d_keys, n: int, stream=None):
+        """One slot's n per-element keys (device [n][key_bytes]) in the
+        level-major layout the per-element kernel reads coalesced."""
+        import torch
+
+        nbytes = int(self._L.sufb200_elem_keys_soa_bytes(in_bits, n))
+        out = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=d_keys.device)
+        check(self._L.sufb200_elem_keys_to_soa(self.h, in_bits, party, _t_ptr(d_keys), myl7_key_bytes(in_bits, 8), n,
+                                               _t_ptr(out), _stream_ptr(stream)))
+        return out
+
+    def trunc_bundle_eval_elem_soa(self, shape: TruncDesc, d_soa: Sequence, d_words, d_xhat, d_y=None,
+                                   d_bools=None, stream=None):
+        """trunc_bundle_eval_elem over level-major key layouts (elem_keys_to_soa)."""
+        import torch
+
+        n = d_xhat.numel()
+        if d_y is None:
+            d_y = torch.empty(n, dtype=torch.int64, device=d_xhat.device)
+        nq = int(shape.nq)
+        ptrs = (C.c_void_p * 4)(*[_t_ptr(k) for k in d_soa[:nq]], *([None] * (4 - nq)))
+        check(self._L.sufb200_trunc_bundle_eval_elem_soa(self.h, C.byref(shape), C.cast(ptrs, C.c_void_p),
+                                                         _t_ptr(d_words), _t_ptr(d_xhat), n, _t_ptr(d_y),
+                                                         _t_ptr(d_bools) if d_bools is not None else None,
+                                                         _stream_ptr(stream)))
+        return d_y
+
     def trunc_bundle_eval_host(self, desc: TruncDesc, keys: Sequence[np.ndarray], xhat: np.ndarray,
                                y: np.ndarray | None = None, bools: np.ndarray | None = None) -> np.ndarray:
         """Host buffers in and out (pinned memory makes the copies true DMA)."""

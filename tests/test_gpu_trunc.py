@@ -240,7 +240,8 @@ def test_per_element_bundles_bit_exact(ctx, torch_cuda, oracle, prg_state, kind,
     gate and keys.  Each party's shares equal the oracle's per-element
     composite eval + postproc word for word, and y0 + y1 is the truncation;
     the f = 12 cases hold elements whose gate has no carry queries (r_low =
-    0), which the slot layout marks absent."""
+    0), which the slot layout marks absent.  The level-major key layout
+    (sufb200_elem_keys_to_soa) gives the same words."""
     from suf_b200.engine import Context, host_mt19937_64, myl7_key_bytes
     from tests.helpers import ONE_LE
 
@@ -267,6 +268,12 @@ def test_per_element_bundles_bit_exact(ctx, torch_cuda, oracle, prg_state, kind,
         dy = ctx.trunc_bundle_eval_elem(shape, dk, kb, to_dev(torch_cuda, words.ravel()), dx, d_bools=db)
         ctx.sync()
         got = from_dev(dy)
+        # the same keys in the level-major layout: the same words
+        soa = [ctx.elem_keys_to_soa(int(shape.q_bits[q]), p, dk[q], n) for q in range(nq)]
+        db2 = torch_cuda.zeros(3 * n, dtype=torch_cuda.int64, device="cuda")
+        dy2 = ctx.trunc_bundle_eval_elem_soa(shape, soa, to_dev(torch_cuda, words.ravel()), dx, d_bools=db2)
+        ctx.sync()
+        assert (from_dev(dy2) == got).all() and (from_dev(db2) == from_dev(db)).all(), p
         pred = np.stack([oracle.myl7_eval(0, keys[q][p], kb[q], False, xhat, 8).view(np.uint64).ravel()
                          for q in range(nq)])
         exp = np.array([oracle.trunc_combine(_elem_desc(shape, words[i]), xhat[i:i + 1], pred[:, i].copy())[0]
@@ -275,3 +282,25 @@ def test_per_element_bundles_bit_exact(ctx, torch_cuda, oracle, prg_state, kind,
         ys.append(got)
     want = (x >> np.uint64(f)) if kind == KIND_TR else (x.view(np.int64) >> f).view(np.uint64)
     assert ((ys[0] + ys[1]) == want).all()
+
+
+def test_per_element_soa_flags_a_bad_key_header(ctx, torch_cuda):
+    """A per-element key whose header does not match its slot is flagged when
+    the keys are rearranged (sufb200_ctx_sync reports it) and that element's
+    query evaluates to 0; the context stays usable."""
+    from suf_b200 import SufB200Error
+    from suf_b200.engine import Context, host_mt19937_64
+    from tests.helpers import ONE_LE
+
+    n = 64
+    r_in, s0, s1, w0, w1, th = Context.trunc_gen_elem(KIND_GAPARS, 12, 5, n)
+    seeds = host_mt19937_64(0xBAD, 4 * n).view(np.uint8).reshape(n, 2, 16)
+    k0, _ = ctx.myl7_gen_batch(0, 12, th[:, 0], ONE_LE, np.ascontiguousarray(seeds[:, 0]),
+                               np.ascontiguousarray(seeds[:, 1]))
+    k0 = k0.copy()
+    k0[7, 2] ^= 1  # element 7: the party byte of its header
+    soa = ctx.elem_keys_to_soa(12, 0, to_dev(torch_cuda, k0.ravel()), n)
+    with pytest.raises(SufB200Error):
+        ctx.sync()
+    ctx.sync()  # the status was cleared
+    assert soa.numel() == n * (25 * 12 + 24)
