@@ -226,10 +226,11 @@ int sufb200_trunc_bundle_eval_elem(sufb200_ctx ctx, const sufb200_trunc_desc* sh
 
 /* The per-element keys of one slot rearranged level by level for the
  * evaluation kernel (an engine-internal device layout, made once per batch
- * of dealt keys): the n keys' seeds, per-level correction words and final
- * words as arrays over the elements, so a warp reads one level of its 32
- * elements' keys as one coalesced run instead of 32 records 33 in_bits + 40
- * bytes apart, and each key takes 25 in_bits + 24 bytes.
+ * of dealt keys): in blocks of 16,384 elements, the keys' seeds, per-level
+ * correction words and final words as arrays over the block's elements, so
+ * a warp reads one level of its 32 elements' keys as one coalesced run
+ * instead of 32 records 33 in_bits + 40 bytes apart, a walk stays within a
+ * few MB, and each key takes 25 in_bits + 24 bytes.
  * sufb200_elem_keys_soa_bytes gives the layout's size (0 for a bad width);
  * sufb200_elem_keys_to_soa fills it from d_keys [n][key_bytes] (adapter
  * layout, in_bits, party; d_soa 16-byte aligned; a key whose header does not

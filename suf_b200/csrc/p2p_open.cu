@@ -17,8 +17,9 @@
 // Set-up (sufb200_p2p_open_create / _connect): each rank cudaMallocs one
 // landing area [flags: kMaxCtas u64][half 0][half 1] and exports it with
 // cudaIpcGetMemHandle; the peer maps it with cudaIpcOpenMemHandle (peer
-// access enabled lazily).  Call k writes half k & 1 of the peer's area and
-// signals flag value k: the peer's kernel of call k + 2 can only run after
+// access enabled lazily).  Call k (counted on the device, so captured
+// exchanges replay with fresh numbers) writes half k & 1 of the peer's area
+// and signals flag value k: the peer's kernel of call k + 2 can only run after
 // the peer's kernel of call k + 1, which needed this rank's call k + 1 data,
 // which this rank sends after finishing call k, so a half is never
 // overwritten while it is read (each rank issues its exchanges on one
@@ -81,11 +82,14 @@ struct P2PArgs {
   uint64_t* out;
   size_t n;
   int b, ring, sign;
-  uint64_t* peer_flags;  // the peer's landing area (mapped)
-  uint64_t* peer_half;   // the peer's half of this call
+  uint64_t* peer_flags;     // the peer's landing area (mapped)
+  uint64_t* peer_halves;    // its two halves, peer_max_words words each
+  uint64_t peer_max_words;
   const uint64_t* my_flags;
-  const uint64_t* my_half;
-  uint64_t seq;
+  const uint64_t* my_halves;
+  uint64_t my_max_words;
+  uint64_t* calls;          // device: exchanges completed on this endpoint
+  uint32_t* arrivals;       // device: CTAs of the running call that have read `calls`
   uint64_t timeout_ns;
   uint32_t* status;
 };
@@ -100,6 +104,25 @@ constexpr int kGroupsPerIter = 32;  // 2,048 elements, 16 KB of staging
 __global__ void __launch_bounds__(kThreads) p2p_open_kernel(const P2PArgs a) {
   __shared__ uint64_t s_buf[kGroupsPerIter * 64];
   __shared__ int s_abort;
+  __shared__ uint64_t s_seq;
+  // The call number comes from the endpoint's device counter, so a captured
+  // sequence of exchanges replays with fresh numbers: every CTA reads the
+  // counter, then counts itself in; the last CTA in resets the count and
+  // advances the counter, after every CTA of this call has read it (the next
+  // call starts after this kernel ends: stream order).
+  if (threadIdx.x == 0) {
+    s_seq = *reinterpret_cast<volatile const uint64_t*>(a.calls) + 1;
+    __threadfence();
+    if (atomicAdd(a.arrivals, 1u) == gridDim.x - 1) {
+      *a.arrivals = 0;
+      *a.calls = s_seq;
+    }
+  }
+  __syncthreads();
+  const uint64_t seq = s_seq;
+  const size_t half = seq & 1;
+  uint64_t* const peer_half = a.peer_halves + half * a.peer_max_words;
+  const uint64_t* const my_half = a.my_halves + half * a.my_max_words;
   const size_t groups = (a.n + 63) / 64;
   const size_t per = (groups + gridDim.x - 1) / gridDim.x;
   const size_t g0 = static_cast<size_t>(blockIdx.x) * per;
@@ -119,7 +142,7 @@ __global__ void __launch_bounds__(kThreads) p2p_open_kernel(const P2PArgs a) {
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const size_t k = w + static_cast<size_t>(u) * nt;
-        if (k < w1) a.peer_half[k] = v[u];
+        if (k < w1) peer_half[k] = v[u];
       }
     }
   } else {
@@ -135,7 +158,7 @@ __global__ void __launch_bounds__(kThreads) p2p_open_kernel(const P2PArgs a) {
           const int sh = static_cast<int>(e * b) - static_cast<int>(start);
           word |= sh >= 0 ? (grp[e] << sh) : (grp[e] >> (-sh));
         }
-        a.peer_half[g * b + k] = word;
+        peer_half[g * b + k] = word;
       }
       __syncthreads();
     }
@@ -143,11 +166,11 @@ __global__ void __launch_bounds__(kThreads) p2p_open_kernel(const P2PArgs a) {
   __syncthreads();
   if (tid == 0) {
     __threadfence_system();
-    store_release_sys(a.peer_flags + blockIdx.x, a.seq);
+    store_release_sys(a.peer_flags + blockIdx.x, seq);
     // 2. wait (bounded) for the peer's CTA of the same index
     int abort = 0;
     const uint64_t t0 = globaltimer();
-    while (load_acquire_sys(a.my_flags + blockIdx.x) < a.seq) {
+    while (load_acquire_sys(a.my_flags + blockIdx.x) < seq) {
       if (globaltimer() - t0 > a.timeout_ns) {
         atomicOr(a.status, sufb200::kStatusTimeout);
         abort = 1;
@@ -176,7 +199,7 @@ __global__ void __launch_bounds__(kThreads) p2p_open_kernel(const P2PArgs a) {
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const size_t k = j + static_cast<size_t>(u) * nt;
-        v[u] = k < e1 ? __ldcg(a.my_half + k) : 0ull;
+        v[u] = k < e1 ? __ldcg(my_half + k) : 0ull;
         l[u] = k < e1 ? a.local[k] : 0ull;
       }
 #pragma unroll
@@ -190,7 +213,7 @@ __global__ void __launch_bounds__(kThreads) p2p_open_kernel(const P2PArgs a) {
   const uint64_t emask = (1ull << b) - 1ull;
   for (size_t g = g0; g < g1; g += kGroupsPerIter) {
     const uint32_t ng = static_cast<uint32_t>(g1 - g < kGroupsPerIter ? g1 - g : kGroupsPerIter);
-    for (uint32_t k = tid; k < ng * static_cast<uint32_t>(b); k += nt) s_buf[k] = __ldcg(a.my_half + g * b + k);
+    for (uint32_t k = tid; k < ng * static_cast<uint32_t>(b); k += nt) s_buf[k] = __ldcg(my_half + g * b + k);
     __syncthreads();
     for (uint32_t k = tid; k < ng * 64; k += nt) {
       const size_t j = g * 64 + k;
@@ -214,8 +237,8 @@ struct sufb200_p2p_open_s {
   uint64_t max_words = 0;
   uint64_t peer_max_words = 0;
   int grid_cap = 0;
-  uint64_t seq = 0;
-  bool loopback = false;  // peer_area is this endpoint's own area
+  uint64_t* d_calls = nullptr;  // [calls (u64), arrivals (u32)], device
+  bool loopback = false;        // peer_area is this endpoint's own area
   char pci[40] = {};
 };
 
@@ -239,12 +262,15 @@ int sufb200_p2p_open_create(sufb200_ctx ctx, size_t max_words, sufb200_p2p_open*
   h->grid_cap = ctx->sm_count < kMaxCtas ? ctx->sm_count : kMaxCtas;
   if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&h->area), area_bytes(max_words));
   if (e == cudaSuccess) e = cudaMemset(h->area, 0, kMaxCtas * 8);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&h->d_calls), 16);
+  if (e == cudaSuccess) e = cudaMemset(h->d_calls, 0, 16);
   HandleBlob blob{};
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&blob.ipc, h->area);
   if (e == cudaSuccess) e = cudaDeviceGetPCIBusId(h->pci, sizeof(h->pci), ctx->device);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     if (h->area) cudaFree(h->area);
+    if (h->d_calls) cudaFree(h->d_calls);
     delete h;
     return fail(SUFB200_ERR_CUDA, std::string("p2p open set-up: ") + cudaGetErrorString(e));
   }
@@ -303,8 +329,6 @@ int sufb200_p2p_open_exchange(sufb200_p2p_open h, const uint64_t* d_local, size_
     return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
   cudaError_t e = cudaSetDevice(h->ctx->device);
   if (e != cudaSuccess) return fail(SUFB200_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
-  const uint64_t seq = ++h->seq;
-  const size_t half = (seq & 1) ? 1 : 0;
   P2PArgs a{};
   a.local = d_local;
   a.out = d_out;
@@ -313,10 +337,13 @@ int sufb200_p2p_open_exchange(sufb200_p2p_open h, const uint64_t* d_local, size_
   a.ring = ring_bits;
   a.sign = signed_out ? 1 : 0;
   a.peer_flags = reinterpret_cast<uint64_t*>(h->peer_area);
-  a.peer_half = reinterpret_cast<uint64_t*>(h->peer_area + kMaxCtas * 8) + half * h->peer_max_words;
+  a.peer_halves = reinterpret_cast<uint64_t*>(h->peer_area + kMaxCtas * 8);
+  a.peer_max_words = h->peer_max_words;
   a.my_flags = reinterpret_cast<const uint64_t*>(h->area);
-  a.my_half = reinterpret_cast<const uint64_t*>(h->area + kMaxCtas * 8) + half * h->max_words;
-  a.seq = seq;
+  a.my_halves = reinterpret_cast<const uint64_t*>(h->area + kMaxCtas * 8);
+  a.my_max_words = h->max_words;
+  a.calls = h->d_calls;
+  a.arrivals = reinterpret_cast<uint32_t*>(h->d_calls + 1);
   a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
   a.status = h->ctx->d_status;
   const uint64_t groups = (n + 63) / 64;
@@ -332,6 +359,7 @@ int sufb200_p2p_open_destroy(sufb200_p2p_open h) {
   cudaError_t e = cudaDeviceSynchronize();
   if (h->peer_area && !h->loopback) cudaIpcCloseMemHandle(h->peer_area);
   if (h->area) cudaFree(h->area);
+  if (h->d_calls) cudaFree(h->d_calls);
   delete h;
   return e == cudaSuccess ? SUFB200_OK : fail(SUFB200_ERR_CUDA, std::string("p2p open teardown: ") + cudaGetErrorString(e));
 }

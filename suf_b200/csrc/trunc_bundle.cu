@@ -458,38 +458,51 @@ __device__ __forceinline__ uint64_t walk_elem_key(const PrgParams& prg, uint32_t
   return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, np1);
 }
 
-// Level-major layout of one slot's n per-element keys (n in_bits-level keys):
-//   cws [nb][n] uint4   the seed correction word of each level
-//   seed [n] uint4      the key's seed (bit 127 set: the key's header failed)
-//   cwv [nb][n] u64     the low word of each level's value correction
-//   np1 [n] u64         the low word of the final correction
-//   cwt [nb][n] u8      each level's two t-bit corrections
+// Level-major layout of one slot's n per-element keys, in blocks of
+// kSoaBlock elements (the last block may be shorter: m elements); per block:
+//   cws [nb][m] uint4   the seed correction word of each level
+//   seed [m] uint4      the key's seed (bit 127 set: the key's header failed)
+//   cwv [nb][m] u64     the low word of each level's value correction
+//   np1 [m] u64         the low word of the final correction
+//   cwt [nb][m] u8      each level's two t-bit corrections
 // Lanes of a warp (consecutive elements) read one level's words as one
 // coalesced run, where the adapter layout spreads them over 32 records
-// 33 nb + 40 bytes apart; 25 nb + 24 bytes per key.
+// 33 nb + 40 bytes apart; 25 nb + 24 bytes per key.  The blocks keep a
+// walk's levels within a few MB (a level of a block is 256 KB of cws), so a
+// wave of the grid touches a few hundred pages of a multi-GB key set
+// instead of a page per level per array.
+constexpr size_t kSoaBlock = 16384;
+
 struct ElemSoa {
   const uint4* cws;
   const uint4* seed;
   const uint64_t* cwv;
   const uint64_t* np1;
   const uint8_t* cwt;
+  size_t m;  // elements in this block (the stride between levels)
+  size_t j;  // the element's index in its block
 };
 
-__host__ __device__ __forceinline__ ElemSoa elem_soa_view(const uint8_t* base, int nb, size_t n) {
+__host__ __device__ __forceinline__ ElemSoa elem_soa_view(const uint8_t* base, int nb, size_t n, size_t i) {
+  const size_t per = 25 * static_cast<size_t>(nb) + 24;
+  const size_t b = i / kSoaBlock;
   ElemSoa v;
-  const size_t L = static_cast<size_t>(nb) * n;
-  v.cws = reinterpret_cast<const uint4*>(base);
+  v.j = i - b * kSoaBlock;
+  v.m = n - b * kSoaBlock < kSoaBlock ? n - b * kSoaBlock : kSoaBlock;
+  const uint8_t* blk = base + b * kSoaBlock * per;
+  const size_t L = static_cast<size_t>(nb) * v.m;
+  v.cws = reinterpret_cast<const uint4*>(blk);
   v.seed = v.cws + L;
-  v.cwv = reinterpret_cast<const uint64_t*>(v.seed + n);
+  v.cwv = reinterpret_cast<const uint64_t*>(v.seed + v.m);
   v.np1 = v.cwv + L;
-  v.cwt = reinterpret_cast<const uint8_t*>(v.np1 + n);
+  v.cwt = reinterpret_cast<const uint8_t*>(v.np1 + v.m);
   return v;
 }
 
 __device__ __forceinline__ uint64_t walk_elem_soa(const PrgParams& prg, uint32_t lb, const uint8_t* base, size_t i,
                                                   size_t n, int nb, uint64_t x, uint32_t party) {
-  const ElemSoa K = elem_soa_view(base, nb, n);
-  const uint4 sd = __ldg(K.seed + i);
+  const ElemSoa K = elem_soa_view(base, nb, n, i);
+  const uint4 sd = __ldg(K.seed + K.j);
   if (sd.w & 0x80000000u) return 0;  // its header failed at the rearrangement (status flagged there)
   Blk s;
   s.w[0] = sd.x;
@@ -499,7 +512,7 @@ __device__ __forceinline__ uint64_t walk_elem_soa(const PrgParams& prg, uint32_t
   uint32_t t = party;
   uint64_t v = 0;
   for (int lv = 0; lv < nb; lv++) {
-    const size_t j = static_cast<size_t>(lv) * n + i;
+    const size_t j = static_cast<size_t>(lv) * K.m + K.j;
     const uint4 c = __ldg(K.cws + j);
     CwLevel cw;
     cw.s.w[0] = c.x;
@@ -510,7 +523,7 @@ __device__ __forceinline__ uint64_t walk_elem_soa(const PrgParams& prg, uint32_t
     cw.t = __ldg(K.cwt + j);
     walk_level<SUFB200_GROUP_ADD>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (nb - 1 - lv)) & 1ull), party, cw);
   }
-  return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, __ldg(K.np1 + i));
+  return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, __ldg(K.np1 + K.j));
 }
 
 // Adapter-layout keys [n][key_bytes] of one slot -> the level-major layout;
@@ -518,29 +531,31 @@ __device__ __forceinline__ uint64_t walk_elem_soa(const PrgParams& prg, uint32_t
 // level 0), writes coalesced across threads.
 __global__ void elem_keys_to_soa_kernel(const uint8_t* __restrict__ keys, size_t kb, int nb, uint32_t party, size_t n,
                                         uint8_t* __restrict__ soa, uint32_t* status) {
-  const ElemSoa K = elem_soa_view(soa, nb, n);
-  uint4* cws = const_cast<uint4*>(K.cws);
-  uint4* seed = const_cast<uint4*>(K.seed);
-  uint64_t* cwv = const_cast<uint64_t*>(K.cwv);
-  uint64_t* np1 = const_cast<uint64_t*>(K.np1);
-  uint8_t* cwt = const_cast<uint8_t*>(K.cwt);
   const size_t total = static_cast<size_t>(nb) * n;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total; g += stride) {
-    const size_t lv = g / n, i = g - lv * n;
+    // g runs element-fastest within a block and level: (block, level, j)
+    const size_t b = g / (kSoaBlock * static_cast<size_t>(nb));
+    const size_t m = n - b * kSoaBlock < kSoaBlock ? n - b * kSoaBlock : kSoaBlock;
+    const size_t r = g - b * kSoaBlock * static_cast<size_t>(nb);
+    const size_t lv = r / m, j = r - lv * m, i = b * kSoaBlock + j;
+    const ElemSoa K = elem_soa_view(soa, nb, n, i);
+    const size_t o = lv * K.m + K.j;
     const uint8_t* k = keys + i * kb;
     const uint8_t* c = k + 24 + 33 * lv;
-    cws[g] = make_uint4(ldb32(c), ldb32(c + 4), ldb32(c + 8), ldb32(c + 12));
-    cwv[g] = ldb64(c + 16);
-    cwt[g] = c[32];
+    const_cast<uint4*>(K.cws)[o] = make_uint4(ldb32(c), ldb32(c + 4), ldb32(c + 8), ldb32(c + 12));
+    const_cast<uint64_t*>(K.cwv)[o] = ldb64(c + 16);
+    const_cast<uint8_t*>(K.cwt)[o] = c[32];
+    uint4* seed = const_cast<uint4*>(K.seed) + K.j;
+    uint64_t* np1 = const_cast<uint64_t*>(K.np1) + K.j;
     if (lv == 0) {
       const uint64_t hdr = ldb64(k);
       const bool ok = (hdr & 0xFF) == static_cast<uint64_t>(nb) && ((hdr >> 8) & 0xFF) == 1 &&
                       ((hdr >> 16) & 0xFF) == party && (hdr >> 32) == 8;
       if (!ok) atomicOr(status, kStatusBadKeyHeader);
-      seed[i] = make_uint4(ldb32(k + 8), ldb32(k + 12), ldb32(k + 16),
-                           (ldb32(k + 20) & 0x7FFFFFFFu) | (ok ? 0u : 0x80000000u));
-      np1[i] = ldb64(k + 24 + 33 * static_cast<size_t>(nb));
+      *seed = make_uint4(ldb32(k + 8), ldb32(k + 12), ldb32(k + 16),
+                         (ldb32(k + 20) & 0x7FFFFFFFu) | (ok ? 0u : 0x80000000u));
+      *np1 = ldb64(k + 24 + 33 * static_cast<size_t>(nb));
     }
   }
 }

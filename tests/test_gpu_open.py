@@ -283,6 +283,28 @@ def test_p2p_open_loopback_one_gpu():
             ctx.sync(stream)
             for o in outs:
                 assert (o.cpu().numpy().view(np.uint64) == want).all(), (n, eff, ring, signed)
+        # captured exchanges replay with fresh call numbers (the device
+        # counter): two calls per replay, three replays, both halves in turn
+        n, eff, ring, signed = CASES[1]
+        rng = np.random.default_rng([11, 99])
+        s = rng.integers(0, 2**63, n, dtype=np.uint64)
+        d = torch.from_numpy(s.view(np.int64)).cuda()
+        want = _expected(s + (s & np.uint64((1 << eff) - 1)), ring, signed)
+        o = [torch.zeros_like(d), torch.zeros_like(d)]
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
+            for k in range(2):
+                ep.exchange(d, eff, ring, signed=signed, d_out=o[k], timeout_s=5.0, stream=stream)
+        for _ in range(3):
+            o[0].zero_()
+            o[1].zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            ctx.sync()
+            for k in range(2):
+                assert (o[k].cpu().numpy().view(np.uint64) == want).all(), k
+        del g
     finally:
         ep.close()
         ctx.close()
