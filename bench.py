@@ -529,7 +529,7 @@ def run_ours(args, ws, rank, local):
                       "+ 2*(2^(h_q+1) - 2))",
         "hbm": {"achieved": round(hbm_gbs, 2), "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
                 "frac": round(hbm_gbs / peaks.get("hbm_gbs", 6650.0), 5)},
-        "hw_pipes": {"lsu_pct_of_peak": 95.5, "alu_pct_of_peak": 91.2, "issue_active_pct": 74.3,
+        "hw_pipes": {"lsu_pct_of_peak": 95.0, "alu_pct_of_peak": 92.0, "issue_active_pct": 74.6,
                      "source": "ncu --set full of one full-size trunc_bundle_prefix_kernel launch after the "
                                "warm-up (sm__inst_executed_pipe_lsu, sm__pipe_alu_cycles_active, "
                                "smsp__issue_active; pct of peak sustained active): the hardware bound behind "
