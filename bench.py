@@ -1458,12 +1458,13 @@ def cpu_softmax_baseline(args):
 
 
 # Our kernels per block (from the ncu launch list): softmax = 4 element-level
-# truncations x (range, frontier, main) + 3 row-level pair truncations + 2
-# interval-LUT gates (both parties per launch) + 9 elementwise stages;
-# LayerNorm = 1 element-level truncation x 3 + 7 row-level pair truncations
-# + 1 LUT gate + 9 row and elementwise stages.
-SOFTMAX_LAUNCHES = 26
-LAYERNORM_LAUNCHES = 20
+# truncations x (frontier, main; their f-bit queries take full-domain tables,
+# so no range pass) + 3 row-level pair truncations + 2 interval-LUT gates
+# (both parties per launch) + 9 elementwise stages; LayerNorm = 1
+# element-level truncation x 2 + 7 row-level pair truncations + 1 LUT gate +
+# 9 row and elementwise stages.
+SOFTMAX_LAUNCHES = 22
+LAYERNORM_LAUNCHES = 19
 
 
 def run_softmax(args, ws, rank, local):

@@ -178,6 +178,45 @@ SUFB200_DEV void prg_half(const PrgParams& P, uint32_t lb, const Blk& s, uint32_
   out.w[3] = aes_last_col<3>(a, lb, SUFB200_PRG_KEY_H(P, 10, 3, xm, hm)) ^ s.w[3];
 }
 
+// The four PRG keys' round keys in shared memory for the lane-split walk:
+// sk[j * 11 + r] holds round r of key K_j (j = 2x + h), one 16-byte row per
+// round, so a lane with half h at a level with bit x reads each round key
+// with one 16-byte load instead of selecting it word by word between the
+// halves (three logic ops per word).  The four keys' rows fall in different
+// bank groups (176-byte key stride), so a warp's loads are one wavefront.
+// Filled once per block by all threads; a barrier must follow.
+#if !defined(SUFB200_HOST_EMU)
+__device__ __forceinline__ void prg_keys_to_smem(const PrgParams& P, uint4* sk) {
+  for (int i = threadIdx.x; i < 44; i += blockDim.x) {
+    const int j = i / 11, r = i - 11 * (i / 11), h = j & 1;
+    const uint32_t xm = (j >> 1) ? ~0u : 0u;
+    sk[i] = make_uint4(SUFB200_PRG_KEY(P, h, r, 0, xm), SUFB200_PRG_KEY(P, h, r, 1, xm),
+                       SUFB200_PRG_KEY(P, h, r, 2, xm), SUFB200_PRG_KEY(P, h, r, 3, xm));
+  }
+}
+#endif
+
+// prg_half with the round keys from prg_keys_to_smem.
+SUFB200_DEV void prg_half_sk(const uint4* sk, uint32_t lb, const Blk& s, uint32_t x, uint32_t h, Blk& out) {
+  const uint4* k = sk + (2u * x + h) * 11u;
+  const uint4 k0 = k[0];
+  Blk a;
+  a.w[0] = s.w[0] ^ k0.x;
+  a.w[1] = s.w[1] ^ k0.y;
+  a.w[2] = s.w[2] ^ k0.z;
+  a.w[3] = s.w[3] ^ k0.w;
+#pragma unroll
+  for (int r = 1; r < 10; r++) {
+    const uint4 kr = k[r];
+    a = aes_round(a, lb, kr.x, kr.y, kr.z, kr.w);
+  }
+  const uint4 kl = k[10];
+  out.w[0] = aes_last_col<0>(a, lb, kl.x) ^ s.w[0];
+  out.w[1] = aes_last_col<1>(a, lb, kl.y) ^ s.w[1];
+  out.w[2] = aes_last_col<2>(a, lb, kl.z) ^ s.w[2];
+  out.w[3] = aes_last_col<3>(a, lb, kl.w) ^ s.w[3];
+}
+
 // Plain AES-128 of one block under 44 round-key words read from shared
 // memory (uniform address across the warp) -- the CTR keystream of the
 // reference key formats.

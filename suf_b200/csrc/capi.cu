@@ -584,6 +584,15 @@ int pack_bundle_keys(const sufb200_trunc_desc& desc, const uint8_t* const* keys,
   return SUFB200_OK;
 }
 
+// True when every query of the bundles takes its full domain within the
+// shared-prefix budget (2^in_bits <= kmax): no range pass is needed.
+bool narrow_queries(const sufb200_trunc_desc* d, int nd, uint32_t kmax) {
+  for (int b = 0; b < nd; b++)
+    for (int q = 0; q < d[b].nq; q++)
+      if (d[b].q_bits[q] >= 32 || (1ull << d[b].q_bits[q]) > kmax) return false;
+  return true;
+}
+
 // One party's bundle with its keys already on the device (a.key, xhat, n,
 // y, bools set): range + frontier + the resuming main pass at shared-prefix
 // sizes (scratch for the range and the frontier tables from the pool,
@@ -618,7 +627,8 @@ int single_core(sufb200_ctx ctx, sufb200::TruncLaunch a, cudaStream_t st, const 
     F[q] = reinterpret_cast<sufb200::FrontierEntry*>(scratch + kAccBytes + 32ull * kmax * q);
     fb.q[q] = sufb200::FrontierLaunch{a.key[q], desc->q_bits[q], 8, acc, kmax, F[q], ctx->d_t0, ctx->d_status};
   }
-  e = sufb200::launch_range(ctx, a.xhat, n, acc, st);
+  e = narrow_queries(&a.desc, 1, kmax) ? sufb200::set_full_range(acc, st)
+                                       : sufb200::launch_range(ctx, a.xhat, n, acc, st);
   if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
   // the main pass, in chunks when a host sink streams results back (the
   // kernel's outputs do not depend on the element index)
@@ -729,7 +739,9 @@ int trunc_pair_core(sufb200_ctx ctx, sufb200::TruncLaunch a0, sufb200::TruncLaun
                                         ctx->d_status};
     }
   }
-  cudaError_t e = sufb200::launch_range(ctx, d_xhat, n, acc, st);
+  const sufb200_trunc_desc both[2] = {a0.desc, a1.desc};
+  cudaError_t e = narrow_queries(both, 2, kmax) ? sufb200::set_full_range(acc, st)
+                                                : sufb200::launch_range(ctx, d_xhat, n, acc, st);
   if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
   if (e == cudaSuccess) e = sufb200::launch_trunc_bundle_prefix_pair(ctx, a0, a1, acc, kmax, F, st);
   cudaFreeAsync(scratch, st);

@@ -58,12 +58,12 @@ SUFB200_DEV void walk_level(const PrgParams& P, uint32_t lb, Blk& s, uint32_t& t
 // MMO blocks and the pair swaps them, so a level costs one AES block per lane
 // instead of two.  Both lanes leave with the same s, t, v as walk_level.
 #if !defined(SUFB200_HOST_EMU)
+// The round keys come from prg_keys_to_smem's table (sk).
 template <int GROUP>
-SUFB200_DEV void walk_level_split(const PrgParams& P, uint32_t lb, Blk& s, uint32_t& t, uint64_t& v, uint32_t x_bit,
+SUFB200_DEV void walk_level_split(const uint4* sk, uint32_t lb, Blk& s, uint32_t& t, uint64_t& v, uint32_t x_bit,
                                   uint32_t party, const CwLevel& cw, uint32_t h, uint32_t pmask) {
-  const uint32_t xm = 0u - x_bit;
   Blk o, e;
-  prg_half(P, lb, s, xm, h, o);
+  prg_half_sk(sk, lb, s, x_bit, h, o);
 #pragma unroll
   for (int c = 0; c < 4; c++) e.w[c] = __shfl_xor_sync(pmask, o.w[c], 1);
   Blk a;

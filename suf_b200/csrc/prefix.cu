@@ -94,6 +94,7 @@ struct FrontierKey {
 // Staging area at the start of dynamic shared memory, below the AES tables
 // (no static shared memory: it would move the table window).
 struct FrontierStage {
+  uint4 prg_keys[44];  // prg_keys_to_smem's round keys (the lane-pair walk)
   BcastKeySmem key[kFrontierMaxKeys];
   FrontierKey fk[kFrontierMaxKeys];
   uint64_t first_item[kFrontierMaxKeys + 1];
@@ -121,6 +122,7 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
   int* order = fs->order;
   uint64_t* first_item = fs->first_item;
   aes_fill_tables(b.q[0].t0);
+  prg_keys_to_smem(prg, fs->prg_keys);
   pdl_wait();  // the plans read the range pass's result
   pdl_trigger();
 #pragma unroll
@@ -180,7 +182,8 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
       emit_entry<GROUP>(out, slot, final_level, s, t, v, party, np1_lo);
     };
     if (hsel <= 1u)
-      frontier_root_pair<GROUP>(prg, lb, seed, party, f.plan, f.h, it - first_item[r], cw_at, emit, hsel, pmask);
+      frontier_root_pair<GROUP>(fs->prg_keys, lb, seed, party, f.plan, f.h, it - first_item[r], cw_at, emit, hsel,
+                                pmask);
     else
       frontier_root<GROUP>(prg, lb, seed, party, f.plan, f.h, it - first_item[r], cw_at, emit);
   };
@@ -298,6 +301,18 @@ cudaError_t launch_range(const sufb200_ctx_s* ctx, const uint64_t* xs, size_t n,
   const size_t want = (n + 255) / 256;
   const size_t cap = static_cast<size_t>(ctx->sm_count) * 4;
   return launch_pdl(range_kernel, static_cast<int>(want < cap ? (want ? want : 1) : cap), 256, 0, st, xs, n, acc);
+}
+
+// A range covering every value: make_plan then gives a query its full domain
+// whenever 2^n entries fit the budget.  Used instead of the range pass when
+// every query of a batch is that narrow (the f-bit carry queries of GapARS
+// bundles at shared-prefix sizes): the pass could only shrink tables that are
+// already small, and the outputs are the same words either way.
+cudaError_t set_full_range(RangeAcc* acc, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(&acc->min_b, 0, sizeof(uint64_t), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(&acc->max_b, 0xFF, sizeof(uint64_t), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(&acc->pivot, 0, sizeof(uint64_t), st);
+  return e;
 }
 
 cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st) {

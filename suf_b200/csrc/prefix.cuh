@@ -177,12 +177,13 @@ SUFB200_DEV void frontier_root(const PrgParams& prg, uint32_t lb, const Blk& see
 
 #if !defined(SUFB200_HOST_EMU)
 // frontier_root over a lane pair (lanes 2k and 2k + 1 of a warp, hsel = lane
-// & 1, pmask = both lanes' bits): every level is walk_level_split, each lane
+// & 1, pmask = both lanes' bits; sk: prg_keys_to_smem's round keys): every
+// level is walk_level_split, each lane
 // computing one of the level's two MMO blocks, so the serial chain of a work
 // item is one AES block per level instead of two.  Both lanes hold the same
 // states throughout; lane hsel = 0 emits.
 template <int GROUP, typename CwAt, typename Emit>
-__device__ __forceinline__ void frontier_root_pair(const PrgParams& prg, uint32_t lb, const Blk& seed,
+__device__ __forceinline__ void frontier_root_pair(const uint4* sk, uint32_t lb, const Blk& seed,
                                                    uint32_t party, const Plan& plan, int h, uint64_t j,
                                                    const CwAt& cw_at, const Emit& emit, uint32_t hsel,
                                                    uint32_t pmask) {
@@ -194,7 +195,7 @@ __device__ __forceinline__ void frontier_root_pair(const PrgParams& prg, uint32_
   uint32_t t = party;
   uint64_t v = 0;
   for (int lv = 0; lv < d0; lv++)
-    walk_level_split<GROUP>(prg, lb, s, t, v, static_cast<uint32_t>((R >> (d0 - 1 - lv)) & 1ull), party, cw_at(lv),
+    walk_level_split<GROUP>(sk, lb, s, t, v, static_cast<uint32_t>((R >> (d0 - 1 - lv)) & 1ull), party, cw_at(lv),
                             hsel, pmask);
   if (h == 0) {
     if (hsel == 0) emit((R - plan.first) & dmask, s, t, v);
@@ -217,7 +218,7 @@ __device__ __forceinline__ void frontier_root_pair(const PrgParams& prg, uint32_
     t = st[l0][4];
     v = (static_cast<uint64_t>(st[l0][6]) << 32) | st[l0][5];
     for (int l = l0; l < h; l++) {
-      walk_level_split<GROUP>(prg, lb, s, t, v, (k >> (h - 1 - l)) & 1u, party, cw_at(d0 + l), hsel, pmask);
+      walk_level_split<GROUP>(sk, lb, s, t, v, (k >> (h - 1 - l)) & 1u, party, cw_at(d0 + l), hsel, pmask);
       if (l + 1 < h) {
         st[l + 1][0] = s.w[0];
         st[l + 1][1] = s.w[1];

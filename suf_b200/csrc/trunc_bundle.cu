@@ -24,7 +24,8 @@ struct QueryKeySmem {
   uint32_t ok;
   uint32_t pad;
 };
-static_assert(8 * sizeof(QueryKeySmem) < kTabBase - 4096, "staging (two bundles) must fit below the tables");
+static_assert(8 * sizeof(QueryKeySmem) % 16 == 0 && 8 * sizeof(QueryKeySmem) + 44 * 16 < kTabBase - 4096,
+              "staging (two bundles and the PRG round keys) must fit below the tables");
 
 __device__ __forceinline__ uint32_t ldb32(const uint8_t* p) {
   return static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8) | (static_cast<uint32_t>(p[2]) << 16) |
@@ -149,7 +150,7 @@ __device__ __forceinline__ uint64_t walk_query(const PrgParams& prg, uint32_t lb
 
 // walk_query over a lane pair (walk_level_split): lanes 2k and 2k+1 of the
 // warp walk the same query together; both return the share.
-__device__ __forceinline__ uint64_t walk_query_split(const PrgParams& prg, uint32_t lb, const QueryKeySmem& K, int n,
+__device__ __forceinline__ uint64_t walk_query_split(const uint4* sk, uint32_t lb, const QueryKeySmem& K, int n,
                                                      uint64_t x, uint32_t party, Blk s, uint32_t t, uint64_t v,
                                                      uint32_t h, uint32_t pmask) {
   for (int lv = 0; lv < n; lv++) {
@@ -161,7 +162,7 @@ __device__ __forceinline__ uint64_t walk_query_split(const PrgParams& prg, uint3
     cw.s.w[3] = cs.w;
     cw.v = K.cw_v[lv];
     cw.t = K.cw_t[lv];
-    walk_level_split<SUFB200_GROUP_ADD>(prg, lb, s, t, v, static_cast<uint32_t>((x >> (n - 1 - lv)) & 1ull), party,
+    walk_level_split<SUFB200_GROUP_ADD>(sk, lb, s, t, v, static_cast<uint32_t>((x >> (n - 1 - lv)) & 1ull), party,
                                         cw, h, pmask);
   }
   return walk_finish<SUFB200_GROUP_ADD>(s, t, v, party, K.np1_lo);
@@ -226,7 +227,9 @@ __global__ void __launch_bounds__(kAesThreads, 1)
     return;
   }
   QueryKeySmem* ks = reinterpret_cast<QueryKeySmem*>(smem);  // party p, query q at ks[4 p + q]
+  uint4* sk = reinterpret_cast<uint4*>(smem + 8 * sizeof(QueryKeySmem));  // the PRG keys' round keys
   aes_fill_tables(a0.t0);
+  prg_keys_to_smem(prg, sk);
   pdl_wait();
   pdl_trigger();
   stage_keys(ks, a0);
@@ -255,7 +258,7 @@ __global__ void __launch_bounds__(kAesThreads, 1)
       const int nb = d.q_bits[q];
       const uint64_t x = nb >= 64 ? xh : (xh & ((1ull << nb) - 1ull));
       const QueryKeySmem& K = ks[4 * party + q];
-      v = walk_query_split(prg, lb, K, nb, x, party, seed_blk(K), party, 0, h, 3u << (lane & ~1));
+      v = walk_query_split(sk, lb, K, nb, x, party, seed_blk(K), party, 0, h, 3u << (lane & ~1));
     }
     uint64_t pr[4];
 #pragma unroll

@@ -402,14 +402,15 @@ class TransformerLayerPair:
         return g
 
     # launches of our kernels per layer (counted from the calls above; the
-    # truncations take the shared-prefix path: range, frontier and main
-    # kernel per party when n >= 16384, else one pair launch)
+    # truncations take the shared-prefix path when n >= 16384: one frontier
+    # and one main launch for both parties, no range pass since their f-bit
+    # queries take full-domain tables; else one pair launch)
     def launches(self) -> int:
         d = self.dims
-        lf = 20 * 2  # two LayerNorm blocks
-        sm = 26  # the softmax block (see bench.py's SOFTMAX_LAUNCHES)
+        lf = 19 * 2  # two LayerNorm blocks (see bench.py's LAYERNORM_LAUNCHES)
+        sm = 22  # the softmax block (see bench.py's SOFTMAX_LAUNCHES)
         def trunc(n):
-            return 6 if n >= 16384 else 1
+            return 2 if n >= 16384 else 1
         mm = 0
         for n in (d.S * 3 * d.D, d.S * d.D, d.S * d.Dff, d.S * d.D):  # qkv, o, ff1, ff2
             mm += 2 * 2 + 1 + trunc(n)  # two ring matmuls (pre-pass + GEMM each), open, truncation
