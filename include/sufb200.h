@@ -191,6 +191,27 @@ int sufb200_trunc_bundle_eval_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc
                                        const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
                                        uint64_t* d_y1, void* stream);
 
+/* The same pair in two steps, for bundles whose queries all take their full
+ * domain at this batch size (the f-bit carries of GapARS truncations:
+ * 2^in_bits <= the shared-prefix budget, n at least the shared-prefix size).
+ * The tables hold every query's evaluations over its whole domain and do not
+ * depend on x^, so they can be computed on another stream while x^ is still
+ * being produced (the layer computes its truncations' tables at its start).
+ * sufb200_trunc_tables_bytes: the tables' size, 0 when the pair does not
+ * qualify; sufb200_trunc_tables_pair_dev fills them (d_tables 256-byte
+ * aligned); sufb200_trunc_bundle_eval_pair_tables_dev runs the main pass over
+ * x^ against them (same outputs as sufb200_trunc_bundle_eval_pair_dev). */
+size_t sufb200_trunc_tables_bytes(const sufb200_trunc_desc* desc0, const sufb200_trunc_desc* desc1, size_t n);
+int sufb200_trunc_tables_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* d_keys0,
+                                  const size_t* key_bytes0, const sufb200_trunc_desc* desc1,
+                                  const uint8_t* const* d_keys1, const size_t* key_bytes1, size_t n, void* d_tables,
+                                  size_t tables_bytes, void* stream);
+int sufb200_trunc_bundle_eval_pair_tables_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0,
+                                              const uint8_t* const* d_keys0, const size_t* key_bytes0,
+                                              const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
+                                              const size_t* key_bytes1, const void* d_tables, const uint64_t* d_xhat,
+                                              size_t n, uint64_t* d_y0, uint64_t* d_y1, void* stream);
+
 /* Host-buffer form: xhat, y (and bools, may be NULL) in host memory; copies
  * in and out inside the call and returns when y is on the host.  Replaces
  * composite_eval_batch_backend with a host CompositeBatchInput::hatx

@@ -777,16 +777,19 @@ int sufb200_trunc_bundle_eval_pair(sufb200_ctx ctx, const sufb200_trunc_desc* de
   return rc;
 }
 
-int sufb200_trunc_bundle_eval_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0,
-                                       const uint8_t* const* d_keys0, const size_t* key_bytes0,
-                                       const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
-                                       const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
-                                       uint64_t* d_y1, void* stream) {
+namespace {
+
+// Checks of a pair of bundles whose keys are device pointers; fills a0 / a1's
+// descriptors and key pointers.
+int dev_pair_launches(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* d_keys0,
+                      const size_t* key_bytes0, const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
+                      const size_t* key_bytes1, sufb200::TruncLaunch& a0, sufb200::TruncLaunch& a1) {
   if (int rc = check_ctx(ctx, true)) return rc;
   if (int rc = check_bundle_desc(desc0, d_keys0, key_bytes0)) return rc;
   if (int rc = check_bundle_desc(desc1, d_keys1, key_bytes1)) return rc;
   if (desc0->party != 0 || desc1->party != 1) return fail(SUFB200_ERR_INVALID, "desc0 / desc1 must be parties 0 / 1");
-  sufb200::TruncLaunch a0{}, a1{};
+  a0 = sufb200::TruncLaunch{};
+  a1 = sufb200::TruncLaunch{};
   a0.desc = *desc0;
   a1.desc = *desc1;
   for (int p = 0; p < 2; p++) {
@@ -801,10 +804,104 @@ int sufb200_trunc_bundle_eval_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc
       (p ? a1 : a0).key[q] = dk[q];
     }
   }
+  return SUFB200_OK;
+}
+
+// Layout of a pair's full-domain tables: the range record, then query q's
+// 2^in_bits entries of 32 bytes, party 0's queries first.
+size_t tables_layout(const sufb200_trunc_desc* d0, const sufb200_trunc_desc* d1, size_t n, size_t off[8]) {
+  if (!d0 || !d1 || n < prefix_min_n() || d0->nq <= 0 || d1->nq <= 0 || d0->nq > 4 || d1->nq > 4) return 0;
+  const uint32_t kmax = sufb200::prefix_budget(n);
+  const sufb200_trunc_desc both[2] = {*d0, *d1};
+  if (!narrow_queries(both, 2, kmax)) return 0;
+  size_t at = kAccBytes;
+  for (int p = 0; p < 2; p++)
+    for (int q = 0; q < both[p].nq; q++) {
+      off[4 * p + q] = at;
+      at += 32ull << both[p].q_bits[q];
+    }
+  return at;
+}
+
+}  // namespace
+
+int sufb200_trunc_bundle_eval_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0,
+                                       const uint8_t* const* d_keys0, const size_t* key_bytes0,
+                                       const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
+                                       const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
+                                       uint64_t* d_y1, void* stream) {
+  sufb200::TruncLaunch a0, a1;
+  if (int rc = dev_pair_launches(ctx, desc0, d_keys0, key_bytes0, desc1, d_keys1, key_bytes1, a0, a1)) return rc;
   if (n == 0) return SUFB200_OK;
   if (!d_xhat || !d_y0 || !d_y1 || !aligned8(d_xhat) || !aligned8(d_y0) || !aligned8(d_y1))
     return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
   return trunc_pair_core(ctx, a0, a1, d_xhat, n, d_y0, d_y1, as_stream(stream));
+}
+
+size_t sufb200_trunc_tables_bytes(const sufb200_trunc_desc* desc0, const sufb200_trunc_desc* desc1, size_t n) {
+  size_t off[8];
+  return tables_layout(desc0, desc1, n, off);
+}
+
+int sufb200_trunc_tables_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* d_keys0,
+                                  const size_t* key_bytes0, const sufb200_trunc_desc* desc1,
+                                  const uint8_t* const* d_keys1, const size_t* key_bytes1, size_t n, void* d_tables,
+                                  size_t tables_bytes, void* stream) {
+  sufb200::TruncLaunch a0, a1;
+  if (int rc = dev_pair_launches(ctx, desc0, d_keys0, key_bytes0, desc1, d_keys1, key_bytes1, a0, a1)) return rc;
+  size_t off[8] = {};
+  const size_t need = tables_layout(desc0, desc1, n, off);
+  if (need == 0) return fail(SUFB200_ERR_UNSUPPORTED, "not a pair of full-domain bundles at shared-prefix size");
+  if (!d_tables || tables_bytes < need || (reinterpret_cast<uintptr_t>(d_tables) & 255u))
+    return fail(SUFB200_ERR_INVALID, "tables buffer null, unaligned (256 bytes) or smaller than sufb200_trunc_tables_bytes");
+  cudaStream_t st = as_stream(stream);
+  uint8_t* base = static_cast<uint8_t*>(d_tables);
+  auto* acc = reinterpret_cast<sufb200::RangeAcc*>(base);
+  const uint32_t kmax = sufb200::prefix_budget(n);
+  sufb200::FrontierBatch fb{};
+  int k = 0;
+  for (int p = 0; p < 2; p++) {
+    const sufb200::TruncLaunch& a = p ? a1 : a0;
+    for (int q = 0; q < a.desc.nq; q++, k++)
+      fb.q[k] = sufb200::FrontierLaunch{a.key[q], a.desc.q_bits[q], 8, acc, kmax,
+                                        reinterpret_cast<sufb200::FrontierEntry*>(base + off[4 * p + q]), ctx->d_t0,
+                                        ctx->d_status};
+  }
+  fb.nq = k;
+  cudaError_t e = sufb200::set_full_range(acc, st);
+  if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
+  return e == cudaSuccess ? SUFB200_OK : cuda_fail(e, "pair tables launch");
+}
+
+int sufb200_trunc_bundle_eval_pair_tables_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0,
+                                              const uint8_t* const* d_keys0, const size_t* key_bytes0,
+                                              const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
+                                              const size_t* key_bytes1, const void* d_tables, const uint64_t* d_xhat,
+                                              size_t n, uint64_t* d_y0, uint64_t* d_y1, void* stream) {
+  sufb200::TruncLaunch a0, a1;
+  if (int rc = dev_pair_launches(ctx, desc0, d_keys0, key_bytes0, desc1, d_keys1, key_bytes1, a0, a1)) return rc;
+  size_t off[8] = {};
+  if (tables_layout(desc0, desc1, n, off) == 0)
+    return fail(SUFB200_ERR_UNSUPPORTED, "not a pair of full-domain bundles at shared-prefix size");
+  if (!d_tables || !d_xhat || !d_y0 || !d_y1 || !aligned8(d_xhat) || !aligned8(d_y0) || !aligned8(d_y1))
+    return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
+  const uint8_t* base = static_cast<const uint8_t*>(d_tables);
+  sufb200::FrontierEntry* F[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  for (int p = 0; p < 2; p++)
+    for (int q = 0; q < (p ? a1 : a0).desc.nq; q++)
+      F[4 * p + q] = reinterpret_cast<sufb200::FrontierEntry*>(const_cast<uint8_t*>(base) + off[4 * p + q]);
+  for (sufb200::TruncLaunch* a : {&a0, &a1}) {
+    a->xhat = d_xhat;
+    a->n = n;
+    a->bools = nullptr;
+    a->t0 = ctx->d_t0;
+    a->status = ctx->d_status;
+  }
+  a0.y = d_y0;
+  a1.y = d_y1;
+  const cudaError_t e = sufb200::launch_trunc_bundle_prefix_pair(
+      ctx, a0, a1, reinterpret_cast<const sufb200::RangeAcc*>(base), sufb200::prefix_budget(n), F, as_stream(stream));
+  return e == cudaSuccess ? SUFB200_OK : cuda_fail(e, "pair bundle launch");
 }
 
 int sufb200_trunc_bundle_eval_jobs(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* keys,

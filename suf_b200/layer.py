@@ -100,7 +100,7 @@ class _Trunc:
     """One GapARS truncation bundle for both parties: descriptors, myl7 keys
     (host) and the split of its input mask r_in = r[0] + r[1]."""
 
-    def __init__(self, ctx: Context, rng, frac_bits: int, dev=None):
+    def __init__(self, ctx: Context, rng, frac_bits: int, dev=None, n: int = 0):
         import torch
 
         r_in, d0, d1, thetas = Context.trunc_gen(TRUNC_GAPARS, frac_bits, int(rng.integers(1, 2**63)))
@@ -117,8 +117,35 @@ class _Trunc:
         nq = int(d0.nq)
         self.kptr = [(C.c_void_p * 4)(*[k.data_ptr() for k in ks], *([None] * (4 - nq))) for ks in self.keys]
         self.ksz = [(C.c_size_t * 4)(*[k.numel() for k in ks], *([0] * (4 - nq))) for ks in self.keys]
+        # full-domain tables of the carry queries (x^-independent) when the
+        # bundle's n qualifies: computed by prepare() off the critical path
+        self.n = n
+        nbytes = int(_lib.lib().sufb200_trunc_tables_bytes(C.byref(d0), C.byref(d1), n)) if n else 0
+        self.tables = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
+        self.ready = None  # the event prepare() recorded
+
+    def prepare(self, ctx: Context, stream, event):
+        """Fill the tables on `stream`; `event` is recorded after them."""
+        if self.tables is None:
+            return
+        check(_lib.lib().sufb200_trunc_tables_pair_dev(
+            ctx.h, C.byref(self.desc[0]), C.cast(self.kptr[0], C.c_void_p), C.cast(self.ksz[0], C.c_void_p),
+            C.byref(self.desc[1]), C.cast(self.kptr[1], C.c_void_p), C.cast(self.ksz[1], C.c_void_p), self.n,
+            _t_ptr(self.tables), self.tables.numel(), _stream_ptr(stream)))
+        self.ready = event
 
     def eval_pair(self, ctx: Context, d_xhat, d_y0, d_y1, stream):
+        if self.tables is not None and self.ready is not None and d_xhat.numel() == self.n:
+            import torch
+
+            (stream if stream is not None else torch.cuda.current_stream()).wait_event(self.ready)
+            check(_lib.lib().sufb200_trunc_bundle_eval_pair_tables_dev(
+                ctx.h, C.byref(self.desc[0]), C.cast(self.kptr[0], C.c_void_p), C.cast(self.ksz[0], C.c_void_p),
+                C.byref(self.desc[1]), C.cast(self.kptr[1], C.c_void_p), C.cast(self.ksz[1], C.c_void_p),
+                _t_ptr(self.tables), _t_ptr(d_xhat), d_xhat.numel(), _t_ptr(d_y0), _t_ptr(d_y1),
+                _stream_ptr(stream)))
+            self.ready = None
+            return
         check(_lib.lib().sufb200_trunc_bundle_eval_pair_dev(
             ctx.h, C.byref(self.desc[0]), C.cast(self.kptr[0], C.c_void_p), C.cast(self.ksz[0], C.c_void_p),
             C.byref(self.desc[1]), C.cast(self.kptr[1], C.c_void_p), C.cast(self.ksz[1], C.c_void_p), _t_ptr(d_xhat),
@@ -214,8 +241,9 @@ class TransformerLayerPair:
         self.ln1 = LayerNormBlock(ctx, S, D, seed=int(rng.integers(1, 2**62)), tables=sm_tab)
         self.ln2 = LayerNormBlock(ctx, S, D, seed=int(rng.integers(1, 2**62)), tables=sm_tab)
         self.softmax = SoftmaxBlock(ctx, [S] * (H * S), seed=int(rng.integers(1, 2**62)), tables=sm_tab)
-        self.tr = {name: _Trunc(ctx, rng, fk, dev) for name, fk in (("qkv", f), ("scores", f + 3), ("pv", f),
-                                                                     ("o", f), ("ff1", f), ("ff2", f))}
+        sizes = {"qkv": S * 3 * D, "scores": H * S * S, "pv": S * D, "o": S * D, "ff1": S * Dff, "ff2": S * D}
+        self.tr = {name: _Trunc(ctx, rng, fk, dev, sizes[name])
+                   for name, fk in (("qkv", f), ("scores", f + 3), ("pv", f), ("o", f), ("ff1", f), ("ff2", f))}
         self.trip_s = _Triples(rng, dev, H, S, Dh, S, transposed=True)
         self.trip_pv = _Triples(rng, dev, H, S, S, Dh, transposed=False)
         self.rounds = S.bit_length() - 1
@@ -226,6 +254,7 @@ class TransformerLayerPair:
             return torch.empty(n, dtype=torch.int64, device=dev)
 
         self._side = self._fork = self._join = None  # party 1's stream (created on first use)
+        self._tab_stream = self._tab_fork = self._tab_done = None  # the truncation tables' stream
         wide = max(S * 3 * D, S * Dff)  # the widest public-weight product
         self.b = {
             "h": (buf(S * D), buf(S * D)), "acc": (buf(wide), buf(wide)), "xhat": buf(max(wide, H * S * S)),
@@ -333,6 +362,18 @@ class TransformerLayerPair:
         L = _lib.lib()
         b = self.b
         x = (d_x0, d_x1)
+        # the truncations' full-domain tables depend on their keys only: they
+        # are filled on a side stream while LayerNorm and the first matmuls run
+        main = stream if stream is not None else torch.cuda.current_stream(self.dev)
+        if self._tab_stream is None:
+            self._tab_stream = torch.cuda.Stream(device=self.dev)
+            self._tab_fork = torch.cuda.Event()
+            self._tab_done = torch.cuda.Event()
+        self._tab_fork.record(main)
+        self._tab_stream.wait_event(self._tab_fork)
+        for tr in self.tr.values():
+            tr.prepare(self.ctx, self._tab_stream, self._tab_done)
+        self._tab_done.record(self._tab_stream)
         # attention
         h = self.ln1.run(x[0], x[1], b["h"][0], b["h"][1], stream=stream)
         keep("h1", h, S * D)

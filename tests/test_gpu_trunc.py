@@ -304,3 +304,41 @@ def test_per_element_soa_flags_a_bad_key_header(ctx, torch_cuda):
         ctx.sync()
     ctx.sync()  # the status was cleared
     assert soa.numel() == n * (25 * 12 + 24)
+
+
+@pytest.mark.parametrize("f,n", [(12, 20_000), (15, 99_072)])
+def test_pair_tables_entry_matches(ctx, torch_cuda, oracle, prg_state, f, n):
+    """sufb200_trunc_tables_pair_dev + sufb200_trunc_bundle_eval_pair_tables_dev
+    (the GapARS carries' full-domain tables made apart from x^, then the main
+    pass) give the words of sufb200_trunc_bundle_eval_pair_dev."""
+    import ctypes as C
+
+    from suf_b200 import _lib
+
+    oracle.prg_init(prg_state)
+    rng = np.random.default_rng(31 + f + n)
+    x = signed_fixed(rng, n, 30)
+    r_in, descs, keys = trunc_material(oracle, KIND_GAPARS, f, 5 + n)
+    xhat = x + np.uint64(r_in)
+    dx = to_dev(torch_cuda, xhat)
+    pd = [to_product_desc(descs[p]) for p in (0, 1)]
+    dk = [[to_dev(torch_cuda, np.ascontiguousarray(k, dtype=np.uint8)) for k in keys[p]] for p in (0, 1)]
+    ptrs = [(C.c_void_p * 4)(*[k.data_ptr() for k in dk[p]], *([None] * (4 - len(dk[p])))) for p in (0, 1)]
+    sizes = [(C.c_size_t * 4)(*[k.numel() for k in dk[p]], *([0] * (4 - len(dk[p])))) for p in (0, 1)]
+    L = _lib.lib()
+    args = (C.byref(pd[0]), C.cast(ptrs[0], C.c_void_p), C.cast(sizes[0], C.c_void_p), C.byref(pd[1]),
+            C.cast(ptrs[1], C.c_void_p), C.cast(sizes[1], C.c_void_p))
+    ref = [torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda") for _ in (0, 1)]
+    _lib.check(L.sufb200_trunc_bundle_eval_pair_dev(ctx.h, *args, dx.data_ptr(), n, ref[0].data_ptr(),
+                                                    ref[1].data_ptr(), None))
+    nbytes = int(L.sufb200_trunc_tables_bytes(C.byref(pd[0]), C.byref(pd[1]), n))
+    assert nbytes > 0
+    tab = torch_cuda.empty(nbytes, dtype=torch_cuda.uint8, device="cuda")
+    _lib.check(L.sufb200_trunc_tables_pair_dev(ctx.h, *args, n, tab.data_ptr(), nbytes, None))
+    out = [torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda") for _ in (0, 1)]
+    _lib.check(L.sufb200_trunc_bundle_eval_pair_tables_dev(ctx.h, *args, tab.data_ptr(), dx.data_ptr(), n,
+                                                           out[0].data_ptr(), out[1].data_ptr(), None))
+    ctx.sync()
+    for p in (0, 1):
+        assert (from_dev(out[p]) == from_dev(ref[p])).all(), p
+    assert ((from_dev(out[0]) + from_dev(out[1])) == (x.view(np.int64) >> f).view(np.uint64)).all()
