@@ -1323,7 +1323,14 @@ def run_silu(args, ws, rank, local):
     engine_peak = ctx.probe_aes_engine()
     launches = 1 if pair else len(parties)
     kernel_ms = ms / launches
-    blocks = n * (len(parties) // launches) * ((fx["out_words"] + 1) // 2)  # one AES block per two words
+    # One AES block per two words; a dealt pair (one AES key, nonce and cut
+    # table for both parties) shares its keystream, so the pair launch
+    # encrypts each counter block once for both share rows.
+    k0, k1 = (np.asarray(k).view(np.uint8) for k in fx["keys"])
+    ivs = int(k0[4:8].view(np.uint32)[0])
+    shared = pair and all((k0[a:b] == k1[a:b]).all() for a, b in ((0, 8), (16, 24), (40, 216 + 8 * ivs)))
+    blocks_alg = n * (len(parties) // launches) * ((fx["out_words"] + 1) // 2)
+    blocks = n * ((fx["out_words"] + 1) // 2) if shared else blocks_alg
     hbm = n * (8 + 8 * r * (len(parties) // launches))
     out = None
     if rank == 0:
@@ -1346,9 +1353,13 @@ def run_silu(args, ws, rank, local):
                             "frac": round((blocks / engine_peak * 1e6) / (kernel_ms * 1e3), 4),
                             "peak": round(engine_peak / 1e9, 2), "traffic": hbm,
                             "kernel": "coeff_lut_pair_kernel" if pair else "coeff_lut_kernel",
-                            "work_model": f"{len(parties) // launches} x 393,216 elements per launch, one AES "
-                                          "block per two coefficient words (2 per element)",
-                            "note": "frac = AES-engine floor of the launch's blocks / measured launch time"},
+                            "work_model": f"{len(parties) // launches} x {n:,} elements per launch, one AES "
+                                          "block per two coefficient words (2 per element)"
+                                          + (", each block serving both parties' share rows (the dealt pair "
+                                             "shares its keystream)" if shared else ""),
+                            "blocks_executed": blocks, "blocks_per_party_sum": blocks_alg,
+                            "note": "frac = AES-engine floor of the blocks the launch executes / measured "
+                                    "launch time"},
                "cpu_baseline": cpu_silu_baseline(args, fx, xhat) if (ws == 1 and not args.no_cpu) else None,
                "clocks": clk.summary(), "gpu_launches": args.steps * launches, "reconstruction_ok": ok,
                "ms_per_step_all": [round(v, 4) for v in ms_steps]}

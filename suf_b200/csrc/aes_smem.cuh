@@ -234,6 +234,22 @@ SUFB200_DEV Blk aes_encrypt_smem_rk(const Blk& in, uint32_t lb, const uint32_t* 
   return o;
 }
 
+// One block under 44 round-key words held in registers (a row of at most
+// two words: one CTR block covers it).
+SUFB200_DEV Blk aes_encrypt1_rk(const Blk& in, uint32_t lb, const uint32_t (&rk)[44]) {
+  Blk a;
+#pragma unroll
+  for (int c = 0; c < 4; c++) a.w[c] = in.w[c] ^ rk[c];
+#pragma unroll
+  for (int r = 1; r < 10; r++) a = aes_round(a, lb, rk[4 * r + 0], rk[4 * r + 1], rk[4 * r + 2], rk[4 * r + 3]);
+  Blk o;
+  o.w[0] = aes_last_col<0>(a, lb, rk[40]);
+  o.w[1] = aes_last_col<1>(a, lb, rk[41]);
+  o.w[2] = aes_last_col<2>(a, lb, rk[42]);
+  o.w[3] = aes_last_col<3>(a, lb, rk[43]);
+  return o;
+}
+
 // Two independent blocks under the same 44 round-key words held in
 // registers, their rounds interleaved (two table-lookup chains in flight per
 // thread, no round-key loads) -- the CTR keystream of a short coefficient row.

@@ -218,10 +218,79 @@ __global__ void __launch_bounds__(kAesThreads, 1) interval_lut_kernel(const RefF
     lut_element(a, i, s_rk, s_tab, tab_in_smem, lb);
 }
 
+// True in every thread of the block when two staged broadcast LUT keys
+// produce one keystream: the same header, nonce, round keys and cut table.
+// The reference's dealer gives both parties of a LUT key one AES key and
+// nonce -- party 0's share words are the keystream itself, party 1's the
+// payload minus it (cuda/pfss_kernels.cu:545-719) -- so with both parties'
+// keys on one GPU each counter block is encrypted once for both outputs.
+__device__ __forceinline__ bool lut_keys_share_keystream(const RefFmtLaunch& a0, const RefFmtLaunch& a1,
+                                                         const uint32_t* rk0, const uint32_t* rk1) {
+  const uint64_t h0 = *reinterpret_cast<const uint64_t*>(a0.keys);
+  const uint64_t h1 = *reinterpret_cast<const uint64_t*>(a1.keys);
+  const uint32_t ivs = static_cast<uint32_t>(h0 >> 32), ow = static_cast<uint32_t>((h0 >> 16) & 0xFFFF);
+  const size_t need = 216u + 8u * (static_cast<size_t>(ivs) + 1 + static_cast<size_t>(ivs) * ow);
+  bool same = h0 == h1 && ivs != 0 && ow == static_cast<uint32_t>(a0.out_words) && need <= a0.key_bytes &&
+              need <= a1.key_bytes && a0.idx_base == a1.idx_base &&
+              *reinterpret_cast<const uint64_t*>(a0.keys + 16) == *reinterpret_cast<const uint64_t*>(a1.keys + 16);
+  if (same) {
+    for (int i = threadIdx.x; i < 44; i += blockDim.x) same = same && rk0[i] == rk1[i];
+    const uint64_t* c0 = reinterpret_cast<const uint64_t*>(a0.keys + 216);
+    const uint64_t* c1 = reinterpret_cast<const uint64_t*>(a1.keys + 216);
+    for (uint32_t i = threadIdx.x; i <= ivs; i += blockDim.x) same = same && c0[i] == c1[i];
+  }
+  return __syncthreads_and(same) != 0;
+}
+
+// Element i of both parties' gates when their keys share the keystream:
+// one interval search and one AES block per two words, two share rows.
+__device__ __forceinline__ void lut_element_shared(const RefFmtLaunch& a0, const RefFmtLaunch& a1, size_t i,
+                                                   const uint32_t* s_rk, const uint64_t* cuts, const uint64_t* pay0,
+                                                   const uint64_t* pay1, uint32_t lb) {
+  const uint64_t h = *reinterpret_cast<const uint64_t*>(a0.keys);
+  const int in_bits = static_cast<int>(h & 0xFFFF);
+  const int ow = static_cast<int>((h >> 16) & 0xFFFF);
+  const uint32_t ivs = static_cast<uint32_t>(h >> 32);
+  const uint32_t party0 = a0.keys[8], party1 = a1.keys[8];
+  const uint64_t nonce = *reinterpret_cast<const uint64_t*>(a0.keys + 16);
+  const uint64_t m = mask_bits(in_bits);
+  const uint64_t x = a0.xs[i] & m;
+  int iv = static_cast<int>(ivs) - 1;
+  if (ivs > 1) {
+    int lo = 0, hi = static_cast<int>(ivs);
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if ((cuts[mid] & m) <= x) lo = mid + 1; else hi = mid;
+    }
+    iv = lo - 1;
+    if (iv < 0) iv = 0;
+    if (iv >= static_cast<int>(ivs)) iv = static_cast<int>(ivs) - 1;
+  }
+  const uint64_t idx = a0.idx_base + i;
+  const uint64_t* row0 = pay0 + static_cast<size_t>(iv) * ow;
+  const uint64_t* row1 = pay1 + static_cast<size_t>(iv) * ow;
+  uint64_t* out0 = reinterpret_cast<uint64_t*>(a0.out) + i * static_cast<size_t>(ow);
+  uint64_t* out1 = reinterpret_cast<uint64_t*>(a1.out) + i * static_cast<size_t>(ow);
+  for (int w = 0; w < ow; w += 2) {
+    const uint64_t ctr = nonce ^ (idx << 32) ^ (static_cast<uint64_t>(iv) * static_cast<uint64_t>(ow) + w);
+    const Blk ks = aes_encrypt_smem_rk(ctr_block(ctr), lb, s_rk);
+    const uint64_t ks0 = (static_cast<uint64_t>(ks.w[1]) << 32) | ks.w[0];
+    const uint64_t ks1 = (static_cast<uint64_t>(ks.w[3]) << 32) | ks.w[2];
+    out0[w] = party0 == 0 ? ks0 : (row0[w] - ks0);
+    out1[w] = party1 == 0 ? ks0 : (row1[w] - ks0);
+    if (w + 1 < ow) {
+      out0[w + 1] = party0 == 0 ? ks1 : (row0[w + 1] - ks1);
+      out1[w + 1] = party1 == 0 ? ks1 : (row1[w + 1] - ks1);
+    }
+  }
+}
+
 // Both parties' broadcast-key gates over one x^ in one launch (elements
 // [0, n) party 0's key, [n, 2n) party 1's), spread over as many SMs as the
 // batch can use: the softmax and LayerNorm blocks' gates on 128 to 99,072
-// values, where one launch per party was latency-bound.
+// values, where one launch per party was latency-bound.  When the two keys
+// share their keystream the launch covers n items, each serving both
+// parties.
 __global__ void __launch_bounds__(kAesThreads, 1) interval_lut_pair_kernel(const RefFmtLaunch a0, const RefFmtLaunch a1) {
   extern __shared__ __align__(16) uint8_t smem[];
   if (!aes_layout_ok()) {
@@ -242,6 +311,17 @@ __global__ void __launch_bounds__(kAesThreads, 1) interval_lut_pair_kernel(const
   const uint32_t lb = lane_base();
   const size_t n = a0.n;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  if (lut_keys_share_keystream(a0, a1, s_rk0, s_rk1)) {
+    const uint32_t ivs = static_cast<uint32_t>(*reinterpret_cast<const uint64_t*>(a0.keys) >> 32);
+    const uint64_t* cuts = tab0 ? s_tab0 : reinterpret_cast<const uint64_t*>(a0.keys + 216);
+    const uint64_t* pay1 = (tab1 ? s_tab1 : reinterpret_cast<const uint64_t*>(a1.keys + 216)) + ivs + 1;
+    // 32-item warp chunks dealt round-robin over the blocks, so the n items
+    // spread over every block the launch sized for 2n.
+    const size_t first = ((static_cast<size_t>(threadIdx.x >> 5) * gridDim.x + blockIdx.x) << 5) + (threadIdx.x & 31u);
+    for (size_t i = first; i < n; i += stride)
+      lut_element_shared(a0, a1, i, s_rk0, cuts, cuts + ivs + 1, pay1, lb);
+    return;
+  }
   for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < 2 * n; g += stride) {
     if (g < n)
       lut_element(a0, g, s_rk0, s_tab0, tab0, lb);
@@ -310,8 +390,96 @@ __device__ __forceinline__ int coeff_interval(const CoeffSide& S, uint64_t xh) {
   return ub - 1 < 0 ? 0 : (ub - 1 >= static_cast<int>(S.ivs) ? static_cast<int>(S.ivs) - 1 : ub - 1);
 }
 
+// True in every thread of the block when the two staged sides produce one
+// keystream (same round keys, nonce, counter base, cuts and row shape; see
+// lut_keys_share_keystream for why the reference's dealt pairs do).
+__device__ __forceinline__ bool coeff_sides_share_keystream(const CoeffSide& S0, const CoeffSide& S1,
+                                                            const uint32_t* rk0, const uint32_t* rk1) {
+  bool same = S0.ok && S1.ok && S0.nonce == S1.nonce && S0.idx_base == S1.idx_base && S0.m == S1.m &&
+              S0.ivs == S1.ivs && S0.ow == S1.ow && S0.r == S1.r && S0.d1 == S1.d1;
+  if (same) {
+    for (int i = threadIdx.x; i < 44; i += blockDim.x) same = same && rk0[i] == rk1[i];
+    for (uint32_t i = threadIdx.x; i < S0.ivs; i += blockDim.x) same = same && S0.cuts[i] == S1.cuts[i];
+  }
+  return __syncthreads_and(same) != 0;
+}
+
+// Keystream word w (< 4) of an element from its CTR blocks k0 (words 0, 1)
+// and k1 (words 2, 3).
+__device__ __forceinline__ uint64_t ks_word(const Blk& k0, const Blk& k1, int w) {
+  const Blk& b = w < 2 ? k0 : k1;
+  return (w & 1) ? ((static_cast<uint64_t>(b.w[3]) << 32) | b.w[2]) : ((static_cast<uint64_t>(b.w[1]) << 32) | b.w[0]);
+}
+
+// Both parties' gates when their keys share the keystream: item i is
+// element i of both -- one interval search, one AES block per two words of
+// the row (a single block for rows of one or two words), two polynomial
+// rows over the party's share words.
+__device__ __forceinline__ void coeff_shared_items(const CoeffSide& S0, const CoeffSide& S1, const uint32_t* s_rk,
+                                                   const uint64_t* xs, size_t n, size_t first, size_t step,
+                                                   uint64_t xh_next, uint32_t lb) {
+  const int r = S0.r, d1 = S0.d1, ow = S0.ow;
+  const uint32_t party0 = S0.party, party1 = S1.party;
+  uint32_t rk[44];
+  if (ow <= 4) {
+#pragma unroll
+    for (int k = 0; k < 44; k++) rk[k] = s_rk[k];
+  }
+  for (size_t i = first; i < n; i += step) {
+    const uint64_t xh = xh_next;
+    const size_t in = i + step;
+    xh_next = in < n ? __ldg(xs + in) : 0ull;
+    const int iv = coeff_interval(S0, xh);
+    const uint64_t base = S0.nonce ^ ((S0.idx_base + i) << 32);
+    const uint64_t w0 = static_cast<uint64_t>(iv) * static_cast<uint64_t>(ow);
+    const uint64_t* row0 = S0.pay + static_cast<size_t>(iv) * ow;
+    const uint64_t* row1 = S1.pay + static_cast<size_t>(iv) * ow;
+    uint64_t* out0 = S0.out + i * static_cast<size_t>(r);
+    uint64_t* out1 = S1.out + i * static_cast<size_t>(r);
+    if (ow <= 4) {
+      Blk k0, k1;
+      if (ow <= 2)
+        k0 = k1 = aes_encrypt1_rk(ctr_block(base ^ w0), lb, rk);
+      else
+        aes_encrypt2_rk(ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2)), lb, rk, k0, k1);
+      int w = 0;
+      for (int j = 0; j < r; j++) {
+        uint64_t acc0 = 0, acc1 = 0, pw = 1;
+        for (int k = 0; k < d1; k++, w++) {
+          const uint64_t ksw = ks_word(k0, k1, w);
+          acc0 += (party0 == 0 ? ksw : (row0[w] - ksw)) * pw;
+          acc1 += (party1 == 0 ? ksw : (row1[w] - ksw)) * pw;
+          pw *= xh;
+        }
+        out0[j] = (acc0 + S0.r_out[j]) & S0.ring_mask;
+        out1[j] = (acc1 + S1.r_out[j]) & S1.ring_mask;
+      }
+      continue;
+    }
+    uint64_t ks0 = 0, ks1 = 0;
+    int w = 0;
+    for (int j = 0; j < r; j++) {
+      uint64_t acc0 = 0, acc1 = 0, pw = 1;
+      for (int k = 0; k < d1; k++, w++) {
+        if ((w & 1) == 0) {
+          const Blk ks = aes_encrypt_smem_rk(ctr_block(base ^ (w0 + w)), lb, s_rk);
+          ks0 = (static_cast<uint64_t>(ks.w[1]) << 32) | ks.w[0];
+          ks1 = (static_cast<uint64_t>(ks.w[3]) << 32) | ks.w[2];
+        }
+        const uint64_t ksw = (w & 1) ? ks1 : ks0;
+        acc0 += (party0 == 0 ? ksw : (row0[w] - ksw)) * pw;
+        acc1 += (party1 == 0 ? ksw : (row1[w] - ksw)) * pw;
+        pw *= xh;
+      }
+      out0[j] = (acc0 + S0.r_out[j]) & S0.ring_mask;
+      out1[j] = (acc1 + S1.r_out[j]) & S1.ring_mask;
+    }
+  }
+}
+
 // Elements of NP gates over one x^ (NP = 2: both parties; items [0, n) are
-// party 0's, [n, 2n) party 1's).  Warps take 32-item chunks dealt
+// party 0's, [n, 2n) party 1's, or, when the two keys share the keystream,
+// item i is element i of both).  Warps take 32-item chunks dealt
 // round-robin over the blocks (chunk = warp-in-block * grid + block), so the
 // last partial wave spreads over every SM while each warp's x^ loads stay
 // coalesced, and each lane loads its next item's x^ before working on the
@@ -344,6 +512,10 @@ __device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const Coe
     for (int q = 0; q < NP; q++)
       if (!s_side[q].ok) atomicOr(a0.status, kStatusBadKeyHeader);
   const uint32_t lb = lane_base();
+  if (NP == 2 && coeff_sides_share_keystream(s_side[0], s_side[1], s_rk, s_rk + 44)) {
+    coeff_shared_items(s_side[0], s_side[1], s_rk, xs, n, first, step, xh_next, lb);
+    return;
+  }
   uint32_t rk[44];
   int cur = -1;
   for (size_t g = first; g < total; g += step) {
@@ -367,23 +539,23 @@ __device__ __forceinline__ void coeff_lut_body(const RefFmtLaunch& a0, const Coe
     const int d1 = S.d1;
     if (S.ow <= 4) {
       // Rows of at most four words (configs[2]'s SiLU gate: r = 4, degree 0):
-      // both CTR blocks of an element at once, round keys in registers.
+      // both CTR blocks of an element at once (one for rows of at most two
+      // words), round keys in registers.
       if (q != cur) {
 #pragma unroll
         for (int k = 0; k < 44; k++) rk[k] = s_rk[44 * q + k];
         cur = q;
       }
       Blk k0, k1;
-      aes_encrypt2_rk(ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2)), lb, rk, k0, k1);
-      const uint64_t ks[4] = {(static_cast<uint64_t>(k0.w[1]) << 32) | k0.w[0],
-                              (static_cast<uint64_t>(k0.w[3]) << 32) | k0.w[2],
-                              (static_cast<uint64_t>(k1.w[1]) << 32) | k1.w[0],
-                              (static_cast<uint64_t>(k1.w[3]) << 32) | k1.w[2]};
+      if (S.ow <= 2)
+        k0 = k1 = aes_encrypt1_rk(ctr_block(base ^ w0), lb, rk);
+      else
+        aes_encrypt2_rk(ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2)), lb, rk, k0, k1);
       int w = 0;
       for (int j = 0; j < r; j++) {
         uint64_t acc = 0, pw = 1;
         for (int k = 0; k < d1; k++, w++) {
-          const uint64_t ksw = w == 0 ? ks[0] : (w == 1 ? ks[1] : (w == 2 ? ks[2] : ks[3]));
+          const uint64_t ksw = ks_word(k0, k1, w);
           const uint64_t c = party == 0 ? ksw : (row[w] - ksw);
           acc += c * pw;
           pw *= xh;

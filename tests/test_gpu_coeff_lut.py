@@ -91,11 +91,15 @@ def test_coeff_lut_rejects_shape_mismatch(ctx, torch_cuda, oracle):
         coeff_lut_eval(ctx, d["keys"][0][:300], dx, 4, 0)  # shorter than its table
 
 
-@pytest.mark.parametrize("r,degree,n", [(4, 0, 393_216), (1, 1, 20_001), (3, 2, 1), (8, 0, 77_777)])
-def test_coeff_lut_pair_equals_per_party(ctx, torch_cuda, oracle, r, degree, n):
+@pytest.mark.parametrize("r,degree,n,dealt", [(4, 0, 393_216, True), (1, 1, 20_001, True), (3, 2, 1, True),
+                                              (8, 0, 77_777, True), (1, 0, 5_003, True), (4, 0, 70_001, False),
+                                              (1, 1, 33, False)])
+def test_coeff_lut_pair_equals_per_party(ctx, torch_cuda, oracle, r, degree, n, dealt):
     """sufb200_coeff_lut_eval_pair: both parties in one launch give each
     party's sufb200_coeff_lut_eval output word for word (item counts that
-    split a warp chunk between the parties, a single element, several waves)."""
+    split a warp chunk between the parties, a single element, several waves).
+    A dealt pair (one seed and nonce) takes the launch's shared-keystream
+    path; keys of two different seeds take the per-party path."""
     from suf_b200.engine import coeff_lut_eval_pair
 
     rng = np.random.default_rng(7 * r + n)
@@ -105,7 +109,8 @@ def test_coeff_lut_pair_equals_per_party(ctx, torch_cuda, oracle, r, degree, n):
     cuts = np.concatenate([[np.uint64(0)], cuts, [np.uint64(0)]]).astype(np.uint64)
     pay = rng.integers(0, 2**63, ivs * ow, dtype=np.uint64) * np.uint64(2)
     seed = oracle.seed_from_id(55 + r, 7)
-    keys = [oracle.interval_key(p, 55 + r, 64, ow, cuts, pay, seed) for p in (0, 1)]
+    seeds = (seed, seed if dealt else oracle.seed_from_id(56 + r, 7))
+    keys = [oracle.interval_key(p, 55 + r, 64, ow, cuts, pay, seeds[p]) for p in (0, 1)]
     xh = rng.integers(0, 2**63, n, dtype=np.uint64) * np.uint64(2) + rng.integers(0, 2, n, dtype=np.uint64)
     dx = to_dev(torch_cuda, xh)
     r_out = rng.integers(0, 2**63, (2, r), dtype=np.uint64)
