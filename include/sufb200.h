@@ -191,26 +191,32 @@ int sufb200_trunc_bundle_eval_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc
                                        const size_t* key_bytes1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
                                        uint64_t* d_y1, void* stream);
 
-/* The same pair in two steps, for bundles whose queries all take their full
- * domain at this batch size (the f-bit carries of GapARS truncations:
- * 2^in_bits <= the shared-prefix budget, n at least the shared-prefix size).
- * The tables hold every query's evaluations over its whole domain and do not
- * depend on x^, so they can be computed on another stream while x^ is still
- * being produced (the layer computes its truncations' tables at its start).
- * sufb200_trunc_tables_bytes: the tables' size, 0 when the pair does not
- * qualify; sufb200_trunc_tables_pair_dev fills them (d_tables 256-byte
- * aligned); sufb200_trunc_bundle_eval_pair_tables_dev runs the main pass over
- * x^ against them (same outputs as sufb200_trunc_bundle_eval_pair_dev). */
-size_t sufb200_trunc_tables_bytes(const sufb200_trunc_desc* desc0, const sufb200_trunc_desc* desc1, size_t n);
-int sufb200_trunc_tables_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* d_keys0,
-                                  const size_t* key_bytes0, const sufb200_trunc_desc* desc1,
-                                  const uint8_t* const* d_keys1, const size_t* key_bytes1, size_t n, void* d_tables,
-                                  size_t tables_bytes, void* stream);
+/* The same pair in two steps, for bundles whose queries are all at most 16
+ * bits wide (the f-bit carries of GapARS truncations), at any batch size.
+ * A party's tables hold each query's evaluations over its whole domain and
+ * depend on that party's keys only, not on x^, so they can be computed on
+ * another stream while x^ is still being produced, or once per key set.
+ * sufb200_trunc_tables_bytes: one party's table size (0 when a query is
+ * wider than 16 bits); sufb200_trunc_tables_dev fills one party's tables
+ * (d_tables 256-byte aligned); sufb200_trunc_bundle_eval_pair_tables_dev
+ * runs both parties' main pass over x^ against them (the same outputs as
+ * sufb200_trunc_bundle_eval_pair_dev, one launch, no tree walk). */
+size_t sufb200_trunc_tables_bytes(const sufb200_trunc_desc* desc);
+int sufb200_trunc_tables_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* d_keys,
+                             const size_t* key_bytes, void* d_tables, size_t tables_bytes, void* stream);
+/* Many bundles' tables (either party's) in as few launches as the keys
+ * allow (16 keys per launch): descs[count], d_keys / key_bytes [count][4]
+ * (the layout of the softmax / LayerNorm party structs' trunc_keys),
+ * d_tables / tables_bytes [count]; a NULL d_tables[i] skips bundle i. */
+int sufb200_trunc_tables_many_dev(sufb200_ctx ctx, int count, const sufb200_trunc_desc* descs,
+                                  const uint8_t* const* d_keys, const size_t* key_bytes, void* const* d_tables,
+                                  const size_t* tables_bytes, void* stream);
 int sufb200_trunc_bundle_eval_pair_tables_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0,
                                               const uint8_t* const* d_keys0, const size_t* key_bytes0,
-                                              const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
-                                              const size_t* key_bytes1, const void* d_tables, const uint64_t* d_xhat,
-                                              size_t n, uint64_t* d_y0, uint64_t* d_y1, void* stream);
+                                              const void* d_tables0, const sufb200_trunc_desc* desc1,
+                                              const uint8_t* const* d_keys1, const size_t* key_bytes1,
+                                              const void* d_tables1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
+                                              uint64_t* d_y1, void* stream);
 
 /* Host-buffer form: xhat, y (and bools, may be NULL) in host memory; copies
  * in and out inside the call and returns when y is on the host.  Replaces
@@ -593,6 +599,10 @@ typedef struct sufb200_softmax_party {
   const uint8_t* trunc_keys[SUFB200_SOFTMAX_TRUNCS][4];    /* myl7 key of each query: host, or device */
   size_t trunc_key_bytes[SUFB200_SOFTMAX_TRUNCS][4];
   int32_t trunc_keys_device;  /* nonzero: trunc_keys are device pointers (resident; no copy per call) */
+  /* device, or NULL: bundle k's tables (sufb200_trunc_tables_dev over this
+   * party's device keys).  With device keys and both parties' tables set,
+   * the block evaluates bundle k against them instead of walking its keys. */
+  const void* trunc_tables[SUFB200_SOFTMAX_TRUNCS];
 } sufb200_softmax_party;
 
 /* nn::SoftmaxBlockTask (include/nn/softmax_block_task.hpp) for BOTH parties
@@ -628,6 +638,7 @@ typedef struct sufb200_layernorm_party {
   const uint8_t* trunc_keys[SUFB200_LAYERNORM_TRUNCS][4]; /* host, or device (trunc_keys_device) */
   size_t trunc_key_bytes[SUFB200_LAYERNORM_TRUNCS][4];
   int32_t trunc_keys_device;  /* nonzero: trunc_keys are device pointers */
+  const void* trunc_tables[SUFB200_LAYERNORM_TRUNCS]; /* device or NULL, as in sufb200_softmax_party */
 } sufb200_layernorm_party;
 
 /* runtime::LayerNormTask with RsqrtTask (include/runtime/phase_tasks.hpp:

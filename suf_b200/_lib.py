@@ -77,11 +77,11 @@ _SIGS = {
                                             _sz, _vp, _vp, _vp]),
     "sufb200_trunc_bundle_eval_pair_dev": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, C.POINTER(TruncDesc), _vp, _vp,
                                                 _vp, _sz, _vp, _vp, _vp]),
-    "sufb200_trunc_tables_bytes": (_sz, [C.POINTER(TruncDesc), C.POINTER(TruncDesc), _sz]),
-    "sufb200_trunc_tables_pair_dev": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, C.POINTER(TruncDesc), _vp, _vp, _sz,
-                                           _vp, _sz, _vp]),
-    "sufb200_trunc_bundle_eval_pair_tables_dev": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, C.POINTER(TruncDesc), _vp,
-                                                       _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
+    "sufb200_trunc_tables_bytes": (_sz, [C.POINTER(TruncDesc)]),
+    "sufb200_trunc_tables_dev": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp]),
+    "sufb200_trunc_tables_many_dev": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "sufb200_trunc_bundle_eval_pair_tables_dev": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, C.POINTER(TruncDesc),
+                                                       _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "sufb200_trunc_bundle_eval_host": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp]),
     "sufb200_trunc_bundle_eval_noalloc": (_i, [_vp, C.POINTER(TruncDesc), _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "sufb200_trunc_gen_elem": (_i, [_i, _i, _u64, _sz, C.POINTER(TruncDesc), C.POINTER(TruncDesc), _vp, _vp, _vp,

@@ -234,6 +234,40 @@ SUFB200_DEV Blk aes_encrypt_smem_rk(const Blk& in, uint32_t lb, const uint32_t* 
   return o;
 }
 
+// NB independent blocks under the 11 round keys in shared memory (one
+// 16-byte broadcast load per round for all NB), their rounds interleaved:
+// NB table-lookup chains in flight per thread and no round-key registers.
+// The middle rounds stay a loop (one round of NB blocks is about 64 * NB
+// instructions): fully unrolled, four blocks are some 40 KB of code, which
+// a warp streams through the instruction cache once per element.
+template <int NB>
+SUFB200_DEV void aes_encrypt_n_sk(Blk (&b)[NB], uint32_t lb, const uint4* rk) {
+  const uint4 k0 = rk[0];
+#pragma unroll
+  for (int j = 0; j < NB; j++) {
+    b[j].w[0] ^= k0.x;
+    b[j].w[1] ^= k0.y;
+    b[j].w[2] ^= k0.z;
+    b[j].w[3] ^= k0.w;
+  }
+#pragma unroll 1
+  for (int r = 1; r < 10; r++) {
+    const uint4 kr = rk[r];
+#pragma unroll
+    for (int j = 0; j < NB; j++) b[j] = aes_round(b[j], lb, kr.x, kr.y, kr.z, kr.w);
+  }
+  const uint4 kl = rk[10];
+#pragma unroll
+  for (int j = 0; j < NB; j++) {
+    Blk o;
+    o.w[0] = aes_last_col<0>(b[j], lb, kl.x);
+    o.w[1] = aes_last_col<1>(b[j], lb, kl.y);
+    o.w[2] = aes_last_col<2>(b[j], lb, kl.z);
+    o.w[3] = aes_last_col<3>(b[j], lb, kl.w);
+    b[j] = o;
+  }
+}
+
 // One block under 44 round-key words held in registers (a row of at most
 // two words: one CTR block covers it).
 SUFB200_DEV Blk aes_encrypt1_rk(const Blk& in, uint32_t lb, const uint32_t (&rk)[44]) {

@@ -9,6 +9,7 @@
 #include <mutex>
 #include <random>
 #include <string>
+#include <algorithm>
 #include <vector>
 
 #include "host_aes.hpp"
@@ -781,45 +782,54 @@ namespace {
 
 // Checks of a pair of bundles whose keys are device pointers; fills a0 / a1's
 // descriptors and key pointers.
+// One party's bundle with its keys on the device: desc and key sizes checked.
+int dev_launch(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* d_keys,
+               const size_t* key_bytes, sufb200::TruncLaunch& a) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (int rc = check_bundle_desc(desc, d_keys, key_bytes)) return rc;
+  a = sufb200::TruncLaunch{};
+  a.desc = *desc;
+  for (int q = 0; q < desc->nq; q++) {
+    const int nb = desc->q_bits[q];
+    if (nb < 1 || nb > 64) return fail(SUFB200_ERR_INVALID, "query in_bits out of range");
+    if (!d_keys[q] || key_bytes[q] != sufb200::host::myl7_key_bytes(nb, 8))
+      return fail(SUFB200_ERR_KEY, "query " + std::to_string(q) + ": key size does not match an 8-byte myl7 key");
+    a.key[q] = d_keys[q];
+  }
+  return SUFB200_OK;
+}
+
 int dev_pair_launches(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* d_keys0,
                       const size_t* key_bytes0, const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
                       const size_t* key_bytes1, sufb200::TruncLaunch& a0, sufb200::TruncLaunch& a1) {
-  if (int rc = check_ctx(ctx, true)) return rc;
-  if (int rc = check_bundle_desc(desc0, d_keys0, key_bytes0)) return rc;
-  if (int rc = check_bundle_desc(desc1, d_keys1, key_bytes1)) return rc;
+  if (int rc = dev_launch(ctx, desc0, d_keys0, key_bytes0, a0)) return rc;
+  if (int rc = dev_launch(ctx, desc1, d_keys1, key_bytes1, a1)) return rc;
   if (desc0->party != 0 || desc1->party != 1) return fail(SUFB200_ERR_INVALID, "desc0 / desc1 must be parties 0 / 1");
-  a0 = sufb200::TruncLaunch{};
-  a1 = sufb200::TruncLaunch{};
-  a0.desc = *desc0;
-  a1.desc = *desc1;
-  for (int p = 0; p < 2; p++) {
-    const sufb200_trunc_desc* d = p ? desc1 : desc0;
-    const uint8_t* const* dk = p ? d_keys1 : d_keys0;
-    const size_t* kb = p ? key_bytes1 : key_bytes0;
-    for (int q = 0; q < d->nq; q++) {
-      const int nb = d->q_bits[q];
-      if (nb < 1 || nb > 64) return fail(SUFB200_ERR_INVALID, "query in_bits out of range");
-      if (!dk[q] || kb[q] != sufb200::host::myl7_key_bytes(nb, 8))
-        return fail(SUFB200_ERR_KEY, "query " + std::to_string(q) + ": key size does not match an 8-byte myl7 key");
-      (p ? a1 : a0).key[q] = dk[q];
-    }
-  }
   return SUFB200_OK;
 }
 
 // Layout of a pair's full-domain tables: the range record, then query q's
 // 2^in_bits entries of 32 bytes, party 0's queries first.
-size_t tables_layout(const sufb200_trunc_desc* d0, const sufb200_trunc_desc* d1, size_t n, size_t off[8]) {
-  if (!d0 || !d1 || n < prefix_min_n() || d0->nq <= 0 || d1->nq <= 0 || d0->nq > 4 || d1->nq > 4) return 0;
-  const uint32_t kmax = sufb200::prefix_budget(n);
-  const sufb200_trunc_desc both[2] = {*d0, *d1};
-  if (!narrow_queries(both, 2, kmax)) return 0;
+// Tables of one party's bundle whose queries are all at most kTablesMaxBits
+// wide: the range word, then each query's 2^bits frontier entries (32
+// bytes each).  Returns the size (0 when the bundle does not qualify), the
+// entries' offsets and the frontier budget (2^widest bits, at least 256),
+// whatever the batch size.
+constexpr int kTablesMaxBits = 16;
+
+size_t tables_layout(const sufb200_trunc_desc* d, size_t off[4], uint32_t* kmax) {
+  if (!d || d->nq <= 0 || d->nq > 4) return 0;
+  int widest = 0;
+  for (int q = 0; q < d->nq; q++) {
+    if (d->q_bits[q] < 1 || d->q_bits[q] > kTablesMaxBits) return 0;
+    widest = d->q_bits[q] > widest ? d->q_bits[q] : widest;
+  }
+  *kmax = (1u << widest) < 256u ? 256u : (1u << widest);
   size_t at = kAccBytes;
-  for (int p = 0; p < 2; p++)
-    for (int q = 0; q < both[p].nq; q++) {
-      off[4 * p + q] = at;
-      at += 32ull << both[p].q_bits[q];
-    }
+  for (int q = 0; q < d->nq; q++) {
+    off[q] = at;
+    at += 32ull << d->q_bits[q];
+  }
   return at;
 }
 
@@ -838,58 +848,84 @@ int sufb200_trunc_bundle_eval_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc
   return trunc_pair_core(ctx, a0, a1, d_xhat, n, d_y0, d_y1, as_stream(stream));
 }
 
-size_t sufb200_trunc_tables_bytes(const sufb200_trunc_desc* desc0, const sufb200_trunc_desc* desc1, size_t n) {
-  size_t off[8];
-  return tables_layout(desc0, desc1, n, off);
+size_t sufb200_trunc_tables_bytes(const sufb200_trunc_desc* desc) {
+  size_t off[4];
+  uint32_t kmax = 0;
+  return tables_layout(desc, off, &kmax);
 }
 
-int sufb200_trunc_tables_pair_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0, const uint8_t* const* d_keys0,
-                                  const size_t* key_bytes0, const sufb200_trunc_desc* desc1,
-                                  const uint8_t* const* d_keys1, const size_t* key_bytes1, size_t n, void* d_tables,
-                                  size_t tables_bytes, void* stream) {
-  sufb200::TruncLaunch a0, a1;
-  if (int rc = dev_pair_launches(ctx, desc0, d_keys0, key_bytes0, desc1, d_keys1, key_bytes1, a0, a1)) return rc;
-  size_t off[8] = {};
-  const size_t need = tables_layout(desc0, desc1, n, off);
-  if (need == 0) return fail(SUFB200_ERR_UNSUPPORTED, "not a pair of full-domain bundles at shared-prefix size");
-  if (!d_tables || tables_bytes < need || (reinterpret_cast<uintptr_t>(d_tables) & 255u))
-    return fail(SUFB200_ERR_INVALID, "tables buffer null, unaligned (256 bytes) or smaller than sufb200_trunc_tables_bytes");
-  cudaStream_t st = as_stream(stream);
-  uint8_t* base = static_cast<uint8_t*>(d_tables);
-  auto* acc = reinterpret_cast<sufb200::RangeAcc*>(base);
-  const uint32_t kmax = sufb200::prefix_budget(n);
-  sufb200::FrontierBatch fb{};
-  int k = 0;
-  for (int p = 0; p < 2; p++) {
-    const sufb200::TruncLaunch& a = p ? a1 : a0;
-    for (int q = 0; q < a.desc.nq; q++, k++)
-      fb.q[k] = sufb200::FrontierLaunch{a.key[q], a.desc.q_bits[q], 8, acc, kmax,
-                                        reinterpret_cast<sufb200::FrontierEntry*>(base + off[4 * p + q]), ctx->d_t0,
-                                        ctx->d_status};
+int sufb200_trunc_tables_many_dev(sufb200_ctx ctx, int count, const sufb200_trunc_desc* descs,
+                                  const uint8_t* const* d_keys, const size_t* key_bytes, void* const* d_tables,
+                                  const size_t* tables_bytes, void* stream) {
+  if (int rc = check_ctx(ctx, true)) return rc;
+  if (count < 0 || (count > 0 && (!descs || !d_keys || !key_bytes || !d_tables || !tables_bytes)))
+    return fail(SUFB200_ERR_INVALID, "bad tables list");
+  std::vector<sufb200::FrontierLaunch> work;
+  for (int i = 0; i < count; i++) {
+    if (!d_tables[i]) continue;
+    sufb200::TruncLaunch a;
+    if (int rc = dev_launch(ctx, &descs[i], d_keys + 4 * i, key_bytes + 4 * i, a)) return rc;
+    size_t off[4] = {};
+    uint32_t kmax = 0;
+    const size_t need = tables_layout(&descs[i], off, &kmax);
+    if (need == 0)
+      return fail(SUFB200_ERR_UNSUPPORTED,
+                  "bundle " + std::to_string(i) + ": no query, or a query wider than the tables' 16 bits");
+    if (tables_bytes[i] < need || (reinterpret_cast<uintptr_t>(d_tables[i]) & 255u))
+      return fail(SUFB200_ERR_INVALID, "bundle " + std::to_string(i) +
+                                           ": tables buffer unaligned (256 bytes) or smaller than sufb200_trunc_tables_bytes");
+    uint8_t* base = static_cast<uint8_t*>(d_tables[i]);
+    auto* acc = reinterpret_cast<sufb200::RangeAcc*>(base);
+    for (int q = 0; q < a.desc.nq; q++)
+      work.push_back(sufb200::FrontierLaunch{a.key[q], a.desc.q_bits[q], 8, acc, kmax,
+                                             reinterpret_cast<sufb200::FrontierEntry*>(base + off[q]), ctx->d_t0,
+                                             ctx->d_status, acc});
   }
-  fb.nq = k;
-  cudaError_t e = sufb200::set_full_range(acc, st);
-  if (e == cudaSuccess) e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
-  return e == cudaSuccess ? SUFB200_OK : cuda_fail(e, "pair tables launch");
+  cudaStream_t st = as_stream(stream);
+  for (size_t at = 0; at < work.size(); at += sufb200::kFrontierMaxKeys) {
+    sufb200::FrontierBatch fb{};
+    fb.nq = static_cast<int>(std::min<size_t>(sufb200::kFrontierMaxKeys, work.size() - at));
+    for (int q = 0; q < fb.nq; q++) fb.q[q] = work[at + q];
+    const cudaError_t e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
+    if (e != cudaSuccess) return cuda_fail(e, "tables launch");
+  }
+  return SUFB200_OK;
+}
+
+int sufb200_trunc_tables_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc, const uint8_t* const* d_keys,
+                             const size_t* key_bytes, void* d_tables, size_t tables_bytes, void* stream) {
+  if (!desc || !d_keys || !key_bytes) return fail(SUFB200_ERR_INVALID, "null descriptor or key list");
+  if (!d_tables) return fail(SUFB200_ERR_INVALID, "null tables buffer");
+  const uint8_t* keys[4] = {nullptr, nullptr, nullptr, nullptr};
+  size_t sizes[4] = {0, 0, 0, 0};
+  for (int q = 0; q < desc->nq && q < 4; q++) {
+    keys[q] = d_keys[q];
+    sizes[q] = key_bytes[q];
+  }
+  return sufb200_trunc_tables_many_dev(ctx, 1, desc, keys, sizes, &d_tables, &tables_bytes, stream);
 }
 
 int sufb200_trunc_bundle_eval_pair_tables_dev(sufb200_ctx ctx, const sufb200_trunc_desc* desc0,
                                               const uint8_t* const* d_keys0, const size_t* key_bytes0,
-                                              const sufb200_trunc_desc* desc1, const uint8_t* const* d_keys1,
-                                              const size_t* key_bytes1, const void* d_tables, const uint64_t* d_xhat,
-                                              size_t n, uint64_t* d_y0, uint64_t* d_y1, void* stream) {
+                                              const void* d_tables0, const sufb200_trunc_desc* desc1,
+                                              const uint8_t* const* d_keys1, const size_t* key_bytes1,
+                                              const void* d_tables1, const uint64_t* d_xhat, size_t n, uint64_t* d_y0,
+                                              uint64_t* d_y1, void* stream) {
   sufb200::TruncLaunch a0, a1;
   if (int rc = dev_pair_launches(ctx, desc0, d_keys0, key_bytes0, desc1, d_keys1, key_bytes1, a0, a1)) return rc;
-  size_t off[8] = {};
-  if (tables_layout(desc0, desc1, n, off) == 0)
-    return fail(SUFB200_ERR_UNSUPPORTED, "not a pair of full-domain bundles at shared-prefix size");
-  if (!d_tables || !d_xhat || !d_y0 || !d_y1 || !aligned8(d_xhat) || !aligned8(d_y0) || !aligned8(d_y1))
+  size_t off[2][4] = {};
+  uint32_t kmax[2] = {0, 0};
+  if (tables_layout(desc0, off[0], &kmax[0]) == 0 || tables_layout(desc1, off[1], &kmax[1]) == 0)
+    return fail(SUFB200_ERR_UNSUPPORTED, "bundle has a query wider than the tables' 16 bits");
+  if (n == 0) return SUFB200_OK;
+  if (!d_tables0 || !d_tables1 || !d_xhat || !d_y0 || !d_y1 || !aligned8(d_xhat) || !aligned8(d_y0) ||
+      !aligned8(d_y1))
     return fail(SUFB200_ERR_INVALID, "null or misaligned device pointer");
-  const uint8_t* base = static_cast<const uint8_t*>(d_tables);
+  const uint8_t* base[2] = {static_cast<const uint8_t*>(d_tables0), static_cast<const uint8_t*>(d_tables1)};
   sufb200::FrontierEntry* F[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   for (int p = 0; p < 2; p++)
     for (int q = 0; q < (p ? a1 : a0).desc.nq; q++)
-      F[4 * p + q] = reinterpret_cast<sufb200::FrontierEntry*>(const_cast<uint8_t*>(base) + off[4 * p + q]);
+      F[4 * p + q] = reinterpret_cast<sufb200::FrontierEntry*>(const_cast<uint8_t*>(base[p]) + off[p][q]);
   for (sufb200::TruncLaunch* a : {&a0, &a1}) {
     a->xhat = d_xhat;
     a->n = n;
@@ -899,8 +935,11 @@ int sufb200_trunc_bundle_eval_pair_tables_dev(sufb200_ctx ctx, const sufb200_tru
   }
   a0.y = d_y0;
   a1.y = d_y1;
+  // Both tables hold the full-domain range word; every query's table covers
+  // its whole domain under either budget, so the larger one serves both.
   const cudaError_t e = sufb200::launch_trunc_bundle_prefix_pair(
-      ctx, a0, a1, reinterpret_cast<const sufb200::RangeAcc*>(base), sufb200::prefix_budget(n), F, as_stream(stream));
+      ctx, a0, a1, reinterpret_cast<const sufb200::RangeAcc*>(base[0]), kmax[0] > kmax[1] ? kmax[0] : kmax[1], F,
+      as_stream(stream));
   return e == cudaSuccess ? SUFB200_OK : cuda_fail(e, "pair bundle launch");
 }
 

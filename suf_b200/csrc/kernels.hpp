@@ -160,11 +160,15 @@ struct FrontierLaunch {
   FrontierEntry* out;  // device [kmax]
   const uint32_t* t0;
   uint32_t* status;
+  // Non-null: plan over every value (the range set_full_range writes)
+  // without reading acc, and store that range here for the main pass that
+  // later reads these tables.
+  RangeAcc* full;
 };
 // The frontier tables of up to eight keys over one batch (one bundle's
 // queries, or both parties' bundles), built in one launch (all keys share
 // the range accumulator and the status word of q[0]).
-constexpr int kFrontierMaxKeys = 8;
+constexpr int kFrontierMaxKeys = 16;
 struct FrontierBatch {
   FrontierLaunch q[kFrontierMaxKeys];
   int nq;

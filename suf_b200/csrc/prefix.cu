@@ -133,7 +133,21 @@ __global__ void __launch_bounds__(kAesThreads, 1) frontier_kernel(const PrgParam
 #pragma unroll
     for (int q = 0; q < kFrontierMaxKeys; q++) {
       if (q >= nq) continue;
-      const Plan p = make_plan(*b.q[q].acc, b.q[q].in_bits, b.q[q].kmax);
+      RangeAcc r;
+      if (b.q[q].full) {
+        r.min_b = 0ull;
+        r.max_b = ~0ull;
+        r.pivot = 0ull;
+        r.pad = 0ull;
+        if (blockIdx.x == 0) {
+          b.q[q].full->min_b = r.min_b;
+          b.q[q].full->max_b = r.max_b;
+          b.q[q].full->pivot = r.pivot;
+        }
+      } else {
+        r = *b.q[q].acc;
+      }
+      const Plan p = make_plan(r, b.q[q].in_bits, b.q[q].kmax);
       const int h = expand_height(p);
       fk[q].plan = p;
       fk[q].out = b.q[q].out;

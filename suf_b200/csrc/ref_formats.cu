@@ -407,23 +407,79 @@ __device__ __forceinline__ bool coeff_sides_share_keystream(const CoeffSide& S0,
 // Keystream word w (< 4) of an element from its CTR blocks k0 (words 0, 1)
 // and k1 (words 2, 3).
 __device__ __forceinline__ uint64_t ks_word(const Blk& k0, const Blk& k1, int w) {
-  const Blk& b = w < 2 ? k0 : k1;
-  return (w & 1) ? ((static_cast<uint64_t>(b.w[3]) << 32) | b.w[2]) : ((static_cast<uint64_t>(b.w[1]) << 32) | b.w[0]);
+  const uint32_t lo = w == 0 ? k0.w[0] : (w == 1 ? k0.w[2] : (w == 2 ? k1.w[0] : k1.w[2]));
+  const uint32_t hi = w == 0 ? k0.w[1] : (w == 1 ? k0.w[3] : (w == 2 ? k1.w[1] : k1.w[3]));
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
+// One element's two share rows from its keystream blocks k0 (words 0, 1)
+// and k1 (words 2, 3): the polynomial over x^ of each party's share words.
+__device__ __forceinline__ void coeff_emit_shared(const CoeffSide& S0, const CoeffSide& S1, size_t i, int iv,
+                                                  uint64_t xh, const Blk& k0, const Blk& k1) {
+  const int r = S0.r, d1 = S0.d1, ow = S0.ow;
+  const uint32_t party0 = S0.party, party1 = S1.party;
+  const uint64_t* row0 = S0.pay + static_cast<size_t>(iv) * ow;
+  const uint64_t* row1 = S1.pay + static_cast<size_t>(iv) * ow;
+  uint64_t* out0 = S0.out + i * static_cast<size_t>(r);
+  uint64_t* out1 = S1.out + i * static_cast<size_t>(r);
+  int w = 0;
+  for (int j = 0; j < r; j++) {
+    uint64_t acc0 = 0, acc1 = 0, pw = 1;
+    for (int k = 0; k < d1; k++, w++) {
+      const uint64_t ksw = ks_word(k0, k1, w);
+      acc0 += (party0 == 0 ? ksw : (row0[w] - ksw)) * pw;
+      acc1 += (party1 == 0 ? ksw : (row1[w] - ksw)) * pw;
+      pw *= xh;
+    }
+    out0[j] = (acc0 + S0.r_out[j]) & S0.ring_mask;
+    out1[j] = (acc1 + S1.r_out[j]) & S1.ring_mask;
+  }
 }
 
 // Both parties' gates when their keys share the keystream: item i is
 // element i of both -- one interval search, one AES block per two words of
-// the row (a single block for rows of one or two words), two polynomial
-// rows over the party's share words.
+// the row, two polynomial rows over the party's share words.  Rows of one
+// or two words (one CTR block) take two elements per iteration (i and
+// i + step, two chains in flight, round keys read from shared memory);
+// rows of three or four words one element with both blocks interleaved
+// (round keys in registers, fully unrolled: that measured faster for the
+// SiLU gate's four-word rows than two elements of four rolled chains).
 __device__ __forceinline__ void coeff_shared_items(const CoeffSide& S0, const CoeffSide& S1, const uint32_t* s_rk,
                                                    const uint64_t* xs, size_t n, size_t first, size_t step,
                                                    uint64_t xh_next, uint32_t lb) {
   const int r = S0.r, d1 = S0.d1, ow = S0.ow;
   const uint32_t party0 = S0.party, party1 = S1.party;
-  uint32_t rk[44];
+  if (ow <= 2) {
+    const uint4* rk4 = reinterpret_cast<const uint4*>(s_rk);
+    uint64_t xa_next = xh_next, xb_next = first + step < n ? __ldg(xs + first + step) : 0ull;
+    for (size_t i = first; i < n; i += 2 * step) {
+      const size_t i2 = i + step;
+      const uint64_t xa = xa_next, xb = xb_next;
+      xa_next = i + 2 * step < n ? __ldg(xs + i + 2 * step) : 0ull;
+      xb_next = i + 3 * step < n ? __ldg(xs + i + 3 * step) : 0ull;
+      const int iva = coeff_interval(S0, xa), ivb = coeff_interval(S0, xb);
+      Blk k[2] = {ctr_block((S0.nonce ^ ((S0.idx_base + i) << 32)) ^ (static_cast<uint64_t>(iva) * ow)),
+                  ctr_block((S0.nonce ^ ((S0.idx_base + i2) << 32)) ^ (static_cast<uint64_t>(ivb) * ow))};
+      aes_encrypt_n_sk<2>(k, lb, rk4);
+      coeff_emit_shared(S0, S1, i, iva, xa, k[0], k[0]);
+      if (i2 < n) coeff_emit_shared(S0, S1, i2, ivb, xb, k[1], k[1]);
+    }
+    return;
+  }
   if (ow <= 4) {
+    uint32_t rk[44];
 #pragma unroll
     for (int k = 0; k < 44; k++) rk[k] = s_rk[k];
+    for (size_t i = first; i < n; i += step) {
+      const uint64_t xh = xh_next;
+      xh_next = i + step < n ? __ldg(xs + i + step) : 0ull;
+      const int iv = coeff_interval(S0, xh);
+      const uint64_t base = S0.nonce ^ ((S0.idx_base + i) << 32), w0 = static_cast<uint64_t>(iv) * ow;
+      Blk k0, k1;
+      aes_encrypt2_rk(ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2)), lb, rk, k0, k1);
+      coeff_emit_shared(S0, S1, i, iv, xh, k0, k1);
+    }
+    return;
   }
   for (size_t i = first; i < n; i += step) {
     const uint64_t xh = xh_next;
@@ -436,26 +492,6 @@ __device__ __forceinline__ void coeff_shared_items(const CoeffSide& S0, const Co
     const uint64_t* row1 = S1.pay + static_cast<size_t>(iv) * ow;
     uint64_t* out0 = S0.out + i * static_cast<size_t>(r);
     uint64_t* out1 = S1.out + i * static_cast<size_t>(r);
-    if (ow <= 4) {
-      Blk k0, k1;
-      if (ow <= 2)
-        k0 = k1 = aes_encrypt1_rk(ctr_block(base ^ w0), lb, rk);
-      else
-        aes_encrypt2_rk(ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2)), lb, rk, k0, k1);
-      int w = 0;
-      for (int j = 0; j < r; j++) {
-        uint64_t acc0 = 0, acc1 = 0, pw = 1;
-        for (int k = 0; k < d1; k++, w++) {
-          const uint64_t ksw = ks_word(k0, k1, w);
-          acc0 += (party0 == 0 ? ksw : (row0[w] - ksw)) * pw;
-          acc1 += (party1 == 0 ? ksw : (row1[w] - ksw)) * pw;
-          pw *= xh;
-        }
-        out0[j] = (acc0 + S0.r_out[j]) & S0.ring_mask;
-        out1[j] = (acc1 + S1.r_out[j]) & S1.ring_mask;
-      }
-      continue;
-    }
     uint64_t ks0 = 0, ks1 = 0;
     int w = 0;
     for (int j = 0; j < r; j++) {

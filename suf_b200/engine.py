@@ -34,6 +34,39 @@ def _stream_ptr(stream) -> int | None:
     return int(stream.cuda_stream) or None
 
 
+class TruncTables:
+    """Device tables of a list of truncation bundles (either party's), each
+    bundle given as (desc, key pointers [4], key sizes [4]) with its keys on
+    the device; bundles with a query wider than 16 bits (or none) get no
+    tables.  fill(stream) evaluates every table in as few launches as the
+    keys allow (sufb200_trunc_tables_many_dev); ptr(i) is bundle i's table
+    buffer or None."""
+
+    def __init__(self, bundles, dev):
+        import torch
+
+        L = _lib.lib()
+        n = len(bundles)
+        self._descs = (TruncDesc * n)(*[b[0] for b in bundles])
+        self._keys = (C.c_void_p * (4 * n))(*[k for b in bundles for k in list(b[1])[:4]])
+        self._ksz = (C.c_size_t * (4 * n))(*[k for b in bundles for k in list(b[2])[:4]])
+        sizes = [int(L.sufb200_trunc_tables_bytes(C.byref(self._descs[i]))) for i in range(n)]
+        self._bufs = [torch.empty(b, dtype=torch.uint8, device=dev) if b else None for b in sizes]
+        self._ptrs = (C.c_void_p * n)(*[t.data_ptr() if t is not None else None for t in self._bufs])
+        self._bytes = (C.c_size_t * n)(*sizes)
+        self.count = n
+
+    def ptr(self, i: int):
+        return self._ptrs[i]
+
+    def any(self) -> bool:
+        return any(t is not None for t in self._bufs)
+
+    def fill(self, ctx, stream=None):
+        check(_lib.lib().sufb200_trunc_tables_many_dev(ctx.h, self.count, self._descs, self._keys, self._ksz,
+                                                       self._ptrs, self._bytes, _stream_ptr(stream)))
+
+
 def host_mt19937_64(seed: int, n: int) -> np.ndarray:
     out = np.empty(n, dtype=np.uint64)
     check(_lib.lib().sufb200_host_mt19937_64(C.c_uint64(seed), _np_ptr(out) if n else None, n))

@@ -36,7 +36,7 @@ import numpy as np
 
 from . import _lib
 from ._lib import TruncDesc, check
-from .engine import Context, _stream_ptr, _t_ptr, interval_lut_key, seed_from_id
+from .engine import Context, TruncTables, _stream_ptr, _t_ptr, interval_lut_key, seed_from_id
 from .softmax import TRUNC_GAPARS, LayerNormBlock, SoftmaxBlock, load_tables, masked_lut_table
 
 LAYER_TABLES = Path(__file__).resolve().parent / "tables" / "layer_suf_f12.json"
@@ -98,9 +98,9 @@ def _rand64(rng) -> int:
 
 class _Trunc:
     """One GapARS truncation bundle for both parties: descriptors, myl7 keys
-    (host) and the split of its input mask r_in = r[0] + r[1]."""
+    (on the device) and the split of its input mask r_in = r[0] + r[1]."""
 
-    def __init__(self, ctx: Context, rng, frac_bits: int, dev=None, n: int = 0):
+    def __init__(self, ctx: Context, rng, frac_bits: int, dev=None):
         import torch
 
         r_in, d0, d1, thetas = Context.trunc_gen(TRUNC_GAPARS, frac_bits, int(rng.integers(1, 2**63)))
@@ -117,33 +117,25 @@ class _Trunc:
         nq = int(d0.nq)
         self.kptr = [(C.c_void_p * 4)(*[k.data_ptr() for k in ks], *([None] * (4 - nq))) for ks in self.keys]
         self.ksz = [(C.c_size_t * 4)(*[k.numel() for k in ks], *([0] * (4 - nq))) for ks in self.keys]
-        # full-domain tables of the carry queries (x^-independent) when the
-        # bundle's n qualifies: computed by prepare() off the critical path
-        self.n = n
-        nbytes = int(_lib.lib().sufb200_trunc_tables_bytes(C.byref(d0), C.byref(d1), n)) if n else 0
-        self.tables = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
-        self.ready = None  # the event prepare() recorded
+        # (TruncTables, party 0's index, party 1's) when the layer keeps this
+        # bundle's full-domain tables; `ready` is the event after their fill
+        self.tables = None
+        self.ready = None
 
-    def prepare(self, ctx: Context, stream, event):
-        """Fill the tables on `stream`; `event` is recorded after them."""
-        if self.tables is None:
-            return
-        check(_lib.lib().sufb200_trunc_tables_pair_dev(
-            ctx.h, C.byref(self.desc[0]), C.cast(self.kptr[0], C.c_void_p), C.cast(self.ksz[0], C.c_void_p),
-            C.byref(self.desc[1]), C.cast(self.kptr[1], C.c_void_p), C.cast(self.ksz[1], C.c_void_p), self.n,
-            _t_ptr(self.tables), self.tables.numel(), _stream_ptr(stream)))
-        self.ready = event
+    def bundles(self):
+        return [(self.desc[p], self.kptr[p], self.ksz[p]) for p in (0, 1)]
 
     def eval_pair(self, ctx: Context, d_xhat, d_y0, d_y1, stream):
-        if self.tables is not None and self.ready is not None and d_xhat.numel() == self.n:
+        if self.tables is not None and self.ready is not None:
             import torch
 
+            T, i0, i1 = self.tables
             (stream if stream is not None else torch.cuda.current_stream()).wait_event(self.ready)
             check(_lib.lib().sufb200_trunc_bundle_eval_pair_tables_dev(
                 ctx.h, C.byref(self.desc[0]), C.cast(self.kptr[0], C.c_void_p), C.cast(self.ksz[0], C.c_void_p),
-                C.byref(self.desc[1]), C.cast(self.kptr[1], C.c_void_p), C.cast(self.ksz[1], C.c_void_p),
-                _t_ptr(self.tables), _t_ptr(d_xhat), d_xhat.numel(), _t_ptr(d_y0), _t_ptr(d_y1),
-                _stream_ptr(stream)))
+                T.ptr(i0), C.byref(self.desc[1]), C.cast(self.kptr[1], C.c_void_p),
+                C.cast(self.ksz[1], C.c_void_p), T.ptr(i1), _t_ptr(d_xhat), d_xhat.numel(),
+                _t_ptr(d_y0), _t_ptr(d_y1), _stream_ptr(stream)))
             self.ready = None
             return
         check(_lib.lib().sufb200_trunc_bundle_eval_pair_dev(
@@ -241,9 +233,17 @@ class TransformerLayerPair:
         self.ln1 = LayerNormBlock(ctx, S, D, seed=int(rng.integers(1, 2**62)), tables=sm_tab)
         self.ln2 = LayerNormBlock(ctx, S, D, seed=int(rng.integers(1, 2**62)), tables=sm_tab)
         self.softmax = SoftmaxBlock(ctx, [S] * (H * S), seed=int(rng.integers(1, 2**62)), tables=sm_tab)
-        sizes = {"qkv": S * 3 * D, "scores": H * S * S, "pv": S * D, "o": S * D, "ff1": S * Dff, "ff2": S * D}
-        self.tr = {name: _Trunc(ctx, rng, fk, dev, sizes[name])
+        self.tr = {name: _Trunc(ctx, rng, fk, dev)
                    for name, fk in (("qkv", f), ("scores", f + 3), ("pv", f), ("o", f), ("ff1", f), ("ff2", f))}
+        # the truncations' full-domain tables, in the three groups the layer
+        # fills them in (one launch per group)
+        self._tab_groups = []
+        for names in (("qkv", "scores"), ("pv", "o"), ("ff1", "ff2")):
+            T = TruncTables([b for nm in names for b in self.tr[nm].bundles()], dev)
+            for j, nm in enumerate(names):
+                if T.ptr(2 * j) and T.ptr(2 * j + 1):
+                    self.tr[nm].tables = (T, 2 * j, 2 * j + 1)
+            self._tab_groups.append((names, T))
         self.trip_s = _Triples(rng, dev, H, S, Dh, S, transposed=True)
         self.trip_pv = _Triples(rng, dev, H, S, S, Dh, transposed=False)
         self.rounds = S.bit_length() - 1
@@ -254,7 +254,7 @@ class TransformerLayerPair:
             return torch.empty(n, dtype=torch.int64, device=dev)
 
         self._side = self._fork = self._join = None  # party 1's stream (created on first use)
-        self._tab_stream = self._tab_fork = self._tab_done = None  # the truncation tables' stream
+        self._tab_stream = self._tab_fork = self._tab_ev = None  # the truncation tables' stream
         wide = max(S * 3 * D, S * Dff)  # the widest public-weight product
         self.b = {
             "h": (buf(S * D), buf(S * D)), "acc": (buf(wide), buf(wide)), "xhat": buf(max(wide, H * S * S)),
@@ -363,17 +363,28 @@ class TransformerLayerPair:
         b = self.b
         x = (d_x0, d_x1)
         # the truncations' full-domain tables depend on their keys only: they
-        # are filled on a side stream while LayerNorm and the first matmuls run
+        # are filled on a side stream, in the order the layer needs them,
+        # while LayerNorm and the first matmuls run (the first LayerNorm's own
+        # bundles walk their keys: it starts the layer)
         main = stream if stream is not None else torch.cuda.current_stream(self.dev)
         if self._tab_stream is None:
             self._tab_stream = torch.cuda.Stream(device=self.dev)
             self._tab_fork = torch.cuda.Event()
-            self._tab_done = torch.cuda.Event()
+            self._tab_ev = [torch.cuda.Event() for _ in range(5)]
+        ts, ev = self._tab_stream, self._tab_ev
         self._tab_fork.record(main)
-        self._tab_stream.wait_event(self._tab_fork)
-        for tr in self.tr.values():
-            tr.prepare(self.ctx, self._tab_stream, self._tab_done)
-        self._tab_done.record(self._tab_stream)
+        ts.wait_event(self._tab_fork)
+        g = self._tab_groups
+        for (grp, block), e in zip(((g[0], None), (None, self.softmax), (g[1], None), (None, self.ln2),
+                                    (g[2], None)), ev):
+            if grp is not None and grp[1].any():
+                grp[1].fill(self.ctx, ts)
+                for name in grp[0]:
+                    if self.tr[name].tables is not None:
+                        self.tr[name].ready = e
+            if block is not None:
+                block.prepare_tables(ts)
+            e.record(ts)
         # attention
         h = self.ln1.run(x[0], x[1], b["h"][0], b["h"][1], stream=stream)
         keep("h1", h, S * D)
@@ -384,6 +395,7 @@ class TransformerLayerPair:
         keep("scores", b["s"], H * S * S)
         self._rowmax_diff(b["s"], b["t"], stream)
         keep("t", b["t"], H * S * S)
+        main.wait_event(ev[1])
         self.softmax.run(b["t"][0], b["t"][1], b["p"][0], b["p"][1], stream=stream)
         keep("probs", b["p"], H * S * S)
         self._beaver_trunc(b["p"], 0, S * S, S, b["qkv"], 2 * D, Dh, 3 * D, False, self.trip_pv, S, S, Dh, Dh, D,
@@ -394,6 +406,7 @@ class TransformerLayerPair:
         check(L.sufb200_add_pair(_t_ptr(x[0]), _t_ptr(b["a"][0]), _t_ptr(x[1]), _t_ptr(b["a"][1]),
                                  _t_ptr(b["x2"][0]), _t_ptr(b["x2"][1]), S * D, _stream_ptr(stream)))
         # MLP
+        main.wait_event(ev[3])
         h = self.ln2.run(b["x2"][0], b["x2"][1], b["h"][0], b["h"][1], stream=stream)
         keep("h2", h, S * D)
         self._matmul_trunc(h, "ff1", D, Dff, self.tr["ff1"], b["f1"], stream)
@@ -442,20 +455,19 @@ class TransformerLayerPair:
         g._sufb200_keep = tmp  # the graph's intermediate buffers live as long as it does
         return g
 
-    # launches of our kernels per layer (counted from the calls above; the
-    # truncations take the shared-prefix path when n >= 16384: one frontier
-    # and one main launch for both parties, no range pass since their f-bit
-    # queries take full-domain tables; else one pair launch)
+    # launches of our kernels per layer (counted from the calls above).  Every
+    # truncation bundle with tables is one launch against them; the side
+    # stream fills the tables with one frontier launch per 16 keys: three for
+    # the layer's own six bundles (three groups of 8 keys), two
+    # each for the softmax block (28 keys) and the second LayerNorm block
+    # (24 keys), whose four and one element-level bundles then skip their
+    # own frontier launch.
     def launches(self) -> int:
         d = self.dims
-        lf = 19 * 2  # two LayerNorm blocks (see bench.py's LAYERNORM_LAUNCHES)
-        sm = 22  # the softmax block (see bench.py's SOFTMAX_LAUNCHES)
-        def trunc(n):
-            return 2 if n >= 16384 else 1
-        mm = 0
-        for n in (d.S * 3 * d.D, d.S * d.D, d.S * d.Dff, d.S * d.D):  # qkv, o, ff1, ff2
-            mm += 2 * 2 + 1 + trunc(n)  # two ring matmuls (pre-pass + GEMM each), open, truncation
-        bv = 2 * (1 + trunc(d.H * d.S * d.S))  # scores, pv (the pv truncation is S*D elements)
+        ln = 19 + (19 - 1) + 2  # LayerNorm 1 walks its keys; LayerNorm 2 against tables (bench.py's LAYERNORM_LAUNCHES)
+        sm = 22 - 4 + 2  # the softmax block against tables (bench.py's SOFTMAX_LAUNCHES)
+        mm = 4 * (2 * 2 + 1 + 1)  # qkv, o, ff1, ff2: two ring matmuls (pre-pass + GEMM each), open, truncation
+        bv = 2 * (1 + 1)  # scores, pv: the Beaver open, the truncation
         relu = self.rounds * 3 + 1  # open, the pair gate launch, update per round; the final max-difference
         gelu = 1 + 1  # open, the pair gate launch
-        return lf + sm + mm + bv + relu + gelu + 2
+        return ln + sm + mm + bv + relu + gelu + 2 + 3

@@ -49,6 +49,7 @@ class SoftmaxParty(C.Structure):
         ("trunc_keys", (C.c_void_p * 4) * N_TRUNCS),
         ("trunc_key_bytes", (C.c_size_t * 4) * N_TRUNCS),
         ("trunc_keys_device", C.c_int32),
+        ("trunc_tables", C.c_void_p * N_TRUNCS),
     ]
 
 
@@ -105,6 +106,16 @@ def _triples(rng: np.random.Generator, n: int):
     return out
 
 
+def _block_tables(parts, dev):
+    """Both parties' tables of a block's truncation bundles (TruncTables
+    over party 0's bundles, then party 1's)."""
+    from .engine import TruncTables
+
+    K = len(parts[0].trunc)
+    return TruncTables([(parts[p].trunc[k], parts[p].trunc_keys[k], parts[p].trunc_key_bytes[k])
+                        for p in (0, 1) for k in range(K)], dev)
+
+
 class SoftmaxBlock:
     """Dealer material for one softmax block shape (rows, ragged row lengths)
     for both parties, resident on the context's device, and the block call.
@@ -122,8 +133,9 @@ class SoftmaxBlock:
         self.rows = int(lens.size)
         off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
         self.n = int(off[-1])
-        dev = torch.device("cuda", ctx.device if hasattr(ctx, "device") else 0)
+        dev = self._dev = torch.device("cuda", ctx.device if hasattr(ctx, "device") else 0)
         self._keep = []  # host key arrays and device tensors the structs point at
+        self._tables = None  # prepare_tables()
 
         def dcopy(a: np.ndarray):
             t = torch.from_numpy(np.ascontiguousarray(a).view(np.int64) if a.dtype == np.uint64 else a).to(dev)
@@ -186,6 +198,19 @@ class SoftmaxBlock:
             parts[p].trunc_keys_device = 1
         self.parts = parts
 
+    def prepare_tables(self, stream=None):
+        """Fill the tables of every truncation bundle with queries of at most
+        16 bits on `stream` (they depend on the keys only) and switch those
+        bundles to table evaluation: block calls ordered after this on the
+        device read them instead of walking the keys."""
+        if self._tables is None:
+            self._tables = _block_tables(self.parts, self._dev)
+        self._tables.fill(self.ctx, stream)
+        K = len(self.parts[0].trunc)
+        for p in (0, 1):
+            for k in range(K):
+                self.parts[p].trunc_tables[k] = self._tables.ptr(p * K + k)
+
     def run(self, d_t0, d_t1, d_prob0=None, d_prob1=None, stream=None):
         """Both parties' shares of the packed max-differences t (Q f, int64
         tensors of n words on the device) -> shares of the packed
@@ -227,6 +252,7 @@ class LayerNormParty(C.Structure):
         ("trunc_keys", (C.c_void_p * 4) * N_LN_TRUNCS),
         ("trunc_key_bytes", (C.c_size_t * 4) * N_LN_TRUNCS),
         ("trunc_keys_device", C.c_int32),
+        ("trunc_tables", C.c_void_p * N_LN_TRUNCS),
     ]
 
 
@@ -248,8 +274,9 @@ class LayerNormBlock:
         n = self.n = self.rows * self.cols
         self.inv_len = int(round((1 << f) / cols))
         self.eps = int(round((1 << f) / 1024))
-        dev = torch.device("cuda", ctx.device)
+        dev = self._dev = torch.device("cuda", ctx.device)
         self._keep = []
+        self._tables = None  # prepare_tables()
 
         def dcopy(a: np.ndarray):
             t = torch.from_numpy(np.ascontiguousarray(a).view(np.int64) if a.dtype == np.uint64 else a).to(dev)
@@ -301,6 +328,19 @@ class LayerNormBlock:
         for p in (0, 1):
             parts[p].trunc_keys_device = 1
         self.parts = parts
+
+    def prepare_tables(self, stream=None):
+        """Fill the tables of every truncation bundle with queries of at most
+        16 bits on `stream` (they depend on the keys only) and switch those
+        bundles to table evaluation: block calls ordered after this on the
+        device read them instead of walking the keys."""
+        if self._tables is None:
+            self._tables = _block_tables(self.parts, self._dev)
+        self._tables.fill(self.ctx, stream)
+        K = len(self.parts[0].trunc)
+        for p in (0, 1):
+            for k in range(K):
+                self.parts[p].trunc_tables[k] = self._tables.ptr(p * K + k)
 
     def run(self, d_x0, d_x1, d_out0=None, d_out1=None, stream=None):
         """Both parties' shares of x (rows * cols, Q f, int64 tensors on the

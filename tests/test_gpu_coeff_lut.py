@@ -92,8 +92,8 @@ def test_coeff_lut_rejects_shape_mismatch(ctx, torch_cuda, oracle):
 
 
 @pytest.mark.parametrize("r,degree,n,dealt", [(4, 0, 393_216, True), (1, 1, 20_001, True), (3, 2, 1, True),
-                                              (8, 0, 77_777, True), (1, 0, 5_003, True), (4, 0, 70_001, False),
-                                              (1, 1, 33, False)])
+                                              (8, 0, 77_777, True), (1, 0, 5_003, True), (3, 0, 40_003, True),
+                                              (1, 2, 9_999, True), (4, 0, 70_001, False), (1, 1, 33, False)])
 def test_coeff_lut_pair_equals_per_party(ctx, torch_cuda, oracle, r, degree, n, dealt):
     """sufb200_coeff_lut_eval_pair: both parties in one launch give each
     party's sufb200_coeff_lut_eval output word for word (item counts that

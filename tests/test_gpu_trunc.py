@@ -306,11 +306,12 @@ def test_per_element_soa_flags_a_bad_key_header(ctx, torch_cuda):
     assert soa.numel() == n * (25 * 12 + 24)
 
 
-@pytest.mark.parametrize("f,n", [(12, 20_000), (15, 99_072)])
+@pytest.mark.parametrize("f,n", [(12, 20_000), (15, 99_072), (12, 128), (12, 1_536), (3, 1_000), (16, 5_001)])
 def test_pair_tables_entry_matches(ctx, torch_cuda, oracle, prg_state, f, n):
-    """sufb200_trunc_tables_pair_dev + sufb200_trunc_bundle_eval_pair_tables_dev
-    (the GapARS carries' full-domain tables made apart from x^, then the main
-    pass) give the words of sufb200_trunc_bundle_eval_pair_dev."""
+    """sufb200_trunc_tables_dev (each party's full-domain tables of the GapARS
+    carries, made apart from x^) + sufb200_trunc_bundle_eval_pair_tables_dev
+    give the words of sufb200_trunc_bundle_eval_pair_dev, at element-level
+    and row-level batch sizes."""
     import ctypes as C
 
     from suf_b200 import _lib
@@ -326,19 +327,47 @@ def test_pair_tables_entry_matches(ctx, torch_cuda, oracle, prg_state, f, n):
     ptrs = [(C.c_void_p * 4)(*[k.data_ptr() for k in dk[p]], *([None] * (4 - len(dk[p])))) for p in (0, 1)]
     sizes = [(C.c_size_t * 4)(*[k.numel() for k in dk[p]], *([0] * (4 - len(dk[p])))) for p in (0, 1)]
     L = _lib.lib()
-    args = (C.byref(pd[0]), C.cast(ptrs[0], C.c_void_p), C.cast(sizes[0], C.c_void_p), C.byref(pd[1]),
-            C.cast(ptrs[1], C.c_void_p), C.cast(sizes[1], C.c_void_p))
+    side = [(C.byref(pd[p]), C.cast(ptrs[p], C.c_void_p), C.cast(sizes[p], C.c_void_p)) for p in (0, 1)]
     ref = [torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda") for _ in (0, 1)]
-    _lib.check(L.sufb200_trunc_bundle_eval_pair_dev(ctx.h, *args, dx.data_ptr(), n, ref[0].data_ptr(),
+    _lib.check(L.sufb200_trunc_bundle_eval_pair_dev(ctx.h, *side[0], *side[1], dx.data_ptr(), n, ref[0].data_ptr(),
                                                     ref[1].data_ptr(), None))
-    nbytes = int(L.sufb200_trunc_tables_bytes(C.byref(pd[0]), C.byref(pd[1]), n))
-    assert nbytes > 0
-    tab = torch_cuda.empty(nbytes, dtype=torch_cuda.uint8, device="cuda")
-    _lib.check(L.sufb200_trunc_tables_pair_dev(ctx.h, *args, n, tab.data_ptr(), nbytes, None))
+    tabs = []
+    for p in (0, 1):
+        nbytes = int(L.sufb200_trunc_tables_bytes(C.byref(pd[p])))
+        assert nbytes > 0
+        tabs.append(torch_cuda.empty(nbytes, dtype=torch_cuda.uint8, device="cuda"))
+        _lib.check(L.sufb200_trunc_tables_dev(ctx.h, *side[p], tabs[p].data_ptr(), nbytes, None))
     out = [torch_cuda.empty(n, dtype=torch_cuda.int64, device="cuda") for _ in (0, 1)]
-    _lib.check(L.sufb200_trunc_bundle_eval_pair_tables_dev(ctx.h, *args, tab.data_ptr(), dx.data_ptr(), n,
-                                                           out[0].data_ptr(), out[1].data_ptr(), None))
+    _lib.check(L.sufb200_trunc_bundle_eval_pair_tables_dev(ctx.h, *side[0], tabs[0].data_ptr(), *side[1],
+                                                           tabs[1].data_ptr(), dx.data_ptr(), n, out[0].data_ptr(),
+                                                           out[1].data_ptr(), None))
     ctx.sync()
     for p in (0, 1):
         assert (from_dev(out[p]) == from_dev(ref[p])).all(), p
     assert ((from_dev(out[0]) + from_dev(out[1])) == (x.view(np.int64) >> f).view(np.uint64)).all()
+
+
+def test_tables_reject_wide_queries(ctx, torch_cuda, oracle, prg_state):
+    """A bundle with a query wider than 16 bits has no tables: size 0 and
+    SUFB200_ERR_UNSUPPORTED from both tables entries."""
+    import ctypes as C
+
+    from suf_b200 import SufB200Error, _lib
+
+    oracle.prg_init(prg_state)
+    _, descs, keys = trunc_material(oracle, KIND_GAPARS, 24, 9)
+    pd = [to_product_desc(descs[p]) for p in (0, 1)]
+    dk = [[to_dev(torch_cuda, np.ascontiguousarray(k, dtype=np.uint8)) for k in keys[p]] for p in (0, 1)]
+    ptrs = [(C.c_void_p * 4)(*[k.data_ptr() for k in dk[p]], *([None] * (4 - len(dk[p])))) for p in (0, 1)]
+    sizes = [(C.c_size_t * 4)(*[k.numel() for k in dk[p]], *([0] * (4 - len(dk[p])))) for p in (0, 1)]
+    L = _lib.lib()
+    assert int(L.sufb200_trunc_tables_bytes(C.byref(pd[0]))) == 0
+    buf = torch_cuda.empty(1 << 20, dtype=torch_cuda.uint8, device="cuda")
+    side = [(C.byref(pd[p]), C.cast(ptrs[p], C.c_void_p), C.cast(sizes[p], C.c_void_p)) for p in (0, 1)]
+    with pytest.raises(SufB200Error):
+        _lib.check(L.sufb200_trunc_tables_dev(ctx.h, *side[0], buf.data_ptr(), buf.numel(), None))
+    dx = to_dev(torch_cuda, np.zeros(8, dtype=np.uint64))
+    with pytest.raises(SufB200Error):
+        _lib.check(L.sufb200_trunc_bundle_eval_pair_tables_dev(ctx.h, *side[0], buf.data_ptr(), *side[1],
+                                                               buf.data_ptr(), dx.data_ptr(), 8, dx.data_ptr(),
+                                                               dx.data_ptr(), None))

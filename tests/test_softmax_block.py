@@ -139,3 +139,32 @@ def test_layernorm_block_against_reference_protocol_rows(ctx, torch_cuda):
     assert sane.sum() >= 12
     assert (np.abs(got[sane] - ref[sane]) <= 4).all()
     assert (got[sane] == ref[sane]).all(axis=1).sum() >= 0.7 * sane.sum()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("which,shape", [("softmax", (12, 128)), ("softmax", (2, 200)), ("layernorm", (128, 768)),
+                                         ("layernorm", (7, 100))])
+def test_block_tables_give_the_walks_shares(ctx, torch_cuda, which, shape):
+    """prepare_tables(): the blocks' truncation bundles evaluated against
+    their full-domain tables (sufb200_trunc_bundle_eval_pair_tables_dev)
+    give each party the share words of the key walks, bundle by bundle."""
+    from suf_b200.softmax import LayerNormBlock, SoftmaxBlock
+    from tests.conftest import from_dev, to_dev
+
+    rng = np.random.default_rng(sum(shape) + len(which))
+    if which == "softmax":
+        heads, length = shape
+        lens = np.arange(heads * length) % length + 1
+        blk = SoftmaxBlock(ctx, lens, seed=heads + length)
+        v = rng.integers(0, 16 << 12, int(lens.sum()), dtype=np.uint64)
+    else:
+        blk = LayerNormBlock(ctx, *shape, seed=sum(shape))
+        v = np.round(rng.normal(0.0, 1.0, shape[0] * shape[1]) * 4096).astype(np.int64).view(np.uint64)
+    s0, s1 = (to_dev(torch_cuda, a) for a in _shares(rng, v))
+    walk = [from_dev(o, np.uint64) for o in blk.run(s0, s1)]
+    blk.prepare_tables()
+    assert blk._tables.any(), "no bundle qualified for tables"
+    tab = [from_dev(o, np.uint64) for o in blk.run(s0, s1)]
+    ctx.sync()
+    for p in (0, 1):
+        assert (tab[p] == walk[p]).all(), p
