@@ -937,7 +937,7 @@ int sufb200_trunc_bundle_eval_pair_tables_dev(sufb200_ctx ctx, const sufb200_tru
   a1.y = d_y1;
   // Both tables hold the full-domain range word; every query's table covers
   // its whole domain under either budget, so the larger one serves both.
-  const cudaError_t e = sufb200::launch_trunc_bundle_prefix_pair(
+  const cudaError_t e = sufb200::launch_trunc_bundle_lookup_pair(
       ctx, a0, a1, reinterpret_cast<const sufb200::RangeAcc*>(base[0]), kmax[0] > kmax[1] ? kmax[0] : kmax[1], F,
       as_stream(stream));
   return e == cudaSuccess ? SUFB200_OK : cuda_fail(e, "pair bundle launch");

@@ -184,6 +184,11 @@ cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaun
                                        uint32_t kmax, FrontierEntry* const F[4], cudaStream_t st);
 // Both parties' bundles over one x^ in one main pass: F[0..3] party 0's
 // queries, F[4..7] party 1's.
+// Both parties' bundles against full-domain tables (every query's plan at
+// its whole domain): lookups only, no keys or AES tables.
+cudaError_t launch_trunc_bundle_lookup_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
+                                            const RangeAcc* acc, uint32_t kmax, FrontierEntry* const F[8],
+                                            cudaStream_t st);
 cudaError_t launch_trunc_bundle_prefix_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
                                             const RangeAcc* acc, uint32_t kmax, FrontierEntry* const F[8],
                                             cudaStream_t st);

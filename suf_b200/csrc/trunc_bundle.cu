@@ -384,6 +384,48 @@ __global__ void __launch_bounds__(kAesThreads, 1)
   }
 }
 
+// Both parties' bundles over one x^ against full-domain tables (every
+// query planned at its whole domain): an element's predicate share is one
+// 32-byte frontier entry per query, so the pass needs neither the keys nor
+// the AES tables and runs as a plain memory pass, several blocks per SM.
+__global__ void __launch_bounds__(256) trunc_bundle_lookup_pair_kernel(const __grid_constant__ TruncLaunch a0,
+                                                                       const __grid_constant__ TruncLaunch a1,
+                                                                       const RangeAcc* acc, uint32_t kmax,
+                                                                       const FrontierSet fs) {
+  __shared__ Plan s_plan[8];
+  pdl_wait();  // x^ (and the tables) come from earlier work
+  pdl_trigger();
+  if (threadIdx.x < 8) {
+    const int p = threadIdx.x >> 2, q = threadIdx.x & 3;
+    const sufb200_trunc_desc& d = p ? a1.desc : a0.desc;
+    s_plan[threadIdx.x] = q < d.nq ? make_plan(*acc, d.q_bits[q], kmax) : Plan{0, 1, 0};
+  }
+  __syncthreads();
+  const size_t n = a0.n, total = 2 * n;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t g = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total; g += stride) {
+    const int slot = g >= n ? 1 : 0;
+    const size_t i = slot ? g - n : g;
+    const TruncLaunch& a = slot ? a1 : a0;
+    const sufb200_trunc_desc& d = a.desc;
+    const uint64_t xh = a.xhat[i];
+    uint64_t pr[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      if (q >= d.nq) break;
+      const int nb = d.q_bits[q];
+      const Plan P = s_plan[4 * slot + q];
+      const uint32_t idx = plan_index(P, xh & nbit_mask(nb), nb);
+      if (idx < P.count && P.depth == static_cast<uint32_t>(nb)) {
+        pr[q] = __ldg(&fs.F[4 * slot + q][idx].v);
+      } else {  // not a full-domain table: the caller's tables do not match the bundle
+        atomicOr(a.status, kStatusBadArgument);
+      }
+    }
+    combine_store(d, xh, pr, a.y, a.bools, i);
+  }
+}
+
 }  // namespace
 
 namespace {
@@ -695,6 +737,16 @@ cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaun
   const int grid = static_cast<int>(want < static_cast<size_t>(ctx->sm_count) ? (want ? want : 1) : ctx->sm_count);
   return launch_pdl(trunc_bundle_prefix_kernel<1>, grid, kAesThreads, ctx->aes_dyn_bytes, st, ctx->prg, a, a, acc,
                     kmax, fs);
+}
+
+cudaError_t launch_trunc_bundle_lookup_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
+                                            const RangeAcc* acc, uint32_t kmax, FrontierEntry* const F[8],
+                                            cudaStream_t st) {
+  if (a0.n != a1.n || a0.xhat != a1.xhat) return cudaErrorInvalidValue;
+  FrontierSet fs{{F[0], F[1], F[2], F[3], F[4], F[5], F[6], F[7]}};
+  const size_t want = (2 * a0.n + 255) / 256, cap = static_cast<size_t>(ctx->sm_count) * 8;
+  const int grid = static_cast<int>(want < cap ? (want ? want : 1) : cap);
+  return launch_pdl(trunc_bundle_lookup_pair_kernel, grid, 256u, 0, st, a0, a1, acc, kmax, fs);
 }
 
 cudaError_t launch_trunc_bundle_prefix_pair(const sufb200_ctx_s* ctx, const TruncLaunch& a0, const TruncLaunch& a1,
