@@ -603,6 +603,10 @@ typedef struct sufb200_softmax_party {
    * party's device keys).  With device keys and both parties' tables set,
    * the block evaluates bundle k against them instead of walking its keys. */
   const void* trunc_tables[SUFB200_SOFTMAX_TRUNCS];
+  /* cudaEvent_t or NULL: the block makes its stream wait for this event
+   * right before it reads bundle k's tables (tables filled on another
+   * stream while the block's earlier steps run).  Read from party 0. */
+  void* trunc_ready[SUFB200_SOFTMAX_TRUNCS];
 } sufb200_softmax_party;
 
 /* nn::SoftmaxBlockTask (include/nn/softmax_block_task.hpp) for BOTH parties
@@ -639,6 +643,7 @@ typedef struct sufb200_layernorm_party {
   size_t trunc_key_bytes[SUFB200_LAYERNORM_TRUNCS][4];
   int32_t trunc_keys_device;  /* nonzero: trunc_keys are device pointers */
   const void* trunc_tables[SUFB200_LAYERNORM_TRUNCS]; /* device or NULL, as in sufb200_softmax_party */
+  void* trunc_ready[SUFB200_LAYERNORM_TRUNCS];        /* cudaEvent_t or NULL, as in sufb200_softmax_party */
 } sufb200_layernorm_party;
 
 /* runtime::LayerNormTask with RsqrtTask (include/runtime/phase_tasks.hpp:

@@ -882,11 +882,15 @@ int sufb200_trunc_tables_many_dev(sufb200_ctx ctx, int count, const sufb200_trun
                                              ctx->d_status, acc});
   }
   cudaStream_t st = as_stream(stream);
+  // Table fills run beside the work that produces x^: a quarter of the SMs
+  // each (the frontier kernel holds a whole SM's registers and shared
+  // memory per block, so a full-width fill would stall that work).
+  const int max_grid = (ctx->sm_count + 3) / 4;
   for (size_t at = 0; at < work.size(); at += sufb200::kFrontierMaxKeys) {
     sufb200::FrontierBatch fb{};
     fb.nq = static_cast<int>(std::min<size_t>(sufb200::kFrontierMaxKeys, work.size() - at));
     for (int q = 0; q < fb.nq; q++) fb.q[q] = work[at + q];
-    const cudaError_t e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st);
+    const cudaError_t e = sufb200::launch_frontier(ctx, SUFB200_GROUP_ADD, fb, st, max_grid);
     if (e != cudaSuccess) return cuda_fail(e, "tables launch");
   }
   return SUFB200_OK;

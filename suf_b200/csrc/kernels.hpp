@@ -177,7 +177,10 @@ uint32_t prefix_budget(size_t n);
 cudaError_t launch_range(const sufb200_ctx_s* ctx, const uint64_t* xs, size_t n, RangeAcc* acc, cudaStream_t st);
 // The range of "every value" in place of launch_range (see prefix.cu).
 cudaError_t set_full_range(RangeAcc* acc, cudaStream_t st);
-cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st);
+// max_grid > 0 caps the blocks (one per SM): a fill meant to run beside
+// other work leaves the remaining SMs to it.
+cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st,
+                            int max_grid = 0);
 cudaError_t launch_myl7_bcast_prefix(const sufb200_ctx_s* ctx, int group, const DcfLaunch& a, const RangeAcc* acc,
                                      uint32_t kmax, const FrontierEntry* F, cudaStream_t st);
 cudaError_t launch_trunc_bundle_prefix(const sufb200_ctx_s* ctx, const TruncLaunch& a, const RangeAcc* acc,

@@ -178,11 +178,17 @@ int ln_launch_rc(const char* what) {
 
 int ln_trunc2(sufb200_ctx ctx, const sufb200_layernorm_party* p0, const sufb200_layernorm_party* p1, int k,
               const uint64_t* xhat, size_t n, uint64_t* out0, uint64_t* out1, cudaStream_t st) {
-  if (p0->trunc_keys_device && p1->trunc_keys_device && p0->trunc_tables[k] && p1->trunc_tables[k])
+  if (p0->trunc_keys_device && p1->trunc_keys_device && p0->trunc_tables[k] && p1->trunc_tables[k]) {
+    if (p0->trunc_ready[k]) {
+      const cudaError_t e = cudaStreamWaitEvent(st, static_cast<cudaEvent_t>(p0->trunc_ready[k]), 0);
+      if (e != cudaSuccess)
+        return sufb200::record_error(SUFB200_ERR_CUDA, std::string("wait for bundle tables: ") + cudaGetErrorString(e));
+    }
     return sufb200_trunc_bundle_eval_pair_tables_dev(ctx, &p0->trunc[k], p0->trunc_keys[k], p0->trunc_key_bytes[k],
                                                      p0->trunc_tables[k], &p1->trunc[k], p1->trunc_keys[k],
                                                      p1->trunc_key_bytes[k], p1->trunc_tables[k], xhat, n, out0, out1,
                                                      st);
+  }
   if (p0->trunc_keys_device && p1->trunc_keys_device)  // resident keys: no host copy (capturable in a graph)
     return sufb200_trunc_bundle_eval_pair_dev(ctx, &p0->trunc[k], p0->trunc_keys[k], p0->trunc_key_bytes[k],
                                               &p1->trunc[k], p1->trunc_keys[k], p1->trunc_key_bytes[k], xhat, n, out0,

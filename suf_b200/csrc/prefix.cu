@@ -329,11 +329,13 @@ cudaError_t set_full_range(RangeAcc* acc, cudaStream_t st) {
   return e;
 }
 
-cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st) {
+cudaError_t launch_frontier(const sufb200_ctx_s* ctx, int group, const FrontierBatch& b, cudaStream_t st,
+                            int max_grid) {
   if (b.nq < 1 || b.nq > kFrontierMaxKeys) return cudaErrorInvalidValue;
   size_t work = 0;
   for (int q = 0; q < b.nq; q++) work += b.q[q].kmax;
-  const int grid = aes_grid(ctx, 2 * work);  // up to two lanes per work item
+  int grid = aes_grid(ctx, 2 * work);  // up to two lanes per work item
+  if (max_grid > 0 && grid > max_grid) grid = max_grid;
   cudaError_t e;
   if (group == SUFB200_GROUP_ADD) {
     if ((e = set_smem(frontier_kernel<SUFB200_GROUP_ADD>, ctx)) != cudaSuccess) return e;

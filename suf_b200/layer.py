@@ -364,16 +364,19 @@ class TransformerLayerPair:
         x = (d_x0, d_x1)
         # the truncations' full-domain tables depend on their keys only: they
         # are filled on a side stream, in the order the layer needs them,
-        # while LayerNorm and the first matmuls run (the first LayerNorm's own
-        # bundles walk their keys: it starts the layer)
+        # while LayerNorm and the first matmuls run (the first LayerNorm's
+        # mean and variance bundles walk their keys: they start the layer)
         main = stream if stream is not None else torch.cuda.current_stream(self.dev)
         if self._tab_stream is None:
             self._tab_stream = torch.cuda.Stream(device=self.dev)
             self._tab_fork = torch.cuda.Event()
-            self._tab_ev = [torch.cuda.Event() for _ in range(5)]
+            self._tab_ev = [torch.cuda.Event() for _ in range(7)]
         ts, ev = self._tab_stream, self._tab_ev
         self._tab_fork.record(main)
         ts.wait_event(self._tab_fork)
+        # the first LayerNorm's normalised-output bundle (its last step): the
+        # block waits on the event right before it
+        self.ln1.prepare_tables(ts, bundles=(7,), ready=ev[6])
         g = self._tab_groups
         for (grp, block), e in zip(((g[0], None), (None, self.softmax), (g[1], None), (None, self.ln2),
                                     (g[2], None)), ev):
@@ -457,14 +460,17 @@ class TransformerLayerPair:
 
     # launches of our kernels per layer (counted from the calls above).  Every
     # truncation bundle with tables is one launch against them; the side
-    # stream fills the tables with one frontier launch per 16 keys: three for
-    # the layer's own six bundles (three groups of 8 keys), two
-    # each for the softmax block (28 keys) and the second LayerNorm block
-    # (24 keys), whose four and one element-level bundles then skip their
-    # own frontier launch.
+    # stream fills the tables with one frontier launch per 16 keys of a
+    # group: three for the layer's own six bundles (three groups of 8 keys),
+    # two for the softmax block (28 keys), one for the first LayerNorm's
+    # normalised output (4 keys) and two for the second LayerNorm (24 keys);
+    # their element-level bundles then skip their own frontier launch.
     def launches(self) -> int:
         d = self.dims
-        ln = 19 + (19 - 1) + 2  # LayerNorm 1 walks its keys; LayerNorm 2 against tables (bench.py's LAYERNORM_LAUNCHES)
+        # each LayerNorm's element-level bundle against tables, one frontier
+        # launch fewer than bench.py's LAYERNORM_LAUNCHES; table fills: one
+        # for the first (that bundle only), two for the second (every f-bit bundle)
+        ln = (19 - 1 + 1) + (19 - 1 + 2)
         sm = 22 - 4 + 2  # the softmax block against tables (bench.py's SOFTMAX_LAUNCHES)
         mm = 4 * (2 * 2 + 1 + 1)  # qkv, o, ff1, ff2: two ring matmuls (pre-pass + GEMM each), open, truncation
         bv = 2 * (1 + 1)  # scores, pv: the Beaver open, the truncation

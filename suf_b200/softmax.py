@@ -50,6 +50,7 @@ class SoftmaxParty(C.Structure):
         ("trunc_key_bytes", (C.c_size_t * 4) * N_TRUNCS),
         ("trunc_keys_device", C.c_int32),
         ("trunc_tables", C.c_void_p * N_TRUNCS),
+        ("trunc_ready", C.c_void_p * N_TRUNCS),
     ]
 
 
@@ -106,14 +107,30 @@ def _triples(rng: np.random.Generator, n: int):
     return out
 
 
-def _block_tables(parts, dev):
-    """Both parties' tables of a block's truncation bundles (TruncTables
+def _block_tables(parts, dev, ks):
+    """Both parties' tables of a block's truncation bundles ks (TruncTables
     over party 0's bundles, then party 1's)."""
     from .engine import TruncTables
 
-    K = len(parts[0].trunc)
     return TruncTables([(parts[p].trunc[k], parts[p].trunc_keys[k], parts[p].trunc_key_bytes[k])
-                        for p in (0, 1) for k in range(K)], dev)
+                        for p in (0, 1) for k in ks], dev)
+
+
+def _prepare_tables(blk, stream, bundles, ready):
+    import torch
+
+    K = len(blk.parts[0].trunc)
+    ks = tuple(range(K)) if bundles is None else tuple(bundles)
+    T = blk._tables.get(ks)
+    if T is None:
+        T = blk._tables[ks] = _block_tables(blk.parts, blk._dev, ks)
+    T.fill(blk.ctx, stream)
+    if ready is not None:
+        ready.record(stream if stream is not None else torch.cuda.current_stream())
+    for j, k in enumerate(ks):
+        for p in (0, 1):
+            blk.parts[p].trunc_tables[k] = T.ptr(p * len(ks) + j)
+            blk.parts[p].trunc_ready[k] = ready.cuda_event if ready is not None else None
 
 
 class SoftmaxBlock:
@@ -135,7 +152,7 @@ class SoftmaxBlock:
         self.n = int(off[-1])
         dev = self._dev = torch.device("cuda", ctx.device if hasattr(ctx, "device") else 0)
         self._keep = []  # host key arrays and device tensors the structs point at
-        self._tables = None  # prepare_tables()
+        self._tables = {}  # prepare_tables(): bundle subset -> TruncTables
 
         def dcopy(a: np.ndarray):
             t = torch.from_numpy(np.ascontiguousarray(a).view(np.int64) if a.dtype == np.uint64 else a).to(dev)
@@ -198,18 +215,14 @@ class SoftmaxBlock:
             parts[p].trunc_keys_device = 1
         self.parts = parts
 
-    def prepare_tables(self, stream=None):
-        """Fill the tables of every truncation bundle with queries of at most
-        16 bits on `stream` (they depend on the keys only) and switch those
-        bundles to table evaluation: block calls ordered after this on the
-        device read them instead of walking the keys."""
-        if self._tables is None:
-            self._tables = _block_tables(self.parts, self._dev)
-        self._tables.fill(self.ctx, stream)
-        K = len(self.parts[0].trunc)
-        for p in (0, 1):
-            for k in range(K):
-                self.parts[p].trunc_tables[k] = self._tables.ptr(p * K + k)
+    def prepare_tables(self, stream=None, bundles=None, ready=None):
+        """Fill the tables of the truncation bundles `bundles` (default all)
+        whose queries are at most 16 bits wide, on `stream` (they depend on
+        the keys only), and switch those bundles to table evaluation.  Block
+        calls ordered after this on the device read them; with a
+        torch.cuda.Event `ready` (recorded here after the fill) a block call
+        on another stream waits for it right before each such bundle."""
+        _prepare_tables(self, stream, bundles, ready)
 
     def run(self, d_t0, d_t1, d_prob0=None, d_prob1=None, stream=None):
         """Both parties' shares of the packed max-differences t (Q f, int64
@@ -253,6 +266,7 @@ class LayerNormParty(C.Structure):
         ("trunc_key_bytes", (C.c_size_t * 4) * N_LN_TRUNCS),
         ("trunc_keys_device", C.c_int32),
         ("trunc_tables", C.c_void_p * N_LN_TRUNCS),
+        ("trunc_ready", C.c_void_p * N_LN_TRUNCS),
     ]
 
 
@@ -276,7 +290,7 @@ class LayerNormBlock:
         self.eps = int(round((1 << f) / 1024))
         dev = self._dev = torch.device("cuda", ctx.device)
         self._keep = []
-        self._tables = None  # prepare_tables()
+        self._tables = {}  # prepare_tables(): bundle subset -> TruncTables
 
         def dcopy(a: np.ndarray):
             t = torch.from_numpy(np.ascontiguousarray(a).view(np.int64) if a.dtype == np.uint64 else a).to(dev)
@@ -329,18 +343,14 @@ class LayerNormBlock:
             parts[p].trunc_keys_device = 1
         self.parts = parts
 
-    def prepare_tables(self, stream=None):
-        """Fill the tables of every truncation bundle with queries of at most
-        16 bits on `stream` (they depend on the keys only) and switch those
-        bundles to table evaluation: block calls ordered after this on the
-        device read them instead of walking the keys."""
-        if self._tables is None:
-            self._tables = _block_tables(self.parts, self._dev)
-        self._tables.fill(self.ctx, stream)
-        K = len(self.parts[0].trunc)
-        for p in (0, 1):
-            for k in range(K):
-                self.parts[p].trunc_tables[k] = self._tables.ptr(p * K + k)
+    def prepare_tables(self, stream=None, bundles=None, ready=None):
+        """Fill the tables of the truncation bundles `bundles` (default all)
+        whose queries are at most 16 bits wide, on `stream` (they depend on
+        the keys only), and switch those bundles to table evaluation.  Block
+        calls ordered after this on the device read them; with a
+        torch.cuda.Event `ready` (recorded here after the fill) a block call
+        on another stream waits for it right before each such bundle."""
+        _prepare_tables(self, stream, bundles, ready)
 
     def run(self, d_x0, d_x1, d_out0=None, d_out1=None, stream=None):
         """Both parties' shares of x (rows * cols, Q f, int64 tensors on the

@@ -475,9 +475,10 @@ def test_ctypes_mirrors_match_the_c_structs(tmp_path):
         "sufb200_trunc_desc": (TruncDesc, ["frac_bits", "q_bits", "carry_a", "wrap_q", "carry_w", "haty", "m"]),
         "sufb200_softmax_party": (SoftmaxParty, ["recip_rin", "d_recip_lut", "d_row_c", "trunc", "trunc_rin",
                                                  "trunc_keys", "trunc_key_bytes", "trunc_keys_device",
-                                                 "trunc_tables"]),
+                                                 "trunc_tables", "trunc_ready"]),
         "sufb200_layernorm_party": (LayerNormParty, ["d_rsqrt_lut", "d_norm_c", "trunc", "trunc_rin", "trunc_keys",
-                                                     "trunc_key_bytes", "trunc_keys_device", "trunc_tables"]),
+                                                     "trunc_key_bytes", "trunc_keys_device", "trunc_tables",
+                                                     "trunc_ready"]),
     }
     src = ['#include <stdio.h>', '#include <stddef.h>', '#include "sufb200.h"', "int main(void) {"]
     for name, (_, fs) in fields.items():

@@ -163,8 +163,33 @@ def test_block_tables_give_the_walks_shares(ctx, torch_cuda, which, shape):
     s0, s1 = (to_dev(torch_cuda, a) for a in _shares(rng, v))
     walk = [from_dev(o, np.uint64) for o in blk.run(s0, s1)]
     blk.prepare_tables()
-    assert blk._tables.any(), "no bundle qualified for tables"
+    assert any(T.any() for T in blk._tables.values()), "no bundle qualified for tables"
     tab = [from_dev(o, np.uint64) for o in blk.run(s0, s1)]
     ctx.sync()
     for p in (0, 1):
         assert (tab[p] == walk[p]).all(), p
+
+
+@pytest.mark.gpu
+def test_block_tables_ready_event_orders_a_side_stream_fill(ctx, torch_cuda):
+    """Tables filled on another stream with a `ready` event: the block call
+    on the current stream, issued right after with no wait of its own,
+    waits on the event before each such bundle and gives the walks' shares."""
+    from suf_b200.softmax import LayerNormBlock
+    from tests.conftest import from_dev, to_dev
+
+    rng = np.random.default_rng(77)
+    rows, cols = 128, 768
+    blk = LayerNormBlock(ctx, rows, cols, seed=71)
+    v = np.round(rng.normal(0.0, 1.0, rows * cols) * 4096).astype(np.int64).view(np.uint64)
+    s0, s1 = (to_dev(torch_cuda, a) for a in _shares(rng, v))
+    walk = [from_dev(o, np.uint64) for o in blk.run(s0, s1)]
+    side = torch_cuda.cuda.Stream()
+    for _ in range(2):  # a second fill rewrites the same tables
+        ev = torch_cuda.cuda.Event()
+        side.wait_stream(torch_cuda.cuda.current_stream())
+        blk.prepare_tables(side, bundles=(2, 3, 4, 6, 7), ready=ev)
+        tab = [from_dev(o, np.uint64) for o in blk.run(s0, s1)]
+        for p in (0, 1):
+            assert (tab[p] == walk[p]).all(), p
+    ctx.sync()
