@@ -422,6 +422,22 @@ __device__ __forceinline__ void coeff_emit_shared(const CoeffSide& S0, const Coe
   const uint64_t* row1 = S1.pay + static_cast<size_t>(iv) * ow;
   uint64_t* out0 = S0.out + i * static_cast<size_t>(r);
   uint64_t* out1 = S1.out + i * static_cast<size_t>(r);
+  if (r == 4 && d1 == 1 &&
+      ((reinterpret_cast<uintptr_t>(S0.out) | reinterpret_cast<uintptr_t>(S1.out)) & 15u) == 0) {
+    // four degree-0 words: two 16-byte stores a party (32-byte rows from a 16-byte aligned base)
+    uint64_t o0[4], o1[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const uint64_t ksw = ks_word(k0, k1, j);
+      o0[j] = ((party0 == 0 ? ksw : (row0[j] - ksw)) + S0.r_out[j]) & S0.ring_mask;
+      o1[j] = ((party1 == 0 ? ksw : (row1[j] - ksw)) + S1.r_out[j]) & S1.ring_mask;
+    }
+    reinterpret_cast<ulonglong2*>(out0)[0] = make_ulonglong2(o0[0], o0[1]);
+    reinterpret_cast<ulonglong2*>(out0)[1] = make_ulonglong2(o0[2], o0[3]);
+    reinterpret_cast<ulonglong2*>(out1)[0] = make_ulonglong2(o1[0], o1[1]);
+    reinterpret_cast<ulonglong2*>(out1)[1] = make_ulonglong2(o1[2], o1[3]);
+    return;
+  }
   int w = 0;
   for (int j = 0; j < r; j++) {
     uint64_t acc0 = 0, acc1 = 0, pw = 1;
@@ -467,17 +483,15 @@ __device__ __forceinline__ void coeff_shared_items(const CoeffSide& S0, const Co
     return;
   }
   if (ow <= 4) {
-    uint32_t rk[44];
-#pragma unroll
-    for (int k = 0; k < 44; k++) rk[k] = s_rk[k];
+    const uint4* rk4 = reinterpret_cast<const uint4*>(s_rk);
     for (size_t i = first; i < n; i += step) {
       const uint64_t xh = xh_next;
       xh_next = i + step < n ? __ldg(xs + i + step) : 0ull;
       const int iv = coeff_interval(S0, xh);
       const uint64_t base = S0.nonce ^ ((S0.idx_base + i) << 32), w0 = static_cast<uint64_t>(iv) * ow;
-      Blk k0, k1;
-      aes_encrypt2_rk(ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2)), lb, rk, k0, k1);
-      coeff_emit_shared(S0, S1, i, iv, xh, k0, k1);
+      Blk k[2] = {ctr_block(base ^ w0), ctr_block(base ^ (w0 + 2))};
+      aes_encrypt_n_sk<2>(k, lb, rk4);
+      coeff_emit_shared(S0, S1, i, iv, xh, k[0], k[1]);
     }
     return;
   }
